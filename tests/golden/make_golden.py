@@ -1,0 +1,174 @@
+"""Generate the golden fixtures in this folder from the REFERENCE implementation.
+
+Run in a container where the reference package is mounted (default location below,
+override with MASKAHEAD_REF_SRC):
+
+    python tests/golden/make_golden.py
+
+For each case of gen_inputs.CASES it builds the reference's LayerCacheView on the
+seeded inputs and records what the reference's own CPU (torch) path returns:
+
+* selector_topk(backend="torch", return_importance=True)     kernels/ops.py:333-521
+* BitSieveSession._rescore_by_value (value_center="attn")     runtime/session.py:870-954
+* dense_attention_reference over [live prefix | block]       reference.py:279-296
+* sdpa_compact over [value-aware read set | block]           reference.py:403-426
+* value_score (BITSIEVE_VSCORE_FP32=1) + EvictionState.survivors (lookahead)
+                                                              session.py:27-40, eviction.py:325-409
+* quantize_values / quantize_keys payloads                    reference.py:58-90, 182-213
+
+Outputs go to <case>.npz next to this script, with the SHA-256 of the inputs.
+"""
+
+from __future__ import annotations
+
+import os
+import sys
+import types
+from pathlib import Path
+
+import numpy as np
+import torch
+
+HERE = Path(__file__).resolve().parent
+sys.path.insert(0, str(HERE))
+sys.path.insert(0, os.environ.get("MASKAHEAD_REF_SRC", "/root/reference/src"))
+os.environ["BITSIEVE_VSCORE_FP32"] = "1"
+
+from gen_inputs import CASES, digest, make_case, make_retain_case  # noqa: E402
+
+from maskahead.cache import LayerCacheView  # noqa: E402
+from maskahead.eviction import EvictionConfig, EvictionState  # noqa: E402
+from maskahead.kernels.ops import selector_topk  # noqa: E402
+from maskahead.reference import (  # noqa: E402
+    dense_attention_reference, dequantize_keys, dequantize_values, gather_per_kv_head,
+    quantize_keys, quantize_values, sdpa_compact, selector_importance_reference,
+    PackedKeys, PackedValues,
+)
+from maskahead.runtime.session import BitSieveSession, value_score  # noqa: E402
+
+
+def _view(case) -> tuple[LayerCacheView, torch.Tensor, torch.Tensor, dict]:
+    """Reference cache view of the case, plus the prefix K/V as the reference reads them."""
+    spec = case["spec"]
+    n, D = spec["n"], spec["D"]
+    extra = {}
+    packed = spec.get("packed")
+    if not packed:
+        k, v = case["key"], case["value"]
+        view = LayerCacheView(k_bits=16, v_bits=16, length=n, quantized_length=0, residual_length=0,
+                              key_token_group=32, value_channel_group=32, k_q=None, k_scale=None,
+                              k_zero=None, v_q=None, v_scale=None, v_zero=None, k_fp=k, v_fp=v,
+                              k_residual=None, v_residual=None, head_dim=D)
+        return view, k, v, extra
+    kf, vf = case["key_fp"], case["value_fp"]
+    pv = quantize_values(vf, bits=4, channel_group=32)
+    extra.update(vq=pv.payload, vs=pv.scale, vz=pv.zero)
+    v = dequantize_values(pv, dtype=torch.bfloat16)
+    if packed == "channel":
+        pk = quantize_keys(kf, bits=4, token_group=32)
+        extra.update(kq=pk.payload, ks=pk.scale, kz=pk.zero)
+        k = dequantize_keys(pk, dtype=torch.bfloat16)
+        view = LayerCacheView(k_bits=4, v_bits=4, length=n, quantized_length=n, residual_length=0,
+                              key_token_group=32, value_channel_group=32, k_q=pk.payload, k_scale=pk.scale,
+                              k_zero=pk.zero, v_q=pv.payload, v_scale=pv.scale, v_zero=pv.zero, k_fp=None,
+                              v_fp=None, k_residual=None, v_residual=None, head_dim=D)
+        return view, k, v, extra
+    # token mode: c_i = sqrt(max_t |K|) (cache.py:488-490), keys / c quantized like values
+    # (cache.py:491-497); dequant = fp32(code*s+z) * c, one cast (splitk.py:389-395)
+    kchan = kf.abs().amax(dim=2).float().clamp_min(1e-4).sqrt()
+    kn = (kf.float() / kchan.unsqueeze(2)).to(torch.bfloat16)
+    pk = quantize_values(kn, bits=4, channel_group=32)
+    extra.update(kq=pk.payload, ks=pk.scale, kz=pk.zero, kchan=kchan)
+    k = (dequantize_values(pk, dtype=torch.float32) * kchan.unsqueeze(2)).to(torch.bfloat16)
+    return None, k, v, extra
+
+
+def _rescore(importance, k, v, live_mask, topk):
+    """Run the reference's BitSieveSession._rescore_by_value on a minimal stand-in."""
+    sel = types.SimpleNamespace(value_center="attn", value_joint=False, value_per_query=False,
+                                value_set="none", value_caote=False, sort_indices=True)
+    stub = types.SimpleNamespace(
+        cache=types.SimpleNamespace(dequantize_layer=lambda layer: (k, v)),
+        config=types.SimpleNamespace(collect_diagnostics=False, selector=sel),
+    )
+    from maskahead.kernels.ops import SelectorResult
+    res = BitSieveSession._rescore_by_value(stub, 0, SelectorResult(indices=None, values=None,
+                                                                     importance=importance),
+                                            topk, live_mask)
+    return res.indices, stub._last_value_score
+
+
+def build_case(name: str) -> dict:
+    case = make_case(name)
+    spec = case["spec"]
+    view, k, v, extra = _view(case)
+    q, kc, vc, rows = case["query"], case["current_key"], case["current_value"], case["rows"]
+    live = case.get("live_mask")
+    D = spec["D"]
+    n_live = spec["n"] if live is None else int(live[0, 0].sum())
+    topk = min(spec["k"], n_live)
+    if view is not None:
+        res = selector_topk(q, view, query_indices=rows, topk=topk, backend="torch", live_mask=live,
+                            return_importance=True, scaling=D ** -0.5)
+        importance, mass_idx = res.importance, res.indices
+    else:
+        importance = selector_importance_reference(q, k, query_indices=rows, scale=D ** -0.5,
+                                                   live_mask=live)
+        rank_on = importance if live is None else importance.masked_fill(~live, float("-inf"))
+        mass_idx = torch.topk(rank_on, k=topk, dim=-1, sorted=False).indices.sort(dim=-1).values
+    vidx, vscore = _rescore(importance, k, v, live, topk)
+    # dense step-0 attention over the live prefix and the block (session.py:1472-1504, 1506+)
+    if live is None:
+        k_used, v_used = k, v
+    else:
+        pos = live.nonzero()[:, -1].reshape(live.shape[0], live.shape[1], -1)
+        k_used, v_used = gather_per_kv_head(k, pos), gather_per_kv_head(v, pos)
+    dense_out = dense_attention_reference(q, k_used, v_used, kc, vc, scale=D ** -0.5)
+    # sparse sub-step over [read set | block] (session.py:1286-1336)
+    sk = torch.cat([gather_per_kv_head(k, vidx), kc.to(k.dtype)], dim=2)
+    sv = torch.cat([gather_per_kv_head(v, vidx), vc.to(v.dtype)], dim=2)
+    compact_out = sdpa_compact(q.to(k.dtype), sk, sv).to(q.dtype)
+    inputs = {key: val for key, val in case.items() if isinstance(val, torch.Tensor)}
+    inputs.update({key: val for key, val in extra.items()})
+    out = dict(
+        digest=np.array(digest(inputs)),
+        importance=importance.float().numpy(),
+        mass_indices=mass_idx.numpy(),
+        value_score=vscore.float().numpy(),
+        value_indices=vidx.numpy(),
+        dense_out=dense_out.float().numpy(),
+        compact_out=compact_out.float().numpy(),
+        topk=np.array(topk),
+    )
+    for key in ("kq", "ks", "kz", "vq", "vs", "vz", "kchan"):
+        if key in extra:
+            t = extra[key]
+            out["packed_" + key] = t.view(torch.int16).numpy() if t.dtype in (torch.float16, torch.bfloat16) else t.numpy()
+    return out
+
+
+def build_retain() -> dict:
+    r = make_retain_case()
+    a = r["a1"] + r["a_probe"]                                   # session.py:2017-2021
+    score = value_score(a, r["v_live"])                          # session.py:2025 (fp32 centre)
+    L, B, H, live = r["pos"].shape
+    st = EvictionState(num_layers=L, batch_size=B, num_kv_heads=H, capacity=live, device="cpu")
+    st.append(list(range(live)))
+    st.pos[..., :live] = r["pos"]
+    cfg = EvictionConfig(policy="lookahead", recent_window=r["W"], capacity_floor=r["C"],
+                         sink_tokens=r["sinks"], lookahead_blocks=1)
+    keep = st.survivors(cfg, r["C"], None, score)
+    inputs = {key: val for key, val in r.items() if isinstance(val, torch.Tensor)}
+    return dict(digest=np.array(digest(inputs)), score=score.numpy(), keep=keep.numpy())
+
+
+def main() -> None:
+    for name in CASES:
+        np.savez_compressed(HERE / f"{name}.npz", **build_case(name))
+        print("wrote", name)
+    np.savez_compressed(HERE / "retain.npz", **build_retain())
+    print("wrote retain")
+
+
+if __name__ == "__main__":
+    main()
