@@ -1,0 +1,198 @@
+/*
+ * maskahead_b200 -- C ABI of the B200 (sm_100a) select + attend hot path.
+ *
+ * Every entry point takes plain device pointers, element strides and sizes, enqueues
+ * its kernels on the given CUDA stream (cudaStream_t passed as void*, NULL = legacy
+ * default stream), never synchronizes, never allocates device memory, and returns an
+ * int status: MA_OK (0) or a negative MA_ERR_* code. Arguments are validated on the
+ * host before anything is launched; a rejected call launches nothing. Scratch memory
+ * is caller-provided ("workspace") and sized by the matching *_workspace() function;
+ * a workspace must be zero-filled once when it is allocated (kernels leave it ready
+ * for the next call) and must not be shared by calls that can overlap on the GPU.
+ *
+ * Conventions
+ *   query rows:  Q [B, Hq, T, D], Hq = G * H (GQA); the R = G*T rows of KV head h are
+ *                r = g*T + t for query head h*G + g and block position t.
+ *   prefix:      described by ma_kv (layout, strides, optional live-slot mask).
+ *   strides:     in ELEMENTS of the tensor's own type; the innermost dimension is
+ *                contiguous unless stated otherwise.
+ *   D:           head_dim, 64 or 128.
+ *
+ * The entry points replace the reference package's operator bodies (file:line within
+ * brain-lab-research/MaskAhead, src/maskahead/):
+ *   ma_prefix_attention  kernels/splitk.py:493-579 (splitk_attention) and
+ *                        kernels/ops.py:130-264, 766-787 (dense_packed_attention)
+ *   ma_prefix_mass       kernels/splitk.py:582-614 (prefix_scores, mass part) and
+ *                        kernels/ops.py:333-521 (selector_topk importance)
+ *   ma_value_score       runtime/session.py:27-40 (value_score) and 870-954
+ *                        (_rescore_by_value, value_center="attn")
+ *   ma_select_topk       kernels/ops.py:377-380, 509-516; runtime/session.py:1434-1438
+ *   ma_retain            eviction.py:325-409 (EvictionState.survivors, lookahead)
+ *   ma_sparse_attention  runtime/session.py:1286-1336 + reference.py:403-426
+ *                        (_compact_attention -> sdpa_compact over the read set)
+ *   ma_gather_kv         kernels/ops.py:570-662, 835-855 (gather_packed_kv)
+ */
+#ifndef MASKAHEAD_B200_H
+#define MASKAHEAD_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define MA_API __attribute__((visibility("default")))
+#else
+#define MA_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- status codes ---------------------------------------------------------------- */
+#define MA_OK 0
+#define MA_ERR_ARG (-1)          /* invalid shape, stride, pointer or parameter        */
+#define MA_ERR_UNSUPPORTED (-2)  /* valid request outside what the kernels implement   */
+#define MA_ERR_WORKSPACE (-3)    /* workspace missing or smaller than *_workspace()     */
+#define MA_ERR_CUDA (-4)         /* a CUDA runtime call or launch failed                */
+#define MA_ERR_TIMEOUT (-5)      /* a bounded device-side wait gave up                  */
+
+/* ---- element types ----------------------------------------------------------------- */
+#define MA_F32 0
+#define MA_BF16 1
+#define MA_F16 2
+
+/* ---- KV layouts -------------------------------------------------------------------- */
+/* Dense: K/V [B,H,n,D] in `dtype` (fp32 or bf16) -- LayerCacheView k_fp/v_fp
+ * (cache.py:142-143). */
+#define MA_KV_DENSE 0
+/* Packed, token-mode keys: the first nq slots hold 4-bit codes of every token over
+ * channel groups of vgroup (payload [.., D/vgroup, vgroup/2] u8, fp16 scale/zero
+ * [.., D/vgroup]) for both K and V; keys are multiplied by the per-channel divisor
+ * kchan [B,H,D] fp32 after dequantization; slots nq..nq+nf-1 are a `dtype` tail
+ * (cache.py:146-152, 172-189; splitk.py:389-395). */
+#define MA_KV_PACKED_TOKEN 1
+/* Packed, KIVI channel-mode keys: key payload [B,H,ng,D,kgroup/2] u8 and fp16
+ * scale/zero [B,H,ng,D] per group of kgroup tokens; values as in the token layout
+ * (cache.py:154-169). */
+#define MA_KV_PACKED_CHANNEL 2
+
+typedef struct ma_kv {
+  int32_t layout;        /* MA_KV_*                                                   */
+  int32_t dtype;         /* element type of dense K/V and of the tail: MA_F32/MA_BF16  */
+  int32_t nq;            /* packed slots (0 for MA_KV_DENSE)                           */
+  int32_t nf;            /* dense / tail slots after them (all n for MA_KV_DENSE)      */
+  int32_t kgroup;        /* channel-mode key token group (32)                          */
+  int32_t vgroup;        /* value (and token-mode key) channel group (32)              */
+  /* dense K/V or the tail: strides over (b, h, slot), D contiguous                    */
+  const void* kf;
+  const void* vf;
+  int64_t skf[3];
+  int64_t svf[3];
+  /* packed keys: token mode strides over (b, h, slot) of a slot's contiguous
+   * D/2-byte payload; channel mode strides over (b, h, group) of a group's contiguous
+   * [D][kgroup/2] payload. Scale/zero (fp16 bit patterns) strides follow the same axes
+   * with the channel (group) index contiguous.                                          */
+  const uint8_t* kq;
+  const uint16_t* ks;
+  const uint16_t* kz;
+  int64_t skq[3];
+  int64_t sks[3];
+  /* packed values: strides over (b, h, slot)                                          */
+  const uint8_t* vq;
+  const uint16_t* vs;
+  const uint16_t* vz;
+  int64_t svq[3];
+  int64_t svs[3];
+  /* token-mode key divisor [B,H,D] fp32: strides over (b, h)                          */
+  const float* kchan;
+  int64_t skc[2];
+  /* optional live-slot mask, uint8 [B,H,nq+nf] contiguous; 0 = dead slot, never read  */
+  const uint8_t* mask;
+} ma_kv;
+
+/* The query block: Q [B,Hq,T,D], strides over (b, hq, t). */
+typedef struct ma_rows {
+  const void* q;
+  int32_t dtype;         /* MA_F32 or MA_BF16; the output has the same type             */
+  int32_t B, Hq, T, D;
+  int64_t sq[3];
+} ma_rows;
+
+/* The current block's keys/values [B,H,Tc,D] (query dtype), strides over (b, h, t). */
+typedef struct ma_block {
+  const void* k;
+  const void* v;
+  int32_t Tc;
+  int64_t sk[3];
+  int64_t sv[3];
+} ma_block;
+
+/* ---- library ----------------------------------------------------------------------- */
+MA_API int ma_version(void);                       /* (major << 16) | minor                   */
+MA_API const char* ma_status_string(int status);
+
+/* ---- attention over [prefix | current block] ----------------------------------------
+ * out[b, h*G+g, t, :] = softmax over the live prefix slots and the visible current keys.
+ * causal_block > 0: query t sees current key j iff (c_pos0+j)/cb <= (q_pos0+t)/cb.
+ * m_p, l_p ([B,H,R] fp32) and o_p ([B,H,R,D] fp32), all optional (NULL): prefix-only
+ * softmax max, sum of exp(s - m_p) and normalized output per row.                    */
+MA_API size_t ma_prefix_attention_workspace(int B, int H, int R, int n, int D, int Tc);
+MA_API int ma_prefix_attention(const ma_rows* q, const ma_kv* kv, int H, const ma_block* cur,
+                        float scale, int causal_block, int q_pos0, int c_pos0,
+                        void* out, const int64_t so[3],
+                        float* m_p, float* l_p, float* o_p,
+                        void* workspace, size_t workspace_bytes, void* stream);
+
+/* ---- prefix mass --------------------------------------------------------------------
+ * mass[b,h,j] = mean over rows (g, t in q_rows[0..T2)) of exp(s - m_p[r]) / l_p[r],
+ * s = scale * q_r . k_j; 0 on dead slots. mass strides over (b, h).                    */
+MA_API int ma_prefix_mass(const ma_rows* q, const ma_kv* kv, int H, const int32_t* q_rows, int T2,
+                   const float* m_p, const float* l_p, float scale,
+                   float* mass, const int64_t smass[2], void* stream);
+
+/* ---- value-aware score --------------------------------------------------------------
+ * c = sum_j a_j v_j / max(sum_j a_j, 1e-12) over live slots, score_j = a_j*||v_j - c||
+ * (fp32; dead slots: 0). a and score strides over (b, h).                              */
+MA_API size_t ma_value_score_workspace(int B, int H, int n, int D);
+MA_API int ma_value_score(const ma_kv* kv, int B, int H, int D, const float* a, const int64_t sa[2],
+                   float* score, const int64_t sscore[2],
+                   void* workspace, size_t workspace_bytes, void* stream);
+
+/* ---- top-k read set -----------------------------------------------------------------
+ * Per (b, h): the k largest scores among live slots (ties: lower slot first), written
+ * as ascending slot indices (int64) with their scores (values optional).             */
+MA_API int ma_select_topk(const float* score, int B, int H, int n, const int64_t sscore[2],
+                   const uint8_t* mask, int k, int64_t* indices, float* values,
+                   const int64_t sidx[2], void* stream);
+
+/* ---- lookahead retention ------------------------------------------------------------
+ * Per lane (the flattened [L,B,H] axis): keep the W = min(recent_window, capacity)
+ * largest positions, the sinks (pos < sink_tokens) and the best remaining slots by
+ * score, capacity in total, as live-axis indices ordered by position. score and pos
+ * are [lanes, live] contiguous; when phys is not NULL the score of live entry i is
+ * score_phys[lane, phys[lane, i]] with score row length n_phys.                       */
+MA_API int ma_retain(const float* score, const int32_t* phys, int n_phys, const int32_t* pos,
+              int lanes, int live, int capacity, int recent_window, int sink_tokens,
+              int64_t* keep, void* stream);
+
+/* ---- attention over the read set and the current block ------------------------------
+ * Keys/values of prefix slots idx[b,h,0..k) (read directly from the cache layout,
+ * dequantized in the staging), then the current block, for every row.               */
+MA_API size_t ma_sparse_attention_workspace(int B, int H, int R, int k, int D, int Tc);
+MA_API int ma_sparse_attention(const ma_rows* q, const ma_kv* kv, int H,
+                        const int64_t* idx, int k, const int64_t sidx[2],
+                        const ma_block* cur, float scale,
+                        void* out, const int64_t so[3],
+                        void* workspace, size_t workspace_bytes, void* stream);
+
+/* ---- gather + dequantize ------------------------------------------------------------
+ * out_k/out_v [B,H,k,D] (out_dtype) = the prefix slots idx[b,h,:].                   */
+MA_API int ma_gather_kv(const ma_kv* kv, int B, int H, int D, const int64_t* idx, int k,
+                 const int64_t sidx[2], void* out_k, void* out_v, const int64_t sok[3],
+                 const int64_t sov[3], int32_t out_dtype, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* MASKAHEAD_B200_H */

@@ -1,0 +1,162 @@
+"""ctypes binding of ``libmaskahead_b200.so`` (the C ABI of include/maskahead_b200.h).
+
+The library is built in-tree by ``maskahead_b200.build``. There is no fallback: if the
+library is missing or CUDA is unavailable, every operator raises
+``KernelUnavailableError``.
+"""
+
+from __future__ import annotations
+
+import ctypes
+from pathlib import Path
+
+import torch
+
+LIB_PATH = Path(__file__).resolve().parent / "_lib" / "libmaskahead_b200.so"
+
+MA_OK = 0
+MA_F32, MA_BF16, MA_F16 = 0, 1, 2
+MA_KV_DENSE, MA_KV_PACKED_TOKEN, MA_KV_PACKED_CHANNEL = 0, 1, 2
+
+
+class KernelUnavailableError(RuntimeError):
+    """The sm_100a library or a CUDA device is not available (ops.py:19-21 in the reference)."""
+
+
+class MaError(RuntimeError):
+    """A C-ABI entry point returned a negative status."""
+
+    def __init__(self, fn: str, status: int, detail: str):
+        super().__init__(f"{fn} failed with status {status} ({detail})")
+        self.status = status
+
+
+c_i64_3 = ctypes.c_int64 * 3
+c_i64_2 = ctypes.c_int64 * 2
+
+
+class MaKV(ctypes.Structure):
+    _fields_ = [
+        ("layout", ctypes.c_int32), ("dtype", ctypes.c_int32), ("nq", ctypes.c_int32),
+        ("nf", ctypes.c_int32), ("kgroup", ctypes.c_int32), ("vgroup", ctypes.c_int32),
+        ("kf", ctypes.c_void_p), ("vf", ctypes.c_void_p), ("skf", c_i64_3), ("svf", c_i64_3),
+        ("kq", ctypes.c_void_p), ("ks", ctypes.c_void_p), ("kz", ctypes.c_void_p),
+        ("skq", c_i64_3), ("sks", c_i64_3),
+        ("vq", ctypes.c_void_p), ("vs", ctypes.c_void_p), ("vz", ctypes.c_void_p),
+        ("svq", c_i64_3), ("svs", c_i64_3),
+        ("kchan", ctypes.c_void_p), ("skc", c_i64_2),
+        ("mask", ctypes.c_void_p),
+    ]
+
+
+class MaRows(ctypes.Structure):
+    _fields_ = [
+        ("q", ctypes.c_void_p), ("dtype", ctypes.c_int32), ("B", ctypes.c_int32),
+        ("Hq", ctypes.c_int32), ("T", ctypes.c_int32), ("D", ctypes.c_int32), ("sq", c_i64_3),
+    ]
+
+
+class MaBlock(ctypes.Structure):
+    _fields_ = [
+        ("k", ctypes.c_void_p), ("v", ctypes.c_void_p), ("Tc", ctypes.c_int32),
+        ("sk", c_i64_3), ("sv", c_i64_3),
+    ]
+
+
+_P = ctypes.POINTER
+_vp, _i32, _f32, _sz = ctypes.c_void_p, ctypes.c_int, ctypes.c_float, ctypes.c_size_t
+
+_SIGNATURES = {
+    "ma_version": (_i32, []),
+    "ma_status_string": (ctypes.c_char_p, [_i32]),
+    "ma_prefix_attention_workspace": (_sz, [_i32] * 6),
+    "ma_prefix_attention": (_i32, [_P(MaRows), _P(MaKV), _i32, _P(MaBlock), _f32, _i32, _i32, _i32,
+                                   _vp, _P(ctypes.c_int64), _vp, _vp, _vp, _vp, _sz, _vp]),
+    "ma_prefix_mass": (_i32, [_P(MaRows), _P(MaKV), _i32, _vp, _i32, _vp, _vp, _f32, _vp,
+                              _P(ctypes.c_int64), _vp]),
+    "ma_value_score_workspace": (_sz, [_i32] * 4),
+    "ma_value_score": (_i32, [_P(MaKV), _i32, _i32, _i32, _vp, _P(ctypes.c_int64), _vp,
+                              _P(ctypes.c_int64), _vp, _sz, _vp]),
+    "ma_select_topk": (_i32, [_vp, _i32, _i32, _i32, _P(ctypes.c_int64), _vp, _i32, _vp, _vp,
+                              _P(ctypes.c_int64), _vp]),
+    "ma_retain": (_i32, [_vp, _vp, _i32, _vp, _i32, _i32, _i32, _i32, _i32, _vp, _vp]),
+    "ma_sparse_attention_workspace": (_sz, [_i32] * 6),
+    "ma_sparse_attention": (_i32, [_P(MaRows), _P(MaKV), _i32, _vp, _i32, _P(ctypes.c_int64),
+                                   _P(MaBlock), _f32, _vp, _P(ctypes.c_int64), _vp, _sz, _vp]),
+    "ma_gather_kv": (_i32, [_P(MaKV), _i32, _i32, _i32, _vp, _i32, _P(ctypes.c_int64), _vp, _vp,
+                            _P(ctypes.c_int64), _P(ctypes.c_int64), _i32, _vp]),
+}
+
+EXPORTED = tuple(_SIGNATURES)
+
+_lib: ctypes.CDLL | None = None
+
+
+def load_library() -> ctypes.CDLL:
+    """Load (once) and return the C-ABI library; raises KernelUnavailableError."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    if not LIB_PATH.exists():
+        raise KernelUnavailableError(
+            f"{LIB_PATH} is missing: build it with `python -m maskahead_b200.build`")
+    lib = ctypes.CDLL(str(LIB_PATH))
+    for name, (res, args) in _SIGNATURES.items():
+        fn = getattr(lib, name)
+        fn.restype = res
+        fn.argtypes = args
+    _lib = lib
+    return lib
+
+
+def lib() -> ctypes.CDLL:
+    """The library, for a compute call: also requires a CUDA device."""
+    if not torch.cuda.is_available():
+        raise KernelUnavailableError("maskahead_b200 kernels need a CUDA device (sm_100a)")
+    return load_library()
+
+
+def check(fn: str, status: int) -> None:
+    if status != MA_OK:
+        detail = load_library().ma_status_string(status).decode()
+        raise MaError(fn, status, detail)
+
+
+def dtype_code(dt: torch.dtype) -> int:
+    if dt == torch.float32:
+        return MA_F32
+    if dt == torch.bfloat16:
+        return MA_BF16
+    raise ValueError(f"unsupported dtype {dt}: the kernels take float32 or bfloat16")
+
+
+def ptr(t: torch.Tensor | None) -> int | None:
+    return None if t is None else t.data_ptr()
+
+
+def i64(*vals) -> ctypes.Array:
+    return (ctypes.c_int64 * len(vals))(*[int(v) for v in vals])
+
+
+def stream_handle(device: torch.device) -> int:
+    return torch.cuda.current_stream(device).cuda_stream
+
+
+# ------------------------------------------------------------------------ workspaces
+_WORKSPACES: dict[tuple, torch.Tensor] = {}
+
+
+def workspace(device: torch.device, purpose: str, nbytes: int) -> torch.Tensor:
+    """Grow-only, zero-initialized scratch per (device, purpose).
+
+    Like the reference's module-level scratch pools (ops.py:274-317) it is shared by
+    every call on the device, so calls that can overlap (several streams or threads)
+    must bring their own workspace.
+    """
+    key = (device.type, device.index, purpose)
+    buf = _WORKSPACES.get(key)
+    if buf is None or buf.numel() < nbytes:
+        size = max(nbytes, 1 << 20)
+        buf = torch.zeros(size + 256, dtype=torch.uint8, device=device)
+        _WORKSPACES[key] = buf
+    return buf

@@ -1,0 +1,303 @@
+// C ABI of the select + attend hot path: argument validation, split planning and the
+// launch sequence of every entry point declared in include/maskahead_b200.h.
+#include "ma_kernels.cuh"
+
+namespace ma {
+
+int device_sm_count() {
+  static int cached[64] = {0};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 148;
+  if (cached[dev] == 0) {
+    int sms = 0;
+    if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || sms <= 0)
+      sms = 148;
+    cached[dev] = sms;
+  }
+  return cached[dev];
+}
+
+}  // namespace ma
+
+using namespace ma;
+
+namespace {
+
+inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+inline bool aligned4(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 3u) == 0; }
+inline int esize(int dtype) { return dtype == MA_F32 ? 4 : 2; }
+inline bool valid_dtype(int dtype) { return dtype == MA_F32 || dtype == MA_BF16; }
+
+// strides (elements) whose byte size keeps every row start 16-byte aligned
+inline bool strides16(const int64_t* s, int count, int elem) {
+  for (int i = 0; i < count; ++i)
+    if (s[i] < 0 || ((s[i] * elem) & 15) != 0) return false;
+  return true;
+}
+
+int check_rows(const ma_rows* q) {
+  if (!q || !q->q) return MA_ERR_ARG;
+  if (!valid_dtype(q->dtype)) return MA_ERR_ARG;
+  if (q->B <= 0 || q->Hq <= 0 || q->T <= 0) return MA_ERR_ARG;
+  if (q->D != 64 && q->D != 128) return MA_ERR_UNSUPPORTED;
+  if (!aligned16(q->q) || !strides16(q->sq, 3, esize(q->dtype))) return MA_ERR_ARG;
+  return MA_OK;
+}
+
+int check_kv(const ma_kv* kv, int D) {
+  if (!kv) return MA_ERR_ARG;
+  if (kv->nq < 0 || kv->nf < 0) return MA_ERR_ARG;
+  if (!valid_dtype(kv->dtype)) return MA_ERR_ARG;
+  if (kv->nf > 0) {
+    if (!kv->kf || !kv->vf || !aligned16(kv->kf) || !aligned16(kv->vf)) return MA_ERR_ARG;
+    if (!strides16(kv->skf, 3, esize(kv->dtype)) || !strides16(kv->svf, 3, esize(kv->dtype))) return MA_ERR_ARG;
+  }
+  if (kv->layout == MA_KV_DENSE) {
+    if (kv->nq != 0) return MA_ERR_ARG;
+    return MA_OK;
+  }
+  if (kv->layout != MA_KV_PACKED_TOKEN && kv->layout != MA_KV_PACKED_CHANNEL) return MA_ERR_ARG;
+  if (kv->nq == 0) return MA_OK;
+  if (kv->vgroup <= 0 || (kv->vgroup % 8) != 0 || D % kv->vgroup) return MA_ERR_UNSUPPORTED;
+  if (!kv->vq || !kv->vs || !kv->vz || !kv->kq || !kv->ks || !kv->kz) return MA_ERR_ARG;
+  if (!aligned4(kv->vq) || !aligned4(kv->kq)) return MA_ERR_ARG;
+  for (int i = 0; i < 3; ++i)
+    if ((kv->svq[i] & 3) || (kv->skq[i] & 3) || kv->svq[i] < 0 || kv->skq[i] < 0 || kv->sks[i] < 0 ||
+        kv->svs[i] < 0)
+      return MA_ERR_ARG;
+  if (kv->layout == MA_KV_PACKED_TOKEN) {
+    if (!kv->kchan) return MA_ERR_ARG;
+  } else {
+    if (kv->kgroup <= 0 || (kv->kgroup % 2) != 0) return MA_ERR_UNSUPPORTED;
+    if (kv->nq % kv->kgroup) return MA_ERR_ARG;
+  }
+  return MA_OK;
+}
+
+int check_block(const ma_block* cur, const ma_rows* q, int H) {
+  if (!cur) return MA_ERR_ARG;
+  if (cur->Tc < 0) return MA_ERR_ARG;
+  if (cur->Tc == 0) return MA_OK;
+  if (!cur->k || !cur->v || !aligned16(cur->k) || !aligned16(cur->v)) return MA_ERR_ARG;
+  if (!strides16(cur->sk, 3, esize(q->dtype)) || !strides16(cur->sv, 3, esize(q->dtype))) return MA_ERR_ARG;
+  (void)H;
+  return MA_OK;
+}
+
+bool use_mma(const ma_rows& q, const ma_kv& kv) {
+  // bf16 queries over a bf16 (or bf16-dequantized packed) cache go to the tensor cores
+  return q.dtype == MA_BF16 && kv.dtype == MA_BF16 && q.D == 128;
+}
+
+struct Plan {
+  int nsplit;     // splits over the keys
+  int split_len;  // keys per split (a multiple of the key tile)
+  int S;          // partial slots per (b, h): nsplit (+1 for the current block)
+  int Rp;         // padded rows
+};
+
+int row_tile(bool mma) { return mma ? mma_row_tile() : simt_row_block(); }
+int key_tile(bool mma) { return mma ? mma_key_tile() : simt_key_tile(); }
+
+Plan plan_splits(int BH, int R, int n, int Tc, bool mma) {
+  Plan p;
+  const int rt = row_tile(mma), kt = key_tile(mma);
+  const int row_blocks = (R + rt - 1) / rt;
+  p.Rp = row_blocks * rt;
+  if (n <= 0) {
+    p.nsplit = 0;
+    p.split_len = kt;
+  } else {
+    const int sms = device_sm_count();
+    const int per_split = BH * row_blocks;
+    // tensor-core CTAs hold one SM each (registers, shared memory): one wave;
+    // the CUDA-core kernel fits several per SM: two waves
+    const int waves = mma ? 1 : 2;
+    int target = (waves * sms) / (per_split > 0 ? per_split : 1);
+    if (target < 1) target = 1;
+    const int max_splits = (n + kt - 1) / kt;
+    int ns = target < max_splits ? target : max_splits;
+    int len = (n + ns - 1) / ns;
+    len = ((len + kt - 1) / kt) * kt;
+    p.split_len = len;
+    p.nsplit = (n + len - 1) / len;
+  }
+  p.S = p.nsplit + (Tc > 0 ? 1 : 0);
+  if (p.S == 0) p.S = 1;
+  return p;
+}
+
+size_t attention_ws(int B, int H, int R, int n, int D, int Tc) {
+  size_t best = 0;
+  for (int m = 0; m < 2; ++m) {
+    const Plan p = plan_splits(B * H, R, n, Tc, m == 1);
+    const size_t bytes = partials_bytes(B * H, p.S, p.Rp, D) + 256;
+    if (bytes > best) best = bytes;
+  }
+  return best;
+}
+
+Partials carve_partials(void* ws, int BH, const Plan& p, int D) {
+  Partials P;
+  char* base = reinterpret_cast<char*>((reinterpret_cast<uintptr_t>(ws) + 255) & ~uintptr_t(255));
+  P.ml = reinterpret_cast<float2*>(base);
+  P.acc = reinterpret_cast<float*>(base + (size_t)BH * p.S * p.Rp * sizeof(float2));
+  P.S = p.S;
+  P.Rp = p.Rp;
+  (void)D;
+  return P;
+}
+
+// shared by the prefix and the read-set attention: partial pass + combine
+int run_attention(const ma_rows& q, const ma_kv& kv, int H, const ma_block& cur, float scale,
+                  int causal_block, int q_pos0, int c_pos0, const int64_t* idx, int64_t si0,
+                  int64_t si1, int n_keys, void* out, const int64_t so[3], float* m_p, float* l_p,
+                  float* o_p, void* ws, size_t ws_bytes, cudaStream_t st) {
+  const int G = q.Hq / H;
+  const int R = G * q.T;
+  const bool mma = use_mma(q, kv);
+  const Plan p = plan_splits(q.B * H, R, n_keys, cur.Tc, mma);
+  if (!ws || ws_bytes < partials_bytes(q.B * H, p.S, p.Rp, q.D) + 256) return MA_ERR_WORKSPACE;
+  const Partials P = carve_partials(ws, q.B * H, p, q.D);
+  int rc;
+  if (p.nsplit + (cur.Tc > 0 ? 1 : 0) > 0) {
+    rc = mma ? launch_attn_partial_mma(q, kv, H, cur, scale, causal_block, q_pos0, c_pos0, idx, si0, si1,
+                                       n_keys, p.split_len, p.nsplit, P, st)
+             : launch_attn_partial_simt(q, kv, H, cur, scale, causal_block, q_pos0, c_pos0, idx, si0,
+                                        si1, n_keys, p.split_len, p.nsplit, P, st);
+    if (rc != MA_OK) return rc;
+  }
+  return launch_attn_combine(q, H, P, p.nsplit, cur.Tc > 0, out, so, m_p, l_p, o_p, st);
+}
+
+}  // namespace
+
+extern "C" {
+
+int ma_version(void) { return (0 << 16) | 1; }
+
+const char* ma_status_string(int status) {
+  switch (status) {
+    case MA_OK: return "ok";
+    case MA_ERR_ARG: return "invalid argument";
+    case MA_ERR_UNSUPPORTED: return "unsupported configuration";
+    case MA_ERR_WORKSPACE: return "workspace missing or too small";
+    case MA_ERR_CUDA: return "CUDA error";
+    case MA_ERR_TIMEOUT: return "device-side wait timed out";
+    default: return "unknown status";
+  }
+}
+
+size_t ma_prefix_attention_workspace(int B, int H, int R, int n, int D, int Tc) {
+  if (B <= 0 || H <= 0 || R <= 0 || n < 0 || D <= 0 || Tc < 0) return 0;
+  return attention_ws(B, H, R, n, D, Tc);
+}
+
+int ma_prefix_attention(const ma_rows* q, const ma_kv* kv, int H, const ma_block* cur, float scale,
+                        int causal_block, int q_pos0, int c_pos0, void* out, const int64_t so[3],
+                        float* m_p, float* l_p, float* o_p, void* workspace, size_t workspace_bytes,
+                        void* stream) {
+  int rc = check_rows(q);
+  if (rc) return rc;
+  if (H <= 0 || q->Hq % H) return MA_ERR_ARG;
+  if ((rc = check_kv(kv, q->D))) return rc;
+  if ((rc = check_block(cur, q, H))) return rc;
+  if (!out || !so || !aligned16(out) || !strides16(so, 3, esize(q->dtype))) return MA_ERR_ARG;
+  if ((m_p == nullptr) != (l_p == nullptr)) return MA_ERR_ARG;
+  if (o_p && !aligned16(o_p)) return MA_ERR_ARG;
+  if (causal_block < 0) return MA_ERR_ARG;
+  if (kv->nq + kv->nf == 0 && cur->Tc == 0) return MA_ERR_ARG;
+  return run_attention(*q, *kv, H, *cur, scale, causal_block, q_pos0, c_pos0, nullptr, 0, 0,
+                       kv->nq + kv->nf, out, so, m_p, l_p, o_p, workspace, workspace_bytes,
+                       (cudaStream_t)stream);
+}
+
+int ma_prefix_mass(const ma_rows* q, const ma_kv* kv, int H, const int32_t* q_rows, int T2,
+                   const float* m_p, const float* l_p, float scale, float* mass, const int64_t smass[2],
+                   void* stream) {
+  int rc = check_rows(q);
+  if (rc) return rc;
+  if (H <= 0 || q->Hq % H) return MA_ERR_ARG;
+  if ((rc = check_kv(kv, q->D))) return rc;
+  if (!q_rows || T2 <= 0 || T2 > q->T || !m_p || !l_p || !mass || !smass) return MA_ERR_ARG;
+  if (smass[0] < 0 || smass[1] < 0) return MA_ERR_ARG;
+  return launch_prefix_mass(*q, *kv, H, q_rows, T2, m_p, l_p, scale, mass, smass[0], smass[1],
+                            (cudaStream_t)stream);
+}
+
+size_t ma_value_score_workspace(int B, int H, int n, int D) {
+  if (B <= 0 || H <= 0 || n < 0 || D <= 0) return 0;
+  return value_score_ws_bytes(B, H, n, D);
+}
+
+int ma_value_score(const ma_kv* kv, int B, int H, int D, const float* a, const int64_t sa[2],
+                   float* score, const int64_t sscore[2], void* workspace, size_t workspace_bytes,
+                   void* stream) {
+  if (B <= 0 || H <= 0) return MA_ERR_ARG;
+  if (D != 64 && D != 128) return MA_ERR_UNSUPPORTED;
+  int rc = check_kv(kv, D);
+  if (rc) return rc;
+  if (!a || !sa || !score || !sscore) return MA_ERR_ARG;
+  const int n = kv->nq + kv->nf;
+  if (!workspace || workspace_bytes < value_score_ws_bytes(B, H, n, D)) return MA_ERR_WORKSPACE;
+  if ((reinterpret_cast<uintptr_t>(workspace) & 255) != 0) return MA_ERR_WORKSPACE;
+  return launch_value_score(*kv, B, H, D, a, sa[0], sa[1], score, sscore[0], sscore[1], workspace,
+                            (cudaStream_t)stream);
+}
+
+int ma_select_topk(const float* score, int B, int H, int n, const int64_t sscore[2], const uint8_t* mask,
+                   int k, int64_t* indices, float* values, const int64_t sidx[2], void* stream) {
+  if (!score || !sscore || !indices || !sidx || B <= 0 || H <= 0 || n <= 0) return MA_ERR_ARG;
+  if (k < 0 || k > n) return MA_ERR_ARG;
+  if (k == 0) return MA_OK;
+  return launch_select_topk(score, B, H, n, sscore[0], sscore[1], mask, k, indices, values, sidx[0],
+                            sidx[1], (cudaStream_t)stream);
+}
+
+int ma_retain(const float* score, const int32_t* phys, int n_phys, const int32_t* pos, int lanes, int live,
+              int capacity, int recent_window, int sink_tokens, int64_t* keep, void* stream) {
+  if (!score || !pos || !keep || lanes <= 0 || live <= 0) return MA_ERR_ARG;
+  if (capacity <= 0 || capacity > live || recent_window < 0 || sink_tokens < 0) return MA_ERR_ARG;
+  if (phys && n_phys <= 0) return MA_ERR_ARG;
+  if (capacity > 16384 || live > 65536) return MA_ERR_UNSUPPORTED;
+  return launch_retain(score, phys, n_phys, pos, lanes, live, capacity, recent_window, sink_tokens, keep,
+                       (cudaStream_t)stream);
+}
+
+size_t ma_sparse_attention_workspace(int B, int H, int R, int k, int D, int Tc) {
+  if (B <= 0 || H <= 0 || R <= 0 || k < 0 || D <= 0 || Tc < 0) return 0;
+  return attention_ws(B, H, R, k, D, Tc);
+}
+
+int ma_sparse_attention(const ma_rows* q, const ma_kv* kv, int H, const int64_t* idx, int k,
+                        const int64_t sidx[2], const ma_block* cur, float scale, void* out,
+                        const int64_t so[3], void* workspace, size_t workspace_bytes, void* stream) {
+  int rc = check_rows(q);
+  if (rc) return rc;
+  if (H <= 0 || q->Hq % H) return MA_ERR_ARG;
+  if ((rc = check_kv(kv, q->D))) return rc;
+  if ((rc = check_block(cur, q, H))) return rc;
+  if (k < 0 || (k > 0 && (!idx || !sidx))) return MA_ERR_ARG;
+  if (k == 0 && cur->Tc == 0) return MA_ERR_ARG;
+  if (!out || !so || !aligned16(out) || !strides16(so, 3, esize(q->dtype))) return MA_ERR_ARG;
+  return run_attention(*q, *kv, H, *cur, scale, 0, 0, 0, idx, k ? sidx[0] : 0, k ? sidx[1] : 0, k, out,
+                       so, nullptr, nullptr, nullptr, workspace, workspace_bytes, (cudaStream_t)stream);
+}
+
+int ma_gather_kv(const ma_kv* kv, int B, int H, int D, const int64_t* idx, int k, const int64_t sidx[2],
+                 void* out_k, void* out_v, const int64_t sok[3], const int64_t sov[3], int32_t out_dtype,
+                 void* stream) {
+  if (B <= 0 || H <= 0 || k < 0) return MA_ERR_ARG;
+  if (D != 64 && D != 128) return MA_ERR_UNSUPPORTED;
+  int rc = check_kv(kv, D);
+  if (rc) return rc;
+  if (!valid_dtype(out_dtype)) return MA_ERR_ARG;
+  if (k > 0 && (!idx || !sidx || !out_k || !out_v || !sok || !sov)) return MA_ERR_ARG;
+  if (k > 0 && (!aligned16(out_k) || !aligned16(out_v) || !strides16(sok, 3, esize(out_dtype)) ||
+                !strides16(sov, 3, esize(out_dtype))))
+    return MA_ERR_ARG;
+  return launch_gather_kv(*kv, B, H, D, idx, k, k ? sidx[0] : 0, k ? sidx[1] : 0, out_k, out_v, sok, sov,
+                          out_dtype, (cudaStream_t)stream);
+}
+
+}  // extern "C"

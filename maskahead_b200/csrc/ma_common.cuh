@@ -1,0 +1,188 @@
+// Shared device code of the maskahead_b200 kernels: KV-layout readers, partial-result
+// layout, warp/block helpers. All kernels are written for sm_100a (B200).
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "../../include/maskahead_b200.h"
+
+namespace ma {
+
+constexpr int kMaxD = 128;
+
+// ----------------------------------------------------------------------------------
+// Element conversion
+// ----------------------------------------------------------------------------------
+__device__ __forceinline__ float bf16_round(float x) {
+  return __bfloat162float(__float2bfloat16_rn(x));
+}
+__device__ __forceinline__ float half_bits_to_float(uint16_t h) {
+  return __half2float(__ushort_as_half(h));
+}
+__device__ __forceinline__ void bf16x8_to_float(const uint4& u, float f[8]) {
+  const __nv_bfloat162* p = reinterpret_cast<const __nv_bfloat162*>(&u);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    float2 t = __bfloat1622float2(p[i]);
+    f[2 * i] = t.x;
+    f[2 * i + 1] = t.y;
+  }
+}
+__device__ __forceinline__ uint4 float8_to_bf16x8(const float f[8]) {
+  uint4 u;
+  __nv_bfloat162* p = reinterpret_cast<__nv_bfloat162*>(&u);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) p[i] = __floats2bfloat162_rn(f[2 * i], f[2 * i + 1]);
+  return u;
+}
+
+// ----------------------------------------------------------------------------------
+// Query / output element access ([B,Hq,T,D] with strides over b, hq, t)
+// ----------------------------------------------------------------------------------
+template <typename T>
+__device__ __forceinline__ void load8(const T* p, float f[8]);
+template <>
+__device__ __forceinline__ void load8<float>(const float* p, float f[8]) {
+  float4 a = *reinterpret_cast<const float4*>(p);
+  float4 b = *reinterpret_cast<const float4*>(p + 4);
+  f[0] = a.x; f[1] = a.y; f[2] = a.z; f[3] = a.w;
+  f[4] = b.x; f[5] = b.y; f[6] = b.z; f[7] = b.w;
+}
+template <>
+__device__ __forceinline__ void load8<__nv_bfloat16>(const __nv_bfloat16* p, float f[8]) {
+  bf16x8_to_float(*reinterpret_cast<const uint4*>(p), f);
+}
+
+template <typename T>
+__device__ __forceinline__ void store4(T* p, float a, float b, float c, float d);
+template <>
+__device__ __forceinline__ void store4<float>(float* p, float a, float b, float c, float d) {
+  *reinterpret_cast<float4*>(p) = make_float4(a, b, c, d);
+}
+template <>
+__device__ __forceinline__ void store4<__nv_bfloat16>(__nv_bfloat16* p, float a, float b, float c,
+                                                      float d) {
+  __nv_bfloat162 x = __floats2bfloat162_rn(a, b);
+  __nv_bfloat162 y = __floats2bfloat162_rn(c, d);
+  uint2 u;
+  u.x = *reinterpret_cast<uint32_t*>(&x);
+  u.y = *reinterpret_cast<uint32_t*>(&y);
+  *reinterpret_cast<uint2*>(p) = u;
+}
+
+// ----------------------------------------------------------------------------------
+// KV reader: 8 consecutive channels [8*c8, 8*c8+8) of slot j of (b, h), dequantized.
+// Packed codes are rounded to the tail dtype (bf16 in every shipped configuration), as
+// the reference dequantizes the cache to its compute dtype before attending.
+// ----------------------------------------------------------------------------------
+// Slot j exists (0 <= j < nq + nf) and is live. Slots outside the prefix (a bad index
+// in a caller's read set) read as dead, so no kernel ever addresses outside the cache.
+__device__ __forceinline__ bool kv_live(const ma_kv& kv, int H, int b, int h, int j) {
+  const int64_t n = (int64_t)kv.nq + kv.nf;
+  if (j < 0 || j >= n) return false;
+  if (kv.mask == nullptr) return true;
+  return kv.mask[((int64_t)b * H + h) * n + j] != 0;
+}
+
+__device__ __forceinline__ void dequant8_token(const uint8_t* payload, uint16_t scale_bits,
+                                               uint16_t zero_bits, float f[8]) {
+  // 4 bytes = 8 codes; element 2i is the low nibble of byte i (reference.py:41-45)
+  const uint32_t w = *reinterpret_cast<const uint32_t*>(payload);
+  const float s = half_bits_to_float(scale_bits);
+  const float z = half_bits_to_float(zero_bits);
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const uint32_t code = (w >> (4 * i)) & 0xFu;
+    f[i] = fmaf((float)code, s, z);
+  }
+}
+
+template <bool KEY>
+__device__ __forceinline__ void kv_read8(const ma_kv& kv, int b, int h, int j, int c8, float f[8]) {
+  const int d0 = 8 * c8;
+  if (j >= kv.nq) {  // dense slot (the whole prefix for MA_KV_DENSE, else the tail)
+    const int jt = j - kv.nq;
+    const int64_t* s = KEY ? kv.skf : kv.svf;
+    const int64_t off = (int64_t)b * s[0] + (int64_t)h * s[1] + (int64_t)jt * s[2] + d0;
+    if (kv.dtype == MA_BF16) {
+      load8(reinterpret_cast<const __nv_bfloat16*>(KEY ? kv.kf : kv.vf) + off, f);
+    } else {
+      load8(reinterpret_cast<const float*>(KEY ? kv.kf : kv.vf) + off, f);
+    }
+    return;
+  }
+  const bool round_bf16 = kv.dtype == MA_BF16;
+  if (!KEY || kv.layout == MA_KV_PACKED_TOKEN) {
+    const uint8_t* q = KEY ? kv.kq : kv.vq;
+    const uint16_t* sc = KEY ? kv.ks : kv.vs;
+    const uint16_t* zp = KEY ? kv.kz : kv.vz;
+    const int64_t* sq = KEY ? kv.skq : kv.svq;
+    const int64_t* ss = KEY ? kv.sks : kv.svs;
+    const int g = d0 / kv.vgroup;
+    const int64_t qo = (int64_t)b * sq[0] + (int64_t)h * sq[1] + (int64_t)j * sq[2] + d0 / 2;
+    const int64_t so = (int64_t)b * ss[0] + (int64_t)h * ss[1] + (int64_t)j * ss[2] + g;
+    dequant8_token(q + qo, sc[so], zp[so], f);
+    if (KEY) {
+      const float* kc = kv.kchan + (int64_t)b * kv.skc[0] + (int64_t)h * kv.skc[1] + d0;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) f[i] *= kc[i];
+    }
+  } else {  // KIVI channel-mode keys: one scale/zero per (token group, channel)
+    const int gi = j / kv.kgroup;
+    const int ti = j - gi * kv.kgroup;
+    const int bytes_per_ch = kv.kgroup / 2;
+    const uint8_t* base = kv.kq + (int64_t)b * kv.skq[0] + (int64_t)h * kv.skq[1] +
+                          (int64_t)gi * kv.skq[2];
+    const int64_t so = (int64_t)b * kv.sks[0] + (int64_t)h * kv.sks[1] + (int64_t)gi * kv.sks[2];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const int d = d0 + i;
+      const uint32_t byte = base[(int64_t)d * bytes_per_ch + ti / 2];
+      const uint32_t code = (ti & 1) ? (byte >> 4) : (byte & 0xFu);
+      f[i] = fmaf((float)code, half_bits_to_float(kv.ks[so + d]), half_bits_to_float(kv.kz[so + d]));
+    }
+  }
+  if (round_bf16) {
+#pragma unroll
+    for (int i = 0; i < 8; ++i) f[i] = bf16_round(f[i]);
+  }
+}
+
+// ----------------------------------------------------------------------------------
+// Split-K partial results: per (b*H + h, split, row) a pair (m, l) and acc[D], fp32.
+// ----------------------------------------------------------------------------------
+struct Partials {
+  float2* ml;   // [BH][S][Rp]
+  float* acc;   // [BH][S][Rp][D]
+  int S;        // splits (the current block, when present, is the last one)
+  int Rp;       // padded rows
+};
+
+__host__ __device__ inline size_t partials_bytes(int BH, int S, int Rp, int D) {
+  return (size_t)BH * S * Rp * (sizeof(float2) + sizeof(float) * D);
+}
+
+// ----------------------------------------------------------------------------------
+// Warp / block helpers
+// ----------------------------------------------------------------------------------
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+
+// fp32 -> uint32 with the same order (-inf < ... < +inf); dead slots use key 0.
+__device__ __forceinline__ uint32_t order_key(float x) {
+  uint32_t u = __float_as_uint(x);
+  return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+
+}  // namespace ma

@@ -1,0 +1,52 @@
+// Internal launcher declarations shared by the kernel translation units and the C ABI.
+#pragma once
+
+#include "ma_common.cuh"
+
+namespace ma {
+
+// ma_attention_simt.cu
+int launch_attn_partial_simt(const ma_rows& q, const ma_kv& kv, int H, const ma_block& cur,
+                             float scale, int causal_block, int q_pos0, int c_pos0,
+                             const int64_t* idx, int64_t si0, int64_t si1, int n_keys,
+                             int split_len, int nsplit, const Partials& P, cudaStream_t st);
+int simt_row_block();
+int simt_key_tile();
+
+// ma_attention_mma.cu (bf16 queries and caches, tensor cores)
+int launch_attn_partial_mma(const ma_rows& q, const ma_kv& kv, int H, const ma_block& cur,
+                            float scale, int causal_block, int q_pos0, int c_pos0,
+                            const int64_t* idx, int64_t si0, int64_t si1, int n_keys,
+                            int split_len, int nsplit, const Partials& P, cudaStream_t st);
+int mma_row_tile();
+int mma_key_tile();
+
+// ma_combine.cu
+int launch_attn_combine(const ma_rows& q, int H, const Partials& P, int nsplit, bool has_cur,
+                        void* out, const int64_t so[3], float* m_p, float* l_p, float* o_p,
+                        cudaStream_t st);
+
+// ma_score.cu
+int launch_prefix_mass(const ma_rows& q, const ma_kv& kv, int H, const int32_t* q_rows, int T2,
+                       const float* m_p, const float* l_p, float scale, float* mass,
+                       int64_t sm0, int64_t sm1, cudaStream_t st);
+size_t value_score_ws_bytes(int B, int H, int n, int D);
+int launch_value_score(const ma_kv& kv, int B, int H, int D, const float* a, int64_t sa0,
+                       int64_t sa1, float* score, int64_t ss0, int64_t ss1, void* ws,
+                       cudaStream_t st);
+
+// ma_select.cu
+int launch_select_topk(const float* score, int B, int H, int n, int64_t ss0, int64_t ss1,
+                       const uint8_t* mask, int k, int64_t* indices, float* values, int64_t si0,
+                       int64_t si1, cudaStream_t st);
+int launch_retain(const float* score, const int32_t* phys, int n_phys, const int32_t* pos,
+                  int lanes, int live, int capacity, int recent_window, int sink_tokens,
+                  int64_t* keep, cudaStream_t st);
+int launch_gather_kv(const ma_kv& kv, int B, int H, int D, const int64_t* idx, int k, int64_t si0,
+                     int64_t si1, void* out_k, void* out_v, const int64_t sok[3],
+                     const int64_t sov[3], int out_dtype, cudaStream_t st);
+
+// device properties, cached per device
+int device_sm_count();
+
+}  // namespace ma

@@ -1,0 +1,310 @@
+// Selection kernels: the per-head top-k read set and the lookahead retained set, plus
+// the indexed gather of dequantized rows.
+//
+// Top-k is a block-wide MSB-first radix select on order-preserving uint32 keys (four
+// 8-bit digits, shared-memory histograms), followed by an index-order compaction, so
+// the read set comes out already sorted ascending (the reference sorts after
+// torch.topk: src/maskahead/kernels/ops.py:377-380, 509-516). Ties at the k-th score
+// go to the lower slot index.
+#include "ma_kernels.cuh"
+
+namespace ma {
+
+namespace {
+
+constexpr int kSelThreads = 1024;
+
+// Exclusive block-wide prefix sum over one int per thread (blockDim.x == 1024).
+__device__ __forceinline__ int block_exclusive_scan(int v, int* sWarp, int& total) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  int x = v;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int y = __shfl_up_sync(0xffffffffu, x, o);
+    if (lane >= o) x += y;
+  }
+  if (lane == 31) sWarp[warp] = x;
+  __syncthreads();
+  if (warp == 0) {
+    int w = sWarp[lane];
+    int wx = w;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int y = __shfl_up_sync(0xffffffffu, wx, o);
+      if (lane >= o) wx += y;
+    }
+    sWarp[lane] = wx - w;       // exclusive prefix of warp totals
+    if (lane == 31) sWarp[32] = wx;
+  }
+  __syncthreads();
+  const int res = sWarp[warp] + x - v;
+  total = sWarp[32];
+  __syncthreads();
+  return res;
+}
+
+struct KthResult {
+  uint32_t key;   // the k-th largest key
+  int need;       // how many keys equal to `key` belong to the top k
+};
+
+// k-th largest of n keys (1 <= k <= n); key(j) must be cheap and pure.
+template <class KeyFn>
+__device__ KthResult radix_kth(KeyFn key, int n, int k, unsigned* sHist, int* sSel) {
+  uint32_t prefix = 0, mask = 0;
+  int kk = k;
+  for (int pass = 0; pass < 4; ++pass) {
+    const int shift = 24 - 8 * pass;
+    for (int i = threadIdx.x; i < 256; i += blockDim.x) sHist[i] = 0u;
+    __syncthreads();
+    for (int j = threadIdx.x; j < n; j += blockDim.x) {
+      const uint32_t x = key(j);
+      if ((x & mask) == prefix) atomicAdd(&sHist[(x >> shift) & 255u], 1u);
+    }
+    __syncthreads();
+    if (threadIdx.x < 32) {
+      // lane l owns digits 255-8l .. 248-8l (descending order)
+      const int lane = threadIdx.x;
+      int c[8];
+      int loc = 0;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        c[i] = (int)sHist[255 - (lane * 8 + i)];
+        loc += c[i];
+      }
+      int incl = loc;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int y = __shfl_up_sync(0xffffffffu, incl, o);
+        if (lane >= o) incl += y;
+      }
+      int cum = incl - loc;  // keys with a larger digit than this lane's first digit
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        if (cum < kk && cum + c[i] >= kk) {
+          sSel[0] = 255 - (lane * 8 + i);
+          sSel[1] = cum;
+        }
+        cum += c[i];
+      }
+    }
+    __syncthreads();
+    prefix |= (uint32_t)sSel[0] << shift;
+    mask |= 255u << shift;
+    kk -= sSel[1];
+    __syncthreads();
+  }
+  return KthResult{prefix, kk};
+}
+
+// Write, in increasing j, every j whose key is above the threshold plus the first
+// `need` ties; calls emit(rank, j) with rank the output position.
+template <class KeyFn, class EmitFn>
+__device__ void emit_selected(KeyFn key, int n, KthResult th, int* sWarp, EmitFn emit) {
+  const int per = (n + blockDim.x - 1) / blockDim.x;
+  const int lo = min(n, (int)threadIdx.x * per), hi = min(n, lo + per);
+  int gt = 0, eq = 0;
+  for (int j = lo; j < hi; ++j) {
+    const uint32_t x = key(j);
+    gt += x > th.key;
+    eq += x == th.key;
+  }
+  int tot;
+  const int eq_before = block_exclusive_scan(eq, sWarp, tot);
+  const int take = max(0, min(eq, th.need - eq_before));
+  int off = block_exclusive_scan(gt + take, sWarp, tot);
+  int taken = 0;
+  for (int j = lo; j < hi; ++j) {
+    const uint32_t x = key(j);
+    if (x > th.key || (x == th.key && taken < take)) {
+      if (x == th.key) ++taken;
+      emit(off++, j);
+    }
+  }
+}
+
+__global__ void __launch_bounds__(kSelThreads)
+select_topk_kernel(const float* __restrict__ score, int H, int n, int64_t ss0, int64_t ss1,
+                   const uint8_t* __restrict__ mask, int k, int64_t* __restrict__ indices,
+                   float* __restrict__ values, int64_t si0, int64_t si1) {
+  __shared__ unsigned sHist[256];
+  __shared__ int sSel[2];
+  __shared__ int sWarp[33];
+  const int bh = blockIdx.x;
+  const int b = bh / H, h = bh - (bh / H) * H;
+  const float* s = score + (int64_t)b * ss0 + (int64_t)h * ss1;
+  const uint8_t* m = mask ? mask + (int64_t)bh * n : nullptr;
+  auto key = [&](int j) -> uint32_t {
+    if (m && m[j] == 0) return 0u;
+    return order_key(s[j]);
+  };
+  const KthResult th = radix_kth(key, n, k, sHist, sSel);
+  int64_t* oi = indices + (int64_t)b * si0 + (int64_t)h * si1;
+  float* ov = values ? values + (int64_t)b * si0 + (int64_t)h * si1 : nullptr;
+  emit_selected(key, n, th, sWarp, [&](int r, int j) {
+    oi[r] = j;
+    if (ov) ov[r] = s[j];
+  });
+}
+
+// Lookahead survivors of one lane (eviction.py:364-409): recent window by position,
+// sinks at +inf, window excluded from the score contest, union ordered by position.
+__global__ void __launch_bounds__(kSelThreads)
+retain_kernel(const float* __restrict__ score, const int32_t* __restrict__ phys, int n_phys,
+              const int32_t* __restrict__ pos, int live, int capacity, int W, int sinks,
+              int64_t* __restrict__ keep, int sort_cap) {
+  extern __shared__ unsigned char smem[];
+  unsigned long long* sSort = reinterpret_cast<unsigned long long*>(smem);   // [sort_cap]
+  unsigned char* sRecent = smem + (size_t)sort_cap * sizeof(unsigned long long);  // [live]
+  __shared__ unsigned sHist[256];
+  __shared__ int sSel[2];
+  __shared__ int sWarp[33];
+  const int lane_id = blockIdx.x;
+  const int32_t* p = pos + (int64_t)lane_id * live;
+  const float* sc = phys ? score + (int64_t)lane_id * n_phys : score + (int64_t)lane_id * live;
+  const int32_t* ph = phys ? phys + (int64_t)lane_id * live : nullptr;
+
+  for (int i = threadIdx.x; i < live; i += blockDim.x) sRecent[i] = 0;
+  __syncthreads();
+  if (W > 0) {
+    auto pkey = [&](int i) -> uint32_t { return (uint32_t)p[i] ^ 0x80000000u; };
+    const KthResult th = radix_kth(pkey, live, W, sHist, sSel);
+    emit_selected(pkey, live, th, sWarp, [&](int, int i) { sRecent[i] = 1; });
+    __syncthreads();
+  }
+  const int rest = capacity - W;
+  const uint32_t kInf = 0xFF800000u;  // order_key(+inf)
+  auto rkey = [&](int i) -> uint32_t {
+    if (sRecent[i]) return 0u;
+    if (p[i] < sinks) return kInf;
+    if (ph) {
+      const int slot = ph[i];
+      return (slot >= 0 && slot < n_phys) ? order_key(sc[slot]) : 0u;  // bad slot: never kept by score
+    }
+    return order_key(sc[i]);
+  };
+  // union, in live-index order, as (position, index) sort keys
+  auto ukey = [&](int i) -> unsigned long long {
+    return ((unsigned long long)((uint32_t)p[i] ^ 0x80000000u) << 32) | (unsigned)i;
+  };
+  if (rest > 0) {
+    const KthResult th = radix_kth(rkey, live, rest, sHist, sSel);
+    // mark extras in sRecent with value 2 (keeps window entries at 1)
+    emit_selected(rkey, live, th, sWarp, [&](int, int i) { sRecent[i] = 2; });
+    __syncthreads();
+  }
+  // compact the kept set in index order
+  const int per = (live + blockDim.x - 1) / blockDim.x;
+  const int lo = min(live, (int)threadIdx.x * per), hi = min(live, lo + per);
+  int cnt = 0;
+  for (int i = lo; i < hi; ++i) cnt += sRecent[i] != 0;
+  int tot;
+  int off = block_exclusive_scan(cnt, sWarp, tot);
+  for (int i = lo; i < hi; ++i)
+    if (sRecent[i]) sSort[off++] = ukey(i);
+  for (int i = tot + threadIdx.x; i < sort_cap; i += blockDim.x) sSort[i] = ~0ull;
+  __syncthreads();
+  // bitonic sort by position (already sorted when the live axis is, as the reference keeps it)
+  for (int size = 2; size <= sort_cap; size <<= 1) {
+    for (int stride = size >> 1; stride > 0; stride >>= 1) {
+      for (int i = threadIdx.x; i < sort_cap; i += blockDim.x) {
+        const int j = i ^ stride;
+        if (j > i) {
+          const bool up = (i & size) == 0;
+          const unsigned long long a = sSort[i], c = sSort[j];
+          if ((a > c) == up) {
+            sSort[i] = c;
+            sSort[j] = a;
+          }
+        }
+      }
+      __syncthreads();
+    }
+  }
+  int64_t* out = keep + (int64_t)lane_id * capacity;
+  for (int i = threadIdx.x; i < capacity; i += blockDim.x) out[i] = (int64_t)(sSort[i] & 0xffffffffull);
+}
+
+constexpr int kGatherTok = 32;
+
+template <typename OT>
+__global__ void gather_kv_kernel(ma_kv kv, int H, int D, const int64_t* __restrict__ idx, int k,
+                                 int64_t si0, int64_t si1, OT* __restrict__ ok_,
+                                 OT* __restrict__ ov_, int64_t sok0, int64_t sok1, int64_t sok2,
+                                 int64_t sov0, int64_t sov1, int64_t sov2) {
+  const int bh = blockIdx.y;
+  const int b = bh / H, h = bh - (bh / H) * H;
+  const int chunks = D / 8;
+  const int i0 = blockIdx.x * kGatherTok;
+  for (int c = threadIdx.x; c < kGatherTok * chunks; c += blockDim.x) {
+    const int ii = c / chunks, c8 = c - (c / chunks) * chunks;
+    const int i = i0 + ii;
+    if (i >= k) continue;
+    const int64_t slot64 = idx[(int64_t)b * si0 + (int64_t)h * si1 + i];
+    const int slot = (int)slot64;
+    float fk[8], fv[8];
+    if (slot64 >= 0 && slot64 < (int64_t)kv.nq + kv.nf) {
+      kv_read8<true>(kv, b, h, slot, c8, fk);
+      kv_read8<false>(kv, b, h, slot, c8, fv);
+    } else {  // a slot outside the prefix gathers zeros
+#pragma unroll
+      for (int e = 0; e < 8; ++e) fk[e] = fv[e] = 0.f;
+    }
+    OT* dk = ok_ + (int64_t)b * sok0 + (int64_t)h * sok1 + (int64_t)i * sok2 + 8 * c8;
+    OT* dv = ov_ + (int64_t)b * sov0 + (int64_t)h * sov1 + (int64_t)i * sov2 + 8 * c8;
+    store4(dk, fk[0], fk[1], fk[2], fk[3]);
+    store4(dk + 4, fk[4], fk[5], fk[6], fk[7]);
+    store4(dv, fv[0], fv[1], fv[2], fv[3]);
+    store4(dv + 4, fv[4], fv[5], fv[6], fv[7]);
+  }
+}
+
+}  // namespace
+
+int launch_select_topk(const float* score, int B, int H, int n, int64_t ss0, int64_t ss1,
+                       const uint8_t* mask, int k, int64_t* indices, float* values, int64_t si0,
+                       int64_t si1, cudaStream_t st) {
+  select_topk_kernel<<<B * H, kSelThreads, 0, st>>>(score, H, n, ss0, ss1, mask, k, indices, values,
+                                                    si0, si1);
+  return cudaGetLastError() == cudaSuccess ? MA_OK : MA_ERR_CUDA;
+}
+
+int retain_sort_cap(int capacity) {
+  int c = 1;
+  while (c < capacity) c <<= 1;
+  return c;
+}
+
+int launch_retain(const float* score, const int32_t* phys, int n_phys, const int32_t* pos,
+                  int lanes, int live, int capacity, int recent_window, int sink_tokens,
+                  int64_t* keep, cudaStream_t st) {
+  const int cap = retain_sort_cap(capacity);
+  const size_t smem = (size_t)cap * sizeof(unsigned long long) + (((size_t)live + 15) / 16) * 16;
+  if (smem > 200 * 1024) return MA_ERR_UNSUPPORTED;
+  if (cudaFuncSetAttribute(retain_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
+      cudaSuccess)
+    return MA_ERR_CUDA;
+  const int W = recent_window < capacity ? recent_window : capacity;
+  retain_kernel<<<lanes, kSelThreads, smem, st>>>(score, phys, n_phys, pos, live, capacity, W,
+                                                  sink_tokens, keep, cap);
+  return cudaGetLastError() == cudaSuccess ? MA_OK : MA_ERR_CUDA;
+}
+
+int launch_gather_kv(const ma_kv& kv, int B, int H, int D, const int64_t* idx, int k, int64_t si0,
+                     int64_t si1, void* out_k, void* out_v, const int64_t sok[3],
+                     const int64_t sov[3], int out_dtype, cudaStream_t st) {
+  if (k == 0) return MA_OK;
+  dim3 grid((k + kGatherTok - 1) / kGatherTok, B * H);
+  if (out_dtype == MA_F32) {
+    gather_kv_kernel<float><<<grid, 256, 0, st>>>(kv, H, D, idx, k, si0, si1, (float*)out_k,
+                                                  (float*)out_v, sok[0], sok[1], sok[2], sov[0],
+                                                  sov[1], sov[2]);
+  } else {
+    gather_kv_kernel<__nv_bfloat16><<<grid, 256, 0, st>>>(
+        kv, H, D, idx, k, si0, si1, (__nv_bfloat16*)out_k, (__nv_bfloat16*)out_v, sok[0], sok[1],
+        sok[2], sov[0], sov[1], sov[2]);
+  }
+  return cudaGetLastError() == cudaSuccess ? MA_OK : MA_ERR_CUDA;
+}
+
+}  // namespace ma

@@ -1,0 +1,160 @@
+"""Session-level hot path: step 0, sparse sub-steps and lookahead retention.
+
+These functions are what the reference session's fast path does per layer
+(src/maskahead/runtime/session.py), written against the sm_100a operators:
+
+  fast_step0          _fast_step0 (1403-1454): dense attention over [live prefix |
+                      block], the block's prefix mass, the value-aware score and the
+                      ascending top-k read set -- without the gather: sub-steps read the
+                      selected slots straight from the cache.
+  compact_attention   _compact_attention / sdpa_compact (1286-1336; reference.py:403-426):
+                      attention over [read set | block].
+  probe_attention     the lookahead probe (2317-2332): block-causal attention of the probe
+                      forward plus the prefix mass of the probe rows.
+  value_score         value_score (27-40) with the fp32 centre.
+  lookahead_survivors EvictionState.survivors for the lookahead policy (eviction.py:364-409).
+"""
+
+from __future__ import annotations
+
+from dataclasses import dataclass
+
+import torch
+
+from . import _lib
+from .kernels._common import block_struct, rows_struct
+from .kernels.ops import select_topk_indices
+from .kernels.splitk import prefix_scores, splitk_attention
+from .layouts import Prefix, as_prefix, kv_descriptor
+
+__all__ = ["Step0Result", "fast_step0", "compact_attention", "probe_attention", "value_score",
+           "lookahead_survivors"]
+
+
+@dataclass(slots=True)
+class Step0Result:
+    out: torch.Tensor                    # [B, Hq, T, D] attention output
+    indices: torch.Tensor | None         # [B, Hkv, k] ascending read set (None: dense layer)
+    mass: torch.Tensor | None            # [B, Hkv, n] prefix mass of the selection rows
+    score: torch.Tensor | None           # [B, Hkv, n] value-aware score (value_aware only)
+
+
+def fast_step0(query: torch.Tensor, prefix, current_key: torch.Tensor, current_value: torch.Tensor, *,
+               query_indices, topk: int, value_aware: bool = True, scaling: float | None = None,
+               select: bool = True, want_mass: bool = False) -> Step0Result:
+    """Step 0 of one layer: attention output, mass, score and the read set (session.py:1403-1454).
+
+    The read set is the top min(topk, live) slots by score (value_aware) or mass, dead
+    slots never chosen, as ascending slot indices.
+    """
+    prefix = as_prefix(prefix)
+    if prefix.n == 0:
+        out, _ = splitk_attention(query, prefix, current_key, current_value, scaling=scaling)
+        return Step0Result(out, None, None, None)
+    need_stats = select or want_mass
+    out, stats = splitk_attention(query, prefix, current_key, current_value, scaling=scaling,
+                                  want_prefix=need_stats)
+    if not need_stats:
+        return Step0Result(out, None, None, None)
+    value = select and value_aware
+    mass, score = prefix_scores(query, prefix, stats, query_indices, value=value, scaling=scaling)
+    idx = None
+    if select:
+        live = prefix.n if prefix.mask is None else None
+        k = int(topk) if live is None else min(int(topk), live)
+        rank = score if value else mass
+        idx, _ = select_topk_indices(rank, k, prefix.mask, want_values=False)
+    return Step0Result(out, idx, mass, score)
+
+
+def compact_attention(query: torch.Tensor, prefix, indices: torch.Tensor, current_key: torch.Tensor,
+                      current_value: torch.Tensor, *, scaling: float | None = None) -> torch.Tensor:
+    """Attention of every query row over [prefix[indices] | current block] (sdpa_compact
+    over the gathered read set, session.py:1286-1336), reading the selected slots
+    directly from the (packed or dense) cache."""
+    lib = _lib.lib()
+    prefix = as_prefix(prefix)
+    b, hq, t, d = query.shape
+    hkv = current_key.shape[1]
+    desc = kv_descriptor(Prefix(**{s: getattr(prefix, s) for s in Prefix.__slots__ if s != "mask"}),
+                         batch=b, heads=hkv, head_dim=d)
+    rows, qkeep = rows_struct(query)
+    cur, ckeep = block_struct(current_key, current_value, query.dtype)
+    idx = indices if indices.dtype == torch.int64 and indices.stride(-1) == 1 else indices.to(torch.int64).contiguous()
+    k = idx.shape[2]
+    out = torch.empty_like(query)
+    nbytes = lib.ma_sparse_attention_workspace(b, hkv, (hq // hkv) * t, k, d, cur.Tc)
+    ws = _lib.workspace(query.device, "attention", nbytes)
+    scale = float(scaling if scaling is not None else d ** -0.5)
+    _lib.check("ma_sparse_attention", lib.ma_sparse_attention(
+        rows, desc.kv, hkv, idx.data_ptr(), k, _lib.i64(idx.stride(0), idx.stride(1)), cur, scale,
+        out.data_ptr(), _lib.i64(*out.stride()[:3]), ws.data_ptr(), ws.numel(),
+        _lib.stream_handle(query.device)))
+    del qkeep, ckeep
+    return out
+
+
+def probe_attention(query: torch.Tensor, prefix, current_key: torch.Tensor, current_value: torch.Tensor, *,
+                    block_size: int = 32, scaling: float | None = None, probe_rows: torch.Tensor | None = None):
+    """Lookahead probe of one layer (session.py:2317-2332): block-causal attention of the
+    probe forward [block k+1 | probe blocks] over [live prefix | itself], and the prefix
+    mass of the probe rows (positions block_size..T) times the number of probe blocks.
+    probe_rows: those positions as a device int32 tensor (optional; avoids a host copy,
+    e.g. under CUDA-graph capture)."""
+    t = query.shape[2]
+    out, stats = splitk_attention(query, prefix, current_key, current_value, scaling=scaling,
+                                  causal_block=block_size, q_pos0=0, c_pos0=0, want_prefix=True)
+    rows = probe_rows if probe_rows is not None else list(range(block_size, t))
+    if len(rows) == 0:
+        return out, None
+    mass, _ = prefix_scores(query, prefix, stats, rows, value=False, scaling=scaling)
+    return out, mass * max(1, (t - block_size) // block_size)
+
+
+def value_score(a: torch.Tensor, v: torch.Tensor, live_mask: torch.Tensor | None = None) -> torch.Tensor:
+    """a_i * ||v_i - c||, c = sum_j a_j v_j / max(sum_j a_j, 1e-12), fp32 (session.py:27-40).
+
+    a [..., n], v [..., n, D] (float32 or bfloat16). Dead slots (live_mask False) are left
+    out of the centre and score 0.
+    """
+    lib = _lib.lib()
+    lead = a.shape[:-1]
+    n, d = v.shape[-2], v.shape[-1]
+    a3 = a.reshape(-1, 1, n).to(torch.float32).contiguous()
+    v4 = v.reshape(-1, 1, n, d)
+    if v4.stride(-1) != 1:
+        v4 = v4.contiguous()
+    mask = None if live_mask is None else live_mask.reshape(-1, 1, n)
+    desc = kv_descriptor(Prefix.dense(v4, v4, mask=mask))
+    bb = a3.shape[0]
+    score = torch.empty_like(a3)
+    nbytes = lib.ma_value_score_workspace(bb, 1, n, d)
+    ws = _lib.workspace(a.device, "value_score", nbytes)
+    _lib.check("ma_value_score", lib.ma_value_score(
+        desc.kv, bb, 1, d, a3.data_ptr(), _lib.i64(a3.stride(0), a3.stride(1)), score.data_ptr(),
+        _lib.i64(score.stride(0), score.stride(1)), ws.data_ptr(), ws.numel(), _lib.stream_handle(a.device)))
+    return score.reshape(*lead, n)
+
+
+def lookahead_survivors(pos: torch.Tensor, score: torch.Tensor, capacity: int, *, recent_window: int,
+                        sink_tokens: int = 0, phys: torch.Tensor | None = None) -> torch.Tensor:
+    """Live-axis indices to keep [L, B, H, capacity] int64, ordered by position.
+
+    pos [L,B,H,live] int; score [L,B,H,live] fp32 (or per physical slot [L,B,H,n_phys]
+    with phys [L,B,H,live] the slot of each live entry). Keeps the
+    W = min(recent_window, capacity) newest, the sinks (pos < sink_tokens) and the best
+    remaining entries by score (eviction.py:364-409).
+    """
+    lib = _lib.lib()
+    live = pos.shape[-1]
+    lanes = pos.numel() // live if live else 0
+    if capacity > live:
+        raise ValueError(f"capacity {capacity} exceeds the live set {live}")
+    p = pos.to(torch.int32).contiguous()
+    s = score.to(torch.float32).contiguous()
+    ph = None if phys is None else phys.to(torch.int32).contiguous()
+    keep = torch.empty((*pos.shape[:-1], capacity), device=pos.device, dtype=torch.int64)
+    _lib.check("ma_retain", lib.ma_retain(
+        s.data_ptr(), _lib.ptr(ph), int(s.shape[-1]) if ph is not None else 0, p.data_ptr(), lanes, live,
+        int(capacity), int(recent_window), int(sink_tokens), keep.data_ptr(), _lib.stream_handle(pos.device)))
+    return keep

@@ -1,0 +1,127 @@
+"""Split-K attention over [prefix | current block] and the prefix scores, on sm_100a.
+
+Drop-in counterparts of src/maskahead/kernels/splitk.py in the reference:
+
+    out, stats = splitk_attention(q, prefix, kc, vc, want_prefix=True)
+    mass, score = prefix_scores(q, prefix, stats, q_rows, value=True)
+
+Same signatures and return shapes. The reference's tuning keywords (block sizes,
+dequantization thresholds) are accepted and ignored: there is one kernel family. O_p is
+returned in fp32. The value score's centre is c = sum_j a_j v_j / sum_j a_j in fp32
+over the live slots (session.py:27-40 with the fp32 centre), which equals the mean of
+O_p over the selection rows that the reference uses (splitk.py:600-601).
+"""
+
+from __future__ import annotations
+
+import torch
+
+from .. import _lib
+from ..layouts import Prefix, as_prefix, kv_descriptor
+from ._common import block_struct, rows_struct
+
+__all__ = ["Prefix", "splitk_attention", "prefix_scores", "dequantize_prefix"]
+
+
+def splitk_attention(query, prefix, current_key, current_value, *, scaling=None,
+                     causal_block: int = 0, q_pos0: int = 0, c_pos0: int = 0, want_prefix: bool = False,
+                     **_tuning):
+    """softmax over [prefix | current] for every query row (splitk.py:493-579).
+
+    Returns (out [B,Hq,T,D] in the query dtype, stats) with stats = (M_p, L_p, O_p,
+    prefix) when want_prefix: prefix-only max and sum [B,Hkv,R] and normalized output
+    [B,Hkv,R,D] fp32 per row r = g*T + t. causal_block > 0: query q_pos0+t sees current
+    key c_pos0+j only if (c_pos0+j)//causal_block <= (q_pos0+t)//causal_block.
+    """
+    lib = _lib.lib()
+    prefix = as_prefix(prefix)
+    b, hq, t, d = query.shape
+    if current_key is not None:
+        hkv = current_key.shape[1]
+    else:
+        hkv = (prefix.kf if prefix.kf is not None else prefix.vq).shape[1]
+    g = hq // hkv
+    r = g * t
+    dev = query.device
+    rows, qkeep = rows_struct(query)
+    cur, ckeep = block_struct(current_key, current_value, query.dtype)
+    if prefix.n:
+        desc = kv_descriptor(prefix, batch=b, heads=hkv, head_dim=d)
+        kv = desc.kv
+    else:
+        desc, kv = None, _lib.MaKV()
+        kv.layout, kv.dtype = _lib.MA_KV_DENSE, rows.dtype
+    out = torch.empty_like(query)
+    if want_prefix:
+        mp = torch.empty((b, hkv, r), device=dev, dtype=torch.float32)
+        lp = torch.empty_like(mp)
+        op = torch.empty((b, hkv, r, d), device=dev, dtype=torch.float32)
+    else:
+        mp = lp = op = None
+    nbytes = lib.ma_prefix_attention_workspace(b, hkv, r, prefix.n, d, cur.Tc)
+    ws = _lib.workspace(dev, "attention", nbytes)
+    scale = float(scaling if scaling is not None else d ** -0.5)
+    _lib.check("ma_prefix_attention", lib.ma_prefix_attention(
+        rows, kv, hkv, cur, scale, int(causal_block), int(q_pos0), int(c_pos0),
+        out.data_ptr(), _lib.i64(*out.stride()[:3]), _lib.ptr(mp), _lib.ptr(lp), _lib.ptr(op),
+        ws.data_ptr(), ws.numel(), _lib.stream_handle(dev)))
+    del qkeep, ckeep, desc
+    return out, ((mp, lp, op, prefix) if want_prefix else None)
+
+
+def prefix_scores(query, prefix, stats, q_rows, *, value: bool, scaling=None, **_tuning):
+    """Per prefix slot: mass a_j (mean prefix-softmax over the selection rows) and, with
+    value=True, a_j * ||v_j - c|| with c = sum_j a_j v_j / sum_j a_j (splitk.py:582-614).
+
+    q_rows: positions t within the block (int tensor or list); every query head of the
+    KV head contributes. Returns (mass, score) as [B, Hkv, n] fp32 (score None when
+    value=False). Dead slots score 0.
+    """
+    lib = _lib.lib()
+    b, hq, t, d = query.shape
+    mp, lp, _op, used = stats
+    prefix = used if used is not None else as_prefix(prefix)
+    hkv = mp.shape[1]
+    n = prefix.n
+    dev = query.device
+    mass = torch.empty((b, hkv, n), device=dev, dtype=torch.float32)
+    if n == 0:
+        return mass, (torch.empty_like(mass) if value else None)
+    if isinstance(q_rows, torch.Tensor) and q_rows.is_cuda and q_rows.dtype == torch.int32:
+        rows_t = q_rows.contiguous()
+    else:
+        rows_t = torch.as_tensor(q_rows, dtype=torch.int32).to(dev).contiguous()
+    rows, qkeep = rows_struct(query)
+    desc = kv_descriptor(prefix, batch=b, heads=hkv, head_dim=d)
+    scale = float(scaling if scaling is not None else d ** -0.5)
+    stream = _lib.stream_handle(dev)
+    _lib.check("ma_prefix_mass", lib.ma_prefix_mass(
+        rows, desc.kv, hkv, rows_t.data_ptr(), int(rows_t.numel()), mp.data_ptr(), lp.data_ptr(), scale,
+        mass.data_ptr(), _lib.i64(mass.stride(0), mass.stride(1)), stream))
+    score = None
+    if value:
+        score = torch.empty_like(mass)
+        nbytes = lib.ma_value_score_workspace(b, hkv, n, d)
+        ws = _lib.workspace(dev, "value_score", nbytes)
+        _lib.check("ma_value_score", lib.ma_value_score(
+            desc.kv, b, hkv, d, mass.data_ptr(), _lib.i64(mass.stride(0), mass.stride(1)),
+            score.data_ptr(), _lib.i64(score.stride(0), score.stride(1)), ws.data_ptr(), ws.numel(), stream))
+    del qkeep, rows_t
+    return mass, score
+
+
+def dequantize_prefix(prefix, b: int, hkv: int, d: int, dtype=torch.bfloat16, **_tuning):
+    """The whole prefix as contiguous [B, Hkv, n, D] tensors (splitk.py:465-480)."""
+    from .ops import gather_packed_kv
+
+    prefix = as_prefix(prefix)
+    n = prefix.n
+    dev = (prefix.kq if prefix.nq else prefix.kf).device
+    ko = torch.empty((b, hkv, n, d), device=dev, dtype=dtype)
+    vo = torch.empty_like(ko)
+    if n == 0:
+        return ko, vo
+    idx = torch.arange(n, device=dev, dtype=torch.int64).expand(b, hkv, n)
+    unmasked = Prefix(**{s: getattr(prefix, s) for s in Prefix.__slots__})
+    unmasked.mask = None
+    return gather_packed_kv(unmasked, idx, dtype=dtype, out_key=ko, out_value=vo)

@@ -227,17 +227,20 @@ def topk_sorted(score: torch.Tensor, k: int, live_mask: torch.Tensor | None = No
     The reference ranks with torch.topk then sorts the indices (ops.py:377-380, 509-516;
     session.py:944-946). Its order among exactly equal scores is an artefact of the
     CPU partial sort, so this restatement fixes the rule: larger score first, and
-    among equal scores the lower index first. Dead entries rank -inf (ops.py:377).
-    Returns (indices int64 [..., k], values fp32 [..., k]).
+    among equal scores the lower index first. Dead entries rank below every live entry,
+    -inf included (the reference masks them to -inf, ops.py:374-380, so that they are
+    never chosen while a live entry is left). Returns (indices int64 [..., k], values
+    fp32 [..., k]) with the values of the live entries.
     """
-    s = score.detach().to(torch.float32).clone()
-    if live_mask is not None:
-        s = s.masked_fill(~live_mask, float("-inf"))
+    s = score.detach().to(torch.float32).contiguous()
     flat = s.reshape(-1, s.shape[-1]).numpy()
+    dead = None if live_mask is None else (~live_mask).reshape(-1, s.shape[-1]).numpy()
     out_i = np.empty((flat.shape[0], k), dtype=np.int64)
     out_v = np.empty((flat.shape[0], k), dtype=np.float32)
     for row in range(flat.shape[0]):
         keys = order_keys(flat[row])
+        if dead is not None:
+            keys = np.where(dead[row], np.uint32(0), keys)
         # stable sort on (-key, index): lexsort uses the last key as primary
         order = np.lexsort((np.arange(keys.size), -keys.astype(np.int64)))[:k]
         order = np.sort(order)
