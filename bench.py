@@ -174,10 +174,11 @@ class Workload:
 
 
 def kernel_launches(cfg: dict, retain: bool) -> int:
-    """Kernels of one block-step: step 0 = attention partial + combine + mass + value
-    centre + value apply + top-k (6); each sub-step = partial + combine (2); retention =
-    per layer probe partial + combine + mass (3), then value centre + apply + survivors."""
-    per_layer = 6 + 2 * (cfg["substeps"] - 1)
+    """Kernels of one block-step: step 0 = attention partial + combine + mass (with the
+    value centre) + value apply + top-k (5); each sub-step = partial + combine (2);
+    retention = per layer probe partial + combine + mass (3), then value centre + apply +
+    survivors."""
+    per_layer = 5 + 2 * (cfg["substeps"] - 1)
     n = per_layer * cfg["L"]
     if retain:
         n += 3 * cfg["L"] + 3

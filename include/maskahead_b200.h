@@ -22,7 +22,7 @@
  * brain-lab-research/MaskAhead, src/maskahead/):
  *   ma_prefix_attention  kernels/splitk.py:493-579 (splitk_attention) and
  *                        kernels/ops.py:130-264, 766-787 (dense_packed_attention)
- *   ma_prefix_mass       kernels/splitk.py:582-614 (prefix_scores, mass part) and
+ *   ma_prefix_scores     kernels/splitk.py:582-614 (prefix_scores) and
  *                        kernels/ops.py:333-521 (selector_topk importance)
  *   ma_value_score       runtime/session.py:27-40 (value_score) and 870-954
  *                        (_rescore_by_value, value_center="attn")
@@ -143,12 +143,17 @@ MA_API int ma_prefix_attention(const ma_rows* q, const ma_kv* kv, int H, const m
                         float* m_p, float* l_p, float* o_p,
                         void* workspace, size_t workspace_bytes, void* stream);
 
-/* ---- prefix mass --------------------------------------------------------------------
+/* ---- prefix scores (mass and value-aware score) -------------------------------------
  * mass[b,h,j] = mean over rows (g, t in q_rows[0..T2)) of exp(s - m_p[r]) / l_p[r],
- * s = scale * q_r . k_j; 0 on dead slots. mass strides over (b, h).                    */
-MA_API int ma_prefix_mass(const ma_rows* q, const ma_kv* kv, int H, const int32_t* q_rows, int T2,
-                   const float* m_p, const float* l_p, float scale,
-                   float* mass, const int64_t smass[2], void* stream);
+ * s = scale * q_r . k_j; 0 on dead slots. With score != NULL also
+ * score[b,h,j] = mass_j * ||v_j - c||, c = sum_j mass_j v_j / max(sum_j mass_j, 1e-12)
+ * over live slots (fp32), as ma_value_score. mass/score strides over (b, h). Rows whose
+ * q_rows entry lies outside [0, T) are skipped. The workspace (score != NULL only) is
+ * sized by ma_value_score_workspace(B, H, n, D).                                      */
+MA_API int ma_prefix_scores(const ma_rows* q, const ma_kv* kv, int H, const int32_t* q_rows, int T2,
+                     const float* m_p, const float* l_p, float scale,
+                     float* mass, const int64_t smass[2], float* score, const int64_t sscore[2],
+                     void* workspace, size_t workspace_bytes, void* stream);
 
 /* ---- value-aware score --------------------------------------------------------------
  * c = sum_j a_j v_j / max(sum_j a_j, 1e-12) over live slots, score_j = a_j*||v_j - c||

@@ -72,8 +72,8 @@ _SIGNATURES = {
     "ma_prefix_attention_workspace": (_sz, [_i32] * 6),
     "ma_prefix_attention": (_i32, [_P(MaRows), _P(MaKV), _i32, _P(MaBlock), _f32, _i32, _i32, _i32,
                                    _vp, _P(ctypes.c_int64), _vp, _vp, _vp, _vp, _sz, _vp]),
-    "ma_prefix_mass": (_i32, [_P(MaRows), _P(MaKV), _i32, _vp, _i32, _vp, _vp, _f32, _vp,
-                              _P(ctypes.c_int64), _vp]),
+    "ma_prefix_scores": (_i32, [_P(MaRows), _P(MaKV), _i32, _vp, _i32, _vp, _vp, _f32, _vp,
+                                _P(ctypes.c_int64), _vp, _P(ctypes.c_int64), _vp, _sz, _vp]),
     "ma_value_score_workspace": (_sz, [_i32] * 4),
     "ma_value_score": (_i32, [_P(MaKV), _i32, _i32, _i32, _vp, _P(ctypes.c_int64), _vp,
                               _P(ctypes.c_int64), _vp, _sz, _vp]),

@@ -99,6 +99,9 @@ struct Plan {
 int row_tile(bool mma) { return mma ? mma_row_tile() : simt_row_block(); }
 int key_tile(bool mma) { return mma ? mma_key_tile() : simt_key_tile(); }
 
+// Splits over the keys: enough CTAs for one wave (tensor-core CTAs hold an SM each) or
+// two (CUDA-core CTAs, several per SM), the current block included, but no split shorter
+// than a few key tiles -- each split pays for staging its rows and writing R x D partials.
 Plan plan_splits(int BH, int R, int n, int Tc, bool mma) {
   Plan p;
   const int rt = row_tile(mma), kt = key_tile(mma);
@@ -110,13 +113,13 @@ Plan plan_splits(int BH, int R, int n, int Tc, bool mma) {
   } else {
     const int sms = device_sm_count();
     const int per_split = BH * row_blocks;
-    // tensor-core CTAs hold one SM each (registers, shared memory): one wave;
-    // the CUDA-core kernel fits several per SM: two waves
     const int waves = mma ? 1 : 2;
-    int target = (waves * sms) / (per_split > 0 ? per_split : 1);
+    int target = (waves * sms) / (per_split > 0 ? per_split : 1) - (Tc > 0 ? 1 : 0);
     if (target < 1) target = 1;
-    const int max_splits = (n + kt - 1) / kt;
+    const int min_len = (mma ? 4 : 2) * kt;
+    const int max_splits = (n + min_len - 1) / min_len;
     int ns = target < max_splits ? target : max_splits;
+    if (ns > 255) ns = 255;
     int len = (n + ns - 1) / ns;
     len = ((len + kt - 1) / kt) * kt;
     p.split_len = len;
@@ -212,17 +215,39 @@ int ma_prefix_attention(const ma_rows* q, const ma_kv* kv, int H, const ma_block
                        (cudaStream_t)stream);
 }
 
-int ma_prefix_mass(const ma_rows* q, const ma_kv* kv, int H, const int32_t* q_rows, int T2,
-                   const float* m_p, const float* l_p, float scale, float* mass, const int64_t smass[2],
-                   void* stream) {
+int ma_prefix_scores(const ma_rows* q, const ma_kv* kv, int H, const int32_t* q_rows, int T2,
+                     const float* m_p, const float* l_p, float scale, float* mass, const int64_t smass[2],
+                     float* score, const int64_t sscore[2], void* workspace, size_t workspace_bytes,
+                     void* stream) {
   int rc = check_rows(q);
   if (rc) return rc;
   if (H <= 0 || q->Hq % H) return MA_ERR_ARG;
   if ((rc = check_kv(kv, q->D))) return rc;
-  if (!q_rows || T2 <= 0 || T2 > q->T || !m_p || !l_p || !mass || !smass) return MA_ERR_ARG;
+  if (!q_rows || T2 <= 0 || !m_p || !l_p || !mass || !smass) return MA_ERR_ARG;
   if (smass[0] < 0 || smass[1] < 0) return MA_ERR_ARG;
-  return launch_prefix_mass(*q, *kv, H, q_rows, T2, m_p, l_p, scale, mass, smass[0], smass[1],
-                            (cudaStream_t)stream);
+  if (score && (!sscore || sscore[0] < 0 || sscore[1] < 0)) return MA_ERR_ARG;
+  const int n = kv->nq + kv->nf;
+  if (n == 0) return MA_OK;
+  const int BH = q->B * H;
+  ValueWs w = {nullptr, nullptr, nullptr};
+  if (score) {
+    if (!workspace || workspace_bytes < value_score_ws_bytes(q->B, H, n, q->D)) return MA_ERR_WORKSPACE;
+    if ((reinterpret_cast<uintptr_t>(workspace) & 255) != 0) return MA_ERR_WORKSPACE;
+    w = carve_value_ws(workspace, BH, q->D);
+  }
+  cudaStream_t st = (cudaStream_t)stream;
+  const int G = q->Hq / H;
+  if (use_mma(*q, *kv) && G * T2 <= 256) {
+    rc = launch_prefix_mass_mma(*q, *kv, H, q_rows, T2, m_p, l_p, scale, mass, smass[0], smass[1], w.part,
+                                w.counters, w.centre, st);
+    if (rc || !score) return rc;
+    return launch_value_apply(*kv, q->B, H, q->D, mass, smass[0], smass[1], w.centre, score, sscore[0],
+                              sscore[1], st);
+  }
+  rc = launch_prefix_mass(*q, *kv, H, q_rows, T2, m_p, l_p, scale, mass, smass[0], smass[1], st);
+  if (rc || !score) return rc;
+  return launch_value_score(*kv, q->B, H, q->D, mass, smass[0], smass[1], score, sscore[0], sscore[1], workspace,
+                            st);
 }
 
 size_t ma_value_score_workspace(int B, int H, int n, int D) {

@@ -31,9 +31,22 @@ int launch_prefix_mass(const ma_rows& q, const ma_kv& kv, int H, const int32_t* 
                        const float* m_p, const float* l_p, float scale, float* mass,
                        int64_t sm0, int64_t sm1, cudaStream_t st);
 size_t value_score_ws_bytes(int B, int H, int n, int D);
+struct ValueWs {
+  unsigned* counters;  // [BH], zero between calls
+  float* centre;       // [BH][D]
+  float* part;         // [BH][tiles][D+1]
+};
+ValueWs carve_value_ws(void* ws, int BH, int D);
+int launch_value_apply(const ma_kv& kv, int B, int H, int D, const float* a, int64_t sa0, int64_t sa1,
+                       const float* centre, float* score, int64_t ss0, int64_t ss1, cudaStream_t st);
 int launch_value_score(const ma_kv& kv, int B, int H, int D, const float* a, int64_t sa0,
                        int64_t sa1, float* score, int64_t ss0, int64_t ss1, void* ws,
                        cudaStream_t st);
+
+// ma_mass_mma.cu (bf16, R2 = G*T2 <= 256): mass, optionally the value-score centre
+int launch_prefix_mass_mma(const ma_rows& q, const ma_kv& kv, int H, const int32_t* q_rows, int T2,
+                           const float* m_p, const float* l_p, float scale, float* mass, int64_t sm0,
+                           int64_t sm1, float* part, unsigned* counters, float* centre, cudaStream_t st);
 
 // ma_select.cu
 int launch_select_topk(const float* score, int B, int H, int n, int64_t ss0, int64_t ss1,

@@ -246,7 +246,27 @@ size_t value_score_ws_bytes(int B, int H, int n, int D) {
   const size_t ntile = (size_t)(n + kVTok - 1) / kVTok;
   const size_t cnt = ((BH * sizeof(unsigned) + 255) / 256) * 256;
   const size_t cen = ((BH * D * sizeof(float) + 255) / 256) * 256;
-  return cnt + cen + BH * ntile * (D + 1) * sizeof(float);
+  return cnt + cen + BH * (ntile > 0 ? ntile : 1) * (D + 1) * sizeof(float);
+}
+
+ValueWs carve_value_ws(void* ws, int BH, int D) {
+  ValueWs w;
+  char* p = reinterpret_cast<char*>(ws);
+  w.counters = reinterpret_cast<unsigned*>(p);
+  p += (((size_t)BH * sizeof(unsigned) + 255) / 256) * 256;
+  w.centre = reinterpret_cast<float*>(p);
+  p += (((size_t)BH * D * sizeof(float) + 255) / 256) * 256;
+  w.part = reinterpret_cast<float*>(p);
+  return w;
+}
+
+int launch_value_apply(const ma_kv& kv, int B, int H, int D, const float* a, int64_t sa0, int64_t sa1,
+                       const float* centre, float* score, int64_t ss0, int64_t ss1, cudaStream_t st) {
+  const int n = kv.nq + kv.nf;
+  if (n == 0) return MA_OK;
+  dim3 grid((n + kVTok - 1) / kVTok, B * H);
+  value_apply_kernel<<<grid, kThreads, 0, st>>>(kv, H, D, a, sa0, sa1, centre, score, ss0, ss1);
+  return cudaGetLastError() == cudaSuccess ? MA_OK : MA_ERR_CUDA;
 }
 
 int launch_value_score(const ma_kv& kv, int B, int H, int D, const float* a, int64_t sa0,
@@ -254,19 +274,12 @@ int launch_value_score(const ma_kv& kv, int B, int H, int D, const float* a, int
                        cudaStream_t st) {
   const int n = kv.nq + kv.nf;
   if (n == 0) return MA_OK;
-  const size_t BH = (size_t)B * H;
   const int ntile = (n + kVTok - 1) / kVTok;
-  char* p = reinterpret_cast<char*>(ws);
-  unsigned* counters = reinterpret_cast<unsigned*>(p);
-  p += ((BH * sizeof(unsigned) + 255) / 256) * 256;
-  float* centre = reinterpret_cast<float*>(p);
-  p += ((BH * D * sizeof(float) + 255) / 256) * 256;
-  float* part = reinterpret_cast<float*>(p);
-  dim3 grid(ntile, (unsigned)BH);
-  value_centre_kernel<<<grid, kThreads, 0, st>>>(kv, H, D, a, sa0, sa1, ntile, part, counters, centre);
+  const ValueWs w = carve_value_ws(ws, B * H, D);
+  dim3 grid(ntile, B * H);
+  value_centre_kernel<<<grid, kThreads, 0, st>>>(kv, H, D, a, sa0, sa1, ntile, w.part, w.counters, w.centre);
   if (cudaGetLastError() != cudaSuccess) return MA_ERR_CUDA;
-  value_apply_kernel<<<grid, kThreads, 0, st>>>(kv, H, D, a, sa0, sa1, centre, score, ss0, ss1);
-  return cudaGetLastError() == cudaSuccess ? MA_OK : MA_ERR_CUDA;
+  return launch_value_apply(kv, B, H, D, a, sa0, sa1, w.centre, score, ss0, ss1, st);
 }
 
 }  // namespace ma

@@ -123,10 +123,16 @@ __device__ void emit_selected(KeyFn key, int n, KthResult th, int* sWarp, EmitFn
   }
 }
 
+// One CTA per (b, h). The order keys are staged in shared memory when they fit
+// (n <= kSelSmemKeys), so the four histogram passes and the two compaction passes read
+// them on-chip; larger rows re-read the scores (from L2).
+constexpr int kSelSmemKeys = 48 * 1024;
+
 __global__ void __launch_bounds__(kSelThreads)
 select_topk_kernel(const float* __restrict__ score, int H, int n, int64_t ss0, int64_t ss1,
                    const uint8_t* __restrict__ mask, int k, int64_t* __restrict__ indices,
-                   float* __restrict__ values, int64_t si0, int64_t si1) {
+                   float* __restrict__ values, int64_t si0, int64_t si1, int staged) {
+  extern __shared__ uint32_t sKeys[];
   __shared__ unsigned sHist[256];
   __shared__ int sSel[2];
   __shared__ int sWarp[33];
@@ -134,17 +140,26 @@ select_topk_kernel(const float* __restrict__ score, int H, int n, int64_t ss0, i
   const int b = bh / H, h = bh - (bh / H) * H;
   const float* s = score + (int64_t)b * ss0 + (int64_t)h * ss1;
   const uint8_t* m = mask ? mask + (int64_t)bh * n : nullptr;
-  auto key = [&](int j) -> uint32_t {
+  auto gkey = [&](int j) -> uint32_t {
     if (m && m[j] == 0) return 0u;
     return order_key(s[j]);
   };
-  const KthResult th = radix_kth(key, n, k, sHist, sSel);
   int64_t* oi = indices + (int64_t)b * si0 + (int64_t)h * si1;
   float* ov = values ? values + (int64_t)b * si0 + (int64_t)h * si1 : nullptr;
-  emit_selected(key, n, th, sWarp, [&](int r, int j) {
+  auto emit = [&](int r, int j) {
     oi[r] = j;
     if (ov) ov[r] = s[j];
-  });
+  };
+  if (staged) {
+    for (int j = threadIdx.x; j < n; j += blockDim.x) sKeys[j] = gkey(j);
+    __syncthreads();
+    auto skey = [&](int j) -> uint32_t { return sKeys[j]; };
+    const KthResult th = radix_kth(skey, n, k, sHist, sSel);
+    emit_selected(skey, n, th, sWarp, emit);
+  } else {
+    const KthResult th = radix_kth(gkey, n, k, sHist, sSel);
+    emit_selected(gkey, n, th, sWarp, emit);
+  }
 }
 
 // Lookahead survivors of one lane (eviction.py:364-409): recent window by position,
@@ -264,8 +279,14 @@ __global__ void gather_kv_kernel(ma_kv kv, int H, int D, const int64_t* __restri
 int launch_select_topk(const float* score, int B, int H, int n, int64_t ss0, int64_t ss1,
                        const uint8_t* mask, int k, int64_t* indices, float* values, int64_t si0,
                        int64_t si1, cudaStream_t st) {
-  select_topk_kernel<<<B * H, kSelThreads, 0, st>>>(score, H, n, ss0, ss1, mask, k, indices, values,
-                                                    si0, si1);
+  const int staged = n <= kSelSmemKeys ? 1 : 0;
+  const size_t smem = staged ? (size_t)n * sizeof(uint32_t) : 0;
+  if (staged && smem > 48 * 1024 &&
+      cudaFuncSetAttribute(select_topk_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
+          cudaSuccess)
+    return MA_ERR_CUDA;
+  select_topk_kernel<<<B * H, kSelThreads, smem, st>>>(score, H, n, ss0, ss1, mask, k, indices, values,
+                                                       si0, si1, staged);
   return cudaGetLastError() == cudaSuccess ? MA_OK : MA_ERR_CUDA;
 }
 

@@ -35,7 +35,7 @@ def lib():
 
 def test_header_declares_entry_points():
     names = _declared()
-    assert {"ma_prefix_attention", "ma_prefix_mass", "ma_value_score", "ma_select_topk", "ma_retain",
+    assert {"ma_prefix_attention", "ma_prefix_scores", "ma_value_score", "ma_select_topk", "ma_retain",
             "ma_sparse_attention", "ma_gather_kv"} <= names
 
 
