@@ -163,6 +163,22 @@ MA_API int ma_value_score(const ma_kv* kv, int B, int H, int D, const float* a, 
                    float* score, const int64_t sscore[2],
                    void* workspace, size_t workspace_bytes, void* stream);
 
+/* ---- value-aware score without a workspace -------------------------------------------
+ * No counterpart in the reference. The same result as ma_value_score for callers that
+ * cannot allocate device memory -- a host binding (JNI, cgo, a plugin interface) that
+ * is handed only its input and output buffers and has no device allocator, or code whose
+ * framework owns every device allocation. Its scratch is a static device array of
+ * MA_NOALLOC_SCRATCH_BYTES (8 MiB) inside the library, held by every GPU that loads the
+ * library until the process exits. Sizes whose scratch (ma_value_score_workspace(B, H,
+ * n, D)) exceeds it return MA_ERR_UNSUPPORTED. The first call on a device looks up the
+ * array's device address; make that first call before any stream capture. Every call
+ * shares the array: calls that can overlap on the GPU (two streams, two threads) race.
+ * Allocates nothing (no cudaMalloc, cudaFree or allocating library routine).           */
+#define MA_NOALLOC_SCRATCH_BYTES ((size_t)8 << 20)
+MA_API int ma_value_score_noalloc(const ma_kv* kv, int B, int H, int D, const float* a,
+                                  const int64_t sa[2], float* score, const int64_t sscore[2],
+                                  void* stream);
+
 /* ---- top-k read set -----------------------------------------------------------------
  * Per (b, h): the k largest scores among live slots (ties: lower slot first), written
  * as ascending slot indices (int64) with their scores (values optional).             */

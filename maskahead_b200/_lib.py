@@ -77,6 +77,8 @@ _SIGNATURES = {
     "ma_value_score_workspace": (_sz, [_i32] * 4),
     "ma_value_score": (_i32, [_P(MaKV), _i32, _i32, _i32, _vp, _P(ctypes.c_int64), _vp,
                               _P(ctypes.c_int64), _vp, _sz, _vp]),
+    "ma_value_score_noalloc": (_i32, [_P(MaKV), _i32, _i32, _i32, _vp, _P(ctypes.c_int64), _vp,
+                                      _P(ctypes.c_int64), _vp]),
     "ma_select_topk": (_i32, [_vp, _i32, _i32, _i32, _P(ctypes.c_int64), _vp, _i32, _vp, _vp,
                               _P(ctypes.c_int64), _vp]),
     "ma_retain": (_i32, [_vp, _vp, _i32, _vp, _i32, _i32, _i32, _i32, _i32, _vp, _vp]),
