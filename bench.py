@@ -36,6 +36,9 @@ sys.path.insert(0, str(ROOT))
 CFG = dict(name="cfg2", L=28, B=1, Hq=28, H=4, D=128, T=32, n=8192, k=1024, C=2048, substeps=4,
            probe_blocks=1, interval=4, W=64, sinks=4, seed=1234)
 METRIC = "µs per block-step select+attend; achieved HBM GB/s vs peak; tokens/s at 1/2/4/8 GPU"
+# DRAM bytes per launch of the step-0 attention partial pass at this workload, from the
+# ncu capture summarized in profiles/attn_partial_mma_cfg2_step0.md (re-taken per kernel change)
+ATTN_TRAFFIC_BYTES = 17_129_984
 
 
 def parse_args():
@@ -446,7 +449,10 @@ def run_ours(args):
                    "l2": "inputs larger than L2 (470 MB K/V per step)", "timing": "CUDA-graph replay, CUDA events"},
         "roofline": {"kernel": "step-0 attention (attn_partial_mma + attn_combine) per layer", "bound": "hbm",
                      "achieved": achieved, "peak": hbm_peak, "unit": "GB/s", "frac": achieved / hbm_peak,
-                     "traffic": None, "peak_kind": f"{peak_kind} burst", "us_per_launch": ms_attn * 1e3,
+                     "traffic": ATTN_TRAFFIC_BYTES, "peak_kind": f"{peak_kind} burst",
+                     "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum of attn_partial_mma, "
+                                       "profiles/attn_partial_mma_cfg2_step0.md",
+                     "us_per_launch": ms_attn * 1e3,
                      "tensor_tflops": tflops, "tensor_frac": tflops / tf_peak,
                      "bytes_per_launch": ab["step0_layer"]},
         "algorithmic_bytes_per_step": ab["block_step"] + ab["retention"] / c["interval"],
