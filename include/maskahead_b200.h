@@ -148,8 +148,8 @@ MA_API int ma_prefix_attention(const ma_rows* q, const ma_kv* kv, int H, const m
  * s = scale * q_r . k_j; 0 on dead slots. With score != NULL also
  * score[b,h,j] = mass_j * ||v_j - c||, c = sum_j mass_j v_j / max(sum_j mass_j, 1e-12)
  * over live slots (fp32), as ma_value_score. mass/score strides over (b, h). Rows whose
- * q_rows entry lies outside [0, T) are skipped. The workspace (score != NULL only) is
- * sized by ma_value_score_workspace(B, H, n, D).                                      */
+ * q_rows entry lies outside [0, T) are skipped. The workspace is sized by
+ * ma_value_score_workspace(B, H, n, D).                                               */
 MA_API int ma_prefix_scores(const ma_rows* q, const ma_kv* kv, int H, const int32_t* q_rows, int T2,
                      const float* m_p, const float* l_p, float scale,
                      float* mass, const int64_t smass[2], float* score, const int64_t sscore[2],

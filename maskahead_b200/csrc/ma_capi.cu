@@ -96,8 +96,8 @@ struct Plan {
   int Rp;         // padded rows
 };
 
-int row_tile(bool mma) { return mma ? mma_row_tile() : simt_row_block(); }
-int key_tile(bool mma) { return mma ? mma_key_tile() : simt_key_tile(); }
+int row_tile(bool mma) { return mma ? tc_row_tile() : simt_row_block(); }
+int key_tile(bool mma) { return mma ? tc_key_tile() : simt_key_tile(); }
 
 // Splits over the keys: enough CTAs for one wave (tensor-core CTAs hold an SM each) or
 // two (CUDA-core CTAs, several per SM), the current block included, but no split shorter
@@ -116,7 +116,7 @@ Plan plan_splits(int BH, int R, int n, int Tc, bool mma) {
     const int waves = mma ? 1 : 2;
     int target = (waves * sms) / (per_split > 0 ? per_split : 1) - (Tc > 0 ? 1 : 0);
     if (target < 1) target = 1;
-    const int min_len = (mma ? 4 : 2) * kt;
+    const int min_len = (mma ? 2 : 2) * kt;
     const int max_splits = (n + min_len - 1) / min_len;
     int ns = target < max_splits ? target : max_splits;
     if (ns > 255) ns = 255;
@@ -134,15 +134,18 @@ size_t attention_ws(int B, int H, int R, int n, int D, int Tc) {
   size_t best = 0;
   for (int m = 0; m < 2; ++m) {
     const Plan p = plan_splits(B * H, R, n, Tc, m == 1);
-    const size_t bytes = partials_bytes(B * H, p.S, p.Rp, D) + 256;
+    const size_t bytes = partials_bytes(B * H, p.S, p.Rp, D) + 512;
     if (bytes > best) best = bytes;
   }
   return best;
 }
 
-Partials carve_partials(void* ws, int BH, const Plan& p, int D) {
+// workspace: [256-byte aligned] error word block (256 B), then the split partials
+Partials carve_partials(void* ws, int BH, const Plan& p, int D, int** err) {
   Partials P;
   char* base = reinterpret_cast<char*>((reinterpret_cast<uintptr_t>(ws) + 255) & ~uintptr_t(255));
+  *err = reinterpret_cast<int*>(base);
+  base += 256;
   P.ml = reinterpret_cast<float2*>(base);
   P.acc = reinterpret_cast<float*>(base + (size_t)BH * p.S * p.Rp * sizeof(float2));
   P.S = p.S;
@@ -160,12 +163,13 @@ int run_attention(const ma_rows& q, const ma_kv& kv, int H, const ma_block& cur,
   const int R = G * q.T;
   const bool mma = use_mma(q, kv);
   const Plan p = plan_splits(q.B * H, R, n_keys, cur.Tc, mma);
-  if (!ws || ws_bytes < partials_bytes(q.B * H, p.S, p.Rp, q.D) + 256) return MA_ERR_WORKSPACE;
-  const Partials P = carve_partials(ws, q.B * H, p, q.D);
+  if (!ws || ws_bytes < partials_bytes(q.B * H, p.S, p.Rp, q.D) + 512) return MA_ERR_WORKSPACE;
+  int* err = nullptr;
+  const Partials P = carve_partials(ws, q.B * H, p, q.D, &err);
   int rc;
   if (p.nsplit + (cur.Tc > 0 ? 1 : 0) > 0) {
-    rc = mma ? launch_attn_partial_mma(q, kv, H, cur, scale, causal_block, q_pos0, c_pos0, idx, si0, si1,
-                                       n_keys, p.split_len, p.nsplit, P, st)
+    rc = mma ? launch_attn_partial_tc(q, kv, H, cur, scale, causal_block, q_pos0, c_pos0, idx, si0, si1,
+                                      n_keys, p.split_len, p.nsplit, P, err, st)
              : launch_attn_partial_simt(q, kv, H, cur, scale, causal_block, q_pos0, c_pos0, idx, si0,
                                         si1, n_keys, p.split_len, p.nsplit, P, st);
     if (rc != MA_OK) return rc;
@@ -229,17 +233,18 @@ int ma_prefix_scores(const ma_rows* q, const ma_kv* kv, int H, const int32_t* q_
   const int n = kv->nq + kv->nf;
   if (n == 0) return MA_OK;
   const int BH = q->B * H;
-  ValueWs w = {nullptr, nullptr, nullptr};
-  if (score) {
+  const int G = q->Hq / H;
+  const bool tc = use_mma(*q, *kv) && G * T2 <= 256;
+  ValueWs w = {nullptr, nullptr, nullptr, nullptr};
+  if (score || tc) {  // the tensor-core kernel reports bounded-wait timeouts in the workspace
     if (!workspace || workspace_bytes < value_score_ws_bytes(q->B, H, n, q->D)) return MA_ERR_WORKSPACE;
     if ((reinterpret_cast<uintptr_t>(workspace) & 255) != 0) return MA_ERR_WORKSPACE;
     w = carve_value_ws(workspace, BH, q->D);
   }
   cudaStream_t st = (cudaStream_t)stream;
-  const int G = q->Hq / H;
-  if (use_mma(*q, *kv) && G * T2 <= 256) {
-    rc = launch_prefix_mass_mma(*q, *kv, H, q_rows, T2, m_p, l_p, scale, mass, smass[0], smass[1], w.part,
-                                w.counters, w.centre, st);
+  if (tc) {
+    rc = launch_prefix_mass_tc(*q, *kv, H, q_rows, T2, m_p, l_p, scale, mass, smass[0], smass[1],
+                               score ? w.part : nullptr, w.counters, score ? w.centre : nullptr, w.err, st);
     if (rc || !score) return rc;
     return launch_value_apply(*kv, q->B, H, q->D, mass, smass[0], smass[1], w.centre, score, sscore[0],
                               sscore[1], st);

@@ -50,7 +50,7 @@ attn_combine_kernel(ma_rows q, int H, Partials P, int nsplit, int has_cur, QT* _
   if (active) {
     const float* base = P.acc + row0 * D + d0;
     const int64_t step = (int64_t)P.Rp * D;
-#pragma unroll 4
+#pragma unroll 16
     for (int s = 0; s < nsplit; ++s) {
       const float w = sW[warp][s];
       const float4 a = __ldcg(reinterpret_cast<const float4*>(base + s * step));

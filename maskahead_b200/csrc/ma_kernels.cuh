@@ -13,13 +13,12 @@ int launch_attn_partial_simt(const ma_rows& q, const ma_kv& kv, int H, const ma_
 int simt_row_block();
 int simt_key_tile();
 
-// ma_attention_mma.cu (bf16 queries and caches, tensor cores)
-int launch_attn_partial_mma(const ma_rows& q, const ma_kv& kv, int H, const ma_block& cur,
-                            float scale, int causal_block, int q_pos0, int c_pos0,
-                            const int64_t* idx, int64_t si0, int64_t si1, int n_keys,
-                            int split_len, int nsplit, const Partials& P, cudaStream_t st);
-int mma_row_tile();
-int mma_key_tile();
+// ma_attention_tc.cu (bf16 queries and caches, tcgen05 / TMEM)
+int launch_attn_partial_tc(const ma_rows& q, const ma_kv& kv, int H, const ma_block& cur, float scale,
+                           int causal_block, int q_pos0, int c_pos0, const int64_t* idx, int64_t si0, int64_t si1,
+                           int n_keys, int split_len, int nsplit, const Partials& P, int* err, cudaStream_t st);
+int tc_row_tile();
+int tc_key_tile();
 
 // ma_combine.cu
 int launch_attn_combine(const ma_rows& q, int H, const Partials& P, int nsplit, bool has_cur,
@@ -33,6 +32,7 @@ int launch_prefix_mass(const ma_rows& q, const ma_kv& kv, int H, const int32_t* 
 size_t value_score_ws_bytes(int B, int H, int n, int D);
 struct ValueWs {
   unsigned* counters;  // [BH], zero between calls
+  int* err;            // device-side error word (a bounded wait gave up)
   float* centre;       // [BH][D]
   float* part;         // [BH][tiles][D+1]
 };
@@ -43,10 +43,10 @@ int launch_value_score(const ma_kv& kv, int B, int H, int D, const float* a, int
                        int64_t sa1, float* score, int64_t ss0, int64_t ss1, void* ws,
                        cudaStream_t st);
 
-// ma_mass_mma.cu (bf16, R2 = G*T2 <= 256): mass, optionally the value-score centre
-int launch_prefix_mass_mma(const ma_rows& q, const ma_kv& kv, int H, const int32_t* q_rows, int T2,
-                           const float* m_p, const float* l_p, float scale, float* mass, int64_t sm0,
-                           int64_t sm1, float* part, unsigned* counters, float* centre, cudaStream_t st);
+// ma_mass_tc.cu (bf16, R2 = G*T2 <= 256): mass, optionally the value-score centre
+int launch_prefix_mass_tc(const ma_rows& q, const ma_kv& kv, int H, const int32_t* q_rows, int T2, const float* m_p,
+                          const float* l_p, float scale, float* mass, int64_t sm0, int64_t sm1, float* part,
+                          unsigned* counters, float* centre, int* err, cudaStream_t st);
 
 // ma_select.cu
 int launch_select_topk(const float* score, int B, int H, int n, int64_t ss0, int64_t ss1,

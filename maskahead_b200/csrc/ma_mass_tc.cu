@@ -1,0 +1,310 @@
+// Prefix mass with tcgen05 MMAs, with the value-score centre fused in.
+//
+// Transposed product: for a tile of 128 prefix slots, S^T = K Q^T (tcgen05.mma, M = 128
+// slots, N = the selection rows padded to 16, K = 128 channels; accumulator in TMEM), so
+// TMEM lane j holds slot j's logits against every selection row. Each thread owns one
+// slot (its lane) and half of the rows: it loads its logits with tcgen05.ld and sums
+//     exp(s_rj * scale - M_p,r) / L_p,r          (splitk.py:320-359; reference.py:318-366)
+// in registers; the two halves meet in shared memory in a fixed order, then
+// a_j = sum / R2 (0 on dead slots). bf16 products are exact in fp32 and accumulate in
+// fp32, so a_j is fp32-accurate. With a centre requested the CTA also accumulates
+// sum_j a_j v_j and sum_j a_j from the V tiles it streams, and the last CTA of the head
+// reduces the per-CTA partials in slot order into c = sum a v / max(sum a, 1e-12)
+// (session.py:27-40, 870-899) for the value-apply kernel.
+//
+// Slot tiles stream through a 2-stage cp.async ring (each CTA holds its whole range,
+// up to 256 slots, in flight from the start). Waits on the tensor core are bounded.
+#include "ma_kernels.cuh"
+#include "ma_mma.cuh"
+#include "ma_tcgen05.cuh"
+
+namespace ma {
+
+namespace {
+
+using namespace tc;
+
+constexpr int kWarps = 8;
+constexpr int kThreads = kWarps * 32;
+constexpr int kTile = 128;                  // slots per tile (= M, = TMEM lanes)
+constexpr int kD = 128;
+constexpr int kChunks = kD / 8;
+constexpr int kMaxRows = 256;               // selection rows (N of the MMA)
+constexpr int kStages = 2;
+constexpr float kLog2e = 1.4426950408889634f;
+constexpr int kQBytes = kMaxRows * kD * 2;  // 64 KB
+constexpr int kTileBytes = kTile * kD * 2;  // 32 KB (K or V)
+constexpr int kSmemBytes = 1024 + kQBytes + 2 * kStages * kTileBytes;
+constexpr uint32_t kTmemCols = 256;
+
+struct Args {
+  ma_rows q;
+  ma_kv kv;
+  const int32_t* q_rows;
+  const float* m_p;
+  const float* l_p;
+  float* mass;
+  int64_t sm0, sm1;
+  float* part;          // [BH][ctas][D+1] centre partials (centre only)
+  unsigned* counters;   // [BH]
+  float* centre;        // [BH][D]
+  int* err;
+  float scale;
+  int H, T2, slots_per_cta;
+};
+
+template <bool PACKED, bool CENTRE>
+__device__ __forceinline__ void load_tile(const Args& A, int b, int h, int j0, int end, uint8_t* sK, uint8_t* sV,
+                                          uint8_t* sOk) {
+  const __nv_bfloat16* kf = reinterpret_cast<const __nv_bfloat16*>(A.kv.kf);
+  const __nv_bfloat16* vf = reinterpret_cast<const __nv_bfloat16*>(A.kv.vf);
+  for (int c = threadIdx.x; c < kTile * kChunks; c += kThreads) {
+    const int jj = c / kChunks, ch = c % kChunks;
+    const int j = j0 + jj;
+    const bool ok = j < end && kv_live(A.kv, A.H, b, h, j);
+    uint8_t* dk = sK + kmajor_off(jj, ch, kTile);
+    uint8_t* dv = sV + jj * (kD * 2) + ch * 16;
+    if (ok && (!PACKED || j >= A.kv.nq)) {
+      const int row = j - A.kv.nq;
+      cp_async16(tc::smem_addr(dk), kf + (int64_t)b * A.kv.skf[0] + (int64_t)h * A.kv.skf[1] + (int64_t)row * A.kv.skf[2] + ch * 8, true);
+      if (CENTRE)
+        cp_async16(tc::smem_addr(dv), vf + (int64_t)b * A.kv.svf[0] + (int64_t)h * A.kv.svf[1] + (int64_t)row * A.kv.svf[2] + ch * 8, true);
+    } else if (ok) {
+      float f[8];
+      kv_read8<true>(A.kv, b, h, j, ch, f);
+      *reinterpret_cast<uint4*>(dk) = float8_to_bf16x8(f);
+      if (CENTRE) {
+        kv_read8<false>(A.kv, b, h, j, ch, f);
+        *reinterpret_cast<uint4*>(dv) = float8_to_bf16x8(f);
+      }
+    } else {
+      *reinterpret_cast<uint4*>(dk) = make_uint4(0, 0, 0, 0);
+      if (CENTRE) *reinterpret_cast<uint4*>(dv) = make_uint4(0, 0, 0, 0);
+    }
+    if (ch == 0) sOk[jj] = ok ? 1 : 0;
+  }
+  cp_async_commit();
+}
+
+template <bool PACKED, bool CENTRE>
+__global__ void __launch_bounds__(kThreads, 1) prefix_mass_tc(const Args A) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sQ = smem;                         // K-major [2 d blocks][Npad rows][128 B]
+  uint8_t* sRing = sQ + kQBytes;              // [stage][K tile (swizzled) | V tile (row-major)]
+  __shared__ float sM2[kMaxRows], sInvL[kMaxRows];
+  __shared__ float sHalf[2][kTile];
+  __shared__ float sA[kTile];
+  __shared__ uint8_t sOk[kStages][kTile];
+  __shared__ float sRed[kThreads];
+  __shared__ uint32_t s_taddr;
+  __shared__ __align__(8) uint64_t mbar;
+  __shared__ int s_abort;
+  __shared__ bool sLast;
+
+  const int n = A.kv.nq + A.kv.nf;
+  const int bh = blockIdx.y;
+  const int H = A.H;
+  const int b = bh / H, h = bh - (bh / H) * H;
+  const int G = A.q.Hq / H;
+  const int T = A.q.T;
+  const int R2 = G * A.T2;
+  const int Npad = (R2 + 15) & ~15;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int quarter = warp & 3, chalf = warp >> 2;
+  const int slot_lane = quarter * 32 + lane;          // this thread's slot within a tile (TMEM lane)
+  const int begin = blockIdx.x * A.slots_per_cta;
+  const int end = min(n, begin + A.slots_per_cta);
+  const float inv_rows = 1.f / (float)R2;
+  const float c2 = A.scale * kLog2e;
+
+  // selection rows: r2 = g*T2 + i -> query row (h*G + g, q_rows[i]); per-row constants
+  {
+    const __nv_bfloat16* qp = reinterpret_cast<const __nv_bfloat16*>(A.q.q);
+    for (int c = threadIdx.x; c < Npad * kChunks; c += kThreads) {
+      const int rr = c / kChunks, ch = c % kChunks;
+      const int g = rr / A.T2;
+      const int t = rr < R2 ? A.q_rows[rr - g * A.T2] : -1;
+      const bool ok = t >= 0 && t < T;
+      uint8_t* dst = sQ + kmajor_off(rr, ch, Npad);
+      if (ok) {
+        cp_async16(tc::smem_addr(dst), qp + (int64_t)b * A.q.sq[0] + (int64_t)(h * G + g) * A.q.sq[1] + (int64_t)t * A.q.sq[2] + ch * 8, true);
+      } else {
+        *reinterpret_cast<uint4*>(dst) = make_uint4(0, 0, 0, 0);
+      }
+      if (ch == 0) {
+        const int64_t ri = (int64_t)bh * G * T + (int64_t)g * T + t;
+        const float L = ok ? A.l_p[ri] : 0.f;
+        const bool live_row = ok && L > 0.f;
+        sM2[rr] = live_row ? A.m_p[ri] * kLog2e : INFINITY;   // exp2(s - inf) = 0: no contribution
+        sInvL[rr] = live_row ? 1.f / L : 0.f;
+      }
+    }
+  }
+  for (int st = 0; st < kStages; ++st) {
+    const int j0 = begin + st * kTile;
+    uint8_t* sK = sRing + 2 * st * kTileBytes;
+    if (j0 < end) load_tile<PACKED, CENTRE>(A, b, h, j0, end, sK, sK + kTileBytes, sOk[st]);
+    else cp_async_commit();
+  }
+  if (threadIdx.x == 0) {
+    mbar_init(&mbar, 1);
+    s_abort = 0;
+  }
+  if (warp == 0) tmem_alloc(&s_taddr, kTmemCols);
+  fence_before_sync();
+  __syncthreads();
+  fence_after_sync();
+  const uint32_t taddr = s_taddr;
+  const uint32_t tRow = taddr + ((uint32_t)(quarter * 32) << 16);   // this thread's lane
+  const uint32_t idesc = idesc_bf16(kTile, Npad, false, false);
+  const int cols_half = Npad / 2;                                    // rows handled per half
+  const int c_lo = chalf * cols_half;
+  uint32_t phase = 0;
+  int stage = 0;
+  float cacc = 0.f, asum = 0.f;
+  const int cd = threadIdx.x & (kD - 1), vhalf = threadIdx.x >> 7;
+  bool aborted = false;
+
+  for (int j0 = begin; j0 < end; j0 += kTile) {
+    uint8_t* sK = sRing + 2 * stage * kTileBytes;
+    uint8_t* sV = sK + kTileBytes;
+    cp_async_wait<kStages - 1>();
+    fence_proxy_async();
+    fence_before_sync();
+    __syncthreads();
+    fence_after_sync();
+    if (s_abort) {
+      aborted = true;
+      break;
+    }
+    if (threadIdx.x == 0) {
+      const uint32_t ka = tc::smem_addr(sK), qa = tc::smem_addr(sQ);
+#pragma unroll
+      for (int kk = 0; kk < kD / 16; ++kk) {
+        const uint64_t ad = smem_desc(ka + (kk >> 2) * (kTile * 128) + (kk & 3) * 32, 16, 1024);
+        const uint64_t bd = smem_desc(qa + (kk >> 2) * (Npad * 128) + (kk & 3) * 32, 16, 1024);
+        mma_bf16(taddr, ad, bd, idesc, kk > 0);
+      }
+      mma_commit(&mbar);
+    }
+    const bool ok = mbar_wait(&mbar, phase);
+    phase ^= 1;
+    fence_after_sync();
+    if (!ok) s_abort = 1;
+    // this thread: slot slot_lane, rows [c_lo, c_lo + cols_half)
+    float acc = 0.f;
+#pragma unroll 1
+    for (int c0 = 0; c0 < cols_half; c0 += 32) {
+      float sv[32];
+      tmem_ld32(tRow + c_lo + c0, sv);   // cols_half is a multiple of 8: reads stay in the allocation
+      tmem_ld_wait();
+#pragma unroll
+      for (int i = 0; i < 32; ++i) {
+        const int r = c_lo + c0 + i;
+        if (c0 + i < cols_half) acc = fmaf(ex2(fmaf(sv[i], c2, -sM2[r])), sInvL[r], acc);
+      }
+    }
+    sHalf[chalf][slot_lane] = acc;
+    __syncthreads();
+    if (threadIdx.x < kTile) {
+      const int j = j0 + threadIdx.x;
+      const float a = sOk[stage][threadIdx.x] ? (sHalf[0][threadIdx.x] + sHalf[1][threadIdx.x]) * inv_rows : 0.f;
+      if (j < end) A.mass[(int64_t)b * A.sm0 + (int64_t)h * A.sm1 + j] = a;
+      sA[threadIdx.x] = j < end ? a : 0.f;
+    }
+    if (CENTRE) {
+      __syncthreads();
+      const __nv_bfloat16* v = reinterpret_cast<const __nv_bfloat16*>(sV);
+      const int jlo = vhalf * (kTile / 2);
+#pragma unroll 4
+      for (int jj = jlo; jj < jlo + kTile / 2; ++jj) {
+        const float a = sA[jj];
+        cacc = fmaf(a, __bfloat162float(v[jj * kD + cd]), cacc);
+        asum += a;
+      }
+    }
+    fence_before_sync();
+    __syncthreads();   // this stage and sA are consumed
+    const int jn = j0 + kStages * kTile;
+    if (jn < end) load_tile<PACKED, CENTRE>(A, b, h, jn, end, sK, sV, sOk[stage]);
+    else cp_async_commit();
+    stage = (stage + 1) % kStages;
+  }
+
+  if (aborted && threadIdx.x == 0) atomicExch(A.err, 1);
+  if (aborted) mbar_wait(&mbar, phase);     // drain the in-flight MMA (bounded)
+  fence_before_sync();
+  __syncthreads();
+  fence_after_sync();
+  if (warp == 0) tmem_dealloc(taddr, kTmemCols);
+  if (!CENTRE) return;
+
+  // per-CTA centre partial, then the last CTA of the head reduces them in CTA order
+  float* mine = A.part + ((int64_t)bh * gridDim.x + blockIdx.x) * (kD + 1);
+  sRed[threadIdx.x] = aborted ? NAN : cacc;
+  if (cd == 0) sHalf[0][vhalf] = asum;
+  __syncthreads();
+  if (threadIdx.x < kD) mine[threadIdx.x] = sRed[threadIdx.x] + sRed[threadIdx.x + kD];
+  if (threadIdx.x == 0) mine[kD] = sHalf[0][0] + sHalf[0][1];
+  __threadfence();
+  __syncthreads();
+  if (threadIdx.x == 0) sLast = atomicAdd(&A.counters[bh], 1u) == gridDim.x - 1;
+  __syncthreads();
+  if (!sLast) return;
+  __threadfence();
+  const float* base = A.part + (int64_t)bh * gridDim.x * (kD + 1);
+  if (threadIdx.x <= kD) {
+    float tot = 0.f;
+    for (unsigned t = 0; t < gridDim.x; ++t) tot += __ldcg(base + (int64_t)t * (kD + 1) + threadIdx.x);
+    sRed[threadIdx.x] = tot;
+  }
+  __syncthreads();
+  if (threadIdx.x < kD) A.centre[(int64_t)bh * kD + threadIdx.x] = sRed[threadIdx.x] / fmaxf(sRed[kD], 1e-12f);
+  if (threadIdx.x == 0) A.counters[bh] = 0u;
+}
+
+}  // namespace
+
+int launch_prefix_mass_tc(const ma_rows& q, const ma_kv& kv, int H, const int32_t* q_rows, int T2, const float* m_p,
+                          const float* l_p, float scale, float* mass, int64_t sm0, int64_t sm1, float* part,
+                          unsigned* counters, float* centre, int* err, cudaStream_t st) {
+  const int n = kv.nq + kv.nf;
+  const int BH = q.B * H;
+  Args A;
+  A.q = q;
+  A.kv = kv;
+  A.q_rows = q_rows;
+  A.m_p = m_p;
+  A.l_p = l_p;
+  A.mass = mass;
+  A.sm0 = sm0;
+  A.sm1 = sm1;
+  A.part = part;
+  A.counters = counters;
+  A.centre = centre;
+  A.err = err;
+  A.scale = scale;
+  A.H = H;
+  A.T2 = T2;
+  // CTAs: one wave over the heads, at least one tile each
+  const int sms = device_sm_count();
+  int per_head = sms / (BH > 0 ? BH : 1);
+  if (per_head < 1) per_head = 1;
+  int spc = (n + per_head - 1) / per_head;
+  spc = ((spc + kTile - 1) / kTile) * kTile;
+  A.slots_per_cta = spc < kTile ? kTile : spc;
+  dim3 grid((n + A.slots_per_cta - 1) / A.slots_per_cta, BH);
+  const bool packed = kv.layout != MA_KV_DENSE;
+  const bool cen = centre != nullptr;
+  auto go = [&](auto kernel) -> int {
+    if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes) != cudaSuccess)
+      return MA_ERR_CUDA;
+    kernel<<<grid, kThreads, kSmemBytes, st>>>(A);
+    return cudaGetLastError() == cudaSuccess ? MA_OK : MA_ERR_CUDA;
+  };
+  if (packed) return cen ? go(prefix_mass_tc<true, true>) : go(prefix_mass_tc<true, false>);
+  return cen ? go(prefix_mass_tc<false, true>) : go(prefix_mass_tc<false, false>);
+}
+
+}  // namespace ma

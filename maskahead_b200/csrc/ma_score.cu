@@ -244,7 +244,7 @@ int launch_prefix_mass(const ma_rows& q, const ma_kv& kv, int H, const int32_t* 
 size_t value_score_ws_bytes(int B, int H, int n, int D) {
   const size_t BH = (size_t)B * H;
   const size_t ntile = (size_t)(n + kVTok - 1) / kVTok;
-  const size_t cnt = ((BH * sizeof(unsigned) + 255) / 256) * 256;
+  const size_t cnt = (((BH + 1) * sizeof(unsigned) + 255) / 256) * 256;
   const size_t cen = ((BH * D * sizeof(float) + 255) / 256) * 256;
   return cnt + cen + BH * (ntile > 0 ? ntile : 1) * (D + 1) * sizeof(float);
 }
@@ -253,7 +253,8 @@ ValueWs carve_value_ws(void* ws, int BH, int D) {
   ValueWs w;
   char* p = reinterpret_cast<char*>(ws);
   w.counters = reinterpret_cast<unsigned*>(p);
-  p += (((size_t)BH * sizeof(unsigned) + 255) / 256) * 256;
+  w.err = reinterpret_cast<int*>(p) + BH;
+  p += (((size_t)(BH + 1) * sizeof(unsigned) + 255) / 256) * 256;
   w.centre = reinterpret_cast<float*>(p);
   p += (((size_t)BH * D * sizeof(float) + 255) / 256) * 256;
   w.part = reinterpret_cast<float*>(p);

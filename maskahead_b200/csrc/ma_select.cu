@@ -57,9 +57,15 @@ __device__ KthResult radix_kth(KeyFn key, int n, int k, unsigned* sHist, int* sS
     const int shift = 24 - 8 * pass;
     for (int i = threadIdx.x; i < 256; i += blockDim.x) sHist[i] = 0u;
     __syncthreads();
-    for (int j = threadIdx.x; j < n; j += blockDim.x) {
-      const uint32_t x = key(j);
-      if ((x & mask) == prefix) atomicAdd(&sHist[(x >> shift) & 255u], 1u);
+    for (int j0 = 0; j0 < n; j0 += blockDim.x) {
+      // lanes that hit the same bin add once (scores of one head share their top bits,
+      // so per-element atomics would serialize on a handful of bins)
+      const int j = j0 + threadIdx.x;
+      const uint32_t x = j < n ? key(j) : 0u;
+      const bool take = j < n && (x & mask) == prefix;
+      const uint32_t bin = take ? ((x >> shift) & 255u) : 256u;
+      const unsigned peers = __match_any_sync(0xffffffffu, bin);
+      if (take && (threadIdx.x & 31) == __ffs(peers) - 1) atomicAdd(&sHist[bin], (unsigned)__popc(peers));
     }
     __syncthreads();
     if (threadIdx.x < 32) {

@@ -95,13 +95,11 @@ def prefix_scores(query, prefix, stats, q_rows, *, value: bool, scaling=None, **
     desc = kv_descriptor(prefix, batch=b, heads=hkv, head_dim=d)
     scale = float(scaling if scaling is not None else d ** -0.5)
     score = torch.empty_like(mass) if value else None
-    ws = None
-    if value:
-        ws = _lib.workspace(dev, "value_score", lib.ma_value_score_workspace(b, hkv, n, d))
+    ws = _lib.workspace(dev, "value_score", lib.ma_value_score_workspace(b, hkv, n, d))
     _lib.check("ma_prefix_scores", lib.ma_prefix_scores(
         rows, desc.kv, hkv, rows_t.data_ptr(), int(rows_t.numel()), mp.data_ptr(), lp.data_ptr(), scale,
         mass.data_ptr(), _lib.i64(mass.stride(0), mass.stride(1)), _lib.ptr(score),
-        _lib.i64(*(score.stride()[:2] if value else (0, 0))), _lib.ptr(ws), 0 if ws is None else ws.numel(),
+        _lib.i64(*(score.stride()[:2] if value else (0, 0))), ws.data_ptr(), ws.numel(),
         _lib.stream_handle(dev)))
     del qkeep, rows_t
     return mass, score
