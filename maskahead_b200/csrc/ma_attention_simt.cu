@@ -1,13 +1,14 @@
 // Split-K attention over [prefix | current block] (or [read set | current block]) on
 // CUDA cores in fp32. This is the kernel family for fp32 caches (the CPU-runnable
 // configuration keeps K/V in fp32 and its selections need fp32-exact logits); bf16
-// caches use the tensor-core kernels in ma_attention_mma.cu, which write the same
-// partial-result format and share the combine kernel.
+// caches use the tcgen05 kernel in ma_attention_tc.cu; both write the split partials
+// of ma_common.cuh and share the combine kernel.
 //
 // Semantics follow the reference's split-K kernels (src/maskahead/kernels/splitk.py:
 // 115-190 _sk_fwd, 271-318 _sk_combine): every split keeps an online-softmax
 // (max m, sum l, unnormalized acc) per row; dead prefix slots and block-causally hidden
-// current keys get s = -inf; a row with no visible key keeps m = -inf, l = 0.
+// current keys get s = -inf; a row with no visible key keeps m = -inf, l = 0. The
+// partial output is written normalized (acc / l, fp32).
 #include "ma_kernels.cuh"
 
 namespace ma {
@@ -157,11 +158,12 @@ attn_partial_simt(ma_rows q, ma_kv kv, int H, ma_block cur, float scale, int cau
   if (r < R) {
     const int64_t prow = ((int64_t)bh * P.S + split) * P.Rp + r;
     if (lane8 == 0) P.ml[prow] = make_float2(m, l);
-    float* a = P.acc + prow * D;
+    float* a = reinterpret_cast<float*>(P.o) + prow * D;
+    const float inv = l > 0.f ? 1.f / l : 0.f;   // normalized output; 0 without a visible key
 #pragma unroll
     for (int i = 0; i < kMaxD / 8; ++i) {
       const int d = lane8 + 8 * i;
-      if (d < D) a[d] = o[i];
+      if (d < D) a[d] = o[i] * inv;
     }
   }
 }

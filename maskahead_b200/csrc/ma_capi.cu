@@ -88,12 +88,16 @@ bool use_mma(const ma_rows& q, const ma_kv& kv) {
   // bf16 queries over a bf16 (or bf16-dequantized packed) cache go to the tensor cores
   return q.dtype == MA_BF16 && kv.dtype == MA_BF16 && q.D == 128;
 }
+// the attention kernel also needs a positive scale (its row maxima are taken on the raw
+// logits q.k)
+bool use_mma_attention(const ma_rows& q, const ma_kv& kv, float scale) { return use_mma(q, kv) && scale > 0.f; }
 
 struct Plan {
   int nsplit;     // splits over the keys
   int split_len;  // keys per split (a multiple of the key tile)
   int S;          // partial slots per (b, h): nsplit (+1 for the current block)
   int Rp;         // padded rows
+  bool o_bf16;    // partial outputs in bf16 (tensor-core kernel)
 };
 
 int row_tile(bool mma) { return mma ? tc_row_tile() : simt_row_block(); }
@@ -106,7 +110,8 @@ Plan plan_splits(int BH, int R, int n, int Tc, bool mma) {
   Plan p;
   const int rt = row_tile(mma), kt = key_tile(mma);
   const int row_blocks = (R + rt - 1) / rt;
-  p.Rp = row_blocks * rt;
+  // tensor-core partial rows are stored per 32-row warp box
+  p.Rp = mma ? ((R + 31) / 32) * 32 : row_blocks * rt;
   if (n <= 0) {
     p.nsplit = 0;
     p.split_len = kt;
@@ -116,7 +121,7 @@ Plan plan_splits(int BH, int R, int n, int Tc, bool mma) {
     const int waves = mma ? 1 : 2;
     int target = (waves * sms) / (per_split > 0 ? per_split : 1) - (Tc > 0 ? 1 : 0);
     if (target < 1) target = 1;
-    const int min_len = (mma ? 2 : 2) * kt;
+    const int min_len = (mma ? 1 : 2) * kt;
     const int max_splits = (n + min_len - 1) / min_len;
     int ns = target < max_splits ? target : max_splits;
     if (ns > 255) ns = 255;
@@ -127,6 +132,7 @@ Plan plan_splits(int BH, int R, int n, int Tc, bool mma) {
   }
   p.S = p.nsplit + (Tc > 0 ? 1 : 0);
   if (p.S == 0) p.S = 1;
+  p.o_bf16 = mma;
   return p;
 }
 
@@ -134,7 +140,7 @@ size_t attention_ws(int B, int H, int R, int n, int D, int Tc) {
   size_t best = 0;
   for (int m = 0; m < 2; ++m) {
     const Plan p = plan_splits(B * H, R, n, Tc, m == 1);
-    const size_t bytes = partials_bytes(B * H, p.S, p.Rp, D) + 512;
+    const size_t bytes = partials_bytes(B * H, p.S, p.Rp, D, p.o_bf16) + 512;
     if (bytes > best) best = bytes;
   }
   return best;
@@ -147,7 +153,8 @@ Partials carve_partials(void* ws, int BH, const Plan& p, int D, int** err) {
   *err = reinterpret_cast<int*>(base);
   base += 256;
   P.ml = reinterpret_cast<float2*>(base);
-  P.acc = reinterpret_cast<float*>(base + (size_t)BH * p.S * p.Rp * sizeof(float2));
+  P.o = base + (size_t)BH * p.S * p.Rp * sizeof(float2);
+  P.o_bf16 = p.o_bf16 ? 1 : 0;
   P.S = p.S;
   P.Rp = p.Rp;
   (void)D;
@@ -161,9 +168,9 @@ int run_attention(const ma_rows& q, const ma_kv& kv, int H, const ma_block& cur,
                   float* o_p, void* ws, size_t ws_bytes, cudaStream_t st) {
   const int G = q.Hq / H;
   const int R = G * q.T;
-  const bool mma = use_mma(q, kv);
+  const bool mma = use_mma_attention(q, kv, scale);
   const Plan p = plan_splits(q.B * H, R, n_keys, cur.Tc, mma);
-  if (!ws || ws_bytes < partials_bytes(q.B * H, p.S, p.Rp, q.D) + 512) return MA_ERR_WORKSPACE;
+  if (!ws || ws_bytes < partials_bytes(q.B * H, p.S, p.Rp, q.D, p.o_bf16) + 512) return MA_ERR_WORKSPACE;
   int* err = nullptr;
   const Partials P = carve_partials(ws, q.B * H, p, q.D, &err);
   int rc;
@@ -243,9 +250,10 @@ int ma_prefix_scores(const ma_rows* q, const ma_kv* kv, int H, const int32_t* q_
   }
   cudaStream_t st = (cudaStream_t)stream;
   if (tc) {
-    rc = launch_prefix_mass_tc(*q, *kv, H, q_rows, T2, m_p, l_p, scale, mass, smass[0], smass[1],
-                               score ? w.part : nullptr, w.counters, score ? w.centre : nullptr, w.err, st);
-    if (rc || !score) return rc;
+    bool fused = false;
+    rc = launch_prefix_mass_tc(*q, *kv, H, q_rows, T2, m_p, l_p, scale, mass, smass[0], smass[1], score,
+                               score ? sscore[0] : 0, score ? sscore[1] : 0, w, score != nullptr, &fused, st);
+    if (rc || !score || fused) return rc;
     return launch_value_apply(*kv, q->B, H, q->D, mass, smass[0], smass[1], w.centre, score, sscore[0],
                               sscore[1], st);
   }

@@ -152,17 +152,22 @@ __device__ __forceinline__ void kv_read8(const ma_kv& kv, int b, int h, int j, i
 }
 
 // ----------------------------------------------------------------------------------
-// Split-K partial results: per (b*H + h, split, row) a pair (m, l) and acc[D], fp32.
+// Split-K partial results: per (b*H + h, split, row) the pair (m, l) -- the split's
+// row max and its softmax sum under that max -- and the split's normalized output
+// o = acc / l over D channels (0 for a row without a visible key). The CUDA-core kernel
+// writes o in fp32, the tensor-core kernel in bf16 (the combine weights each split by
+// l * exp(m - M), so normalized outputs lose nothing to the split's scale).
 // ----------------------------------------------------------------------------------
 struct Partials {
   float2* ml;   // [BH][S][Rp]
-  float* acc;   // [BH][S][Rp][D]
+  void* o;      // [BH][S][Rp][D], fp32 or bf16 (o_bf16)
+  int o_bf16;   // 1: o holds bf16
   int S;        // splits (the current block, when present, is the last one)
   int Rp;       // padded rows
 };
 
-__host__ __device__ inline size_t partials_bytes(int BH, int S, int Rp, int D) {
-  return (size_t)BH * S * Rp * (sizeof(float2) + sizeof(float) * D);
+__host__ __device__ inline size_t partials_bytes(int BH, int S, int Rp, int D, bool o_bf16) {
+  return (size_t)BH * S * Rp * (sizeof(float2) + (o_bf16 ? 2 : 4) * (size_t)D);
 }
 
 // ----------------------------------------------------------------------------------

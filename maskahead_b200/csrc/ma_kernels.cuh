@@ -30,12 +30,15 @@ int launch_prefix_mass(const ma_rows& q, const ma_kv& kv, int H, const int32_t* 
                        const float* m_p, const float* l_p, float scale, float* mass,
                        int64_t sm0, int64_t sm1, cudaStream_t st);
 size_t value_score_ws_bytes(int B, int H, int n, int D);
+// The sync block's layout does not depend on B*H, so a workspace shared by calls of
+// different sizes never reads one call's words as another's counters.
 struct ValueWs {
-  unsigned* counters;  // [BH], zero between calls
   int* err;            // device-side error word (a bounded wait gave up)
+  uint2* sync;         // [BH]: x = arrival counter (zero between calls), y = centre generation
   float* centre;       // [BH][D]
   float* part;         // [BH][tiles][D+1]
 };
+size_t value_sync_bytes(int BH);
 ValueWs carve_value_ws(void* ws, int BH, int D);
 int launch_value_apply(const ma_kv& kv, int B, int H, int D, const float* a, int64_t sa0, int64_t sa1,
                        const float* centre, float* score, int64_t ss0, int64_t ss1, cudaStream_t st);
@@ -44,9 +47,11 @@ int launch_value_score(const ma_kv& kv, int B, int H, int D, const float* a, int
                        cudaStream_t st);
 
 // ma_mass_tc.cu (bf16, R2 = G*T2 <= 256): mass, optionally the value-score centre
+// With score != NULL the value score a_j ||v_j - c|| is computed in the same (cooperative)
+// launch; *fused reports whether it was (else the caller runs launch_value_apply).
 int launch_prefix_mass_tc(const ma_rows& q, const ma_kv& kv, int H, const int32_t* q_rows, int T2, const float* m_p,
-                          const float* l_p, float scale, float* mass, int64_t sm0, int64_t sm1, float* part,
-                          unsigned* counters, float* centre, int* err, cudaStream_t st);
+                          const float* l_p, float scale, float* mass, int64_t sm0, int64_t sm1, float* score,
+                          int64_t ss0, int64_t ss1, const ValueWs& w, bool want_centre, bool* fused, cudaStream_t st);
 
 // ma_select.cu
 int launch_select_topk(const float* score, int B, int H, int n, int64_t ss0, int64_t ss1,

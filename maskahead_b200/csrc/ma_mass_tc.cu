@@ -1,19 +1,26 @@
-// Prefix mass with tcgen05 MMAs, with the value-score centre fused in.
+// Prefix mass with tcgen05 MMAs, with the value-score centre -- and the value score
+// itself -- fused in.
 //
 // Transposed product: for a tile of 128 prefix slots, S^T = K Q^T (tcgen05.mma, M = 128
 // slots, N = the selection rows padded to 16, K = 128 channels; accumulator in TMEM), so
 // TMEM lane j holds slot j's logits against every selection row. Each thread owns one
 // slot (its lane) and half of the rows: it loads its logits with tcgen05.ld and sums
-//     exp(s_rj * scale - M_p,r) / L_p,r          (splitk.py:320-359; reference.py:318-366)
+//     exp(s_rj * scale - M_p,r) / L_p,r = 2^(s_rj * scale * log2e - B_r),
+//     B_r = M_p,r * log2e + log2(L_p,r)            (splitk.py:320-359; reference.py:318-366)
 // in registers; the two halves meet in shared memory in a fixed order, then
 // a_j = sum / R2 (0 on dead slots). bf16 products are exact in fp32 and accumulate in
-// fp32, so a_j is fp32-accurate. With a centre requested the CTA also accumulates
-// sum_j a_j v_j and sum_j a_j from the V tiles it streams, and the last CTA of the head
-// reduces the per-CTA partials in slot order into c = sum a v / max(sum a, 1e-12)
-// (session.py:27-40, 870-899) for the value-apply kernel.
+// fp32, so a_j is fp32-accurate.
+//
+// With a centre requested the CTA also accumulates sum_j a_j v_j and sum_j a_j from the
+// V tiles it streams, and the last CTA of the head (a counter in the workspace) reduces
+// the per-CTA partials in CTA order into c = sum a v / max(sum a, 1e-12) (session.py:
+// 27-40, 870-899), then advances the head's generation word. With the score requested
+// as well the launch is cooperative (every CTA resident): each CTA waits (bounded) for
+// its head's generation to advance, reads c and writes a_j * ||v_j - c|| for its own slots
+// -- one launch for mass, centre and score.
 //
 // Slot tiles stream through a 2-stage cp.async ring (each CTA holds its whole range,
-// up to 256 slots, in flight from the start). Waits on the tensor core are bounded.
+// up to 256 slots, in flight from the start). Every wait is bounded.
 #include "ma_kernels.cuh"
 #include "ma_mma.cuh"
 #include "ma_tcgen05.cuh"
@@ -36,6 +43,8 @@ constexpr int kQBytes = kMaxRows * kD * 2;  // 64 KB
 constexpr int kTileBytes = kTile * kD * 2;  // 32 KB (K or V)
 constexpr int kSmemBytes = 1024 + kQBytes + 2 * kStages * kTileBytes;
 constexpr uint32_t kTmemCols = 256;
+constexpr int kMaxCtas = 1024;              // partial slots per head (the launcher never exceeds)
+constexpr uint64_t kWaitNs = 200000000ull;  // bound on the wait for the head's centre
 
 struct Args {
   ma_rows q;
@@ -45,8 +54,10 @@ struct Args {
   const float* l_p;
   float* mass;
   int64_t sm0, sm1;
+  float* score;         // fused value score (cooperative launch), or null
+  int64_t ss0, ss1;
   float* part;          // [BH][ctas][D+1] centre partials (centre only)
-  unsigned* counters;   // [BH]
+  uint2* sync;          // [BH]: arrival counter, centre generation
   float* centre;        // [BH][D]
   int* err;
   float scale;
@@ -86,21 +97,30 @@ __device__ __forceinline__ void load_tile(const Args& A, int b, int h, int j0, i
   cp_async_commit();
 }
 
+__device__ __forceinline__ unsigned ld_acquire(const unsigned* p) {
+  unsigned v;
+  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];\n" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
 template <bool PACKED, bool CENTRE>
 __global__ void __launch_bounds__(kThreads, 1) prefix_mass_tc(const Args A) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sQ = smem;                         // K-major [2 d blocks][Npad rows][128 B]
   uint8_t* sRing = sQ + kQBytes;              // [stage][K tile (swizzled) | V tile (row-major)]
-  __shared__ float sM2[kMaxRows], sInvL[kMaxRows];
+  __shared__ __align__(16) float sB[kMaxRows];   // per selection row: B_r (+inf: no contribution)
+  __shared__ int sRowT[kMaxRows];                // block position of selection row r (-1: none)
   __shared__ float sHalf[2][kTile];
-  __shared__ float sA[kTile];
+  __shared__ __align__(16) float sA[kTile];
   __shared__ uint8_t sOk[kStages][kTile];
-  __shared__ float sRed[kThreads];
+  __shared__ float sRed[4][kD];
+  __shared__ float sTot[kD + 1];
+  __shared__ float sAsum[4];
   __shared__ uint32_t s_taddr;
   __shared__ __align__(8) uint64_t mbar;
-  __shared__ int s_abort;
-  __shared__ bool sLast;
+  __shared__ int s_abort, s_wait_ok, sLast;
+  __shared__ unsigned sGen;
 
   const int n = A.kv.nq + A.kv.nf;
   const int bh = blockIdx.y;
@@ -118,30 +138,38 @@ __global__ void __launch_bounds__(kThreads, 1) prefix_mass_tc(const Args A) {
   const float inv_rows = 1.f / (float)R2;
   const float c2 = A.scale * kLog2e;
 
-  // selection rows: r2 = g*T2 + i -> query row (h*G + g, q_rows[i]); per-row constants
+  // the head's centre generation before this CTA arrives (the last CTA advances it)
+  if (CENTRE && threadIdx.x == 0) sGen = *reinterpret_cast<volatile const unsigned*>(&A.sync[bh].y);
+  // selection rows r2 = g*T2 + i -> query row (h*G + g, q_rows[i]) and B_r, one row per thread
+  for (int rr = threadIdx.x; rr < Npad; rr += kThreads) {
+    const int g = rr / A.T2;
+    const int t = rr < R2 ? A.q_rows[rr - g * A.T2] : -1;
+    const bool ok = t >= 0 && t < T;
+    float Bv = INFINITY;   // exp2(s - inf) = 0: no contribution
+    if (ok) {
+      const int64_t ri = (int64_t)bh * G * T + (int64_t)g * T + t;
+      const float L = A.l_p[ri];
+      if (L > 0.f) Bv = fmaf(A.m_p[ri], kLog2e, log2f(L));
+    }
+    sRowT[rr] = ok ? t : -1;
+    sB[rr] = Bv;
+  }
+  __syncthreads();
   {
     const __nv_bfloat16* qp = reinterpret_cast<const __nv_bfloat16*>(A.q.q);
     for (int c = threadIdx.x; c < Npad * kChunks; c += kThreads) {
       const int rr = c / kChunks, ch = c % kChunks;
-      const int g = rr / A.T2;
-      const int t = rr < R2 ? A.q_rows[rr - g * A.T2] : -1;
-      const bool ok = t >= 0 && t < T;
+      const int t = sRowT[rr];
       uint8_t* dst = sQ + kmajor_off(rr, ch, Npad);
-      if (ok) {
+      if (t >= 0) {
+        const int g = rr / A.T2;
         cp_async16(tc::smem_addr(dst), qp + (int64_t)b * A.q.sq[0] + (int64_t)(h * G + g) * A.q.sq[1] + (int64_t)t * A.q.sq[2] + ch * 8, true);
       } else {
         *reinterpret_cast<uint4*>(dst) = make_uint4(0, 0, 0, 0);
       }
-      if (ch == 0) {
-        const int64_t ri = (int64_t)bh * G * T + (int64_t)g * T + t;
-        const float L = ok ? A.l_p[ri] : 0.f;
-        const bool live_row = ok && L > 0.f;
-        sM2[rr] = live_row ? A.m_p[ri] * kLog2e : INFINITY;   // exp2(s - inf) = 0: no contribution
-        sInvL[rr] = live_row ? 1.f / L : 0.f;
-      }
     }
   }
-  for (int st = 0; st < kStages; ++st) {
+  for (int st = 0; st < kStages; ++st) {   // the queries join the group of the first tile
     const int j0 = begin + st * kTile;
     uint8_t* sK = sRing + 2 * st * kTileBytes;
     if (j0 < end) load_tile<PACKED, CENTRE>(A, b, h, j0, end, sK, sK + kTileBytes, sOk[st]);
@@ -150,6 +178,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefix_mass_tc(const Args A) {
   if (threadIdx.x == 0) {
     mbar_init(&mbar, 1);
     s_abort = 0;
+    s_wait_ok = 1;
   }
   if (warp == 0) tmem_alloc(&s_taddr, kTmemCols);
   fence_before_sync();
@@ -162,8 +191,9 @@ __global__ void __launch_bounds__(kThreads, 1) prefix_mass_tc(const Args A) {
   const int c_lo = chalf * cols_half;
   uint32_t phase = 0;
   int stage = 0;
-  float cacc = 0.f, asum = 0.f;
-  const int cd = threadIdx.x & (kD - 1), vhalf = threadIdx.x >> 7;
+  // centre: channel pair cp (channels 2cp, 2cp+1) over key quarter kq of every tile
+  const int cp = threadIdx.x & 63, kq = threadIdx.x >> 6;
+  float cacc0 = 0.f, cacc1 = 0.f, asum = 0.f;
   bool aborted = false;
 
   for (int j0 = begin; j0 < end; j0 += kTile) {
@@ -192,20 +222,26 @@ __global__ void __launch_bounds__(kThreads, 1) prefix_mass_tc(const Args A) {
     phase ^= 1;
     fence_after_sync();
     if (!ok) s_abort = 1;
-    // this thread: slot slot_lane, rows [c_lo, c_lo + cols_half)
-    float acc = 0.f;
+    // this thread: slot slot_lane, rows [c_lo, c_lo + cols_half), in row order
+    float acc[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll 1
     for (int c0 = 0; c0 < cols_half; c0 += 32) {
       float sv[32];
-      tmem_ld32(tRow + c_lo + c0, sv);   // cols_half is a multiple of 8: reads stay in the allocation
+      tmem_ld32(tRow + c_lo + c0, sv);   // columns stay inside the 256-column allocation
       tmem_ld_wait();
+      const int lim = cols_half - c0;
 #pragma unroll
-      for (int i = 0; i < 32; ++i) {
-        const int r = c_lo + c0 + i;
-        if (c0 + i < cols_half) acc = fmaf(ex2(fmaf(sv[i], c2, -sM2[r])), sInvL[r], acc);
+      for (int i = 0; i < 32; i += 4) {
+        const float4 b4 = *reinterpret_cast<const float4*>(&sB[c_lo + c0 + i]);
+        if (i < lim) {   // lim is a multiple of 8
+          acc[0] += ex2(fmaf(sv[i], c2, -b4.x));
+          acc[1] += ex2(fmaf(sv[i + 1], c2, -b4.y));
+          acc[2] += ex2(fmaf(sv[i + 2], c2, -b4.z));
+          acc[3] += ex2(fmaf(sv[i + 3], c2, -b4.w));
+        }
       }
     }
-    sHalf[chalf][slot_lane] = acc;
+    sHalf[chalf][slot_lane] = (acc[0] + acc[1]) + (acc[2] + acc[3]);
     __syncthreads();
     if (threadIdx.x < kTile) {
       const int j = j0 + threadIdx.x;
@@ -215,13 +251,18 @@ __global__ void __launch_bounds__(kThreads, 1) prefix_mass_tc(const Args A) {
     }
     if (CENTRE) {
       __syncthreads();
-      const __nv_bfloat16* v = reinterpret_cast<const __nv_bfloat16*>(sV);
-      const int jlo = vhalf * (kTile / 2);
-#pragma unroll 4
-      for (int jj = jlo; jj < jlo + kTile / 2; ++jj) {
-        const float a = sA[jj];
-        cacc = fmaf(a, __bfloat162float(v[jj * kD + cd]), cacc);
-        asum += a;
+      const __nv_bfloat162* v2 = reinterpret_cast<const __nv_bfloat162*>(sV);   // [key][64 channel pairs]
+#pragma unroll 2
+      for (int j4 = 0; j4 < kTile / 4; j4 += 4) {
+        const float4 a4 = *reinterpret_cast<const float4*>(&sA[kq * (kTile / 4) + j4]);
+        const float av[4] = {a4.x, a4.y, a4.z, a4.w};
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          const float2 v = __bfloat1622float2(v2[(kq * (kTile / 4) + j4 + u) * (kD / 2) + cp]);
+          cacc0 = fmaf(av[u], v.x, cacc0);
+          cacc1 = fmaf(av[u], v.y, cacc1);
+          asum += av[u];
+        }
       }
     }
     fence_before_sync();
@@ -234,41 +275,111 @@ __global__ void __launch_bounds__(kThreads, 1) prefix_mass_tc(const Args A) {
 
   if (aborted && threadIdx.x == 0) atomicExch(A.err, 1);
   if (aborted) mbar_wait(&mbar, phase);     // drain the in-flight MMA (bounded)
+  cp_async_wait<0>();
   fence_before_sync();
   __syncthreads();
   fence_after_sync();
   if (warp == 0) tmem_dealloc(taddr, kTmemCols);
   if (!CENTRE) return;
 
-  // per-CTA centre partial, then the last CTA of the head reduces them in CTA order
+  // per-CTA centre partial (key quarters summed in order); the last CTA of the head
+  // reduces the partials in CTA order and publishes c by advancing the generation
+  sRed[kq][2 * cp] = cacc0;
+  sRed[kq][2 * cp + 1] = cacc1;
+  if (cp == 0) sAsum[kq] = asum;
+  __syncthreads();
   float* mine = A.part + ((int64_t)bh * gridDim.x + blockIdx.x) * (kD + 1);
-  sRed[threadIdx.x] = aborted ? NAN : cacc;
-  if (cd == 0) sHalf[0][vhalf] = asum;
-  __syncthreads();
-  if (threadIdx.x < kD) mine[threadIdx.x] = sRed[threadIdx.x] + sRed[threadIdx.x + kD];
-  if (threadIdx.x == 0) mine[kD] = sHalf[0][0] + sHalf[0][1];
+  if (threadIdx.x < kD)
+    mine[threadIdx.x] = aborted ? NAN : ((sRed[0][threadIdx.x] + sRed[1][threadIdx.x]) + sRed[2][threadIdx.x]) + sRed[3][threadIdx.x];
+  if (threadIdx.x == 0) mine[kD] = ((sAsum[0] + sAsum[1]) + sAsum[2]) + sAsum[3];
   __threadfence();
   __syncthreads();
-  if (threadIdx.x == 0) sLast = atomicAdd(&A.counters[bh], 1u) == gridDim.x - 1;
+  if (threadIdx.x == 0) sLast = atomicAdd(&A.sync[bh].x, 1u) == gridDim.x - 1 ? 1 : 0;
   __syncthreads();
-  if (!sLast) return;
-  __threadfence();
-  const float* base = A.part + (int64_t)bh * gridDim.x * (kD + 1);
-  if (threadIdx.x <= kD) {
-    float tot = 0.f;
-    for (unsigned t = 0; t < gridDim.x; ++t) tot += __ldcg(base + (int64_t)t * (kD + 1) + threadIdx.x);
-    sRed[threadIdx.x] = tot;
+  if (sLast) {
+    __threadfence();
+    if (threadIdx.x <= kD) {
+      const float* base = A.part + (int64_t)bh * gridDim.x * (kD + 1) + threadIdx.x;
+      float tot = 0.f;
+      for (unsigned t0 = 0; t0 < gridDim.x; t0 += 16) {
+        float v[16];
+#pragma unroll
+        for (int i = 0; i < 16; ++i) v[i] = t0 + i < gridDim.x ? __ldcg(base + (int64_t)(t0 + i) * (kD + 1)) : 0.f;
+#pragma unroll
+        for (int i = 0; i < 16; ++i) tot += v[i];   // CTA order
+      }
+      sTot[threadIdx.x] = tot;
+    }
+    __syncthreads();
+    if (threadIdx.x < kD) A.centre[(int64_t)bh * kD + threadIdx.x] = sTot[threadIdx.x] / fmaxf(sTot[kD], 1e-12f);
+    if (threadIdx.x == 0) A.sync[bh].x = 0u;
+    __threadfence();
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      __threadfence();
+      atomicAdd(&A.sync[bh].y, 1u);
+    }
+  }
+  if (A.score == nullptr) return;
+
+  // fused value score (cooperative launch: every CTA of the head is resident)
+  if (!sLast && threadIdx.x == 0) {
+    const uint64_t t0 = global_ns();
+    while (ld_acquire(&A.sync[bh].y) == sGen) {
+      if (global_ns() - t0 > kWaitNs) {
+        s_wait_ok = 0;
+        atomicExch(A.err, 1);
+        break;
+      }
+      __nanosleep(256);
+    }
   }
   __syncthreads();
-  if (threadIdx.x < kD) A.centre[(int64_t)bh * kD + threadIdx.x] = sRed[threadIdx.x] / fmaxf(sRed[kD], 1e-12f);
-  if (threadIdx.x == 0) A.counters[bh] = 0u;
+  const bool ok_c = s_wait_ok != 0;
+  const int grp = threadIdx.x >> 4, l16 = threadIdx.x & 15;
+  float cc[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) cc[i] = __ldcg(A.centre + (int64_t)bh * kD + 8 * l16 + i);
+  constexpr int kBatch = 4;
+  for (int jb = begin; jb < end; jb += (kThreads / 16) * kBatch) {
+    float f[kBatch][8];
+    bool live[kBatch];
+#pragma unroll
+    for (int u = 0; u < kBatch; ++u) {
+      const int j = jb + u * (kThreads / 16) + grp;
+      live[u] = j < end && kv_live(A.kv, H, b, h, j);
+      if (live[u]) {
+        kv_read8<false>(A.kv, b, h, j, l16, f[u]);
+      } else {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) f[u][i] = cc[i];
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < kBatch; ++u) {
+      float s2 = 0.f;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const float x = f[u][i] - cc[i];
+        s2 = fmaf(x, x, s2);
+      }
+#pragma unroll
+      for (int o = 8; o > 0; o >>= 1) s2 += __shfl_xor_sync(0xffffffffu, s2, o);
+      const int j = jb + u * (kThreads / 16) + grp;
+      if (l16 == 0 && j < end) {
+        const float aj = live[u] ? A.mass[(int64_t)b * A.sm0 + (int64_t)h * A.sm1 + j] : 0.f;
+        A.score[(int64_t)b * A.ss0 + (int64_t)h * A.ss1 + j] = ok_c ? aj * sqrtf(s2) : NAN;
+      }
+    }
+  }
 }
 
 }  // namespace
 
 int launch_prefix_mass_tc(const ma_rows& q, const ma_kv& kv, int H, const int32_t* q_rows, int T2, const float* m_p,
-                          const float* l_p, float scale, float* mass, int64_t sm0, int64_t sm1, float* part,
-                          unsigned* counters, float* centre, int* err, cudaStream_t st) {
+                          const float* l_p, float scale, float* mass, int64_t sm0, int64_t sm1, float* score,
+                          int64_t ss0, int64_t ss1, const ValueWs& w, bool want_centre, bool* fused, cudaStream_t st) {
+  *fused = false;
   const int n = kv.nq + kv.nf;
   const int BH = q.B * H;
   Args A;
@@ -280,10 +391,13 @@ int launch_prefix_mass_tc(const ma_rows& q, const ma_kv& kv, int H, const int32_
   A.mass = mass;
   A.sm0 = sm0;
   A.sm1 = sm1;
-  A.part = part;
-  A.counters = counters;
-  A.centre = centre;
-  A.err = err;
+  A.score = nullptr;
+  A.ss0 = ss0;
+  A.ss1 = ss1;
+  A.part = want_centre ? w.part : nullptr;
+  A.sync = w.sync;
+  A.centre = want_centre ? w.centre : nullptr;
+  A.err = w.err;
   A.scale = scale;
   A.H = H;
   A.T2 = T2;
@@ -295,16 +409,42 @@ int launch_prefix_mass_tc(const ma_rows& q, const ma_kv& kv, int H, const int32_
   spc = ((spc + kTile - 1) / kTile) * kTile;
   A.slots_per_cta = spc < kTile ? kTile : spc;
   dim3 grid((n + A.slots_per_cta - 1) / A.slots_per_cta, BH);
+  if ((int)grid.x > kMaxCtas) return MA_ERR_UNSUPPORTED;
   const bool packed = kv.layout != MA_KV_DENSE;
-  const bool cen = centre != nullptr;
   auto go = [&](auto kernel) -> int {
     if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes) != cudaSuccess)
       return MA_ERR_CUDA;
+    if (score != nullptr && want_centre) {
+      // the fused score needs every CTA resident at once: a cooperative launch that fits
+      int dev = 0, coop = 0, per_sm = 0;
+      if (cudaGetDevice(&dev) == cudaSuccess &&
+          cudaDeviceGetAttribute(&coop, cudaDevAttrCooperativeLaunch, dev) == cudaSuccess && coop &&
+          cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, kThreads, kSmemBytes) == cudaSuccess &&
+          (long long)grid.x * grid.y <= (long long)per_sm * sms) {
+        Args Ac = A;
+        Ac.score = score;
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = grid;
+        cfg.blockDim = dim3(kThreads);
+        cfg.dynamicSmemBytes = kSmemBytes;
+        cfg.stream = st;
+        cudaLaunchAttribute attr[1];
+        attr[0].id = cudaLaunchAttributeCooperative;
+        attr[0].val.cooperative = 1;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+        if (cudaLaunchKernelEx(&cfg, kernel, Ac) == cudaSuccess) {
+          *fused = true;
+          return MA_OK;
+        }
+        (void)cudaGetLastError();
+      }
+    }
     kernel<<<grid, kThreads, kSmemBytes, st>>>(A);
     return cudaGetLastError() == cudaSuccess ? MA_OK : MA_ERR_CUDA;
   };
-  if (packed) return cen ? go(prefix_mass_tc<true, true>) : go(prefix_mass_tc<true, false>);
-  return cen ? go(prefix_mass_tc<false, true>) : go(prefix_mass_tc<false, false>);
+  if (packed) return want_centre ? go(prefix_mass_tc<true, true>) : go(prefix_mass_tc<true, false>);
+  return want_centre ? go(prefix_mass_tc<false, true>) : go(prefix_mass_tc<false, false>);
 }
 
 }  // namespace ma

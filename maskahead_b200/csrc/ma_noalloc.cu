@@ -55,8 +55,7 @@ int ma_value_score_noalloc(const ma_kv* kv, int B, int H, int D, const float* a,
   int rc = scratch_address(&ws);
   if (rc != MA_OK) return rc;
   // the per-head counters must start at zero; earlier calls leave the rest behind
-  const size_t counters = (((size_t)B * H * sizeof(unsigned) + 255) / 256) * 256;
-  if (cudaMemsetAsync(ws, 0, counters, (cudaStream_t)stream) != cudaSuccess) return MA_ERR_CUDA;
+  if (cudaMemsetAsync(ws, 0, ma::value_sync_bytes(B * H), (cudaStream_t)stream) != cudaSuccess) return MA_ERR_CUDA;
   return ma_value_score(kv, B, H, D, a, sa, score, sscore, ws, kScratchBytes, stream);
 }
 

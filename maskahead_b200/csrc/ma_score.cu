@@ -136,7 +136,7 @@ __device__ __forceinline__ void stage_values(const ma_kv& kv, int H, int D, int 
 
 __global__ void __launch_bounds__(kThreads)
 value_centre_kernel(ma_kv kv, int H, int D, const float* __restrict__ a, int64_t sa0, int64_t sa1,
-                    int ntile, float* __restrict__ part, unsigned* __restrict__ counters,
+                    int ntile, float* __restrict__ part, uint2* __restrict__ sync,
                     float* __restrict__ centre) {
   const int n = kv.nq + kv.nf;
   const int bh = blockIdx.y;
@@ -177,7 +177,7 @@ value_centre_kernel(ma_kv kv, int H, int D, const float* __restrict__ a, int64_t
   __threadfence();
   __syncthreads();
   if (threadIdx.x == 0) {
-    const unsigned prev = atomicAdd(&counters[bh], 1u);
+    const unsigned prev = atomicAdd(&sync[bh].x, 1u);
     sLast = prev == (unsigned)(ntile - 1);
   }
   __syncthreads();
@@ -191,8 +191,15 @@ value_centre_kernel(ma_kv kv, int H, int D, const float* __restrict__ a, int64_t
   }
   __syncthreads();
   if (threadIdx.x < D) centre[(int64_t)bh * D + threadIdx.x] = sRed[threadIdx.x] / fmaxf(sRed[D], 1e-12f);
-  if (threadIdx.x == 0) counters[bh] = 0u;   // ready for the next call
+  if (threadIdx.x == 0) sync[bh].x = 0u;   // ready for the next call
 }
+
+// a_j * ||v_j - c||: one group of D/8 lanes (a half-warp for D = 128) per key, each lane
+// holding 8 channels of the row (one 16-byte load of a bf16 row) and the same 8 channels
+// of the centre in registers; every group takes kApplyKeys keys with all loads issued
+// before the first reduction. Dead slots score 0.
+constexpr int kApplyKeys = 4;
+constexpr int kApplyTok = (kThreads / 16) * kApplyKeys;   // keys per CTA
 
 __global__ void __launch_bounds__(kThreads)
 value_apply_kernel(ma_kv kv, int H, int D, const float* __restrict__ a, int64_t sa0, int64_t sa1,
@@ -201,25 +208,39 @@ value_apply_kernel(ma_kv kv, int H, int D, const float* __restrict__ a, int64_t 
   const int n = kv.nq + kv.nf;
   const int bh = blockIdx.y;
   const int b = bh / H, h = bh - (bh / H) * H;
-  const int j0 = blockIdx.x * kVTok;
-  __shared__ float sV[kVTok][kMaxD];
-  __shared__ float sA[kVTok];
-  __shared__ float sC[kMaxD];
-  stage_values(kv, H, D, b, h, j0, n, a, sa0, sa1, sV, sA);
-  if (threadIdx.x < D) sC[threadIdx.x] = __ldcg(centre + (int64_t)bh * D + threadIdx.x);
-  __syncthreads();
-  // one key per half-warp
-  const int hw = threadIdx.x >> 4, l16 = threadIdx.x & 15;
-  for (int jj = hw; jj < kVTok; jj += kThreads / 16) {
-    float s = 0.f;
-    for (int d = l16; d < D; d += 16) {
-      const float x = sV[jj][d] - sC[d];
-      s = fmaf(x, x, s);
+  const int grp = threadIdx.x >> 4, l16 = threadIdx.x & 15;
+  const bool lane_on = l16 < D / 8;
+  float cc[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) cc[i] = lane_on ? __ldcg(centre + (int64_t)bh * D + 8 * l16 + i) : 0.f;
+  float f[kApplyKeys][8];
+  bool live[kApplyKeys];
+#pragma unroll
+  for (int u = 0; u < kApplyKeys; ++u) {
+    const int j = blockIdx.x * kApplyTok + u * (kThreads / 16) + grp;
+    live[u] = j < n && kv_live(kv, H, b, h, j);
+    if (live[u] && lane_on) {
+      kv_read8<false>(kv, b, h, j, l16, f[u]);
+    } else {
+#pragma unroll
+      for (int i = 0; i < 8; ++i) f[u][i] = cc[i];
+    }
+  }
+#pragma unroll
+  for (int u = 0; u < kApplyKeys; ++u) {
+    float s2 = 0.f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const float x = f[u][i] - cc[i];
+      s2 = fmaf(x, x, s2);
     }
 #pragma unroll
-    for (int o = 8; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
-    const int j = j0 + jj;
-    if (l16 == 0 && j < n) score[(int64_t)b * ss0 + (int64_t)h * ss1 + j] = sA[jj] * sqrtf(s);
+    for (int o = 8; o > 0; o >>= 1) s2 += __shfl_xor_sync(0xffffffffu, s2, o);
+    const int j = blockIdx.x * kApplyTok + u * (kThreads / 16) + grp;
+    if (l16 == 0 && j < n) {
+      const float aj = live[u] ? a[(int64_t)b * sa0 + (int64_t)h * sa1 + j] : 0.f;
+      score[(int64_t)b * ss0 + (int64_t)h * ss1 + j] = aj * sqrtf(s2);
+    }
   }
 }
 
@@ -240,11 +261,14 @@ int launch_prefix_mass(const ma_rows& q, const ma_kv& kv, int H, const int32_t* 
   return cudaGetLastError() == cudaSuccess ? MA_OK : MA_ERR_CUDA;
 }
 
-// workspace: counters [BH] (256-byte aligned block), centre [BH][D], partials [BH][ntile][D+1]
+// workspace: the error word and the per-head (counter, generation) pairs (one 256-byte
+// aligned block), centre [BH][D], partials [BH][ntile][D+1]
+size_t value_sync_bytes(int BH) { return ((8 + (size_t)BH * sizeof(uint2) + 255) / 256) * 256; }
+
 size_t value_score_ws_bytes(int B, int H, int n, int D) {
   const size_t BH = (size_t)B * H;
   const size_t ntile = (size_t)(n + kVTok - 1) / kVTok;
-  const size_t cnt = (((BH + 1) * sizeof(unsigned) + 255) / 256) * 256;
+  const size_t cnt = value_sync_bytes((int)BH);
   const size_t cen = ((BH * D * sizeof(float) + 255) / 256) * 256;
   return cnt + cen + BH * (ntile > 0 ? ntile : 1) * (D + 1) * sizeof(float);
 }
@@ -252,9 +276,9 @@ size_t value_score_ws_bytes(int B, int H, int n, int D) {
 ValueWs carve_value_ws(void* ws, int BH, int D) {
   ValueWs w;
   char* p = reinterpret_cast<char*>(ws);
-  w.counters = reinterpret_cast<unsigned*>(p);
-  w.err = reinterpret_cast<int*>(p) + BH;
-  p += (((size_t)(BH + 1) * sizeof(unsigned) + 255) / 256) * 256;
+  w.err = reinterpret_cast<int*>(p);
+  w.sync = reinterpret_cast<uint2*>(p + 8);
+  p += value_sync_bytes(BH);
   w.centre = reinterpret_cast<float*>(p);
   p += (((size_t)BH * D * sizeof(float) + 255) / 256) * 256;
   w.part = reinterpret_cast<float*>(p);
@@ -265,7 +289,7 @@ int launch_value_apply(const ma_kv& kv, int B, int H, int D, const float* a, int
                        const float* centre, float* score, int64_t ss0, int64_t ss1, cudaStream_t st) {
   const int n = kv.nq + kv.nf;
   if (n == 0) return MA_OK;
-  dim3 grid((n + kVTok - 1) / kVTok, B * H);
+  dim3 grid((n + kApplyTok - 1) / kApplyTok, B * H);
   value_apply_kernel<<<grid, kThreads, 0, st>>>(kv, H, D, a, sa0, sa1, centre, score, ss0, ss1);
   return cudaGetLastError() == cudaSuccess ? MA_OK : MA_ERR_CUDA;
 }
@@ -278,7 +302,7 @@ int launch_value_score(const ma_kv& kv, int B, int H, int D, const float* a, int
   const int ntile = (n + kVTok - 1) / kVTok;
   const ValueWs w = carve_value_ws(ws, B * H, D);
   dim3 grid(ntile, B * H);
-  value_centre_kernel<<<grid, kThreads, 0, st>>>(kv, H, D, a, sa0, sa1, ntile, w.part, w.counters, w.centre);
+  value_centre_kernel<<<grid, kThreads, 0, st>>>(kv, H, D, a, sa0, sa1, ntile, w.part, w.sync, w.centre);
   if (cudaGetLastError() != cudaSuccess) return MA_ERR_CUDA;
   return launch_value_apply(kv, B, H, D, a, sa0, sa1, w.centre, score, ss0, ss1, st);
 }

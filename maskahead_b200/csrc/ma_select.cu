@@ -2,7 +2,8 @@
 // the indexed gather of dequantized rows.
 //
 // Top-k is a block-wide MSB-first radix select on order-preserving uint32 keys (four
-// 8-bit digits, shared-memory histograms), followed by an index-order compaction, so
+// 8-bit digits, shared-memory histograms; the keys of rows up to 16384 slots stay in
+// registers), followed by an index-order compaction, so
 // the read set comes out already sorted ascending (the reference sorts after
 // torch.topk: src/maskahead/kernels/ops.py:377-380, 509-516). Ties at the k-th score
 // go to the lower slot index.
@@ -168,6 +169,125 @@ select_topk_kernel(const float* __restrict__ score, int H, int n, int64_t ss0, i
   }
 }
 
+// Register-resident variant for n <= 1024 * PER (PER keys per thread, thread t owning
+// slots [t*PER, t*PER + PER)): the keys are read once from global memory and stay in
+// registers through the four radix passes and the emission, so the passes touch shared
+// memory only for the 256-bin histogram. Histogram updates are aggregated per warp on
+// lane 0's bin (ballot), which absorbs the heavy collisions of the leading digits; the
+// remaining lanes add individually. The emission needs one block scan of the packed
+// counts (ties << 16 | larger): the ties taken before a thread are min(ties before, need).
+template <int PER>
+__global__ void __launch_bounds__(kSelThreads)
+select_topk_reg(const float* __restrict__ score, int H, int n, int64_t ss0, int64_t ss1,
+                const uint8_t* __restrict__ mask, int k, int64_t* __restrict__ indices,
+                float* __restrict__ values, int64_t si0, int64_t si1) {
+  __shared__ unsigned sHist[256];
+  __shared__ int sSel[2][2];
+  __shared__ int sWarp[33];
+  const int bh = blockIdx.x;
+  const int b = bh / H, h = bh - (bh / H) * H;
+  const float* s = score + (int64_t)b * ss0 + (int64_t)h * ss1;
+  const uint8_t* m = mask ? mask + (int64_t)bh * n : nullptr;
+  const int lane = threadIdx.x & 31;
+  const int j0 = threadIdx.x * PER;
+  uint32_t key[PER];
+  const bool vec = ((reinterpret_cast<uintptr_t>(s) & 15) == 0) && j0 + PER <= n;
+  if (vec) {
+#pragma unroll
+    for (int c = 0; c < PER / 4; ++c) {
+      const float4 v = __ldcg(reinterpret_cast<const float4*>(s + j0) + c);
+      key[4 * c] = order_key(v.x);
+      key[4 * c + 1] = order_key(v.y);
+      key[4 * c + 2] = order_key(v.z);
+      key[4 * c + 3] = order_key(v.w);
+    }
+  } else {
+#pragma unroll
+    for (int i = 0; i < PER; ++i) key[i] = j0 + i < n ? order_key(__ldcg(s + j0 + i)) : 0u;
+  }
+  if (m) {
+#pragma unroll
+    for (int i = 0; i < PER; ++i)
+      if (j0 + i < n && m[j0 + i] == 0) key[i] = 0u;   // dead slots rank below every live one
+  }
+  const int nv = max(0, min(PER, n - j0));   // this thread's slots inside the row
+
+  uint32_t prefix = 0, pmask = 0;
+  int kk = k;
+#pragma unroll 1
+  for (int pass = 0; pass < 4; ++pass) {
+    const int shift = 24 - 8 * pass;
+    if (threadIdx.x < 256) sHist[threadIdx.x] = 0u;
+    __syncthreads();
+#pragma unroll
+    for (int i = 0; i < PER; ++i) {
+      const uint32_t x = key[i];
+      const bool take = i < nv && (x & pmask) == prefix;
+      const uint32_t bin = take ? ((x >> shift) & 255u) : 256u;
+      const uint32_t b0 = __shfl_sync(0xffffffffu, bin, 0);
+      const unsigned same = __ballot_sync(0xffffffffu, bin == b0);
+      if (lane == 0 && b0 < 256u) atomicAdd(&sHist[b0], (unsigned)__popc(same));
+      if (take && bin != b0) atomicAdd(&sHist[bin], 1u);
+    }
+    __syncthreads();
+    if (threadIdx.x < 32) {
+      // lane l owns digits 255-8l .. 248-8l (descending order)
+      int c[8];
+      int loc = 0;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        c[i] = (int)sHist[255 - (lane * 8 + i)];
+        loc += c[i];
+      }
+      int incl = loc;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int y = __shfl_up_sync(0xffffffffu, incl, o);
+        if (lane >= o) incl += y;
+      }
+      int cum = incl - loc;  // keys with a larger digit than this lane's first digit
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        if (cum < kk && cum + c[i] >= kk) {
+          sSel[pass & 1][0] = 255 - (lane * 8 + i);
+          sSel[pass & 1][1] = cum;
+        }
+        cum += c[i];
+      }
+    }
+    __syncthreads();
+    prefix |= (uint32_t)sSel[pass & 1][0] << shift;
+    pmask |= 255u << shift;
+    kk -= sSel[pass & 1][1];
+  }
+  // emission in slot order: keys above the k-th plus the first kk ties
+  int gt = 0, eq = 0;
+#pragma unroll
+  for (int i = 0; i < PER; ++i) {
+    gt += (i < nv && key[i] > prefix) ? 1 : 0;
+    eq += (i < nv && key[i] == prefix) ? 1 : 0;
+  }
+  int tot;
+  const int before = block_exclusive_scan((eq << 16) | gt, sWarp, tot);
+  const int gt_before = before & 0xFFFF, eq_before = before >> 16;
+  const int take = max(0, min(eq, kk - eq_before));
+  int off = gt_before + min(eq_before, kk);
+  int taken = 0;
+  int64_t* oi = indices + (int64_t)b * si0 + (int64_t)h * si1;
+  float* ov = values ? values + (int64_t)b * si0 + (int64_t)h * si1 : nullptr;
+#pragma unroll
+  for (int i = 0; i < PER; ++i) {
+    const uint32_t x = key[i];
+    const bool tie = x == prefix;
+    if (i < nv && (x > prefix || (tie && taken < take))) {
+      taken += tie ? 1 : 0;
+      oi[off] = j0 + i;
+      if (ov) ov[off] = s[j0 + i];
+      ++off;
+    }
+  }
+}
+
 // Lookahead survivors of one lane (eviction.py:364-409): recent window by position,
 // sinks at +inf, window excluded from the score contest, union ordered by position.
 __global__ void __launch_bounds__(kSelThreads)
@@ -285,6 +405,15 @@ __global__ void gather_kv_kernel(ma_kv kv, int H, int D, const int64_t* __restri
 int launch_select_topk(const float* score, int B, int H, int n, int64_t ss0, int64_t ss1,
                        const uint8_t* mask, int k, int64_t* indices, float* values, int64_t si0,
                        int64_t si1, cudaStream_t st) {
+  if (n <= 1024 * 16) {  // keys in registers
+    auto go = [&](auto kernel) {
+      kernel<<<B * H, kSelThreads, 0, st>>>(score, H, n, ss0, ss1, mask, k, indices, values, si0, si1);
+    };
+    if (n <= 1024 * 4) go(select_topk_reg<4>);
+    else if (n <= 1024 * 8) go(select_topk_reg<8>);
+    else go(select_topk_reg<16>);
+    return cudaGetLastError() == cudaSuccess ? MA_OK : MA_ERR_CUDA;
+  }
   const int staged = n <= kSelSmemKeys ? 1 : 0;
   const size_t smem = staged ? (size_t)n * sizeof(uint32_t) : 0;
   if (staged && smem > 48 * 1024 &&

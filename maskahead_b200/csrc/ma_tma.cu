@@ -49,18 +49,20 @@ bool make_tma_map_bf16_4d(CUtensorMap* map, const void* base, const uint64_t dim
   return r == CUDA_SUCCESS;
 }
 
-bool make_tma_map_f32_2d(CUtensorMap* map, const void* base, uint64_t cols, uint64_t rows, uint64_t row_stride_bytes,
-                         uint32_t box_cols, uint32_t box_rows) {
+bool make_tma_map_2d(CUtensorMap* map, bool bf16, const void* base, uint64_t cols, uint64_t rows,
+                     uint64_t row_stride_bytes, uint32_t box_cols, uint32_t box_rows) {
   EncodeFn fn = encode_fn();
   if (fn == nullptr) return false;
+  const uint32_t esz = bf16 ? 2 : 4;
   if ((reinterpret_cast<uintptr_t>(base) & 15) != 0 || (row_stride_bytes & 15) != 0) return false;
-  if (box_cols * 4 > 128 || box_cols == 0 || box_rows == 0 || box_rows > 256 || cols == 0 || rows == 0) return false;
+  if (box_cols * esz > 128 || box_cols == 0 || box_rows == 0 || box_rows > 256 || cols == 0 || rows == 0) return false;
   cuuint64_t gdim[2] = {cols, rows};
   cuuint64_t gstr[1] = {row_stride_bytes};
   cuuint32_t bdim[2] = {box_cols, box_rows};
   cuuint32_t estr[2] = {1, 1};
-  const CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<void*>(base), gdim, gstr, bdim, estr,
-                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+  const CUresult r = fn(map, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2,
+                        const_cast<void*>(base), gdim, gstr, bdim, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                        CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS;
 }

@@ -52,8 +52,8 @@ __device__ __forceinline__ void store_wait_read() { asm volatile("cp.async.bulk.
 // uses its cp.async path).
 bool make_tma_map_bf16_4d(CUtensorMap* map, const void* base, const uint64_t dims[4],
                           const uint64_t strides_bytes[3], const uint32_t box[4]);
-// Host: a 2-D fp32 tensor map [rows][cols] (row stride in bytes), 128-byte swizzle.
-bool make_tma_map_f32_2d(CUtensorMap* map, const void* base, uint64_t cols, uint64_t rows, uint64_t row_stride_bytes,
-                         uint32_t box_cols, uint32_t box_rows);
+// Host: a 2-D tensor map [rows][cols] (bf16 or fp32, row stride in bytes), 128-byte swizzle.
+bool make_tma_map_2d(CUtensorMap* map, bool bf16, const void* base, uint64_t cols, uint64_t rows,
+                     uint64_t row_stride_bytes, uint32_t box_cols, uint32_t box_rows);
 
 }  // namespace ma
