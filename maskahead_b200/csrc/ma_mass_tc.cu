@@ -113,6 +113,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefix_mass_tc(const Args A) {
   __shared__ int sRowT[kMaxRows];                // block position of selection row r (-1: none)
   __shared__ float sHalf[2][kTile];
   __shared__ __align__(16) float sA[kTile];
+  __shared__ float sAres[kStages][kTile];        // a_j of the tiles still in the ring
   __shared__ uint8_t sOk[kStages][kTile];
   __shared__ float sRed[4][kD];
   __shared__ float sTot[kD + 1];
@@ -196,7 +197,10 @@ __global__ void __launch_bounds__(kThreads, 1) prefix_mass_tc(const Args A) {
   float cacc0 = 0.f, cacc1 = 0.f, asum = 0.f;
   bool aborted = false;
 
-  for (int j0 = begin; j0 < end; j0 += kTile) {
+  const int ntiles = end > begin ? (end - begin + kTile - 1) / kTile : 0;
+  const bool resident = ntiles <= kStages;   // every V tile of the CTA stays in the ring
+  int tt = 0;
+  for (int j0 = begin; j0 < end; j0 += kTile, ++tt) {
     uint8_t* sK = sRing + 2 * stage * kTileBytes;
     uint8_t* sV = sK + kTileBytes;
     cp_async_wait<kStages - 1>();
@@ -225,14 +229,16 @@ __global__ void __launch_bounds__(kThreads, 1) prefix_mass_tc(const Args A) {
     // this thread: slot slot_lane, rows [c_lo, c_lo + cols_half), in row order
     float acc[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll 1
-    for (int c0 = 0; c0 < cols_half; c0 += 32) {
-      float sv[32];
-      tmem_ld32(tRow + c_lo + c0, sv);   // columns stay inside the 256-column allocation
+    for (int c0 = 0; c0 < cols_half; c0 += 64) {
+      // two 32-column loads per wait (columns stay inside the 256-column allocation)
+      float sv[64];
+      tmem_ld32(tRow + c_lo + c0, sv);
+      tmem_ld32(tRow + c_lo + c0 + 32, sv + 32);
       tmem_ld_wait();
       const int lim = cols_half - c0;
 #pragma unroll
-      for (int i = 0; i < 32; i += 4) {
-        const float4 b4 = *reinterpret_cast<const float4*>(&sB[c_lo + c0 + i]);
+      for (int i = 0; i < 64; i += 4) {
+        const float4 b4 = *reinterpret_cast<const float4*>(&sB[(c_lo + c0 + i) & (kMaxRows - 1)]);
         if (i < lim) {   // lim is a multiple of 8
           acc[0] += ex2(fmaf(sv[i], c2, -b4.x));
           acc[1] += ex2(fmaf(sv[i + 1], c2, -b4.y));
@@ -248,6 +254,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefix_mass_tc(const Args A) {
       const float a = sOk[stage][threadIdx.x] ? (sHalf[0][threadIdx.x] + sHalf[1][threadIdx.x]) * inv_rows : 0.f;
       if (j < end) A.mass[(int64_t)b * A.sm0 + (int64_t)h * A.sm1 + j] = a;
       sA[threadIdx.x] = j < end ? a : 0.f;
+      if (tt < kStages) sAres[tt][threadIdx.x] = j < end ? a : 0.f;
     }
     if (CENTRE) {
       __syncthreads();
@@ -340,6 +347,28 @@ __global__ void __launch_bounds__(kThreads, 1) prefix_mass_tc(const Args A) {
   float cc[8];
 #pragma unroll
   for (int i = 0; i < 8; ++i) cc[i] = __ldcg(A.centre + (int64_t)bh * kD + 8 * l16 + i);
+  if (resident) {
+    // V tiles and a_j still on chip: tile t sits in ring stage t (row-major bf16 rows)
+    for (int t = 0; t < ntiles; ++t) {
+      const uint8_t* sVt = sRing + (2 * t + 1) * kTileBytes;
+#pragma unroll 2
+      for (int jj = grp; jj < kTile; jj += kThreads / 16) {
+        const int j = begin + t * kTile + jj;
+        float f[8];
+        bf16x8_to_float(*reinterpret_cast<const uint4*>(sVt + jj * (kD * 2) + l16 * 16), f);
+        float s2 = 0.f;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const float x = f[i] - cc[i];
+          s2 = fmaf(x, x, s2);
+        }
+#pragma unroll
+        for (int o = 8; o > 0; o >>= 1) s2 += __shfl_xor_sync(0xffffffffu, s2, o);
+        if (l16 == 0 && j < end) A.score[(int64_t)b * A.ss0 + (int64_t)h * A.ss1 + j] = ok_c ? sAres[t][jj] * sqrtf(s2) : NAN;
+      }
+    }
+    return;
+  }
   constexpr int kBatch = 4;
   for (int jb = begin; jb < end; jb += (kThreads / 16) * kBatch) {
     float f[kBatch][8];
