@@ -31,6 +31,9 @@
  *   ma_sparse_attention  runtime/session.py:1286-1336 + reference.py:403-426
  *                        (_compact_attention -> sdpa_compact over the read set)
  *   ma_gather_kv         kernels/ops.py:570-662, 835-855 (gather_packed_kv)
+ *   ma_quantize_tokens, ma_quantize_keys_channel, ma_key_divisor
+ *                        reference.py:58-90, 182-213 and cache.py:484-497 (the packing
+ *                        of the append path)
  */
 #ifndef MASKAHEAD_B200_H
 #define MASKAHEAD_B200_H
@@ -108,6 +111,19 @@ typedef struct ma_kv {
   int64_t skc[2];
   /* optional live-slot mask, uint8 [B,H,nq+nf] contiguous; 0 = dead slot, never read  */
   const uint8_t* mask;
+  /* Paged storage (optional; the reference has none -- the serving batch uses it): with
+   * pages != NULL, slot j of sequence b in the paged part -- slots [0, nq) of a packed
+   * layout, every slot of MA_KV_DENSE -- lives in page pages[b*spg + j/page_size] at
+   * position j % page_size, and that part's strides run over (page, h, position)
+   * instead of (b, h, slot); for channel-mode keys over (page, h, token group within
+   * the page), page_size a multiple of kgroup. A page index outside [0, num_pages)
+   * reads as a dead slot. The dense tail of a packed layout stays per sequence.       */
+  const int32_t* pages;
+  int64_t spg;
+  int32_t page_size;
+  int32_t num_pages;
+  /* optional live length per sequence, int32 [B]: slots >= lens[b] are dead            */
+  const int32_t* lens;
 } ma_kv;
 
 /* The query block: Q [B,Hq,T,D], strides over (b, hq, t). */
@@ -181,9 +197,11 @@ MA_API int ma_value_score_noalloc(const ma_kv* kv, int B, int H, int D, const fl
 
 /* ---- top-k read set -----------------------------------------------------------------
  * Per (b, h): the k largest scores among live slots (ties: lower slot first), written
- * as ascending slot indices (int64) with their scores (values optional).             */
+ * as ascending slot indices (int64) with their scores (values optional). Live: mask
+ * (optional, uint8 [B,H,n]) nonzero and slot < lens[b] (optional, int32 [B]); dead
+ * slots rank below every live one.                                                    */
 MA_API int ma_select_topk(const float* score, int B, int H, int n, const int64_t sscore[2],
-                   const uint8_t* mask, int k, int64_t* indices, float* values,
+                   const uint8_t* mask, const int32_t* lens, int k, int64_t* indices, float* values,
                    const int64_t sidx[2], void* stream);
 
 /* ---- lookahead retention ------------------------------------------------------------
@@ -211,6 +229,31 @@ MA_API int ma_sparse_attention(const ma_rows* q, const ma_kv* kv, int H,
 MA_API int ma_gather_kv(const ma_kv* kv, int B, int H, int D, const int64_t* idx, int k,
                  const int64_t sidx[2], void* out_k, void* out_v, const int64_t sok[3],
                  const int64_t sov[3], int32_t out_dtype, void* stream);
+
+/* ---- quantize-on-append -------------------------------------------------------------
+ * Dense rows x [B,H,n,D] (MA_BF16 or MA_F32, strides over (b, h, slot)) -> 4-bit codes
+ * with fp16 scale/zero, as the reference's quantizers compute them in x's dtype
+ * (reference.py:58-90 quantize_keys, 182-213 quantize_values; cache.py:484-497 append).
+ * group must be 32; D a multiple of 32.
+ * ma_quantize_tokens: per token and group of 32 channels -> payload [B,H,n,D/32,16]
+ *   (16-byte aligned rows: strides sp over (b, h, slot) in bytes), scale/zero
+ *   [B,H,n,D/32] (strides ss over (b, h, slot)); values, or token-mode keys when kchan
+ *   ([B,H,D] fp32, strides skc over (b, h)) is given: x / kchan rounded to x's dtype
+ *   first (cache.py:491-497).
+ * ma_quantize_keys_channel: KIVI keys, per channel and group of 32 tokens (n a multiple
+ *   of 32) -> payload [B,H,n/32,D,16] (strides over (b, h, group)), scale/zero
+ *   [B,H,n/32,D] (strides over (b, h, group)).
+ * ma_key_divisor: token-mode divisor kchan[b,h,d] = sqrt(max(max_t |k[b,h,t,d]|, 1e-4))
+ *   (cache.py:488-490).                                                               */
+MA_API int ma_quantize_tokens(const void* x, int32_t dtype, int B, int H, int n, int D, const int64_t sx[3],
+                              const float* kchan, const int64_t skc[2], int group, uint8_t* payload,
+                              const int64_t sp[3], uint16_t* scale, uint16_t* zero, const int64_t ss[3],
+                              void* stream);
+MA_API int ma_quantize_keys_channel(const void* k, int32_t dtype, int B, int H, int n, int D, const int64_t sk[3],
+                                    int group, uint8_t* payload, const int64_t sp[3], uint16_t* scale,
+                                    uint16_t* zero, const int64_t ss[3], void* stream);
+MA_API int ma_key_divisor(const void* k, int32_t dtype, int B, int H, int n, int D, const int64_t sk[3],
+                          float* kchan, const int64_t skc[2], void* stream);
 
 #ifdef __cplusplus
 }

@@ -46,6 +46,8 @@ class MaKV(ctypes.Structure):
         ("svq", c_i64_3), ("svs", c_i64_3),
         ("kchan", ctypes.c_void_p), ("skc", c_i64_2),
         ("mask", ctypes.c_void_p),
+        ("pages", ctypes.c_void_p), ("spg", ctypes.c_int64), ("page_size", ctypes.c_int32),
+        ("num_pages", ctypes.c_int32), ("lens", ctypes.c_void_p),
     ]
 
 
@@ -79,7 +81,7 @@ _SIGNATURES = {
                               _P(ctypes.c_int64), _vp, _sz, _vp]),
     "ma_value_score_noalloc": (_i32, [_P(MaKV), _i32, _i32, _i32, _vp, _P(ctypes.c_int64), _vp,
                                       _P(ctypes.c_int64), _vp]),
-    "ma_select_topk": (_i32, [_vp, _i32, _i32, _i32, _P(ctypes.c_int64), _vp, _i32, _vp, _vp,
+    "ma_select_topk": (_i32, [_vp, _i32, _i32, _i32, _P(ctypes.c_int64), _vp, _vp, _i32, _vp, _vp,
                               _P(ctypes.c_int64), _vp]),
     "ma_retain": (_i32, [_vp, _vp, _i32, _vp, _i32, _i32, _i32, _i32, _i32, _vp, _vp]),
     "ma_sparse_attention_workspace": (_sz, [_i32] * 6),
@@ -87,6 +89,13 @@ _SIGNATURES = {
                                    _P(MaBlock), _f32, _vp, _P(ctypes.c_int64), _vp, _sz, _vp]),
     "ma_gather_kv": (_i32, [_P(MaKV), _i32, _i32, _i32, _vp, _i32, _P(ctypes.c_int64), _vp, _vp,
                             _P(ctypes.c_int64), _P(ctypes.c_int64), _i32, _vp]),
+    "ma_quantize_tokens": (_i32, [_vp, _i32, _i32, _i32, _i32, _i32, _P(ctypes.c_int64), _vp,
+                                  _P(ctypes.c_int64), _i32, _vp, _P(ctypes.c_int64), _vp, _vp,
+                                  _P(ctypes.c_int64), _vp]),
+    "ma_quantize_keys_channel": (_i32, [_vp, _i32, _i32, _i32, _i32, _i32, _P(ctypes.c_int64), _i32, _vp,
+                                        _P(ctypes.c_int64), _vp, _vp, _P(ctypes.c_int64), _vp]),
+    "ma_key_divisor": (_i32, [_vp, _i32, _i32, _i32, _i32, _i32, _P(ctypes.c_int64), _vp,
+                              _P(ctypes.c_int64), _vp]),
 }
 
 EXPORTED = tuple(_SIGNATURES)

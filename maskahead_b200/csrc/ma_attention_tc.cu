@@ -109,9 +109,10 @@ __device__ __forceinline__ void stage_rows(const Args& A, int b, int h, bool is_
       if (ok && A.idx) slot = (int)A.idx[(int64_t)b * A.si0 + (int64_t)h * A.si1 + j];
       ok = ok && kv_live(A.kv, A.H, b, h, slot);
       if (ok && (!PACKED || slot >= A.kv.nq)) {
-        const int row = slot - A.kv.nq;
-        cp_async16(smem_addr(dk), kf + (int64_t)b * A.kv.skf[0] + (int64_t)h * A.kv.skf[1] + (int64_t)row * A.kv.skf[2] + ch * 8, true);
-        cp_async16(smem_addr(dv), vf + (int64_t)b * A.kv.svf[0] + (int64_t)h * A.kv.svf[1] + (int64_t)row * A.kv.svf[2] + ch * 8, true);
+        int sb = b, row = slot - A.kv.nq;
+        if (!PACKED && A.kv.pages) kv_page(A.kv, b, row, sb, row);   // a paged dense cache
+        cp_async16(smem_addr(dk), kf + (int64_t)sb * A.kv.skf[0] + (int64_t)h * A.kv.skf[1] + (int64_t)row * A.kv.skf[2] + ch * 8, true);
+        cp_async16(smem_addr(dv), vf + (int64_t)sb * A.kv.svf[0] + (int64_t)h * A.kv.svf[1] + (int64_t)row * A.kv.svf[2] + ch * 8, true);
       } else if (ok) {
         float fk[8], fv[8];
         kv_read8<true>(A.kv, b, h, slot, ch, fk);
@@ -622,7 +623,8 @@ int launch_attn_partial_tc(const ma_rows& q, const ma_kv& kv, int H, const ma_bl
   const int R = G * q.T;
   // TMA for contiguous bf16 rows: the dense prefix without a mask, the current block, and
   // the queries when a row tile is made of whole query heads
-  A.tma_kv = (kv.layout == MA_KV_DENSE && kv.dtype == MA_BF16 && !idx && !kv.mask && n_keys > 0 &&
+  A.tma_kv = (kv.layout == MA_KV_DENSE && kv.dtype == MA_BF16 && !idx && !kv.mask && !kv.pages && !kv.lens &&
+              n_keys > 0 &&
               tma_map_rows(&A.kmap, kv.kf, q.B, H, kv.nf, kv.skf) &&
               tma_map_rows(&A.vmap, kv.vf, q.B, H, kv.nf, kv.svf)) ? 1 : 0;
   A.tma_cur = (cur.Tc > 0 && tma_map_rows(&A.ckmap, cur.k, q.B, H, cur.Tc, cur.sk) &&

@@ -52,6 +52,11 @@ int check_kv(const ma_kv* kv, int D) {
     if (!kv->kf || !kv->vf || !aligned16(kv->kf) || !aligned16(kv->vf)) return MA_ERR_ARG;
     if (!strides16(kv->skf, 3, esize(kv->dtype)) || !strides16(kv->svf, 3, esize(kv->dtype))) return MA_ERR_ARG;
   }
+  if (kv->pages) {
+    if (kv->page_size <= 0 || kv->num_pages <= 0 || kv->spg < 0) return MA_ERR_ARG;
+    if (kv->layout == MA_KV_PACKED_CHANNEL && (kv->kgroup <= 0 || kv->page_size % kv->kgroup != 0))
+      return MA_ERR_ARG;
+  }
   if (kv->layout == MA_KV_DENSE) {
     if (kv->nq != 0) return MA_ERR_ARG;
     return MA_OK;
@@ -69,7 +74,7 @@ int check_kv(const ma_kv* kv, int D) {
     if (!kv->kchan) return MA_ERR_ARG;
   } else {
     if (kv->kgroup <= 0 || (kv->kgroup % 2) != 0) return MA_ERR_UNSUPPORTED;
-    if (kv->nq % kv->kgroup) return MA_ERR_ARG;
+    if (!kv->pages && kv->nq % kv->kgroup) return MA_ERR_ARG;
   }
   return MA_OK;
 }
@@ -284,12 +289,53 @@ int ma_value_score(const ma_kv* kv, int B, int H, int D, const float* a, const i
 }
 
 int ma_select_topk(const float* score, int B, int H, int n, const int64_t sscore[2], const uint8_t* mask,
-                   int k, int64_t* indices, float* values, const int64_t sidx[2], void* stream) {
+                   const int32_t* lens, int k, int64_t* indices, float* values, const int64_t sidx[2],
+                   void* stream) {
   if (!score || !sscore || !indices || !sidx || B <= 0 || H <= 0 || n <= 0) return MA_ERR_ARG;
   if (k < 0 || k > n) return MA_ERR_ARG;
   if (k == 0) return MA_OK;
-  return launch_select_topk(score, B, H, n, sscore[0], sscore[1], mask, k, indices, values, sidx[0],
+  return launch_select_topk(score, B, H, n, sscore[0], sscore[1], mask, lens, k, indices, values, sidx[0],
                             sidx[1], (cudaStream_t)stream);
+}
+
+int ma_quantize_tokens(const void* x, int32_t dtype, int B, int H, int n, int D, const int64_t sx[3],
+                       const float* kchan, const int64_t skc[2], int group, uint8_t* payload, const int64_t sp[3],
+                       uint16_t* scale, uint16_t* zero, const int64_t ss[3], void* stream) {
+  if (!x || !payload || !scale || !zero || !sx || !sp || !ss || B < 0 || H < 0 || n < 0 || D <= 0) return MA_ERR_ARG;
+  if (!valid_dtype(dtype)) return MA_ERR_ARG;
+  if (group != 32 || D % 32 != 0) return MA_ERR_UNSUPPORTED;
+  if (kchan && (!skc || skc[0] < 0 || skc[1] < 0)) return MA_ERR_ARG;
+  if ((reinterpret_cast<uintptr_t>(payload) & 15) != 0 || !strides16(sp, 3, 1)) return MA_ERR_ARG;
+  if ((reinterpret_cast<uintptr_t>(x) & (esize(dtype) - 1)) != 0) return MA_ERR_ARG;
+  for (int i = 0; i < 3; ++i)
+    if (sx[i] < 0 || ss[i] < 0) return MA_ERR_ARG;
+  return launch_quantize_tokens(x, dtype, B, H, n, D, sx, kchan, skc, payload, sp, scale, zero, ss,
+                                (cudaStream_t)stream);
+}
+
+int ma_quantize_keys_channel(const void* k, int32_t dtype, int B, int H, int n, int D, const int64_t sk[3], int group,
+                             uint8_t* payload, const int64_t sp[3], uint16_t* scale, uint16_t* zero,
+                             const int64_t ss[3], void* stream) {
+  if (!k || !payload || !scale || !zero || !sk || !sp || !ss || B < 0 || H < 0 || n < 0 || D <= 0) return MA_ERR_ARG;
+  if (!valid_dtype(dtype)) return MA_ERR_ARG;
+  if (group != 32) return MA_ERR_UNSUPPORTED;
+  if (n % 32 != 0) return MA_ERR_ARG;
+  if ((reinterpret_cast<uintptr_t>(payload) & 15) != 0 || !strides16(sp, 3, 1)) return MA_ERR_ARG;
+  if ((reinterpret_cast<uintptr_t>(k) & (esize(dtype) - 1)) != 0) return MA_ERR_ARG;
+  for (int i = 0; i < 3; ++i)
+    if (sk[i] < 0 || ss[i] < 0) return MA_ERR_ARG;
+  return launch_quantize_channels(k, dtype, B, H, n, D, sk, payload, sp, scale, zero, ss, (cudaStream_t)stream);
+}
+
+int ma_key_divisor(const void* k, int32_t dtype, int B, int H, int n, int D, const int64_t sk[3], float* kchan,
+                   const int64_t skc[2], void* stream) {
+  if (!k || !kchan || !sk || !skc || B < 0 || H < 0 || n < 0 || D <= 0) return MA_ERR_ARG;
+  if (!valid_dtype(dtype)) return MA_ERR_ARG;
+  if (D > kMaxD) return MA_ERR_UNSUPPORTED;
+  for (int i = 0; i < 3; ++i)
+    if (sk[i] < 0) return MA_ERR_ARG;
+  if (skc[0] < 0 || skc[1] < 0) return MA_ERR_ARG;
+  return launch_key_divisor(k, dtype, B, H, n, D, sk, kchan, skc, (cudaStream_t)stream);
 }
 
 int ma_retain(const float* score, const int32_t* phys, int n_phys, const int32_t* pos, int lanes, int live,

@@ -78,11 +78,46 @@ __device__ __forceinline__ void store4<__nv_bfloat16>(__nv_bfloat16* p, float a,
 // Packed codes are rounded to the tail dtype (bf16 in every shipped configuration), as
 // the reference dequantizes the cache to its compute dtype before attending.
 // ----------------------------------------------------------------------------------
-// Slot j exists (0 <= j < nq + nf) and is live. Slots outside the prefix (a bad index
-// in a caller's read set) read as dead, so no kernel ever addresses outside the cache.
+// Storage coordinates of position j of sequence b's paged part: (page, position) with a
+// page table, else (b, j). The page is -1 when the table entry is out of range.
+__device__ __forceinline__ void kv_page(const ma_kv& kv, int b, int j, int& sb, int& sj) {
+  if (kv.pages == nullptr) {
+    sb = b;
+    sj = j;
+    return;
+  }
+  const int pi = j / kv.page_size;
+  const int p = kv.pages[(int64_t)b * kv.spg + pi];
+  sb = (p >= 0 && p < kv.num_pages) ? p : -1;
+  sj = j - pi * kv.page_size;
+}
+// Whether slot j of sequence b sits in the paged part of the layout.
+__device__ __forceinline__ bool kv_paged(const ma_kv& kv, int j) {
+  return kv.pages != nullptr && (kv.layout == MA_KV_DENSE || j < kv.nq);
+}
+
+// Slot j exists: inside the prefix, below lens[b], its page (if paged) in range.
+__device__ __forceinline__ bool kv_exists(const ma_kv& kv, int b, int j) {
+  if (j < 0 || (int64_t)j >= (int64_t)kv.nq + kv.nf) return false;
+  if (kv.lens != nullptr && j >= kv.lens[b]) return false;
+  if (kv_paged(kv, j)) {
+    const int p = kv.pages[(int64_t)b * kv.spg + j / kv.page_size];
+    if (p < 0 || p >= kv.num_pages) return false;
+  }
+  return true;
+}
+
+// Slot j exists (0 <= j < nq + nf, below lens[b]) and is live (mask, page table). Slots
+// outside the prefix (a bad index in a caller's read set) read as dead, so no kernel
+// ever addresses outside the cache.
 __device__ __forceinline__ bool kv_live(const ma_kv& kv, int H, int b, int h, int j) {
   const int64_t n = (int64_t)kv.nq + kv.nf;
   if (j < 0 || j >= n) return false;
+  if (kv.lens != nullptr && j >= kv.lens[b]) return false;
+  if (kv_paged(kv, j)) {
+    const int p = kv.pages[(int64_t)b * kv.spg + j / kv.page_size];
+    if (p < 0 || p >= kv.num_pages) return false;
+  }
   if (kv.mask == nullptr) return true;
   return kv.mask[((int64_t)b * H + h) * n + j] != 0;
 }
@@ -100,9 +135,12 @@ __device__ __forceinline__ void dequant8_token(const uint8_t* payload, uint16_t 
   }
 }
 
+// Callers read live slots only (kv_live), so a paged slot's page is in range.
 template <bool KEY>
 __device__ __forceinline__ void kv_read8(const ma_kv& kv, int b, int h, int j, int c8, float f[8]) {
   const int d0 = 8 * c8;
+  const int seq = b;                               // the divisor k_chan is per sequence
+  if (kv_paged(kv, j)) kv_page(kv, seq, j, b, j);  // from here on (b, j) address the storage
   if (j >= kv.nq) {  // dense slot (the whole prefix for MA_KV_DENSE, else the tail)
     const int jt = j - kv.nq;
     const int64_t* s = KEY ? kv.skf : kv.svf;
@@ -126,7 +164,7 @@ __device__ __forceinline__ void kv_read8(const ma_kv& kv, int b, int h, int j, i
     const int64_t so = (int64_t)b * ss[0] + (int64_t)h * ss[1] + (int64_t)j * ss[2] + g;
     dequant8_token(q + qo, sc[so], zp[so], f);
     if (KEY) {
-      const float* kc = kv.kchan + (int64_t)b * kv.skc[0] + (int64_t)h * kv.skc[1] + d0;
+      const float* kc = kv.kchan + (int64_t)seq * kv.skc[0] + (int64_t)h * kv.skc[1] + d0;
 #pragma unroll
       for (int i = 0; i < 8; ++i) f[i] *= kc[i];
     }

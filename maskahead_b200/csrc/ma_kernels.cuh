@@ -55,8 +55,18 @@ int launch_prefix_mass_tc(const ma_rows& q, const ma_kv& kv, int H, const int32_
 
 // ma_select.cu
 int launch_select_topk(const float* score, int B, int H, int n, int64_t ss0, int64_t ss1,
-                       const uint8_t* mask, int k, int64_t* indices, float* values, int64_t si0,
-                       int64_t si1, cudaStream_t st);
+                       const uint8_t* mask, const int32_t* lens, int k, int64_t* indices, float* values,
+                       int64_t si0, int64_t si1, cudaStream_t st);
+
+// ma_quant.cu
+int launch_quantize_tokens(const void* x, int dtype, int B, int H, int n, int D, const int64_t sx[3], const float* kchan,
+                           const int64_t skc[2], uint8_t* payload, const int64_t sp[3], uint16_t* scale, uint16_t* zero,
+                           const int64_t ss[3], cudaStream_t st);
+int launch_quantize_channels(const void* x, int dtype, int B, int H, int n, int D, const int64_t sx[3],
+                             uint8_t* payload, const int64_t sp[3], uint16_t* scale, uint16_t* zero, const int64_t ss[3],
+                             cudaStream_t st);
+int launch_key_divisor(const void* k, int dtype, int B, int H, int n, int D, const int64_t sk[3], float* kchan,
+                       const int64_t skc[2], cudaStream_t st);
 int launch_retain(const float* score, const int32_t* phys, int n_phys, const int32_t* pos,
                   int lanes, int live, int capacity, int recent_window, int sink_tokens,
                   int64_t* keep, cudaStream_t st);

@@ -76,10 +76,11 @@ __device__ __forceinline__ void load_tile(const Args& A, int b, int h, int j0, i
     uint8_t* dk = sK + kmajor_off(jj, ch, kTile);
     uint8_t* dv = sV + jj * (kD * 2) + ch * 16;
     if (ok && (!PACKED || j >= A.kv.nq)) {
-      const int row = j - A.kv.nq;
-      cp_async16(tc::smem_addr(dk), kf + (int64_t)b * A.kv.skf[0] + (int64_t)h * A.kv.skf[1] + (int64_t)row * A.kv.skf[2] + ch * 8, true);
+      int sb = b, row = j - A.kv.nq;
+      if (!PACKED && A.kv.pages) kv_page(A.kv, b, row, sb, row);   // a paged dense cache
+      cp_async16(tc::smem_addr(dk), kf + (int64_t)sb * A.kv.skf[0] + (int64_t)h * A.kv.skf[1] + (int64_t)row * A.kv.skf[2] + ch * 8, true);
       if (CENTRE)
-        cp_async16(tc::smem_addr(dv), vf + (int64_t)b * A.kv.svf[0] + (int64_t)h * A.kv.svf[1] + (int64_t)row * A.kv.svf[2] + ch * 8, true);
+        cp_async16(tc::smem_addr(dv), vf + (int64_t)sb * A.kv.svf[0] + (int64_t)h * A.kv.svf[1] + (int64_t)row * A.kv.svf[2] + ch * 8, true);
     } else if (ok) {
       float f[8];
       kv_read8<true>(A.kv, b, h, j, ch, f);

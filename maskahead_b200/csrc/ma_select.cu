@@ -137,7 +137,8 @@ constexpr int kSelSmemKeys = 48 * 1024;
 
 __global__ void __launch_bounds__(kSelThreads)
 select_topk_kernel(const float* __restrict__ score, int H, int n, int64_t ss0, int64_t ss1,
-                   const uint8_t* __restrict__ mask, int k, int64_t* __restrict__ indices,
+                   const uint8_t* __restrict__ mask, const int32_t* __restrict__ lens, int k,
+                   int64_t* __restrict__ indices,
                    float* __restrict__ values, int64_t si0, int64_t si1, int staged) {
   extern __shared__ uint32_t sKeys[];
   __shared__ unsigned sHist[256];
@@ -147,8 +148,9 @@ select_topk_kernel(const float* __restrict__ score, int H, int n, int64_t ss0, i
   const int b = bh / H, h = bh - (bh / H) * H;
   const float* s = score + (int64_t)b * ss0 + (int64_t)h * ss1;
   const uint8_t* m = mask ? mask + (int64_t)bh * n : nullptr;
+  const int len = lens ? lens[b] : n;
   auto gkey = [&](int j) -> uint32_t {
-    if (m && m[j] == 0) return 0u;
+    if (j >= len || (m && m[j] == 0)) return 0u;
     return order_key(s[j]);
   };
   int64_t* oi = indices + (int64_t)b * si0 + (int64_t)h * si1;
@@ -179,7 +181,8 @@ select_topk_kernel(const float* __restrict__ score, int H, int n, int64_t ss0, i
 template <int PER>
 __global__ void __launch_bounds__(kSelThreads)
 select_topk_reg(const float* __restrict__ score, int H, int n, int64_t ss0, int64_t ss1,
-                const uint8_t* __restrict__ mask, int k, int64_t* __restrict__ indices,
+                const uint8_t* __restrict__ mask, const int32_t* __restrict__ lens, int k,
+                int64_t* __restrict__ indices,
                 float* __restrict__ values, int64_t si0, int64_t si1) {
   __shared__ unsigned sHist[256];
   __shared__ int sSel[2][2];
@@ -209,6 +212,12 @@ select_topk_reg(const float* __restrict__ score, int H, int n, int64_t ss0, int6
 #pragma unroll
     for (int i = 0; i < PER; ++i)
       if (j0 + i < n && m[j0 + i] == 0) key[i] = 0u;   // dead slots rank below every live one
+  }
+  if (lens) {
+    const int len = lens[b];
+#pragma unroll
+    for (int i = 0; i < PER; ++i)
+      if (j0 + i >= len) key[i] = 0u;
   }
   const int nv = max(0, min(PER, n - j0));   // this thread's slots inside the row
 
@@ -384,10 +393,10 @@ __global__ void gather_kv_kernel(ma_kv kv, int H, int D, const int64_t* __restri
     const int64_t slot64 = idx[(int64_t)b * si0 + (int64_t)h * si1 + i];
     const int slot = (int)slot64;
     float fk[8], fv[8];
-    if (slot64 >= 0 && slot64 < (int64_t)kv.nq + kv.nf) {
+    if (slot64 >= 0 && slot64 < (int64_t)kv.nq + kv.nf && kv_exists(kv, b, slot)) {
       kv_read8<true>(kv, b, h, slot, c8, fk);
       kv_read8<false>(kv, b, h, slot, c8, fv);
-    } else {  // a slot outside the prefix gathers zeros
+    } else {  // a slot outside the prefix (or its sequence, or its page table) gathers zeros
 #pragma unroll
       for (int e = 0; e < 8; ++e) fk[e] = fv[e] = 0.f;
     }
@@ -403,11 +412,11 @@ __global__ void gather_kv_kernel(ma_kv kv, int H, int D, const int64_t* __restri
 }  // namespace
 
 int launch_select_topk(const float* score, int B, int H, int n, int64_t ss0, int64_t ss1,
-                       const uint8_t* mask, int k, int64_t* indices, float* values, int64_t si0,
-                       int64_t si1, cudaStream_t st) {
+                       const uint8_t* mask, const int32_t* lens, int k, int64_t* indices, float* values,
+                       int64_t si0, int64_t si1, cudaStream_t st) {
   if (n <= 1024 * 16) {  // keys in registers
     auto go = [&](auto kernel) {
-      kernel<<<B * H, kSelThreads, 0, st>>>(score, H, n, ss0, ss1, mask, k, indices, values, si0, si1);
+      kernel<<<B * H, kSelThreads, 0, st>>>(score, H, n, ss0, ss1, mask, lens, k, indices, values, si0, si1);
     };
     if (n <= 1024 * 4) go(select_topk_reg<4>);
     else if (n <= 1024 * 8) go(select_topk_reg<8>);
@@ -420,7 +429,7 @@ int launch_select_topk(const float* score, int B, int H, int n, int64_t ss0, int
       cudaFuncSetAttribute(select_topk_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
           cudaSuccess)
     return MA_ERR_CUDA;
-  select_topk_kernel<<<B * H, kSelThreads, smem, st>>>(score, H, n, ss0, ss1, mask, k, indices, values,
+  select_topk_kernel<<<B * H, kSelThreads, smem, st>>>(score, H, n, ss0, ss1, mask, lens, k, indices, values,
                                                        si0, si1, staged);
   return cudaGetLastError() == cudaSuccess ? MA_OK : MA_ERR_CUDA;
 }

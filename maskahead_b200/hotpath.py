@@ -63,7 +63,7 @@ def fast_step0(query: torch.Tensor, prefix, current_key: torch.Tensor, current_v
         live = prefix.n if prefix.mask is None else None
         k = int(topk) if live is None else min(int(topk), live)
         rank = score if value else mass
-        idx, _ = select_topk_indices(rank, k, prefix.mask, want_values=False)
+        idx, _ = select_topk_indices(rank, k, prefix.mask, want_values=False, lens=prefix.lens)
     return Step0Result(out, idx, mass, score)
 
 

@@ -45,11 +45,12 @@ def _view_heads(view) -> int:
 
 
 def select_topk_indices(score: torch.Tensor, k: int, live_mask: torch.Tensor | None = None,
-                        want_values: bool = True):
+                        want_values: bool = True, lens: torch.Tensor | None = None):
     """Top-k per (b, h) row of score [B,H,n] among live slots, as ascending indices.
 
-    Ties at the k-th score go to the lower slot. Returns (indices int64 [B,H,k],
-    values fp32 [B,H,k] | None).
+    Live: live_mask (optional [B,H,n]) and slot < lens[b] (optional int32 [B], ragged
+    sequences). Ties at the k-th score go to the lower slot; dead slots rank below every
+    live one. Returns (indices int64 [B,H,k], values fp32 [B,H,k] | None).
     """
     lib = _lib.lib()
     if score.ndim != 3 or score.dtype != torch.float32:
@@ -66,9 +67,14 @@ def select_topk_indices(score: torch.Tensor, k: int, live_mask: torch.Tensor | N
         m = live_mask.to(torch.uint8).contiguous()
         if tuple(m.shape) != (b, h, n):
             raise ValueError("live_mask must match score")
+    ln = None
+    if lens is not None:
+        ln = lens.to(device=dev, dtype=torch.int32).contiguous()
+        if tuple(ln.shape) != (b,):
+            raise ValueError("lens must be [B]")
     if k:
         _lib.check("ma_select_topk", lib.ma_select_topk(
-            s.data_ptr(), b, h, n, _lib.i64(s.stride(0), s.stride(1)), _lib.ptr(m), k, idx.data_ptr(),
+            s.data_ptr(), b, h, n, _lib.i64(s.stride(0), s.stride(1)), _lib.ptr(m), _lib.ptr(ln), k, idx.data_ptr(),
             _lib.ptr(vals), _lib.i64(idx.stride(0), idx.stride(1)), _lib.stream_handle(dev)))
     return idx, vals
 

@@ -10,6 +10,12 @@ object with these attributes works). Layouts (cache.py:142-189):
   token keys    k_q, k_scale, k_zero as V, plus k_chan [B,H,D] fp32
   channel keys  k_q [B,H,ng,D,16] u8, k_scale / k_zero [B,H,ng,D] fp16  (KIVI)
   tail          k_residual, v_residual [B, H, rcap, D] bf16
+
+Paged storage (no counterpart in the reference; the serving batch uses it): the packed
+part (or a dense cache) is a pool of pages whose first axis is the page instead of the
+sequence -- e.g. v_q [P, H, page_size, D/32, 16] -- and ``pages`` [B, max_pages] int32
+maps each sequence's logical page to a pool page; ``lens`` [B] int32 gives each
+sequence's live length (ragged batches).
 """
 
 from __future__ import annotations
@@ -50,12 +56,15 @@ class Prefix:
     """The prefix a kernel reads: packed (+ bf16 tail) or plain dense. [B, Hkv, n, D]."""
 
     __slots__ = ("kq", "ks", "kz", "vq", "vs", "vz", "kf", "vf", "nq", "nf", "kb", "vb", "kg", "vg", "mask",
-                 "kmode", "kch")
+                 "kmode", "kch", "pages", "page_size", "lens")
 
     def __init__(self, *, kq=None, ks=None, kz=None, vq=None, vs=None, vz=None, kf=None, vf=None,
-                 nq=0, nf=0, kb=16, vb=16, kg=32, vg=32, mask=None, kmode=0, kch=None):
+                 nq=0, nf=0, kb=16, vb=16, kg=32, vg=32, mask=None, kmode=0, kch=None, pages=None,
+                 page_size=0, lens=None):
         self.mask = mask          # optional uint8/bool [B, Hkv, n]: 0 = dead slot, never attended
         self.kmode, self.kch = kmode, kch    # kmode 1: per-token keys with divisor kch [B, Hkv, D]
+        self.pages, self.page_size = pages, int(page_size)   # optional page table [B, max_pages] int32
+        self.lens = lens          # optional live length per sequence [B] int32
         self.kq, self.ks, self.kz, self.vq, self.vs, self.vz = kq, ks, kz, vq, vs, vz
         self.kf, self.vf, self.nq, self.nf = kf, vf, int(nq), int(nf)
         self.kb, self.vb, self.kg, self.vg = kb, vb, kg, vg
@@ -130,11 +139,13 @@ def kv_descriptor(prefix: Prefix, *, batch: int | None = None, heads: int | None
     device = dense_src.device
     kv.nq, kv.nf = int(prefix.nq), int(prefix.nf)
     kv.kgroup, kv.vgroup = int(prefix.kg), int(prefix.vg)
+    paged = prefix.pages is not None
     if prefix.nq:
         if prefix.kb != 4 or prefix.vb != 4:
             raise NotImplementedError("packed caches: the kernels read 4-bit keys and values")
         kv.layout = _lib.MA_KV_PACKED_TOKEN if prefix.kmode == 1 else _lib.MA_KV_PACKED_CHANNEL
         B, H = prefix.vq.shape[0], prefix.vq.shape[1]
+        pool = prefix.vq.shape[0]
         D = prefix.vq.shape[3] * prefix.vq.shape[4] * 2
         for name in ("kq", "vq"):
             t = getattr(prefix, name)
@@ -168,7 +179,23 @@ def kv_descriptor(prefix: Prefix, *, batch: int | None = None, heads: int | None
     else:
         kv.layout = _lib.MA_KV_DENSE
         B, H, D = prefix.kf.shape[0], prefix.kf.shape[1], prefix.kf.shape[3]
+        pool = prefix.kf.shape[0]
         kv.dtype = _lib.dtype_code(prefix.kf.dtype)
+    if paged:
+        pt = prefix.pages
+        if pt.dtype != torch.int32 or pt.ndim != 2 or pt.stride(1) != 1:
+            raise ValueError("pages must be an int32 [B, max_pages] tensor with a contiguous page axis")
+        if prefix.page_size <= 0:
+            raise ValueError("paged prefixes need page_size")
+        B = pt.shape[0]
+        kv.pages, kv.spg, kv.page_size, kv.num_pages = pt.data_ptr(), pt.stride(0), prefix.page_size, pool
+        keep.append(pt)
+    if prefix.lens is not None:
+        ln = prefix.lens
+        if ln.dtype != torch.int32 or tuple(ln.shape) != (B,) or ln.stride(0) != 1:
+            raise ValueError("lens must be a contiguous int32 [B] tensor")
+        kv.lens = ln.data_ptr()
+        keep.append(ln)
     if prefix.nf:
         for name in ("kf", "vf"):
             t = getattr(prefix, name)
@@ -193,3 +220,80 @@ def kv_descriptor(prefix: Prefix, *, batch: int | None = None, heads: int | None
     if head_dim is not None and head_dim != D:
         raise ValueError("prefix head_dim does not match the query")
     return KVDesc(kv, keep, device, B, H, D, prefix.n)
+
+
+# ------------------------------------------------------------------- quantize-on-append
+def _check_rows(x: torch.Tensor, name: str) -> None:
+    if x.ndim != 4 or x.stride(-1) != 1:
+        raise ValueError(f"{name} must be rank 4 [B, H, n, D] with a contiguous head_dim")
+    if x.dtype not in (torch.bfloat16, torch.float32):
+        raise ValueError(f"{name} must be bfloat16 or float32")
+
+
+def key_divisor(key: torch.Tensor) -> torch.Tensor:
+    """Token-mode key divisor sqrt(max(max_t |K|, 1e-4)) per (b, h, channel), fp32
+    [B, H, D] (cache.py:488-490)."""
+    _check_rows(key, "key")
+    lib = _lib.lib()
+    b, h, n, d = key.shape
+    out = torch.empty((b, h, d), device=key.device, dtype=torch.float32)
+    _lib.check("ma_key_divisor", lib.ma_key_divisor(
+        key.data_ptr(), _lib.dtype_code(key.dtype), b, h, n, d, i64(*_strides3(key)), out.data_ptr(),
+        i64(out.stride(0), out.stride(1)), _lib.stream_handle(key.device)))
+    return out
+
+
+def quantize_tokens(x: torch.Tensor, kchan: torch.Tensor | None = None, group: int = 32):
+    """Per-token 4-bit quantization over groups of 32 channels, computed in x's dtype as
+    the reference does (reference.py:182-213; token-mode keys x / kchan first, cache.py:
+    491-497). Returns payload [B,H,n,D/32,16] u8, scale and zero [B,H,n,D/32] fp16."""
+    _check_rows(x, "x")
+    lib = _lib.lib()
+    b, h, n, d = x.shape
+    pay = torch.empty((b, h, n, d // group, group // 2), device=x.device, dtype=torch.uint8)
+    sc = torch.empty((b, h, n, d // group), device=x.device, dtype=torch.float16)
+    zr = torch.empty_like(sc)
+    kc = None
+    if kchan is not None:
+        kc = kchan.to(torch.float32)
+        if kc.stride(-1) != 1:
+            kc = kc.contiguous()
+    _lib.check("ma_quantize_tokens", lib.ma_quantize_tokens(
+        x.data_ptr(), _lib.dtype_code(x.dtype), b, h, n, d, i64(*_strides3(x)), _lib.ptr(kc),
+        i64(kc.stride(0), kc.stride(1)) if kc is not None else None, group, pay.data_ptr(), i64(*_strides3(pay)),
+        sc.data_ptr(), zr.data_ptr(), i64(*_strides3(sc)), _lib.stream_handle(x.device)))
+    return pay, sc, zr
+
+
+def quantize_keys_channel(key: torch.Tensor, group: int = 32):
+    """KIVI per-channel 4-bit key quantization over groups of 32 tokens (reference.py:
+    58-90). Returns payload [B,H,n/32,D,16] u8, scale and zero [B,H,n/32,D] fp16."""
+    _check_rows(key, "key")
+    lib = _lib.lib()
+    b, h, n, d = key.shape
+    ng = n // group
+    pay = torch.empty((b, h, ng, d, group // 2), device=key.device, dtype=torch.uint8)
+    sc = torch.empty((b, h, ng, d), device=key.device, dtype=torch.float16)
+    zr = torch.empty_like(sc)
+    _lib.check("ma_quantize_keys_channel", lib.ma_quantize_keys_channel(
+        key.data_ptr(), _lib.dtype_code(key.dtype), b, h, n, d, i64(*_strides3(key)), group, pay.data_ptr(),
+        i64(*_strides3(pay)), sc.data_ptr(), zr.data_ptr(), i64(*_strides3(sc)), _lib.stream_handle(key.device)))
+    return pay, sc, zr
+
+
+def pack_prefix(key: torch.Tensor, value: torch.Tensor, *, key_mode: str = "token", group: int = 32,
+                kchan: torch.Tensor | None = None) -> Prefix:
+    """A fully packed k4v4 prefix from dense K/V [B, H, n, D] on the device: values per
+    token, keys per token (with the divisor, computed from K unless given) or per
+    channel (KIVI)."""
+    vq, vs, vz = quantize_tokens(value, group=group)
+    n = key.shape[2]
+    if key_mode == "token":
+        kch = key_divisor(key) if kchan is None else kchan
+        kq, ks, kz = quantize_tokens(key, kch, group=group)
+        return Prefix(kq=kq, ks=ks, kz=kz, vq=vq, vs=vs, vz=vz, nq=n, kb=4, vb=4, kg=group, vg=group, kmode=1,
+                      kch=kch)
+    if key_mode == "channel":
+        kq, ks, kz = quantize_keys_channel(key, group=group)
+        return Prefix(kq=kq, ks=ks, kz=kz, vq=vq, vs=vs, vz=vz, nq=n, kb=4, vb=4, kg=group, vg=group, kmode=0)
+    raise ValueError(f"key_mode must be 'token' or 'channel', got {key_mode!r}")

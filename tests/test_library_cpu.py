@@ -66,7 +66,7 @@ def test_argument_validation_without_gpu(lib):
     rows = MaRows()
     assert lib.ma_prefix_attention(rows, MaKV(), 4, MaBlock(), 1.0, 0, 0, 0, None, i64(0, 0, 0), None,
                                    None, None, None, 0, None) == -1
-    assert lib.ma_select_topk(None, 1, 1, 8, i64(8, 8), None, 3, None, None, i64(3, 3), None) == -1
+    assert lib.ma_select_topk(None, 1, 1, 8, i64(8, 8), None, None, 3, None, None, i64(3, 3), None) == -1
     assert lib.ma_retain(None, None, 0, None, 1, 8, 4, 2, 0, None, None) == -1
 
 
