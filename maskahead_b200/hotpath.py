@@ -11,7 +11,8 @@ These functions are what the reference session's fast path does per layer
                       attention over [read set | block].
   probe_attention     the lookahead probe (2317-2332): block-causal attention of the probe
                       forward plus the prefix mass of the probe rows.
-  value_score         value_score (27-40) with the fp32 centre.
+  value_score         value_score (27-40) with the fp32 centre, over dense values;
+  value_score_prefix  the same over any cache layout (packed values dequantized in place).
   lookahead_survivors EvictionState.survivors for the lookahead policy (eviction.py:364-409).
 """
 
@@ -28,7 +29,7 @@ from .kernels.splitk import prefix_scores, splitk_attention
 from .layouts import Prefix, as_prefix, kv_descriptor
 
 __all__ = ["Step0Result", "fast_step0", "compact_attention", "probe_attention", "value_score",
-           "lookahead_survivors"]
+           "value_score_prefix", "lookahead_survivors"]
 
 
 @dataclass(slots=True)
@@ -134,6 +135,26 @@ def value_score(a: torch.Tensor, v: torch.Tensor, live_mask: torch.Tensor | None
         desc.kv, bb, 1, d, a3.data_ptr(), _lib.i64(a3.stride(0), a3.stride(1)), score.data_ptr(),
         _lib.i64(score.stride(0), score.stride(1)), ws.data_ptr(), ws.numel(), _lib.stream_handle(a.device)))
     return score.reshape(*lead, n)
+
+
+def value_score_prefix(a: torch.Tensor, prefix) -> torch.Tensor:
+    """value_score over a cache layout (dense, packed k4v4 or paged): a [B, Hkv, n] fp32,
+    the values read (dequantized) from the prefix; dead slots score 0 (session.py:27-40,
+    with the live values _live_values would dequantize, session.py:2020-2025)."""
+    lib = _lib.lib()
+    prefix = as_prefix(prefix)
+    b, h, n = a.shape
+    desc = kv_descriptor(prefix, batch=b, heads=h)
+    a3 = a.to(torch.float32)
+    if a3.stride(-1) != 1:
+        a3 = a3.contiguous()
+    score = torch.empty((b, h, n), device=a.device, dtype=torch.float32)
+    nbytes = lib.ma_value_score_workspace(b, h, n, desc.head_dim)
+    ws = _lib.workspace(a.device, "value_score", nbytes)
+    _lib.check("ma_value_score", lib.ma_value_score(
+        desc.kv, b, h, desc.head_dim, a3.data_ptr(), _lib.i64(a3.stride(0), a3.stride(1)), score.data_ptr(),
+        _lib.i64(score.stride(0), score.stride(1)), ws.data_ptr(), ws.numel(), _lib.stream_handle(a.device)))
+    return score
 
 
 def lookahead_survivors(pos: torch.Tensor, score: torch.Tensor, capacity: int, *, recent_window: int,
