@@ -31,6 +31,7 @@
 
 #include "ma_kernels.cuh"
 #include "ma_mma.cuh"
+#include "ma_stage.cuh"
 #include "ma_tcgen05.cuh"
 #include "ma_tma.cuh"
 
@@ -87,7 +88,12 @@ struct __align__(64) Args {
 // Per-thread staging of keys [j0, j0+kBN): gathered, masked or packed rows.
 template <bool PACKED>
 __device__ __forceinline__ void stage_rows(const Args& A, int b, int h, bool is_cur, int j0, int end, uint8_t* sK,
-                                           uint8_t* sV, uint8_t* sOk) {
+                                           uint8_t* sV, uint8_t* sOk, const float* sKch) {
+  if (PACKED && !is_cur) {   // packed prefix rows: wide loads, dequantized into the tile
+    stage::packed_tile<kBN, true, true>(A.kv, A.H, b, h, j0, end, A.idx, A.si0, A.si1, sK, sV, sOk, sKch,
+                                        threadIdx.x, kSoftThreads);
+    return;
+  }
   const __nv_bfloat16* ck = reinterpret_cast<const __nv_bfloat16*>(A.cur.k);
   const __nv_bfloat16* cv = reinterpret_cast<const __nv_bfloat16*>(A.cur.v);
   const __nv_bfloat16* kf = reinterpret_cast<const __nv_bfloat16*>(A.kv.kf);
@@ -192,6 +198,7 @@ __global__ void __launch_bounds__(kThreads, 1) attn_partial_tc(const __grid_cons
   uint8_t* ring = sQ + kQBytes;                         // [stage][K tile | V tile]
   uint8_t* sP = ring + kStages * kStageBytes;           // [2 M tiles][128 rows][128 B]
   __shared__ __align__(16) uint8_t sOkb[kStages][kBN];
+  __shared__ float sKch[kD];                            // token-mode key divisor of (b, h)
   __shared__ uint32_t s_taddr;
   // full: a stage's tile landed; s_full/s_free: an S buffer computed / read out;
   // p_full: P(t) written; o_done: O += P(t) V(t) completed; empty: a stage's last reader
@@ -364,11 +371,15 @@ __global__ void __launch_bounds__(kThreads, 1) attn_partial_tc(const __grid_cons
       __syncwarp();
       if (lane == 0) mbar_arrive(&q_full);
     }
+    if (PACKED && !is_cur && A.kv.layout == MA_KV_PACKED_TOKEN) {
+      if (threadIdx.x < kD) sKch[threadIdx.x] = A.kv.kchan[(int64_t)b * A.kv.skc[0] + (int64_t)h * A.kv.skc[1] + threadIdx.x];
+      softmax_sync();
+    }
     if (!tma_kv) {
       // prologue: tiles 0 .. kStages-2, one cp.async group each (tile i = group i)
       for (int st = 0; st < kStages - 1; ++st) {
         uint8_t* sK = ring + st * kStageBytes;
-        if (st < ntiles) stage_rows<PACKED>(A, b, h, is_cur, begin + st * kBN, end, sK, sK + kKVBytes, sOkb[st]);
+        if (st < ntiles) stage_rows<PACKED>(A, b, h, is_cur, begin + st * kBN, end, sK, sK + kKVBytes, sOkb[st], sKch);
         cp_async_commit();
       }
       if (ntiles > 0) {
@@ -453,7 +464,7 @@ __global__ void __launch_bounds__(kThreads, 1) attn_partial_tc(const __grid_cons
         const int sn = tn % kStages;
         if (tn < ntiles && ok) {
           uint8_t* sK = ring + sn * kStageBytes;
-          stage_rows<PACKED>(A, b, h, is_cur, begin + tn * kBN, end, sK, sK + kKVBytes, sOkb[sn]);
+          stage_rows<PACKED>(A, b, h, is_cur, begin + tn * kBN, end, sK, sK + kKVBytes, sOkb[sn], sKch);
         }
         cp_async_commit();
       }

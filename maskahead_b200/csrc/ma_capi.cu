@@ -24,7 +24,6 @@ using namespace ma;
 namespace {
 
 inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
-inline bool aligned4(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 3u) == 0; }
 inline int esize(int dtype) { return dtype == MA_F32 ? 4 : 2; }
 inline bool valid_dtype(int dtype) { return dtype == MA_F32 || dtype == MA_BF16; }
 
@@ -65,11 +64,13 @@ int check_kv(const ma_kv* kv, int D) {
   if (kv->nq == 0) return MA_OK;
   if (kv->vgroup <= 0 || (kv->vgroup % 8) != 0 || D % kv->vgroup) return MA_ERR_UNSUPPORTED;
   if (!kv->vq || !kv->vs || !kv->vz || !kv->kq || !kv->ks || !kv->kz) return MA_ERR_ARG;
-  if (!aligned4(kv->vq) || !aligned4(kv->kq)) return MA_ERR_ARG;
+  // payload rows are read with 16-byte loads: 16-byte aligned bases and strides
+  if (!aligned16(kv->vq) || !aligned16(kv->kq)) return MA_ERR_ARG;
   for (int i = 0; i < 3; ++i)
-    if ((kv->svq[i] & 3) || (kv->skq[i] & 3) || kv->svq[i] < 0 || kv->skq[i] < 0 || kv->sks[i] < 0 ||
+    if ((kv->svq[i] & 15) || (kv->skq[i] & 15) || kv->svq[i] < 0 || kv->skq[i] < 0 || kv->sks[i] < 0 ||
         kv->svs[i] < 0)
       return MA_ERR_ARG;
+  if (kv->vgroup != 32 || (kv->layout == MA_KV_PACKED_CHANNEL && kv->kgroup != 32)) return MA_ERR_UNSUPPORTED;
   if (kv->layout == MA_KV_PACKED_TOKEN) {
     if (!kv->kchan) return MA_ERR_ARG;
   } else {

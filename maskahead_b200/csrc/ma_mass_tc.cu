@@ -23,6 +23,7 @@
 // up to 256 slots, in flight from the start). Every wait is bounded.
 #include "ma_kernels.cuh"
 #include "ma_mma.cuh"
+#include "ma_stage.cuh"
 #include "ma_tcgen05.cuh"
 
 namespace ma {
@@ -66,7 +67,13 @@ struct Args {
 
 template <bool PACKED, bool CENTRE>
 __device__ __forceinline__ void load_tile(const Args& A, int b, int h, int j0, int end, uint8_t* sK, uint8_t* sV,
-                                          uint8_t* sOk) {
+                                          uint8_t* sOk, const float* sKch) {
+  if (PACKED) {   // packed slots: wide loads, dequantized into the tiles (dense tail by cp.async)
+    stage::packed_tile<kTile, false, CENTRE>(A.kv, A.H, b, h, j0, end, nullptr, 0, 0, sK, sV, sOk, sKch, threadIdx.x,
+                                             kThreads);
+    cp_async_commit();
+    return;
+  }
   const __nv_bfloat16* kf = reinterpret_cast<const __nv_bfloat16*>(A.kv.kf);
   const __nv_bfloat16* vf = reinterpret_cast<const __nv_bfloat16*>(A.kv.vf);
   for (int c = threadIdx.x; c < kTile * kChunks; c += kThreads) {
@@ -117,6 +124,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefix_mass_tc(const Args A) {
   __shared__ float sAres[kStages][kTile];        // a_j of the tiles still in the ring
   __shared__ uint8_t sOk[kStages][kTile];
   __shared__ float sRed[4][kD];
+  __shared__ float sKch[kD];                     // token-mode key divisor of (b, h)
   __shared__ float sTot[kD + 1];
   __shared__ float sAsum[4];
   __shared__ uint32_t s_taddr;
@@ -142,6 +150,8 @@ __global__ void __launch_bounds__(kThreads, 1) prefix_mass_tc(const Args A) {
 
   // the head's centre generation before this CTA arrives (the last CTA advances it)
   if (CENTRE && threadIdx.x == 0) sGen = *reinterpret_cast<volatile const unsigned*>(&A.sync[bh].y);
+  if (PACKED && A.kv.layout == MA_KV_PACKED_TOKEN && threadIdx.x < kD)
+    sKch[threadIdx.x] = A.kv.kchan[(int64_t)b * A.kv.skc[0] + (int64_t)h * A.kv.skc[1] + threadIdx.x];
   // selection rows r2 = g*T2 + i -> query row (h*G + g, q_rows[i]) and B_r, one row per thread
   for (int rr = threadIdx.x; rr < Npad; rr += kThreads) {
     const int g = rr / A.T2;
@@ -174,7 +184,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefix_mass_tc(const Args A) {
   for (int st = 0; st < kStages; ++st) {   // the queries join the group of the first tile
     const int j0 = begin + st * kTile;
     uint8_t* sK = sRing + 2 * st * kTileBytes;
-    if (j0 < end) load_tile<PACKED, CENTRE>(A, b, h, j0, end, sK, sK + kTileBytes, sOk[st]);
+    if (j0 < end) load_tile<PACKED, CENTRE>(A, b, h, j0, end, sK, sK + kTileBytes, sOk[st], sKch);
     else cp_async_commit();
   }
   if (threadIdx.x == 0) {
@@ -276,7 +286,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefix_mass_tc(const Args A) {
     fence_before_sync();
     __syncthreads();   // this stage and sA are consumed
     const int jn = j0 + kStages * kTile;
-    if (jn < end) load_tile<PACKED, CENTRE>(A, b, h, jn, end, sK, sV, sOk[stage]);
+    if (jn < end) load_tile<PACKED, CENTRE>(A, b, h, jn, end, sK, sV, sOk[stage], sKch);
     else cp_async_commit();
     stage = (stage + 1) % kStages;
   }
