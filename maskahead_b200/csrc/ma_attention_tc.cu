@@ -29,6 +29,9 @@
 // Semantics follow src/maskahead/kernels/splitk.py:115-190 (_sk_fwd).
 #include <string.h>
 
+#include <algorithm>
+
+#include "ma_combine.cuh"
 #include "ma_kernels.cuh"
 #include "ma_mma.cuh"
 #include "ma_stage.cuh"
@@ -83,7 +86,10 @@ struct __align__(64) Args {
   int tma_out;                  // partial rows leave by TMA
   Partials P;
   int* err;
+  int fuse;                     // merge the splits in this (cooperative) launch
+  FusedMerge fm;
 };
+constexpr uint64_t kMergeWaitNs = 200000000ull;   // bound on the wait for a group's splits
 
 // Per-thread staging of keys [j0, j0+kBN): gathered, masked or packed rows.
 template <bool PACKED>
@@ -205,7 +211,8 @@ __global__ void __launch_bounds__(kThreads, 1) attn_partial_tc(const __grid_cons
   // (the P.V MMA) completed
   __shared__ __align__(8) uint64_t full[kStages], empty[kStages], s_full[2], s_free[2], p_full, o_done, q_full,
       mbar_fin;
-  __shared__ int s_abort;
+  __shared__ int s_abort, s_merge_ok;
+  __shared__ unsigned s_gen;
 
   const int split = blockIdx.x;
   const int bh = blockIdx.y;
@@ -245,6 +252,8 @@ __global__ void __launch_bounds__(kThreads, 1) attn_partial_tc(const __grid_cons
   const int ntiles = end > begin ? (end - begin + kBN - 1) / kBN : 0;
   const float c2 = A.scale * kLog2e;                         // logit -> base-2 exponent units
 
+  const int group = bh * gridDim.z + blockIdx.z;            // fused merge: (head, row block)
+  if (A.fuse && threadIdx.x == 0) s_gen = *reinterpret_cast<volatile const unsigned*>(&A.fm.sync[group].y);
   if (threadIdx.x == kSoftThreads) {   // MMA warp, lane 0
     if (A.tma_q) prefetch_map(&A.qmap);
     if (tma_kv) {
@@ -351,6 +360,9 @@ __global__ void __launch_bounds__(kThreads, 1) attn_partial_tc(const __grid_cons
     __syncwarp();
   } else {
     // ------------------------------------------------------------ softmax warps
+    // (with a programmatic launch: the read set, the partials workspace and the outputs
+    // may still be in use by the kernel before; the MMA warp only loads inputs)
+    pdl_wait();
     bool ok = true;
     if (!A.tma_q && ntiles > 0) {  // queries by cp.async (waited at once: a rare layout)
       const __nv_bfloat16* qp = reinterpret_cast<const __nv_bfloat16*>(A.q.q);
@@ -565,7 +577,12 @@ __global__ void __launch_bounds__(kThreads, 1) attn_partial_tc(const __grid_cons
             tma::store_2d(&A.omap, 0, prow0, box);
             tma::store_2d(&A.omap, 64, prow0, box + kOutBox);
             tma::store_commit();
-            tma::store_wait_read();
+            if (A.fuse) {   // other CTAs read these rows: complete, then order for generic loads
+              tma::store_wait_all();
+              asm volatile("fence.proxy.async.global;\n" ::: "memory");
+            } else {
+              tma::store_wait_read();
+            }
           }
           __syncwarp();
         } else {
@@ -593,6 +610,50 @@ __global__ void __launch_bounds__(kThreads, 1) attn_partial_tc(const __grid_cons
   __syncthreads();
   fence_after_sync();
   if (warp == 0) tmem_dealloc(taddr, kTmemCols);
+  if (!A.fuse) return;
+
+  // ---- fused merge: every CTA of the (head, row block) group is resident (cooperative
+  // launch); the last to arrive advances the group's generation, the others wait for it
+  __threadfence();
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    bool ok = true;
+    const unsigned prev = atomicAdd(&A.fm.sync[group].x, 1u);
+    if (prev == gridDim.x - 1) {
+      A.fm.sync[group].x = 0u;   // ready for the next call
+      __threadfence();
+      atomicAdd(&A.fm.sync[group].y, 1u);
+    } else {
+      const uint64_t t0 = global_ns();
+      while (ld_acquire_u32(&A.fm.sync[group].y) == s_gen) {
+        if (global_ns() - t0 > kMergeWaitNs) {
+          ok = false;
+          atomicExch(A.err, 1);
+          break;
+        }
+        __nanosleep(128);
+      }
+    }
+    s_merge_ok = ok ? 1 : 0;
+  }
+  __syncthreads();
+  // this split's share of the group's rows, one warp per row (weights scratch in the ring)
+  const int R_blk = min(kRowTile, R - r0);
+  const int per = (R_blk + (int)gridDim.x - 1) / (int)gridDim.x;
+  const int lo = split * per, hi = min(R_blk, lo + per);
+  float* sW = reinterpret_cast<float*>(ring) + warp * kCombineMaxSplits;
+  __nv_bfloat16* out = reinterpret_cast<__nv_bfloat16*>(A.fm.out);
+  for (int rr = lo + warp; rr < hi; rr += kWarps) {
+    if (s_merge_ok) {
+      combine_row<__nv_bfloat16, __nv_bfloat16>(A.q, H, A.P, A.nsplit, A.cur.Tc > 0, out, A.fm.so[0], A.fm.so[1],
+                                                A.fm.so[2], A.fm.m_p, A.fm.l_p, A.fm.o_p, bh, r0 + rr, sW);
+    } else if (lane == 0) {   // a split never arrived: the row is reported as NaN
+      const int r = r0 + rr;
+      const int g = r / T, t = r - (r / T) * T;
+      __nv_bfloat16* dst = out + (int64_t)b * A.fm.so[0] + (int64_t)(h * G + g) * A.fm.so[1] + (int64_t)t * A.fm.so[2];
+      for (int d = 0; d < kD; ++d) dst[d] = __float2bfloat16_rn(NAN);
+    }
+  }
 }
 
 bool tma_map_rows(CUtensorMap* map, const void* base, int B, int H, int n, const int64_t s[3]) {
@@ -610,7 +671,9 @@ int tc_key_tile() { return kBN; }
 
 int launch_attn_partial_tc(const ma_rows& q, const ma_kv& kv, int H, const ma_block& cur, float scale,
                            int causal_block, int q_pos0, int c_pos0, const int64_t* idx, int64_t si0, int64_t si1,
-                           int n_keys, int split_len, int nsplit, const Partials& P, int* err, cudaStream_t st) {
+                           int n_keys, int split_len, int nsplit, const Partials& P, int* err, const FusedMerge* fm,
+                           bool* fused, cudaStream_t st) {
+  *fused = false;
   if (q.D != kD || !(scale > 0.f) || !P.o_bf16) return MA_ERR_UNSUPPORTED;
   Args A;
   memset(&A, 0, sizeof(A));
@@ -655,8 +718,38 @@ int launch_attn_partial_tc(const ma_rows& q, const ma_kv& kv, int H, const ma_bl
   auto go = [&](auto kernel) -> int {
     if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes) != cudaSuccess)
       return MA_ERR_CUDA;
-    kernel<<<grid, kThreads, kSmemBytes, st>>>(A);
-    return cudaGetLastError() == cudaSuccess ? MA_OK : MA_ERR_CUDA;
+    // fused merge: one wave of resident CTAs (cooperative launch), merge scratch in place
+    // (only when each split's share of the rows is one pass of its warps: the merge of a
+    // row is two dependent global round trips, so more rows per CTA serialize)
+    const int rows_per_split = (std::min(kRowTile, R) + (int)grid.x - 1) / (int)grid.x;
+    if (fm != nullptr && (int)(grid.y * grid.z) <= fm->sync_slots && (int)grid.x <= kCombineMaxSplits &&
+        q.dtype == MA_BF16 && rows_per_split <= kWarps) {
+      int dev = 0, coop = 0, per_sm = 0;
+      if (cudaGetDevice(&dev) == cudaSuccess &&
+          cudaDeviceGetAttribute(&coop, cudaDevAttrCooperativeLaunch, dev) == cudaSuccess && coop &&
+          cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, kThreads, kSmemBytes) == cudaSuccess &&
+          (long long)grid.x * grid.y * grid.z <= (long long)per_sm * device_sm_count()) {
+        Args Af = A;
+        Af.fuse = 1;
+        Af.fm = *fm;
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = grid;
+        cfg.blockDim = dim3(kThreads);
+        cfg.dynamicSmemBytes = kSmemBytes;
+        cfg.stream = st;
+        cudaLaunchAttribute attr[1];
+        attr[0].id = cudaLaunchAttributeCooperative;
+        attr[0].val.cooperative = 1;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+        if (cudaLaunchKernelEx(&cfg, kernel, Af) == cudaSuccess) {
+          *fused = true;
+          return MA_OK;
+        }
+        (void)cudaGetLastError();
+      }
+    }
+    return launch_pdl(kernel, grid, dim3(kThreads), kSmemBytes, st, A) == cudaSuccess ? MA_OK : MA_ERR_CUDA;
   };
   return kv.layout != MA_KV_DENSE ? go(attn_partial_tc<true>) : go(attn_partial_tc<false>);
 }

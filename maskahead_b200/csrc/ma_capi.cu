@@ -142,22 +142,30 @@ Plan plan_splits(int BH, int R, int n, int Tc, bool mma) {
   return p;
 }
 
+// The fused merge's (counter, generation) pairs: a fixed-size block at the front of the
+// workspace, so its words never move with the call's sizes.
+constexpr int kSyncSlots = 8192;
+constexpr size_t kSyncBytes = (size_t)kSyncSlots * sizeof(uint2);
+
 size_t attention_ws(int B, int H, int R, int n, int D, int Tc) {
   size_t best = 0;
   for (int m = 0; m < 2; ++m) {
     const Plan p = plan_splits(B * H, R, n, Tc, m == 1);
-    const size_t bytes = partials_bytes(B * H, p.S, p.Rp, D, p.o_bf16) + 512;
+    const size_t bytes = partials_bytes(B * H, p.S, p.Rp, D, p.o_bf16) + 512 + kSyncBytes;
     if (bytes > best) best = bytes;
   }
   return best;
 }
 
-// workspace: [256-byte aligned] error word block (256 B), then the split partials
-Partials carve_partials(void* ws, int BH, const Plan& p, int D, int** err) {
+// workspace: [256-byte aligned] error word block (256 B), the merge sync block, then the
+// split partials
+Partials carve_partials(void* ws, int BH, const Plan& p, int D, int** err, uint2** sync) {
   Partials P;
   char* base = reinterpret_cast<char*>((reinterpret_cast<uintptr_t>(ws) + 255) & ~uintptr_t(255));
   *err = reinterpret_cast<int*>(base);
   base += 256;
+  *sync = reinterpret_cast<uint2*>(base);
+  base += kSyncBytes;
   P.ml = reinterpret_cast<float2*>(base);
   P.o = base + (size_t)BH * p.S * p.Rp * sizeof(float2);
   P.o_bf16 = p.o_bf16 ? 1 : 0;
@@ -176,16 +184,33 @@ int run_attention(const ma_rows& q, const ma_kv& kv, int H, const ma_block& cur,
   const int R = G * q.T;
   const bool mma = use_mma_attention(q, kv, scale);
   const Plan p = plan_splits(q.B * H, R, n_keys, cur.Tc, mma);
-  if (!ws || ws_bytes < partials_bytes(q.B * H, p.S, p.Rp, q.D, p.o_bf16) + 512) return MA_ERR_WORKSPACE;
+  if (!ws || ws_bytes < partials_bytes(q.B * H, p.S, p.Rp, q.D, p.o_bf16) + 512 + kSyncBytes)
+    return MA_ERR_WORKSPACE;
   int* err = nullptr;
-  const Partials P = carve_partials(ws, q.B * H, p, q.D, &err);
+  uint2* sync = nullptr;
+  const Partials P = carve_partials(ws, q.B * H, p, q.D, &err, &sync);
   int rc;
   if (p.nsplit + (cur.Tc > 0 ? 1 : 0) > 0) {
-    rc = mma ? launch_attn_partial_tc(q, kv, H, cur, scale, causal_block, q_pos0, c_pos0, idx, si0, si1,
-                                      n_keys, p.split_len, p.nsplit, P, err, st)
-             : launch_attn_partial_simt(q, kv, H, cur, scale, causal_block, q_pos0, c_pos0, idx, si0,
-                                        si1, n_keys, p.split_len, p.nsplit, P, st);
-    if (rc != MA_OK) return rc;
+    if (mma) {
+      FusedMerge fm;
+      fm.out = out;
+      fm.so[0] = so[0];
+      fm.so[1] = so[1];
+      fm.so[2] = so[2];
+      fm.m_p = m_p;
+      fm.l_p = l_p;
+      fm.o_p = o_p;
+      fm.sync = sync;
+      fm.sync_slots = kSyncSlots;
+      bool fused = false;
+      rc = launch_attn_partial_tc(q, kv, H, cur, scale, causal_block, q_pos0, c_pos0, idx, si0, si1, n_keys,
+                                  p.split_len, p.nsplit, P, err, &fm, &fused, st);
+      if (rc != MA_OK || fused) return rc;
+    } else {
+      rc = launch_attn_partial_simt(q, kv, H, cur, scale, causal_block, q_pos0, c_pos0, idx, si0, si1, n_keys,
+                                    p.split_len, p.nsplit, P, st);
+      if (rc != MA_OK) return rc;
+    }
   }
   return launch_attn_combine(q, H, P, p.nsplit, cur.Tc > 0, out, so, m_p, l_p, o_p, st);
 }

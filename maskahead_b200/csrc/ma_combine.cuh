@@ -1,0 +1,136 @@
+// One row of the split-K merge: prefix splits first (giving the prefix-only softmax
+// statistics M_p, L_p and O_p that the mass pass needs), then the current block.
+// Follows the reference's combine (src/maskahead/kernels/splitk.py:271-318), with the
+// row order r = g*T + t of every KV head. Used by the combine kernel and by the
+// attention kernel's fused (cooperative) merge.
+#pragma once
+
+#include "ma_common.cuh"
+
+namespace ma {
+
+constexpr int kCombineMaxSplits = 256;   // partial slots per row (the planner never exceeds this)
+constexpr int kCombineChunk = 16;
+
+// Four channels of a partial row, fp32 or bf16.
+__device__ __forceinline__ float4 load_o4(const float* p) { return __ldcg(reinterpret_cast<const float4*>(p)); }
+__device__ __forceinline__ float4 load_o4(const __nv_bfloat16* p) {
+  const uint2 u = __ldcg(reinterpret_cast<const uint2*>(p));
+  const float2 a = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&u.x));
+  const float2 b = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&u.y));
+  return make_float4(a.x, a.y, b.x, b.y);
+}
+
+// One warp merges row r of KV head bh. The first kCombineChunk splits' partial outputs
+// are requested before the (m, l) pairs are reduced, so the two global round trips
+// overlap; lanes hold the pairs of splits lane, lane+32, ... in registers, form the
+// weights w_s = l_s * exp(m_s - M) once (into sWw, this warp's kCombineMaxSplits floats),
+// and every lane accumulates its 4 channels over the splits.
+template <typename QT, typename OT>
+__device__ __forceinline__ void combine_row(const ma_rows& q, int H, const Partials& P, int nsplit, bool has_cur,
+                                            QT* __restrict__ out, int64_t so0, int64_t so1, int64_t so2,
+                                            float* __restrict__ m_p, float* __restrict__ l_p, float* __restrict__ o_p,
+                                            int bh, int r, float* __restrict__ sWw) {
+  const int D = q.D;
+  const int G = q.Hq / H;
+  const int R = G * q.T;
+  const int lane = threadIdx.x & 31;
+  const int d0 = 4 * lane;
+  const bool active = d0 < D;
+  const int64_t row0 = (int64_t)bh * P.S * P.Rp + r;   // partial row of split 0; split s adds s*Rp
+  const OT* o = reinterpret_cast<const OT*>(P.o);
+  const OT* base = o + row0 * D + d0;
+  const int64_t step = (int64_t)P.Rp * D;
+
+  // the first chunk of partial outputs and the current block's row, in flight early
+  float4 buf[kCombineChunk];
+#pragma unroll
+  for (int i = 0; i < kCombineChunk; ++i)
+    buf[i] = (active && i < nsplit) ? load_o4(base + i * step) : make_float4(0.f, 0.f, 0.f, 0.f);
+  const int64_t crow = row0 + (int64_t)nsplit * P.Rp;
+  float2 mlc = make_float2(-INFINITY, 0.f);
+  float4 oc = make_float4(0.f, 0.f, 0.f, 0.f);
+  if (has_cur) {
+    mlc = __ldcg(&P.ml[crow]);
+    if (active) oc = load_o4(o + crow * D + d0);
+  }
+  // prefix splits: (m, l) pairs in registers, global max, weights, sum
+  float2 ml[kCombineMaxSplits / 32];
+#pragma unroll
+  for (int i = 0; i < kCombineMaxSplits / 32; ++i) {
+    const int sidx = lane + 32 * i;
+    ml[i] = sidx < nsplit ? __ldcg(&P.ml[row0 + (int64_t)sidx * P.Rp]) : make_float2(-INFINITY, 0.f);
+  }
+  float M = -INFINITY;
+#pragma unroll
+  for (int i = 0; i < kCombineMaxSplits / 32; ++i) M = fmaxf(M, ml[i].x);
+  M = warp_max(M);
+  const float Ms = (M == -INFINITY) ? 0.f : M;
+  float L = 0.f;
+#pragma unroll
+  for (int i = 0; i < kCombineMaxSplits / 32; ++i) {
+    const int sidx = lane + 32 * i;
+    if (sidx < nsplit) {
+      const float w = ml[i].y * expf(ml[i].x - Ms);
+      sWw[sidx] = w;
+      L += w;
+    }
+  }
+  L = warp_sum(L);
+  __syncwarp();
+  float4 A = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+  for (int i = 0; i < kCombineChunk; ++i) {
+    if (i < nsplit) {
+      const float w = sWw[i];
+      A.x = fmaf(buf[i].x, w, A.x);
+      A.y = fmaf(buf[i].y, w, A.y);
+      A.z = fmaf(buf[i].z, w, A.z);
+      A.w = fmaf(buf[i].w, w, A.w);
+    }
+  }
+  for (int s0 = kCombineChunk; s0 < nsplit; s0 += kCombineChunk) {
+#pragma unroll
+    for (int i = 0; i < kCombineChunk; ++i)
+      buf[i] = (active && s0 + i < nsplit) ? load_o4(base + (s0 + i) * step) : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+    for (int i = 0; i < kCombineChunk; ++i) {
+      if (s0 + i < nsplit) {
+        const float w = sWw[s0 + i];
+        A.x = fmaf(buf[i].x, w, A.x);
+        A.y = fmaf(buf[i].y, w, A.y);
+        A.z = fmaf(buf[i].z, w, A.z);
+        A.w = fmaf(buf[i].w, w, A.w);
+      }
+    }
+  }
+  const int64_t srow = (int64_t)bh * R + r;
+  if (m_p != nullptr && lane == 0) {
+    m_p[srow] = M;
+    l_p[srow] = L;
+  }
+  if (o_p != nullptr && active) {
+    const float inv = 1.f / (L > 0.f ? L : 1.f);
+    *reinterpret_cast<float4*>(o_p + srow * D + d0) = make_float4(A.x * inv, A.y * inv, A.z * inv, A.w * inv);
+  }
+  if (has_cur) {
+    const float mn = fmaxf(M, mlc.x);
+    const float ms = (mn == -INFINITY) ? 0.f : mn;
+    const float ea = expf(M - ms), eb = mlc.y * expf(mlc.x - ms);
+    L = L * ea + eb;
+    A.x = A.x * ea + oc.x * eb;
+    A.y = A.y * ea + oc.y * eb;
+    A.z = A.z * ea + oc.z * eb;
+    A.w = A.w * ea + oc.w * eb;
+  }
+  if (active) {
+    const float inv = 1.f / (L > 0.f ? L : 1.f);
+    const int b = bh / H, h = bh - (bh / H) * H;
+    const int g = r / q.T, t = r - (r / q.T) * q.T;
+    QT* dst = out + (int64_t)b * so0 + (int64_t)(h * G + g) * so1 + (int64_t)t * so2 + d0;
+    store4(dst, A.x * inv, A.y * inv, A.z * inv, A.w * inv);
+  }
+}
+
+
+}  // namespace ma

@@ -14,9 +14,24 @@ int simt_row_block();
 int simt_key_tile();
 
 // ma_attention_tc.cu (bf16 queries and caches, tcgen05 / TMEM)
+// The merge of the splits fused into the same (cooperative) launch: every split CTA of a
+// (head, row block) arrives on sync[group].x, the last advances sync[group].y, and each
+// CTA then merges its share of the group's rows into out / m_p / l_p / o_p.
+struct FusedMerge {
+  void* out;
+  int64_t so[3];
+  float* m_p;
+  float* l_p;
+  float* o_p;
+  uint2* sync;      // [B*H*row blocks], zero counters between calls
+  int sync_slots;   // capacity of sync
+};
+// Returns MA_OK with *fused = true when the merge ran inside the launch (the caller
+// then skips launch_attn_combine).
 int launch_attn_partial_tc(const ma_rows& q, const ma_kv& kv, int H, const ma_block& cur, float scale,
                            int causal_block, int q_pos0, int c_pos0, const int64_t* idx, int64_t si0, int64_t si1,
-                           int n_keys, int split_len, int nsplit, const Partials& P, int* err, cudaStream_t st);
+                           int n_keys, int split_len, int nsplit, const Partials& P, int* err, const FusedMerge* fm,
+                           bool* fused, cudaStream_t st);
 int tc_row_tile();
 int tc_key_tile();
 

@@ -105,11 +105,6 @@ __device__ __forceinline__ void load_tile(const Args& A, int b, int h, int j0, i
   cp_async_commit();
 }
 
-__device__ __forceinline__ unsigned ld_acquire(const unsigned* p) {
-  unsigned v;
-  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];\n" : "=r"(v) : "l"(p) : "memory");
-  return v;
-}
 
 template <bool PACKED, bool CENTRE>
 __global__ void __launch_bounds__(kThreads, 1) prefix_mass_tc(const Args A) {
@@ -343,7 +338,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefix_mass_tc(const Args A) {
   // fused value score (cooperative launch: every CTA of the head is resident)
   if (!sLast && threadIdx.x == 0) {
     const uint64_t t0 = global_ns();
-    while (ld_acquire(&A.sync[bh].y) == sGen) {
+    while (ld_acquire_u32(&A.sync[bh].y) == sGen) {
       if (global_ns() - t0 > kWaitNs) {
         s_wait_ok = 0;
         atomicExch(A.err, 1);

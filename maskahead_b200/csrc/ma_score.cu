@@ -208,6 +208,7 @@ value_apply_kernel(ma_kv kv, int H, int D, const float* __restrict__ a, int64_t 
   const int n = kv.nq + kv.nf;
   const int bh = blockIdx.y;
   const int b = bh / H, h = bh - (bh / H) * H;
+  pdl_wait();   // the mass and centre of the kernels before
   const int grp = threadIdx.x >> 4, l16 = threadIdx.x & 15;
   const bool lane_on = l16 < D / 8;
   float cc[8];
@@ -290,7 +291,7 @@ int launch_value_apply(const ma_kv& kv, int B, int H, int D, const float* a, int
   const int n = kv.nq + kv.nf;
   if (n == 0) return MA_OK;
   dim3 grid((n + kApplyTok - 1) / kApplyTok, B * H);
-  value_apply_kernel<<<grid, kThreads, 0, st>>>(kv, H, D, a, sa0, sa1, centre, score, ss0, ss1);
+  launch_pdl(value_apply_kernel, grid, dim3(kThreads), 0, st, kv, H, D, a, sa0, sa1, centre, score, ss0, ss1);
   return cudaGetLastError() == cudaSuccess ? MA_OK : MA_ERR_CUDA;
 }
 

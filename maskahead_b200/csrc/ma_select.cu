@@ -187,6 +187,7 @@ select_topk_reg(const float* __restrict__ score, int H, int n, int64_t ss0, int6
   __shared__ unsigned sHist[256];
   __shared__ int sSel[2][2];
   __shared__ int sWarp[33];
+  pdl_wait();   // the scores of the kernel before
   const int bh = blockIdx.x;
   const int b = bh / H, h = bh - (bh / H) * H;
   const float* s = score + (int64_t)b * ss0 + (int64_t)h * ss1;
@@ -416,7 +417,8 @@ int launch_select_topk(const float* score, int B, int H, int n, int64_t ss0, int
                        int64_t si0, int64_t si1, cudaStream_t st) {
   if (n <= 1024 * 16) {  // keys in registers
     auto go = [&](auto kernel) {
-      kernel<<<B * H, kSelThreads, 0, st>>>(score, H, n, ss0, ss1, mask, lens, k, indices, values, si0, si1);
+      launch_pdl(kernel, dim3(B * H), dim3(kSelThreads), 0, st, score, H, n, ss0, ss1, mask, lens, k, indices,
+                 values, si0, si1);
     };
     if (n <= 1024 * 4) go(select_topk_reg<4>);
     else if (n <= 1024 * 8) go(select_topk_reg<8>);

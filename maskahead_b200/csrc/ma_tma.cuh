@@ -44,6 +44,8 @@ __device__ __forceinline__ void store_2d(const CUtensorMap* map, int c0, int c1,
 __device__ __forceinline__ void store_commit() { asm volatile("cp.async.bulk.commit_group;\n" ::: "memory"); }
 // wait until the issued stores have finished reading shared memory
 __device__ __forceinline__ void store_wait_read() { asm volatile("cp.async.bulk.wait_group.read 0;\n" ::: "memory"); }
+// wait until the issued stores are complete (their writes performed)
+__device__ __forceinline__ void store_wait_all() { asm volatile("cp.async.bulk.wait_group 0;\n" ::: "memory"); }
 
 }  // namespace tma
 
