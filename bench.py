@@ -62,9 +62,9 @@ CONFIGS = {
                           "64-slot pages (shuffled pool), sequences sharded across ranks; step 0 + 3 sub-steps"),
 }
 METRIC = "µs per block-step select+attend; achieved HBM GB/s vs peak; tokens/s at 1/2/4/8 GPU"
-# DRAM bytes per launch of the step-0 attention partial pass at cfg2, from the ncu capture
-# summarized in profiles/attn_partial_tc_cfg2_step0.md (re-taken per kernel change)
-ATTN_TRAFFIC_BYTES = {"cfg2": None}
+# DRAM bytes per launch of the step-0 attention kernel, from the ncu captures summarized in
+# profiles/attn_partial_tc_cfg2_step0.md and profiles/attn_partial_tc_cfg3_packed.md
+ATTN_TRAFFIC_BYTES = {"cfg2": 17_158_912, "cfg3": 5_673_728}
 
 
 def parse_args():
@@ -154,16 +154,18 @@ def rank_share(cfg: dict, rank: int, world: int) -> dict:
         return dict(lens=lens, H=h, Hq=cfg["Hq"] // world, head0=rank * h)
     if cfg["scaling"] == "weak":
         return dict(lens=lens, H=cfg["H"], Hq=cfg["Hq"], head0=0)
-    # strong scaling over sequences: contiguous ranges balanced by total length
+    # strong scaling over sequences: contiguous ranges, each cut at the prefix sum nearest
+    # to its ideal share of the total length (every share within one sequence of ideal)
     total = sum(lens)
-    bounds, acc, r = [0], 0, 1
-    for i, n in enumerate(lens):
-        acc += n
-        if r < world and acc >= total * r / world:
-            bounds.append(i + 1)
-            r += 1
-    while len(bounds) < world + 1:
-        bounds.append(len(lens))
+    prefix = [0]
+    for n in lens:
+        prefix.append(prefix[-1] + n)
+    bounds = [0]
+    for r in range(1, world):
+        goal = total * r / world
+        i = min(range(bounds[-1], len(lens) + 1), key=lambda j: abs(prefix[j] - goal))
+        bounds.append(i)
+    bounds.append(len(lens))
     return dict(lens=lens[bounds[rank]:bounds[rank + 1]], H=cfg["H"], Hq=cfg["Hq"], head0=0)
 
 
@@ -266,12 +268,7 @@ class Workload:
         """KV-head sharding: the full [B, Hq, T, D] output from every rank's heads (NCCL)."""
         if self.world == 1 or self.cfg["shard"] != "heads":
             return out
-        import torch
-        import torch.distributed as dist
-
-        buf = torch.empty((self.world,) + tuple(out.shape), device=out.device, dtype=out.dtype)
-        dist.all_gather_into_tensor(buf, out.contiguous())
-        return buf.permute(1, 0, 2, 3, 4).reshape(out.shape[0], -1, out.shape[2], out.shape[3])
+        return gather_heads(out, self.world)
 
     def block_step(self, retain: bool):
         """One block-step over every layer through the public hot-path API."""
@@ -307,6 +304,18 @@ class Workload:
             keep = lookahead_survivors(self.pos, score, c["C"], recent_window=c["W"], sink_tokens=c["sinks"])
         self.outputs = (outs, idxs, keep)
         return self.outputs
+
+
+def gather_heads(out, world: int):
+    """All-gather of per-rank head outputs [B, Hq/world, T, D] into [B, Hq, T, D]; rank r
+    holds query heads [r*Hq/world, (r+1)*Hq/world) (the heads of its KV heads)."""
+    import torch
+    import torch.distributed as dist
+
+    b = out.shape[0]
+    buf = torch.empty((world * b,) + tuple(out.shape[1:]), device=out.device, dtype=out.dtype)
+    dist.all_gather_into_tensor(buf, out.contiguous())   # rank-major along dim 0
+    return buf.view(world, b, *out.shape[1:]).permute(1, 0, 2, 3, 4).reshape(b, -1, out.shape[2], out.shape[3])
 
 
 def fused_scores(cfg: dict, share: dict) -> bool:
@@ -654,7 +663,8 @@ def run_ours(args):
                      "achieved": achieved, "peak": hbm_peak, "unit": "GB/s", "frac": achieved / hbm_peak,
                      "traffic": ATTN_TRAFFIC_BYTES.get(c["name"]), "peak_kind": f"{peak_kind} burst",
                      "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum of attn_partial_tc, "
-                                       "profiles/attn_partial_tc_cfg2_step0.md",
+                                       "profiles/attn_partial_tc_cfg2_step0.md (cfg2), "
+                                       "profiles/attn_partial_tc_cfg3_packed.md (cfg3)",
                      "us_per_launch": ms_attn * 1e3, "tensor_tflops": tflops, "tensor_frac": tflops / tf_peak,
                      "bytes_per_launch": ab["step0_layer"]},
         "algorithmic_bytes_per_step": step_bytes,
