@@ -529,7 +529,7 @@ def run_ours(args):
     for i in range(max(1, args.warmup)):
         wl.block_step(retain=retain_at(i))
     torch.cuda.synchronize()
-    graphs = {}
+    graphs, graph_outputs = {}, {}
     side = torch.cuda.Stream(dev)
     timing = "CUDA-graph replay, CUDA events"
     try:
@@ -538,7 +538,7 @@ def run_ours(args):
             for retain in sorted({retain_at(i) for i in range(c["interval"])}):
                 g = torch.cuda.CUDAGraph()
                 with torch.cuda.graph(g, stream=side):
-                    wl.block_step(retain)
+                    graph_outputs[retain] = wl.block_step(retain)
                 graphs[retain] = g
         stream.wait_stream(side)
         torch.cuda.synchronize()
@@ -603,6 +603,8 @@ def run_ours(args):
         h2d_retain = sum(t.numel() * t.element_size() for t in hp)
         d2h = outs_h.numel() * outs_h.element_size() + idx_h.numel() * 8
 
+        # the outputs of the captured step live in the graph's static buffers (wl.outputs
+        # holds them after the capture); eager steps produce fresh ones
         def e2e_step(i):
             retain = retain_at(i)
             wl.Q.copy_(hq, non_blocking=True)
@@ -611,9 +613,14 @@ def run_ours(args):
             if retain:
                 for dst, src in zip((wl.QP, wl.KCP, wl.VCP), hp):
                     dst.copy_(src, non_blocking=True)
-            outs, idxs, _ = wl.block_step(retain)
-            outs_h.copy_(torch.stack(outs), non_blocking=True)
-            idx_h.copy_(torch.stack(idxs), non_blocking=True)
+            if graphs:
+                graphs[retain].replay()
+                outs, idxs, _ = graph_outputs[retain]
+            else:
+                outs, idxs, _ = wl.block_step(retain)
+            for layer in range(c["L"]):
+                outs_h[layer].copy_(outs[layer], non_blocking=True)
+                idx_h[layer].copy_(idxs[layer], non_blocking=True)
 
         for i in range(2):
             e2e_step(i)
@@ -624,7 +631,10 @@ def run_ours(args):
         e2e = {"value": tokens / (ms_e / args.steps / 1e3), "unit": "tokens/s",
                "h2d_bytes_per_step": int(h2d_every + (h2d_retain / c["interval"] if c["retention"] else 0)),
                "d2h_bytes_per_step": int(d2h), "ms_per_step": ms_e / args.steps,
-               "path": "eager public API (maskahead_b200.hotpath) per layer, pinned host copies in and out"}
+               "path": ("pinned host -> device copies of the step's queries and block K/V, the block-step "
+                        "through the public API (maskahead_b200.hotpath) " +
+                        ("as a CUDA-graph replay" if graphs else "eagerly") +
+                        ", device -> pinned host copies of every layer's output and read set")}
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:

@@ -387,7 +387,34 @@ __global__ void __launch_bounds__(kThreads, 1) attn_partial_tc(const __grid_cons
       if (threadIdx.x < kD) sKch[threadIdx.x] = A.kv.kchan[(int64_t)b * A.kv.skc[0] + (int64_t)h * A.kv.skc[1] + threadIdx.x];
       softmax_sync();
     }
-    if (!tma_kv) {
+    // packed token-mode prefix: the register-pipelined staging (ma_stage.cuh), one
+    // (row, channel group) item per thread; tiles 0 and 1 up front, then tile t+2 is
+    // dequantized at iteration t from loads issued one iteration earlier
+    const bool tokpipe = PACKED && !is_cur && A.kv.layout == MA_KV_PACKED_TOKEN;
+    const int tj = threadIdx.x >> 2, tg = threadIdx.x & 3;
+    stage::TokItem pR, pC;
+    int sI = -1;
+    if (tokpipe) {
+      for (int u = 0; u < 2 && u < ntiles; ++u) {
+        stage::TokItem it;
+        stage::tok_locate(A.kv, A.H, b, h, stage::tok_slot(b, h, begin + u * kBN + tj, end, A.idx, A.si0, A.si1), it);
+        stage::tok_fetch(A.kv, h, tg, it);
+        uint8_t* sK = ring + u * kStageBytes;
+        stage::tok_store<kBN>(A.kv, b, h, tj, tg, it, sK, sK + kKVBytes, sOkb[u], sKch);
+      }
+      fence_proxy_async();
+      __syncwarp();
+      if (lane == 0)
+        for (int u = 0; u < 2 && u < ntiles; ++u) mbar_arrive(&full[u]);
+      pR.ok = pC.ok = false;
+      if (2 < ntiles) {
+        stage::tok_locate(A.kv, A.H, b, h, stage::tok_slot(b, h, begin + 2 * kBN + tj, end, A.idx, A.si0, A.si1), pR);
+        stage::tok_fetch(A.kv, h, tg, pR);
+      }
+      if (3 < ntiles)
+        stage::tok_locate(A.kv, A.H, b, h, stage::tok_slot(b, h, begin + 3 * kBN + tj, end, A.idx, A.si0, A.si1), pC);
+      if (4 < ntiles) sI = stage::tok_slot(b, h, begin + 4 * kBN + tj, end, A.idx, A.si0, A.si1);
+    } else if (!tma_kv) {
       // prologue: tiles 0 .. kStages-2, one cp.async group each (tile i = group i)
       for (int st = 0; st < kStages - 1; ++st) {
         uint8_t* sK = ring + st * kStageBytes;
@@ -417,8 +444,21 @@ __global__ void __launch_bounds__(kThreads, 1) attn_partial_tc(const __grid_cons
       fence_before_sync();
       __syncwarp();
       if (lane == 0) mbar_arrive(&s_free[t & 1]);
-      // (b) cp.async path: tile t+1's copies landed -> visible to the tensor core
-      if (!tma_kv) {
+      // (b) token pipeline: tile t+2 into its stage (its previous tile's P.V completed one
+      // iteration ago), loads advance one tile; cp.async path: tile t+1's copies landed
+      if (tokpipe) {
+        if (t + 2 < ntiles) {
+          uint8_t* sK = ring + ((t + 2) % kStages) * kStageBytes;
+          stage::tok_store<kBN>(A.kv, b, h, tj, tg, pR, sK, sK + kKVBytes, sOkb[(t + 2) % kStages], sKch);
+          fence_proxy_async();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&full[(t + 2) % kStages]);
+        }
+        pR = pC;
+        if (t + 3 < ntiles) stage::tok_fetch(A.kv, h, tg, pR);
+        if (t + 4 < ntiles) stage::tok_locate(A.kv, A.H, b, h, sI, pC);
+        sI = (t + 5 < ntiles) ? stage::tok_slot(b, h, begin + (t + 5) * kBN + tj, end, A.idx, A.si0, A.si1) : -1;
+      } else if (!tma_kv) {
         cp_async_wait<kStages - 3>();
         fence_proxy_async();
         __syncwarp();
@@ -471,7 +511,7 @@ __global__ void __launch_bounds__(kThreads, 1) attn_partial_tc(const __grid_cons
         fence_after_sync();
         if (!ok) s_abort = 1;
       }
-      if (!tma_kv) {
+      if (!tma_kv && !tokpipe) {
         const int tn = t + kStages - 1;
         const int sn = tn % kStages;
         if (tn < ntiles && ok) {

@@ -196,5 +196,94 @@ __device__ __forceinline__ void packed_tile(const ma_kv& kv, int H, int b, int h
   }
 }
 
+// ---------------------------------------------------------------------------------
+// Register pipeline of the token-mode staging: ONE (row, 32-channel group) item per
+// thread and tile (64 rows x 4 groups = 256 threads). Its dependent loads are spread over
+// the four iterations before the item is needed --
+//   tok_slot    the read-set index (or the contiguous slot),
+//   tok_locate  liveness (lens, page table, mask) and storage coordinates,
+//   tok_fetch   the 16-byte K and V payloads and their scale/zero,
+//   tok_store   dequantization into the bf16 tile (the only step that waits),
+// so every global load has a whole tile of work to land.
+struct TokItem {
+  int slot;          // logical slot (-1: none)
+  int sb, sj;        // storage coordinates of the packed part
+  bool ok, tail;     // live; in the dense tail
+  uint4 pk, pv;      // payloads
+  uint16_t ks, kz, vs, vz;
+};
+
+__device__ __forceinline__ int tok_slot(int b, int h, int j, int end, const int64_t* idx, int64_t si0, int64_t si1) {
+  if (j >= end) return -1;
+  return idx ? (int)idx[(int64_t)b * si0 + (int64_t)h * si1 + j] : j;
+}
+
+__device__ __forceinline__ void tok_locate(const ma_kv& kv, int H, int b, int h, int slot, TokItem& it) {
+  it.slot = slot;
+  it.ok = slot >= 0 && kv_live(kv, H, b, h, slot);
+  it.tail = it.ok && slot >= kv.nq;
+  it.sb = b;
+  it.sj = slot;
+  if (it.ok && !it.tail && kv_paged(kv, slot)) kv_page(kv, b, slot, it.sb, it.sj);
+}
+
+__device__ __forceinline__ void tok_fetch(const ma_kv& kv, int h, int g, TokItem& it) {
+  if (!it.ok || it.tail) return;
+  const int64_t vo = (int64_t)it.sb * kv.svq[0] + (int64_t)h * kv.svq[1] + (int64_t)it.sj * kv.svq[2] + g * 16;
+  const int64_t vso = (int64_t)it.sb * kv.svs[0] + (int64_t)h * kv.svs[1] + (int64_t)it.sj * kv.svs[2] + g;
+  const int64_t ko = (int64_t)it.sb * kv.skq[0] + (int64_t)h * kv.skq[1] + (int64_t)it.sj * kv.skq[2] + g * 16;
+  const int64_t kso = (int64_t)it.sb * kv.sks[0] + (int64_t)h * kv.sks[1] + (int64_t)it.sj * kv.sks[2] + g;
+  it.pv = *reinterpret_cast<const uint4*>(kv.vq + vo);
+  it.pk = *reinterpret_cast<const uint4*>(kv.kq + ko);
+  it.vs = kv.vs[vso];
+  it.vz = kv.vz[vso];
+  it.ks = kv.ks[kso];
+  it.kz = kv.kz[kso];
+}
+
+// Item -> row jj, channels [32g, 32g+32) of the swizzled bf16 K and V tiles (ROWS rows).
+template <int ROWS>
+__device__ __forceinline__ void tok_store(const ma_kv& kv, int b, int h, int jj, int g, const TokItem& it, uint8_t* sK,
+                                          uint8_t* sV, uint8_t* sOk, const float* kchan_s) {
+  if (it.ok && !it.tail) {
+    float f[32];
+    dequant32(it.pv, half_bits_to_float(it.vs), half_bits_to_float(it.vz), f);
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {
+      float t[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) t[i] = bf16_round(f[8 * c + i]);
+      *reinterpret_cast<uint4*>(sV + tc::kmajor_off(jj, g * 4 + c, ROWS)) = bf16x8(t);
+    }
+    dequant32(it.pk, half_bits_to_float(it.ks), half_bits_to_float(it.kz), f);
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {
+      float t[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) t[i] = f[8 * c + i] * kchan_s[g * kGroupCh + 8 * c + i];
+      *reinterpret_cast<uint4*>(sK + tc::kmajor_off(jj, g * 4 + c, ROWS)) = bf16x8(t);
+    }
+  } else if (it.tail) {   // a dense bf16 tail row (rare): plain 16-byte loads
+    const int row = it.slot - kv.nq;
+    const __nv_bfloat16* kf = reinterpret_cast<const __nv_bfloat16*>(kv.kf);
+    const __nv_bfloat16* vf = reinterpret_cast<const __nv_bfloat16*>(kv.vf);
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {
+      const int ch = g * 4 + c;
+      const uint4 kk = *reinterpret_cast<const uint4*>(kf + (int64_t)b * kv.skf[0] + (int64_t)h * kv.skf[1] + (int64_t)row * kv.skf[2] + ch * 8);
+      const uint4 vv = *reinterpret_cast<const uint4*>(vf + (int64_t)b * kv.svf[0] + (int64_t)h * kv.svf[1] + (int64_t)row * kv.svf[2] + ch * 8);
+      *reinterpret_cast<uint4*>(sK + tc::kmajor_off(jj, ch, ROWS)) = kk;
+      *reinterpret_cast<uint4*>(sV + tc::kmajor_off(jj, ch, ROWS)) = vv;
+    }
+  } else {
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {
+      *reinterpret_cast<uint4*>(sV + tc::kmajor_off(jj, g * 4 + c, ROWS)) = make_uint4(0, 0, 0, 0);
+      *reinterpret_cast<uint4*>(sK + tc::kmajor_off(jj, g * 4 + c, ROWS)) = make_uint4(0, 0, 0, 0);
+    }
+  }
+  if (g == 0) sOk[jj] = it.ok ? 1 : 0;
+}
+
 }  // namespace stage
 }  // namespace ma
