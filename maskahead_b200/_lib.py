@@ -71,6 +71,7 @@ _vp, _i32, _f32, _sz = ctypes.c_void_p, ctypes.c_int, ctypes.c_float, ctypes.c_s
 _SIGNATURES = {
     "ma_version": (_i32, []),
     "ma_status_string": (ctypes.c_char_p, [_i32]),
+    "ma_set_attention_kernel": (_i32, [_i32]),
     "ma_prefix_attention_workspace": (_sz, [_i32] * 6),
     "ma_prefix_attention": (_i32, [_P(MaRows), _P(MaKV), _i32, _P(MaBlock), _f32, _i32, _i32, _i32,
                                    _vp, _P(ctypes.c_int64), _vp, _vp, _vp, _vp, _sz, _vp]),

@@ -290,6 +290,7 @@ __global__ void __launch_bounds__(kThreads, 1) attn_partial_tc(const __grid_cons
   if (!softmax_warp) {
     // ------------------------------------------------------------ MMA / TMA warp
     if (lane == 0) {
+      pdl_wait();   // with a programmatic launch, the inputs may come from the kernel before
       bool ok = true;
       bool q_ok = !A.tma_q;
       int issued = 0, waited = 0;   // TMA tiles issued / seen complete
@@ -361,7 +362,7 @@ __global__ void __launch_bounds__(kThreads, 1) attn_partial_tc(const __grid_cons
   } else {
     // ------------------------------------------------------------ softmax warps
     // (with a programmatic launch: the read set, the partials workspace and the outputs
-    // may still be in use by the kernel before; the MMA warp only loads inputs)
+    // may still be in use by the kernel before)
     pdl_wait();
     bool ok = true;
     if (!A.tma_q && ntiles > 0) {  // queries by cp.async (waited at once: a rare layout)

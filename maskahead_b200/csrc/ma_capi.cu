@@ -23,6 +23,9 @@ using namespace ma;
 
 namespace {
 
+int g_attention_kernel = 0;   // ma_set_attention_kernel
+bool fa_disabled() { return g_attention_kernel == 1; }
+
 inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 inline int esize(int dtype) { return dtype == MA_F32 ? 4 : 2; }
 inline bool valid_dtype(int dtype) { return dtype == MA_F32 || dtype == MA_BF16; }
@@ -112,9 +115,9 @@ int key_tile(bool mma) { return mma ? tc_key_tile() : simt_key_tile(); }
 // Splits over the keys: enough CTAs for one wave (tensor-core CTAs hold an SM each) or
 // two (CUDA-core CTAs, several per SM), the current block included, but no split shorter
 // than a few key tiles -- each split pays for staging its rows and writing R x D partials.
-Plan plan_splits(int BH, int R, int n, int Tc, bool mma) {
+Plan plan_splits(int BH, int R, int n, int Tc, bool mma, int key_tile_override = 0) {
   Plan p;
-  const int rt = row_tile(mma), kt = key_tile(mma);
+  const int rt = row_tile(mma), kt = key_tile_override > 0 ? key_tile_override : key_tile(mma);
   const int row_blocks = (R + rt - 1) / rt;
   // tensor-core partial rows are stored per 32-row warp box
   p.Rp = mma ? ((R + 31) / 32) * 32 : row_blocks * rt;
@@ -183,12 +186,15 @@ int run_attention(const ma_rows& q, const ma_kv& kv, int H, const ma_block& cur,
   const int G = q.Hq / H;
   const int R = G * q.T;
   const bool mma = use_mma_attention(q, kv, scale);
-  const Plan p = plan_splits(q.B * H, R, n_keys, cur.Tc, mma);
+  // TMA-fed dense bf16 calls take the 128-key-tile kernel (its plan never needs more
+  // partial slots than the 64-key one, which sizes the workspace)
+  const bool fa = mma && fa_eligible(q, kv, idx, cur, n_keys);
+  Plan p = plan_splits(q.B * H, R, n_keys, cur.Tc, mma, fa ? fa_key_tile() : 0);
   if (!ws || ws_bytes < partials_bytes(q.B * H, p.S, p.Rp, q.D, p.o_bf16) + 512 + kSyncBytes)
     return MA_ERR_WORKSPACE;
   int* err = nullptr;
   uint2* sync = nullptr;
-  const Partials P = carve_partials(ws, q.B * H, p, q.D, &err, &sync);
+  Partials P = carve_partials(ws, q.B * H, p, q.D, &err, &sync);
   int rc;
   if (p.nsplit + (cur.Tc > 0 ? 1 : 0) > 0) {
     if (mma) {
@@ -203,8 +209,18 @@ int run_attention(const ma_rows& q, const ma_kv& kv, int H, const ma_block& cur,
       fm.sync = sync;
       fm.sync_slots = kSyncSlots;
       bool fused = false;
-      rc = launch_attn_partial_tc(q, kv, H, cur, scale, causal_block, q_pos0, c_pos0, idx, si0, si1, n_keys,
-                                  p.split_len, p.nsplit, P, err, &fm, &fused, st);
+      rc = MA_ERR_UNSUPPORTED;
+      if (fa && !fa_disabled()) {
+        rc = launch_attn_partial_fa(q, kv, H, cur, scale, causal_block, q_pos0, c_pos0, n_keys, p.split_len,
+                                    p.nsplit, P, err, &fm, &fused, st);
+        if (rc == MA_ERR_UNSUPPORTED) {   // a tensor map the TMA cannot describe: 64-key kernel
+          p = plan_splits(q.B * H, R, n_keys, cur.Tc, mma);
+          P = carve_partials(ws, q.B * H, p, q.D, &err, &sync);
+        }
+      }
+      if (rc == MA_ERR_UNSUPPORTED)
+        rc = launch_attn_partial_tc(q, kv, H, cur, scale, causal_block, q_pos0, c_pos0, idx, si0, si1, n_keys,
+                                    p.split_len, p.nsplit, P, err, &fm, &fused, st);
       if (rc != MA_OK || fused) return rc;
     } else {
       rc = launch_attn_partial_simt(q, kv, H, cur, scale, causal_block, q_pos0, c_pos0, idx, si0, si1, n_keys,
@@ -220,6 +236,12 @@ int run_attention(const ma_rows& q, const ma_kv& kv, int H, const ma_block& cur,
 extern "C" {
 
 int ma_version(void) { return (0 << 16) | 1; }
+
+int ma_set_attention_kernel(int which) {
+  const int prev = g_attention_kernel;
+  g_attention_kernel = (which == 1) ? 1 : 0;
+  return prev;
+}
 
 const char* ma_status_string(int status) {
   switch (status) {

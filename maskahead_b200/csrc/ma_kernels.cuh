@@ -35,6 +35,16 @@ int launch_attn_partial_tc(const ma_rows& q, const ma_kv& kv, int H, const ma_bl
 int tc_row_tile();
 int tc_key_tile();
 
+// ma_attention_fa.cu (TMA-fed bf16: the dense prefix without a read set, mask or paging,
+// and the current block; 128-key tiles, one softmax warpgroup per 128-row M tile, P in
+// tensor memory). split_len must be a multiple of fa_key_tile(); MA_ERR_UNSUPPORTED when
+// the call is not TMA-eligible (the caller then uses launch_attn_partial_tc).
+bool fa_eligible(const ma_rows& q, const ma_kv& kv, const int64_t* idx, const ma_block& cur, int n_keys);
+int fa_key_tile();
+int launch_attn_partial_fa(const ma_rows& q, const ma_kv& kv, int H, const ma_block& cur, float scale,
+                           int causal_block, int q_pos0, int c_pos0, int n_keys, int split_len, int nsplit,
+                           const Partials& P, int* err, const FusedMerge* fm, bool* fused, cudaStream_t st);
+
 // ma_combine.cu
 int launch_attn_combine(const ma_rows& q, int H, const Partials& P, int nsplit, bool has_cur,
                         void* out, const int64_t so[3], float* m_p, float* l_p, float* o_p,

@@ -1,0 +1,107 @@
+"""GPU parity of the 128-key-tile attention kernel (TMA-fed dense bf16 prefix and current
+block) and of the 64-key-tile kernel it replaces there, against the CPU oracle.
+
+Both kernels are run on the same inputs (``ma_set_attention_kernel``) and compared with
+``oracle.prefix_attention`` at the bf16 bar of the other attention tests (atol = rtol =
+2e-2: bf16 output rounding plus the bf16 P operand of P.V); the prefix-only statistics
+(max, sum, normalized output) are compared the same way. The sizes cover: an empty prefix,
+prefixes shorter than one tile, one key past a tile boundary, several splits, a
+current block longer than one tile, one and two 128-row M tiles, and several row tiles
+(R = G*T > 256).
+"""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+import oracle
+
+pytestmark = pytest.mark.gpu
+
+DEV = "cuda"
+TOL = 2e-2
+
+
+def _lib():
+    from maskahead_b200._lib import load_library
+
+    return load_library()
+
+
+def _run(which, q, k, v, kc, vc, causal, q_pos0, c_pos0, want_prefix):
+    from maskahead_b200.kernels import splitk_attention
+    from maskahead_b200.layouts import Prefix
+
+    prev = _lib().ma_set_attention_kernel(which)
+    try:
+        pre = Prefix.dense(k, v)
+        out, st = splitk_attention(q, pre, kc, vc, causal_block=causal, q_pos0=q_pos0, c_pos0=c_pos0,
+                                   want_prefix=want_prefix)
+        torch.cuda.synchronize()
+    finally:
+        _lib().ma_set_attention_kernel(prev)
+    return out, st
+
+
+@pytest.mark.parametrize("B,Hq,H,T,n,Tc,causal", [
+    (1, 4, 1, 32, 0, 32, 32),        # current block only
+    (1, 4, 1, 32, 1, 32, 0),         # one prefix key
+    (2, 6, 2, 64, 127, 64, 32),      # one partial tile
+    (1, 7, 1, 32, 129, 32, 32),      # a tile boundary + 1, R = 224 (two M tiles)
+    (1, 28, 4, 32, 1100, 32, 32),    # cfg2-like heads, several splits
+    (1, 8, 2, 128, 5000, 160, 64),   # current block longer than a tile, R = 512 (two row tiles)
+    (1, 4, 4, 256, 2048, 256, 128),  # T = 256: one query head per row tile
+])
+def test_fa_kernel_matches_oracle_and_tc(B, Hq, H, T, n, Tc, causal):
+    gen = torch.Generator().manual_seed(1000 * n + T + Hq)
+    D = 128
+    q = torch.randn(B, Hq, T, D, generator=gen).to(torch.bfloat16)
+    k = torch.randn(B, H, n, D, generator=gen).to(torch.bfloat16)
+    v = torch.randn(B, H, n, D, generator=gen).to(torch.bfloat16)
+    kc = torch.randn(B, H, Tc, D, generator=gen).to(torch.bfloat16)
+    vc = torch.randn(B, H, Tc, D, generator=gen).to(torch.bfloat16)
+    q_pos0 = Tc - T                  # the queries are the last T positions of the block
+    want, (mp, lp, op) = oracle.prefix_attention(q, k, v, kc, vc, causal_block=causal, q_pos0=q_pos0, c_pos0=0)
+    dev = [x.to(DEV) for x in (q, k, v, kc, vc)]
+    outs = {}
+    for which in (0, 1):
+        out, st = _run(which, *dev, causal, q_pos0, 0, n > 0)
+        np.testing.assert_allclose(out.float().cpu().numpy(), want.float().numpy(), rtol=TOL, atol=TOL,
+                                   err_msg=f"kernel {which}")
+        if n > 0:
+            np.testing.assert_allclose(st[0].cpu().numpy(), mp.numpy(), rtol=1e-5, atol=1e-5)
+            np.testing.assert_allclose(st[1].cpu().numpy(), lp.numpy(), rtol=TOL, atol=TOL)
+            np.testing.assert_allclose(st[2].cpu().numpy(), op.numpy(), rtol=TOL, atol=TOL)
+        outs[which] = out.float().cpu()
+    # the two kernels differ only in summation order and the lazy-rescale reference
+    np.testing.assert_allclose(outs[0].numpy(), outs[1].numpy(), rtol=TOL, atol=TOL)
+
+
+def test_fa_kernel_large_logits_rescale():
+    """Logits growing along the keys force the lazy rescale of O on nearly every tile."""
+    gen = torch.Generator().manual_seed(7)
+    B, Hq, H, T, n, D = 1, 8, 2, 32, 3000, 128
+    q = torch.randn(B, Hq, T, D, generator=gen).to(torch.bfloat16)
+    ramp = torch.linspace(0.0, 6.0, n)[None, None, :, None]
+    k = (torch.randn(B, H, n, D, generator=gen) * 0.5 + ramp * q.float().mean(dim=(1, 2))[:, None, None, :].sign())
+    k = k.to(torch.bfloat16)
+    v = torch.randn(B, H, n, D, generator=gen).to(torch.bfloat16)
+    kc = torch.randn(B, H, T, D, generator=gen).to(torch.bfloat16)
+    vc = torch.randn(B, H, T, D, generator=gen).to(torch.bfloat16)
+    want, _ = oracle.prefix_attention(q, k, v, kc, vc, causal_block=32)
+    out, _ = _run(0, *[x.to(DEV) for x in (q, k, v, kc, vc)], 32, 0, 0, False)
+    np.testing.assert_allclose(out.float().cpu().numpy(), want.float().numpy(), rtol=TOL, atol=TOL)
+
+
+def test_fa_kernel_repeated_calls_are_identical():
+    """The fused merge's counters reset between calls: the same inputs give the same bits."""
+    gen = torch.Generator().manual_seed(3)
+    B, Hq, H, T, n, D = 1, 28, 4, 32, 8192, 128
+    dev = [torch.randn(*s, generator=gen).to(torch.bfloat16).to(DEV)
+           for s in ((B, Hq, T, D), (B, H, n, D), (B, H, n, D), (B, H, T, D), (B, H, T, D))]
+    first, _ = _run(0, *dev, 32, 0, 0, False)
+    for _ in range(3):
+        again, _ = _run(0, *dev, 32, 0, 0, False)
+        assert torch.equal(first, again)
