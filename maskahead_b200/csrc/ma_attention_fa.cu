@@ -1,22 +1,23 @@
 // Split-K attention over [prefix | current block] for contiguous bf16 keys/values read by
-// TMA, with the softmax of each M tile in its own warpgroup and P kept in tensor memory.
+// TMA: one 128-row M tile per CTA, S double-buffered and P kept in tensor memory.
 //
-// CTA = 2 softmax warpgroups (warps 0-3: rows 0-127, warps 4-7: rows 128-255 of one KV
-// head's R = G*T query rows) + 1 MMA/TMA warp. Keys come in tiles of 128: K through 3
-// slots (a slot is refilled once its S was read), V through 2 (refilled when its P.V
-// completes), 32 KB each. Tensor memory (512 columns): S_m = Q_m K^T in columns
-// [128m, 128m+128) and O_m in [256+128m, 256+128m+128). Per tile t and M tile m:
-//   MMA warp   S_m(t) = Q_m K(t)^T (8 MMAs 128x128x16, A = Q in shared memory)
-//   warpgroup  row max over the 128 logits (lazy, base 2), P = 2^(u - m) rounded to bf16
-//              and written back over the first 64 columns of S_m as bf16 pairs
-//   MMA warp   O_m += P_m V(t) (8 MMAs, A = P_m from tensor memory, B = V MN-major)
-// The two warpgroups run out of phase, so the tensor core works on one M tile while the
-// other's softmax runs. S_m(t+1) is issued only once O_m += P_m(t) V(t) has completed
-// (its P shares the columns), which also keeps the lazy rescale of O_m race-free. With
-// one M tile (R - r0 <= 128) the warpgroups split the keys instead (even / odd tiles, the
-// same rows, separate S, P and O) and merge their (m, l, O) at the end.
-// Per split: (m, l) and o = acc / l as bf16 (ma_common.cuh), stored by TMA, the merge
-// as in ma_attention_tc.cu (fused into a cooperative launch when it is one pass).
+// CTA = 8 softmax warps + 1 MMA/TMA warp over 128 query rows (r0..r0+127 of one KV head's
+// R = G*T rows, ordered g*T + t) and one key range (a split of the prefix, or the current
+// block). Keys come in tiles of 128: K and V each through 3 slots of 32 KB (a K slot is
+// refilled once its S was read, a V slot once its P.V completed). Tensor memory (512
+// columns): S(t) = Q K(t)^T in buffer t&1 (columns [128(t&1), +128)), O in [256, 384).
+// Per tile t:
+//   MMA warp   S(t) = Q K(t)^T (8 MMAs 128x128x16, A = Q, B = K, K-major in shared memory),
+//              issued once K(t) is loaded and P.V(t-2) (whose P lives in the buffer) is done
+//   softmax    warp w holds rows 32(w&3).. of the tile and keys 64(w>>2).. of each S: its
+//              64 logits, the row max exchanged with its partner warp (w^4) through shared
+//              memory, lazy rescale of its half of O, P = 2^(u - m) rounded to bf16 written
+//              as bf16 pairs over the first 32 of its own 64 columns
+//   MMA warp   O += P V(t) (8 MMAs, A = P from tensor memory, B = V MN-major)
+// so S(t+1) is computed while the softmax of tile t runs. A rescale of O first waits for
+// the previous P.V to complete (lazy: only when the row max grows by more than e^8).
+// Per split: (m, l) and o = acc / l as bf16 (ma_common.cuh), stored by TMA, the merge as
+// in ma_attention_tc.cu (fused into a cooperative launch when it is one pass).
 // Every wait is bounded. Semantics follow src/maskahead/kernels/splitk.py:115-190.
 #include <string.h>
 
@@ -37,16 +38,15 @@ constexpr int kSoftWarps = 8;
 constexpr int kSoftThreads = kSoftWarps * 32;
 constexpr int kWarps = kSoftWarps + 1;
 constexpr int kThreads = kWarps * 32;
-constexpr int kMTile = 128;
-constexpr int kRowTile = 2 * kMTile;
+constexpr int kRowTile = 128;                      // query rows per CTA (one M tile)
 constexpr int kBN = 128;                           // keys per tile
 constexpr int kD = 128;
-constexpr int kKSlots = 3;                        // K tiles in flight (freed once S was read)
-constexpr int kVSlots = 2;                        // V tiles in flight (freed when P.V completes)
+constexpr int kKSlots = 3;                         // K tiles in flight (freed once S was read)
+constexpr int kVSlots = 3;                         // V tiles in flight (freed when P.V completes)
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr float kLazyLog2 = 8.0f * kLog2e;
 
-constexpr int kQBlock = kRowTile * 128;            // 32 KB: one 64-channel block of 256 rows
+constexpr int kQBlock = kRowTile * 128;            // 16 KB: one 64-channel block of 128 rows
 constexpr int kQBytes = 2 * kQBlock;
 constexpr int kKVBlock = kBN * 128;                // 16 KB: [128 rows][128 B]
 constexpr int kKVBytes = 2 * kKVBlock;             // a K or V tile: 32 KB
@@ -56,17 +56,19 @@ constexpr uint32_t kColS = 0, kColO = 256;
 constexpr int kOutBox = 32 * 128;
 constexpr uint64_t kMergeWaitNs = 200000000ull;
 constexpr uint64_t kStallNs = 500000000ull;        // MMA issuer: longest time without progress
+constexpr uint64_t kWaitNs = 500000000ull;
 
 struct __align__(64) Args {
   CUtensorMap kmap, vmap;       // prefix K/V [B][H][n][D]
   CUtensorMap ckmap, cvmap;     // current block K/V [B][H][Tc][D]
-  CUtensorMap qmap;             // queries [B][Hq][T][D]
+  CUtensorMap qmap;             // queries [B][Hq][T][D]: boxes of 128 rows
   CUtensorMap omap;             // partial outputs [BH * S * Rp][D] bf16 (stores)
   ma_rows q;
   ma_kv kv;
   ma_block cur;
   float scale;
   int H, causal_block, q_pos0, c_pos0, n_keys, split_len, nsplit;
+  int q_tall;                   // T >= 128: a row tile is 128 rows of one query head
   int tma_out;
   Partials P;
   int* err;
@@ -137,10 +139,12 @@ __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
   __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
   return *reinterpret_cast<uint32_t*>(&v);
 }
-// barrier of one softmax warpgroup (ids 1 and 2; 0 is __syncthreads)
-__device__ __forceinline__ void wg_sync(int m) {
-  asm volatile("bar.sync %0, 128;\n" ::"r"(1 + m) : "memory");
+// barrier of the warp pair (q, q+4) that shares rows 32q..32q+31 (ids 1-4; 0 is
+// __syncthreads, 5 the softmax warps)
+__device__ __forceinline__ void pair_sync(int q) {
+  asm volatile("bar.sync %0, 64;\n" ::"r"(1 + q) : "memory");
 }
+__device__ __forceinline__ void softmax_sync() { asm volatile("bar.sync 5, %0;\n" ::"r"(kSoftThreads) : "memory"); }
 
 // one 128-key tile of K or V (two 64-channel boxes) into dst, completing on `bar`
 __device__ __forceinline__ void tma_tile(const CUtensorMap* map, int b, int h, int j0, uint8_t* dst, uint64_t* bar) {
@@ -152,13 +156,14 @@ __device__ __forceinline__ void tma_tile(const CUtensorMap* map, int b, int h, i
 __global__ void __launch_bounds__(kThreads, 1) attn_partial_fa(const __grid_constant__ Args A) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t* sQ = smem;                                   // [2 d blocks][256 rows][128 B]
-  uint8_t* ring = sQ + kQBytes;                         // K slots, then V slots
-  uint8_t* sKs = ring;
-  uint8_t* sVs = ring + kKSlots * kKVBytes;
+  uint8_t* sQ = smem;                                   // [2 d blocks][128 rows][128 B]
+  uint8_t* sKs = sQ + kQBytes;                          // K slots
+  uint8_t* sVs = sKs + kKSlots * kKVBytes;              // V slots
   __shared__ uint32_t s_taddr;
-  __shared__ __align__(8) uint64_t kfull[kKSlots], vfull[kVSlots], s_full[2], p_full[2], o_done[2], q_full, mbar_fin;
+  __shared__ __align__(8) uint64_t kfull[kKSlots], vfull[kVSlots], s_full[2], p_full[2], o_done, q_full, mbar_fin;
   __shared__ int s_abort, s_merge_ok;
+  __shared__ float sPM[2][kRowTile];   // per key half: the row's tile max (fp32, exact)
+  __shared__ int sBad[2][4];           // per key half and row quarter: this tile aborts
 
   const int split = blockIdx.x;
   const int bh = blockIdx.y;
@@ -168,19 +173,14 @@ __global__ void __launch_bounds__(kThreads, 1) attn_partial_fa(const __grid_cons
   const int G = A.q.Hq / H;
   const int R = G * T;
   const int r0 = blockIdx.z * kRowTile;
-  const int mtiles = min(2, (R - r0 + kMTile - 1) / kMTile);
-  // one M tile: the two warpgroups split the keys (even / odd tiles) over the same rows,
-  // each with its own S, P and O, and merge at the end
-  const bool dual = mtiles == 1;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const bool softmax_warp = warp < kSoftWarps;
-  const int mt = (warp >> 2) & 1, quarter = warp & 3;
-  const int mrow = dual ? 0 : mt;                        // the M tile whose rows this warp holds
-  const int r = r0 + mrow * kMTile + quarter * 32 + lane;
-  const int wrow0 = r0 + mrow * kMTile + quarter * 32;
-  const bool wg_on = softmax_warp && mt < (dual ? 2 : mtiles);
-  const bool warp_rows = wg_on && wrow0 < R;             // warp-uniform
-  const bool row_ok = wg_on && r < R;
+  const int quarter = warp & 3, hf = (warp >> 2) & 1;   // rows 32*quarter.., keys 64*hf.. of a tile
+  const int rl = quarter * 32 + lane;
+  const int r = r0 + rl;
+  const int wrow0 = r0 + quarter * 32;
+  const bool warp_rows = softmax_warp && wrow0 < R;      // the same for both warps of a pair
+  const bool row_ok = softmax_warp && r < R;
   const int t_row = row_ok ? r % T : 0;
 
   const bool is_cur = split == A.nsplit;
@@ -197,9 +197,6 @@ __global__ void __launch_bounds__(kThreads, 1) attn_partial_fa(const __grid_cons
     vis_end = min(end, ((A.q_pos0 + t_row) / A.causal_block + 1) * A.causal_block - A.c_pos0);
   if (!row_ok) vis_end = begin;
   const int ntiles = end > begin ? (end - begin + kBN - 1) / kBN : 0;
-  // chain m (S_m, P_m, O_m): every tile for M tile m, or tiles m, m+2, ... in dual mode
-  const int nt0 = dual ? (ntiles + 1) / 2 : ntiles;
-  const int nt1 = dual ? ntiles / 2 : (mtiles > 1 ? ntiles : 0);
   const float c2 = A.scale * kLog2e;
   const int group = bh * gridDim.z + blockIdx.z;
 
@@ -211,11 +208,11 @@ __global__ void __launch_bounds__(kThreads, 1) attn_partial_fa(const __grid_cons
     prefetch_map(is_cur ? &A.cvmap : &A.vmap);
     for (int i = 0; i < kKSlots; ++i) mbar_init(&kfull[i], 1);
     for (int i = 0; i < kVSlots; ++i) mbar_init(&vfull[i], 1);
-    for (int m = 0; m < 2; ++m) {
-      mbar_init(&s_full[m], 1);
-      mbar_init(&p_full[m], 4);   // the warpgroup's warps
-      mbar_init(&o_done[m], 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&s_full[i], 1);
+      mbar_init(&p_full[i], kSoftWarps);
     }
+    mbar_init(&o_done, 1);
     mbar_init(&q_full, 1);
     mbar_init(&mbar_fin, 1);
     s_abort = 0;
@@ -227,38 +224,40 @@ __global__ void __launch_bounds__(kThreads, 1) attn_partial_fa(const __grid_cons
   fence_after_sync();
   const uint32_t taddr = s_taddr;
   const uint32_t lane_base = (uint32_t)(quarter * 32) << 16;
-  const uint32_t tS = taddr + lane_base + kColS + mt * 128;   // this warpgroup's S (and P)
-  const uint32_t tO = taddr + lane_base + kColO + mt * 128;   // this warpgroup's O
+  const uint32_t tSh = taddr + lane_base + kColS + 64 * hf;   // this warp's 64 columns of S buffer 0
+  const uint32_t tOh = taddr + lane_base + kColO + 64 * hf;   // this warp's half of O
   float m_run = -INFINITY, l_run = 0.f, m_true = -INFINITY;
 
   if (!softmax_warp) {
     // ------------------------------------------------------------ MMA / TMA warp
     if (lane == 0) {
-      // Event loop over the chains S_m(0) PV_m(0) S_m(1) PV_m(1) ..., issuing whatever
-      // became ready: S_m(u) needs its K tile and PV_m(u-1) completed (P_m lives in S_m's
-      // columns), PV_m(u) needs its V tile and the warpgroup's P_m(u). A K slot takes the
-      // next K tile once every S that read it was consumed (its P.V issued), a V slot once
-      // every P.V that read it completed. Each barrier has at most one completed but
-      // unobserved phase, so the parity tests are unambiguous.
+      // Event loop: S(t) needs K(t) loaded and P.V(t-2) completed (P(t-2) lives in the
+      // buffer); P.V(t) needs V(t), the softmax's P(t) and P.V(t-1) seen complete. A K slot
+      // takes its next tile once the S it held was consumed (its P.V issued), a V slot once
+      // its P.V completed. Each barrier has at most one completed but unobserved phase, so
+      // the parity tests are unambiguous.
       pdl_wait();   // with a programmatic launch, the inputs may come from the kernel before
       bool ok = true;
       int kIss = 0, kObs = 0, vIss = 0, vObs = 0;   // tiles issued / seen loaded
-      int sN[2] = {0, 0}, pN[2] = {0, 0}, oD[2] = {0, 0};
-      const int nt[2] = {nt0, nt1};
+      int sN = 0, pN = 0, oD = 0;                   // S issued, P.V issued, P.V seen complete
       const CUtensorMap* km = is_cur ? &A.ckmap : &A.kmap;
       const CUtensorMap* vm = is_cur ? &A.cvmap : &A.vmap;
-      const int hq0 = h * G + r0 / T;
-      tma::expect_tx(&q_full, (uint32_t)(kRowTile * 256));
-      tma::load_4d(sQ, &A.qmap, 0, 0, hq0, b, &q_full);
-      tma::load_4d(sQ + kQBlock, &A.qmap, 64, 0, hq0, b, &q_full);
+      tma::expect_tx(&q_full, (uint32_t)kQBytes);
+      if (A.q_tall) {   // 128 consecutive positions of one query head
+        tma::load_4d(sQ, &A.qmap, 0, r0 % T, h * G + r0 / T, b, &q_full);
+        tma::load_4d(sQ + kQBlock, &A.qmap, 64, r0 % T, h * G + r0 / T, b, &q_full);
+      } else {          // 128 / T whole query heads
+        tma::load_4d(sQ, &A.qmap, 0, 0, h * G + r0 / T, b, &q_full);
+        tma::load_4d(sQ + kQBlock, &A.qmap, 64, 0, h * G + r0 / T, b, &q_full);
+      }
       for (; kIss < kKSlots && kIss < ntiles; ++kIss)
         tma_tile(km, b, h, begin + kIss * kBN, sKs + kIss * kKVBytes, &kfull[kIss]);
       for (; vIss < kVSlots && vIss < ntiles; ++vIss)
         tma_tile(vm, b, h, begin + vIss * kBN, sVs + vIss * kKVBytes, &vfull[vIss]);
       const bool q_ok = mbar_wait(&q_full, 0);
       ok = q_ok;
-      const uint32_t idS = idesc_bf16(kMTile, kBN, false, false);
-      const uint32_t idO = idesc_bf16(kMTile, kD, false, true);
+      const uint32_t idS = idesc_bf16(kRowTile, kBN, false, false);
+      const uint32_t idO = idesc_bf16(kRowTile, kD, false, true);
       // base descriptors; a K step or a slot only moves the start address (field bits
       // [0,14) = address >> 4, no carry below 256 KB), so each MMA adds a constant
       const uint64_t qdesc = smem_desc(smem_addr(sQ), 16, 1024);
@@ -267,7 +266,7 @@ __global__ void __launch_bounds__(kThreads, 1) attn_partial_fa(const __grid_cons
       uint64_t t_idle = 0;
       bool armed = false;
       int spins = 0;
-      while (ok && (pN[0] < nt[0] || pN[1] < nt[1])) {
+      while (ok && pN < ntiles) {
         bool progress = false;
         if (kObs < kIss && mbar_test(&kfull[kObs % kKSlots], (uint32_t)(kObs / kKSlots) & 1u)) {
           ++kObs;
@@ -277,66 +276,45 @@ __global__ void __launch_bounds__(kThreads, 1) attn_partial_fa(const __grid_cons
           ++vObs;
           progress = true;
         }
-#pragma unroll
-        for (int m = 0; m < 2; ++m) {
-          if (oD[m] < pN[m] && mbar_test(&o_done[m], (uint32_t)oD[m] & 1u)) {
-            ++oD[m];
-            progress = true;
-          }
-          if (sN[m] == pN[m] && sN[m] < nt[m]) {
-            const int u = sN[m];
-            const int t = dual ? 2 * u + m : u;
-            if (kObs > t && oD[m] >= u) {
-              fence_after_sync();
-              const uint64_t ad0 = qdesc + (uint64_t)((dual ? 0 : m) * (kMTile * 128 / 16));
-              const uint64_t bd0 = kdesc + (uint64_t)((t % kKSlots) * (kKVBytes / 16));
-              const uint32_t dS = taddr + kColS + m * 128;
-#pragma unroll
-              for (int kk = 0; kk < kD / 16; ++kk)
-                mma_bf16(dS, ad0 + (uint64_t)(((kk >> 2) * kQBlock + (kk & 3) * 32) >> 4),
-                         bd0 + (uint64_t)(((kk >> 2) * kKVBlock + (kk & 3) * 32) >> 4), idS, kk > 0);
-              mma_commit(&s_full[m]);
-              sN[m] = u + 1;
-              progress = true;
-            }
-          } else if (pN[m] < sN[m]) {
-            const int u = pN[m];
-            const int t = dual ? 2 * u + m : u;
-            if (vObs > t && mbar_test(&p_full[m], (uint32_t)u & 1u)) {
-              fence_after_sync();
-              const uint64_t bd0 = vdesc + (uint64_t)((t % kVSlots) * (kKVBytes / 16));
-              const uint32_t dO = taddr + kColO + m * kD, aP = taddr + kColS + m * 128;
-#pragma unroll
-              for (int kk = 0; kk < kBN / 16; ++kk)
-                mma_bf16_ta(dO, aP + kk * 8, bd0 + (uint64_t)(kk * (2048 / 16)), idO, u > 0 || kk > 0);
-              mma_commit(&o_done[m]);
-              pN[m] = u + 1;
-              progress = true;
-            }
-          }
+        if (oD < pN && mbar_test(&o_done, (uint32_t)oD & 1u)) {
+          ++oD;
+          progress = true;
         }
-        // K slot of tile kIss - kKSlots: free once that tile's P.V was issued by every chain
-        // that reads it (the warpgroup had read its S)
-        if (kIss < ntiles) {
-          const int prev = kIss - kKSlots;
-          const bool free_slot = dual ? pN[prev & 1] > (prev >> 1)
-                                      : (pN[0] > prev && pN[1] > prev);
-          if (free_slot) {
-            tma_tile(km, b, h, begin + kIss * kBN, sKs + (kIss % kKSlots) * kKVBytes, &kfull[kIss % kKSlots]);
-            ++kIss;
-            progress = true;
-          }
+        if (sN < ntiles && kObs > sN && oD >= sN - 1) {
+          fence_after_sync();
+          const uint64_t bd0 = kdesc + (uint64_t)((sN % kKSlots) * (kKVBytes / 16));
+          const uint32_t dS = taddr + kColS + (sN & 1) * 128;
+#pragma unroll
+          for (int kk = 0; kk < kD / 16; ++kk)
+            mma_bf16(dS, qdesc + (uint64_t)(((kk >> 2) * kQBlock + (kk & 3) * 32) >> 4),
+                     bd0 + (uint64_t)(((kk >> 2) * kKVBlock + (kk & 3) * 32) >> 4), idS, kk > 0);
+          mma_commit(&s_full[sN & 1]);
+          ++sN;
+          progress = true;
         }
-        // V slot of tile vIss - kVSlots: free once its P.V completed in every chain
-        if (vIss < ntiles) {
-          const int prev = vIss - kVSlots;
-          const bool free_slot = dual ? oD[prev & 1] > (prev >> 1)
-                                      : (oD[0] > prev && oD[1] > prev);
-          if (free_slot) {
-            tma_tile(vm, b, h, begin + vIss * kBN, sVs + (vIss % kVSlots) * kKVBytes, &vfull[vIss % kVSlots]);
-            ++vIss;
-            progress = true;
-          }
+        if (pN < sN && vObs > pN && oD >= pN && mbar_test(&p_full[pN & 1], (uint32_t)(pN >> 1) & 1u)) {
+          fence_after_sync();
+          const uint64_t bd0 = vdesc + (uint64_t)((pN % kVSlots) * (kKVBytes / 16));
+          const uint32_t aP = taddr + kColS + (pN & 1) * 128;
+#pragma unroll
+          for (int kk = 0; kk < kBN / 16; ++kk)   // keys 16kk..: P columns 64 (kk / 4) + 8 (kk % 4)
+            mma_bf16_ta(taddr + kColO, aP + (kk >> 2) * 64 + (kk & 3) * 8, bd0 + (uint64_t)(kk * (2048 / 16)), idO,
+                        pN > 0 || kk > 0);
+          mma_commit(&o_done);
+          ++pN;
+          progress = true;
+        }
+        // a K slot is free once the S it held was consumed (P.V of that tile issued)
+        if (kIss < ntiles && pN > kIss - kKSlots) {
+          tma_tile(km, b, h, begin + kIss * kBN, sKs + (kIss % kKSlots) * kKVBytes, &kfull[kIss % kKSlots]);
+          ++kIss;
+          progress = true;
+        }
+        // a V slot is free once its P.V completed
+        if (vIss < ntiles && oD > vIss - kVSlots) {
+          tma_tile(vm, b, h, begin + vIss * kBN, sVs + (vIss % kVSlots) * kKVBytes, &vfull[vIss % kVSlots]);
+          ++vIss;
+          progress = true;
         }
         if (progress) {
           spins = 0;
@@ -364,163 +342,155 @@ __global__ void __launch_bounds__(kThreads, 1) attn_partial_fa(const __grid_cons
         mbar_wait(&vfull[tt % kVSlots], (uint32_t)(tt / kVSlots) & 1u, 20000000ull);
     }
     __syncwarp();
-  } else if (wg_on) {
-    // ------------------------------------------------------------ softmax warpgroup mt
+  } else {
+    // ------------------------------------------------------------ softmax warps
     pdl_wait();   // the partials and outputs may still be in use by the kernel before
     bool ok = true;
-    const int nt_me = mt == 0 ? nt0 : nt1;
     const float2 c2x2 = make_float2(c2, c2);
-    for (int u = 0; u < nt_me; ++u) {
-      const int t = dual ? 2 * u + mt : u;
-      const int j0 = begin + t * kBN;
-      ok = mbar_wait(&s_full[mt], (uint32_t)u & 1u);
+    for (int t = 0; t < ntiles; ++t) {
+      const int bsel = t & 1;
+      ok = mbar_wait(&s_full[bsel], (uint32_t)(t >> 1) & 1u);
       fence_after_sync();
       if (!ok) s_abort = 1;
-      if (s_abort) break;
-      const int lim = vis_end - j0;   // keys i >= lim are hidden from this row
       if (warp_rows) {
-        // pass 1: the tile max over the raw logits (scale > 0 keeps the order); the four
-        // loads share one wait, hidden keys read as -inf
-        const bool part = !__all_sync(0xffffffffu, lim >= kBN);
-        float tmax;
-        {
-          float mx[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
-#pragma unroll 1
-          for (int hh = 0; hh < 2; ++hh) {
-            float s[64];
-            tmem_ld32(tS + hh * 64, s);
-            tmem_ld32(tS + hh * 64 + 32, s + 32);
-            tmem_ld_wait();
-            if (part) {
+        // this warp's 64 logits of the row (keys 64hf..64hf+63 of the tile)
+        const uint32_t tS = tSh + 128 * bsel;
+        const int lim = vis_end - (begin + t * kBN) - 64 * hf;   // keys i >= lim are hidden
+        float sv[64];
+        bool bad = s_abort != 0;
+        if (!bad) {
+          tmem_ld32(tS, sv);
+          tmem_ld32(tS + 32, sv + 32);
+          tmem_ld_wait();
+          if (!__all_sync(0xffffffffu, lim >= 64)) {
 #pragma unroll
-              for (int i = 0; i < 64; ++i) s[i] = hh * 64 + i < lim ? s[i] : -INFINITY;
-            }
-#pragma unroll
-            for (int i = 0; i < 64; i += 8) {
-#pragma unroll
-              for (int j = 0; j < 4; ++j) mx[j] = max3f(mx[j], s[i + j], s[i + 4 + j]);
-            }
+            for (int i = 0; i < 64; ++i) sv[i] = i < lim ? sv[i] : -INFINITY;
           }
-          tmax = fmaxf(max3f(mx[0], mx[1], mx[2]), mx[3]);
+        } else {
+#pragma unroll
+          for (int i = 0; i < 64; ++i) sv[i] = -INFINITY;
         }
-        // lazy rescale of O_m (its last P.V completed before S_m(u) was issued)
+        float mx[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) mx[j] = max3f(sv[j], sv[4 + j], sv[8 + j]);
+#pragma unroll
+        for (int i = 12; i + 8 <= 60; i += 8) {
+#pragma unroll
+          for (int j = 0; j < 4; ++j) mx[j] = max3f(mx[j], sv[i + j], sv[i + 4 + j]);
+        }
+        const float pm = max3f(max3f(mx[0], mx[1], sv[60]), max3f(mx[2], mx[3], sv[61]), fmaxf(sv[62], sv[63]));
+        // the pair's exchange: partial maxima and abort flags (the second barrier keeps the
+        // slots until both have read them)
+        sPM[hf][rl] = pm;
+        if (lane == 0) sBad[hf][quarter] = bad ? 1 : 0;
+        pair_sync(quarter);
+        const float tmax = fmaxf(pm, sPM[hf ^ 1][rl]);
+        bad = bad || sBad[hf ^ 1][quarter] != 0;
+        pair_sync(quarter);
+        if (bad) break;   // both warps of the pair leave together
+        // lazy rescale of this warp's half of O, after P.V(t-1) completed
         m_true = fmaxf(m_true, tmax);
         const float m_new = fmaxf(m_run, tmax * c2);
-        const bool grow = u > 0 && m_new > m_run + kLazyLog2;
+        const bool grow = t > 0 && m_new > m_run + kLazyLog2;
         if (__any_sync(0xffffffffu, grow)) {
+          if (!mbar_wait(&o_done, (uint32_t)(t - 1) & 1u, kWaitNs)) s_abort = 1;
+          fence_after_sync();
           const float alpha = grow ? ex2(m_run - m_new) : 1.f;
 #pragma unroll 1
-          for (int c = 0; c < kD / 32; ++c) {
+          for (int c = 0; c < 2; ++c) {
             float o[32];
-            tmem_ld32(tO + c * 32, o);
+            tmem_ld32(tOh + c * 32, o);
             tmem_ld_wait();
 #pragma unroll
             for (int i = 0; i < 32; ++i) o[i] *= alpha;
-            tmem_st32(tO + c * 32, o);
+            tmem_st32(tOh + c * 32, o);
           }
-          tmem_st_wait();
           if (grow) {
             l_run *= alpha;
             m_run = m_new;
           }
         }
-        if (u == 0) m_run = m_new;
+        if (t == 0) m_run = m_new;
         const float msl = (m_run == -INFINITY) ? 0.f : m_run;
-        // pass 2: P = 2^(s c2 - m) (packed FMA, one ex2 per key) as bf16 pairs over the
-        // first 64 columns of S_m (half hh's P lands on columns already read), the row sum
-        // from the fp32 values
+        // P = 2^(s c2 - m) (packed FMA, one ex2 per key) as bf16 pairs over the first 32 of
+        // this warp's 64 columns (already read); the row sum from the fp32 values
         const float2 nm2 = make_float2(-msl, -msl);
         float2 acc0 = make_float2(0.f, 0.f), acc1 = make_float2(0.f, 0.f);
-#pragma unroll 1
-        for (int hh = 0; hh < 2; ++hh) {
-          float sc[64];
-          tmem_ld32(tS + hh * 64, sc);
-          tmem_ld32(tS + hh * 64 + 32, sc + 32);
-          tmem_ld_wait();
-          if (part) {
 #pragma unroll
-            for (int i = 0; i < 64; ++i) sc[i] = hh * 64 + i < lim ? sc[i] : -INFINITY;
+        for (int c = 0; c < 2; ++c) {
+          uint32_t w[16];
+#pragma unroll
+          for (int i = 0; i < 16; ++i) {
+            float2 x = ffma2(make_float2(sv[32 * c + 2 * i], sv[32 * c + 2 * i + 1]), c2x2, nm2);
+            x.x = ex2(x.x);
+            x.y = ex2(x.y);
+            if (i & 1) acc1 = fadd2(acc1, x); else acc0 = fadd2(acc0, x);
+            w[i] = pack_bf16x2(x.x, x.y);
           }
-#pragma unroll
-          for (int c = 0; c < 2; ++c) {
-            uint32_t w[16];
-#pragma unroll
-            for (int i = 0; i < 16; ++i) {
-              float2 x = ffma2(make_float2(sc[32 * c + 2 * i], sc[32 * c + 2 * i + 1]), c2x2, nm2);
-              x.x = ex2(x.x);
-              x.y = ex2(x.y);
-              if (i & 1) acc1 = fadd2(acc1, x); else acc0 = fadd2(acc0, x);
-              w[i] = pack_bf16x2(x.x, x.y);
-            }
-            tmem_st16(tS + hh * 32 + c * 16, w);
-          }
+          tmem_st16(tS + c * 16, w);
         }
         tmem_st_wait();
         l_run += (acc0.x + acc0.y) + (acc1.x + acc1.y);
+      } else if (s_abort) {
+        break;   // no rows: nothing shared with a partner
       }
       fence_before_sync();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&p_full[mt]);
+      if (lane == 0) mbar_arrive(&p_full[bsel]);
     }
-    if (ok && nt_me > 0) {
-      ok = mbar_wait(&o_done[mt], (uint32_t)(nt_me - 1) & 1u);
+    if (ntiles > 0 && !s_abort) {
+      if (!mbar_wait(&o_done, (uint32_t)(ntiles - 1) & 1u, kWaitNs)) s_abort = 1;
       fence_after_sync();
     }
-    if (!ok) s_abort = 1;
   }
-  // join: every MMA done (the MMA warp drained), every warpgroup out of its loop
+  // join: every MMA done (the MMA warp drained), every softmax warp out of its loop
   fence_before_sync();
   __syncthreads();
   fence_after_sync();
 
-  // dual mode: each chain's (m_run, l_run, m_true) per row, in the (drained) V slots
-  float (*sMrg)[3][kMTile] = reinterpret_cast<float (*)[3][kMTile]>(sVs);
-  if (dual && softmax_warp) {
-    const int rl = quarter * 32 + lane;
-    sMrg[mt][0][rl] = m_run;
-    sMrg[mt][1][rl] = l_run;
-    sMrg[mt][2][rl] = m_true;
-    asm volatile("bar.sync 1, %0;\n" ::"r"(kSoftThreads) : "memory");
-  }
-  if (softmax_warp && wg_on) {
+  if (softmax_warp) {
+    // the row sum over both key halves (the slots are drained: scratch in the V slots)
+    float* sPL = reinterpret_cast<float*>(sVs);
+    sPL[hf * kRowTile + rl] = l_run;
+    softmax_sync();
+    const float l = l_run + sPL[(hf ^ 1) * kRowTile + rl];
     const int64_t prow = ((int64_t)bh * A.P.S + split) * A.P.Rp + r;
     const int prow0 = (int)(((int64_t)bh * A.P.S + split) * A.P.Rp + wrow0);
     if (s_abort != 0) {
       if (threadIdx.x == 0) atomicExch(A.err, 1);
-      if (row_ok && (!dual || mt == 0)) A.P.ml[prow] = make_float2(NAN, NAN);
-    } else if (!dual) {
+      if (row_ok && hf == 0) A.P.ml[prow] = make_float2(NAN, NAN);
+    } else {
       // the exact max: l under m_run times 2^(m_run - m_true) <= 1; o = acc / l is the same
       // under either reference
-      if (row_ok) {
+      if (row_ok && hf == 0) {
         const float fix = (m_true == -INFINITY) ? 1.f : ex2(m_run - m_true * c2);
-        A.P.ml[prow] = make_float2(m_true * A.scale, l_run * fix);
+        A.P.ml[prow] = make_float2(m_true * A.scale, l * fix);
       }
-      const float inv = l_run > 0.f ? 1.f / l_run : 0.f;
+      const float inv = l > 0.f ? 1.f / l : 0.f;
       if (warp_rows) {
+        float o[64];
+        if (ntiles > 0) {
+          tmem_ld32(tOh, o);
+          tmem_ld32(tOh + 32, o + 32);
+          tmem_ld_wait();
+#pragma unroll
+          for (int i = 0; i < 64; ++i) o[i] *= inv;
+        } else {
+#pragma unroll
+          for (int i = 0; i < 64; ++i) o[i] = 0.f;
+        }
         if (ntiles > 0 && A.tma_out) {
-          // the warp's 32 rows -> two 32-row x 64-channel boxes in the (drained) ring,
-          // 128-byte swizzled, then two TMA box stores by lane 0
-          uint8_t* box = ring + warp * (2 * kOutBox);
-#pragma unroll 1
-          for (int c = 0; c < kD / 32; ++c) {
-            float o[32];
-            tmem_ld32(tO + c * 32, o);
-            tmem_ld_wait();
-            uint8_t* line = box + (c >> 1) * kOutBox + lane * 128;
+          // the warp's 32 rows x 64 channels -> one box in the K slots, 128-byte swizzled
+          // (chunk q of line i at q ^ (i & 7)), stored by lane 0
+          uint8_t* box = sKs + warp * kOutBox;
+          uint8_t* line = box + lane * 128;
 #pragma unroll
-            for (int qq = 0; qq < 4; ++qq) {
-              float f8[8];
-#pragma unroll
-              for (int i = 0; i < 8; ++i) f8[i] = o[8 * qq + i] * inv;
-              const int chunk = (c & 1) * 4 + qq;
-              *reinterpret_cast<uint4*>(line + ((chunk ^ (lane & 7)) << 4)) = float8_to_bf16x8(f8);
-            }
-          }
+          for (int qq = 0; qq < 8; ++qq)
+            *reinterpret_cast<uint4*>(line + ((qq ^ (lane & 7)) << 4)) = float8_to_bf16x8(o + 8 * qq);
           fence_proxy_async();
           __syncwarp();
           if (lane == 0) {
-            tma::store_2d(&A.omap, 0, prow0, box);
-            tma::store_2d(&A.omap, 64, prow0, box + kOutBox);
+            tma::store_2d(&A.omap, 64 * hf, prow0, box);
             tma::store_commit();
             if (A.fuse) {   // other CTAs read these rows: complete, then order for generic loads
               tma::store_wait_all();
@@ -530,86 +500,8 @@ __global__ void __launch_bounds__(kThreads, 1) attn_partial_fa(const __grid_cons
             }
           }
           __syncwarp();
-        } else {
-          __nv_bfloat16* obase = reinterpret_cast<__nv_bfloat16*>(A.P.o);
-#pragma unroll 1
-          for (int c = 0; c < kD / 32; ++c) {
-            float o[32];
-            if (ntiles > 0) {
-              tmem_ld32(tO + c * 32, o);
-              tmem_ld_wait();
-            }
-#pragma unroll
-            for (int i = 0; i < 32; ++i) o[i] = ntiles > 0 ? o[i] * inv : 0.f;
-            if (row_ok) {
-              uint4* dst = reinterpret_cast<uint4*>(obase + prow * kD + c * 32);
-#pragma unroll
-              for (int qq = 0; qq < 4; ++qq) dst[qq] = float8_to_bf16x8(o + 8 * qq);
-            }
-          }
-        }
-      }
-    } else {
-      // dual: merge the two chains' (m, l, O) per row; warpgroup m writes channels
-      // [64m, 64m+64) of the warp's 32 rows
-      const int rl = quarter * 32 + lane;
-      const float m0 = sMrg[0][0][rl], m1 = sMrg[1][0][rl];
-      const float M = fmaxf(m0, m1);
-      const float f0 = (M == -INFINITY || nt0 == 0) ? 0.f : ex2(m0 - M);
-      const float f1 = (M == -INFINITY || nt1 == 0) ? 0.f : ex2(m1 - M);
-      const float l = sMrg[0][1][rl] * f0 + sMrg[1][1][rl] * f1;
-      const float mtr = fmaxf(sMrg[0][2][rl], sMrg[1][2][rl]);
-      if (row_ok && mt == 0) {
-        const float fix = (mtr == -INFINITY) ? 1.f : ex2(M - mtr * c2);
-        A.P.ml[prow] = make_float2(mtr * A.scale, l * fix);
-      }
-      const float inv = l > 0.f ? 1.f / l : 0.f;
-      const float g0 = f0 * inv, g1 = f1 * inv;
-      const uint32_t tO0 = taddr + lane_base + kColO + 64 * mt;   // chain 0's O, this half
-      const uint32_t tO1 = tO0 + 128;                              // chain 1's O
-      if (warp_rows) {
-        float o[64];
-        if (ntiles > 0) {
-          tmem_ld32(tO0, o);
-          tmem_ld32(tO0 + 32, o + 32);
-          tmem_ld_wait();
-#pragma unroll
-          for (int i = 0; i < 64; ++i) o[i] *= g0;
-          if (nt1 > 0) {
-#pragma unroll
-            for (int c = 0; c < 2; ++c) {
-              float o1[32];
-              tmem_ld32(tO1 + 32 * c, o1);
-              tmem_ld_wait();
-#pragma unroll
-              for (int i = 0; i < 32; ++i) o[32 * c + i] = fmaf(o1[i], g1, o[32 * c + i]);
-            }
-          }
-        } else {
-#pragma unroll
-          for (int i = 0; i < 64; ++i) o[i] = 0.f;
-        }
-        if (ntiles > 0 && A.tma_out) {
-          uint8_t* box = ring + warp * kOutBox;
-          uint8_t* line = box + lane * 128;
-#pragma unroll
-          for (int qq = 0; qq < 8; ++qq)
-            *reinterpret_cast<uint4*>(line + ((qq ^ (lane & 7)) << 4)) = float8_to_bf16x8(o + 8 * qq);
-          fence_proxy_async();
-          __syncwarp();
-          if (lane == 0) {
-            tma::store_2d(&A.omap, 64 * mt, prow0, box);
-            tma::store_commit();
-            if (A.fuse) {
-              tma::store_wait_all();
-              asm volatile("fence.proxy.async.global;\n" ::: "memory");
-            } else {
-              tma::store_wait_read();
-            }
-          }
-          __syncwarp();
         } else if (row_ok) {
-          uint4* dst = reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(A.P.o) + prow * kD + 64 * mt);
+          uint4* dst = reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(A.P.o) + prow * kD + 64 * hf);
 #pragma unroll
           for (int qq = 0; qq < 8; ++qq) dst[qq] = float8_to_bf16x8(o + 8 * qq);
         }
@@ -647,11 +539,11 @@ __global__ void __launch_bounds__(kThreads, 1) attn_partial_fa(const __grid_cons
     s_merge_ok = ok ? 1 : 0;
   }
   __syncthreads();
-  // this split's share of the group's rows, one warp per row (weights scratch in the ring)
+  // this split's share of the group's rows, one warp per row (weights scratch in the slots)
   const int R_blk = min(kRowTile, R - r0);
   const int per = (R_blk + (int)gridDim.x - 1) / (int)gridDim.x;
   const int lo = split * per, hi = min(R_blk, lo + per);
-  float* sW = reinterpret_cast<float*>(ring) + warp * kCombineMaxSplits;
+  float* sW = reinterpret_cast<float*>(sKs) + warp * kCombineMaxSplits;
   __nv_bfloat16* out = reinterpret_cast<__nv_bfloat16*>(A.fm.out);
   for (int rr = lo + warp; rr < hi; rr += kWarps) {
     if (s_merge_ok) {
@@ -659,8 +551,8 @@ __global__ void __launch_bounds__(kThreads, 1) attn_partial_fa(const __grid_cons
                                                 A.fm.so[2], A.fm.m_p, A.fm.l_p, A.fm.o_p, bh, r0 + rr, sW);
     } else if (lane == 0) {   // a split never arrived: the row is reported as NaN
       const int rw = r0 + rr;
-      const int g = rw / T, t = rw - (rw / T) * T;
-      __nv_bfloat16* dst = out + (int64_t)b * A.fm.so[0] + (int64_t)(h * G + g) * A.fm.so[1] + (int64_t)t * A.fm.so[2];
+      const int g = rw / T, tt = rw - (rw / T) * T;
+      __nv_bfloat16* dst = out + (int64_t)b * A.fm.so[0] + (int64_t)(h * G + g) * A.fm.so[1] + (int64_t)tt * A.fm.so[2];
       for (int d = 0; d < kD; ++d) dst[d] = __float2bfloat16_rn(NAN);
     }
   }
@@ -677,12 +569,14 @@ bool tma_map_rows(CUtensorMap* map, const void* base, int B, int H, int n, const
 }  // namespace
 
 int fa_key_tile() { return kBN; }
+int fa_row_tile() { return kRowTile; }
 
 bool fa_eligible(const ma_rows& q, const ma_kv& kv, const int64_t* idx, const ma_block& cur, int n_keys) {
   const bool prefix_ok = n_keys == 0 || (kv.layout == MA_KV_DENSE && kv.dtype == MA_BF16 && !idx && !kv.mask &&
                                          !kv.pages && !kv.lens);
-  return q.dtype == MA_BF16 && q.D == kD && q.T <= kRowTile && kRowTile % q.T == 0 && prefix_ok &&
-         (n_keys > 0 || cur.Tc > 0);
+  // a row tile is 128 / T whole query heads, or 128 positions of one head
+  const bool rows_ok = q.T > 0 && (q.T <= kRowTile ? kRowTile % q.T == 0 : q.T % kRowTile == 0);
+  return q.dtype == MA_BF16 && q.D == kD && rows_ok && prefix_ok && (n_keys > 0 || cur.Tc > 0);
 }
 
 int launch_attn_partial_fa(const ma_rows& q, const ma_kv& kv, int H, const ma_block& cur, float scale,
@@ -715,7 +609,8 @@ int launch_attn_partial_fa(const ma_rows& q, const ma_kv& kv, int H, const ma_bl
   {
     const uint64_t dims[4] = {128, (uint64_t)q.T, (uint64_t)q.Hq, (uint64_t)q.B};
     const uint64_t strides[3] = {(uint64_t)q.sq[2] * 2, (uint64_t)q.sq[1] * 2, (uint64_t)q.sq[0] * 2};
-    const uint32_t box[4] = {64, (uint32_t)q.T, (uint32_t)(kRowTile / q.T), 1};
+    A.q_tall = q.T >= kRowTile ? 1 : 0;
+    const uint32_t box[4] = {64, (uint32_t)(A.q_tall ? kRowTile : q.T), (uint32_t)(A.q_tall ? 1 : kRowTile / q.T), 1};
     if (!make_tma_map_bf16_4d(&A.qmap, q.q, dims, strides, box)) return MA_ERR_UNSUPPORTED;
   }
   const int G = q.Hq / H;

@@ -115,9 +115,9 @@ int key_tile(bool mma) { return mma ? tc_key_tile() : simt_key_tile(); }
 // Splits over the keys: enough CTAs for one wave (tensor-core CTAs hold an SM each) or
 // two (CUDA-core CTAs, several per SM), the current block included, but no split shorter
 // than a few key tiles -- each split pays for staging its rows and writing R x D partials.
-Plan plan_splits(int BH, int R, int n, int Tc, bool mma, int key_tile_override = 0) {
+Plan plan_splits(int BH, int R, int n, int Tc, bool mma, bool fa = false) {
   Plan p;
-  const int rt = row_tile(mma), kt = key_tile_override > 0 ? key_tile_override : key_tile(mma);
+  const int rt = fa ? fa_row_tile() : row_tile(mma), kt = fa ? fa_key_tile() : key_tile(mma);
   const int row_blocks = (R + rt - 1) / rt;
   // tensor-core partial rows are stored per 32-row warp box
   p.Rp = mma ? ((R + 31) / 32) * 32 : row_blocks * rt;
@@ -152,8 +152,8 @@ constexpr size_t kSyncBytes = (size_t)kSyncSlots * sizeof(uint2);
 
 size_t attention_ws(int B, int H, int R, int n, int D, int Tc) {
   size_t best = 0;
-  for (int m = 0; m < 2; ++m) {
-    const Plan p = plan_splits(B * H, R, n, Tc, m == 1);
+  for (int m = 0; m < 3; ++m) {
+    const Plan p = plan_splits(B * H, R, n, Tc, m >= 1, m == 2);
     const size_t bytes = partials_bytes(B * H, p.S, p.Rp, D, p.o_bf16) + 512 + kSyncBytes;
     if (bytes > best) best = bytes;
   }
@@ -186,10 +186,10 @@ int run_attention(const ma_rows& q, const ma_kv& kv, int H, const ma_block& cur,
   const int G = q.Hq / H;
   const int R = G * q.T;
   const bool mma = use_mma_attention(q, kv, scale);
-  // TMA-fed dense bf16 calls take the 128-key-tile kernel (its plan never needs more
-  // partial slots than the 64-key one, which sizes the workspace)
-  const bool fa = mma && fa_eligible(q, kv, idx, cur, n_keys);
-  Plan p = plan_splits(q.B * H, R, n_keys, cur.Tc, mma, fa ? fa_key_tile() : 0);
+  // TMA-fed dense bf16 calls take the 128 x 128-tile kernel (its plan is sized into the
+  // workspace too)
+  const bool fa = mma && !fa_disabled() && fa_eligible(q, kv, idx, cur, n_keys);
+  Plan p = plan_splits(q.B * H, R, n_keys, cur.Tc, mma, fa);
   if (!ws || ws_bytes < partials_bytes(q.B * H, p.S, p.Rp, q.D, p.o_bf16) + 512 + kSyncBytes)
     return MA_ERR_WORKSPACE;
   int* err = nullptr;
@@ -210,7 +210,7 @@ int run_attention(const ma_rows& q, const ma_kv& kv, int H, const ma_block& cur,
       fm.sync_slots = kSyncSlots;
       bool fused = false;
       rc = MA_ERR_UNSUPPORTED;
-      if (fa && !fa_disabled()) {
+      if (fa) {
         rc = launch_attn_partial_fa(q, kv, H, cur, scale, causal_block, q_pos0, c_pos0, n_keys, p.split_len,
                                     p.nsplit, P, err, &fm, &fused, st);
         if (rc == MA_ERR_UNSUPPORTED) {   // a tensor map the TMA cannot describe: 64-key kernel
