@@ -146,9 +146,10 @@ typedef struct ma_block {
 /* ---- library ----------------------------------------------------------------------- */
 MA_API int ma_version(void);                       /* (major << 16) | minor                   */
 MA_API const char* ma_status_string(int status);
-/* Attention kernel choice for TMA-eligible dense bf16 calls (process-wide; for tests and
- * A/B timing): 0 = automatic (128-key-tile kernel), 1 = always the 64-key-tile kernel.
- * Returns the previous setting. Not part of the reference's interface.               */
+/* Kernel choice for TMA-eligible dense bf16 calls (process-wide; for tests and A/B
+ * timing): 0 = automatic (the TMA-pipelined attention and mass kernels), 1 = always the
+ * general kernels (64-key attention tiles, cp.async-staged mass). Returns the previous
+ * setting. Not part of the reference's interface.                                     */
 MA_API int ma_set_attention_kernel(int which);
 
 /* ---- attention over [prefix | current block] ----------------------------------------

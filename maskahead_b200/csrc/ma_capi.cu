@@ -304,8 +304,13 @@ int ma_prefix_scores(const ma_rows* q, const ma_kv* kv, int H, const int32_t* q_
   cudaStream_t st = (cudaStream_t)stream;
   if (tc) {
     bool fused = false;
-    rc = launch_prefix_mass_tc(*q, *kv, H, q_rows, T2, m_p, l_p, scale, mass, smass[0], smass[1], score,
-                               score ? sscore[0] : 0, score ? sscore[1] : 0, w, score != nullptr, &fused, st);
+    rc = MA_ERR_UNSUPPORTED;
+    if (!fa_disabled())   // TMA-fed dense bf16 cache: the pipelined kernel
+      rc = launch_prefix_mass_fa(*q, *kv, H, q_rows, T2, m_p, l_p, scale, mass, smass[0], smass[1], score,
+                                 score ? sscore[0] : 0, score ? sscore[1] : 0, w, score != nullptr, &fused, st);
+    if (rc == MA_ERR_UNSUPPORTED)
+      rc = launch_prefix_mass_tc(*q, *kv, H, q_rows, T2, m_p, l_p, scale, mass, smass[0], smass[1], score,
+                                 score ? sscore[0] : 0, score ? sscore[1] : 0, w, score != nullptr, &fused, st);
     if (rc || !score || fused) return rc;
     return launch_value_apply(*kv, q->B, H, q->D, mass, smass[0], smass[1], w.centre, score, sscore[0],
                               sscore[1], st);

@@ -80,6 +80,12 @@ int launch_prefix_mass_tc(const ma_rows& q, const ma_kv& kv, int H, const int32_
                           const float* l_p, float scale, float* mass, int64_t sm0, int64_t sm1, float* score,
                           int64_t ss0, int64_t ss1, const ValueWs& w, bool want_centre, bool* fused, cudaStream_t st);
 
+// ma_mass_fa.cu (TMA-fed dense bf16 cache without paging or a packed part): the same
+// contract as launch_prefix_mass_tc; MA_ERR_UNSUPPORTED when the cache is not eligible.
+int launch_prefix_mass_fa(const ma_rows& q, const ma_kv& kv, int H, const int32_t* q_rows, int T2, const float* m_p,
+                          const float* l_p, float scale, float* mass, int64_t sm0, int64_t sm1, float* score,
+                          int64_t ss0, int64_t ss1, const ValueWs& w, bool want_centre, bool* fused, cudaStream_t st);
+
 // ma_select.cu
 int launch_select_topk(const float* score, int B, int H, int n, int64_t ss0, int64_t ss1,
                        const uint8_t* mask, const int32_t* lens, int k, int64_t* indices, float* values,

@@ -1,0 +1,558 @@
+// Prefix mass, value-score centre and value score for contiguous bf16 caches read by TMA,
+// with a warp-specialized pipeline (the TMA-fed counterpart of ma_mass_tc.cu).
+//
+// Per slot j of the prefix, over the R2 = G*T2 selection rows r of its KV head:
+//     a_j = (1/R2) sum_r 2^(s_rj * scale * log2e - B_r),  B_r = M_p,r log2e + log2 L_p,r
+// (splitk.py:320-359; reference.py:318-366), the head's centre
+//     c = sum_j a_j v_j / max(sum_j a_j, 1e-12)            (session.py:27-40, 870-899)
+// and the value score a_j ||v_j - c||.
+//
+// CTA = 8 sum warps + 1 producer/MMA warp over one slot range of one head (one wave of
+// CTAs). Phase 1, per tile of 128 slots: the producer streams K and V tiles by TMA (two
+// slots each), issues S^T = K Q^T (tcgen05, M = 128 slots, N = the selection rows padded
+// to 16, double-buffered in tensor memory); sum warp w owns slot lane 32(w&3).. and half
+// of the rows (w>>2): it sums its exponentials from tensor memory, the halves meet in
+// shared memory, a_j is written, and the warps accumulate sum_j a_j v_j (channel pairs x
+// key quarters) from the V tile. The last CTA of the head reduces the per-CTA partials
+// in CTA order into c and advances the head's generation word. Phase 2 (cooperative
+// launch, every CTA resident): each CTA waits (bounded) for the generation, the producer
+// streams its V tiles again (newest first: V was loaded with an L2 evict_last policy, so
+// most come from L2) through all four slots, and the sum warps write a_j ||v_j - c||.
+// Every wait is bounded.
+#include <string.h>
+
+#include "ma_kernels.cuh"
+#include "ma_stage.cuh"
+#include "ma_tcgen05.cuh"
+#include "ma_tma.cuh"
+
+namespace ma {
+
+namespace {
+
+using namespace tc;
+
+constexpr int kSumWarps = 8;
+constexpr int kSumThreads = kSumWarps * 32;
+constexpr int kThreads = kSumThreads + 32;
+constexpr int kTile = 128;                   // slots per tile (= M = TMEM lanes)
+constexpr int kD = 128;
+constexpr int kMaxRows = 256;                // selection rows (N of the MMA)
+constexpr int kQBytes = kMaxRows * kD * 2;   // 64 KB
+constexpr int kBlock = kTile * 128;          // one 64-channel box of a tile: 16 KB
+constexpr int kTileBytes = 2 * kBlock;       // a K or V tile: 32 KB
+constexpr int kSlots = 4;                    // phase 1: K in slots 0-1, V in 2-3; phase 2: V in all
+constexpr int kSmemBytes = 1024 + kQBytes + kSlots * kTileBytes;
+constexpr uint32_t kTmemCols = 512;          // two S^T buffers of up to 256 columns
+constexpr float kLog2e = 1.4426950408889634f;
+constexpr uint64_t kWaitNs = 200000000ull;
+constexpr uint64_t kStallNs = 500000000ull;
+
+struct __align__(64) Args {
+  CUtensorMap kmap, vmap;   // K/V [B][H][n][D], boxes of 64 channels x 128 slots
+  ma_rows q;
+  ma_kv kv;
+  const int32_t* q_rows;
+  const float* m_p;
+  const float* l_p;
+  float* mass;
+  int64_t sm0, sm1;
+  float* score;             // phase 2 (cooperative launch), or null
+  int64_t ss0, ss1;
+  float* part;              // [BH][ctas][D+1] centre partials (centre only)
+  uint2* sync;              // [BH]: arrival counter, centre generation
+  float* centre;            // [BH][D]
+  int* err;
+  float scale;
+  int H, T2, slots_per_cta, want_centre;
+};
+
+__device__ __forceinline__ void mbar_arrive(uint64_t* mbar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];\n" ::"r"(smem_addr(mbar)) : "memory");
+}
+__device__ __forceinline__ bool mbar_test(uint64_t* mbar, uint32_t phase) {
+  uint32_t ok;
+  asm volatile(
+      "{\n.reg .pred p;\nmbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\nselp.u32 %0, 1, 0, p;\n}\n"
+      : "=r"(ok)
+      : "r"(smem_addr(mbar)), "r"(phase)
+      : "memory");
+  return ok != 0;
+}
+__device__ __forceinline__ void sum_sync() { asm volatile("bar.sync 1, %0;\n" ::"r"(kSumThreads) : "memory"); }
+
+__device__ __forceinline__ void tile_load(const CUtensorMap* map, int b, int h, int j0, uint8_t* dst, uint64_t* bar,
+                                          uint64_t policy) {
+  tma::expect_tx(bar, kTileBytes);
+  tma::load_4d_hint(dst, map, 0, j0, h, b, bar, policy);
+  tma::load_4d_hint(dst + kBlock, map, 64, j0, h, b, bar, policy);
+}
+
+// byte offset of channel chunk c (8 channels) of slot row j in a TMA tile (two 64-channel
+// boxes of 128 lines, 128-byte swizzle)
+__device__ __forceinline__ uint32_t chunk_off(int j, int c) {
+  return (uint32_t)((c >> 3) * kBlock + j * 128 + (((c & 7) ^ (j & 7)) << 4));
+}
+
+__global__ void __launch_bounds__(kThreads, 1) prefix_mass_fa(const __grid_constant__ Args A) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sQ = smem;                      // K-major [2 d blocks][Npad rows][128 B]
+  uint8_t* sSlot = sQ + kQBytes;           // 4 tile slots
+  __shared__ __align__(16) float sB[kMaxRows];   // per selection row: B_r (+inf: no contribution)
+  __shared__ int sRowT[kMaxRows];                // block position of selection row r (-1: none)
+  __shared__ float sHalf[2][kTile];
+  __shared__ __align__(16) float sA[kTile];
+  __shared__ float sRed[4][kD];
+  __shared__ float sTot[kD + 1];
+  __shared__ float sAsum[4];
+  __shared__ uint32_t s_taddr;
+  __shared__ __align__(8) uint64_t kfull[2], vfull[2], s_full[2], s_free[2], v_free[2], wfull[kSlots],
+      wfree[kSlots], mbar_fin;
+  __shared__ int s_abort, s_wait_ok, sLast;
+
+  const int n = A.kv.nf;
+  const int bh = blockIdx.y;
+  const int H = A.H;
+  const int b = bh / H, h = bh - (bh / H) * H;
+  const int G = A.q.Hq / H;
+  const int T = A.q.T;
+  const int R2 = G * A.T2;
+  const int Npad = (R2 + 15) & ~15;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const bool sum_warp = warp < kSumWarps;
+  const int quarter = warp & 3, chalf = (warp >> 2) & 1;
+  const int slot_lane = quarter * 32 + lane;          // this thread's slot within a tile (TMEM lane)
+  const int begin = blockIdx.x * A.slots_per_cta;
+  const int end = min(n, begin + A.slots_per_cta);
+  const int ntiles = end > begin ? (end - begin + kTile - 1) / kTile : 0;
+  const float inv_rows = 1.f / (float)R2;
+  const float c2 = A.scale * kLog2e;
+  const bool centre = A.want_centre != 0;
+
+  // the head's centre generation before this CTA arrives (the last CTA advances it)
+  unsigned gen0 = 0;
+  if (centre && threadIdx.x == 0) gen0 = *reinterpret_cast<volatile const unsigned*>(&A.sync[bh].y);
+  if (threadIdx.x == kSumThreads) {
+    asm volatile("prefetch.tensormap [%0];\n" ::"l"(reinterpret_cast<uint64_t>(&A.kmap)) : "memory");
+    asm volatile("prefetch.tensormap [%0];\n" ::"l"(reinterpret_cast<uint64_t>(&A.vmap)) : "memory");
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&kfull[i], 1);
+      mbar_init(&vfull[i], 1);
+      mbar_init(&s_full[i], 1);
+      mbar_init(&s_free[i], kSumWarps);
+      mbar_init(&v_free[i], kSumWarps);
+    }
+    for (int i = 0; i < kSlots; ++i) {
+      mbar_init(&wfull[i], 1);
+      mbar_init(&wfree[i], kSumWarps);
+    }
+    mbar_init(&mbar_fin, 1);
+    s_abort = 0;
+    s_wait_ok = 1;
+    asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
+  }
+  if (sum_warp) {
+    pdl_wait();   // m_p, l_p (and with a programmatic launch, the outputs) of the kernel before
+    // selection rows r2 = g*T2 + i -> query row (h*G + g, q_rows[i]) and B_r
+    for (int rr = threadIdx.x; rr < Npad; rr += kSumThreads) {
+      const int g = rr / A.T2;
+      const int t = rr < R2 ? A.q_rows[rr - g * A.T2] : -1;
+      const bool ok = t >= 0 && t < T;
+      float Bv = INFINITY;   // exp2(s - inf) = 0: no contribution
+      if (ok) {
+        const int64_t ri = (int64_t)bh * G * T + (int64_t)g * T + t;
+        const float L = A.l_p[ri];
+        if (L > 0.f) Bv = fmaf(A.m_p[ri], kLog2e, log2f(L));
+      }
+      sRowT[rr] = ok ? t : -1;
+      sB[rr] = Bv;
+    }
+    sum_sync();
+    // the selection rows' queries, K-major SW128 with Npad rows (zeros for padding)
+    const __nv_bfloat16* qp = reinterpret_cast<const __nv_bfloat16*>(A.q.q);
+    for (int c = threadIdx.x; c < Npad * (kD / 8); c += kSumThreads) {
+      const int rr = c / (kD / 8), ch = c % (kD / 8);
+      const int t = sRowT[rr];
+      uint8_t* dst = sQ + kmajor_off(rr, ch, Npad);
+      if (t >= 0) {
+        const int g = rr / A.T2;
+        cp_async16(smem_addr(dst), qp + (int64_t)b * A.q.sq[0] + (int64_t)(h * G + g) * A.q.sq[1] + (int64_t)t * A.q.sq[2] + ch * 8, true);
+      } else {
+        *reinterpret_cast<uint4*>(dst) = make_uint4(0, 0, 0, 0);
+      }
+    }
+    cp_async_commit();
+    cp_async_wait<0>();
+    fence_proxy_async();
+  }
+  if (warp == 0) tmem_alloc(&s_taddr, kTmemCols);
+  fence_before_sync();
+  __syncthreads();
+  fence_after_sync();
+  const uint32_t taddr = s_taddr;
+  float cacc0 = 0.f, cacc1 = 0.f, asum = 0.f;
+  const int cp = threadIdx.x & 63, kq = (threadIdx.x >> 6) & 3;   // centre: channel pair, key quarter
+
+  if (!sum_warp) {
+    // ------------------------------------------------------------ producer / MMA warp
+    if (lane == 0) {
+      pdl_wait();
+      bool ok = true;
+      int kIss = 0, kObs = 0, vIss = 0, vObs = 0, sN = 0, sDone = 0, sfObs = 0, vfObs = 0;
+      const uint64_t pol_k = tma::policy_evict_first(), pol_v = tma::policy_evict_last();
+      for (; kIss < 2 && kIss < ntiles; ++kIss)
+        tile_load(&A.kmap, b, h, begin + kIss * kTile, sSlot + kIss * kTileBytes, &kfull[kIss], pol_k);
+      if (centre)
+        for (; vIss < 2 && vIss < ntiles; ++vIss)
+          tile_load(&A.vmap, b, h, begin + vIss * kTile, sSlot + (2 + vIss) * kTileBytes, &vfull[vIss], pol_v);
+      const int vTiles = centre ? ntiles : 0;
+      const uint32_t idesc = idesc_bf16(kTile, Npad, false, false);
+      const uint64_t kdesc = smem_desc(smem_addr(sSlot), 16, 1024);
+      const uint64_t qdesc = smem_desc(smem_addr(sQ), 16, 1024);
+      const uint32_t qblk = (uint32_t)(Npad * 128);   // bytes of one 64-channel block of Q
+      uint64_t t_idle = 0;
+      bool armed = false;
+      int spins = 0;
+      while (ok && (sN < ntiles || kIss < ntiles || vIss < vTiles)) {
+        bool progress = false;
+        if (kObs < kIss && mbar_test(&kfull[kObs & 1], (uint32_t)(kObs >> 1) & 1u)) {
+          ++kObs;
+          progress = true;
+        }
+        if (sDone < sN && mbar_test(&s_full[sDone & 1], (uint32_t)(sDone >> 1) & 1u)) {
+          ++sDone;
+          progress = true;
+        }
+        if (sfObs < sDone && mbar_test(&s_free[sfObs & 1], (uint32_t)(sfObs >> 1) & 1u)) {
+          ++sfObs;
+          progress = true;
+        }
+        if (vfObs < vObs && mbar_test(&v_free[vfObs & 1], (uint32_t)(vfObs >> 1) & 1u)) {
+          ++vfObs;
+          progress = true;
+        }
+        if (vObs < vIss && mbar_test(&vfull[vObs & 1], (uint32_t)(vObs >> 1) & 1u)) {
+          ++vObs;
+          progress = true;
+        }
+        // S^T(t) = K(t) Q^T into buffer t&1, once K(t) is in and the sum warps released
+        // the buffer's previous tile
+        if (sN < ntiles && kObs > sN && sfObs >= sN - 1 && sDone >= sN - 1) {
+          fence_after_sync();
+          const uint64_t ad0 = kdesc + (uint64_t)((sN & 1) * (kTileBytes >> 4));
+          const uint32_t d = taddr + (sN & 1) * 256;
+#pragma unroll
+          for (int kk = 0; kk < kD / 16; ++kk)
+            mma_bf16(d, ad0 + (uint64_t)(((kk >> 2) * kBlock + (kk & 3) * 32) >> 4),
+                     qdesc + (uint64_t)(((kk >> 2) * qblk + (kk & 3) * 32) >> 4), idesc, kk > 0);
+          mma_commit(&s_full[sN & 1]);
+          ++sN;
+          progress = true;
+        }
+        // K slot of tile kIss - 2 is free once its S^T completed
+        if (kIss < ntiles && sDone > kIss - 2) {
+          tile_load(&A.kmap, b, h, begin + kIss * kTile, sSlot + (kIss & 1) * kTileBytes, &kfull[kIss & 1], pol_k);
+          ++kIss;
+          progress = true;
+        }
+        // V slot of tile vIss - 2 is free once the sum warps released it
+        if (vIss < vTiles && vfObs > vIss - 2) {
+          tile_load(&A.vmap, b, h, begin + vIss * kTile, sSlot + (2 + (vIss & 1)) * kTileBytes, &vfull[vIss & 1],
+                    pol_v);
+          ++vIss;
+          progress = true;
+        }
+        if (progress) {
+          spins = 0;
+          armed = false;
+        } else if (++spins == 256) {   // idle: bound the time without progress
+          spins = 0;
+          const uint64_t now = global_ns();
+          if (!armed) {
+            t_idle = now;
+            armed = true;
+          } else if (now - t_idle > kStallNs) {
+            ok = false;
+          }
+          if (s_abort) ok = false;
+        }
+      }
+      if (!ok) s_abort = 1;
+      // drain (bounded): every MMA, every load still in flight
+      mma_commit(&mbar_fin);
+      mbar_wait(&mbar_fin, 0, 20000000ull);
+      for (int tt = kObs; tt < kIss; ++tt) mbar_wait(&kfull[tt & 1], (uint32_t)(tt >> 1) & 1u, 20000000ull);
+      for (int tt = vObs; tt < vIss; ++tt) mbar_wait(&vfull[tt & 1], (uint32_t)(tt >> 1) & 1u, 20000000ull);
+    }
+    __syncwarp();
+  } else {
+    // ------------------------------------------------------------ sum warps
+    __shared__ int sDecide;
+    const int cols_half = Npad / 2;   // a multiple of 8
+    const int c_lo = chalf * cols_half;
+    const uint32_t tRow = taddr + ((uint32_t)(quarter * 32) << 16);
+    for (int t = 0; t < ntiles; ++t) {
+      const int j0 = begin + t * kTile;
+      if (!mbar_wait(&s_full[t & 1], (uint32_t)(t >> 1) & 1u, kWaitNs)) s_abort = 1;
+      fence_after_sync();
+      // this thread: slot slot_lane, rows [c_lo, c_lo + cols_half), in row order
+      float acc[4] = {0.f, 0.f, 0.f, 0.f};
+      const uint32_t tS = tRow + (t & 1) * 256 + c_lo;
+#pragma unroll 1
+      for (int c0 = 0; c0 < cols_half; c0 += 64) {
+        float sv[64];
+        tmem_ld32(tS + c0, sv);
+        tmem_ld32(tS + c0 + 32, sv + 32);
+        tmem_ld_wait();
+        const int lim = cols_half - c0;
+#pragma unroll
+        for (int i = 0; i < 64; i += 4) {
+          const float4 b4 = *reinterpret_cast<const float4*>(&sB[(c_lo + c0 + i) & (kMaxRows - 1)]);
+          if (i < lim) {   // lim is a multiple of 8
+            acc[0] += ex2(fmaf(sv[i], c2, -b4.x));
+            acc[1] += ex2(fmaf(sv[i + 1], c2, -b4.y));
+            acc[2] += ex2(fmaf(sv[i + 2], c2, -b4.z));
+            acc[3] += ex2(fmaf(sv[i + 3], c2, -b4.w));
+          }
+        }
+      }
+      sHalf[chalf][slot_lane] = (acc[0] + acc[1]) + (acc[2] + acc[3]);
+      fence_before_sync();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&s_free[t & 1]);
+      sum_sync();
+      if (threadIdx.x < kTile) {
+        const int j = j0 + threadIdx.x;
+        const bool live = j < end && kv_live(A.kv, H, b, h, j);
+        const float a = live ? (sHalf[0][threadIdx.x] + sHalf[1][threadIdx.x]) * inv_rows : 0.f;
+        if (j < end) A.mass[(int64_t)b * A.sm0 + (int64_t)h * A.sm1 + j] = a;
+        sA[threadIdx.x] = a;
+      }
+      if (centre && !mbar_wait(&vfull[t & 1], (uint32_t)(t >> 1) & 1u, kWaitNs)) s_abort = 1;
+      if (threadIdx.x == 0) sDecide = s_abort;
+      sum_sync();
+      if (sDecide) break;   // every sum warp leaves at the same tile
+      if (centre) {
+        // sum_j a_j v_j over this thread's key quarter, channels 2cp, 2cp+1
+        const uint8_t* sV = sSlot + (2 + (t & 1)) * kTileBytes;
+#pragma unroll 4
+        for (int jj = 0; jj < kTile / 4; ++jj) {
+          const int j = kq * (kTile / 4) + jj;
+          const float a = sA[j];
+          const float2 v = __bfloat1622float2(
+              *reinterpret_cast<const __nv_bfloat162*>(sV + chunk_off(j, cp >> 2) + (cp & 3) * 4));
+          cacc0 = fmaf(a, v.x, cacc0);
+          cacc1 = fmaf(a, v.y, cacc1);
+          asum += a;
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&v_free[t & 1]);
+      }
+    }
+  }
+  // join: the producer drained, the sum warps are out of their loop
+  fence_before_sync();
+  __syncthreads();
+  fence_after_sync();
+  if (warp == 0) tmem_dealloc(taddr, kTmemCols);
+  const bool aborted = s_abort != 0;
+  if (aborted && threadIdx.x == 0) atomicExch(A.err, 1);
+  if (!centre) return;
+
+  // per-CTA centre partial (key quarters summed in order); the last CTA of the head
+  // reduces the partials in CTA order and publishes c by advancing the generation
+  if (sum_warp) {
+    sRed[kq][2 * cp] = cacc0;
+    sRed[kq][2 * cp + 1] = cacc1;
+    if (cp == 0) sAsum[kq] = asum;
+  }
+  __syncthreads();
+  float* mine = A.part + ((int64_t)bh * gridDim.x + blockIdx.x) * (kD + 1);
+  if (threadIdx.x < kD)
+    mine[threadIdx.x] = aborted ? NAN : ((sRed[0][threadIdx.x] + sRed[1][threadIdx.x]) + sRed[2][threadIdx.x]) + sRed[3][threadIdx.x];
+  if (threadIdx.x == 0) mine[kD] = ((sAsum[0] + sAsum[1]) + sAsum[2]) + sAsum[3];
+  __threadfence();
+  __syncthreads();
+  if (threadIdx.x == 0) sLast = atomicAdd(&A.sync[bh].x, 1u) == gridDim.x - 1 ? 1 : 0;
+  __syncthreads();
+  if (sLast) {
+    __threadfence();
+    if (threadIdx.x <= kD) {
+      const float* base = A.part + (int64_t)bh * gridDim.x * (kD + 1) + threadIdx.x;
+      float tot = 0.f;
+      for (unsigned t0 = 0; t0 < gridDim.x; t0 += 16) {
+        float v[16];
+#pragma unroll
+        for (int i = 0; i < 16; ++i) v[i] = t0 + i < gridDim.x ? __ldcg(base + (int64_t)(t0 + i) * (kD + 1)) : 0.f;
+#pragma unroll
+        for (int i = 0; i < 16; ++i) tot += v[i];   // CTA order
+      }
+      sTot[threadIdx.x] = tot;
+    }
+    __syncthreads();
+    if (threadIdx.x < kD) A.centre[(int64_t)bh * kD + threadIdx.x] = sTot[threadIdx.x] / fmaxf(sTot[kD], 1e-12f);
+    if (threadIdx.x == 0) A.sync[bh].x = 0u;
+    __threadfence();
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      __threadfence();
+      atomicAdd(&A.sync[bh].y, 1u);
+    }
+  }
+  if (A.score == nullptr) return;
+
+  // ---- phase 2: a_j ||v_j - c|| for this CTA's slots (cooperative launch: every CTA of
+  // the head is resident, so the generation advances)
+  if (!sLast && threadIdx.x == 0) {
+    const uint64_t t0 = global_ns();
+    while (ld_acquire_u32(&A.sync[bh].y) == gen0) {
+      if (global_ns() - t0 > kWaitNs) {
+        s_wait_ok = 0;
+        atomicExch(A.err, 1);
+        break;
+      }
+      __nanosleep(256);
+    }
+  }
+  __syncthreads();
+  const bool ok_c = s_wait_ok != 0 && !aborted;
+  if (!sum_warp) {
+    if (lane == 0 && ok_c) {
+      // the CTA's V tiles again, newest first, through all four slots
+      const uint64_t pol = tma::policy_evict_first();
+      int u = 0;
+      for (; u < ntiles; ++u) {
+        const int slot = u % kSlots;
+        if (u >= kSlots && !mbar_wait(&wfree[slot], (uint32_t)((u / kSlots) - 1) & 1u, kWaitNs)) break;
+        tile_load(&A.vmap, b, h, begin + (ntiles - 1 - u) * kTile, sSlot + slot * kTileBytes, &wfull[slot], pol);
+      }
+      // drain (bounded): the last load of every slot
+      for (int uu = max(0, u - kSlots); uu < u; ++uu)
+        mbar_wait(&wfull[uu % kSlots], (uint32_t)(uu / kSlots) & 1u, 20000000ull);
+    }
+    __syncwarp();
+  } else {
+    const int grp = threadIdx.x >> 4, l16 = threadIdx.x & 15;
+    float* sc = A.score + (int64_t)b * A.ss0 + (int64_t)h * A.ss1;
+    if (!ok_c) {
+      for (int j = begin + threadIdx.x; j < end; j += kSumThreads) sc[j] = NAN;
+    } else {
+      float cc[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) cc[i] = __ldcg(A.centre + (int64_t)bh * kD + 8 * l16 + i);
+      const float* ms = A.mass + (int64_t)b * A.sm0 + (int64_t)h * A.sm1;
+      for (int u = 0; u < ntiles; ++u) {
+        const int slot = u % kSlots;
+        const int j0 = begin + (ntiles - 1 - u) * kTile;
+        if (!mbar_wait(&wfull[slot], (uint32_t)(u / kSlots) & 1u, kWaitNs)) {
+          atomicExch(A.err, 1);
+          for (int j = j0 + threadIdx.x; j < min(end, j0 + kTile); j += kSumThreads) sc[j] = NAN;
+          break;
+        }
+        const uint8_t* sV = sSlot + slot * kTileBytes;
+#pragma unroll 2
+        for (int jj = grp; jj < kTile; jj += kSumThreads / 16) {
+          const int j = j0 + jj;
+          float f[8];
+          bf16x8_to_float(*reinterpret_cast<const uint4*>(sV + chunk_off(jj, l16)), f);
+          float s2 = 0.f;
+#pragma unroll
+          for (int i = 0; i < 8; ++i) {
+            const float x = f[i] - cc[i];
+            s2 = fmaf(x, x, s2);
+          }
+#pragma unroll
+          for (int o = 8; o > 0; o >>= 1) s2 += __shfl_xor_sync(0xffffffffu, s2, o);
+          if (l16 == 0 && j < end) sc[j] = kv_live(A.kv, H, b, h, j) ? __ldcg(ms + j) * sqrtf(s2) : 0.f;
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&wfree[slot]);
+      }
+    }
+  }
+}
+
+bool tma_map_rows(CUtensorMap* map, const void* base, int B, int H, int n, const int64_t s[3]) {
+  // bf16 [B][H][n][128] with element strides s (b, h, row); box: 64 channels x 128 rows
+  const uint64_t dims[4] = {128, (uint64_t)n, (uint64_t)H, (uint64_t)B};
+  const uint64_t strides[3] = {(uint64_t)s[2] * 2, (uint64_t)s[1] * 2, (uint64_t)s[0] * 2};
+  const uint32_t box[4] = {64, (uint32_t)kTile, 1, 1};
+  return make_tma_map_bf16_4d(map, base, dims, strides, box);
+}
+
+}  // namespace
+
+int launch_prefix_mass_fa(const ma_rows& q, const ma_kv& kv, int H, const int32_t* q_rows, int T2, const float* m_p,
+                          const float* l_p, float scale, float* mass, int64_t sm0, int64_t sm1, float* score,
+                          int64_t ss0, int64_t ss1, const ValueWs& w, bool want_centre, bool* fused, cudaStream_t st) {
+  *fused = false;
+  const int n = kv.nf;
+  const int BH = q.B * H;
+  const int G = q.Hq / H;
+  if (!(kv.layout == MA_KV_DENSE && kv.dtype == MA_BF16 && !kv.pages && kv.nq == 0 && q.dtype == MA_BF16 &&
+        q.D == kD && G * T2 <= kMaxRows && n > 0))
+    return MA_ERR_UNSUPPORTED;
+  Args A;
+  memset(&A, 0, sizeof(A));
+  if (!tma_map_rows(&A.kmap, kv.kf, q.B, H, n, kv.skf) || !tma_map_rows(&A.vmap, kv.vf, q.B, H, n, kv.svf))
+    return MA_ERR_UNSUPPORTED;
+  A.q = q;
+  A.kv = kv;
+  A.q_rows = q_rows;
+  A.m_p = m_p;
+  A.l_p = l_p;
+  A.mass = mass;
+  A.sm0 = sm0;
+  A.sm1 = sm1;
+  A.score = nullptr;
+  A.ss0 = ss0;
+  A.ss1 = ss1;
+  A.part = want_centre ? w.part : nullptr;
+  A.sync = w.sync;
+  A.centre = want_centre ? w.centre : nullptr;
+  A.err = w.err;
+  A.scale = scale;
+  A.H = H;
+  A.T2 = T2;
+  A.want_centre = want_centre ? 1 : 0;
+  // one wave of CTAs over the heads, whole tiles each
+  const int sms = device_sm_count();
+  int per_head = sms / (BH > 0 ? BH : 1);
+  if (per_head < 1) per_head = 1;
+  int spc = (n + per_head - 1) / per_head;
+  spc = ((spc + kTile - 1) / kTile) * kTile;
+  A.slots_per_cta = spc;
+  dim3 grid((n + spc - 1) / spc, BH);
+  if (cudaFuncSetAttribute(prefix_mass_fa, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes) != cudaSuccess)
+    return MA_ERR_CUDA;
+  if (score != nullptr && want_centre) {
+    // the fused score needs every CTA resident at once: a cooperative launch that fits
+    int dev = 0, coop = 0, per_sm = 0;
+    if (cudaGetDevice(&dev) == cudaSuccess &&
+        cudaDeviceGetAttribute(&coop, cudaDevAttrCooperativeLaunch, dev) == cudaSuccess && coop &&
+        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, prefix_mass_fa, kThreads, kSmemBytes) == cudaSuccess &&
+        (long long)grid.x * grid.y <= (long long)per_sm * sms) {
+      Args Ac = A;
+      Ac.score = score;
+      cudaLaunchConfig_t cfg = {};
+      cfg.gridDim = grid;
+      cfg.blockDim = dim3(kThreads);
+      cfg.dynamicSmemBytes = kSmemBytes;
+      cfg.stream = st;
+      cudaLaunchAttribute attr[1];
+      attr[0].id = cudaLaunchAttributeCooperative;
+      attr[0].val.cooperative = 1;
+      cfg.attrs = attr;
+      cfg.numAttrs = 1;
+      if (cudaLaunchKernelEx(&cfg, prefix_mass_fa, Ac) == cudaSuccess) {
+        *fused = true;
+        return MA_OK;
+      }
+      (void)cudaGetLastError();
+    }
+  }
+  return launch_pdl(prefix_mass_fa, grid, dim3(kThreads), kSmemBytes, st, A) == cudaSuccess ? MA_OK : MA_ERR_CUDA;
+}
+
+}  // namespace ma

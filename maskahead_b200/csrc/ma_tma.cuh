@@ -33,6 +33,27 @@ __device__ __forceinline__ void load_4d(void* smem_dst, const CUtensorMap* map, 
       : "memory");
 }
 
+// The same load with an L2 cache policy (createpolicy): evict_last keeps the box in L2
+// for a second pass over it, evict_first lets a read-once stream leave early.
+__device__ __forceinline__ uint64_t policy_evict_last() {
+  uint64_t p;
+  asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;\n" : "=l"(p));
+  return p;
+}
+__device__ __forceinline__ uint64_t policy_evict_first() {
+  uint64_t p;
+  asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;\n" : "=l"(p));
+  return p;
+}
+__device__ __forceinline__ void load_4d_hint(void* smem_dst, const CUtensorMap* map, int c0, int c1, int c2, int c3,
+                                             uint64_t* mbar, uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], "
+      "[%1, {%3, %4, %5, %6}], [%2], %7;\n" ::"r"(tc::smem_addr(smem_dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(tc::smem_addr(mbar)), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "l"(policy)
+      : "memory");
+}
+
 // Shared -> global tensor store of one box (never at a negative coordinate); completion
 // is tracked per thread with bulk groups.
 __device__ __forceinline__ void store_2d(const CUtensorMap* map, int c0, int c1, const void* smem_src) {

@@ -1,0 +1,87 @@
+"""GPU parity of the TMA-pipelined prefix-mass / value-score kernel (dense bf16 caches)
+against the CPU oracle and against the general (cp.async-staged) kernel.
+
+Bars: mass a_j to fp32 rounding (rtol 2e-5 against the oracle's fp32 restatement, whose
+statistics M_p, L_p come from the same device attention call); the value score
+a_j ||v_j - c|| to rtol 5e-5. The two device kernels sum in different orders, so they
+are compared at the same bars. Sizes cover several tiles per CTA, a ragged last tile,
+selection-row counts that pad the MMA's N (1, 32, 224 rows) and a live-slot mask.
+"""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+import oracle
+
+pytestmark = pytest.mark.gpu
+
+DEV = "cuda"
+
+
+def _lib():
+    from maskahead_b200._lib import load_library
+
+    return load_library()
+
+
+def _scores(which, q, pre, st, rows):
+    from maskahead_b200.kernels import prefix_scores
+
+    prev = _lib().ma_set_attention_kernel(which)
+    try:
+        mass, score = prefix_scores(q, pre, st, rows, value=True)
+        torch.cuda.synchronize()
+    finally:
+        _lib().ma_set_attention_kernel(prev)
+    return mass.cpu(), score.cpu()
+
+
+@pytest.mark.parametrize("B,Hq,H,T,n,rows,masked", [
+    (1, 28, 4, 32, 8192, list(range(32)), False),     # cfg2 shape: R2 = 224
+    (1, 8, 2, 32, 40000, list(range(0, 32, 4)), False),   # several tiles per CTA, R2 = 32
+    (2, 4, 4, 16, 3001, [5], True),                  # one selection row, ragged tail, mask
+])
+def test_mass_fa_matches_oracle_and_general_kernel(B, Hq, H, T, n, rows, masked):
+    from maskahead_b200.kernels import splitk_attention
+    from maskahead_b200.layouts import Prefix
+
+    gen = torch.Generator().manual_seed(n + Hq)
+    D = 128
+    q = torch.randn(B, Hq, T, D, generator=gen).to(torch.bfloat16)
+    k = torch.randn(B, H, n, D, generator=gen).to(torch.bfloat16)
+    v = torch.randn(B, H, n, D, generator=gen).to(torch.bfloat16)
+    live = (torch.rand(B, H, n, generator=gen) > 0.2) if masked else None
+    qd, kd, vd = q.to(DEV), k.to(DEV), v.to(DEV)
+    pre = Prefix.dense(kd, vd, mask=None if live is None else live.to(DEV))
+    _, st = splitk_attention(qd, pre, None, None, want_prefix=True)
+    torch.cuda.synchronize()
+    rows_t = torch.tensor(rows, dtype=torch.int32, device=DEV)
+    mass0, score0 = _scores(0, qd, pre, st, rows_t)
+    mass1, score1 = _scores(1, qd, pre, st, rows_t)
+    want_mass = oracle.prefix_mass(q, k, st[0].cpu(), st[1].cpu(), rows, live_mask=live)
+    np.testing.assert_allclose(mass0.numpy(), want_mass.numpy(), rtol=2e-5, atol=1e-9)
+    np.testing.assert_allclose(mass1.numpy(), want_mass.numpy(), rtol=2e-5, atol=1e-9)
+    want_score = oracle.value_score(want_mass, v)
+    np.testing.assert_allclose(score0.numpy(), want_score.numpy(), rtol=5e-5, atol=1e-9)
+    np.testing.assert_allclose(score0.numpy(), score1.numpy(), rtol=5e-5, atol=1e-9)
+
+
+def test_mass_fa_repeated_calls_are_identical():
+    """The centre counters and generations reset between calls: same inputs, same bits."""
+    from maskahead_b200.kernels import prefix_scores, splitk_attention
+    from maskahead_b200.layouts import Prefix
+
+    gen = torch.Generator().manual_seed(11)
+    q = torch.randn(1, 28, 32, 128, generator=gen).to(torch.bfloat16).to(DEV)
+    k = torch.randn(1, 4, 20000, 128, generator=gen).to(torch.bfloat16).to(DEV)
+    v = torch.randn(1, 4, 20000, 128, generator=gen).to(torch.bfloat16).to(DEV)
+    pre = Prefix.dense(k, v)
+    _, st = splitk_attention(q, pre, None, None, want_prefix=True)
+    rows = torch.arange(32, dtype=torch.int32, device=DEV)
+    m0, s0 = prefix_scores(q, pre, st, rows, value=True)
+    for _ in range(3):
+        m1, s1 = prefix_scores(q, pre, st, rows, value=True)
+        assert torch.equal(m0, m1) and torch.equal(s0, s1)
