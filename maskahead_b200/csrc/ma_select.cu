@@ -298,6 +298,181 @@ select_topk_reg(const float* __restrict__ score, int H, int n, int64_t ss0, int6
   }
 }
 
+// Cluster variant for rows longer than one CTA's registers hold: a cluster of kSelCluster
+// CTAs per (b, h), CTA rank r owning the contiguous chunk [r*chunk, r*chunk + chunk) with
+// PER keys per thread in registers. Each radix pass builds the CTA's 256-bin histogram,
+// adds it into rank 0's shared memory (distributed shared memory atomics; one buffer per
+// pass, zeroed before the first cluster barrier), and after a cluster barrier every CTA
+// reads the summed histogram and picks the same digit. The emission ranks the CTAs' (larger,
+// ties) counts in rank order through rank 0 as well, so the read set stays ascending and
+// ties go to the lower slots. Cluster barriers wait only on the cluster's own CTAs, which
+// the hardware co-schedules; every CTA takes the same barriers in the same order.
+constexpr int kSelCluster = 8;
+
+__device__ __forceinline__ uint32_t cluster_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;\n" : "=r"(r));
+  return r;
+}
+__device__ __forceinline__ void cluster_sync() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\nbarrier.cluster.wait.acquire.aligned;\n" ::: "memory");
+}
+// address of this shared variable in CTA `rank` of the cluster
+__device__ __forceinline__ uint32_t peer_addr(const void* p, uint32_t rank) {
+  uint32_t a;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;\n" : "=r"(a) : "r"(static_cast<uint32_t>(__cvta_generic_to_shared(p))), "r"(rank));
+  return a;
+}
+__device__ __forceinline__ void peer_add(uint32_t addr, uint32_t v) {
+  asm volatile("red.shared::cluster.add.u32 [%0], %1;\n" ::"r"(addr), "r"(v) : "memory");
+}
+__device__ __forceinline__ uint32_t peer_ld(uint32_t addr) {
+  uint32_t v;
+  asm volatile("ld.shared::cluster.u32 %0, [%1];\n" : "=r"(v) : "r"(addr) : "memory");
+  return v;
+}
+__device__ __forceinline__ void peer_st(uint32_t addr, uint32_t v) {
+  asm volatile("st.shared::cluster.u32 [%0], %1;\n" ::"r"(addr), "r"(v) : "memory");
+}
+
+template <int PER>
+__global__ void __launch_bounds__(kSelThreads)
+select_topk_cluster(const float* __restrict__ score, int H, int n, int64_t ss0, int64_t ss1,
+                    const uint8_t* __restrict__ mask, const int32_t* __restrict__ lens, int k,
+                    int64_t* __restrict__ indices, float* __restrict__ values, int64_t si0, int64_t si1) {
+  __shared__ unsigned sHist[256];                  // this CTA's histogram
+  __shared__ unsigned sGlob[4][256];               // rank 0: the cluster's, one per pass
+  __shared__ unsigned sCnt[kSelCluster];           // rank 0: (ties << 16 | larger) per rank
+  __shared__ int sSel[2][2];
+  __shared__ int sWarp[33];
+  const uint32_t rank = cluster_rank();
+  for (int i = threadIdx.x; i < 4 * 256; i += blockDim.x) (&sGlob[0][0])[i] = 0u;
+  cluster_sync();   // every CTA of the cluster started, rank 0's buffers are zero
+  pdl_wait();
+  const int bh = blockIdx.y;
+  const int b = bh / H, h = bh - (bh / H) * H;
+  const float* s = score + (int64_t)b * ss0 + (int64_t)h * ss1;
+  const uint8_t* m = mask ? mask + (int64_t)bh * n : nullptr;
+  const int lane = threadIdx.x & 31;
+  const int chunk = kSelThreads * PER;
+  const int j0 = (int)rank * chunk + threadIdx.x * PER;
+  uint32_t key[PER];
+  const bool vec = ((reinterpret_cast<uintptr_t>(s) & 15) == 0) && j0 + PER <= n;
+  if (vec) {
+#pragma unroll
+    for (int c = 0; c < PER / 4; ++c) {
+      const float4 v = __ldcg(reinterpret_cast<const float4*>(s + j0) + c);
+      key[4 * c] = order_key(v.x);
+      key[4 * c + 1] = order_key(v.y);
+      key[4 * c + 2] = order_key(v.z);
+      key[4 * c + 3] = order_key(v.w);
+    }
+  } else {
+#pragma unroll
+    for (int i = 0; i < PER; ++i) key[i] = j0 + i < n ? order_key(__ldcg(s + j0 + i)) : 0u;
+  }
+  if (m) {
+#pragma unroll
+    for (int i = 0; i < PER; ++i)
+      if (j0 + i < n && m[j0 + i] == 0) key[i] = 0u;   // dead slots rank below every live one
+  }
+  if (lens) {
+    const int len = lens[b];
+#pragma unroll
+    for (int i = 0; i < PER; ++i)
+      if (j0 + i >= len) key[i] = 0u;
+  }
+  const int nv = max(0, min(PER, n - j0));   // this thread's slots inside the row
+
+  uint32_t prefix = 0, pmask = 0;
+  int kk = k;
+#pragma unroll 1
+  for (int pass = 0; pass < 4; ++pass) {
+    const int shift = 24 - 8 * pass;
+    if (threadIdx.x < 256) sHist[threadIdx.x] = 0u;
+    __syncthreads();
+#pragma unroll
+    for (int i = 0; i < PER; ++i) {
+      const uint32_t x = key[i];
+      const bool take = i < nv && (x & pmask) == prefix;
+      const uint32_t bin = take ? ((x >> shift) & 255u) : 256u;
+      const uint32_t b0 = __shfl_sync(0xffffffffu, bin, 0);
+      const unsigned same = __ballot_sync(0xffffffffu, bin == b0);
+      if (lane == 0 && b0 < 256u) atomicAdd(&sHist[b0], (unsigned)__popc(same));
+      if (take && bin != b0) atomicAdd(&sHist[bin], 1u);
+    }
+    __syncthreads();
+    if (threadIdx.x < 256 && sHist[threadIdx.x] != 0u)
+      peer_add(peer_addr(&sGlob[pass][threadIdx.x], 0), sHist[threadIdx.x]);
+    cluster_sync();   // the cluster's histogram for this pass is complete in rank 0
+    if (threadIdx.x < 32) {
+      // lane l owns digits 255-8l .. 248-8l (descending order)
+      int c[8];
+      int loc = 0;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        c[i] = (int)peer_ld(peer_addr(&sGlob[pass][255 - (lane * 8 + i)], 0));
+        loc += c[i];
+      }
+      int incl = loc;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int y = __shfl_up_sync(0xffffffffu, incl, o);
+        if (lane >= o) incl += y;
+      }
+      int cum = incl - loc;  // keys with a larger digit than this lane's first digit
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        if (cum < kk && cum + c[i] >= kk) {
+          sSel[pass & 1][0] = 255 - (lane * 8 + i);
+          sSel[pass & 1][1] = cum;
+        }
+        cum += c[i];
+      }
+    }
+    __syncthreads();
+    prefix |= (uint32_t)sSel[pass & 1][0] << shift;
+    pmask |= 255u << shift;
+    kk -= sSel[pass & 1][1];
+  }
+  // emission in slot order: keys above the k-th plus the first kk ties, ranks in order
+  int gt = 0, eq = 0;
+#pragma unroll
+  for (int i = 0; i < PER; ++i) {
+    gt += (i < nv && key[i] > prefix) ? 1 : 0;
+    eq += (i < nv && key[i] == prefix) ? 1 : 0;
+  }
+  int tot;
+  const int before = block_exclusive_scan((eq << 16) | gt, sWarp, tot);
+  if (threadIdx.x == 0) peer_st(peer_addr(&sCnt[rank], 0), (uint32_t)tot);
+  cluster_sync();   // every rank's counts are in rank 0
+  int gt_r = 0, eq_r = 0;   // larger keys and ties in the lower ranks
+  for (uint32_t rr = 0; rr < rank; ++rr) {
+    const uint32_t c = peer_ld(peer_addr(&sCnt[rr], 0));
+    gt_r += (int)(c & 0xFFFFu);
+    eq_r += (int)(c >> 16);
+  }
+  const int kk_cta = max(0, min(tot >> 16, kk - eq_r));   // ties this CTA takes
+  const int gt_before = before & 0xFFFF, eq_before = before >> 16;
+  const int take = max(0, min(eq, kk_cta - eq_before));
+  int off = gt_r + min(eq_r, kk) + gt_before + min(eq_before, kk_cta);
+  int taken = 0;
+  int64_t* oi = indices + (int64_t)b * si0 + (int64_t)h * si1;
+  float* ov = values ? values + (int64_t)b * si0 + (int64_t)h * si1 : nullptr;
+#pragma unroll
+  for (int i = 0; i < PER; ++i) {
+    const uint32_t x = key[i];
+    const bool tie = x == prefix;
+    if (i < nv && (x > prefix || (tie && taken < take))) {
+      taken += tie ? 1 : 0;
+      oi[off] = j0 + i;
+      if (ov) ov[off] = s[j0 + i];
+      ++off;
+    }
+  }
+  cluster_sync();   // no CTA leaves while another may still read rank 0's shared memory
+}
+
 // Lookahead survivors of one lane (eviction.py:364-409): recent window by position,
 // sinks at +inf, window excluded from the score contest, union ordered by position.
 __global__ void __launch_bounds__(kSelThreads)
@@ -424,6 +599,27 @@ int launch_select_topk(const float* score, int B, int H, int n, int64_t ss0, int
     else if (n <= 1024 * 8) go(select_topk_reg<8>);
     else go(select_topk_reg<16>);
     return cudaGetLastError() == cudaSuccess ? MA_OK : MA_ERR_CUDA;
+  }
+  if (n <= kSelCluster * 1024 * 16) {  // keys in the registers of a cluster of CTAs
+    auto go = [&](auto kernel) -> int {
+      cudaLaunchConfig_t cfg = {};
+      cfg.gridDim = dim3(kSelCluster, B * H);
+      cfg.blockDim = dim3(kSelThreads);
+      cfg.dynamicSmemBytes = 0;
+      cfg.stream = st;
+      cudaLaunchAttribute attr[1];
+      attr[0].id = cudaLaunchAttributeClusterDimension;
+      attr[0].val.clusterDim.x = kSelCluster;
+      attr[0].val.clusterDim.y = 1;
+      attr[0].val.clusterDim.z = 1;
+      cfg.attrs = attr;
+      cfg.numAttrs = 1;
+      return cudaLaunchKernelEx(&cfg, kernel, score, H, n, ss0, ss1, mask, lens, k, indices, values, si0, si1) ==
+                     cudaSuccess ? MA_OK : MA_ERR_CUDA;
+    };
+    if (n <= kSelCluster * 1024 * 4) return go(select_topk_cluster<4>);
+    if (n <= kSelCluster * 1024 * 8) return go(select_topk_cluster<8>);
+    return go(select_topk_cluster<16>);
   }
   const int staged = n <= kSelSmemKeys ? 1 : 0;
   const size_t smem = staged ? (size_t)n * sizeof(uint32_t) : 0;

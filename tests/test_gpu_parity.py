@@ -121,7 +121,8 @@ def test_retention_matches_reference():
     np.testing.assert_array_equal(keep.cpu().numpy(), g["keep"])
 
 
-@pytest.mark.parametrize("n,k", [(1, 1), (7, 3), (100, 100), (1000, 17), (5000, 1024), (70000, 4096)])
+@pytest.mark.parametrize("n,k", [(1, 1), (7, 3), (100, 100), (1000, 17), (5000, 1024), (20000, 3000),
+                                 (40000, 4096), (65536, 4096), (70000, 4096), (131072, 8192), (140000, 512)])
 def test_select_topk_bit_exact_with_ties(n, k):
     from maskahead_b200.kernels import select_topk_indices
 
