@@ -56,6 +56,7 @@ constexpr uint32_t kColS = 0, kColO = 256;
 constexpr int kOutBox = 32 * 128;
 constexpr uint64_t kMergeWaitNs = 200000000ull;
 constexpr uint64_t kStallNs = 500000000ull;        // MMA issuer: longest time without progress
+constexpr unsigned kIdleNs = 64;                   // MMA issuer back-off when nothing was ready
 constexpr uint64_t kWaitNs = 500000000ull;
 
 struct __align__(64) Args {
@@ -76,29 +77,8 @@ struct __align__(64) Args {
   FusedMerge fm;
 };
 
-__device__ __forceinline__ void mbar_arrive(uint64_t* mbar) {
-  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];\n" ::"r"(smem_addr(mbar)) : "memory");
-}
-// non-blocking test of a phase parity
-__device__ __forceinline__ bool mbar_test(uint64_t* mbar, uint32_t phase) {
-  uint32_t ok;
-  asm volatile(
-      "{\n.reg .pred p;\nmbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\nselp.u32 %0, 1, 0, p;\n}\n"
-      : "=r"(ok)
-      : "r"(smem_addr(mbar)), "r"(phase)
-      : "memory");
-  return ok != 0;
-}
 __device__ __forceinline__ void prefetch_map(const CUtensorMap* m) {
   asm volatile("prefetch.tensormap [%0];\n" ::"l"(reinterpret_cast<uint64_t>(m)) : "memory");
-}
-// tensor-memory store of 16 consecutive 32-bit columns of this warp's 32 lanes
-__device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t* r) {
-  asm volatile(
-      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};\n" ::"r"(
-          taddr),
-      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]), "r"(r[9]),
-      "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15]));
 }
 // D[tmem] (+)= A[tmem] * B[smem]: the A operand (M x 16, bf16 pairs per column) in TMEM
 __device__ __forceinline__ void mma_bf16_ta(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc,
@@ -107,33 +87,6 @@ __device__ __forceinline__ void mma_bf16_ta(uint32_t d_tmem, uint32_t a_tmem, ui
       "{\n.reg .pred p;\nsetp.ne.b32 p, %4, 0;\n"
       "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n}\n" ::"r"(d_tmem),
       "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate ? 1 : 0));
-}
-// packed fp32 pairs (sm_100): one instruction for two lanes of work
-__device__ __forceinline__ uint64_t f2_bits(float2 a) {
-  uint64_t u;
-  asm("mov.b64 %0, {%1, %2};" : "=l"(u) : "f"(a.x), "f"(a.y));
-  return u;
-}
-__device__ __forceinline__ float2 bits_f2(uint64_t u) {
-  float2 a;
-  asm("mov.b64 {%0, %1}, %2;" : "=f"(a.x), "=f"(a.y) : "l"(u));
-  return a;
-}
-__device__ __forceinline__ float2 ffma2(float2 a, float2 b, float2 c) {
-  uint64_t d;
-  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(f2_bits(a)), "l"(f2_bits(b)), "l"(f2_bits(c)));
-  return bits_f2(d);
-}
-__device__ __forceinline__ float2 fadd2(float2 a, float2 b) {
-  uint64_t d;
-  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(f2_bits(a)), "l"(f2_bits(b)));
-  return bits_f2(d);
-}
-// three-input maximum (sm_100)
-__device__ __forceinline__ float max3f(float a, float b, float c) {
-  float d;
-  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
-  return d;
 }
 __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
   __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
@@ -319,7 +272,8 @@ __global__ void __launch_bounds__(kThreads, 1) attn_partial_fa(const __grid_cons
         if (progress) {
           spins = 0;
           armed = false;
-        } else if (++spins == 256) {   // idle: bound the time without progress
+        } else if (__nanosleep(kIdleNs), ++spins == 256) {   // idle: back off (the issue slots
+          // of this sub-partition belong to two compute warps), bound the time without progress
           spins = 0;
           const uint64_t now = global_ns();
           if (!armed) {

@@ -41,12 +41,14 @@ constexpr int kMaxRows = 256;                // selection rows (N of the MMA)
 constexpr int kQBytes = kMaxRows * kD * 2;   // 64 KB
 constexpr int kBlock = kTile * 128;          // one 64-channel box of a tile: 16 KB
 constexpr int kTileBytes = 2 * kBlock;       // a K or V tile: 32 KB
-constexpr int kSlots = 4;                    // phase 1: K in slots 0-1, V in 2-3; phase 2: V in all
-constexpr int kSmemBytes = 1024 + kQBytes + kSlots * kTileBytes;
+constexpr int kMaxSlots = 6;                 // tile slots (phase 1: K ring, then V ring; phase 2: V in all)
+constexpr int kSmemLimit = 227 * 1024;       // dynamic + static shared memory of one CTA
+constexpr int kStaticSmem = 8 * 1024;        // bound on this kernel's static shared memory
 constexpr uint32_t kTmemCols = 512;          // two S^T buffers of up to 256 columns
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr uint64_t kWaitNs = 200000000ull;
 constexpr uint64_t kStallNs = 500000000ull;
+constexpr unsigned kIdleNs = 64;                   // producer back-off when nothing was ready
 
 struct __align__(64) Args {
   CUtensorMap kmap, vmap;   // K/V [B][H][n][D], boxes of 64 channels x 128 slots
@@ -65,20 +67,9 @@ struct __align__(64) Args {
   int* err;
   float scale;
   int H, T2, slots_per_cta, want_centre;
+  int nK, nV;               // K ring and V ring slots (phase 2 streams V through nK + nV)
 };
 
-__device__ __forceinline__ void mbar_arrive(uint64_t* mbar) {
-  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];\n" ::"r"(smem_addr(mbar)) : "memory");
-}
-__device__ __forceinline__ bool mbar_test(uint64_t* mbar, uint32_t phase) {
-  uint32_t ok;
-  asm volatile(
-      "{\n.reg .pred p;\nmbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\nselp.u32 %0, 1, 0, p;\n}\n"
-      : "=r"(ok)
-      : "r"(smem_addr(mbar)), "r"(phase)
-      : "memory");
-  return ok != 0;
-}
 __device__ __forceinline__ void sum_sync() { asm volatile("bar.sync 1, %0;\n" ::"r"(kSumThreads) : "memory"); }
 
 __device__ __forceinline__ void tile_load(const CUtensorMap* map, int b, int h, int j0, uint8_t* dst, uint64_t* bar,
@@ -98,17 +89,14 @@ __global__ void __launch_bounds__(kThreads, 1) prefix_mass_fa(const __grid_const
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sQ = smem;                      // K-major [2 d blocks][Npad rows][128 B]
-  uint8_t* sSlot = sQ + kQBytes;           // 4 tile slots
-  __shared__ __align__(16) float sB[kMaxRows];   // per selection row: B_r (+inf: no contribution)
+  __shared__ __align__(16) float sNB[kMaxRows];  // per selection row: -B_r (-inf: no contribution)
   __shared__ int sRowT[kMaxRows];                // block position of selection row r (-1: none)
   __shared__ float sHalf[2][kTile];
   __shared__ __align__(16) float sA[kTile];
-  __shared__ float sRed[4][kD];
   __shared__ float sTot[kD + 1];
-  __shared__ float sAsum[4];
   __shared__ uint32_t s_taddr;
-  __shared__ __align__(8) uint64_t kfull[2], vfull[2], s_full[2], s_free[2], v_free[2], wfull[kSlots],
-      wfree[kSlots], mbar_fin;
+  __shared__ __align__(8) uint64_t kfull[kMaxSlots], vfull[kMaxSlots], s_full[2], s_free[2], v_free[kMaxSlots],
+      wfull[kMaxSlots], wfree[kMaxSlots], mbar_fin;
   __shared__ int s_abort, s_wait_ok, sLast;
 
   const int n = A.kv.nf;
@@ -119,6 +107,8 @@ __global__ void __launch_bounds__(kThreads, 1) prefix_mass_fa(const __grid_const
   const int T = A.q.T;
   const int R2 = G * A.T2;
   const int Npad = (R2 + 15) & ~15;
+  uint8_t* sSlot = sQ + Npad * 256;        // nK + nV tile slots (Npad * 256 is a multiple of 4 KB)
+  const int nK = A.nK, nV = A.nV, nS = A.nK + A.nV;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const bool sum_warp = warp < kSumWarps;
   const int quarter = warp & 3, chalf = (warp >> 2) & 1;
@@ -137,13 +127,13 @@ __global__ void __launch_bounds__(kThreads, 1) prefix_mass_fa(const __grid_const
     asm volatile("prefetch.tensormap [%0];\n" ::"l"(reinterpret_cast<uint64_t>(&A.kmap)) : "memory");
     asm volatile("prefetch.tensormap [%0];\n" ::"l"(reinterpret_cast<uint64_t>(&A.vmap)) : "memory");
     for (int i = 0; i < 2; ++i) {
-      mbar_init(&kfull[i], 1);
-      mbar_init(&vfull[i], 1);
       mbar_init(&s_full[i], 1);
       mbar_init(&s_free[i], kSumWarps);
-      mbar_init(&v_free[i], kSumWarps);
     }
-    for (int i = 0; i < kSlots; ++i) {
+    for (int i = 0; i < kMaxSlots; ++i) {
+      mbar_init(&kfull[i], 1);
+      mbar_init(&vfull[i], 1);
+      mbar_init(&v_free[i], kSumWarps);
       mbar_init(&wfull[i], 1);
       mbar_init(&wfree[i], kSumWarps);
     }
@@ -155,7 +145,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefix_mass_fa(const __grid_const
   if (sum_warp) {
     pdl_wait();   // m_p, l_p (and with a programmatic launch, the outputs) of the kernel before
     // selection rows r2 = g*T2 + i -> query row (h*G + g, q_rows[i]) and B_r
-    for (int rr = threadIdx.x; rr < Npad; rr += kSumThreads) {
+    for (int rr = threadIdx.x; rr < kMaxRows; rr += kSumThreads) {
       const int g = rr / A.T2;
       const int t = rr < R2 ? A.q_rows[rr - g * A.T2] : -1;
       const bool ok = t >= 0 && t < T;
@@ -166,7 +156,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefix_mass_fa(const __grid_const
         if (L > 0.f) Bv = fmaf(A.m_p[ri], kLog2e, log2f(L));
       }
       sRowT[rr] = ok ? t : -1;
-      sB[rr] = Bv;
+      sNB[rr] = -Bv;
     }
     sum_sync();
     // the selection rows' queries, K-major SW128 with Npad rows (zeros for padding)
@@ -191,8 +181,10 @@ __global__ void __launch_bounds__(kThreads, 1) prefix_mass_fa(const __grid_const
   __syncthreads();
   fence_after_sync();
   const uint32_t taddr = s_taddr;
-  float cacc0 = 0.f, cacc1 = 0.f, asum = 0.f;
-  const int cp = threadIdx.x & 63, kq = (threadIdx.x >> 6) & 3;   // centre: channel pair, key quarter
+  // centre: thread = (channel chunk cc of 8 channels, slot group sg of 8 slots per tile)
+  float cacc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+  float asum = 0.f;
+  const int cc = threadIdx.x & 15, sg = (threadIdx.x >> 4) & 15;
 
   if (!sum_warp) {
     // ------------------------------------------------------------ producer / MMA warp
@@ -201,11 +193,11 @@ __global__ void __launch_bounds__(kThreads, 1) prefix_mass_fa(const __grid_const
       bool ok = true;
       int kIss = 0, kObs = 0, vIss = 0, vObs = 0, sN = 0, sDone = 0, sfObs = 0, vfObs = 0;
       const uint64_t pol_k = tma::policy_evict_first(), pol_v = tma::policy_evict_last();
-      for (; kIss < 2 && kIss < ntiles; ++kIss)
+      for (; kIss < nK && kIss < ntiles; ++kIss)
         tile_load(&A.kmap, b, h, begin + kIss * kTile, sSlot + kIss * kTileBytes, &kfull[kIss], pol_k);
       if (centre)
-        for (; vIss < 2 && vIss < ntiles; ++vIss)
-          tile_load(&A.vmap, b, h, begin + vIss * kTile, sSlot + (2 + vIss) * kTileBytes, &vfull[vIss], pol_v);
+        for (; vIss < nV && vIss < ntiles; ++vIss)
+          tile_load(&A.vmap, b, h, begin + vIss * kTile, sSlot + (nK + vIss) * kTileBytes, &vfull[vIss], pol_v);
       const int vTiles = centre ? ntiles : 0;
       const uint32_t idesc = idesc_bf16(kTile, Npad, false, false);
       const uint64_t kdesc = smem_desc(smem_addr(sSlot), 16, 1024);
@@ -216,7 +208,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefix_mass_fa(const __grid_const
       int spins = 0;
       while (ok && (sN < ntiles || kIss < ntiles || vIss < vTiles)) {
         bool progress = false;
-        if (kObs < kIss && mbar_test(&kfull[kObs & 1], (uint32_t)(kObs >> 1) & 1u)) {
+        if (kObs < kIss && mbar_test(&kfull[kObs % nK], (uint32_t)(kObs / nK) & 1u)) {
           ++kObs;
           progress = true;
         }
@@ -228,11 +220,11 @@ __global__ void __launch_bounds__(kThreads, 1) prefix_mass_fa(const __grid_const
           ++sfObs;
           progress = true;
         }
-        if (vfObs < vObs && mbar_test(&v_free[vfObs & 1], (uint32_t)(vfObs >> 1) & 1u)) {
+        if (vfObs < vObs && mbar_test(&v_free[vfObs % nV], (uint32_t)(vfObs / nV) & 1u)) {
           ++vfObs;
           progress = true;
         }
-        if (vObs < vIss && mbar_test(&vfull[vObs & 1], (uint32_t)(vObs >> 1) & 1u)) {
+        if (vObs < vIss && mbar_test(&vfull[vObs % nV], (uint32_t)(vObs / nV) & 1u)) {
           ++vObs;
           progress = true;
         }
@@ -240,7 +232,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefix_mass_fa(const __grid_const
         // the buffer's previous tile
         if (sN < ntiles && kObs > sN && sfObs >= sN - 1 && sDone >= sN - 1) {
           fence_after_sync();
-          const uint64_t ad0 = kdesc + (uint64_t)((sN & 1) * (kTileBytes >> 4));
+          const uint64_t ad0 = kdesc + (uint64_t)((sN % nK) * (kTileBytes >> 4));
           const uint32_t d = taddr + (sN & 1) * 256;
 #pragma unroll
           for (int kk = 0; kk < kD / 16; ++kk)
@@ -250,15 +242,15 @@ __global__ void __launch_bounds__(kThreads, 1) prefix_mass_fa(const __grid_const
           ++sN;
           progress = true;
         }
-        // K slot of tile kIss - 2 is free once its S^T completed
-        if (kIss < ntiles && sDone > kIss - 2) {
-          tile_load(&A.kmap, b, h, begin + kIss * kTile, sSlot + (kIss & 1) * kTileBytes, &kfull[kIss & 1], pol_k);
+        // K slot of tile kIss - nK is free once its S^T completed
+        if (kIss < ntiles && sDone > kIss - nK) {
+          tile_load(&A.kmap, b, h, begin + kIss * kTile, sSlot + (kIss % nK) * kTileBytes, &kfull[kIss % nK], pol_k);
           ++kIss;
           progress = true;
         }
-        // V slot of tile vIss - 2 is free once the sum warps released it
-        if (vIss < vTiles && vfObs > vIss - 2) {
-          tile_load(&A.vmap, b, h, begin + vIss * kTile, sSlot + (2 + (vIss & 1)) * kTileBytes, &vfull[vIss & 1],
+        // V slot of tile vIss - nV is free once the sum warps released it
+        if (vIss < vTiles && vfObs > vIss - nV) {
+          tile_load(&A.vmap, b, h, begin + vIss * kTile, sSlot + (nK + vIss % nV) * kTileBytes, &vfull[vIss % nV],
                     pol_v);
           ++vIss;
           progress = true;
@@ -266,7 +258,8 @@ __global__ void __launch_bounds__(kThreads, 1) prefix_mass_fa(const __grid_const
         if (progress) {
           spins = 0;
           armed = false;
-        } else if (++spins == 256) {   // idle: bound the time without progress
+        } else if (__nanosleep(kIdleNs), ++spins == 256) {   // idle: back off (the issue slots
+          // of this sub-partition belong to two compute warps), bound the time without progress
           spins = 0;
           const uint64_t now = global_ns();
           if (!armed) {
@@ -282,42 +275,59 @@ __global__ void __launch_bounds__(kThreads, 1) prefix_mass_fa(const __grid_const
       // drain (bounded): every MMA, every load still in flight
       mma_commit(&mbar_fin);
       mbar_wait(&mbar_fin, 0, 20000000ull);
-      for (int tt = kObs; tt < kIss; ++tt) mbar_wait(&kfull[tt & 1], (uint32_t)(tt >> 1) & 1u, 20000000ull);
-      for (int tt = vObs; tt < vIss; ++tt) mbar_wait(&vfull[tt & 1], (uint32_t)(tt >> 1) & 1u, 20000000ull);
+      for (int tt = kObs; tt < kIss; ++tt) mbar_wait(&kfull[tt % nK], (uint32_t)(tt / nK) & 1u, 20000000ull);
+      for (int tt = vObs; tt < vIss; ++tt) mbar_wait(&vfull[tt % nV], (uint32_t)(tt / nV) & 1u, 20000000ull);
     }
     __syncwarp();
   } else {
     // ------------------------------------------------------------ sum warps
     __shared__ int sDecide;
-    const int cols_half = Npad / 2;   // a multiple of 8
-    const int c_lo = chalf * cols_half;
     const uint32_t tRow = taddr + ((uint32_t)(quarter * 32) << 16);
+    const float2 c2x2 = make_float2(c2, c2);
+    // the row chunks are 64 columns, taken alternately by the two warps of a slot quarter;
+    // rows past R2 read -inf from sNB, and the columns past Npad of a last partial chunk
+    // are zeroed once here (the MMAs never write them), so no chunk needs a bound check
+    if ((Npad & 63) != 0 && ((Npad >> 6) & 1) == chalf) {
+      const uint32_t z[16] = {0u, 0u, 0u, 0u, 0u, 0u, 0u, 0u, 0u, 0u, 0u, 0u, 0u, 0u, 0u, 0u};
+      for (int col = Npad; col < (Npad | 63) + 1; col += 16) {
+        tmem_st16(tRow + col, z);
+        tmem_st16(tRow + 256 + col, z);
+      }
+      tmem_st_wait();
+    }
     for (int t = 0; t < ntiles; ++t) {
       const int j0 = begin + t * kTile;
       if (!mbar_wait(&s_full[t & 1], (uint32_t)(t >> 1) & 1u, kWaitNs)) s_abort = 1;
       fence_after_sync();
-      // this thread: slot slot_lane, rows [c_lo, c_lo + cols_half), in row order
-      float acc[4] = {0.f, 0.f, 0.f, 0.f};
-      const uint32_t tS = tRow + (t & 1) * 256 + c_lo;
+      // this thread: slot slot_lane, row chunks chalf, chalf + 2, ...
+      float2 a0 = make_float2(0.f, 0.f), a1 = a0, a2 = a0, a3 = a0;
+      const uint32_t tS = tRow + (t & 1) * 256;
 #pragma unroll 1
-      for (int c0 = 0; c0 < cols_half; c0 += 64) {
+      for (int c = chalf; c * 64 < Npad; c += 2) {
         float sv[64];
-        tmem_ld32(tS + c0, sv);
-        tmem_ld32(tS + c0 + 32, sv + 32);
+        tmem_ld32(tS + c * 64, sv);
+        tmem_ld32(tS + c * 64 + 32, sv + 32);
         tmem_ld_wait();
-        const int lim = cols_half - c0;
+        const float* nb = sNB + c * 64;
 #pragma unroll
-        for (int i = 0; i < 64; i += 4) {
-          const float4 b4 = *reinterpret_cast<const float4*>(&sB[(c_lo + c0 + i) & (kMaxRows - 1)]);
-          if (i < lim) {   // lim is a multiple of 8
-            acc[0] += ex2(fmaf(sv[i], c2, -b4.x));
-            acc[1] += ex2(fmaf(sv[i + 1], c2, -b4.y));
-            acc[2] += ex2(fmaf(sv[i + 2], c2, -b4.z));
-            acc[3] += ex2(fmaf(sv[i + 3], c2, -b4.w));
-          }
+        for (int i = 0; i < 64; i += 8) {
+          const float4 b0 = *reinterpret_cast<const float4*>(nb + i);
+          const float4 b1 = *reinterpret_cast<const float4*>(nb + i + 4);
+          float2 x0 = ffma2(make_float2(sv[i], sv[i + 1]), c2x2, make_float2(b0.x, b0.y));
+          float2 x1 = ffma2(make_float2(sv[i + 2], sv[i + 3]), c2x2, make_float2(b0.z, b0.w));
+          float2 x2 = ffma2(make_float2(sv[i + 4], sv[i + 5]), c2x2, make_float2(b1.x, b1.y));
+          float2 x3 = ffma2(make_float2(sv[i + 6], sv[i + 7]), c2x2, make_float2(b1.z, b1.w));
+          x0 = make_float2(ex2(x0.x), ex2(x0.y));
+          x1 = make_float2(ex2(x1.x), ex2(x1.y));
+          x2 = make_float2(ex2(x2.x), ex2(x2.y));
+          x3 = make_float2(ex2(x3.x), ex2(x3.y));
+          a0 = fadd2(a0, x0);
+          a1 = fadd2(a1, x1);
+          a2 = fadd2(a2, x2);
+          a3 = fadd2(a3, x3);
         }
       }
-      sHalf[chalf][slot_lane] = (acc[0] + acc[1]) + (acc[2] + acc[3]);
+      sHalf[chalf][slot_lane] = ((a0.x + a0.y) + (a1.x + a1.y)) + ((a2.x + a2.y) + (a3.x + a3.y));
       fence_before_sync();
       __syncwarp();
       if (lane == 0) mbar_arrive(&s_free[t & 1]);
@@ -329,25 +339,26 @@ __global__ void __launch_bounds__(kThreads, 1) prefix_mass_fa(const __grid_const
         if (j < end) A.mass[(int64_t)b * A.sm0 + (int64_t)h * A.sm1 + j] = a;
         sA[threadIdx.x] = a;
       }
-      if (centre && !mbar_wait(&vfull[t & 1], (uint32_t)(t >> 1) & 1u, kWaitNs)) s_abort = 1;
+      if (centre && !mbar_wait(&vfull[t % nV], (uint32_t)(t / nV) & 1u, kWaitNs)) s_abort = 1;
       if (threadIdx.x == 0) sDecide = s_abort;
       sum_sync();
       if (sDecide) break;   // every sum warp leaves at the same tile
       if (centre) {
-        // sum_j a_j v_j over this thread's key quarter, channels 2cp, 2cp+1
-        const uint8_t* sV = sSlot + (2 + (t & 1)) * kTileBytes;
+        // sum_j a_j v_j: slots sg + 16i of the tile, channels 8cc..8cc+7 (16-byte reads; a
+        // warp reads two whole rows per step)
+        const uint8_t* sV = sSlot + (nK + t % nV) * kTileBytes;
 #pragma unroll 4
-        for (int jj = 0; jj < kTile / 4; ++jj) {
-          const int j = kq * (kTile / 4) + jj;
+        for (int i = 0; i < kTile / 16; ++i) {
+          const int j = sg + 16 * i;
           const float a = sA[j];
-          const float2 v = __bfloat1622float2(
-              *reinterpret_cast<const __nv_bfloat162*>(sV + chunk_off(j, cp >> 2) + (cp & 3) * 4));
-          cacc0 = fmaf(a, v.x, cacc0);
-          cacc1 = fmaf(a, v.y, cacc1);
+          float f[8];
+          bf16x8_to_float(*reinterpret_cast<const uint4*>(sV + chunk_off(j, cc)), f);
+#pragma unroll
+          for (int e = 0; e < 8; ++e) cacc[e] = fmaf(a, f[e], cacc[e]);
           asum += a;
         }
         __syncwarp();
-        if (lane == 0) mbar_arrive(&v_free[t & 1]);
+        if (lane == 0) mbar_arrive(&v_free[t % nV]);
       }
     }
   }
@@ -360,18 +371,30 @@ __global__ void __launch_bounds__(kThreads, 1) prefix_mass_fa(const __grid_const
   if (aborted && threadIdx.x == 0) atomicExch(A.err, 1);
   if (!centre) return;
 
-  // per-CTA centre partial (key quarters summed in order); the last CTA of the head
+  // centre partials per slot group, in K slot 0 (drained; V tiles may stay in their slots)
+  float* sRed = reinterpret_cast<float*>(sSlot);           // [16][kD]
+  float* sAsum = sRed + 16 * kD;                           // [16]
+  // per-CTA centre partial (slot groups summed in order); the last CTA of the head
   // reduces the partials in CTA order and publishes c by advancing the generation
   if (sum_warp) {
-    sRed[kq][2 * cp] = cacc0;
-    sRed[kq][2 * cp + 1] = cacc1;
-    if (cp == 0) sAsum[kq] = asum;
+#pragma unroll
+    for (int e = 0; e < 8; ++e) sRed[sg * kD + 8 * cc + e] = cacc[e];
+    if (cc == 0) sAsum[sg] = asum;
   }
   __syncthreads();
   float* mine = A.part + ((int64_t)bh * gridDim.x + blockIdx.x) * (kD + 1);
-  if (threadIdx.x < kD)
-    mine[threadIdx.x] = aborted ? NAN : ((sRed[0][threadIdx.x] + sRed[1][threadIdx.x]) + sRed[2][threadIdx.x]) + sRed[3][threadIdx.x];
-  if (threadIdx.x == 0) mine[kD] = ((sAsum[0] + sAsum[1]) + sAsum[2]) + sAsum[3];
+  if (threadIdx.x < kD) {   // slot groups summed in order
+    float tot = 0.f;
+#pragma unroll
+    for (int g = 0; g < 16; ++g) tot += sRed[g * kD + threadIdx.x];
+    mine[threadIdx.x] = aborted ? NAN : tot;
+  }
+  if (threadIdx.x == 0) {
+    float tot = 0.f;
+#pragma unroll
+    for (int g = 0; g < 16; ++g) tot += sAsum[g];
+    mine[kD] = tot;
+  }
   __threadfence();
   __syncthreads();
   if (threadIdx.x == 0) sLast = atomicAdd(&A.sync[bh].x, 1u) == gridDim.x - 1 ? 1 : 0;
@@ -417,57 +440,69 @@ __global__ void __launch_bounds__(kThreads, 1) prefix_mass_fa(const __grid_const
   }
   __syncthreads();
   const bool ok_c = s_wait_ok != 0 && !aborted;
+  // every V tile of the CTA still in its phase-1 slot (the V ring never wrapped)
+  const bool resident = ntiles <= nV;
   if (!sum_warp) {
-    if (lane == 0 && ok_c) {
-      // the CTA's V tiles again, newest first, through all four slots
+    if (lane == 0 && ok_c && !resident) {
+      // the CTA's V tiles again, newest first, through every slot
       const uint64_t pol = tma::policy_evict_first();
       int u = 0;
       for (; u < ntiles; ++u) {
-        const int slot = u % kSlots;
-        if (u >= kSlots && !mbar_wait(&wfree[slot], (uint32_t)((u / kSlots) - 1) & 1u, kWaitNs)) break;
+        const int slot = u % nS;
+        if (u >= nS && !mbar_wait(&wfree[slot], (uint32_t)((u / nS) - 1) & 1u, kWaitNs)) break;
         tile_load(&A.vmap, b, h, begin + (ntiles - 1 - u) * kTile, sSlot + slot * kTileBytes, &wfull[slot], pol);
       }
       // drain (bounded): the last load of every slot
-      for (int uu = max(0, u - kSlots); uu < u; ++uu)
-        mbar_wait(&wfull[uu % kSlots], (uint32_t)(uu / kSlots) & 1u, 20000000ull);
+      for (int uu = max(0, u - nS); uu < u; ++uu)
+        mbar_wait(&wfull[uu % nS], (uint32_t)(uu / nS) & 1u, 20000000ull);
     }
     __syncwarp();
   } else {
-    const int grp = threadIdx.x >> 4, l16 = threadIdx.x & 15;
+    // thread = slot row rl of the tile (TMEM-lane order, as in phase 1) and channel half
+    // chalf; the halves' sums meet in shared memory (the Q region, free now)
     float* sc = A.score + (int64_t)b * A.ss0 + (int64_t)h * A.ss1;
+    float* sC = reinterpret_cast<float*>(sQ);      // [kD] the centre
+    float* sPart = sC + kD;                        // [2 tile parities][kTile] upper-half sums
     if (!ok_c) {
       for (int j = begin + threadIdx.x; j < end; j += kSumThreads) sc[j] = NAN;
     } else {
-      float cc[8];
-#pragma unroll
-      for (int i = 0; i < 8; ++i) cc[i] = __ldcg(A.centre + (int64_t)bh * kD + 8 * l16 + i);
+      if (threadIdx.x < kD) sC[threadIdx.x] = __ldcg(A.centre + (int64_t)bh * kD + threadIdx.x);
+      sum_sync();
       const float* ms = A.mass + (int64_t)b * A.sm0 + (int64_t)h * A.sm1;
+      const float* cb = sC + 64 * chalf;
       for (int u = 0; u < ntiles; ++u) {
-        const int slot = u % kSlots;
+        const int slot = resident ? nK + (ntiles - 1 - u) : u % nS;
         const int j0 = begin + (ntiles - 1 - u) * kTile;
-        if (!mbar_wait(&wfull[slot], (uint32_t)(u / kSlots) & 1u, kWaitNs)) {
-          atomicExch(A.err, 1);
-          for (int j = j0 + threadIdx.x; j < min(end, j0 + kTile); j += kSumThreads) sc[j] = NAN;
-          break;
-        }
-        const uint8_t* sV = sSlot + slot * kTileBytes;
-#pragma unroll 2
-        for (int jj = grp; jj < kTile; jj += kSumThreads / 16) {
-          const int j = j0 + jj;
-          float f[8];
-          bf16x8_to_float(*reinterpret_cast<const uint4*>(sV + chunk_off(jj, l16)), f);
-          float s2 = 0.f;
+        const int j = j0 + slot_lane;
+        float aj = 0.f;   // issued before the tile's wait
+        if (chalf == 0 && j < end) aj = __ldcg(ms + j);
+        bool ok_t = resident || mbar_wait(&wfull[slot], (uint32_t)(u / nS) & 1u, kWaitNs);
+        float2 s0 = make_float2(0.f, 0.f), s1 = s0;
+        if (ok_t) {
+          const uint8_t* sV = sSlot + slot * kTileBytes;
 #pragma unroll
-          for (int i = 0; i < 8; ++i) {
-            const float x = f[i] - cc[i];
-            s2 = fmaf(x, x, s2);
+          for (int c = 0; c < 8; ++c) {
+            float f[8];
+            bf16x8_to_float(*reinterpret_cast<const uint4*>(sV + chunk_off(slot_lane, 8 * chalf + c)), f);
+            const float4 c0 = *reinterpret_cast<const float4*>(cb + 8 * c);
+            const float4 c1 = *reinterpret_cast<const float4*>(cb + 8 * c + 4);
+            const float2 x0 = make_float2(f[0] - c0.x, f[1] - c0.y), x1 = make_float2(f[2] - c0.z, f[3] - c0.w);
+            const float2 x2 = make_float2(f[4] - c1.x, f[5] - c1.y), x3 = make_float2(f[6] - c1.z, f[7] - c1.w);
+            s0 = ffma2(x0, x0, s0);
+            s1 = ffma2(x1, x1, s1);
+            s0 = ffma2(x2, x2, s0);
+            s1 = ffma2(x3, x3, s1);
           }
-#pragma unroll
-          for (int o = 8; o > 0; o >>= 1) s2 += __shfl_xor_sync(0xffffffffu, s2, o);
-          if (l16 == 0 && j < end) sc[j] = kv_live(A.kv, H, b, h, j) ? __ldcg(ms + j) * sqrtf(s2) : 0.f;
         }
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&wfree[slot]);
+        const float s2 = (s0.x + s0.y) + (s1.x + s1.y);
+        if (chalf == 1) sPart[(u & 1) * kTile + slot_lane] = s2;
+        if (!ok_t) atomicExch(A.err, 1);
+        sum_sync();   // the upper halves are in; this tile's slot is read
+        if (chalf == 0 && j < end) {
+          const float tot = s2 + sPart[(u & 1) * kTile + slot_lane];
+          sc[j] = !ok_t ? NAN : (kv_live(A.kv, H, b, h, j) ? aj * sqrtf(tot) : 0.f);
+        }
+        if (lane == 0 && !resident) mbar_arrive(&wfree[slot]);
       }
     }
   }
@@ -516,6 +551,21 @@ int launch_prefix_mass_fa(const ma_rows& q, const ma_kv& kv, int H, const int32_
   A.H = H;
   A.T2 = T2;
   A.want_centre = want_centre ? 1 : 0;
+  // Q takes Npad * 256 bytes; the rest holds up to six 32 KB tile slots. With the centre,
+  // K gets the deeper ring (a K slot is needed again one tile after its S^T completes, a
+  // V slot only after the next tiles' sums): 5 slots -> K 3 + V 2.
+  const int Npad = (G * T2 + 15) & ~15;
+  int nslots = (kSmemLimit - kStaticSmem - 1024 - Npad * 256) / kTileBytes;
+  if (nslots > kMaxSlots) nslots = kMaxSlots;
+  if (nslots < 4) return MA_ERR_UNSUPPORTED;
+  if (want_centre) {
+    A.nV = nslots >= 5 ? nslots - 3 : 2;
+    A.nK = nslots - A.nV;
+  } else {
+    A.nK = nslots;
+    A.nV = 0;
+  }
+  const int smem = 1024 + Npad * 256 + nslots * kTileBytes;
   // one wave of CTAs over the heads, whole tiles each
   const int sms = device_sm_count();
   int per_head = sms / (BH > 0 ? BH : 1);
@@ -524,21 +574,21 @@ int launch_prefix_mass_fa(const ma_rows& q, const ma_kv& kv, int H, const int32_
   spc = ((spc + kTile - 1) / kTile) * kTile;
   A.slots_per_cta = spc;
   dim3 grid((n + spc - 1) / spc, BH);
-  if (cudaFuncSetAttribute(prefix_mass_fa, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes) != cudaSuccess)
+  if (cudaFuncSetAttribute(prefix_mass_fa, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
     return MA_ERR_CUDA;
   if (score != nullptr && want_centre) {
     // the fused score needs every CTA resident at once: a cooperative launch that fits
     int dev = 0, coop = 0, per_sm = 0;
     if (cudaGetDevice(&dev) == cudaSuccess &&
         cudaDeviceGetAttribute(&coop, cudaDevAttrCooperativeLaunch, dev) == cudaSuccess && coop &&
-        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, prefix_mass_fa, kThreads, kSmemBytes) == cudaSuccess &&
+        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, prefix_mass_fa, kThreads, smem) == cudaSuccess &&
         (long long)grid.x * grid.y <= (long long)per_sm * sms) {
       Args Ac = A;
       Ac.score = score;
       cudaLaunchConfig_t cfg = {};
       cfg.gridDim = grid;
       cfg.blockDim = dim3(kThreads);
-      cfg.dynamicSmemBytes = kSmemBytes;
+      cfg.dynamicSmemBytes = smem;
       cfg.stream = st;
       cudaLaunchAttribute attr[1];
       attr[0].id = cudaLaunchAttributeCooperative;
@@ -552,7 +602,7 @@ int launch_prefix_mass_fa(const ma_rows& q, const ma_kv& kv, int H, const int32_
       (void)cudaGetLastError();
     }
   }
-  return launch_pdl(prefix_mass_fa, grid, dim3(kThreads), kSmemBytes, st, A) == cudaSuccess ? MA_OK : MA_ERR_CUDA;
+  return launch_pdl(prefix_mass_fa, grid, dim3(kThreads), smem, st, A) == cudaSuccess ? MA_OK : MA_ERR_CUDA;
 }
 
 }  // namespace ma
