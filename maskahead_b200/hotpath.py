@@ -4,11 +4,14 @@ These functions are what the reference session's fast path does per layer
 (src/maskahead/runtime/session.py), written against the sm_100a operators:
 
   fast_step0          _fast_step0 (1403-1454): dense attention over [live prefix |
-                      block], the block's prefix mass, the value-aware score and the
-                      ascending top-k read set -- without the gather: sub-steps read the
-                      selected slots straight from the cache.
+                      block], the block's prefix mass, the value-aware score, the
+                      ascending top-k read set and (gather=True) the read set's K/V rows
+                      gathered once into a compact dense cache (1438-1447, gather_dequant
+                      1174-1190).
+  gather_read_set     that gather on its own.
   compact_attention   _compact_attention / sdpa_compact (1286-1336; reference.py:403-426):
-                      attention over [read set | block].
+                      attention over [read set | block], from the compact cache (as the
+                      reference does) or by index straight from the cache.
   probe_attention     the lookahead probe (2317-2332): block-causal attention of the probe
                       forward plus the prefix mass of the probe rows.
   value_score         value_score (27-40) with the fp32 centre, over dense values;
@@ -24,11 +27,11 @@ import torch
 
 from . import _lib
 from .kernels._common import block_struct, rows_struct
-from .kernels.ops import select_topk_indices
+from .kernels.ops import gather_packed_kv, select_topk_indices
 from .kernels.splitk import prefix_scores, splitk_attention
 from .layouts import Prefix, as_prefix, kv_descriptor
 
-__all__ = ["Step0Result", "fast_step0", "compact_attention", "probe_attention", "value_score",
+__all__ = ["Step0Result", "fast_step0", "gather_read_set", "compact_attention", "probe_attention", "value_score",
            "value_score_prefix", "lookahead_survivors"]
 
 
@@ -38,15 +41,20 @@ class Step0Result:
     indices: torch.Tensor | None         # [B, Hkv, k] ascending read set (None: dense layer)
     mass: torch.Tensor | None            # [B, Hkv, n] prefix mass of the selection rows
     score: torch.Tensor | None           # [B, Hkv, n] value-aware score (value_aware only)
+    compact: Prefix | None = None        # the read set's rows, gathered (gather=True only)
 
 
 def fast_step0(query: torch.Tensor, prefix, current_key: torch.Tensor, current_value: torch.Tensor, *,
                query_indices, topk: int, value_aware: bool = True, scaling: float | None = None,
-               select: bool = True, want_mass: bool = False) -> Step0Result:
+               select: bool = True, want_mass: bool = False, gather: bool = False,
+               compact_out: tuple[torch.Tensor, torch.Tensor] | None = None) -> Step0Result:
     """Step 0 of one layer: attention output, mass, score and the read set (session.py:1403-1454).
 
     The read set is the top min(topk, live) slots by score (value_aware) or mass, dead
-    slots never chosen, as ascending slot indices.
+    slots never chosen, as ascending slot indices. gather=True also gathers the read set's
+    K/V rows (dequantized to the query dtype) into a compact dense cache for the
+    sub-steps, optionally into the caller's buffers compact_out = (key, value), each
+    [B, Hkv, >= k, D] (the session's state.key / state.value).
     """
     prefix = as_prefix(prefix)
     if prefix.n == 0:
@@ -65,14 +73,35 @@ def fast_step0(query: torch.Tensor, prefix, current_key: torch.Tensor, current_v
         k = int(topk) if live is None else min(int(topk), live)
         rank = score if value else mass
         idx, _ = select_topk_indices(rank, k, prefix.mask, want_values=False, lens=prefix.lens)
-    return Step0Result(out, idx, mass, score)
+    compact = None
+    if select and gather:
+        compact = gather_read_set(prefix, idx, dtype=query.dtype, out=compact_out)
+    return Step0Result(out, idx, mass, score, compact)
 
 
-def compact_attention(query: torch.Tensor, prefix, indices: torch.Tensor, current_key: torch.Tensor,
+def gather_read_set(prefix, indices: torch.Tensor, *, dtype: torch.dtype = torch.bfloat16,
+                    out: tuple[torch.Tensor, torch.Tensor] | None = None) -> Prefix:
+    """The read set's K/V rows per KV head, dequantized into contiguous [B, Hkv, k, D]
+    tensors -- the session's compact cache (session.py:1174-1190, 1438-1447) -- as a dense
+    Prefix for compact_attention. out = (key, value) buffers of at least k rows."""
+    k = indices.shape[2]
+    ok = ov = None
+    if out is not None:
+        ok, ov = out[0][:, :, :k, :], out[1][:, :, :k, :]
+    ck, cv = gather_packed_kv(prefix, indices, dtype=dtype, out_key=ok, out_value=ov)
+    return Prefix.dense(ck, cv)
+
+
+def compact_attention(query: torch.Tensor, prefix, indices: torch.Tensor | None, current_key: torch.Tensor,
                       current_value: torch.Tensor, *, scaling: float | None = None) -> torch.Tensor:
     """Attention of every query row over [prefix[indices] | current block] (sdpa_compact
-    over the gathered read set, session.py:1286-1336), reading the selected slots
-    directly from the (packed or dense) cache."""
+    over the gathered read set, session.py:1286-1336). indices=None: prefix is the
+    compact cache itself (gather_read_set / fast_step0(gather=True)), attended as a
+    contiguous dense cache; else the selected slots are read straight from the (packed or
+    dense) cache by index."""
+    if indices is None:
+        out, _ = splitk_attention(query, prefix, current_key, current_value, scaling=scaling)
+        return out
     lib = _lib.lib()
     prefix = as_prefix(prefix)
     b, hq, t, d = query.shape

@@ -76,6 +76,24 @@ def test_sparse_substep_matches_reference(name):
     np.testing.assert_allclose(out.float().cpu().numpy(), g["compact_out"], rtol=rtol, atol=atol)
 
 
+@pytest.mark.parametrize("name", list(CASES))
+def test_compact_cache_substep_matches_reference(name):
+    """The session's path: the read set gathered once into a compact cache (dequantized),
+    every sub-step attending [compact | block] as a contiguous cache."""
+    from maskahead_b200.hotpath import compact_attention, gather_read_set
+
+    g = _golden(name)
+    case, k, v, extra = load_case(name)
+    q, kc, vc = case["query"], case["current_key"], case["current_value"]
+    prefix = device_prefix(case, k, v, extra)
+    idx = torch.from_numpy(g["value_indices"]).to(DEV)
+    compact = gather_read_set(prefix, idx, dtype=q.dtype)
+    out = compact_attention(q.to(DEV), compact, None, kc.to(DEV), vc.to(DEV), scaling=case["spec"]["D"] ** -0.5)
+    torch.cuda.synchronize()
+    atol, rtol = _out_tol(q.dtype)
+    np.testing.assert_allclose(out.float().cpu().numpy(), g["compact_out"], rtol=rtol, atol=atol)
+
+
 @pytest.mark.parametrize("name", ["small_bf16", "small_k4v4_token", "small_k4v4_channel", "cfg1"])
 def test_gather_is_bit_exact(name):
     from maskahead_b200.kernels import gather_packed_kv
