@@ -230,7 +230,9 @@ MA_API int ma_sparse_attention(const ma_rows* q, const ma_kv* kv, int H,
                         void* workspace, size_t workspace_bytes, void* stream);
 
 /* ---- gather + dequantize ------------------------------------------------------------
- * out_k/out_v [B,H,k,D] (out_dtype) = the prefix slots idx[b,h,:].                   */
+ * out_k/out_v [B,H,k,D] (out_dtype) = the prefix slots idx[b,h,:]; idx = NULL (sidx
+ * ignored): slots 0..k-1, i.e. the whole prefix dequantized when k = nq + nf. Slots past
+ * lens[b] or on a bad page read as zeros.                                             */
 MA_API int ma_gather_kv(const ma_kv* kv, int B, int H, int D, const int64_t* idx, int k,
                  const int64_t sidx[2], void* out_k, void* out_v, const int64_t sok[3],
                  const int64_t sov[3], int32_t out_dtype, void* stream);

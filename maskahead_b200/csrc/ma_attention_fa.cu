@@ -144,6 +144,10 @@ __global__ void __launch_bounds__(kThreads, 1) attn_partial_fa(const __grid_cons
   } else {
     begin = split * A.split_len;
     end = min(A.n_keys, begin + A.split_len);
+    if (A.kv.lens) {   // a ragged batch: slots past lens[b] do not exist (lens may come from
+      pdl_wait();      // the kernel before, with a programmatic launch)
+      end = max(begin, min(end, A.kv.lens[b]));
+    }
   }
   int vis_end = end;
   if (is_cur && A.causal_block > 0)
@@ -527,7 +531,7 @@ int fa_row_tile() { return kRowTile; }
 
 bool fa_eligible(const ma_rows& q, const ma_kv& kv, const int64_t* idx, const ma_block& cur, int n_keys) {
   const bool prefix_ok = n_keys == 0 || (kv.layout == MA_KV_DENSE && kv.dtype == MA_BF16 && !idx && !kv.mask &&
-                                         !kv.pages && !kv.lens);
+                                         !kv.pages);
   // a row tile is 128 / T whole query heads, or 128 positions of one head
   const bool rows_ok = q.T > 0 && (q.T <= kRowTile ? kRowTile % q.T == 0 : q.T % kRowTile == 0);
   return q.dtype == MA_BF16 && q.D == kD && rows_ok && prefix_ok && (n_keys > 0 || cur.Tc > 0);

@@ -133,6 +133,12 @@ Plan plan_splits(int BH, int R, int n, int Tc, bool mma, bool fa = false) {
     const int min_len = (mma ? 1 : 2) * kt;
     const int max_splits = (n + min_len - 1) / min_len;
     int ns = target < max_splits ? target : max_splits;
+    // the pipelined kernel: at most 32 key tiles per split, so long rows of a large batch
+    // spread over many short CTAs (several waves balance ragged lengths)
+    if (fa) {
+      const int by_len = (n + 32 * kt - 1) / (32 * kt);
+      if (ns < by_len) ns = by_len < max_splits ? by_len : max_splits;
+    }
     if (ns > 255) ns = 255;
     int len = (n + ns - 1) / ns;
     len = ((len + kt - 1) / kt) * kt;
@@ -429,11 +435,11 @@ int ma_gather_kv(const ma_kv* kv, int B, int H, int D, const int64_t* idx, int k
   int rc = check_kv(kv, D);
   if (rc) return rc;
   if (!valid_dtype(out_dtype)) return MA_ERR_ARG;
-  if (k > 0 && (!idx || !sidx || !out_k || !out_v || !sok || !sov)) return MA_ERR_ARG;
+  if (k > 0 && ((idx && !sidx) || !out_k || !out_v || !sok || !sov)) return MA_ERR_ARG;
   if (k > 0 && (!aligned16(out_k) || !aligned16(out_v) || !strides16(sok, 3, esize(out_dtype)) ||
                 !strides16(sov, 3, esize(out_dtype))))
     return MA_ERR_ARG;
-  return launch_gather_kv(*kv, B, H, D, idx, k, k ? sidx[0] : 0, k ? sidx[1] : 0, out_k, out_v, sok, sov,
+  return launch_gather_kv(*kv, B, H, D, idx, k, (k && idx) ? sidx[0] : 0, (k && idx) ? sidx[1] : 0, out_k, out_v, sok, sov,
                           out_dtype, (cudaStream_t)stream);
 }
 

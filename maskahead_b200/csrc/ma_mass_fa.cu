@@ -114,7 +114,12 @@ __global__ void __launch_bounds__(kThreads, 1) prefix_mass_fa(const __grid_const
   const int quarter = warp & 3, chalf = (warp >> 2) & 1;
   const int slot_lane = quarter * 32 + lane;          // this thread's slot within a tile (TMEM lane)
   const int begin = blockIdx.x * A.slots_per_cta;
-  const int end = min(n, begin + A.slots_per_cta);
+  const int end_all = min(n, begin + A.slots_per_cta);
+  int end = end_all;
+  if (A.kv.lens) {   // a ragged batch: no work past lens[b] (lens may come from the kernel
+    pdl_wait();      // before, with a programmatic launch); those slots get 0 below
+    end = max(begin, min(end_all, A.kv.lens[b]));
+  }
   const int ntiles = end > begin ? (end - begin + kTile - 1) / kTile : 0;
   const float inv_rows = 1.f / (float)R2;
   const float c2 = A.scale * kLog2e;
@@ -362,6 +367,13 @@ __global__ void __launch_bounds__(kThreads, 1) prefix_mass_fa(const __grid_const
       }
     }
   }
+  // slots past lens[b]: mass (and score) 0
+  if (sum_warp && end < end_all) {
+    for (int j = end + threadIdx.x; j < end_all; j += kSumThreads) {
+      A.mass[(int64_t)b * A.sm0 + (int64_t)h * A.sm1 + j] = 0.f;
+      if (A.score) A.score[(int64_t)b * A.ss0 + (int64_t)h * A.ss1 + j] = 0.f;
+    }
+  }
   // join: the producer drained, the sum warps are out of their loop
   fence_before_sync();
   __syncthreads();
@@ -576,6 +588,13 @@ int launch_prefix_mass_fa(const ma_rows& q, const ma_kv& kv, int H, const int32_
   dim3 grid((n + spc - 1) / spc, BH);
   if (cudaFuncSetAttribute(prefix_mass_fa, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
     return MA_ERR_CUDA;
+  if (score != nullptr && want_centre && grid.x == 1) {
+    // one CTA per head: it reduces its own centre, so the score needs no other CTA
+    Args As = A;
+    As.score = score;
+    *fused = true;
+    return launch_pdl(prefix_mass_fa, grid, dim3(kThreads), smem, st, As) == cudaSuccess ? MA_OK : MA_ERR_CUDA;
+  }
   if (score != nullptr && want_centre) {
     // the fused score needs every CTA resident at once: a cooperative launch that fits
     int dev = 0, coop = 0, per_sm = 0;

@@ -566,7 +566,7 @@ __global__ void gather_kv_kernel(ma_kv kv, int H, int D, const int64_t* __restri
     const int ii = c / chunks, c8 = c - (c / chunks) * chunks;
     const int i = i0 + ii;
     if (i >= k) continue;
-    const int64_t slot64 = idx[(int64_t)b * si0 + (int64_t)h * si1 + i];
+    const int64_t slot64 = idx ? idx[(int64_t)b * si0 + (int64_t)h * si1 + i] : (int64_t)i;   // no index: slot i
     const int slot = (int)slot64;
     float fk[8], fv[8];
     if (slot64 >= 0 && slot64 < (int64_t)kv.nq + kv.nf && kv_exists(kv, b, slot)) {
@@ -582,6 +582,70 @@ __global__ void gather_kv_kernel(ma_kv kv, int H, int D, const int64_t* __restri
     store4(dk + 4, fk[4], fk[5], fk[6], fk[7]);
     store4(dv, fv[0], fv[1], fv[2], fv[3]);
     store4(dv + 4, fv[4], fv[5], fv[6], fv[7]);
+  }
+}
+
+
+// The whole token-mode packed prefix of one (b, h) dequantized in slot order (no index):
+// thread = (slot jj of 64, 32-channel group g); 16-byte payload loads, the group's fp16
+// scale/zero, codes to fp32 exactly (2^23 + code, minus 2^23), code*scale + zero in fp32
+// (times the per-channel divisor for keys), rounded once to bf16 -- kv_read8's values.
+// Slots past lens[b], on a bad page or past nq (a dense tail) go through kv_read8 or zero.
+constexpr int kUnpackTok = 64;
+
+__device__ __forceinline__ void unpack32(const uint4& p, float s, float z, const float* mul, float* f) {
+  const uint32_t w[4] = {p.x, p.y, p.z, p.w};
+#pragma unroll
+  for (int i = 0; i < 32; ++i) {
+    const float code = __uint_as_float(0x4B000000u | ((w[i >> 3] >> (4 * (i & 7))) & 0xFu)) - 8388608.f;
+    f[i] = fmaf(code, s, z);
+    if (mul) f[i] *= mul[i];
+  }
+}
+
+__global__ void __launch_bounds__(256) unpack_token_kernel(ma_kv kv, int H, int n, __nv_bfloat16* __restrict__ ok_,
+                                                           __nv_bfloat16* __restrict__ ov_, int64_t sok0, int64_t sok1,
+                                                           int64_t sok2, int64_t sov0, int64_t sov1, int64_t sov2) {
+  const int bh = blockIdx.y;
+  const int b = bh / H, h = bh - (bh / H) * H;
+  const int jj = threadIdx.x >> 2, g = threadIdx.x & 3;
+  const float* kch = kv.kchan + (int64_t)b * kv.skc[0] + (int64_t)h * kv.skc[1] + 32 * g;
+  for (int j = blockIdx.x * kUnpackTok + jj; j < n; j += gridDim.x * kUnpackTok) {
+    __nv_bfloat16* dk = ok_ + (int64_t)b * sok0 + (int64_t)h * sok1 + (int64_t)j * sok2 + 32 * g;
+    __nv_bfloat16* dv = ov_ + (int64_t)b * sov0 + (int64_t)h * sov1 + (int64_t)j * sov2 + 32 * g;
+    const bool live = kv_exists(kv, b, j);
+    float f[32];
+    if (j < kv.nq && live) {
+      int sb = b, sj = j;
+      if (kv_paged(kv, j)) kv_page(kv, b, j, sb, sj);
+      const uint4 pk = __ldg(reinterpret_cast<const uint4*>(kv.kq + (int64_t)sb * kv.skq[0] + (int64_t)h * kv.skq[1] + (int64_t)sj * kv.skq[2] + 16 * g));
+      const uint4 pv = __ldg(reinterpret_cast<const uint4*>(kv.vq + (int64_t)sb * kv.svq[0] + (int64_t)h * kv.svq[1] + (int64_t)sj * kv.svq[2] + 16 * g));
+      const int64_t kso = (int64_t)sb * kv.sks[0] + (int64_t)h * kv.sks[1] + (int64_t)sj * kv.sks[2] + g;
+      const int64_t vso = (int64_t)sb * kv.svs[0] + (int64_t)h * kv.svs[1] + (int64_t)sj * kv.svs[2] + g;
+      const float ks = half_bits_to_float(kv.ks[kso]), kz = half_bits_to_float(kv.kz[kso]);
+      const float vs = half_bits_to_float(kv.vs[vso]), vz = half_bits_to_float(kv.vz[vso]);
+      unpack32(pk, ks, kz, kch, f);
+#pragma unroll
+      for (int c = 0; c < 4; ++c) reinterpret_cast<uint4*>(dk)[c] = float8_to_bf16x8(f + 8 * c);
+      unpack32(pv, vs, vz, nullptr, f);
+#pragma unroll
+      for (int c = 0; c < 4; ++c) reinterpret_cast<uint4*>(dv)[c] = float8_to_bf16x8(f + 8 * c);
+    } else if (j >= kv.nq && live) {   // the dense tail
+#pragma unroll
+      for (int c = 0; c < 4; ++c) kv_read8<true>(kv, b, h, j, 4 * g + c, f + 8 * c);
+#pragma unroll
+      for (int c = 0; c < 4; ++c) reinterpret_cast<uint4*>(dk)[c] = float8_to_bf16x8(f + 8 * c);
+#pragma unroll
+      for (int c = 0; c < 4; ++c) kv_read8<false>(kv, b, h, j, 4 * g + c, f + 8 * c);
+#pragma unroll
+      for (int c = 0; c < 4; ++c) reinterpret_cast<uint4*>(dv)[c] = float8_to_bf16x8(f + 8 * c);
+    } else {
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        reinterpret_cast<uint4*>(dk)[c] = make_uint4(0, 0, 0, 0);
+        reinterpret_cast<uint4*>(dv)[c] = make_uint4(0, 0, 0, 0);
+      }
+    }
   }
 }
 
@@ -657,6 +721,16 @@ int launch_gather_kv(const ma_kv& kv, int B, int H, int D, const int64_t* idx, i
                      int64_t si1, void* out_k, void* out_v, const int64_t sok[3],
                      const int64_t sov[3], int out_dtype, cudaStream_t st) {
   if (k == 0) return MA_OK;
+  if (!idx && kv.layout == MA_KV_PACKED_TOKEN && kv.dtype == MA_BF16 && out_dtype == MA_BF16 && D == 128 &&
+      kv.kchan && kv.vgroup == 32 && kv.kgroup == 32 && (kv.nf == 0 || kv.kf)) {
+    // the whole token-mode prefix: the contiguous unpack
+    int gx = (k + kUnpackTok - 1) / kUnpackTok;
+    if (gx > 8) gx = (gx + 3) / 4;   // each CTA takes about four 64-slot rows
+    dim3 ugrid(gx, B * H);
+    unpack_token_kernel<<<ugrid, 256, 0, st>>>(kv, H, k, (__nv_bfloat16*)out_k, (__nv_bfloat16*)out_v, sok[0], sok[1],
+                                               sok[2], sov[0], sov[1], sov[2]);
+    return cudaGetLastError() == cudaSuccess ? MA_OK : MA_ERR_CUDA;
+  }
   dim3 grid((k + kGatherTok - 1) / kGatherTok, B * H);
   if (out_dtype == MA_F32) {
     gather_kv_kernel<float><<<grid, 256, 0, st>>>(kv, H, D, idx, k, si0, si1, (float*)out_k,

@@ -31,7 +31,7 @@ from .kernels.ops import gather_packed_kv, select_topk_indices
 from .kernels.splitk import prefix_scores, splitk_attention
 from .layouts import Prefix, as_prefix, kv_descriptor
 
-__all__ = ["Step0Result", "fast_step0", "gather_read_set", "compact_attention", "probe_attention", "value_score",
+__all__ = ["Step0Result", "fast_step0", "unpacked_prefix", "gather_read_set", "compact_attention", "probe_attention", "value_score",
            "value_score_prefix", "lookahead_survivors"]
 
 
@@ -47,7 +47,7 @@ class Step0Result:
 def fast_step0(query: torch.Tensor, prefix, current_key: torch.Tensor, current_value: torch.Tensor, *,
                query_indices, topk: int, value_aware: bool = True, scaling: float | None = None,
                select: bool = True, want_mass: bool = False, gather: bool = False,
-               compact_out: tuple[torch.Tensor, torch.Tensor] | None = None) -> Step0Result:
+               compact_out: tuple[torch.Tensor, torch.Tensor] | None = None, unpack: bool = True) -> Step0Result:
     """Step 0 of one layer: attention output, mass, score and the read set (session.py:1403-1454).
 
     The read set is the top min(topk, live) slots by score (value_aware) or mass, dead
@@ -55,8 +55,15 @@ def fast_step0(query: torch.Tensor, prefix, current_key: torch.Tensor, current_v
     K/V rows (dequantized to the query dtype) into a compact dense cache for the
     sub-steps, optionally into the caller's buffers compact_out = (key, value), each
     [B, Hkv, >= k, D] (the session's state.key / state.value).
+
+    unpack=True: a packed (k4v4) prefix is dequantized once into a contiguous bf16 copy
+    (a per-device scratch) that the attention, scoring and gather passes then read, as the
+    reference's pass 1 unpacks it (splitk.py:465-480; session.py:1438-1441 gathers from
+    that read); the copy keeps the prefix's mask and lengths.
     """
     prefix = as_prefix(prefix)
+    if unpack and prefix.nq > 0 and query.dtype == torch.bfloat16:
+        prefix = unpacked_prefix(prefix, query.shape[0], current_key.shape[1], query.shape[3])
     if prefix.n == 0:
         out, _ = splitk_attention(query, prefix, current_key, current_value, scaling=scaling)
         return Step0Result(out, None, None, None)
@@ -77,6 +84,21 @@ def fast_step0(query: torch.Tensor, prefix, current_key: torch.Tensor, current_v
     if select and gather:
         compact = gather_read_set(prefix, idx, dtype=query.dtype, out=compact_out)
     return Step0Result(out, idx, mass, score, compact)
+
+
+def unpacked_prefix(prefix, batch: int, heads: int, head_dim: int) -> Prefix:
+    """The prefix dequantized into contiguous bf16 [B, Hkv, n, D] K/V held in a per-device
+    scratch (reused by the next call), with the prefix's mask and lengths."""
+    from .kernels.splitk import dequantize_prefix
+
+    prefix = as_prefix(prefix)
+    n = prefix.n
+    dev = (prefix.kq if prefix.nq else prefix.kf).device
+    nbytes = batch * heads * n * head_dim * 2
+    kb = _lib.workspace(dev, "unpack_k", nbytes)[:nbytes].view(torch.bfloat16).view(batch, heads, n, head_dim)
+    vb = _lib.workspace(dev, "unpack_v", nbytes)[:nbytes].view(torch.bfloat16).view(batch, heads, n, head_dim)
+    dequantize_prefix(prefix, batch, heads, head_dim, out=(kb, vb))
+    return Prefix(kf=kb, vf=vb, nf=n, mask=prefix.mask, lens=prefix.lens)
 
 
 def gather_read_set(prefix, indices: torch.Tensor, *, dtype: torch.dtype = torch.bfloat16,

@@ -105,18 +105,25 @@ def prefix_scores(query, prefix, stats, q_rows, *, value: bool, scaling=None, **
     return mass, score
 
 
-def dequantize_prefix(prefix, b: int, hkv: int, d: int, dtype=torch.bfloat16, **_tuning):
-    """The whole prefix as contiguous [B, Hkv, n, D] tensors (splitk.py:465-480)."""
-    from .ops import gather_packed_kv
-
+def dequantize_prefix(prefix, b: int, hkv: int, d: int, dtype=torch.bfloat16, *, out=None, **_tuning):
+    """The whole prefix as contiguous [B, Hkv, n, D] tensors (splitk.py:465-480): every slot
+    dequantized (packed part) or copied (dense tail) in one launch; slots past lens[b] or on
+    a bad page are zeros. out = (key, value) buffers of that shape (optional)."""
+    lib = _lib.lib()
     prefix = as_prefix(prefix)
     n = prefix.n
     dev = (prefix.kq if prefix.nq else prefix.kf).device
-    ko = torch.empty((b, hkv, n, d), device=dev, dtype=dtype)
-    vo = torch.empty_like(ko)
+    if out is not None:
+        ko, vo = out
+    else:
+        ko = torch.empty((b, hkv, n, d), device=dev, dtype=dtype)
+        vo = torch.empty_like(ko)
     if n == 0:
         return ko, vo
-    idx = torch.arange(n, device=dev, dtype=torch.int64).expand(b, hkv, n)
     unmasked = Prefix(**{s: getattr(prefix, s) for s in Prefix.__slots__})
     unmasked.mask = None
-    return gather_packed_kv(unmasked, idx, dtype=dtype, out_key=ko, out_value=vo)
+    desc = kv_descriptor(unmasked, batch=b, heads=hkv, head_dim=d)
+    _lib.check("ma_gather_kv", lib.ma_gather_kv(
+        desc.kv, b, hkv, d, None, n, None, ko.data_ptr(), vo.data_ptr(), _lib.i64(*ko.stride()[:3]),
+        _lib.i64(*vo.stride()[:3]), _lib.dtype_code(ko.dtype), _lib.stream_handle(dev)))
+    return ko, vo
