@@ -62,9 +62,9 @@ CONFIGS = {
                           "64-slot pages (shuffled pool), sequences sharded across ranks; step 0 + 3 sub-steps"),
 }
 METRIC = "µs per block-step select+attend; achieved HBM GB/s vs peak; tokens/s at 1/2/4/8 GPU"
-# DRAM bytes per launch of the step-0 attention kernel, from the ncu captures summarized in
-# profiles/attn_partial_tc_cfg2_step0.md and profiles/attn_partial_tc_cfg3_packed.md
-ATTN_TRAFFIC_BYTES = {"cfg2": 17_158_912, "cfg3": 5_673_728}
+# DRAM bytes (read + write) per launch of the step-0 attention kernel, from the ncu captures
+# summarized in profiles/attn_partial_fa_cfg2.md and profiles/attn_partial_fa_cfg4_step0.md
+ATTN_TRAFFIC_BYTES = {"cfg2": 17_140_224, "cfg4": 274_293_248}
 
 
 def parse_args():
@@ -77,6 +77,9 @@ def parse_args():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-sample-layers", type=int, default=2)
+    ap.add_argument("--layers", type=int, default=0,
+                    help="override the config's layer count (profiling captures on a small device footprint; "
+                         "the JSON line records it and is not the config's headline number)")
     return ap.parse_args()
 
 
@@ -392,10 +395,11 @@ def algorithmic_bytes(cfg: dict, share: dict) -> dict:
     q = B * Hq * T * D * 2
     cur = 2 * B * H * T * D * 2
     step0 = sum(lens) * H * bt + kchan + 2 * q + cur                # prefix K/V, Q, out, current K/V
-    sub = B * H * k * (bt + 8) + kchan + 2 * q + cur                # read set K/V + indices
+    gather = B * H * k * (bt + 8 + 2 * D * 2) + kchan               # read set K/V + indices -> compact bf16
+    sub = B * H * k * 2 * D * 2 + 2 * q + cur                       # the compact bf16 cache, Q, out, block K/V
     ret = (sum(lens) * H * bt + kchan) if cfg["retention"] else 0   # the probe re-reads the live set
-    return dict(step0_layer=step0, substep_layer=sub,
-                block_step=L * (step0 + (cfg["substeps"] - 1) * sub), retention=L * ret)
+    return dict(step0_layer=step0, gather_layer=gather, substep_layer=sub,
+                block_step=L * (step0 + gather + (cfg["substeps"] - 1) * sub), retention=L * ret)
 
 
 def step0_flops(cfg: dict, share: dict) -> float:
@@ -547,6 +551,7 @@ def run_ours(args):
     import torch.distributed as dist
 
     import maskahead_b200
+    from maskahead_b200.hotpath import unpacked_prefix
     from maskahead_b200.kernels import splitk_attention
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -558,7 +563,9 @@ def run_ours(args):
         import datetime
         dist.init_process_group("nccl", device_id=dev, timeout=datetime.timedelta(seconds=120))
     maskahead_b200.load_library()
-    c = CONFIGS[args.config]
+    c = dict(CONFIGS[args.config])
+    if args.layers > 0:
+        c["L"] = args.layers
     share = rank_share(c, rank, world)
     seed = c["seed"] + (rank if c["scaling"] == "weak" else 0) * 1000 + share["head0"]
     wl = Workload(c, dev, seed, share, world)
@@ -614,14 +621,19 @@ def run_ours(args):
     hbm_peak, tf_peak, peak_kind = peaks()
     g0 = torch.cuda.CUDAGraph()
     side.wait_stream(stream)
+    def step0_attention(layer):
+        # what fast_step0 runs: a packed prefix is unpacked to bf16 first
+        pre = wl.prefix(layer)
+        if pre.nq > 0:
+            pre = unpacked_prefix(pre, wl.B, wl.H, c["D"])
+        splitk_attention(wl.Q[layer, 0], pre, wl.KC[layer, 0], wl.VC[layer, 0], scaling=wl.scale, want_prefix=True)
+
     with torch.cuda.stream(side):
         for layer in range(c["L"]):   # warm the workspaces outside the capture
-            splitk_attention(wl.Q[layer, 0], wl.prefix(layer), wl.KC[layer, 0], wl.VC[layer, 0],
-                             scaling=wl.scale, want_prefix=True)
+            step0_attention(layer)
         with torch.cuda.graph(g0, stream=side):
             for layer in range(c["L"]):
-                splitk_attention(wl.Q[layer, 0], wl.prefix(layer), wl.KC[layer, 0], wl.VC[layer, 0],
-                                 scaling=wl.scale, want_prefix=True)
+                step0_attention(layer)
     stream.wait_stream(side)
     for _ in range(3):
         g0.replay()
@@ -714,15 +726,18 @@ def run_ours(args):
         "warmup": args.warmup, "ms_per_step": ms_step, "us_per_block_step": ms_step * 1e3,
         "higher_is_better": True, "scaling": c["scaling"], "vs_baseline": None, "dtype": "bf16",
         "data": "synthetic (seeded N(0,1) K/V/Q, random-init; no model weights)",
-        "config": {"workload": c["workload"], "global_batch": seqs_job, "seq_len": c["n"],
+        "config": {"workload": c["workload"] + (f" [layers overridden: {c['L']}]" if args.layers > 0 else ""),
+                   "global_batch": seqs_job, "seq_len": c["n"],
                    "parallelism": parallelism, "l2": "inputs larger than L2 (the per-step cache exceeds 126 MB)",
                    "timing": timing},
-        "roofline": {"kernel": "step-0 attention (attn_partial_tc + attn_combine) per layer", "bound": "hbm",
+        "roofline": {"kernel": ("step-0 attention per layer: attn_partial_fa (merge fused)" if c["kv"] == "bf16" else
+                                "step-0 attention per layer: unpack of the packed prefix + attn_partial_fa"),
+                     "bound": "hbm",
                      "achieved": achieved, "peak": hbm_peak, "unit": "GB/s", "frac": achieved / hbm_peak,
                      "traffic": ATTN_TRAFFIC_BYTES.get(c["name"]), "peak_kind": f"{peak_kind} burst",
-                     "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum of attn_partial_tc, "
-                                       "profiles/attn_partial_tc_cfg2_step0.md (cfg2), "
-                                       "profiles/attn_partial_tc_cfg3_packed.md (cfg3)",
+                     "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum of attn_partial_fa, "
+                                       "profiles/attn_partial_fa_cfg2.md (cfg2), profiles/attn_partial_fa_cfg4_step0.md "
+                                       "(cfg4)",
                      "us_per_launch": ms_attn * 1e3, "tensor_tflops": tflops, "tensor_frac": tflops / tf_peak,
                      "bytes_per_launch": ab["step0_layer"]},
         "algorithmic_bytes_per_step": step_bytes,
