@@ -213,6 +213,36 @@ __host__ __device__ inline size_t partials_bytes(int BH, int S, int Rp, int D, b
 // ----------------------------------------------------------------------------------
 // Warp / block helpers
 // ----------------------------------------------------------------------------------
+// ------------------------------------------------------------- thread-block clusters
+// Rank within the cluster, the cluster-wide barrier (release / acquire), and distributed
+// shared memory: the address of a shared variable in CTA `rank` of the cluster, and
+// 32-bit atomics, loads and stores through it.
+__device__ __forceinline__ uint32_t cluster_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;\n" : "=r"(r));
+  return r;
+}
+__device__ __forceinline__ void cluster_sync() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\nbarrier.cluster.wait.acquire.aligned;\n" ::: "memory");
+}
+// address of this shared variable in CTA `rank` of the cluster
+__device__ __forceinline__ uint32_t peer_addr(const void* p, uint32_t rank) {
+  uint32_t a;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;\n" : "=r"(a) : "r"(static_cast<uint32_t>(__cvta_generic_to_shared(p))), "r"(rank));
+  return a;
+}
+__device__ __forceinline__ void peer_add(uint32_t addr, uint32_t v) {
+  asm volatile("red.shared::cluster.add.u32 [%0], %1;\n" ::"r"(addr), "r"(v) : "memory");
+}
+__device__ __forceinline__ uint32_t peer_ld(uint32_t addr) {
+  uint32_t v;
+  asm volatile("ld.shared::cluster.u32 %0, [%1];\n" : "=r"(v) : "r"(addr) : "memory");
+  return v;
+}
+__device__ __forceinline__ void peer_st(uint32_t addr, uint32_t v) {
+  asm volatile("st.shared::cluster.u32 [%0], %1;\n" ::"r"(addr), "r"(v) : "memory");
+}
+
 __device__ __forceinline__ float warp_sum(float v) {
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);

@@ -309,32 +309,6 @@ select_topk_reg(const float* __restrict__ score, int H, int n, int64_t ss0, int6
 // the hardware co-schedules; every CTA takes the same barriers in the same order.
 constexpr int kSelCluster = 8;
 
-__device__ __forceinline__ uint32_t cluster_rank() {
-  uint32_t r;
-  asm volatile("mov.u32 %0, %%cluster_ctarank;\n" : "=r"(r));
-  return r;
-}
-__device__ __forceinline__ void cluster_sync() {
-  asm volatile("barrier.cluster.arrive.release.aligned;\nbarrier.cluster.wait.acquire.aligned;\n" ::: "memory");
-}
-// address of this shared variable in CTA `rank` of the cluster
-__device__ __forceinline__ uint32_t peer_addr(const void* p, uint32_t rank) {
-  uint32_t a;
-  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;\n" : "=r"(a) : "r"(static_cast<uint32_t>(__cvta_generic_to_shared(p))), "r"(rank));
-  return a;
-}
-__device__ __forceinline__ void peer_add(uint32_t addr, uint32_t v) {
-  asm volatile("red.shared::cluster.add.u32 [%0], %1;\n" ::"r"(addr), "r"(v) : "memory");
-}
-__device__ __forceinline__ uint32_t peer_ld(uint32_t addr) {
-  uint32_t v;
-  asm volatile("ld.shared::cluster.u32 %0, [%1];\n" : "=r"(v) : "r"(addr) : "memory");
-  return v;
-}
-__device__ __forceinline__ void peer_st(uint32_t addr, uint32_t v) {
-  asm volatile("st.shared::cluster.u32 [%0], %1;\n" ::"r"(addr), "r"(v) : "memory");
-}
-
 template <int PER>
 __global__ void __launch_bounds__(kSelThreads)
 select_topk_cluster(const float* __restrict__ score, int H, int n, int64_t ss0, int64_t ss1,
