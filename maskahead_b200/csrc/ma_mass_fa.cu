@@ -34,6 +34,7 @@ using namespace tc;
 
 constexpr int kSumWarps = 8;
 constexpr int kSumThreads = kSumWarps * 32;
+static_assert(kSumThreads == 256, "one selection row per sum thread");
 constexpr int kThreads = kSumThreads + 32;
 constexpr int kTile = 128;                   // slots per tile (= M = TMEM lanes)
 constexpr int kD = 128;
@@ -90,10 +91,9 @@ __global__ void __launch_bounds__(kThreads, 1) prefix_mass_fa(const __grid_const
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sQ = smem;                      // K-major [2 d blocks][Npad rows][128 B]
   __shared__ __align__(16) float sNB[kMaxRows];  // per selection row: -B_r (-inf: no contribution)
-  __shared__ int sRowT[kMaxRows];                // block position of selection row r (-1: none)
   __shared__ float sHalf[2][kTile];
   __shared__ __align__(16) float sA[kTile];
-  __shared__ float sTot[kD + 1];
+  __shared__ float sTot[2][kD + 1];
   __shared__ uint32_t s_taddr;
   __shared__ __align__(8) uint64_t kfull[kMaxSlots], vfull[kMaxSlots], s_full[2], s_free[2], v_free[kMaxSlots],
       wfull[kMaxSlots], wfree[kMaxSlots], mbar_fin;
@@ -146,36 +146,42 @@ __global__ void __launch_bounds__(kThreads, 1) prefix_mass_fa(const __grid_const
     s_abort = 0;
     s_wait_ok = 1;
     asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
+    // the first K and V tiles start loading now, while the sum warps stage Q
+    pdl_wait();   // with a programmatic launch, the cache may come from the kernel before
+    const uint64_t pol_k = tma::policy_evict_first(), pol_v = tma::policy_evict_last();
+    for (int i = 0; i < nK && i < ntiles; ++i)
+      tile_load(&A.kmap, b, h, begin + i * kTile, sSlot + i * kTileBytes, &kfull[i], pol_k);
+    if (centre)
+      for (int i = 0; i < nV && i < ntiles; ++i)
+        tile_load(&A.vmap, b, h, begin + i * kTile, sSlot + (nK + i) * kTileBytes, &vfull[i], pol_v);
   }
   if (sum_warp) {
     pdl_wait();   // m_p, l_p (and with a programmatic launch, the outputs) of the kernel before
-    // selection rows r2 = g*T2 + i -> query row (h*G + g, q_rows[i]) and B_r
-    for (int rr = threadIdx.x; rr < kMaxRows; rr += kSumThreads) {
+    // one selection row per thread (kSumThreads == kMaxRows): r2 = g*T2 + i -> query row
+    // (h*G + g, q_rows[i]), -B_r, and the row's query into the K-major SW128 Q tile of Npad
+    // rows (zeros for padding rows)
+    {
+      const int rr = threadIdx.x;
       const int g = rr / A.T2;
       const int t = rr < R2 ? A.q_rows[rr - g * A.T2] : -1;
       const bool ok = t >= 0 && t < T;
+      if (rr < Npad) {
+        const __nv_bfloat16* qrow = reinterpret_cast<const __nv_bfloat16*>(A.q.q) + (int64_t)b * A.q.sq[0] +
+                                    (int64_t)(h * G + g) * A.q.sq[1] + (int64_t)(ok ? t : 0) * A.q.sq[2];
+#pragma unroll
+        for (int ch = 0; ch < kD / 8; ++ch) {
+          uint8_t* dst = sQ + kmajor_off(rr, ch, Npad);
+          if (ok) cp_async16(smem_addr(dst), qrow + ch * 8, true);
+          else *reinterpret_cast<uint4*>(dst) = make_uint4(0, 0, 0, 0);
+        }
+      }
       float Bv = INFINITY;   // exp2(s - inf) = 0: no contribution
       if (ok) {
         const int64_t ri = (int64_t)bh * G * T + (int64_t)g * T + t;
         const float L = A.l_p[ri];
         if (L > 0.f) Bv = fmaf(A.m_p[ri], kLog2e, log2f(L));
       }
-      sRowT[rr] = ok ? t : -1;
       sNB[rr] = -Bv;
-    }
-    sum_sync();
-    // the selection rows' queries, K-major SW128 with Npad rows (zeros for padding)
-    const __nv_bfloat16* qp = reinterpret_cast<const __nv_bfloat16*>(A.q.q);
-    for (int c = threadIdx.x; c < Npad * (kD / 8); c += kSumThreads) {
-      const int rr = c / (kD / 8), ch = c % (kD / 8);
-      const int t = sRowT[rr];
-      uint8_t* dst = sQ + kmajor_off(rr, ch, Npad);
-      if (t >= 0) {
-        const int g = rr / A.T2;
-        cp_async16(smem_addr(dst), qp + (int64_t)b * A.q.sq[0] + (int64_t)(h * G + g) * A.q.sq[1] + (int64_t)t * A.q.sq[2] + ch * 8, true);
-      } else {
-        *reinterpret_cast<uint4*>(dst) = make_uint4(0, 0, 0, 0);
-      }
     }
     cp_async_commit();
     cp_async_wait<0>();
@@ -194,15 +200,11 @@ __global__ void __launch_bounds__(kThreads, 1) prefix_mass_fa(const __grid_const
   if (!sum_warp) {
     // ------------------------------------------------------------ producer / MMA warp
     if (lane == 0) {
-      pdl_wait();
       bool ok = true;
-      int kIss = 0, kObs = 0, vIss = 0, vObs = 0, sN = 0, sDone = 0, sfObs = 0, vfObs = 0;
+      // the first min(nK, ntiles) K and min(nV, ntiles) V tiles were issued at setup
+      int kIss = min(nK, ntiles), kObs = 0, vIss = centre ? min(nV, ntiles) : 0, vObs = 0;
+      int sN = 0, sDone = 0, sfObs = 0, vfObs = 0;
       const uint64_t pol_k = tma::policy_evict_first(), pol_v = tma::policy_evict_last();
-      for (; kIss < nK && kIss < ntiles; ++kIss)
-        tile_load(&A.kmap, b, h, begin + kIss * kTile, sSlot + kIss * kTileBytes, &kfull[kIss], pol_k);
-      if (centre)
-        for (; vIss < nV && vIss < ntiles; ++vIss)
-          tile_load(&A.vmap, b, h, begin + vIss * kTile, sSlot + (nK + vIss) * kTileBytes, &vfull[vIss], pol_v);
       const int vTiles = centre ? ntiles : 0;
       const uint32_t idesc = idesc_bf16(kTile, Npad, false, false);
       const uint64_t kdesc = smem_desc(smem_addr(sSlot), 16, 1024);
@@ -413,20 +415,27 @@ __global__ void __launch_bounds__(kThreads, 1) prefix_mass_fa(const __grid_const
   __syncthreads();
   if (sLast) {
     __threadfence();
-    if (threadIdx.x <= kD) {
-      const float* base = A.part + (int64_t)bh * gridDim.x * (kD + 1) + threadIdx.x;
+    // two threads per column, each over one half of the CTAs in CTA order, up to 32 loads
+    // in flight; the halves are added in order
+    if (threadIdx.x < 2 * (kD + 1)) {
+      const int col = threadIdx.x % (kD + 1), hh = threadIdx.x / (kD + 1);
+      const int P = (int)gridDim.x, mid = (P + 1) / 2;
+      const int p0 = hh ? mid : 0, p1 = hh ? P : mid;
+      const float* base = A.part + (int64_t)bh * P * (kD + 1) + col;
       float tot = 0.f;
-      for (unsigned t0 = 0; t0 < gridDim.x; t0 += 16) {
-        float v[16];
+      for (int t0 = p0; t0 < p1; t0 += 32) {
+        float v[32];
 #pragma unroll
-        for (int i = 0; i < 16; ++i) v[i] = t0 + i < gridDim.x ? __ldcg(base + (int64_t)(t0 + i) * (kD + 1)) : 0.f;
+        for (int i = 0; i < 32; ++i) v[i] = t0 + i < p1 ? __ldcg(base + (int64_t)(t0 + i) * (kD + 1)) : 0.f;
 #pragma unroll
-        for (int i = 0; i < 16; ++i) tot += v[i];   // CTA order
+        for (int i = 0; i < 32; ++i) tot += v[i];   // CTA order
       }
-      sTot[threadIdx.x] = tot;
+      sTot[hh][col] = tot;
     }
     __syncthreads();
-    if (threadIdx.x < kD) A.centre[(int64_t)bh * kD + threadIdx.x] = sTot[threadIdx.x] / fmaxf(sTot[kD], 1e-12f);
+    if (threadIdx.x < kD)
+      A.centre[(int64_t)bh * kD + threadIdx.x] =
+          (sTot[0][threadIdx.x] + sTot[1][threadIdx.x]) / fmaxf(sTot[0][kD] + sTot[1][kD], 1e-12f);
     if (threadIdx.x == 0) A.sync[bh].x = 0u;
     __threadfence();
     __syncthreads();
@@ -447,7 +456,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefix_mass_fa(const __grid_const
         atomicExch(A.err, 1);
         break;
       }
-      __nanosleep(256);
+      __nanosleep(64);
     }
   }
   __syncthreads();
