@@ -174,6 +174,21 @@ __global__ void __launch_bounds__(kThreads, 1) attn_partial_fa(const __grid_cons
     mbar_init(&mbar_fin, 1);
     s_abort = 0;
     asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
+    // the queries and the first K and V tiles start loading now, before the TMEM
+    // allocation and the setup barrier
+    pdl_wait();   // with a programmatic launch, the inputs may come from the kernel before
+    const CUtensorMap* km = is_cur ? &A.ckmap : &A.kmap;
+    const CUtensorMap* vm = is_cur ? &A.cvmap : &A.vmap;
+    tma::expect_tx(&q_full, (uint32_t)kQBytes);
+    if (A.q_tall) {   // 128 consecutive positions of one query head
+      tma::load_4d(sQ, &A.qmap, 0, r0 % T, h * G + r0 / T, b, &q_full);
+      tma::load_4d(sQ + kQBlock, &A.qmap, 64, r0 % T, h * G + r0 / T, b, &q_full);
+    } else {          // 128 / T whole query heads
+      tma::load_4d(sQ, &A.qmap, 0, 0, h * G + r0 / T, b, &q_full);
+      tma::load_4d(sQ + kQBlock, &A.qmap, 64, 0, h * G + r0 / T, b, &q_full);
+    }
+    for (int i = 0; i < kKSlots && i < ntiles; ++i) tma_tile(km, b, h, begin + i * kBN, sKs + i * kKVBytes, &kfull[i]);
+    for (int i = 0; i < kVSlots && i < ntiles; ++i) tma_tile(vm, b, h, begin + i * kBN, sVs + i * kKVBytes, &vfull[i]);
   }
   if (warp == 0) tmem_alloc(&s_taddr, kTmemCols);
   fence_before_sync();
@@ -193,24 +208,12 @@ __global__ void __launch_bounds__(kThreads, 1) attn_partial_fa(const __grid_cons
       // takes its next tile once the S it held was consumed (its P.V issued), a V slot once
       // its P.V completed. Each barrier has at most one completed but unobserved phase, so
       // the parity tests are unambiguous.
-      pdl_wait();   // with a programmatic launch, the inputs may come from the kernel before
       bool ok = true;
-      int kIss = 0, kObs = 0, vIss = 0, vObs = 0;   // tiles issued / seen loaded
+      // the queries and the first min(3, ntiles) K and V tiles were issued at setup
+      int kIss = min(kKSlots, ntiles), kObs = 0, vIss = min(kVSlots, ntiles), vObs = 0;
       int sN = 0, pN = 0, oD = 0;                   // S issued, P.V issued, P.V seen complete
       const CUtensorMap* km = is_cur ? &A.ckmap : &A.kmap;
       const CUtensorMap* vm = is_cur ? &A.cvmap : &A.vmap;
-      tma::expect_tx(&q_full, (uint32_t)kQBytes);
-      if (A.q_tall) {   // 128 consecutive positions of one query head
-        tma::load_4d(sQ, &A.qmap, 0, r0 % T, h * G + r0 / T, b, &q_full);
-        tma::load_4d(sQ + kQBlock, &A.qmap, 64, r0 % T, h * G + r0 / T, b, &q_full);
-      } else {          // 128 / T whole query heads
-        tma::load_4d(sQ, &A.qmap, 0, 0, h * G + r0 / T, b, &q_full);
-        tma::load_4d(sQ + kQBlock, &A.qmap, 64, 0, h * G + r0 / T, b, &q_full);
-      }
-      for (; kIss < kKSlots && kIss < ntiles; ++kIss)
-        tma_tile(km, b, h, begin + kIss * kBN, sKs + kIss * kKVBytes, &kfull[kIss]);
-      for (; vIss < kVSlots && vIss < ntiles; ++vIss)
-        tma_tile(vm, b, h, begin + vIss * kBN, sVs + vIss * kKVBytes, &vfull[vIss]);
       const bool q_ok = mbar_wait(&q_full, 0);
       ok = q_ok;
       const uint32_t idS = idesc_bf16(kRowTile, kBN, false, false);
