@@ -343,6 +343,11 @@ int ma_value_score(const ma_kv* kv, int B, int H, int D, const float* a, const i
   const int n = kv->nq + kv->nf;
   if (!workspace || workspace_bytes < value_score_ws_bytes(B, H, n, D)) return MA_ERR_WORKSPACE;
   if ((reinterpret_cast<uintptr_t>(workspace) & 255) != 0) return MA_ERR_WORKSPACE;
+  if (!fa_disabled()) {
+    rc = launch_value_score_fa(*kv, B, H, D, a, sa[0], sa[1], score, sscore[0], sscore[1], workspace,
+                               (cudaStream_t)stream);
+    if (rc != MA_ERR_UNSUPPORTED) return rc;
+  }
   return launch_value_score(*kv, B, H, D, a, sa[0], sa[1], score, sscore[0], sscore[1], workspace,
                             (cudaStream_t)stream);
 }

@@ -86,6 +86,11 @@ int launch_prefix_mass_fa(const ma_rows& q, const ma_kv& kv, int H, const int32_
                           const float* l_p, float scale, float* mass, int64_t sm0, int64_t sm1, float* score,
                           int64_t ss0, int64_t ss1, const ValueWs& w, bool want_centre, bool* fused, cudaStream_t st);
 
+// a_j ||v_j - c|| from given a_j over a TMA-fed dense bf16 V (the value pass of
+// prefix_mass_fa); MA_ERR_UNSUPPORTED when V or the launch does not qualify.
+int launch_value_score_fa(const ma_kv& kv, int B, int H, int D, const float* a, int64_t sa0, int64_t sa1,
+                          float* score, int64_t ss0, int64_t ss1, void* ws, cudaStream_t st);
+
 // ma_select.cu
 int launch_select_topk(const float* score, int B, int H, int n, int64_t ss0, int64_t ss1,
                        const uint8_t* mask, const int32_t* lens, int k, int64_t* indices, float* values,

@@ -69,6 +69,7 @@ struct __align__(64) Args {
   float scale;
   int H, T2, slots_per_cta, want_centre;
   int nK, nV;               // K ring and V ring slots (phase 2 streams V through nK + nV)
+  int given;                // a_j given in `mass` (value score only: no K, no exponentials)
 };
 
 __device__ __forceinline__ void sum_sync() { asm volatile("bar.sync 1, %0;\n" ::"r"(kSumThreads) : "memory"); }
@@ -124,6 +125,8 @@ __global__ void __launch_bounds__(kThreads, 1) prefix_mass_fa(const __grid_const
   const float inv_rows = 1.f / (float)R2;
   const float c2 = A.scale * kLog2e;
   const bool centre = A.want_centre != 0;
+  const bool given = A.given != 0;
+  const int kTiles = given ? 0 : ntiles;     // tiles that need K and S^T
 
   // the head's centre generation before this CTA arrives (the last CTA advances it)
   unsigned gen0 = 0;
@@ -149,13 +152,15 @@ __global__ void __launch_bounds__(kThreads, 1) prefix_mass_fa(const __grid_const
     // the first K and V tiles start loading now, while the sum warps stage Q
     pdl_wait();   // with a programmatic launch, the cache may come from the kernel before
     const uint64_t pol_k = tma::policy_evict_first(), pol_v = tma::policy_evict_last();
-    for (int i = 0; i < nK && i < ntiles; ++i)
+    for (int i = 0; i < nK && i < kTiles; ++i)
       tile_load(&A.kmap, b, h, begin + i * kTile, sSlot + i * kTileBytes, &kfull[i], pol_k);
     if (centre)
       for (int i = 0; i < nV && i < ntiles; ++i)
         tile_load(&A.vmap, b, h, begin + i * kTile, sSlot + (nK + i) * kTileBytes, &vfull[i], pol_v);
   }
-  if (sum_warp) {
+  if (sum_warp && given) {
+    pdl_wait();   // a (and with a programmatic launch, the outputs) of the kernel before
+  } else if (sum_warp) {
     pdl_wait();   // m_p, l_p (and with a programmatic launch, the outputs) of the kernel before
     // one selection row per thread (kSumThreads == kMaxRows): r2 = g*T2 + i -> query row
     // (h*G + g, q_rows[i]), -B_r, and the row's query into the K-major SW128 Q tile of Npad
@@ -202,7 +207,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefix_mass_fa(const __grid_const
     if (lane == 0) {
       bool ok = true;
       // the first min(nK, ntiles) K and min(nV, ntiles) V tiles were issued at setup
-      int kIss = min(nK, ntiles), kObs = 0, vIss = centre ? min(nV, ntiles) : 0, vObs = 0;
+      int kIss = min(nK, kTiles), kObs = 0, vIss = centre ? min(nV, ntiles) : 0, vObs = 0;
       int sN = 0, sDone = 0, sfObs = 0, vfObs = 0;
       const uint64_t pol_k = tma::policy_evict_first(), pol_v = tma::policy_evict_last();
       const int vTiles = centre ? ntiles : 0;
@@ -213,7 +218,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefix_mass_fa(const __grid_const
       uint64_t t_idle = 0;
       bool armed = false;
       int spins = 0;
-      while (ok && (sN < ntiles || kIss < ntiles || vIss < vTiles)) {
+      while (ok && (sN < kTiles || kIss < kTiles || vIss < vTiles)) {
         bool progress = false;
         if (kObs < kIss && mbar_test(&kfull[kObs % nK], (uint32_t)(kObs / nK) & 1u)) {
           ++kObs;
@@ -237,7 +242,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefix_mass_fa(const __grid_const
         }
         // S^T(t) = K(t) Q^T into buffer t&1, once K(t) is in and the sum warps released
         // the buffer's previous tile
-        if (sN < ntiles && kObs > sN && sfObs >= sN - 1 && sDone >= sN - 1) {
+        if (sN < kTiles && kObs > sN && sfObs >= sN - 1 && sDone >= sN - 1) {
           fence_after_sync();
           const uint64_t ad0 = kdesc + (uint64_t)((sN % nK) * (kTileBytes >> 4));
           const uint32_t d = taddr + (sN & 1) * 256;
@@ -250,7 +255,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefix_mass_fa(const __grid_const
           progress = true;
         }
         // K slot of tile kIss - nK is free once its S^T completed
-        if (kIss < ntiles && sDone > kIss - nK) {
+        if (kIss < kTiles && sDone > kIss - nK) {
           tile_load(&A.kmap, b, h, begin + kIss * kTile, sSlot + (kIss % nK) * kTileBytes, &kfull[kIss % nK], pol_k);
           ++kIss;
           progress = true;
@@ -294,7 +299,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefix_mass_fa(const __grid_const
     // the row chunks are 64 columns, taken alternately by the two warps of a slot quarter;
     // rows past R2 read -inf from sNB, and the columns past Npad of a last partial chunk
     // are zeroed once here (the MMAs never write them), so no chunk needs a bound check
-    if ((Npad & 63) != 0 && ((Npad >> 6) & 1) == chalf) {
+    if (!given && (Npad & 63) != 0 && ((Npad >> 6) & 1) == chalf) {
       const uint32_t z[16] = {0u, 0u, 0u, 0u, 0u, 0u, 0u, 0u, 0u, 0u, 0u, 0u, 0u, 0u, 0u, 0u};
       for (int col = Npad; col < (Npad | 63) + 1; col += 16) {
         tmem_st16(tRow + col, z);
@@ -304,6 +309,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefix_mass_fa(const __grid_const
     }
     for (int t = 0; t < ntiles; ++t) {
       const int j0 = begin + t * kTile;
+      if (!given) {
       if (!mbar_wait(&s_full[t & 1], (uint32_t)(t >> 1) & 1u, kWaitNs)) s_abort = 1;
       fence_after_sync();
       // this thread: slot slot_lane, row chunks chalf, chalf + 2, ...
@@ -338,12 +344,18 @@ __global__ void __launch_bounds__(kThreads, 1) prefix_mass_fa(const __grid_const
       fence_before_sync();
       __syncwarp();
       if (lane == 0) mbar_arrive(&s_free[t & 1]);
+      }
       sum_sync();
       if (threadIdx.x < kTile) {
         const int j = j0 + threadIdx.x;
         const bool live = j < end && kv_live(A.kv, H, b, h, j);
-        const float a = live ? (sHalf[0][threadIdx.x] + sHalf[1][threadIdx.x]) * inv_rows : 0.f;
-        if (j < end) A.mass[(int64_t)b * A.sm0 + (int64_t)h * A.sm1 + j] = a;
+        float a;
+        if (given) {   // the caller's a_j (dead slots 0)
+          a = live ? A.mass[(int64_t)b * A.sm0 + (int64_t)h * A.sm1 + j] : 0.f;
+        } else {
+          a = live ? (sHalf[0][threadIdx.x] + sHalf[1][threadIdx.x]) * inv_rows : 0.f;
+          if (j < end) A.mass[(int64_t)b * A.sm0 + (int64_t)h * A.sm1 + j] = a;
+        }
         sA[threadIdx.x] = a;
       }
       if (centre && !mbar_wait(&vfull[t % nV], (uint32_t)(t / nV) & 1u, kWaitNs)) s_abort = 1;
@@ -372,7 +384,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefix_mass_fa(const __grid_const
   // slots past lens[b]: mass (and score) 0
   if (sum_warp && end < end_all) {
     for (int j = end + threadIdx.x; j < end_all; j += kSumThreads) {
-      A.mass[(int64_t)b * A.sm0 + (int64_t)h * A.sm1 + j] = 0.f;
+      if (!given) A.mass[(int64_t)b * A.sm0 + (int64_t)h * A.sm1 + j] = 0.f;
       if (A.score) A.score[(int64_t)b * A.ss0 + (int64_t)h * A.ss1 + j] = 0.f;
     }
   }
@@ -385,7 +397,8 @@ __global__ void __launch_bounds__(kThreads, 1) prefix_mass_fa(const __grid_const
   if (aborted && threadIdx.x == 0) atomicExch(A.err, 1);
   if (!centre) return;
 
-  // centre partials per slot group, in K slot 0 (drained; V tiles may stay in their slots)
+  // centre partials per slot group, in K slot 0 (drained; V tiles may stay in their slots;
+  // nK >= 1 in every mode)
   float* sRed = reinterpret_cast<float*>(sSlot);           // [16][kD]
   float* sAsum = sRed + 16 * kD;                           // [16]
   // per-CTA centre partial (slot groups summed in order); the last CTA of the head
@@ -631,6 +644,75 @@ int launch_prefix_mass_fa(const ma_rows& q, const ma_kv& kv, int H, const int32_
     }
   }
   return launch_pdl(prefix_mass_fa, grid, dim3(kThreads), smem, st, A) == cudaSuccess ? MA_OK : MA_ERR_CUDA;
+}
+
+int launch_value_score_fa(const ma_kv& kv, int B, int H, int D, const float* a, int64_t sa0, int64_t sa1,
+                          float* score, int64_t ss0, int64_t ss1, void* ws, cudaStream_t st) {
+  const int n = kv.nf;
+  const int BH = B * H;
+  if (!(kv.layout == MA_KV_DENSE && kv.dtype == MA_BF16 && !kv.pages && kv.nq == 0 && D == kD && n > 0))
+    return MA_ERR_UNSUPPORTED;
+  Args A;
+  memset(&A, 0, sizeof(A));
+  if (!tma_map_rows(&A.vmap, kv.vf, B, H, n, kv.svf)) return MA_ERR_UNSUPPORTED;
+  const ValueWs w = carve_value_ws(ws, BH, D);
+  A.kv = kv;
+  A.q.B = B;
+  A.q.Hq = H;   // one "query head" per KV head, one selection row: only the value pass runs
+  A.q.T = 1;
+  A.q.D = D;
+  A.T2 = 1;
+  A.mass = const_cast<float*>(a);   // read only in this mode
+  A.sm0 = sa0;
+  A.sm1 = sa1;
+  A.score = nullptr;
+  A.ss0 = ss0;
+  A.ss1 = ss1;
+  A.part = w.part;
+  A.sync = w.sync;
+  A.centre = w.centre;
+  A.err = w.err;
+  A.H = H;
+  A.want_centre = 1;
+  A.given = 1;
+  // the K ring is unused: one K slot remains as the centre-partial scratch (slot 0, which
+  // must not hold a V tile that phase 2 reads in place), the others hold V
+  const int Npad = 16;
+  int nslots = (kSmemLimit - kStaticSmem - 1024 - Npad * 256) / kTileBytes;
+  if (nslots > kMaxSlots) nslots = kMaxSlots;
+  A.nK = 1;
+  A.nV = nslots - 1;
+  const int smem = 1024 + Npad * 256 + nslots * kTileBytes;
+  const int sms = device_sm_count();
+  int per_head = sms / (BH > 0 ? BH : 1);
+  if (per_head < 1) per_head = 1;
+  int spc = (n + per_head - 1) / per_head;
+  spc = ((spc + kTile - 1) / kTile) * kTile;
+  A.slots_per_cta = spc;
+  dim3 grid((n + spc - 1) / spc, BH);
+  if (cudaFuncSetAttribute(prefix_mass_fa, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
+    return MA_ERR_CUDA;
+  A.score = score;
+  if (grid.x == 1)   // one CTA per head: it reduces its own centre
+    return launch_pdl(prefix_mass_fa, grid, dim3(kThreads), smem, st, A) == cudaSuccess ? MA_OK : MA_ERR_CUDA;
+  int dev = 0, coop = 0, per_sm = 0;
+  if (cudaGetDevice(&dev) == cudaSuccess && cudaDeviceGetAttribute(&coop, cudaDevAttrCooperativeLaunch, dev) == cudaSuccess &&
+      coop && cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, prefix_mass_fa, kThreads, smem) == cudaSuccess &&
+      (long long)grid.x * grid.y <= (long long)per_sm * sms) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeCooperative;
+    attr[0].val.cooperative = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    if (cudaLaunchKernelEx(&cfg, prefix_mass_fa, A) == cudaSuccess) return MA_OK;
+    (void)cudaGetLastError();
+  }
+  return MA_ERR_UNSUPPORTED;
 }
 
 }  // namespace ma
