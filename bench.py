@@ -613,6 +613,12 @@ def run_ours(args):
     torch.cuda.synchronize()
     ms = _max_over_ranks(ms, world, dev)
     ms_step = ms / args.steps
+    # diagnostic: each kind of step on its own (a block-step without / with the retention pass)
+    step_kinds = {}
+    if graphs:
+        for retain, g in sorted(graphs.items()):
+            t = _timed(lambda i: g.replay(), 3, stream) / 3
+            step_kinds["retention" if retain else "plain"] = _max_over_ranks(t, world, dev)
     seqs_job = c["B"] * (world if c["scaling"] == "weak" else 1)
     tokens = c["T"] * seqs_job
     value = tokens / (ms_step / 1e3)
@@ -740,6 +746,7 @@ def run_ours(args):
                                        "(cfg4)",
                      "us_per_launch": ms_attn * 1e3, "tensor_tflops": tflops, "tensor_frac": tflops / tf_peak,
                      "bytes_per_launch": ab["step0_layer"]},
+        "ms_per_step_kind": step_kinds,
         "algorithmic_bytes_per_step": step_bytes,
         "achieved_step_gbs": step_bytes / (ms_step / 1e3) / 1e9,
         "block_steps_per_s": seqs_job / (ms_step / 1e3),

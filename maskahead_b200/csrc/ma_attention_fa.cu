@@ -69,7 +69,8 @@ struct __align__(64) Args {
   ma_block cur;
   float scale;
   int H, causal_block, q_pos0, c_pos0, n_keys, split_len, nsplit;
-  int q_tall;                   // T >= 128: a row tile is 128 rows of one query head
+  int q_mode;                   // the query tile's boxes: 0 = 128/T whole heads, 1 = 128 rows of
+                                // one head (T % 128 == 0), 2 = four 32-row pieces (T % 32 == 0)
   int tma_out;
   Partials P;
   int* err;
@@ -180,12 +181,18 @@ __global__ void __launch_bounds__(kThreads, 1) attn_partial_fa(const __grid_cons
     const CUtensorMap* km = is_cur ? &A.ckmap : &A.kmap;
     const CUtensorMap* vm = is_cur ? &A.cvmap : &A.vmap;
     tma::expect_tx(&q_full, (uint32_t)kQBytes);
-    if (A.q_tall) {   // 128 consecutive positions of one query head
+    if (A.q_mode == 1) {          // 128 consecutive positions of one query head
       tma::load_4d(sQ, &A.qmap, 0, r0 % T, h * G + r0 / T, b, &q_full);
       tma::load_4d(sQ + kQBlock, &A.qmap, 64, r0 % T, h * G + r0 / T, b, &q_full);
-    } else {          // 128 / T whole query heads
+    } else if (A.q_mode == 0) {   // 128 / T whole query heads
       tma::load_4d(sQ, &A.qmap, 0, 0, h * G + r0 / T, b, &q_full);
       tma::load_4d(sQ + kQBlock, &A.qmap, 64, 0, h * G + r0 / T, b, &q_full);
+    } else {                      // four 32-row pieces, each inside one query head
+      for (int i = 0; i < kRowTile / 32; ++i) {
+        const int rp = r0 + 32 * i;   // rows past R load neighbouring or zero rows: never used
+        tma::load_4d(sQ + i * 32 * 128, &A.qmap, 0, rp % T, h * G + rp / T, b, &q_full);
+        tma::load_4d(sQ + kQBlock + i * 32 * 128, &A.qmap, 64, rp % T, h * G + rp / T, b, &q_full);
+      }
     }
     for (int i = 0; i < kKSlots && i < ntiles; ++i) tma_tile(km, b, h, begin + i * kBN, sKs + i * kKVBytes, &kfull[i]);
     for (int i = 0; i < kVSlots && i < ntiles; ++i) tma_tile(vm, b, h, begin + i * kBN, sVs + i * kKVBytes, &vfull[i]);
@@ -535,8 +542,9 @@ int fa_row_tile() { return kRowTile; }
 bool fa_eligible(const ma_rows& q, const ma_kv& kv, const int64_t* idx, const ma_block& cur, int n_keys) {
   const bool prefix_ok = n_keys == 0 || (kv.layout == MA_KV_DENSE && kv.dtype == MA_BF16 && !idx && !kv.mask &&
                                          !kv.pages);
-  // a row tile is 128 / T whole query heads, or 128 positions of one head
-  const bool rows_ok = q.T > 0 && (q.T <= kRowTile ? kRowTile % q.T == 0 : q.T % kRowTile == 0);
+  // a row tile is 128 / T whole query heads, 128 positions of one head, or four 32-row
+  // pieces (each within one head)
+  const bool rows_ok = q.T > 0 && (kRowTile % q.T == 0 || q.T % 32 == 0);
   return q.dtype == MA_BF16 && q.D == kD && rows_ok && prefix_ok && (n_keys > 0 || cur.Tc > 0);
 }
 
@@ -570,8 +578,9 @@ int launch_attn_partial_fa(const ma_rows& q, const ma_kv& kv, int H, const ma_bl
   {
     const uint64_t dims[4] = {128, (uint64_t)q.T, (uint64_t)q.Hq, (uint64_t)q.B};
     const uint64_t strides[3] = {(uint64_t)q.sq[2] * 2, (uint64_t)q.sq[1] * 2, (uint64_t)q.sq[0] * 2};
-    A.q_tall = q.T >= kRowTile ? 1 : 0;
-    const uint32_t box[4] = {64, (uint32_t)(A.q_tall ? kRowTile : q.T), (uint32_t)(A.q_tall ? 1 : kRowTile / q.T), 1};
+    A.q_mode = (q.T % kRowTile == 0) ? 1 : (kRowTile % q.T == 0) ? 0 : 2;
+    const uint32_t box[4] = {64, (uint32_t)(A.q_mode == 1 ? kRowTile : A.q_mode == 0 ? q.T : 32),
+                             (uint32_t)(A.q_mode == 0 ? kRowTile / q.T : 1), 1};
     if (!make_tma_map_bf16_4d(&A.qmap, q.q, dims, strides, box)) return MA_ERR_UNSUPPORTED;
   }
   const int G = q.Hq / H;

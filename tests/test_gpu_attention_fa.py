@@ -6,8 +6,9 @@ Both kernels are run on the same inputs (``ma_set_attention_kernel``) and compar
 2e-2: bf16 output rounding plus the bf16 P operand of P.V); the prefix-only statistics
 (max, sum, normalized output) are compared the same way. The sizes cover: an empty prefix,
 prefixes shorter than one tile, one key past a tile boundary, several splits, a
-current block longer than one tile, one and two 128-row M tiles, and several row tiles
-(R = G*T > 256).
+current block longer than one tile, one and two 128-row M tiles, several row tiles
+(R = G*T > 256), and query blocks whose length neither divides nor is a multiple of 128
+(T = 96, 160: the row tile is loaded as four 32-row pieces).
 """
 
 from __future__ import annotations
@@ -53,6 +54,9 @@ def _run(which, q, k, v, kc, vc, causal, q_pos0, c_pos0, want_prefix):
     (1, 28, 4, 32, 1100, 32, 32),    # cfg2-like heads, several splits
     (1, 8, 2, 128, 5000, 160, 64),   # current block longer than a tile, R = 512 (two row tiles)
     (1, 4, 4, 256, 2048, 256, 128),  # T = 256: one query head per row tile
+    (1, 16, 4, 96, 3000, 96, 32),    # T = 96 (a block + two probe blocks): 32-row query pieces
+    (2, 4, 4, 96, 700, 96, 32),      # T = 96, one head per group: R = 96 < one row tile
+    (1, 6, 2, 160, 1000, 160, 32),   # T = 160: pieces straddle row tiles, R = 480
 ])
 def test_fa_kernel_matches_oracle_and_tc(B, Hq, H, T, n, Tc, causal):
     gen = torch.Generator().manual_seed(1000 * n + T + Hq)
