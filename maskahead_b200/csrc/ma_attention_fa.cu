@@ -119,14 +119,16 @@ __global__ void __launch_bounds__(kThreads, 1) attn_partial_fa(const __grid_cons
   __shared__ float sPM[2][kRowTile];   // per key half: the row's tile max (fp32, exact)
   __shared__ int sBad[2][4];           // per key half and row quarter: this tile aborts
 
-  const int split = blockIdx.x;
-  const int bh = blockIdx.y;
+  // grid (row tiles, splits, heads): the row tiles of one split run side by side, so the
+  // second and later ones read that split's K/V from L2
+  const int split = blockIdx.y;
+  const int bh = blockIdx.z;
   const int H = A.H;
   const int b = bh / H, h = bh - (bh / H) * H;
   const int T = A.q.T;
   const int G = A.q.Hq / H;
   const int R = G * T;
-  const int r0 = blockIdx.z * kRowTile;
+  const int r0 = blockIdx.x * kRowTile;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const bool softmax_warp = warp < kSoftWarps;
   const int quarter = warp & 3, hf = (warp >> 2) & 1;   // rows 32*quarter.., keys 64*hf.. of a tile
@@ -156,7 +158,7 @@ __global__ void __launch_bounds__(kThreads, 1) attn_partial_fa(const __grid_cons
   if (!row_ok) vis_end = begin;
   const int ntiles = end > begin ? (end - begin + kBN - 1) / kBN : 0;
   const float c2 = A.scale * kLog2e;
-  const int group = bh * gridDim.z + blockIdx.z;
+  const int group = bh * gridDim.x + blockIdx.x;
 
   unsigned gen0 = 0;   // the merge generation, read before this CTA arrives (thread 0)
   if (A.fuse && threadIdx.x == 0) gen0 = *reinterpret_cast<volatile const unsigned*>(&A.fm.sync[group].y);
@@ -489,7 +491,7 @@ __global__ void __launch_bounds__(kThreads, 1) attn_partial_fa(const __grid_cons
   if (threadIdx.x == 0) {
     bool ok = true;
     const unsigned prev = atomicAdd(&A.fm.sync[group].x, 1u);
-    if (prev == gridDim.x - 1) {
+    if (prev == gridDim.y - 1) {
       A.fm.sync[group].x = 0u;   // ready for the next call
       __threadfence();
       atomicAdd(&A.fm.sync[group].y, 1u);
@@ -509,7 +511,7 @@ __global__ void __launch_bounds__(kThreads, 1) attn_partial_fa(const __grid_cons
   __syncthreads();
   // this split's share of the group's rows, one warp per row (weights scratch in the slots)
   const int R_blk = min(kRowTile, R - r0);
-  const int per = (R_blk + (int)gridDim.x - 1) / (int)gridDim.x;
+  const int per = (R_blk + (int)gridDim.y - 1) / (int)gridDim.y;
   const int lo = split * per, hi = min(R_blk, lo + per);
   float* sW = reinterpret_cast<float*>(sKs) + warp * kCombineMaxSplits;
   __nv_bfloat16* out = reinterpret_cast<__nv_bfloat16*>(A.fm.out);
@@ -589,14 +591,14 @@ int launch_attn_partial_fa(const ma_rows& q, const ma_kv& kv, int H, const ma_bl
   const uint64_t prow_total = (uint64_t)q.B * H * P.S * P.Rp;
   A.tma_out = (P.Rp % 32 == 0 && prow_total < (1ull << 31) &&
                make_tma_map_2d(&A.omap, true, P.o, kD, prow_total, kD * 2, 64, 32)) ? 1 : 0;
-  dim3 grid(P.S, q.B * H, (R + kRowTile - 1) / kRowTile);
+  dim3 grid((R + kRowTile - 1) / kRowTile, P.S, q.B * H);
   auto kernel = attn_partial_fa;
   if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes) != cudaSuccess)
     return MA_ERR_CUDA;
   // fused merge: one wave of resident CTAs (cooperative launch), when each split's share of
   // the rows is one pass of its warps
-  const int rows_per_split = (std::min(kRowTile, R) + (int)grid.x - 1) / (int)grid.x;
-  if (fm != nullptr && (int)(grid.y * grid.z) <= fm->sync_slots && (int)grid.x <= kCombineMaxSplits &&
+  const int rows_per_split = (std::min(kRowTile, R) + (int)grid.y - 1) / (int)grid.y;
+  if (fm != nullptr && (int)(grid.x * grid.z) <= fm->sync_slots && (int)grid.y <= kCombineMaxSplits &&
       rows_per_split <= kWarps) {
     int dev = 0, coop = 0, per_sm = 0;
     if (cudaGetDevice(&dev) == cudaSuccess &&

@@ -309,55 +309,17 @@ select_topk_reg(const float* __restrict__ score, int H, int n, int64_t ss0, int6
 // the hardware co-schedules; every CTA takes the same barriers in the same order.
 constexpr int kSelCluster = 8;
 
-template <int PER>
-__global__ void __launch_bounds__(kSelThreads)
-select_topk_cluster(const float* __restrict__ score, int H, int n, int64_t ss0, int64_t ss1,
-                    const uint8_t* __restrict__ mask, const int32_t* __restrict__ lens, int k,
-                    int64_t* __restrict__ indices, float* __restrict__ values, int64_t si0, int64_t si1) {
-  __shared__ unsigned sHist[256];                  // this CTA's histogram
-  __shared__ unsigned sGlob[4][256];               // rank 0: the cluster's, one per pass
-  __shared__ unsigned sCnt[kSelCluster];           // rank 0: (ties << 16 | larger) per rank
-  __shared__ int sSel[2][2];
-  __shared__ int sWarp[33];
-  const uint32_t rank = cluster_rank();
-  for (int i = threadIdx.x; i < 4 * 256; i += blockDim.x) (&sGlob[0][0])[i] = 0u;
-  cluster_sync();   // every CTA of the cluster started, rank 0's buffers are zero
-  pdl_wait();
-  const int bh = blockIdx.y;
-  const int b = bh / H, h = bh - (bh / H) * H;
-  const float* s = score + (int64_t)b * ss0 + (int64_t)h * ss1;
-  const uint8_t* m = mask ? mask + (int64_t)bh * n : nullptr;
+// The radix select and the rank-ordered emission shared by the cluster kernels: thread t of
+// cluster rank r holds the order keys of slots j0 .. j0 + nv - 1 (j0 increasing with r and t)
+// in key[]; emit(off, j) is called for the k largest, off their output position in slot
+// order, ties at the k-th key going to the lower slots. sGlob (4 x 256) and sCnt
+// (kSelCluster) are rank 0's; they must be zero and the cluster synchronized before the call.
+// Ends with a cluster barrier, after which no CTA reads another's shared memory.
+template <int PER, class EmitFn>
+__device__ __forceinline__ void cluster_select(const uint32_t (&key)[PER], int nv, int j0, int k, uint32_t rank,
+                                               unsigned* sHist, unsigned (*sGlob)[256], unsigned* sCnt,
+                                               int (*sSel)[2], int* sWarp, EmitFn emit) {
   const int lane = threadIdx.x & 31;
-  const int chunk = kSelThreads * PER;
-  const int j0 = (int)rank * chunk + threadIdx.x * PER;
-  uint32_t key[PER];
-  const bool vec = ((reinterpret_cast<uintptr_t>(s) & 15) == 0) && j0 + PER <= n;
-  if (vec) {
-#pragma unroll
-    for (int c = 0; c < PER / 4; ++c) {
-      const float4 v = __ldcg(reinterpret_cast<const float4*>(s + j0) + c);
-      key[4 * c] = order_key(v.x);
-      key[4 * c + 1] = order_key(v.y);
-      key[4 * c + 2] = order_key(v.z);
-      key[4 * c + 3] = order_key(v.w);
-    }
-  } else {
-#pragma unroll
-    for (int i = 0; i < PER; ++i) key[i] = j0 + i < n ? order_key(__ldcg(s + j0 + i)) : 0u;
-  }
-  if (m) {
-#pragma unroll
-    for (int i = 0; i < PER; ++i)
-      if (j0 + i < n && m[j0 + i] == 0) key[i] = 0u;   // dead slots rank below every live one
-  }
-  if (lens) {
-    const int len = lens[b];
-#pragma unroll
-    for (int i = 0; i < PER; ++i)
-      if (j0 + i >= len) key[i] = 0u;
-  }
-  const int nv = max(0, min(PER, n - j0));   // this thread's slots inside the row
-
   uint32_t prefix = 0, pmask = 0;
   int kk = k;
 #pragma unroll 1
@@ -431,28 +393,187 @@ select_topk_cluster(const float* __restrict__ score, int H, int n, int64_t ss0, 
   const int take = max(0, min(eq, kk_cta - eq_before));
   int off = gt_r + min(eq_r, kk) + gt_before + min(eq_before, kk_cta);
   int taken = 0;
-  int64_t* oi = indices + (int64_t)b * si0 + (int64_t)h * si1;
-  float* ov = values ? values + (int64_t)b * si0 + (int64_t)h * si1 : nullptr;
 #pragma unroll
   for (int i = 0; i < PER; ++i) {
     const uint32_t x = key[i];
     const bool tie = x == prefix;
     if (i < nv && (x > prefix || (tie && taken < take))) {
       taken += tie ? 1 : 0;
-      oi[off] = j0 + i;
-      if (ov) ov[off] = s[j0 + i];
+      emit(off, j0 + i);
       ++off;
     }
   }
   cluster_sync();   // no CTA leaves while another may still read rank 0's shared memory
 }
 
+template <int PER>
+__global__ void __launch_bounds__(kSelThreads)
+select_topk_cluster(const float* __restrict__ score, int H, int n, int64_t ss0, int64_t ss1,
+                    const uint8_t* __restrict__ mask, const int32_t* __restrict__ lens, int k,
+                    int64_t* __restrict__ indices, float* __restrict__ values, int64_t si0, int64_t si1) {
+  __shared__ unsigned sHist[256];                  // this CTA's histogram
+  __shared__ unsigned sGlob[4][256];               // rank 0: the cluster's, one per pass
+  __shared__ unsigned sCnt[kSelCluster];           // rank 0: (ties << 16 | larger) per rank
+  __shared__ int sSel[2][2];
+  __shared__ int sWarp[33];
+  const uint32_t rank = cluster_rank();
+  for (int i = threadIdx.x; i < 4 * 256; i += blockDim.x) (&sGlob[0][0])[i] = 0u;
+  cluster_sync();   // every CTA of the cluster started, rank 0's buffers are zero
+  pdl_wait();
+  const int bh = blockIdx.y;
+  const int b = bh / H, h = bh - (bh / H) * H;
+  const float* s = score + (int64_t)b * ss0 + (int64_t)h * ss1;
+  const uint8_t* m = mask ? mask + (int64_t)bh * n : nullptr;
+  const int chunk = kSelThreads * PER;
+  const int j0 = (int)rank * chunk + threadIdx.x * PER;
+  uint32_t key[PER];
+  const bool vec = ((reinterpret_cast<uintptr_t>(s) & 15) == 0) && j0 + PER <= n;
+  if (vec) {
+#pragma unroll
+    for (int c = 0; c < PER / 4; ++c) {
+      const float4 v = __ldcg(reinterpret_cast<const float4*>(s + j0) + c);
+      key[4 * c] = order_key(v.x);
+      key[4 * c + 1] = order_key(v.y);
+      key[4 * c + 2] = order_key(v.z);
+      key[4 * c + 3] = order_key(v.w);
+    }
+  } else {
+#pragma unroll
+    for (int i = 0; i < PER; ++i) key[i] = j0 + i < n ? order_key(__ldcg(s + j0 + i)) : 0u;
+  }
+  if (m) {
+#pragma unroll
+    for (int i = 0; i < PER; ++i)
+      if (j0 + i < n && m[j0 + i] == 0) key[i] = 0u;   // dead slots rank below every live one
+  }
+  if (lens) {
+    const int len = lens[b];
+#pragma unroll
+    for (int i = 0; i < PER; ++i)
+      if (j0 + i >= len) key[i] = 0u;
+  }
+  const int nv = max(0, min(PER, n - j0));   // this thread's slots inside the row
+
+  int64_t* oi = indices + (int64_t)b * si0 + (int64_t)h * si1;
+  float* ov = values ? values + (int64_t)b * si0 + (int64_t)h * si1 : nullptr;
+  cluster_select<PER>(key, nv, j0, k, rank, sHist, sGlob, sCnt, sSel, sWarp, [&](int off, int j) {
+    oi[off] = j;
+    if (ov) ov[off] = s[j];
+  });
+}
+
+// Lookahead survivors when the live axis is ordered by position, as the reference keeps it
+// (eviction.py:404-409, "recent stays the tail"): the window is then the last W entries, the
+// contest for the other C - W slots runs over entries 0 .. live - W - 1, and the union in
+// slot order is already the position order -- one radix select over a cluster of CTAs
+// (gridDim.x ranks, PER entries per thread), no sort. The cluster first checks that the
+// lane's positions strictly increase; a lane where they do not gets keep[lane][0] = -1 and
+// is left to retain_kernel, launched after this one.
+template <int PER>
+__global__ void __launch_bounds__(kSelThreads, 1)
+retain_sorted(const float* __restrict__ score, const int32_t* __restrict__ phys, int n_phys,
+              const int32_t* __restrict__ pos, int live, int capacity, int W, int sinks,
+              int64_t* __restrict__ keep) {
+  __shared__ unsigned sHist[256];
+  __shared__ unsigned sGlob[4][256];     // rank 0: the cluster's histograms
+  __shared__ unsigned sCnt[kSelCluster];  // rank 0: (ties << 16 | larger) per rank
+  __shared__ unsigned sUnsorted;          // rank 0: CTAs that saw positions out of order
+  __shared__ int sFlag;
+  __shared__ int sSel[2][2];
+  __shared__ int sWarp[33];
+  const uint32_t rank = cluster_rank();
+  for (int i = threadIdx.x; i < 4 * 256; i += blockDim.x) (&sGlob[0][0])[i] = 0u;
+  if (threadIdx.x == 0) sUnsorted = 0u;
+  cluster_sync();   // every CTA of the cluster started, rank 0's buffers are zero
+  const int lane_id = blockIdx.y;
+  const int32_t* p = pos + (int64_t)lane_id * live;
+  const float* sc = score + (int64_t)lane_id * (phys ? n_phys : live);
+  const int32_t* ph = phys ? phys + (int64_t)lane_id * live : nullptr;
+  int64_t* out = keep + (int64_t)lane_id * capacity;
+  const int j0 = (int)rank * (kSelThreads * PER) + threadIdx.x * PER;
+  const int m = live - W;   // the contest's entries
+
+  int pv[PER];
+  if (((reinterpret_cast<uintptr_t>(p + j0) & 15) == 0) && j0 + PER <= live) {
+#pragma unroll
+    for (int c = 0; c < PER / 4; ++c) {
+      const int4 v = __ldg(reinterpret_cast<const int4*>(p + j0) + c);
+      pv[4 * c] = v.x;
+      pv[4 * c + 1] = v.y;
+      pv[4 * c + 2] = v.z;
+      pv[4 * c + 3] = v.w;
+    }
+  } else {
+#pragma unroll
+    for (int i = 0; i < PER; ++i) pv[i] = j0 + i < live ? __ldg(p + j0 + i) : 0;
+  }
+  bool bad = false;
+#pragma unroll
+  for (int i = 0; i + 1 < PER; ++i) bad |= (j0 + i + 1 < live) && pv[i] >= pv[i + 1];
+  if (j0 + PER < live) bad |= pv[PER - 1] >= __ldg(p + j0 + PER);   // into the next thread's slots
+  if (__syncthreads_or(bad) && threadIdx.x == 0) peer_add(peer_addr(&sUnsorted, 0), 1u);
+  cluster_sync();   // every CTA's verdict is in rank 0
+  if (threadIdx.x == 0) sFlag = peer_ld(peer_addr(&sUnsorted, 0)) != 0u ? 1 : 0;
+  __syncthreads();
+  if (sFlag) {   // the same for every CTA of the cluster
+    if (rank == 0 && threadIdx.x == 0) out[0] = -1;
+    cluster_sync();   // rank 0 stays until every CTA has read its verdict
+    return;
+  }
+
+  const uint32_t kInf = 0xFF800000u;   // order_key(+inf): sinks win their slots outright
+  uint32_t key[PER];
+  const bool vec = !ph && ((reinterpret_cast<uintptr_t>(sc + j0) & 15) == 0) && j0 + PER <= m;
+  if (vec) {
+#pragma unroll
+    for (int c = 0; c < PER / 4; ++c) {
+      const float4 v = __ldg(reinterpret_cast<const float4*>(sc + j0) + c);
+      key[4 * c] = order_key(v.x);
+      key[4 * c + 1] = order_key(v.y);
+      key[4 * c + 2] = order_key(v.z);
+      key[4 * c + 3] = order_key(v.w);
+    }
+  } else {
+#pragma unroll
+    for (int i = 0; i < PER; ++i) {
+      const int j = j0 + i;
+      uint32_t x = 0u;
+      if (j < m) {
+        if (ph) {
+          const int slot = __ldg(ph + j);
+          x = (slot >= 0 && slot < n_phys) ? order_key(__ldg(sc + slot)) : 0u;   // bad slot: never kept by score
+        } else {
+          x = order_key(__ldg(sc + j));
+        }
+      }
+      key[i] = x;
+    }
+  }
+  if (sinks > 0) {
+#pragma unroll
+    for (int i = 0; i < PER; ++i)
+      if (pv[i] < sinks) key[i] = kInf;
+  }
+  const int nv = max(0, min(PER, m - j0));   // this thread's entries in the contest
+  const int rest = capacity - W;
+  // the window: entries m .. live - 1, after the contest's winners
+  const int stride = (int)gridDim.x * kSelThreads;
+  for (int t = (int)rank * kSelThreads + threadIdx.x; t < W; t += stride) out[rest + t] = m + t;
+  if (rest > 0) {
+    cluster_select<PER>(key, nv, j0, rest, rank, sHist, sGlob, sCnt, sSel, sWarp,
+                        [&](int off, int j) { out[off] = j; });
+  } else {
+    cluster_sync();   // rank 0 stays until every CTA has read its verdict
+  }
+}
+
 // Lookahead survivors of one lane (eviction.py:364-409): recent window by position,
 // sinks at +inf, window excluded from the score contest, union ordered by position.
+// gated: only the lanes retain_sorted handed over (keep[lane][0] == -1) are computed.
 __global__ void __launch_bounds__(kSelThreads)
 retain_kernel(const float* __restrict__ score, const int32_t* __restrict__ phys, int n_phys,
               const int32_t* __restrict__ pos, int live, int capacity, int W, int sinks,
-              int64_t* __restrict__ keep, int sort_cap) {
+              int64_t* __restrict__ keep, int sort_cap, int gated) {
   extern __shared__ unsigned char smem[];
   unsigned long long* sSort = reinterpret_cast<unsigned long long*>(smem);   // [sort_cap]
   unsigned char* sRecent = smem + (size_t)sort_cap * sizeof(unsigned long long);  // [live]
@@ -460,6 +581,7 @@ retain_kernel(const float* __restrict__ score, const int32_t* __restrict__ phys,
   __shared__ int sSel[2];
   __shared__ int sWarp[33];
   const int lane_id = blockIdx.x;
+  if (gated && keep[(int64_t)lane_id * capacity] != -1) return;   // done by retain_sorted
   const int32_t* p = pos + (int64_t)lane_id * live;
   const float* sc = phys ? score + (int64_t)lane_id * n_phys : score + (int64_t)lane_id * live;
   const int32_t* ph = phys ? phys + (int64_t)lane_id * live : nullptr;
@@ -686,8 +808,33 @@ int launch_retain(const float* score, const int32_t* phys, int n_phys, const int
       cudaSuccess)
     return MA_ERR_CUDA;
   const int W = recent_window < capacity ? recent_window : capacity;
+  int gated = 0;
+  if (live <= kSelCluster * kSelThreads * 8) {   // positions in order: the cluster select
+    auto go = [&](auto kernel, int per) -> bool {
+      cudaLaunchConfig_t cfg = {};
+      const int ncl = (live + kSelThreads * per - 1) / (kSelThreads * per);
+      cfg.gridDim = dim3(ncl, lanes);
+      cfg.blockDim = dim3(kSelThreads);
+      cfg.dynamicSmemBytes = 0;
+      cfg.stream = st;
+      cudaLaunchAttribute attr[1];
+      attr[0].id = cudaLaunchAttributeClusterDimension;
+      attr[0].val.clusterDim.x = ncl;
+      attr[0].val.clusterDim.y = 1;
+      attr[0].val.clusterDim.z = 1;
+      cfg.attrs = attr;
+      cfg.numAttrs = 1;
+      return cudaLaunchKernelEx(&cfg, kernel, score, phys, n_phys, pos, live, capacity, W, sink_tokens, keep) ==
+             cudaSuccess;
+    };
+    bool ok;
+    if (live <= kSelThreads * 4) ok = go(retain_sorted<4>, 4);
+    else ok = go(retain_sorted<8>, 8);
+    if (!ok) return MA_ERR_CUDA;
+    gated = 1;
+  }
   retain_kernel<<<lanes, kSelThreads, smem, st>>>(score, phys, n_phys, pos, live, capacity, W,
-                                                  sink_tokens, keep, cap);
+                                                  sink_tokens, keep, cap, gated);
   return cudaGetLastError() == cudaSuccess ? MA_OK : MA_ERR_CUDA;
 }
 

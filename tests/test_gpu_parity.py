@@ -184,6 +184,35 @@ def test_survivors_bit_exact(live, C, W, sinks):
     np.testing.assert_array_equal(got.cpu().numpy(), want.numpy())
 
 
+@pytest.mark.parametrize("live,C,W,sinks", [(65536, 8192, 128, 4), (20000, 4096, 64, 0), (4096, 4096, 64, 4),
+                                            (70, 64, 64, 2), (5000, 1000, 0, 3)])
+def test_survivors_large_and_physical_slots(live, C, W, sinks):
+    """Rows of the cfg4 size (a cluster of CTAs per lane), a window filling the capacity, no
+    window, and scores given per physical slot through phys (the paged cache): the same keep
+    as the oracle on the scores gathered per live entry. Positions strictly increase along
+    the live axis, and once with one repeated position (the general path)."""
+    from maskahead_b200.hotpath import lookahead_survivors
+
+    gen = torch.Generator().manual_seed(7 * live + C + W)
+    L, B, H = 1, 2, 2
+    n_phys = live + 100
+    score_phys = torch.randint(0, 1000, (L, B, H, n_phys), generator=gen).float()   # ties included
+    phys = torch.stack([torch.randperm(n_phys, generator=gen)[:live] for _ in range(L * B * H)])
+    phys = phys.reshape(L, B, H, live).to(torch.int32)
+    pos = torch.empty(L, B, H, live, dtype=torch.int32)
+    for i in range(L * B * H):
+        pos.view(-1, live)[i] = torch.randperm(2 * live, generator=gen)[:live].sort().values.to(torch.int32)
+    score_live = torch.gather(score_phys, -1, phys.long())
+    for p in (pos, torch.cat([pos[..., :1], pos[..., :-1]], dim=-1)):   # the second repeats position 0
+        want = oracle.survivors_lookahead(p, score_live, C, recent_window=W, sink_tokens=sinks)
+        got = lookahead_survivors(p.to(DEV), score_live.to(DEV), C, recent_window=W, sink_tokens=sinks)
+        got_p = lookahead_survivors(p.to(DEV), score_phys.to(DEV), C, recent_window=W, sink_tokens=sinks,
+                                    phys=phys.to(DEV))
+        torch.cuda.synchronize()
+        np.testing.assert_array_equal(got.cpu().numpy(), want.numpy())
+        np.testing.assert_array_equal(got_p.cpu().numpy(), want.numpy())
+
+
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
 @pytest.mark.parametrize("n", [0, 1, 31, 33, 257, 1100])
 def test_prefix_attention_edges(dtype, n):
