@@ -170,7 +170,9 @@ MA_API int ma_prefix_attention(const ma_rows* q, const ma_kv* kv, int H, const m
  * score[b,h,j] = mass_j * ||v_j - c||, c = sum_j mass_j v_j / max(sum_j mass_j, 1e-12)
  * over live slots (fp32), as ma_value_score. mass/score strides over (b, h). Rows whose
  * q_rows entry lies outside [0, T) are skipped. The workspace is sized by
- * ma_value_score_workspace(B, H, n, D).                                               */
+ * ma_value_score_workspace(B, H, n, D); calls with any B*H may share one workspace (its
+ * per-head counters sit in a block of fixed size at the front). B*H above 65536 returns
+ * MA_ERR_UNSUPPORTED.                                                                  */
 MA_API int ma_prefix_scores(const ma_rows* q, const ma_kv* kv, int H, const int32_t* q_rows, int T2,
                      const float* m_p, const float* l_p, float scale,
                      float* mass, const int64_t smass[2], float* score, const int64_t sscore[2],
@@ -178,7 +180,8 @@ MA_API int ma_prefix_scores(const ma_rows* q, const ma_kv* kv, int H, const int3
 
 /* ---- value-aware score --------------------------------------------------------------
  * c = sum_j a_j v_j / max(sum_j a_j, 1e-12) over live slots, score_j = a_j*||v_j - c||
- * (fp32; dead slots: 0). a and score strides over (b, h).                              */
+ * (fp32; dead slots: 0). a and score strides over (b, h). One workspace serves calls of
+ * every size, and ma_prefix_scores's; B*H above 65536 returns MA_ERR_UNSUPPORTED.       */
 MA_API size_t ma_value_score_workspace(int B, int H, int n, int D);
 MA_API int ma_value_score(const ma_kv* kv, int B, int H, int D, const float* a, const int64_t sa[2],
                    float* score, const int64_t sscore[2],

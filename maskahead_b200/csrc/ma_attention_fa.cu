@@ -5,17 +5,20 @@
 // R = G*T rows, ordered g*T + t) and one key range (a split of the prefix, or the current
 // block). Keys come in tiles of 128: K and V each through 3 slots of 32 KB (a K slot is
 // refilled once its S was read, a V slot once its P.V completed). Tensor memory (512
-// columns): S(t) = Q K(t)^T in buffer t&1 (columns [128(t&1), +128)), O in [256, 384).
+// columns): S(t) = Q K(t)^T in buffer t&1 (columns [128(t&1), +128)), and two output
+// accumulators, O0 for the even tiles in [256, 384) and O1 for the odd ones in [384, 512).
 // Per tile t:
 //   MMA warp   S(t) = Q K(t)^T (8 MMAs 128x128x16, A = Q, B = K, K-major in shared memory),
 //              issued once K(t) is loaded and P.V(t-2) (whose P lives in the buffer) is done
-//   softmax    warp w holds rows 32(w&3).. of the tile and keys 64(w>>2).. of each S: its
-//              64 logits, the row max exchanged with its partner warp (w^4) through shared
-//              memory, lazy rescale of its half of O, P = 2^(u - m) rounded to bf16 written
-//              as bf16 pairs over the first 32 of its own 64 columns
-//   MMA warp   O += P V(t) (8 MMAs, A = P from tensor memory, B = V MN-major)
-// so S(t+1) is computed while the softmax of tile t runs. A rescale of O first waits for
-// the previous P.V to complete (lazy: only when the row max grows by more than e^8).
+//   softmax    the four warps of group t&1 (warps 4(t&1)..+3), warp w holding rows 32(w&3)..
+//              and all 128 keys: the row max, lazy rescale of its O(t&1), P = 2^(u - m)
+//              rounded to bf16 written as bf16 pairs over S's columns 0..31 and 64..95
+//   MMA warp   O(t&1) += P V(t) (8 MMAs, A = P from tensor memory, B = V MN-major)
+// so the two groups work on consecutive tiles at once (the two warps of a sub-partition
+// alternate between exponentials and tensor-memory traffic) while the tensor core runs the
+// next S. Each group keeps its own running max and row sum (a rescale of O first waits for
+// the group's previous P.V: lazy, only when the max grows by more than e^8); the epilogue
+// merges the two states.
 // Per split: (m, l) and o = acc / l as bf16 (ma_common.cuh), stored by TMA, the merge as
 // in ma_attention_tc.cu (fused into a cooperative launch when it is one pass).
 // Every wait is bounded. Semantics follow src/maskahead/kernels/splitk.py:115-190.
@@ -93,10 +96,17 @@ __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
   __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
   return *reinterpret_cast<uint32_t*>(&v);
 }
-// barrier of the warp pair (q, q+4) that shares rows 32q..32q+31 (ids 1-4; 0 is
-// __syncthreads, 5 the softmax warps)
-__device__ __forceinline__ void pair_sync(int q) {
-  asm volatile("bar.sync %0, 64;\n" ::"r"(1 + q) : "memory");
+// the max of 64 values (four independent max3 chains)
+__device__ __forceinline__ float max64(const float (&v)[64]) {
+  float mx[4];
+#pragma unroll
+  for (int j = 0; j < 4; ++j) mx[j] = max3f(v[j], v[4 + j], v[8 + j]);
+#pragma unroll
+  for (int i = 12; i + 8 <= 60; i += 8) {
+#pragma unroll
+    for (int j = 0; j < 4; ++j) mx[j] = max3f(mx[j], v[i + j], v[i + 4 + j]);
+  }
+  return max3f(max3f(mx[0], mx[1], v[60]), max3f(mx[2], mx[3], v[61]), fmaxf(v[62], v[63]));
 }
 __device__ __forceinline__ void softmax_sync() { asm volatile("bar.sync 5, %0;\n" ::"r"(kSoftThreads) : "memory"); }
 
@@ -114,10 +124,8 @@ __global__ void __launch_bounds__(kThreads, 1) attn_partial_fa(const __grid_cons
   uint8_t* sKs = sQ + kQBytes;                          // K slots
   uint8_t* sVs = sKs + kKSlots * kKVBytes;              // V slots
   __shared__ uint32_t s_taddr;
-  __shared__ __align__(8) uint64_t kfull[kKSlots], vfull[kVSlots], s_full[2], p_full[2], o_done, q_full, mbar_fin;
+  __shared__ __align__(8) uint64_t kfull[kKSlots], vfull[kVSlots], s_full[2], p_full[2], o_done[2], q_full, mbar_fin;
   __shared__ int s_abort, s_merge_ok;
-  __shared__ float sPM[2][kRowTile];   // per key half: the row's tile max (fp32, exact)
-  __shared__ int sBad[2][4];           // per key half and row quarter: this tile aborts
 
   // grid (row tiles, splits, heads): the row tiles of one split run side by side, so the
   // second and later ones read that split's K/V from L2
@@ -131,7 +139,7 @@ __global__ void __launch_bounds__(kThreads, 1) attn_partial_fa(const __grid_cons
   const int r0 = blockIdx.x * kRowTile;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const bool softmax_warp = warp < kSoftWarps;
-  const int quarter = warp & 3, hf = (warp >> 2) & 1;   // rows 32*quarter.., keys 64*hf.. of a tile
+  const int quarter = warp & 3, grp = (warp >> 2) & 1;   // rows 32*quarter.., the tiles t = grp mod 2
   const int rl = quarter * 32 + lane;
   const int r = r0 + rl;
   const int wrow0 = r0 + quarter * 32;
@@ -170,9 +178,9 @@ __global__ void __launch_bounds__(kThreads, 1) attn_partial_fa(const __grid_cons
     for (int i = 0; i < kVSlots; ++i) mbar_init(&vfull[i], 1);
     for (int i = 0; i < 2; ++i) {
       mbar_init(&s_full[i], 1);
-      mbar_init(&p_full[i], kSoftWarps);
+      mbar_init(&p_full[i], kSoftWarps / 2);
+      mbar_init(&o_done[i], 1);
     }
-    mbar_init(&o_done, 1);
     mbar_init(&q_full, 1);
     mbar_init(&mbar_fin, 1);
     s_abort = 0;
@@ -205,18 +213,19 @@ __global__ void __launch_bounds__(kThreads, 1) attn_partial_fa(const __grid_cons
   fence_after_sync();
   const uint32_t taddr = s_taddr;
   const uint32_t lane_base = (uint32_t)(quarter * 32) << 16;
-  const uint32_t tSh = taddr + lane_base + kColS + 64 * hf;   // this warp's 64 columns of S buffer 0
-  const uint32_t tOh = taddr + lane_base + kColO + 64 * hf;   // this warp's half of O
+  const uint32_t tS = taddr + lane_base + kColS + 128 * grp;   // this warp's S buffer (its rows)
+  const uint32_t tO = taddr + lane_base + kColO + 128 * grp;   // this warp's O accumulator
   float m_run = -INFINITY, l_run = 0.f, m_true = -INFINITY;
 
   if (!softmax_warp) {
     // ------------------------------------------------------------ MMA / TMA warp
     if (lane == 0) {
-      // Event loop: S(t) needs K(t) loaded and P.V(t-2) completed (P(t-2) lives in the
-      // buffer); P.V(t) needs V(t), the softmax's P(t) and P.V(t-1) seen complete. A K slot
-      // takes its next tile once the S it held was consumed (its P.V issued), a V slot once
-      // its P.V completed. Each barrier has at most one completed but unobserved phase, so
-      // the parity tests are unambiguous.
+      // Event loop: S(t) needs K(t) loaded and P.V(t-2) seen complete (P(t-2) lives in the
+      // buffer, and O(t&1) may be rescaled only after it); P.V(t) needs V(t) and the
+      // softmax's P(t). P.V completes in issue order, so oD counts completions over both
+      // o_done barriers alternately. A K slot takes its next tile once the S it held was
+      // consumed (its P.V issued), a V slot once its P.V completed. Each barrier has at most
+      // one completed but unobserved phase, so the parity tests are unambiguous.
       bool ok = true;
       // the queries and the first min(3, ntiles) K and V tiles were issued at setup
       int kIss = min(kKSlots, ntiles), kObs = 0, vIss = min(kVSlots, ntiles), vObs = 0;
@@ -245,7 +254,7 @@ __global__ void __launch_bounds__(kThreads, 1) attn_partial_fa(const __grid_cons
           ++vObs;
           progress = true;
         }
-        if (oD < pN && mbar_test(&o_done, (uint32_t)oD & 1u)) {
+        if (oD < pN && mbar_test(&o_done[oD & 1], (uint32_t)(oD >> 1) & 1u)) {
           ++oD;
           progress = true;
         }
@@ -261,15 +270,15 @@ __global__ void __launch_bounds__(kThreads, 1) attn_partial_fa(const __grid_cons
           ++sN;
           progress = true;
         }
-        if (pN < sN && vObs > pN && oD >= pN && mbar_test(&p_full[pN & 1], (uint32_t)(pN >> 1) & 1u)) {
+        if (pN < sN && vObs > pN && mbar_test(&p_full[pN & 1], (uint32_t)(pN >> 1) & 1u)) {
           fence_after_sync();
           const uint64_t bd0 = vdesc + (uint64_t)((pN % kVSlots) * (kKVBytes / 16));
           const uint32_t aP = taddr + kColS + (pN & 1) * 128;
 #pragma unroll
           for (int kk = 0; kk < kBN / 16; ++kk)   // keys 16kk..: P columns 64 (kk / 4) + 8 (kk % 4)
-            mma_bf16_ta(taddr + kColO, aP + (kk >> 2) * 64 + (kk & 3) * 8, bd0 + (uint64_t)(kk * (2048 / 16)), idO,
-                        pN > 0 || kk > 0);
-          mma_commit(&o_done);
+            mma_bf16_ta(taddr + kColO + (pN & 1) * 128, aP + (kk >> 2) * 64 + (kk & 3) * 8,
+                        bd0 + (uint64_t)(kk * (2048 / 16)), idO, pN > 1 || kk > 0);
+          mma_commit(&o_done[pN & 1]);
           ++pN;
           progress = true;
         }
@@ -314,102 +323,102 @@ __global__ void __launch_bounds__(kThreads, 1) attn_partial_fa(const __grid_cons
     __syncwarp();
   } else {
     // ------------------------------------------------------------ softmax warps
+    // warp (quarter, grp): rows 32 quarter.. of the tiles t = grp, grp + 2, ..., all 128 keys
+    // of each, with its own running max, row sum and O accumulator; the two warps that share
+    // a sub-partition work on different tiles, so one's exponentials overlap the other's
+    // tensor-memory reads, maxima and stores
     pdl_wait();   // the partials and outputs may still be in use by the kernel before
-    bool ok = true;
     const float2 c2x2 = make_float2(c2, c2);
-    for (int t = 0; t < ntiles; ++t) {
-      const int bsel = t & 1;
-      ok = mbar_wait(&s_full[bsel], (uint32_t)(t >> 1) & 1u);
+    int k = 0;   // this warp's tiles done
+    for (int t = grp; t < ntiles; t += 2, ++k) {
+      const bool ok = mbar_wait(&s_full[grp], (uint32_t)k & 1u);
       fence_after_sync();
       if (!ok) s_abort = 1;
+      if (s_abort) break;
       if (warp_rows) {
-        // this warp's 64 logits of the row (keys 64hf..64hf+63 of the tile)
-        const uint32_t tS = tSh + 128 * bsel;
-        const int lim = vis_end - (begin + t * kBN) - 64 * hf;   // keys i >= lim are hidden
+        const int lim = vis_end - (begin + t * kBN);   // keys i >= lim of the tile are hidden
+        const bool full = __all_sync(0xffffffffu, lim >= kBN);
         float sv[64];
-        bool bad = s_abort != 0;
-        if (!bad) {
-          tmem_ld32(tS, sv);
-          tmem_ld32(tS + 32, sv + 32);
-          tmem_ld_wait();
-          if (!__all_sync(0xffffffffu, lim >= 64)) {
+        // the row max: keys 64..127 (read, not kept), then keys 0..63 (kept)
+        tmem_ld32(tS + 64, sv);
+        tmem_ld32(tS + 96, sv + 32);
+        tmem_ld_wait();
+        if (!full) {
 #pragma unroll
-            for (int i = 0; i < 64; ++i) sv[i] = i < lim ? sv[i] : -INFINITY;
-          }
-        } else {
-#pragma unroll
-          for (int i = 0; i < 64; ++i) sv[i] = -INFINITY;
+          for (int i = 0; i < 64; ++i) sv[i] = 64 + i < lim ? sv[i] : -INFINITY;
         }
-        float mx[4];
+        float pm = max64(sv);
+        tmem_ld32(tS, sv);
+        tmem_ld32(tS + 32, sv + 32);
+        tmem_ld_wait();
+        if (!full) {
 #pragma unroll
-        for (int j = 0; j < 4; ++j) mx[j] = max3f(sv[j], sv[4 + j], sv[8 + j]);
-#pragma unroll
-        for (int i = 12; i + 8 <= 60; i += 8) {
-#pragma unroll
-          for (int j = 0; j < 4; ++j) mx[j] = max3f(mx[j], sv[i + j], sv[i + 4 + j]);
+          for (int i = 0; i < 64; ++i) sv[i] = i < lim ? sv[i] : -INFINITY;
         }
-        const float pm = max3f(max3f(mx[0], mx[1], sv[60]), max3f(mx[2], mx[3], sv[61]), fmaxf(sv[62], sv[63]));
-        // the pair's exchange: partial maxima and abort flags (the second barrier keeps the
-        // slots until both have read them)
-        sPM[hf][rl] = pm;
-        if (lane == 0) sBad[hf][quarter] = bad ? 1 : 0;
-        pair_sync(quarter);
-        const float tmax = fmaxf(pm, sPM[hf ^ 1][rl]);
-        bad = bad || sBad[hf ^ 1][quarter] != 0;
-        pair_sync(quarter);
-        if (bad) break;   // both warps of the pair leave together
-        // lazy rescale of this warp's half of O, after P.V(t-1) completed
-        m_true = fmaxf(m_true, tmax);
-        const float m_new = fmaxf(m_run, tmax * c2);
-        const bool grow = t > 0 && m_new > m_run + kLazyLog2;
+        pm = fmaxf(pm, max64(sv));
+        // lazy rescale of this warp's O, after its previous P.V completed
+        m_true = fmaxf(m_true, pm);
+        const float m_new = fmaxf(m_run, pm * c2);
+        const bool grow = k > 0 && m_new > m_run + kLazyLog2;
         if (__any_sync(0xffffffffu, grow)) {
-          if (!mbar_wait(&o_done, (uint32_t)(t - 1) & 1u, kWaitNs)) s_abort = 1;
+          if (!mbar_wait(&o_done[grp], (uint32_t)(k - 1) & 1u, kWaitNs)) s_abort = 1;
           fence_after_sync();
           const float alpha = grow ? ex2(m_run - m_new) : 1.f;
 #pragma unroll 1
-          for (int c = 0; c < 2; ++c) {
+          for (int c = 0; c < 4; ++c) {
             float o[32];
-            tmem_ld32(tOh + c * 32, o);
+            tmem_ld32(tO + c * 32, o);
             tmem_ld_wait();
 #pragma unroll
             for (int i = 0; i < 32; ++i) o[i] *= alpha;
-            tmem_st32(tOh + c * 32, o);
+            tmem_st32(tO + c * 32, o);
           }
           if (grow) {
             l_run *= alpha;
             m_run = m_new;
           }
         }
-        if (t == 0) m_run = m_new;
+        if (k == 0) m_run = m_new;
         const float msl = (m_run == -INFINITY) ? 0.f : m_run;
-        // P = 2^(s c2 - m) (packed FMA, one ex2 per key) as bf16 pairs over the first 32 of
-        // this warp's 64 columns (already read); the row sum from the fp32 values
+        // P = 2^(s c2 - m) (packed FMA, one ex2 per key) as bf16 pairs: keys 0..63 into
+        // columns 0..31, keys 64..127 (read again) into columns 64..95; the row sum from the
+        // fp32 values
         const float2 nm2 = make_float2(-msl, -msl);
         float2 acc0 = make_float2(0.f, 0.f), acc1 = make_float2(0.f, 0.f);
+#pragma unroll 1
+        for (int half = 0; half < 2; ++half) {
+          if (half == 1) {
+            tmem_ld32(tS + 64, sv);
+            tmem_ld32(tS + 96, sv + 32);
+            tmem_ld_wait();
+            if (!full) {
 #pragma unroll
-        for (int c = 0; c < 2; ++c) {
-          uint32_t w[16];
-#pragma unroll
-          for (int i = 0; i < 16; ++i) {
-            float2 x = ffma2(make_float2(sv[32 * c + 2 * i], sv[32 * c + 2 * i + 1]), c2x2, nm2);
-            x.x = ex2(x.x);
-            x.y = ex2(x.y);
-            if (i & 1) acc1 = fadd2(acc1, x); else acc0 = fadd2(acc0, x);
-            w[i] = pack_bf16x2(x.x, x.y);
+              for (int i = 0; i < 64; ++i) sv[i] = 64 + i < lim ? sv[i] : -INFINITY;
+            }
           }
-          tmem_st16(tS + c * 16, w);
+#pragma unroll
+          for (int c = 0; c < 2; ++c) {
+            uint32_t w[16];
+#pragma unroll
+            for (int i = 0; i < 16; ++i) {
+              float2 x = ffma2(make_float2(sv[32 * c + 2 * i], sv[32 * c + 2 * i + 1]), c2x2, nm2);
+              x.x = ex2(x.x);
+              x.y = ex2(x.y);
+              if (i & 1) acc1 = fadd2(acc1, x); else acc0 = fadd2(acc0, x);
+              w[i] = pack_bf16x2(x.x, x.y);
+            }
+            tmem_st16(tS + 64 * half + c * 16, w);
+          }
         }
         tmem_st_wait();
         l_run += (acc0.x + acc0.y) + (acc1.x + acc1.y);
-      } else if (s_abort) {
-        break;   // no rows: nothing shared with a partner
       }
       fence_before_sync();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&p_full[bsel]);
+      if (lane == 0) mbar_arrive(&p_full[grp]);
     }
-    if (ntiles > 0 && !s_abort) {
-      if (!mbar_wait(&o_done, (uint32_t)(ntiles - 1) & 1u, kWaitNs)) s_abort = 1;
+    if (ntiles > grp && !s_abort) {   // this warp's last P.V
+      if (!mbar_wait(&o_done[grp], (uint32_t)(((ntiles - 1 - grp) >> 1) & 1), kWaitNs)) s_abort = 1;
       fence_after_sync();
     }
   }
@@ -419,48 +428,77 @@ __global__ void __launch_bounds__(kThreads, 1) attn_partial_fa(const __grid_cons
   fence_after_sync();
 
   if (softmax_warp) {
-    // the row sum over both key halves (the slots are drained: scratch in the V slots)
-    float* sPL = reinterpret_cast<float*>(sVs);
-    sPL[hf * kRowTile + rl] = l_run;
+    // the two tile groups' row states meet (the slots are drained: scratch in the V slots):
+    // both are rescaled to the larger running max M, l = l0 f0 + l1 f1, o = (O0 f0 + O1 f1) / l;
+    // warp (quarter, grp) writes channels 64 grp.. of its rows
+    float* sX = reinterpret_cast<float*>(sVs);   // [group][m_run, l_run, m_true][row]
+    sX[(grp * 3 + 0) * kRowTile + rl] = m_run;
+    sX[(grp * 3 + 1) * kRowTile + rl] = l_run;
+    sX[(grp * 3 + 2) * kRowTile + rl] = m_true;
     softmax_sync();
-    const float l = l_run + sPL[(hf ^ 1) * kRowTile + rl];
+    const int og = grp ^ 1;
+    const float m_oth = sX[(og * 3 + 0) * kRowTile + rl], l_oth = sX[(og * 3 + 1) * kRowTile + rl];
+    const float M = fmaxf(m_run, m_oth);
+    const float f_me = m_run == -INFINITY ? 0.f : ex2(m_run - M);
+    const float f_oth = m_oth == -INFINITY ? 0.f : ex2(m_oth - M);
+    const float l = l_run * f_me + l_oth * f_oth;
+    const float mt = fmaxf(m_true, sX[(og * 3 + 2) * kRowTile + rl]);
+    const float f0 = grp == 0 ? f_me : f_oth, f1 = grp == 0 ? f_oth : f_me;
     const int64_t prow = ((int64_t)bh * A.P.S + split) * A.P.Rp + r;
     const int prow0 = (int)(((int64_t)bh * A.P.S + split) * A.P.Rp + wrow0);
     if (s_abort != 0) {
       if (threadIdx.x == 0) atomicExch(A.err, 1);
-      if (row_ok && hf == 0) A.P.ml[prow] = make_float2(NAN, NAN);
+      if (row_ok && grp == 0) A.P.ml[prow] = make_float2(NAN, NAN);
     } else {
-      // the exact max: l under m_run times 2^(m_run - m_true) <= 1; o = acc / l is the same
-      // under either reference
-      if (row_ok && hf == 0) {
-        const float fix = (m_true == -INFINITY) ? 1.f : ex2(m_run - m_true * c2);
-        A.P.ml[prow] = make_float2(m_true * A.scale, l * fix);
+      // the exact max: l under M times 2^(M - m_true) <= 1; o = acc / l is the same under
+      // either reference
+      if (row_ok && grp == 0) {
+        const float fix = (mt == -INFINITY) ? 1.f : ex2(M - mt * c2);
+        A.P.ml[prow] = make_float2(mt * A.scale, l * fix);
       }
       const float inv = l > 0.f ? 1.f / l : 0.f;
       if (warp_rows) {
-        float o[64];
-        if (ntiles > 0) {
-          tmem_ld32(tOh, o);
-          tmem_ld32(tOh + 32, o + 32);
-          tmem_ld_wait();
+        const bool via_tma = ntiles > 0 && A.tma_out;
+        // the warp's 32 rows x 64 channels -> one box in the K slots, 128-byte swizzled
+        // (chunk q of line i at q ^ (i & 7)), stored by lane 0; else straight to global
+        uint8_t* box = sKs + warp * kOutBox;
+        uint8_t* line = box + lane * 128;
+        uint4* dst = reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(A.P.o) + prow * kD + 64 * grp);
+        const uint32_t tO0 = taddr + lane_base + kColO + 64 * grp, tO1 = tO0 + 128;
+#pragma unroll 1
+        for (int c = 0; c < 2; ++c) {
+          float o[32];
+          if (ntiles > 0) {
+            tmem_ld32(tO0 + 32 * c, o);   // O0 holds tiles 0, 2, ..., O1 tiles 1, 3, ...
+            if (ntiles > 1) {
+              float x[32];
+              tmem_ld32(tO1 + 32 * c, x);
+              tmem_ld_wait();
 #pragma unroll
-          for (int i = 0; i < 64; ++i) o[i] *= inv;
-        } else {
+              for (int i = 0; i < 32; ++i) o[i] = (o[i] * f0 + x[i] * f1) * inv;
+            } else {
+              tmem_ld_wait();
 #pragma unroll
-          for (int i = 0; i < 64; ++i) o[i] = 0.f;
+              for (int i = 0; i < 32; ++i) o[i] = o[i] * f0 * inv;
+            }
+          } else {
+#pragma unroll
+            for (int i = 0; i < 32; ++i) o[i] = 0.f;
+          }
+          if (via_tma) {
+#pragma unroll
+            for (int qq = 0; qq < 4; ++qq)
+              *reinterpret_cast<uint4*>(line + (((4 * c + qq) ^ (lane & 7)) << 4)) = float8_to_bf16x8(o + 8 * qq);
+          } else if (row_ok) {
+#pragma unroll
+            for (int qq = 0; qq < 4; ++qq) dst[4 * c + qq] = float8_to_bf16x8(o + 8 * qq);
+          }
         }
-        if (ntiles > 0 && A.tma_out) {
-          // the warp's 32 rows x 64 channels -> one box in the K slots, 128-byte swizzled
-          // (chunk q of line i at q ^ (i & 7)), stored by lane 0
-          uint8_t* box = sKs + warp * kOutBox;
-          uint8_t* line = box + lane * 128;
-#pragma unroll
-          for (int qq = 0; qq < 8; ++qq)
-            *reinterpret_cast<uint4*>(line + ((qq ^ (lane & 7)) << 4)) = float8_to_bf16x8(o + 8 * qq);
+        if (via_tma) {
           fence_proxy_async();
           __syncwarp();
           if (lane == 0) {
-            tma::store_2d(&A.omap, 64 * hf, prow0, box);
+            tma::store_2d(&A.omap, 64 * grp, prow0, box);
             tma::store_commit();
             if (A.fuse) {   // other CTAs read these rows: complete, then order for generic loads
               tma::store_wait_all();
@@ -470,10 +508,6 @@ __global__ void __launch_bounds__(kThreads, 1) attn_partial_fa(const __grid_cons
             }
           }
           __syncwarp();
-        } else if (row_ok) {
-          uint4* dst = reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(A.P.o) + prow * kD + 64 * hf);
-#pragma unroll
-          for (int qq = 0; qq < 8; ++qq) dst[qq] = float8_to_bf16x8(o + 8 * qq);
         }
       }
     }
@@ -509,12 +543,21 @@ __global__ void __launch_bounds__(kThreads, 1) attn_partial_fa(const __grid_cons
     s_merge_ok = ok ? 1 : 0;
   }
   __syncthreads();
-  // this split's share of the group's rows, one warp per row (weights scratch in the slots)
+  // this split's share of the group's rows: a half warp per row with at most 16 prefix
+  // splits, else a warp per row (weights scratch in the slots)
   const int R_blk = min(kRowTile, R - r0);
   const int per = (R_blk + (int)gridDim.y - 1) / (int)gridDim.y;
   const int lo = split * per, hi = min(R_blk, lo + per);
-  float* sW = reinterpret_cast<float*>(sKs) + warp * kCombineMaxSplits;
   __nv_bfloat16* out = reinterpret_cast<__nv_bfloat16*>(A.fm.out);
+  if (A.nsplit <= 16 && s_merge_ok) {
+    for (int rr0 = lo + 2 * warp; rr0 < hi; rr0 += 2 * kWarps) {   // uniform per warp
+      const int rr = rr0 + (lane >> 4);
+      combine_row16<__nv_bfloat16>(A.q, H, A.P, A.nsplit, A.cur.Tc > 0, out, A.fm.so[0], A.fm.so[1], A.fm.so[2],
+                                   A.fm.m_p, A.fm.l_p, A.fm.o_p, bh, r0 + rr, rr < hi);
+    }
+    return;
+  }
+  float* sW = reinterpret_cast<float*>(sKs) + warp * kCombineMaxSplits;
   for (int rr = lo + warp; rr < hi; rr += kWarps) {
     if (s_merge_ok) {
       combine_row<__nv_bfloat16, __nv_bfloat16>(A.q, H, A.P, A.nsplit, A.cur.Tc > 0, out, A.fm.so[0], A.fm.so[1],
@@ -598,8 +641,9 @@ int launch_attn_partial_fa(const ma_rows& q, const ma_kv& kv, int H, const ma_bl
   // fused merge: one wave of resident CTAs (cooperative launch), when each split's share of
   // the rows is one pass of its warps
   const int rows_per_split = (std::min(kRowTile, R) + (int)grid.y - 1) / (int)grid.y;
+  const int rows_per_pass = nsplit <= 16 ? 2 * kWarps : kWarps;   // half warps or warps per row
   if (fm != nullptr && (int)(grid.x * grid.z) <= fm->sync_slots && (int)grid.y <= kCombineMaxSplits &&
-      rows_per_split <= kWarps) {
+      rows_per_split <= rows_per_pass) {
     int dev = 0, coop = 0, per_sm = 0;
     if (cudaGetDevice(&dev) == cudaSuccess &&
         cudaDeviceGetAttribute(&coop, cudaDevAttrCooperativeLaunch, dev) == cudaSuccess && coop &&

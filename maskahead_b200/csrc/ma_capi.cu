@@ -303,6 +303,7 @@ int ma_prefix_scores(const ma_rows* q, const ma_kv* kv, int H, const int32_t* q_
   const bool tc = use_mma(*q, *kv) && G * T2 <= 256;
   ValueWs w = {nullptr, nullptr, nullptr, nullptr};
   if (score || tc) {  // the tensor-core kernel reports bounded-wait timeouts in the workspace
+    if (BH > value_sync_slots()) return MA_ERR_UNSUPPORTED;
     if (!workspace || workspace_bytes < value_score_ws_bytes(q->B, H, n, q->D)) return MA_ERR_WORKSPACE;
     if ((reinterpret_cast<uintptr_t>(workspace) & 255) != 0) return MA_ERR_WORKSPACE;
     w = carve_value_ws(workspace, BH, q->D);
@@ -341,6 +342,7 @@ int ma_value_score(const ma_kv* kv, int B, int H, int D, const float* a, const i
   if (rc) return rc;
   if (!a || !sa || !score || !sscore) return MA_ERR_ARG;
   const int n = kv->nq + kv->nf;
+  if ((int64_t)B * H > value_sync_slots()) return MA_ERR_UNSUPPORTED;
   if (!workspace || workspace_bytes < value_score_ws_bytes(B, H, n, D)) return MA_ERR_WORKSPACE;
   if ((reinterpret_cast<uintptr_t>(workspace) & 255) != 0) return MA_ERR_WORKSPACE;
   if (!fa_disabled()) {

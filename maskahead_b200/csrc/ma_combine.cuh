@@ -132,5 +132,85 @@ __device__ __forceinline__ void combine_row(const ma_rows& q, int H, const Parti
   }
 }
 
+// A half warp (16 lanes) merges row r when there are at most 16 prefix splits, for bf16
+// partials of D = 128: lane l of the half holds channels 8l..8l+7 and split l's (m, l)
+// pair, so a warp merges two rows at once (row r of the upper half ignored when !valid;
+// every lane of the warp must call, shuffles span the whole warp). The arithmetic is
+// combine_row's: w_s = l_s exp(m_s - M), prefix statistics, then the current block.
+template <typename QT>
+__device__ __forceinline__ void combine_row16(const ma_rows& q, int H, const Partials& P, int nsplit, bool has_cur,
+                                              QT* __restrict__ out, int64_t so0, int64_t so1, int64_t so2,
+                                              float* __restrict__ m_p, float* __restrict__ l_p,
+                                              float* __restrict__ o_p, int bh, int r, bool valid) {
+  constexpr int D = 128;
+  const int G = q.Hq / H;
+  const int R = G * q.T;
+  const int l16 = threadIdx.x & 15;
+  const int half = threadIdx.x & 16;
+  const int d0 = 8 * l16;
+  const int64_t row0 = (int64_t)bh * P.S * P.Rp + r;   // partial row of split 0; split s adds s*Rp
+  const __nv_bfloat16* o = reinterpret_cast<const __nv_bfloat16*>(P.o);
+  // every split's 8 channels and the current block's, in flight first
+  uint4 buf[16];
+#pragma unroll
+  for (int i = 0; i < 16; ++i)
+    buf[i] = (valid && i < nsplit) ? __ldcg(reinterpret_cast<const uint4*>(o + (row0 + (int64_t)i * P.Rp) * D + d0))
+                                   : make_uint4(0u, 0u, 0u, 0u);
+  const int64_t crow = row0 + (int64_t)nsplit * P.Rp;
+  float2 mlc = make_float2(-INFINITY, 0.f);
+  uint4 oc = make_uint4(0u, 0u, 0u, 0u);
+  if (valid && has_cur) {
+    mlc = __ldcg(&P.ml[crow]);
+    oc = __ldcg(reinterpret_cast<const uint4*>(o + crow * D + d0));
+  }
+  const float2 mls = (valid && l16 < nsplit) ? __ldcg(&P.ml[row0 + (int64_t)l16 * P.Rp]) : make_float2(-INFINITY, 0.f);
+  float M = mls.x;
+#pragma unroll
+  for (int off = 8; off > 0; off >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, off));
+  const float Ms = (M == -INFINITY) ? 0.f : M;
+  const float w = l16 < nsplit ? mls.y * expf(mls.x - Ms) : 0.f;
+  float L = w;
+#pragma unroll
+  for (int off = 8; off > 0; off >>= 1) L += __shfl_xor_sync(0xffffffffu, L, off);
+  float A[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+  for (int i = 0; i < 16; ++i) {
+    if (i < nsplit) {
+      const float wi = __shfl_sync(0xffffffffu, w, half | i);
+      float f[8];
+      bf16x8_to_float(buf[i], f);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) A[e] = fmaf(f[e], wi, A[e]);
+    }
+  }
+  if (!valid) return;
+  const int64_t srow = (int64_t)bh * R + r;
+  if (m_p != nullptr && l16 == 0) {
+    m_p[srow] = M;
+    l_p[srow] = L;
+  }
+  if (o_p != nullptr) {
+    const float inv = 1.f / (L > 0.f ? L : 1.f);
+    float4* dp = reinterpret_cast<float4*>(o_p + srow * D + d0);
+    dp[0] = make_float4(A[0] * inv, A[1] * inv, A[2] * inv, A[3] * inv);
+    dp[1] = make_float4(A[4] * inv, A[5] * inv, A[6] * inv, A[7] * inv);
+  }
+  if (has_cur) {
+    const float mn = fmaxf(M, mlc.x);
+    const float ms = (mn == -INFINITY) ? 0.f : mn;
+    const float ea = expf(M - ms), eb = mlc.y * expf(mlc.x - ms);
+    L = L * ea + eb;
+    float f[8];
+    bf16x8_to_float(oc, f);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) A[e] = A[e] * ea + f[e] * eb;
+  }
+  const float inv = 1.f / (L > 0.f ? L : 1.f);
+  const int b = bh / H, h = bh - (bh / H) * H;
+  const int g = r / q.T, t = r - (r / q.T) * q.T;
+  QT* dst = out + (int64_t)b * so0 + (int64_t)(h * G + g) * so1 + (int64_t)t * so2 + d0;
+  store4(dst, A[0] * inv, A[1] * inv, A[2] * inv, A[3] * inv);
+  store4(dst + 4, A[4] * inv, A[5] * inv, A[6] * inv, A[7] * inv);
+}
 
 }  // namespace ma

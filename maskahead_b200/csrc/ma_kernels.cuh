@@ -66,6 +66,7 @@ struct ValueWs {
   float* part;         // [BH][tiles][D+1]
 };
 size_t value_sync_bytes(int BH);
+int value_sync_slots();   // the most heads (B * H) one call may have
 ValueWs carve_value_ws(void* ws, int BH, int D);
 int launch_value_apply(const ma_kv& kv, int B, int H, int D, const float* a, int64_t sa0, int64_t sa1,
                        const float* centre, float* score, int64_t ss0, int64_t ss1, cudaStream_t st);

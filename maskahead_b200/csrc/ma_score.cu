@@ -264,7 +264,17 @@ int launch_prefix_mass(const ma_rows& q, const ma_kv& kv, int H, const int32_t* 
 
 // workspace: the error word and the per-head (counter, generation) pairs (one 256-byte
 // aligned block), centre [BH][D], partials [BH][ntile][D+1]
-size_t value_sync_bytes(int BH) { return ((8 + (size_t)BH * sizeof(uint2) + 255) / 256) * 256; }
+// The error word and the per-head (arrival counter, centre generation) pairs: a block of
+// fixed size at the front of the workspace, so a head's counter is the same word in every
+// call. Calls with other head counts share the workspace (a mass call of a few heads, then
+// a value score over every layer's heads); a block that grew with the head count would let
+// one call's centres land on another's counters, which must read zero when a call starts.
+constexpr size_t kValueSyncSlots = size_t(1) << 16;
+size_t value_sync_bytes(int BH) {
+  (void)BH;
+  return ((8 + kValueSyncSlots * sizeof(uint2) + 255) / 256) * 256;
+}
+int value_sync_slots() { return (int)kValueSyncSlots; }
 
 size_t value_score_ws_bytes(int B, int H, int n, int D) {
   const size_t BH = (size_t)B * H;

@@ -85,3 +85,30 @@ def test_mass_fa_repeated_calls_are_identical():
     for _ in range(3):
         m1, s1 = prefix_scores(q, pre, st, rows, value=True)
         assert torch.equal(m0, m1) and torch.equal(s0, s1)
+
+
+@pytest.mark.parametrize("lanes,n", [(160, 1000), (24, 3000)])
+def test_value_score_after_mass_calls_of_other_head_counts(lanes, n):
+    """value_score over many lanes (one CTA per lane when lanes >= SMs, else several) right
+    after a mass call of 4 heads and a value score of 3 lanes on the same workspace: the
+    per-lane counters must not pick up the other calls' centres or partials (a stale
+    counter makes a lane wait for a centre that never comes and score NaN)."""
+    from maskahead_b200.hotpath import value_score
+    from maskahead_b200.kernels import prefix_scores, splitk_attention
+    from maskahead_b200.layouts import Prefix
+
+    gen = torch.Generator().manual_seed(lanes + n)
+    q = torch.randn(1, 28, 32, 128, generator=gen).to(torch.bfloat16).to(DEV)
+    k = torch.randn(1, 4, 4096, 128, generator=gen).to(torch.bfloat16).to(DEV)
+    vv = torch.randn(1, 4, 4096, 128, generator=gen).to(torch.bfloat16).to(DEV)
+    pre = Prefix.dense(k, vv)
+    _, st = splitk_attention(q, pre, None, None, want_prefix=True)
+    prefix_scores(q, pre, st, torch.arange(32, dtype=torch.int32, device=DEV), value=True)
+    value_score(torch.rand(3, n, generator=gen).to(DEV), torch.randn(3, n, 128, generator=gen).to(torch.bfloat16).to(DEV))
+    a = torch.rand(lanes, n, generator=gen)
+    v = torch.randn(lanes, n, 128, generator=gen).to(torch.bfloat16)
+    for _ in range(2):
+        got = value_score(a.to(DEV), v.to(DEV)).cpu()
+        torch.cuda.synchronize()
+        want = oracle.value_score(a, v)
+        np.testing.assert_allclose(got.numpy(), want.numpy(), rtol=5e-5, atol=1e-9)
