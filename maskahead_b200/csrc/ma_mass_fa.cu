@@ -7,13 +7,14 @@
 //     c = sum_j a_j v_j / max(sum_j a_j, 1e-12)            (session.py:27-40, 870-899)
 // and the value score a_j ||v_j - c||.
 //
-// CTA = 8 sum warps + 1 producer/MMA warp over one slot range of one head (one wave of
-// CTAs). Phase 1, per tile of 128 slots: the producer streams K and V tiles by TMA (two
-// slots each), issues S^T = K Q^T (tcgen05, M = 128 slots, N = the selection rows padded
-// to 16, double-buffered in tensor memory); sum warp w owns slot lane 32(w&3).. and half
-// of the rows (w>>2): it sums its exponentials from tensor memory, the halves meet in
-// shared memory, a_j is written, and the warps accumulate sum_j a_j v_j (channel pairs x
-// key quarters) from the V tile. The last CTA of the head reduces the per-CTA partials
+// CTA = 8 sum warps + 1 producer/MMA warp + 2 centre warps over one slot range of one head
+// (one wave of CTAs). Phase 1, per tile of 128 slots: the producer streams K and V tiles by
+// TMA (ring slots of 32 KB), issues S^T = K Q^T (tcgen05, M = 128 slots, N = the selection
+// rows padded to 16, double-buffered in tensor memory); sum warp w owns slot lane 32(w&3)..
+// and half of the rows (w>>2): it sums its exponentials from tensor memory, the halves meet
+// in shared memory, a_j is written (and handed to the centre warps through a double
+// buffer); centre warp c accumulates sum_j a_j v_j over slots 64c.. of the V tile while
+// the sum warps go on to the next tile. The last CTA of the head reduces the per-CTA partials
 // in CTA order into c and advances the head's generation word. Phase 2 (cooperative
 // launch, every CTA resident): each CTA waits (bounded) for the generation, the producer
 // streams its V tiles again (newest first: V was loaded with an L2 evict_last policy, so
@@ -35,11 +36,11 @@ using namespace tc;
 constexpr int kSumWarps = 8;
 constexpr int kSumThreads = kSumWarps * 32;
 static_assert(kSumThreads == 256, "one selection row per sum thread");
-constexpr int kThreads = kSumThreads + 32;
+constexpr int kCentreWarps = 2;              // sum_j a_j v_j: warp c takes slots 64c..64c+63 of each tile
+constexpr int kThreads = kSumThreads + 32 + kCentreWarps * 32;
 constexpr int kTile = 128;                   // slots per tile (= M = TMEM lanes)
 constexpr int kD = 128;
 constexpr int kMaxRows = 256;                // selection rows (N of the MMA)
-constexpr int kQBytes = kMaxRows * kD * 2;   // 64 KB
 constexpr int kBlock = kTile * 128;          // one 64-channel box of a tile: 16 KB
 constexpr int kTileBytes = 2 * kBlock;       // a K or V tile: 32 KB
 constexpr int kMaxSlots = 6;                 // tile slots (phase 1: K ring, then V ring; phase 2: V in all)
@@ -93,11 +94,11 @@ __global__ void __launch_bounds__(kThreads, 1) prefix_mass_fa(const __grid_const
   uint8_t* sQ = smem;                      // K-major [2 d blocks][Npad rows][128 B]
   __shared__ __align__(16) float sNB[kMaxRows];  // per selection row: -B_r (-inf: no contribution)
   __shared__ float sHalf[2][kTile];
-  __shared__ __align__(16) float sA[kTile];
+  __shared__ __align__(16) float sA[2][kTile];   // a_j of tiles t&1 (sum warps -> centre warps)
   __shared__ float sTot[2][kD + 1];
   __shared__ uint32_t s_taddr;
   __shared__ __align__(8) uint64_t kfull[kMaxSlots], vfull[kMaxSlots], s_full[2], s_free[2], v_free[kMaxSlots],
-      wfull[kMaxSlots], wfree[kMaxSlots], mbar_fin;
+      wfull[kMaxSlots], wfree[kMaxSlots], a_full[2], a_free[2], mbar_fin;
   __shared__ int s_abort, s_wait_ok, sLast;
 
   const int n = A.kv.nf;
@@ -137,11 +138,13 @@ __global__ void __launch_bounds__(kThreads, 1) prefix_mass_fa(const __grid_const
     for (int i = 0; i < 2; ++i) {
       mbar_init(&s_full[i], 1);
       mbar_init(&s_free[i], kSumWarps);
+      mbar_init(&a_full[i], 1);
+      mbar_init(&a_free[i], kCentreWarps);
     }
     for (int i = 0; i < kMaxSlots; ++i) {
       mbar_init(&kfull[i], 1);
       mbar_init(&vfull[i], 1);
-      mbar_init(&v_free[i], kSumWarps);
+      mbar_init(&v_free[i], kCentreWarps);
       mbar_init(&wfull[i], 1);
       mbar_init(&wfree[i], kSumWarps);
     }
@@ -197,12 +200,42 @@ __global__ void __launch_bounds__(kThreads, 1) prefix_mass_fa(const __grid_const
   __syncthreads();
   fence_after_sync();
   const uint32_t taddr = s_taddr;
-  // centre: thread = (channel chunk cc of 8 channels, slot group sg of 8 slots per tile)
-  float cacc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+  // centre warps: warp c accumulates a_j v_j over slots 64c.. of each tile, lane l over
+  // channels 4l..4l+3
+  float2 cacc0 = make_float2(0.f, 0.f), cacc1 = cacc0;
   float asum = 0.f;
-  const int cc = threadIdx.x & 15, sg = (threadIdx.x >> 4) & 15;
+  const int cw = warp - kSumWarps - 1;   // 0.. for the centre warps
 
-  if (!sum_warp) {
+  if (cw >= 0) {
+    // ------------------------------------------------------------ centre warps
+    if (centre) {
+      const uint32_t lane_off = (uint32_t)((lane & 1) * 8);   // channels 4l..: half of chunk l/2
+      for (int t = 0; t < ntiles; ++t) {
+        bool ok = mbar_wait(&a_full[t & 1], (uint32_t)(t >> 1) & 1u, kWaitNs);
+        ok = ok && mbar_wait(&vfull[t % nV], (uint32_t)(t / nV) & 1u, kWaitNs);
+        if (!ok) s_abort = 1;
+        if (!ok || s_abort) break;
+        const uint8_t* sV = sSlot + (nK + t % nV) * kTileBytes;
+        const float* a = sA[t & 1];
+#pragma unroll 8
+        for (int i = 0; i < 64; ++i) {
+          const int j = 64 * cw + i;
+          const float aj = a[j];
+          const uint2 u = *reinterpret_cast<const uint2*>(sV + chunk_off(j, lane >> 1) + lane_off);
+          const float2 v0 = make_float2(__uint_as_float(u.x << 16), __uint_as_float(u.x & 0xFFFF0000u));
+          const float2 v1 = make_float2(__uint_as_float(u.y << 16), __uint_as_float(u.y & 0xFFFF0000u));
+          cacc0 = ffma2(make_float2(aj, aj), v0, cacc0);
+          cacc1 = ffma2(make_float2(aj, aj), v1, cacc1);
+          asum += aj;
+        }
+        __syncwarp();
+        if (lane == 0) {
+          mbar_arrive(&v_free[t % nV]);
+          mbar_arrive(&a_free[t & 1]);
+        }
+      }
+    }
+  } else if (!sum_warp) {
     // ------------------------------------------------------------ producer / MMA warp
     if (lane == 0) {
       bool ok = true;
@@ -356,29 +389,16 @@ __global__ void __launch_bounds__(kThreads, 1) prefix_mass_fa(const __grid_const
           a = live ? (sHalf[0][threadIdx.x] + sHalf[1][threadIdx.x]) * inv_rows : 0.f;
           if (j < end) A.mass[(int64_t)b * A.sm0 + (int64_t)h * A.sm1 + j] = a;
         }
-        sA[threadIdx.x] = a;
+        if (centre) {
+          // sA[t&1] held tile t-2: both centre warps must be done with it
+          if (t >= 2 && !mbar_wait(&a_free[t & 1], (uint32_t)((t >> 1) - 1) & 1u, kWaitNs)) s_abort = 1;
+          sA[t & 1][threadIdx.x] = a;
+        }
       }
-      if (centre && !mbar_wait(&vfull[t % nV], (uint32_t)(t / nV) & 1u, kWaitNs)) s_abort = 1;
       if (threadIdx.x == 0) sDecide = s_abort;
       sum_sync();
       if (sDecide) break;   // every sum warp leaves at the same tile
-      if (centre) {
-        // sum_j a_j v_j: slots sg + 16i of the tile, channels 8cc..8cc+7 (16-byte reads; a
-        // warp reads two whole rows per step)
-        const uint8_t* sV = sSlot + (nK + t % nV) * kTileBytes;
-#pragma unroll 4
-        for (int i = 0; i < kTile / 16; ++i) {
-          const int j = sg + 16 * i;
-          const float a = sA[j];
-          float f[8];
-          bf16x8_to_float(*reinterpret_cast<const uint4*>(sV + chunk_off(j, cc)), f);
-#pragma unroll
-          for (int e = 0; e < 8; ++e) cacc[e] = fmaf(a, f[e], cacc[e]);
-          asum += a;
-        }
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&v_free[t % nV]);
-      }
+      if (centre && threadIdx.x == 0) mbar_arrive(&a_full[t & 1]);   // the tile's a_j are in
     }
   }
   // slots past lens[b]: mass (and score) 0
@@ -397,29 +417,28 @@ __global__ void __launch_bounds__(kThreads, 1) prefix_mass_fa(const __grid_const
   if (aborted && threadIdx.x == 0) atomicExch(A.err, 1);
   if (!centre) return;
 
-  // centre partials per slot group, in K slot 0 (drained; V tiles may stay in their slots;
+  // centre partials per centre warp, in K slot 0 (drained; V tiles may stay in their slots;
   // nK >= 1 in every mode)
-  float* sRed = reinterpret_cast<float*>(sSlot);           // [16][kD]
-  float* sAsum = sRed + 16 * kD;                           // [16]
-  // per-CTA centre partial (slot groups summed in order); the last CTA of the head
+  float* sRed = reinterpret_cast<float*>(sSlot);           // [kCentreWarps][kD]
+  float* sAsum = sRed + kCentreWarps * kD;                 // [kCentreWarps]
+  // per-CTA centre partial (the centre warps' halves summed in order); the last CTA of the head
   // reduces the partials in CTA order and publishes c by advancing the generation
-  if (sum_warp) {
-#pragma unroll
-    for (int e = 0; e < 8; ++e) sRed[sg * kD + 8 * cc + e] = cacc[e];
-    if (cc == 0) sAsum[sg] = asum;
+  if (cw >= 0) {
+    *reinterpret_cast<float4*>(sRed + cw * kD + 4 * lane) = make_float4(cacc0.x, cacc0.y, cacc1.x, cacc1.y);
+    if (lane == 0) sAsum[cw] = asum;
   }
   __syncthreads();
   float* mine = A.part + ((int64_t)bh * gridDim.x + blockIdx.x) * (kD + 1);
-  if (threadIdx.x < kD) {   // slot groups summed in order
+  if (threadIdx.x < kD) {   // the centre warps' halves, in order
     float tot = 0.f;
 #pragma unroll
-    for (int g = 0; g < 16; ++g) tot += sRed[g * kD + threadIdx.x];
+    for (int g = 0; g < kCentreWarps; ++g) tot += sRed[g * kD + threadIdx.x];
     mine[threadIdx.x] = aborted ? NAN : tot;
   }
   if (threadIdx.x == 0) {
     float tot = 0.f;
 #pragma unroll
-    for (int g = 0; g < 16; ++g) tot += sAsum[g];
+    for (int g = 0; g < kCentreWarps; ++g) tot += sAsum[g];
     mine[kD] = tot;
   }
   __threadfence();
@@ -477,7 +496,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefix_mass_fa(const __grid_const
   // every V tile of the CTA still in its phase-1 slot (the V ring never wrapped)
   const bool resident = ntiles <= nV;
   if (!sum_warp) {
-    if (lane == 0 && ok_c && !resident) {
+    if (warp == kSumWarps && lane == 0 && ok_c && !resident) {
       // the CTA's V tiles again, newest first, through every slot
       const uint64_t pol = tma::policy_evict_first();
       int u = 0;
