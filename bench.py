@@ -64,7 +64,7 @@ CONFIGS = {
 METRIC = "µs per block-step select+attend; achieved HBM GB/s vs peak; tokens/s at 1/2/4/8 GPU"
 # DRAM bytes (read + write) per launch of the step-0 attention kernel, from the ncu captures
 # summarized in profiles/attn_partial_fa_cfg2.md and profiles/attn_partial_fa_cfg4_step0.md
-ATTN_TRAFFIC_BYTES = {"cfg2": 17_140_224, "cfg4": 274_293_248}
+ATTN_TRAFFIC_BYTES = {"cfg2": 17_142_528, "cfg4": 273_547_264}
 
 
 def parse_args():
@@ -80,6 +80,9 @@ def parse_args():
     ap.add_argument("--layers", type=int, default=0,
                     help="override the config's layer count (profiling captures on a small device footprint; "
                          "the JSON line records it and is not the config's headline number)")
+    ap.add_argument("--eager", action="store_true",
+                    help="time eager block-steps instead of CUDA-graph replays (for launch lists: under ncu "
+                         "the replay of a cooperative kernel node fails to launch)")
     return ap.parse_args()
 
 
@@ -580,6 +583,8 @@ def run_ours(args):
     side = torch.cuda.Stream(dev)
     timing = "CUDA-graph replay, CUDA events"
     try:
+        if args.eager:
+            raise RuntimeError("eager steps requested")
         side.wait_stream(stream)
         with torch.cuda.stream(side):
             for retain in sorted({retain_at(i) for i in range(c["interval"])}):
@@ -597,7 +602,8 @@ def run_ours(args):
     except Exception as exc:  # a collective that cannot be captured: eager steps
         graphs.clear()
         torch.cuda.synchronize()
-        timing = f"eager steps (graph capture failed: {type(exc).__name__}), CUDA events"
+        timing = ("eager steps (--eager), CUDA events" if args.eager else
+                  f"eager steps (graph capture failed: {type(exc).__name__}), CUDA events")
 
         def step(i):
             wl.block_step(retain_at(i))
