@@ -147,13 +147,19 @@ def compact_attention(query: torch.Tensor, prefix, indices: torch.Tensor | None,
 
 
 def probe_attention(query: torch.Tensor, prefix, current_key: torch.Tensor, current_value: torch.Tensor, *,
-                    block_size: int = 32, scaling: float | None = None, probe_rows: torch.Tensor | None = None):
+                    block_size: int = 32, scaling: float | None = None, probe_rows: torch.Tensor | None = None,
+                    unpack: bool = True):
     """Lookahead probe of one layer (session.py:2317-2332): block-causal attention of the
     probe forward [block k+1 | probe blocks] over [live prefix | itself], and the prefix
     mass of the probe rows (positions block_size..T) times the number of probe blocks.
     probe_rows: those positions as a device int32 tensor (optional; avoids a host copy,
-    e.g. under CUDA-graph capture)."""
+    e.g. under CUDA-graph capture). unpack=True: a packed (k4v4) prefix is dequantized once
+    into the bf16 scratch of unpacked_prefix, as for step 0 (the probe runs the attention
+    path, whose pass 1 unpacks the prefix: splitk.py:465-480)."""
     t = query.shape[2]
+    prefix = as_prefix(prefix)
+    if unpack and prefix.nq > 0 and query.dtype == torch.bfloat16:
+        prefix = unpacked_prefix(prefix, query.shape[0], current_key.shape[1], query.shape[3])
     out, stats = splitk_attention(query, prefix, current_key, current_value, scaling=scaling,
                                   causal_block=block_size, q_pos0=0, c_pos0=0, want_prefix=True)
     rows = probe_rows if probe_rows is not None else list(range(block_size, t))
@@ -188,14 +194,21 @@ def value_score(a: torch.Tensor, v: torch.Tensor, live_mask: torch.Tensor | None
     return score.reshape(*lead, n)
 
 
-def value_score_prefix(a: torch.Tensor, prefix) -> torch.Tensor:
+def value_score_prefix(a: torch.Tensor, prefix, *, unpack: bool = True) -> torch.Tensor:
     """value_score over a cache layout (dense, packed k4v4 or paged): a [B, Hkv, n] fp32,
     the values read (dequantized) from the prefix; dead slots score 0 (session.py:27-40,
-    with the live values _live_values would dequantize, session.py:2020-2025)."""
+    with the live values _live_values dequantizes, runtime/session.py:263-268).
+    unpack=True: a packed prefix is first dequantized into the bf16 scratch of
+    unpacked_prefix -- the reference's _live_values returns the values in the compute dtype
+    (bf16) -- and scored from there; unpack=False reads the packed values in place (fp32
+    dequantization)."""
     lib = _lib.lib()
     prefix = as_prefix(prefix)
     b, h, n = a.shape
     desc = kv_descriptor(prefix, batch=b, heads=h)
+    if unpack and prefix.nq > 0 and (prefix.vf is None or prefix.vf.dtype == torch.bfloat16):
+        prefix = unpacked_prefix(prefix, b, h, desc.head_dim)
+        desc = kv_descriptor(prefix, batch=b, heads=h)
     a3 = a.to(torch.float32)
     if a3.stride(-1) != 1:
         a3 = a3.contiguous()
