@@ -78,6 +78,7 @@ struct __align__(64) Args {
   Partials P;
   int* err;
   int fuse;
+  int cmerge;                   // the group's splits form one cluster: partials in shared memory
   FusedMerge fm;
 };
 
@@ -96,6 +97,30 @@ __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
   __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
   return *reinterpret_cast<uint32_t*>(&v);
 }
+// The partial rows of a cluster's splits in their CTAs' shared memory: split s is cluster
+// rank s; its rows at sO (256 bytes per row, 16-byte chunk c of row i at c ^ (i & 15)) and
+// its (m, l) pairs at sML.
+struct ClusterPartials {
+  uint32_t o_base, ml_base;   // this CTA's sO / sML as shared::cta addresses
+  int row, l16;
+  __device__ __forceinline__ uint4 o(int s) const {
+    uint32_t a;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;\n"
+                 : "=r"(a) : "r"(o_base + (uint32_t)(row * 256 + ((l16 ^ (row & 15)) << 4))), "r"(s));
+    uint4 v;
+    asm volatile("ld.shared::cluster.v4.u32 {%0, %1, %2, %3}, [%4];\n"
+                 : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(a) : "memory");
+    return v;
+  }
+  __device__ __forceinline__ float2 ml(int s) const {
+    uint32_t a;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;\n" : "=r"(a) : "r"(ml_base + (uint32_t)(row * 8)), "r"(s));
+    uint32_t x, y;
+    asm volatile("ld.shared::cluster.v2.u32 {%0, %1}, [%2];\n" : "=r"(x), "=r"(y) : "r"(a) : "memory");
+    return make_float2(__uint_as_float(x), __uint_as_float(y));
+  }
+};
+
 // the max of 64 values (four independent max3 chains)
 __device__ __forceinline__ float max64(const float (&v)[64]) {
   float mx[4];
@@ -446,19 +471,25 @@ __global__ void __launch_bounds__(kThreads, 1) attn_partial_fa(const __grid_cons
     const float f0 = grp == 0 ? f_me : f_oth, f1 = grp == 0 ? f_oth : f_me;
     const int64_t prow = ((int64_t)bh * A.P.S + split) * A.P.Rp + r;
     const int prow0 = (int)(((int64_t)bh * A.P.S + split) * A.P.Rp + wrow0);
+    float2* sML = reinterpret_cast<float2*>(sVs + 4096);   // cluster merge: this split's (m, l)
+    uint8_t* sO = sKs;                                     // cluster merge: its rows (32 KB)
     if (s_abort != 0) {
       if (threadIdx.x == 0) atomicExch(A.err, 1);
-      if (row_ok && grp == 0) A.P.ml[prow] = make_float2(NAN, NAN);
+      if (row_ok && grp == 0) {
+        if (A.cmerge) sML[rl] = make_float2(NAN, NAN);
+        else A.P.ml[prow] = make_float2(NAN, NAN);
+      }
     } else {
       // the exact max: l under M times 2^(M - m_true) <= 1; o = acc / l is the same under
       // either reference
       if (row_ok && grp == 0) {
         const float fix = (mt == -INFINITY) ? 1.f : ex2(M - mt * c2);
-        A.P.ml[prow] = make_float2(mt * A.scale, l * fix);
+        if (A.cmerge) sML[rl] = make_float2(mt * A.scale, l * fix);
+        else A.P.ml[prow] = make_float2(mt * A.scale, l * fix);
       }
       const float inv = l > 0.f ? 1.f / l : 0.f;
       if (warp_rows) {
-        const bool via_tma = ntiles > 0 && A.tma_out;
+        const bool via_tma = ntiles > 0 && A.tma_out && !A.cmerge;
         // the warp's 32 rows x 64 channels -> one box in the K slots, 128-byte swizzled
         // (chunk q of line i at q ^ (i & 7)), stored by lane 0; else straight to global
         uint8_t* box = sKs + warp * kOutBox;
@@ -485,7 +516,13 @@ __global__ void __launch_bounds__(kThreads, 1) attn_partial_fa(const __grid_cons
 #pragma unroll
             for (int i = 0; i < 32; ++i) o[i] = 0.f;
           }
-          if (via_tma) {
+          if (A.cmerge) {   // the row into shared memory, chunk cc of row rl at cc ^ (rl & 15)
+#pragma unroll
+            for (int qq = 0; qq < 4; ++qq) {
+              const int cc = 8 * grp + 4 * c + qq;
+              *reinterpret_cast<uint4*>(sO + rl * 256 + ((cc ^ (rl & 15)) << 4)) = float8_to_bf16x8(o + 8 * qq);
+            }
+          } else if (via_tma) {
 #pragma unroll
             for (int qq = 0; qq < 4; ++qq)
               *reinterpret_cast<uint4*>(line + (((4 * c + qq) ^ (lane & 7)) << 4)) = float8_to_bf16x8(o + 8 * qq);
@@ -516,6 +553,27 @@ __global__ void __launch_bounds__(kThreads, 1) attn_partial_fa(const __grid_cons
   __syncthreads();
   fence_after_sync();
   if (warp == 0) tmem_dealloc(taddr, kTmemCols);
+  if (A.cmerge) {
+    // ---- cluster merge: the group's splits are the cluster's CTAs (rank = split); each
+    // merges its share of the rows from every rank's shared memory, by half warps
+    cluster_sync();   // every split's rows and (m, l) are in its shared memory
+    const int R_blk = min(kRowTile, R - r0);
+    const int per = (R_blk + (int)gridDim.y - 1) / (int)gridDim.y;
+    const int lo = split * per, hi = min(R_blk, lo + per);
+    __nv_bfloat16* out = reinterpret_cast<__nv_bfloat16*>(A.fm.out);
+    ClusterPartials src;
+    src.o_base = static_cast<uint32_t>(__cvta_generic_to_shared(sKs));
+    src.ml_base = static_cast<uint32_t>(__cvta_generic_to_shared(sVs + 4096));
+    src.l16 = lane & 15;
+    for (int rr0 = lo + 2 * warp; rr0 < hi; rr0 += 2 * kWarps) {   // uniform per warp
+      const int rr = rr0 + (lane >> 4);
+      src.row = rr < hi ? rr : rr0;
+      combine_row16_from<__nv_bfloat16>(A.q, H, A.nsplit, A.cur.Tc > 0, out, A.fm.so[0], A.fm.so[1], A.fm.so[2],
+                                        A.fm.m_p, A.fm.l_p, A.fm.o_p, bh, r0 + rr, rr < hi, src);
+    }
+    cluster_sync();   // no CTA leaves while another may still read its shared memory
+    return;
+  }
   if (!A.fuse) return;
 
   // ---- fused merge: every CTA of the (head, row block) group is resident (cooperative
@@ -638,9 +696,51 @@ int launch_attn_partial_fa(const ma_rows& q, const ma_kv& kv, int H, const ma_bl
   auto kernel = attn_partial_fa;
   if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes) != cudaSuccess)
     return MA_ERR_CUDA;
+  const int rows_per_split = (std::min(kRowTile, R) + (int)grid.y - 1) / (int)grid.y;
+  // cluster merge: with at most 16 splits (prefix ones + the block) a group's CTAs form one
+  // thread-block cluster and merge through distributed shared memory (no global round
+  // trips); the hardware co-schedules a cluster's CTAs, so no cooperative launch is needed.
+  // Only when every cluster is resident at once: a cluster of one-CTA-per-SM blocks needs
+  // that many free SMs in one GPC, so fewer clusters than SMs / size fit (a second wave
+  // of clusters cost more than the merge saves)
+  if (fm != nullptr && nsplit <= 16 && (int)grid.y <= 16 && rows_per_split <= 2 * kWarps) {
+    static int cluster_nc[17] = {0};   // per cluster size: resident clusters (-1 not schedulable)
+    const int cs = (int)grid.y;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = kSmemBytes;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[2];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 1;
+    attr[0].val.clusterDim.y = cs;
+    attr[0].val.clusterDim.z = 1;
+    attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[1].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    if (cluster_nc[cs] == 0) {
+      int nc = 0;
+      const bool attr_ok = cs <= 8 ||
+                           cudaFuncSetAttribute(kernel, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) == cudaSuccess;
+      cluster_nc[cs] = (attr_ok && cudaOccupancyMaxActiveClusters(&nc, kernel, &cfg) == cudaSuccess && nc >= 1) ? nc : -1;
+      (void)cudaGetLastError();
+    }
+    if (cluster_nc[cs] > 0 && (long long)grid.x * grid.z <= cluster_nc[cs]) {
+      Args Ac = A;
+      Ac.cmerge = 1;
+      Ac.fm = *fm;
+      cfg.numAttrs = 2;
+      if (cudaLaunchKernelEx(&cfg, kernel, Ac) == cudaSuccess) {
+        *fused = true;
+        return MA_OK;
+      }
+      (void)cudaGetLastError();
+    }
+  }
   // fused merge: one wave of resident CTAs (cooperative launch), when each split's share of
   // the rows is one pass of its warps
-  const int rows_per_split = (std::min(kRowTile, R) + (int)grid.y - 1) / (int)grid.y;
   const int rows_per_pass = nsplit <= 16 ? 2 * kWarps : kWarps;   // half warps or warps per row
   if (fm != nullptr && (int)(grid.x * grid.z) <= fm->sync_slots && (int)grid.y <= kCombineMaxSplits &&
       rows_per_split <= rows_per_pass) {

@@ -137,33 +137,30 @@ __device__ __forceinline__ void combine_row(const ma_rows& q, int H, const Parti
 // pair, so a warp merges two rows at once (row r of the upper half ignored when !valid;
 // every lane of the warp must call, shuffles span the whole warp). The arithmetic is
 // combine_row's: w_s = l_s exp(m_s - M), prefix statistics, then the current block.
-template <typename QT>
-__device__ __forceinline__ void combine_row16(const ma_rows& q, int H, const Partials& P, int nsplit, bool has_cur,
-                                              QT* __restrict__ out, int64_t so0, int64_t so1, int64_t so2,
-                                              float* __restrict__ m_p, float* __restrict__ l_p,
-                                              float* __restrict__ o_p, int bh, int r, bool valid) {
+// src.o(s) gives this lane's 8 channels of split s's row (bf16), src.ml(s) its (m, l);
+// split nsplit is the current block.
+template <typename QT, typename Src>
+__device__ __forceinline__ void combine_row16_from(const ma_rows& q, int H, int nsplit, bool has_cur,
+                                                   QT* __restrict__ out, int64_t so0, int64_t so1, int64_t so2,
+                                                   float* __restrict__ m_p, float* __restrict__ l_p,
+                                                   float* __restrict__ o_p, int bh, int r, bool valid, const Src& src) {
   constexpr int D = 128;
   const int G = q.Hq / H;
   const int R = G * q.T;
   const int l16 = threadIdx.x & 15;
   const int half = threadIdx.x & 16;
   const int d0 = 8 * l16;
-  const int64_t row0 = (int64_t)bh * P.S * P.Rp + r;   // partial row of split 0; split s adds s*Rp
-  const __nv_bfloat16* o = reinterpret_cast<const __nv_bfloat16*>(P.o);
   // every split's 8 channels and the current block's, in flight first
   uint4 buf[16];
 #pragma unroll
-  for (int i = 0; i < 16; ++i)
-    buf[i] = (valid && i < nsplit) ? __ldcg(reinterpret_cast<const uint4*>(o + (row0 + (int64_t)i * P.Rp) * D + d0))
-                                   : make_uint4(0u, 0u, 0u, 0u);
-  const int64_t crow = row0 + (int64_t)nsplit * P.Rp;
+  for (int i = 0; i < 16; ++i) buf[i] = (valid && i < nsplit) ? src.o(i) : make_uint4(0u, 0u, 0u, 0u);
   float2 mlc = make_float2(-INFINITY, 0.f);
   uint4 oc = make_uint4(0u, 0u, 0u, 0u);
   if (valid && has_cur) {
-    mlc = __ldcg(&P.ml[crow]);
-    oc = __ldcg(reinterpret_cast<const uint4*>(o + crow * D + d0));
+    mlc = src.ml(nsplit);
+    oc = src.o(nsplit);
   }
-  const float2 mls = (valid && l16 < nsplit) ? __ldcg(&P.ml[row0 + (int64_t)l16 * P.Rp]) : make_float2(-INFINITY, 0.f);
+  const float2 mls = (valid && l16 < nsplit) ? src.ml(l16) : make_float2(-INFINITY, 0.f);
   float M = mls.x;
 #pragma unroll
   for (int off = 8; off > 0; off >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, off));
@@ -211,6 +208,32 @@ __device__ __forceinline__ void combine_row16(const ma_rows& q, int H, const Par
   QT* dst = out + (int64_t)b * so0 + (int64_t)(h * G + g) * so1 + (int64_t)t * so2 + d0;
   store4(dst, A[0] * inv, A[1] * inv, A[2] * inv, A[3] * inv);
   store4(dst + 4, A[4] * inv, A[5] * inv, A[6] * inv, A[7] * inv);
+}
+
+// The partial rows of the global split buffers (bf16, split s of row r at row0 + s*Rp).
+struct GlobalPartials {
+  const __nv_bfloat16* po;
+  const float2* pml;
+  int64_t row0, step;
+  int d0;
+  __device__ __forceinline__ uint4 o(int s) const {
+    return __ldcg(reinterpret_cast<const uint4*>(po + (row0 + (int64_t)s * step) * 128 + d0));
+  }
+  __device__ __forceinline__ float2 ml(int s) const { return __ldcg(&pml[row0 + (int64_t)s * step]); }
+};
+
+template <typename QT>
+__device__ __forceinline__ void combine_row16(const ma_rows& q, int H, const Partials& P, int nsplit, bool has_cur,
+                                              QT* __restrict__ out, int64_t so0, int64_t so1, int64_t so2,
+                                              float* __restrict__ m_p, float* __restrict__ l_p,
+                                              float* __restrict__ o_p, int bh, int r, bool valid) {
+  GlobalPartials src;
+  src.po = reinterpret_cast<const __nv_bfloat16*>(P.o);
+  src.pml = P.ml;
+  src.row0 = (int64_t)bh * P.S * P.Rp + r;
+  src.step = P.Rp;
+  src.d0 = 8 * (threadIdx.x & 15);
+  combine_row16_from<QT>(q, H, nsplit, has_cur, out, so0, so1, so2, m_p, l_p, o_p, bh, r, valid, src);
 }
 
 }  // namespace ma
