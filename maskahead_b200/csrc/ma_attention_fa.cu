@@ -451,6 +451,7 @@ __global__ void __launch_bounds__(kThreads, 1) attn_partial_fa(const __grid_cons
   fence_before_sync();
   __syncthreads();
   fence_after_sync();
+  if (threadIdx.x == 0) pdl_launch_dependents();   // the next kernel's prologue may start
 
   if (softmax_warp) {
     // the two tile groups' row states meet (the slots are drained: scratch in the V slots):

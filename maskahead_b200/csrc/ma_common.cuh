@@ -260,6 +260,12 @@ __device__ __forceinline__ float warp_max(float v) {
 // has completed and its memory is visible -- before it touches anything an earlier
 // kernel writes or reads, and before it ends.
 __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;\n" ::: "memory"); }
+// Lets the next kernel in the stream, if launched by launch_pdl, start its CTAs (on SMs this
+// grid leaves free) once every CTA of this grid has executed it or exited; the dependent
+// still waits in pdl_wait() for this grid to complete before it touches its data.
+__device__ __forceinline__ void pdl_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;\n" ::: "memory");
+}
 
 template <typename... KArgs, typename... Args>
 inline cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,

@@ -130,8 +130,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefix_mass_fa(const __grid_const
   const int kTiles = given ? 0 : ntiles;     // tiles that need K and S^T
 
   // the head's centre generation before this CTA arrives (the last CTA advances it)
-  unsigned gen0 = 0;
-  if (centre && threadIdx.x == 0) gen0 = *reinterpret_cast<volatile const unsigned*>(&A.sync[bh].y);
+  unsigned gen0 = 0;   // read after pdl_wait (below), before this CTA arrives
   if (threadIdx.x == kSumThreads) {
     asm volatile("prefetch.tensormap [%0];\n" ::"l"(reinterpret_cast<uint64_t>(&A.kmap)) : "memory");
     asm volatile("prefetch.tensormap [%0];\n" ::"l"(reinterpret_cast<uint64_t>(&A.vmap)) : "memory");
@@ -163,8 +162,10 @@ __global__ void __launch_bounds__(kThreads, 1) prefix_mass_fa(const __grid_const
   }
   if (sum_warp && given) {
     pdl_wait();   // a (and with a programmatic launch, the outputs) of the kernel before
+    if (centre && threadIdx.x == 0) gen0 = *reinterpret_cast<volatile const unsigned*>(&A.sync[bh].y);
   } else if (sum_warp) {
     pdl_wait();   // m_p, l_p (and with a programmatic launch, the outputs) of the kernel before
+    if (centre && threadIdx.x == 0) gen0 = *reinterpret_cast<volatile const unsigned*>(&A.sync[bh].y);
     // one selection row per thread (kSumThreads == kMaxRows): r2 = g*T2 + i -> query row
     // (h*G + g, q_rows[i]), -B_r, and the row's query into the K-major SW128 Q tile of Npad
     // rows (zeros for padding rows)
@@ -412,6 +413,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefix_mass_fa(const __grid_const
   fence_before_sync();
   __syncthreads();
   fence_after_sync();
+  if (threadIdx.x == 0) pdl_launch_dependents();   // the next kernel's prologue may start
   if (warp == 0) tmem_dealloc(taddr, kTmemCols);
   const bool aborted = s_abort != 0;
   if (aborted && threadIdx.x == 0) atomicExch(A.err, 1);

@@ -270,6 +270,7 @@ select_topk_reg(const float* __restrict__ score, int H, int n, int64_t ss0, int6
     pmask |= 255u << shift;
     kk -= sSel[pass & 1][1];
   }
+  if (threadIdx.x == 0) pdl_launch_dependents();   // the next kernel's prologue may start
   // emission in slot order: keys above the k-th plus the first kk ties
   int gt = 0, eq = 0;
 #pragma unroll
@@ -654,6 +655,8 @@ __global__ void gather_kv_kernel(ma_kv kv, int H, int D, const int64_t* __restri
                                  int64_t si0, int64_t si1, OT* __restrict__ ok_,
                                  OT* __restrict__ ov_, int64_t sok0, int64_t sok1, int64_t sok2,
                                  int64_t sov0, int64_t sov1, int64_t sov2) {
+  pdl_wait();   // the read set of the kernel before
+  if (threadIdx.x == 0) pdl_launch_dependents();
   const int bh = blockIdx.y;
   const int b = bh / H, h = bh - (bh / H) * H;
   const int chunks = D / 8;
@@ -854,13 +857,11 @@ int launch_gather_kv(const ma_kv& kv, int B, int H, int D, const int64_t* idx, i
   }
   dim3 grid((k + kGatherTok - 1) / kGatherTok, B * H);
   if (out_dtype == MA_F32) {
-    gather_kv_kernel<float><<<grid, 256, 0, st>>>(kv, H, D, idx, k, si0, si1, (float*)out_k,
-                                                  (float*)out_v, sok[0], sok[1], sok[2], sov[0],
-                                                  sov[1], sov[2]);
+    launch_pdl(gather_kv_kernel<float>, grid, dim3(256), 0, st, kv, H, D, idx, k, si0, si1, (float*)out_k,
+               (float*)out_v, sok[0], sok[1], sok[2], sov[0], sov[1], sov[2]);
   } else {
-    gather_kv_kernel<__nv_bfloat16><<<grid, 256, 0, st>>>(
-        kv, H, D, idx, k, si0, si1, (__nv_bfloat16*)out_k, (__nv_bfloat16*)out_v, sok[0], sok[1],
-        sok[2], sov[0], sov[1], sov[2]);
+    launch_pdl(gather_kv_kernel<__nv_bfloat16>, grid, dim3(256), 0, st, kv, H, D, idx, k, si0, si1,
+               (__nv_bfloat16*)out_k, (__nv_bfloat16*)out_v, sok[0], sok[1], sok[2], sov[0], sov[1], sov[2]);
   }
   return cudaGetLastError() == cudaSuccess ? MA_OK : MA_ERR_CUDA;
 }
