@@ -193,8 +193,7 @@ __global__ void __launch_bounds__(kThreads, 1) attn_partial_fa(const __grid_cons
   const float c2 = A.scale * kLog2e;
   const int group = bh * gridDim.x + blockIdx.x;
 
-  unsigned gen0 = 0;   // the merge generation, read before this CTA arrives (thread 0)
-  if (A.fuse && threadIdx.x == 0) gen0 = *reinterpret_cast<volatile const unsigned*>(&A.fm.sync[group].y);
+  unsigned gen0 = 0;   // the merge generation, read after pdl_wait, before this CTA arrives (thread 0)
   if (threadIdx.x == kSoftThreads) {
     prefetch_map(&A.qmap);
     prefetch_map(is_cur ? &A.ckmap : &A.kmap);
@@ -353,6 +352,7 @@ __global__ void __launch_bounds__(kThreads, 1) attn_partial_fa(const __grid_cons
     // a sub-partition work on different tiles, so one's exponentials overlap the other's
     // tensor-memory reads, maxima and stores
     pdl_wait();   // the partials and outputs may still be in use by the kernel before
+    if (A.fuse && threadIdx.x == 0) gen0 = *reinterpret_cast<volatile const unsigned*>(&A.fm.sync[group].y);
     const float2 c2x2 = make_float2(c2, c2);
     int k = 0;   // this warp's tiles done
     for (int t = grp; t < ntiles; t += 2, ++k) {
@@ -758,16 +758,20 @@ int launch_attn_partial_fa(const ma_rows& q, const ma_kv& kv, int H, const ma_bl
       cfg.blockDim = dim3(kThreads);
       cfg.dynamicSmemBytes = kSmemBytes;
       cfg.stream = st;
-      cudaLaunchAttribute attr[1];
+      cudaLaunchAttribute attr[2];
       attr[0].id = cudaLaunchAttributeCooperative;
       attr[0].val.cooperative = 1;
+      attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;   // tried first
+      attr[1].val.programmaticStreamSerializationAllowed = 1;
       cfg.attrs = attr;
-      cfg.numAttrs = 1;
-      if (cudaLaunchKernelEx(&cfg, kernel, Af) == cudaSuccess) {
-        *fused = true;
-        return MA_OK;
+      for (int na = 2; na >= 1; --na) {
+        cfg.numAttrs = na;
+        if (cudaLaunchKernelEx(&cfg, kernel, Af) == cudaSuccess) {
+          *fused = true;
+          return MA_OK;
+        }
+        (void)cudaGetLastError();
       }
-      (void)cudaGetLastError();
     }
   }
   return launch_pdl(kernel, grid, dim3(kThreads), kSmemBytes, st, A) == cudaSuccess ? MA_OK : MA_ERR_CUDA;

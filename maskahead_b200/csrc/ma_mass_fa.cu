@@ -652,16 +652,20 @@ int launch_prefix_mass_fa(const ma_rows& q, const ma_kv& kv, int H, const int32_
       cfg.blockDim = dim3(kThreads);
       cfg.dynamicSmemBytes = smem;
       cfg.stream = st;
-      cudaLaunchAttribute attr[1];
+      cudaLaunchAttribute attr[2];
       attr[0].id = cudaLaunchAttributeCooperative;
       attr[0].val.cooperative = 1;
+      attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;   // tried first
+      attr[1].val.programmaticStreamSerializationAllowed = 1;
       cfg.attrs = attr;
-      cfg.numAttrs = 1;
-      if (cudaLaunchKernelEx(&cfg, prefix_mass_fa, Ac) == cudaSuccess) {
-        *fused = true;
-        return MA_OK;
+      for (int na = 2; na >= 1; --na) {
+        cfg.numAttrs = na;
+        if (cudaLaunchKernelEx(&cfg, prefix_mass_fa, Ac) == cudaSuccess) {
+          *fused = true;
+          return MA_OK;
+        }
+        (void)cudaGetLastError();
       }
-      (void)cudaGetLastError();
     }
   }
   return launch_pdl(prefix_mass_fa, grid, dim3(kThreads), smem, st, A) == cudaSuccess ? MA_OK : MA_ERR_CUDA;
@@ -725,13 +729,17 @@ int launch_value_score_fa(const ma_kv& kv, int B, int H, int D, const float* a, 
     cfg.blockDim = dim3(kThreads);
     cfg.dynamicSmemBytes = smem;
     cfg.stream = st;
-    cudaLaunchAttribute attr[1];
+    cudaLaunchAttribute attr[2];
     attr[0].id = cudaLaunchAttributeCooperative;
     attr[0].val.cooperative = 1;
+    attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;   // tried first
+    attr[1].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
-    cfg.numAttrs = 1;
-    if (cudaLaunchKernelEx(&cfg, prefix_mass_fa, A) == cudaSuccess) return MA_OK;
-    (void)cudaGetLastError();
+    for (int na = 2; na >= 1; --na) {
+      cfg.numAttrs = na;
+      if (cudaLaunchKernelEx(&cfg, prefix_mass_fa, A) == cudaSuccess) return MA_OK;
+      (void)cudaGetLastError();
+    }
   }
   return MA_ERR_UNSUPPORTED;
 }
