@@ -240,6 +240,16 @@ MA_API int ma_gather_kv(const ma_kv* kv, int B, int H, int D, const int64_t* idx
                  const int64_t sidx[2], void* out_k, void* out_v, const int64_t sok[3],
                  const int64_t sov[3], int32_t out_dtype, void* stream);
 
+/* ---- unpack of the live slots --------------------------------------------------------
+ * The step-0 unpack of a token-mode packed prefix (splitk.py:465-480 dequantizes the
+ * prefix before attending): out_k/out_v [B,H,nq+nf,128] bf16 get every slot below
+ * lens[b] (every slot without lens) dequantized as ma_gather_kv(idx = NULL) does; slots
+ * at or past lens[b] are NOT written (ma_gather_kv zero-fills them), which spares a
+ * ragged batch the writes for its padding. Consumers that honour lens never read them.
+ * Other layouts: MA_ERR_UNSUPPORTED.                                                  */
+MA_API int ma_unpack_prefix(const ma_kv* kv, int B, int H, int D, void* out_k, void* out_v,
+                            const int64_t sok[3], const int64_t sov[3], void* stream);
+
 /* ---- quantize-on-append -------------------------------------------------------------
  * Dense rows x [B,H,n,D] (MA_BF16 or MA_F32, strides over (b, h, slot)) -> 4-bit codes
  * with fp16 scale/zero, as the reference's quantizers compute them in x's dtype

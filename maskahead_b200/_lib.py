@@ -15,6 +15,7 @@ import torch
 LIB_PATH = Path(__file__).resolve().parent / "_lib" / "libmaskahead_b200.so"
 
 MA_OK = 0
+MA_ERR_UNSUPPORTED = -2
 MA_F32, MA_BF16, MA_F16 = 0, 1, 2
 MA_KV_DENSE, MA_KV_PACKED_TOKEN, MA_KV_PACKED_CHANNEL = 0, 1, 2
 
@@ -90,6 +91,7 @@ _SIGNATURES = {
                                    _P(MaBlock), _f32, _vp, _P(ctypes.c_int64), _vp, _sz, _vp]),
     "ma_gather_kv": (_i32, [_P(MaKV), _i32, _i32, _i32, _vp, _i32, _P(ctypes.c_int64), _vp, _vp,
                             _P(ctypes.c_int64), _P(ctypes.c_int64), _i32, _vp]),
+    "ma_unpack_prefix": (_i32, [_P(MaKV), _i32, _i32, _i32, _vp, _vp, _P(ctypes.c_int64), _P(ctypes.c_int64), _vp]),
     "ma_quantize_tokens": (_i32, [_vp, _i32, _i32, _i32, _i32, _i32, _P(ctypes.c_int64), _vp,
                                   _P(ctypes.c_int64), _i32, _vp, _P(ctypes.c_int64), _vp, _vp,
                                   _P(ctypes.c_int64), _vp]),

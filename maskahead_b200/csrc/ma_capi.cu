@@ -450,4 +450,15 @@ int ma_gather_kv(const ma_kv* kv, int B, int H, int D, const int64_t* idx, int k
                           out_dtype, (cudaStream_t)stream);
 }
 
+int ma_unpack_prefix(const ma_kv* kv, int B, int H, int D, void* out_k, void* out_v, const int64_t sok[3],
+                     const int64_t sov[3], void* stream) {
+  if (B <= 0 || H <= 0) return MA_ERR_ARG;
+  if (D != 128) return MA_ERR_UNSUPPORTED;
+  int rc = check_kv(kv, D);
+  if (rc) return rc;
+  if (!out_k || !out_v || !sok || !sov) return MA_ERR_ARG;
+  if (!aligned16(out_k) || !aligned16(out_v) || !strides16(sok, 3, 2) || !strides16(sov, 3, 2)) return MA_ERR_ARG;
+  return launch_unpack_live(*kv, B, H, D, out_k, out_v, sok, sov, (cudaStream_t)stream);
+}
+
 }  // extern "C"

@@ -109,6 +109,10 @@ int launch_key_divisor(const void* k, int dtype, int B, int H, int n, int D, con
 int launch_retain(const float* score, const int32_t* phys, int n_phys, const int32_t* pos,
                   int lanes, int live, int capacity, int recent_window, int sink_tokens,
                   int64_t* keep, cudaStream_t st);
+// every slot below lens[b] (all nq + nf without lens) of a token-mode packed prefix into
+// contiguous bf16 rows; slots at or past lens[b] are not written
+int launch_unpack_live(const ma_kv& kv, int B, int H, int D, void* out_k, void* out_v, const int64_t sok[3],
+                       const int64_t sov[3], cudaStream_t st);
 int launch_gather_kv(const ma_kv& kv, int B, int H, int D, const int64_t* idx, int k, int64_t si0,
                      int64_t si1, void* out_k, void* out_v, const int64_t sok[3],
                      const int64_t sov[3], int out_dtype, cudaStream_t st);

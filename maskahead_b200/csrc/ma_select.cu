@@ -702,13 +702,16 @@ __device__ __forceinline__ void unpack32(const uint4& p, float s, float z, const
   }
 }
 
+// live_only: slots at or past lens[b] are skipped (not written) instead of zero-filled
 __global__ void __launch_bounds__(256) unpack_token_kernel(ma_kv kv, int H, int n, __nv_bfloat16* __restrict__ ok_,
                                                            __nv_bfloat16* __restrict__ ov_, int64_t sok0, int64_t sok1,
-                                                           int64_t sok2, int64_t sov0, int64_t sov1, int64_t sov2) {
+                                                           int64_t sok2, int64_t sov0, int64_t sov1, int64_t sov2,
+                                                           int live_only) {
   const int bh = blockIdx.y;
   const int b = bh / H, h = bh - (bh / H) * H;
   const int jj = threadIdx.x >> 2, g = threadIdx.x & 3;
   const float* kch = kv.kchan + (int64_t)b * kv.skc[0] + (int64_t)h * kv.skc[1] + 32 * g;
+  if (live_only && kv.lens) n = max(0, min(n, kv.lens[b]));
   for (int j = blockIdx.x * kUnpackTok + jj; j < n; j += gridDim.x * kUnpackTok) {
     __nv_bfloat16* dk = ok_ + (int64_t)b * sok0 + (int64_t)h * sok1 + (int64_t)j * sok2 + 32 * g;
     __nv_bfloat16* dv = ov_ + (int64_t)b * sov0 + (int64_t)h * sov1 + (int64_t)j * sov2 + 32 * g;
@@ -841,6 +844,21 @@ int launch_retain(const float* score, const int32_t* phys, int n_phys, const int
   return cudaGetLastError() == cudaSuccess ? MA_OK : MA_ERR_CUDA;
 }
 
+int launch_unpack_live(const ma_kv& kv, int B, int H, int D, void* out_k, void* out_v, const int64_t sok[3],
+                       const int64_t sov[3], cudaStream_t st) {
+  const int k = kv.nq + kv.nf;
+  if (!(kv.layout == MA_KV_PACKED_TOKEN && kv.dtype == MA_BF16 && D == 128 && kv.kchan && kv.vgroup == 32 &&
+        kv.kgroup == 32 && (kv.nf == 0 || kv.kf)))
+    return MA_ERR_UNSUPPORTED;
+  if (k == 0) return MA_OK;
+  int gx = (k + kUnpackTok - 1) / kUnpackTok;
+  if (gx > 8) gx = (gx + 3) / 4;   // each CTA takes about four 64-slot rows
+  dim3 ugrid(gx, B * H);
+  unpack_token_kernel<<<ugrid, 256, 0, st>>>(kv, H, k, (__nv_bfloat16*)out_k, (__nv_bfloat16*)out_v, sok[0], sok[1],
+                                             sok[2], sov[0], sov[1], sov[2], 1);
+  return cudaGetLastError() == cudaSuccess ? MA_OK : MA_ERR_CUDA;
+}
+
 int launch_gather_kv(const ma_kv& kv, int B, int H, int D, const int64_t* idx, int k, int64_t si0,
                      int64_t si1, void* out_k, void* out_v, const int64_t sok[3],
                      const int64_t sov[3], int out_dtype, cudaStream_t st) {
@@ -852,7 +870,7 @@ int launch_gather_kv(const ma_kv& kv, int B, int H, int D, const int64_t* idx, i
     if (gx > 8) gx = (gx + 3) / 4;   // each CTA takes about four 64-slot rows
     dim3 ugrid(gx, B * H);
     unpack_token_kernel<<<ugrid, 256, 0, st>>>(kv, H, k, (__nv_bfloat16*)out_k, (__nv_bfloat16*)out_v, sok[0], sok[1],
-                                               sok[2], sov[0], sov[1], sov[2]);
+                                               sok[2], sov[0], sov[1], sov[2], 0);
     return cudaGetLastError() == cudaSuccess ? MA_OK : MA_ERR_CUDA;
   }
   dim3 grid((k + kGatherTok - 1) / kGatherTok, B * H);

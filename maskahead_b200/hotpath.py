@@ -97,7 +97,20 @@ def unpacked_prefix(prefix, batch: int, heads: int, head_dim: int) -> Prefix:
     nbytes = batch * heads * n * head_dim * 2
     kb = _lib.workspace(dev, "unpack_k", nbytes)[:nbytes].view(torch.bfloat16).view(batch, heads, n, head_dim)
     vb = _lib.workspace(dev, "unpack_v", nbytes)[:nbytes].view(torch.bfloat16).view(batch, heads, n, head_dim)
-    dequantize_prefix(prefix, batch, heads, head_dim, out=(kb, vb))
+    rc = _lib.MA_ERR_UNSUPPORTED
+    if n > 0 and prefix.lens is not None:
+        # a ragged batch: only the slots below each sequence's length are written (every
+        # consumer of the returned Prefix honours its lens)
+        unmasked = Prefix(**{s: getattr(prefix, s) for s in Prefix.__slots__})
+        unmasked.mask = None
+        desc = kv_descriptor(unmasked, batch=batch, heads=heads, head_dim=head_dim)
+        rc = _lib.lib().ma_unpack_prefix(desc.kv, batch, heads, head_dim, kb.data_ptr(), vb.data_ptr(),
+                                         _lib.i64(*kb.stride()[:3]), _lib.i64(*vb.stride()[:3]),
+                                         _lib.stream_handle(dev))
+        if rc != _lib.MA_ERR_UNSUPPORTED:
+            _lib.check("ma_unpack_prefix", rc)
+    if rc == _lib.MA_ERR_UNSUPPORTED:
+        dequantize_prefix(prefix, batch, heads, head_dim, out=(kb, vb))
     return Prefix(kf=kb, vf=vb, nf=n, mask=prefix.mask, lens=prefix.lens)
 
 

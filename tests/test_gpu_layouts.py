@@ -178,3 +178,36 @@ def test_bad_page_entries_read_as_dead():
     assert (res.mass[1, :, 64:128].cpu() == 0).all()
     assert (res.indices[1].cpu() < 64).all()
     assert torch.isfinite(res.out.float()).all()
+
+
+def test_unpack_prefix_writes_the_live_slots_only():
+    """ma_unpack_prefix (the step-0 unpack of a ragged batch): the slots below each
+    sequence's length equal ma_gather_kv's whole-prefix dequantization, bit for bit, and the
+    slots past it keep what the buffer held (a sentinel here); without lens every slot is
+    written. The unpacked prefix then gives the same step 0 as the packed one."""
+    from maskahead_b200._lib import i64, lib as get_lib
+    from maskahead_b200.hotpath import unpacked_prefix
+    from maskahead_b200.kernels.splitk import dequantize_prefix
+    from maskahead_b200.layouts import kv_descriptor
+
+    c = _paged_batch("k4v4_token", lens=(448, 320, 200))
+    pre, lens = c["prefix"], c["lens"]
+    B, H, D = len(lens), 2, c["D"]          # _paged_batch's default H
+    n = max(lens)
+    want_k, want_v = dequantize_prefix(pre, B, H, D)
+    ko = torch.full((B, H, n, D), 7.0, dtype=torch.bfloat16, device=DEV)
+    vo = torch.full_like(ko, -3.0)
+    lib = get_lib()
+    desc = kv_descriptor(pre, batch=B, heads=H, head_dim=D)
+    rc = lib.ma_unpack_prefix(desc.kv, B, H, D, ko.data_ptr(), vo.data_ptr(), i64(*ko.stride()[:3]),
+                              i64(*vo.stride()[:3]), torch.cuda.current_stream().cuda_stream)
+    assert rc == 0
+    torch.cuda.synchronize()
+    for b, L in enumerate(lens):
+        assert torch.equal(ko[b, :, :L].cpu(), want_k[b, :, :L].cpu())
+        assert torch.equal(vo[b, :, :L].cpu(), want_v[b, :, :L].cpu())
+        assert bool((ko[b, :, L:] == 7.0).all()) and bool((vo[b, :, L:] == -3.0).all())
+    un = unpacked_prefix(pre, B, H, D)
+    for b, L in enumerate(lens):
+        assert torch.equal(un.kf[b, :, :L].cpu(), want_k[b, :, :L].cpu())
+        assert torch.equal(un.vf[b, :, :L].cpu(), want_v[b, :, :L].cpu())
