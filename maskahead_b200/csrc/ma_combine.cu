@@ -26,6 +26,23 @@ attn_combine_kernel(ma_rows q, int H, Partials P, int nsplit, int has_cur, QT* _
   combine_row<QT, OT>(q, H, P, nsplit, has_cur != 0, out, so0, so1, so2, m_p, l_p, o_p, blockIdx.y, r, sW[warp]);
 }
 
+// bf16 partials of D = 128 with at most 16 prefix splits: a half warp per row (every
+// split's row in flight at once), two rows per warp
+template <typename QT>
+__global__ void __launch_bounds__(kWarps * 32)
+attn_combine16_kernel(ma_rows q, int H, Partials P, int nsplit, int has_cur, QT* __restrict__ out,
+                      int64_t so0, int64_t so1, int64_t so2, float* __restrict__ m_p,
+                      float* __restrict__ l_p, float* __restrict__ o_p) {
+  pdl_wait();   // the partials of the attention kernel before
+  const int R = (q.Hq / H) * q.T;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int r0 = (blockIdx.x * kWarps + warp) * 2;
+  if (r0 >= R) return;   // warp-uniform
+  const int r = r0 + (lane >> 4);
+  combine_row16<QT>(q, H, P, nsplit, has_cur != 0, out, so0, so1, so2, m_p, l_p, o_p, blockIdx.y, r < R ? r : r0,
+                    r < R);
+}
+
 }  // namespace
 
 int launch_attn_combine(const ma_rows& q, int H, const Partials& P, int nsplit, bool has_cur,
@@ -33,6 +50,16 @@ int launch_attn_combine(const ma_rows& q, int H, const Partials& P, int nsplit, 
                         cudaStream_t st) {
   const int G = q.Hq / H;
   const int R = G * q.T;
+  if (P.o_bf16 && q.D == 128 && nsplit <= 16) {   // half warps per row
+    dim3 grid16((R + 2 * kWarps - 1) / (2 * kWarps), q.B * H);
+    if (q.dtype == MA_F32)
+      launch_pdl(attn_combine16_kernel<float>, grid16, dim3(kWarps * 32), 0, st, q, H, P, nsplit, has_cur ? 1 : 0,
+                 reinterpret_cast<float*>(out), so[0], so[1], so[2], m_p, l_p, o_p);
+    else
+      launch_pdl(attn_combine16_kernel<__nv_bfloat16>, grid16, dim3(kWarps * 32), 0, st, q, H, P, nsplit,
+                 has_cur ? 1 : 0, reinterpret_cast<__nv_bfloat16*>(out), so[0], so[1], so[2], m_p, l_p, o_p);
+    return cudaGetLastError() == cudaSuccess ? MA_OK : MA_ERR_CUDA;
+  }
   dim3 grid((R + kWarps - 1) / kWarps, q.B * H);
   auto go = [&](auto qt, auto ot) {
     using QT = decltype(qt);

@@ -57,6 +57,7 @@ def _run(which, q, k, v, kc, vc, causal, q_pos0, c_pos0, want_prefix):
     (1, 16, 4, 96, 3000, 96, 32),    # T = 96 (a block + two probe blocks): 32-row query pieces
     (2, 4, 4, 96, 700, 96, 32),      # T = 96, one head per group: R = 96 < one row tile
     (1, 6, 2, 160, 1000, 160, 32),   # T = 160: pieces straddle row tiles, R = 480
+    (8, 28, 4, 32, 8192, 32, 32),    # 192 CTAs: no single wave, the separate (half-warp) merge
 ])
 def test_fa_kernel_matches_oracle_and_tc(B, Hq, H, T, n, Tc, causal):
     gen = torch.Generator().manual_seed(1000 * n + T + Hq)
