@@ -34,6 +34,8 @@
  *   ma_quantize_tokens, ma_quantize_keys_channel, ma_key_divisor
  *                        reference.py:58-90, 182-213 and cache.py:484-497 (the packing
  *                        of the append path)
+ *   ma_compact_tokens    cache.py:659-678 (compact_tokens) and 342-365 (compact): the
+ *                        cache compaction after an eviction (runtime/session.py:270-302)
  */
 #ifndef MASKAHEAD_B200_H
 #define MASKAHEAD_B200_H
@@ -249,6 +251,24 @@ MA_API int ma_gather_kv(const ma_kv* kv, int B, int H, int D, const int64_t* idx
  * Other layouts: MA_ERR_UNSUPPORTED.                                                  */
 MA_API int ma_unpack_prefix(const ma_kv* kv, int B, int H, int D, void* out_k, void* out_v,
                             const int64_t sok[3], const int64_t sov[3], void* stream);
+
+/* ---- compaction of the retained slots ------------------------------------------------
+ * After an eviction decision keep [B,H,C] (int64 physical slot indices, slot axis
+ * contiguous, strides skeep over (b, h)), slot j < C of dst gets the stored bytes of
+ * slot keep[b,h,j] of src, every array of the layout moved bit-exactly: the payloads and
+ * fp16 scale/zero of a token-mode packed cache (cache.py:659-678 compact_tokens, which
+ * re-quantizes nothing), K/V of a dense bf16/fp32 cache (cache.py:342-365 compact, whose
+ * bf16 re-staging is exact). Out of place: src and dst describe two caches of the same
+ * layout, dtype and vgroup whose arrays must not overlap; dst's arrays are written (its
+ * pointers are const only because ma_kv's are). Needs C <= the slots of src (nq packed,
+ * nf dense) and of dst. A packed src must have no dense tail (nf == 0: the reference
+ * requires a fully quantized cache); channel-mode keys (rebuilt by key groups,
+ * cache.py:236-335) and paged storage: MA_ERR_UNSUPPORTED. kchan, mask and lens are not
+ * read; a keep index outside [0, n) writes a zero row (the reference's gather raises).
+ * Several layers at once: pass [L*B] as B when the layer axis merges with the batch
+ * axis (contiguous [L,B,H,...] caches).                                               */
+MA_API int ma_compact_tokens(const ma_kv* src, const ma_kv* dst, int B, int H, int D, const int64_t* keep,
+                             int C, const int64_t skeep[2], void* stream);
 
 /* ---- quantize-on-append -------------------------------------------------------------
  * Dense rows x [B,H,n,D] (MA_BF16 or MA_F32, strides over (b, h, slot)) -> 4-bit codes

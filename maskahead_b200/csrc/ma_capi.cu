@@ -461,4 +461,77 @@ int ma_unpack_prefix(const ma_kv* kv, int B, int H, int D, void* out_k, void* ou
   return launch_unpack_live(*kv, B, H, D, out_k, out_v, sok, sov, (cudaStream_t)stream);
 }
 
+namespace {
+
+// largest power-of-two vector (<= 16 bytes) that divides the row, both bases and every stride
+int compact_vec(const void* src, const void* dst, int row_bytes, const int64_t ss[3], const int64_t ds[3]) {
+  uint64_t bits = (uint64_t)row_bytes | reinterpret_cast<uintptr_t>(src) | reinterpret_cast<uintptr_t>(dst);
+  for (int i = 0; i < 3; ++i) bits |= (uint64_t)ss[i] | (uint64_t)ds[i];
+  int v = 16;
+  while (v > 1 && (bits & (uint64_t)(v - 1))) v >>= 1;
+  return v;
+}
+
+// appends one array (element strides es/ed of an element of `elem` bytes) to the plan
+int compact_add(CompactParams& p, const void* src, const void* dst, const int64_t es[3], const int64_t ed[3],
+                int elem, int row_bytes) {
+  if (!src || !dst) return MA_ERR_ARG;
+  if (src == dst) return MA_ERR_ARG;   // out of place only
+  CompactArray& a = p.arrays[p.narrays++];
+  a.src = static_cast<const unsigned char*>(src);
+  a.dst = static_cast<unsigned char*>(const_cast<void*>(dst));
+  for (int i = 0; i < 3; ++i) {
+    if (es[i] < 0 || ed[i] < 0) return MA_ERR_ARG;
+    a.ss[i] = es[i] * elem;
+    a.ds[i] = ed[i] * elem;
+  }
+  if (a.ds[2] < row_bytes) return MA_ERR_ARG;   // destination rows must not overlap
+  a.row_bytes = row_bytes;
+  a.vec_bytes = compact_vec(src, dst, row_bytes, a.ss, a.ds);
+  return MA_OK;
+}
+
+}  // namespace
+
+int ma_compact_tokens(const ma_kv* src, const ma_kv* dst, int B, int H, int D, const int64_t* keep, int C,
+                      const int64_t skeep[2], void* stream) {
+  if (B <= 0 || H <= 0 || C < 0 || !src || !dst) return MA_ERR_ARG;
+  if (D != 64 && D != 128) return MA_ERR_UNSUPPORTED;
+  int rc = check_kv(src, D);
+  if (rc) return rc;
+  if (src->pages || dst->pages) return MA_ERR_UNSUPPORTED;
+  if (src->layout == MA_KV_PACKED_CHANNEL) return MA_ERR_UNSUPPORTED;
+  if (dst->layout != src->layout || dst->dtype != src->dtype) return MA_ERR_ARG;
+  CompactParams p{};
+  p.H = H;
+  p.C = C;
+  if (src->layout == MA_KV_DENSE) {
+    p.n = src->nf;
+    if (C > src->nf || C > dst->nf) return MA_ERR_ARG;
+    if (C == 0) return MA_OK;
+    const int row = D * esize(src->dtype);
+    if ((rc = compact_add(p, src->kf, dst->kf, src->skf, dst->skf, esize(src->dtype), row))) return rc;
+    if ((rc = compact_add(p, src->vf, dst->vf, src->svf, dst->svf, esize(src->dtype), row))) return rc;
+  } else {
+    // per-token codes only: a dense tail must have been quantized first (cache.py:662-663)
+    if (src->nf != 0) return MA_ERR_UNSUPPORTED;
+    if (dst->vgroup != src->vgroup) return MA_ERR_ARG;
+    p.n = src->nq;
+    if (C > src->nq || C > dst->nq) return MA_ERR_ARG;
+    if (C == 0) return MA_OK;
+    const int groups = D / src->vgroup;
+    if ((rc = compact_add(p, src->kq, dst->kq, src->skq, dst->skq, 1, D / 2))) return rc;
+    if ((rc = compact_add(p, src->ks, dst->ks, src->sks, dst->sks, 2, groups * 2))) return rc;
+    if ((rc = compact_add(p, src->kz, dst->kz, src->sks, dst->sks, 2, groups * 2))) return rc;
+    if ((rc = compact_add(p, src->vq, dst->vq, src->svq, dst->svq, 1, D / 2))) return rc;
+    if ((rc = compact_add(p, src->vs, dst->vs, src->svs, dst->svs, 2, groups * 2))) return rc;
+    if ((rc = compact_add(p, src->vz, dst->vz, src->svs, dst->svs, 2, groups * 2))) return rc;
+  }
+  if (!keep || !skeep || skeep[0] < 0 || skeep[1] < 0) return MA_ERR_ARG;
+  p.keep = keep;
+  p.sk0 = skeep[0];
+  p.sk1 = skeep[1];
+  return launch_compact(p, B, (cudaStream_t)stream);
+}
+
 }  // extern "C"

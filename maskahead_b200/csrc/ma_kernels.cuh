@@ -117,6 +117,28 @@ int launch_gather_kv(const ma_kv& kv, int B, int H, int D, const int64_t* idx, i
                      int64_t si1, void* out_k, void* out_v, const int64_t sok[3],
                      const int64_t sov[3], int out_dtype, cudaStream_t st);
 
+// ma_compact.cu: one array of a cache layout moved by the compaction, byte strides over
+// (b, h, slot); vec_bytes divides row_bytes, both bases and every stride
+struct CompactArray {
+  const unsigned char* src;
+  unsigned char* dst;
+  int64_t ss[3];
+  int64_t ds[3];
+  int row_bytes;
+  int vec_bytes;
+};
+constexpr int kCompactMaxArrays = 6;
+struct CompactParams {
+  CompactArray arrays[kCompactMaxArrays];
+  int narrays;
+  const int64_t* keep;   // [B, H, C], strides sk0, sk1 over (b, h), slot axis contiguous
+  int64_t sk0, sk1;
+  int H, C;
+  int64_t n;             // source slots: a keep index outside [0, n) writes a zero row
+  int chunks;            // set by launch_compact
+};
+int launch_compact(CompactParams& p, int B, cudaStream_t st);
+
 // device properties, cached per device
 int device_sm_count();
 

@@ -297,3 +297,51 @@ def pack_prefix(key: torch.Tensor, value: torch.Tensor, *, key_mode: str = "toke
         kq, ks, kz = quantize_keys_channel(key, group=group)
         return Prefix(kq=kq, ks=ks, kz=kz, vq=vq, vs=vs, vz=vz, nq=n, kb=4, vb=4, kg=group, vg=group, kmode=0)
     raise ValueError(f"key_mode must be 'token' or 'channel', got {key_mode!r}")
+
+
+# ------------------------------------------------------------ compaction after eviction
+def compact_tokens(prefix, keep: torch.Tensor, out: Prefix | None = None) -> Prefix:
+    """Move the kept slots of a cache to the front: slot j of the result holds slot
+    keep[b, h, j] of ``prefix``, every array moved bit-exactly (cache.py:659-678
+    compact_tokens for token-mode packed caches; cache.py:342-365 compact for dense
+    bf16/fp32 caches). keep [B, H, C] int64 physical slots. Out of place: the result goes
+    to ``out`` (a Prefix of the same layout with at least C slots, whose arrays do not
+    overlap the source's) or to new tensors of C slots. Channel-mode keys, paged storage
+    and a packed cache with a dense tail raise (the reference requires a fully quantized
+    cache, cache.py:662-663). The result carries no mask: every slot below C is live."""
+    src = as_prefix(prefix)
+    if keep.ndim != 3:
+        raise ValueError("keep must have shape [B, H, C]")
+    if src.pages is not None:
+        raise NotImplementedError("compaction of paged storage")
+    if src.nq and src.kmode != 1:
+        raise NotImplementedError("channel-mode keys are rebuilt by key groups (cache.py:236-335)")
+    if src.nq and src.nf:
+        raise RuntimeError("compact_tokens needs a fully quantized cache")
+    b, h, c = keep.shape
+    if c > src.n:
+        raise ValueError("compact cannot grow the cache")
+    if out is None:
+        def like(t):
+            return torch.empty((b, h, c, *t.shape[3:]), device=t.device, dtype=t.dtype)
+        if src.nq:
+            out = Prefix(kq=like(src.kq), ks=like(src.ks), kz=like(src.kz), vq=like(src.vq), vs=like(src.vs),
+                         vz=like(src.vz), nq=c, kb=src.kb, vb=src.vb, kg=src.kg, vg=src.vg, kmode=1, kch=src.kch)
+        else:
+            out = Prefix(kf=like(src.kf), vf=like(src.vf), nf=c)
+    sdesc = kv_descriptor(Prefix(**{s: getattr(src, s) for s in Prefix.__slots__ if s not in ("mask", "lens")}))
+    ddesc = kv_descriptor(out)
+    if (sdesc.batch, sdesc.heads) != (b, h) or (ddesc.batch, ddesc.heads) != (b, h):
+        raise ValueError("keep, source and destination disagree on [B, H]")
+    idx = keep.to(torch.int64)
+    if idx.stride(-1) != 1:
+        idx = idx.contiguous()
+    lib = _lib.lib()
+    _lib.check("ma_compact_tokens", lib.ma_compact_tokens(
+        sdesc.kv, ddesc.kv, b, h, sdesc.head_dim, idx.data_ptr(), c, i64(idx.stride(0), idx.stride(1)),
+        _lib.stream_handle(keep.device)))
+    if out.nq:
+        out.nq = c
+    else:
+        out.nf = c
+    return out

@@ -22,7 +22,7 @@ __all__ = [
     "value_score", "rescore_by_value", "order_keys", "topk_sorted", "topk_reference_torch",
     "dense_attention", "prefix_attention", "prefix_mass", "sdpa_compact", "gather_per_kv_head",
     "survivors_lookahead", "lookahead_score", "effective_topk",
-    "pages_to_contiguous",
+    "pages_to_contiguous", "compact_slots",
 ]
 
 
@@ -403,3 +403,23 @@ def pages_to_contiguous(pool: torch.Tensor, page_table: torch.Tensor, length: in
     pages = pool[page_table[:npages].long()]                       # [np, H, ps, ...]
     x = pages.transpose(0, 1).reshape(pool.shape[1], npages * page_size, *pool.shape[3:])
     return x[:, :length]
+
+
+# ------------------------------------------------------------------ compaction (eviction)
+def compact_slots(t: torch.Tensor, keep: torch.Tensor, slot_dim: int = 2) -> torch.Tensor:
+    """Slots keep[..., j] of t, in keep's order, for every trailing element of a slot.
+
+    Restates PackedKVCache.compact_tokens (cache.py:659-678: ``t.gather(3, idx)`` over
+    [L, B, H, slot, ...] for each stored array) and the gather of PackedKVCache.compact
+    (cache.py:342-365: bf16 survivors re-staged unchanged). keep has t's leading
+    dimensions up to the slot axis; an index outside [0, n) gives a zero row (the
+    device kernel's convention, where the reference's gather raises)."""
+    n = t.shape[slot_dim]
+    k = keep.to(torch.int64)
+    bad = (k < 0) | (k >= n)
+    safe = k.clamp(0, max(n - 1, 0))
+    idx = safe.reshape(*safe.shape, *([1] * (t.dim() - slot_dim - 1))).expand(*safe.shape, *t.shape[slot_dim + 1:])
+    out = t.gather(slot_dim, idx)
+    if bool(bad.any()):
+        out = out.masked_fill(bad.reshape(*bad.shape, *([1] * (t.dim() - slot_dim - 1))), 0)
+    return out

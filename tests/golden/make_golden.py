@@ -15,6 +15,8 @@ seeded inputs and records what the reference's own CPU (torch) path returns:
 * value_score (BITSIEVE_VSCORE_FP32=1) + EvictionState.survivors (lookahead)
                                                               session.py:27-40, eviction.py:325-409
 * quantize_values / quantize_keys payloads                    reference.py:58-90, 182-213
+* PackedKVCache.compact_tokens (token-mode k4v4) and .compact (bf16) after an
+  eviction decision                                           cache.py:659-678, 342-365
 
 Outputs go to <case>.npz next to this script, with the SHA-256 of the inputs.
 """
@@ -36,7 +38,8 @@ os.environ["BITSIEVE_VSCORE_FP32"] = "1"
 
 from gen_inputs import CASES, digest, make_case, make_retain_case  # noqa: E402
 
-from maskahead.cache import LayerCacheView  # noqa: E402
+from maskahead.cache import LayerCacheView, PackedKVCache  # noqa: E402
+from maskahead.config import QuantizationConfig  # noqa: E402
 from maskahead.eviction import EvictionConfig, EvictionState  # noqa: E402
 from maskahead.kernels.ops import selector_topk  # noqa: E402
 from maskahead.reference import (  # noqa: E402
@@ -162,12 +165,59 @@ def build_retain() -> dict:
     return dict(digest=np.array(digest(inputs)), score=score.numpy(), keep=keep.numpy())
 
 
+_COMPACT_ARRAYS = ("k_q", "k_scale", "k_zero", "v_q", "v_scale", "v_zero", "k_fp", "v_fp")
+
+
+def build_compact(mode: str, seed: int, L: int, B: int, H: int, n: int, C: int) -> dict:
+    """A reference cache filled by its own append path (begin_append / stage_layer /
+    commit_append quantize the staged bf16 rows), then compacted to the slots `keep`
+    (an ascending random subset per lane, as eviction keeps them): the cache's arrays
+    before (slots < n) and after (slots < C)."""
+    g = torch.Generator().manual_seed(seed)
+    D = 128
+    quant = QuantizationConfig(key_mode="token") if mode == "token" else QuantizationConfig(k_bits=16, v_bits=16)
+    cache = PackedKVCache(num_layers=L, batch_size=B, num_kv_heads=H, head_dim=D, max_tokens=4096,
+                          quant=quant, device="cpu", backend="torch")
+    cache.begin_append(n)
+    for layer in range(L):
+        k = torch.randn(B, H, n, D, generator=g).to(torch.bfloat16)
+        v = torch.randn(B, H, n, D, generator=g).to(torch.bfloat16)
+        cache.stage_layer(layer, k, v)
+    cache.commit_append()
+    out = {}
+    for name in _COMPACT_ARRAYS:
+        t = getattr(cache, name, None)
+        if t is not None:
+            out[f"before_{name}"] = t[:, :, :, :n].clone()
+    if mode == "token":
+        out["k_chan"] = cache.k_chan.clone()
+    keep = torch.stack([torch.randperm(n, generator=g)[:C].sort().values for _ in range(L * B * H)])
+    keep = keep.view(L, B, H, C)
+    if mode == "token":
+        cache.compact_tokens(keep)                                 # cache.py:659-678
+    else:
+        cache.compact(keep)                                        # cache.py:342-365
+    for name in _COMPACT_ARRAYS:
+        t = getattr(cache, name, None)
+        if t is not None:
+            out[f"after_{name}"] = t[:, :, :, :C].clone()
+    out["keep"] = keep
+    res = {}
+    for key, val in out.items():
+        res[key] = val.view(torch.int16).numpy() if val.dtype in (torch.bfloat16, torch.float16) else val.numpy()
+    res["dtypes"] = np.array([f"{key}:{str(val.dtype)}" for key, val in out.items()])
+    return res
+
+
 def main() -> None:
     for name in CASES:
         np.savez_compressed(HERE / f"{name}.npz", **build_case(name))
         print("wrote", name)
     np.savez_compressed(HERE / "retain.npz", **build_retain())
     print("wrote retain")
+    np.savez_compressed(HERE / "compact_token.npz", **build_compact("token", 21, 2, 1, 2, 300, 96))
+    np.savez_compressed(HERE / "compact_bf16.npz", **build_compact("bf16", 22, 1, 1, 2, 160, 48))
+    print("wrote compact_token, compact_bf16")
 
 
 if __name__ == "__main__":

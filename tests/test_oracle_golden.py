@@ -139,3 +139,40 @@ def test_pages_to_contiguous():
         chunk = seq[:, lp * ps:(lp + 1) * ps]
         pool[pp, :, :chunk.shape[1]] = chunk
     np.testing.assert_array_equal(oracle.pages_to_contiguous(pool, table, 10, ps).numpy(), seq.numpy())
+
+
+def load_compact(name):
+    """A compaction fixture: arrays before/after as torch tensors of their recorded dtype."""
+    z = _load(name)
+    dt = dict(s.split(":") for s in z.pop("dtypes").tolist())
+    out = {}
+    for key, arr in z.items():
+        t = torch.from_numpy(arr)
+        if dt[key] in ("torch.bfloat16", "torch.float16"):
+            t = t.view(getattr(torch, dt[key].split(".")[1]))
+        out[key] = t
+    return out
+
+
+@pytest.mark.parametrize("name", ["compact_token", "compact_bf16"])
+def test_compaction_matches_reference(name):
+    """compact_slots (the oracle's compaction) reproduces the reference cache's
+    compact_tokens / compact bit-exactly on every stored array."""
+    f = load_compact(name)
+    keep = f["keep"]
+    names = [k[len("before_"):] for k in f if k.startswith("before_")]
+    assert names
+    for arr in names:
+        got = oracle.compact_slots(f[f"before_{arr}"], keep, slot_dim=3)
+        want = f[f"after_{arr}"]
+        assert got.dtype == want.dtype
+        assert torch.equal(got.view(torch.uint8) if got.dtype != torch.uint8 else got,
+                           want.view(torch.uint8) if want.dtype != torch.uint8 else want), arr
+
+
+def test_compaction_out_of_range_rows_are_zero():
+    t = torch.arange(2 * 3 * 5 * 4, dtype=torch.int16).view(2, 3, 5, 4)
+    keep = torch.tensor([4, -1, 0, 5]).expand(2, 3, 4)
+    got = oracle.compact_slots(t, keep)
+    assert torch.equal(got[:, :, 0], t[:, :, 4]) and torch.equal(got[:, :, 2], t[:, :, 0])
+    assert int(got[:, :, 1].abs().sum()) == 0 and int(got[:, :, 3].abs().sum()) == 0
