@@ -262,9 +262,14 @@ MA_API int ma_unpack_prefix(const ma_kv* kv, int B, int H, int D, void* out_k, v
  * layout, dtype and vgroup whose arrays must not overlap; dst's arrays are written (its
  * pointers are const only because ma_kv's are). Needs C <= the slots of src (nq packed,
  * nf dense) and of dst. A packed src must have no dense tail (nf == 0: the reference
- * requires a fully quantized cache); channel-mode keys (rebuilt by key groups,
- * cache.py:236-335) and paged storage: MA_ERR_UNSUPPORTED. kchan, mask and lens are not
- * read; a keep index outside [0, n) writes a zero row (the reference's gather raises).
+ * requires a fully quantized cache); paged storage: MA_ERR_UNSUPPORTED.
+ * MA_KV_PACKED_CHANNEL: keep indexes KEY GROUPS of kgroup tokens (C groups, n = nq /
+ * kgroup): a kept group's key payload and scale/zero rows move with its kgroup value
+ * slots, which must be packed back to back in src and dst (svq[2] = D/2, svs[2] =
+ * D/vgroup, else MA_ERR_UNSUPPORTED); the dense tail is not touched. This is the group
+ * copy of the reference's group-preserving rebuild (cache.py:236-335, copy_groups).
+ * kchan, mask and lens are not read; a keep index outside [0, n) writes a zero row (the
+ * reference's gather raises).
  * Several layers at once: pass [L*B] as B when the layer axis merges with the batch
  * axis (contiguous [L,B,H,...] caches).                                               */
 MA_API int ma_compact_tokens(const ma_kv* src, const ma_kv* dst, int B, int H, int D, const int64_t* keep,

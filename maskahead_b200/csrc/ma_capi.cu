@@ -500,7 +500,6 @@ int ma_compact_tokens(const ma_kv* src, const ma_kv* dst, int B, int H, int D, c
   int rc = check_kv(src, D);
   if (rc) return rc;
   if (src->pages || dst->pages) return MA_ERR_UNSUPPORTED;
-  if (src->layout == MA_KV_PACKED_CHANNEL) return MA_ERR_UNSUPPORTED;
   if (dst->layout != src->layout || dst->dtype != src->dtype) return MA_ERR_ARG;
   CompactParams p{};
   p.H = H;
@@ -512,6 +511,28 @@ int ma_compact_tokens(const ma_kv* src, const ma_kv* dst, int B, int H, int D, c
     const int row = D * esize(src->dtype);
     if ((rc = compact_add(p, src->kf, dst->kf, src->skf, dst->skf, esize(src->dtype), row))) return rc;
     if ((rc = compact_add(p, src->vf, dst->vf, src->svf, dst->svf, esize(src->dtype), row))) return rc;
+  } else if (src->layout == MA_KV_PACKED_CHANNEL) {
+    // whole key groups: keep indexes groups of kgroup tokens; a group's key payload and
+    // scale/zero rows move with its kgroup value slots, which must be packed back to back
+    // so that they form one row (the group copy of cache.py:236-335 rebuild). The dense
+    // tail is not touched.
+    if (dst->vgroup != src->vgroup || dst->kgroup != src->kgroup) return MA_ERR_ARG;
+    const int kg = src->kgroup, groups = D / src->vgroup;
+    if (src->svq[2] != D / 2 || dst->svq[2] != D / 2 || src->svs[2] != groups || dst->svs[2] != groups)
+      return MA_ERR_UNSUPPORTED;
+    p.n = src->nq / kg;
+    if ((int64_t)C * kg > src->nq || (int64_t)C * kg > dst->nq) return MA_ERR_ARG;
+    if (C == 0) return MA_OK;
+    const int64_t svq_s[3] = {src->svq[0], src->svq[1], src->svq[2] * kg};
+    const int64_t svq_d[3] = {dst->svq[0], dst->svq[1], dst->svq[2] * kg};
+    const int64_t svs_s[3] = {src->svs[0], src->svs[1], src->svs[2] * kg};
+    const int64_t svs_d[3] = {dst->svs[0], dst->svs[1], dst->svs[2] * kg};
+    if ((rc = compact_add(p, src->kq, dst->kq, src->skq, dst->skq, 1, D * kg / 2))) return rc;
+    if ((rc = compact_add(p, src->ks, dst->ks, src->sks, dst->sks, 2, D * 2))) return rc;
+    if ((rc = compact_add(p, src->kz, dst->kz, src->sks, dst->sks, 2, D * 2))) return rc;
+    if ((rc = compact_add(p, src->vq, dst->vq, svq_s, svq_d, 1, kg * D / 2))) return rc;
+    if ((rc = compact_add(p, src->vs, dst->vs, svs_s, svs_d, 2, kg * groups * 2))) return rc;
+    if ((rc = compact_add(p, src->vz, dst->vz, svs_s, svs_d, 2, kg * groups * 2))) return rc;
   } else {
     // per-token codes only: a dense tail must have been quantized first (cache.py:662-663)
     if (src->nf != 0) return MA_ERR_UNSUPPORTED;

@@ -345,3 +345,114 @@ def compact_tokens(prefix, keep: torch.Tensor, out: Prefix | None = None) -> Pre
     else:
         out.nf = c
     return out
+
+
+def _gather_rows_into(desc: KVDesc, slots: torch.Tensor, out_k: torch.Tensor, out_v: torch.Tensor) -> None:
+    """out_k/out_v [B, H, k, D] bf16 <- the dequantized slots[b, h, :] of the cache (ma_gather_kv)."""
+    b, h, k = slots.shape
+    if k == 0:
+        return
+    _lib.check("ma_gather_kv", _lib.lib().ma_gather_kv(
+        desc.kv, b, h, desc.head_dim, slots.data_ptr(), k, i64(slots.stride(0), slots.stride(1)),
+        out_k.data_ptr(), out_v.data_ptr(), i64(*out_k.stride()[:3]), i64(*out_v.stride()[:3]),
+        _lib.dtype_code(out_k.dtype), _lib.stream_handle(slots.device)))
+
+
+def rebuild(prefix, groups_before: torch.Tensor, encode: torch.Tensor, groups_after: torch.Tensor,
+            stage: torch.Tensor) -> tuple[Prefix, torch.Tensor]:
+    """The group-preserving rebuild of a KIVI channel-mode k4v4 cache after an eviction
+    (PackedKVCache.rebuild, cache.py:236-335), on the device.
+
+    New physical layout [groups_before | encoded | groups_after] + a bf16 residual. The
+    index tensors are [B, H, *] int64 padded with -1 (a padded entry is dead: it holds a
+    copy of group / slot 0 or zeros, as in the reference, and the caller masks it):
+    groups_before / groups_after are old key groups whose codes and scales of keys and
+    values move bit-exactly (one compaction launch each); encode are old slots
+    dequantized to bf16 and quantized into fresh groups (dead rows and the padding of
+    the last group are zeros); stage are old slots kept in bf16 (the new residual).
+    Returns the new cache (nq = its quantized slots, nf = the residual) and remap
+    [B, H, old_length]: the new slot of every old slot, -1 if dropped. Every layer at once
+    when the layer axis is merged into the batch axis."""
+    src = as_prefix(prefix)
+    if not src.nq or src.kmode != 0:
+        raise NotImplementedError("rebuild is for packed caches with channel-mode (KIVI) keys")
+    if src.pages is not None:
+        raise NotImplementedError("rebuild of paged storage")
+    gk = int(src.kg)
+    B, H = src.vq.shape[0], src.vq.shape[1]
+    D = src.vq.shape[3] * src.vq.shape[4] * 2
+    dev = src.vq.device
+    old_len, ql_old = src.n, src.nq
+    idx = [t.to(device=dev, dtype=torch.int64) for t in (groups_before, encode, groups_after, stage)]
+    for t in idx:
+        if t.ndim != 3 or tuple(t.shape[:2]) != (B, H):
+            raise ValueError("index tensors must be [B, H, *]")
+    gb, enc, ga, stg = idx
+    g1, m, g3, st = (t.shape[-1] for t in idx)
+    g2 = -(-m // gk)
+    ql = (g1 + g2 + g3) * gk
+    cap = ql + st + 1024
+    ng_cap = -(-cap // gk)
+    kq = torch.empty((B, H, ng_cap, D, gk // 2), device=dev, dtype=torch.uint8)
+    ks = torch.empty((B, H, ng_cap, D), device=dev, dtype=torch.float16)
+    kz = torch.empty_like(ks)
+    vq = torch.empty((B, H, cap, D // src.vg, src.vg // 2), device=dev, dtype=torch.uint8)
+    vs = torch.empty((B, H, cap, D // src.vg), device=dev, dtype=torch.float16)
+    vz = torch.empty_like(vs)
+    rcap = max(st + 256, 64)
+    tail_dtype = src.kf.dtype if src.nf else torch.bfloat16
+    kr = torch.empty((B, H, rcap, D), device=dev, dtype=tail_dtype)
+    vr = torch.empty_like(kr)
+    remap = torch.full((B, H, old_len + 1), -1, device=dev, dtype=torch.int64)   # last: sink for pads
+    ar = torch.arange(gk, device=dev)
+    sdesc = kv_descriptor(Prefix(**{s: getattr(src, s) for s in Prefix.__slots__ if s not in ("mask", "lens")}))
+    lib = _lib.lib()
+
+    def copy_groups(gid: torch.Tensor, at: int) -> None:
+        n = gid.shape[-1]
+        if n == 0:
+            return
+        safe = gid.clamp_min(0).contiguous()
+        dst = Prefix(kq=kq[:, :, at:at + n], ks=ks[:, :, at:at + n], kz=kz[:, :, at:at + n],
+                     vq=vq[:, :, at * gk:(at + n) * gk], vs=vs[:, :, at * gk:(at + n) * gk],
+                     vz=vz[:, :, at * gk:(at + n) * gk], nq=n * gk, kb=4, vb=4, kg=gk, vg=src.vg, kmode=0)
+        ddesc = kv_descriptor(dst)
+        _lib.check("ma_compact_tokens", lib.ma_compact_tokens(
+            sdesc.kv, ddesc.kv, B, H, D, safe.data_ptr(), n, i64(safe.stride(0), safe.stride(1)),
+            _lib.stream_handle(dev)))
+        tok = (safe.unsqueeze(-1) * gk + ar).reshape(B, H, n * gk)
+        new_slot = ((torch.arange(n, device=dev) + at).view(1, 1, n, 1) * gk + ar).expand(B, H, n, gk)
+        valid = (gid >= 0).unsqueeze(-1).expand(-1, -1, -1, gk).reshape(B, H, n * gk)
+        remap.scatter_(-1, torch.where(valid, tok, old_len), new_slot.reshape(B, H, -1))
+
+    copy_groups(gb, 0)
+    copy_groups(ga, g1 + g2)
+    if m:
+        rows_k = torch.zeros((B, H, g2 * gk, D), device=dev, dtype=torch.bfloat16)
+        rows_v = torch.zeros_like(rows_k)
+        _gather_rows_into(sdesc, enc.clamp_min(0).contiguous(), rows_k[:, :, :m], rows_v[:, :, :m])
+        dead = (enc < 0).unsqueeze(-1)
+        rows_k[:, :, :m].masked_fill_(dead, 0)
+        rows_v[:, :, :m].masked_fill_(dead, 0)
+        pk, sk_ = kq[:, :, g1:g1 + g2], ks[:, :, g1:g1 + g2]
+        _lib.check("ma_quantize_keys_channel", lib.ma_quantize_keys_channel(
+            rows_k.data_ptr(), _lib.MA_BF16, B, H, g2 * gk, D, i64(*_strides3(rows_k)), gk, pk.data_ptr(),
+            i64(*_strides3(pk)), sk_.data_ptr(), kz[:, :, g1:g1 + g2].data_ptr(), i64(*_strides3(sk_)),
+            _lib.stream_handle(dev)))
+        pv, sv_ = vq[:, :, g1 * gk:(g1 + g2) * gk], vs[:, :, g1 * gk:(g1 + g2) * gk]
+        _lib.check("ma_quantize_tokens", lib.ma_quantize_tokens(
+            rows_v.data_ptr(), _lib.MA_BF16, B, H, g2 * gk, D, i64(*_strides3(rows_v)), None, None, src.vg,
+            pv.data_ptr(), i64(*_strides3(pv)), sv_.data_ptr(), vz[:, :, g1 * gk:(g1 + g2) * gk].data_ptr(),
+            i64(*_strides3(sv_)), _lib.stream_handle(dev)))
+        slot = torch.arange(m, device=dev).view(1, 1, m).expand(B, H, m) + g1 * gk
+        remap.scatter_(-1, torch.where(enc >= 0, enc, old_len), slot)
+    if st:
+        _gather_rows_into(sdesc, stg.clamp_min(0).contiguous(), kr[:, :, :st], vr[:, :, :st])
+        dead = (stg < 0).unsqueeze(-1)
+        kr[:, :, :st].masked_fill_(dead, 0)
+        vr[:, :, :st].masked_fill_(dead, 0)
+        slot = torch.arange(st, device=dev).view(1, 1, st).expand(B, H, st) + ql
+        remap.scatter_(-1, torch.where(stg >= 0, stg, old_len), slot)
+    out = Prefix(kq=kq, ks=ks, kz=kz, vq=vq, vs=vs, vz=vz, kf=kr, vf=vr, nq=ql, nf=st, kb=4, vb=4, kg=gk,
+                 vg=src.vg, kmode=0)
+    return out, remap[..., :old_len]

@@ -22,7 +22,7 @@ __all__ = [
     "value_score", "rescore_by_value", "order_keys", "topk_sorted", "topk_reference_torch",
     "dense_attention", "prefix_attention", "prefix_mass", "sdpa_compact", "gather_per_kv_head",
     "survivors_lookahead", "lookahead_score", "effective_topk",
-    "pages_to_contiguous", "compact_slots",
+    "pages_to_contiguous", "compact_slots", "rebuild_channel",
 ]
 
 
@@ -423,3 +423,63 @@ def compact_slots(t: torch.Tensor, keep: torch.Tensor, slot_dim: int = 2) -> tor
     if bool(bad.any()):
         out = out.masked_fill(bad.reshape(*bad.shape, *([1] * (t.dim() - slot_dim - 1))), 0)
     return out
+
+
+def rebuild_channel(arrays: dict, groups_before: torch.Tensor, encode: torch.Tensor,
+                    groups_after: torch.Tensor, stage: torch.Tensor, token_group: int = 32) -> tuple[dict, torch.Tensor]:
+    """The group-preserving rebuild of a KIVI channel-mode k4v4 cache (cache.py:236-335).
+
+    arrays: k_q [B,H,ng,D,16], k_scale/k_zero [B,H,ng,D], v_q [B,H,ql,D/32,16],
+    v_scale/v_zero [B,H,ql,D/32], k_residual/v_residual [B,H,rl,D] (bf16). Index tensors
+    [B,H,*] padded with -1; a padded entry copies group / slot 0 (clamp at 0) or is zero,
+    as in the reference. Returns the new arrays over the regions the rebuild defines
+    (groups [0, g1+g2+g3), value slots [0, ql'), residual [0, st)) and remap [B,H,old_len].
+    """
+    gk = token_group
+    kq, ks, kz = arrays["k_q"], arrays["k_scale"], arrays["k_zero"]
+    vq, vs, vz = arrays["v_q"], arrays["v_scale"], arrays["v_zero"]
+    kr, vr = arrays["k_residual"], arrays["v_residual"]
+    B, H = kq.shape[:2]
+    ql_old, rl = vq.shape[2], kr.shape[2]
+    old_len = ql_old + rl
+    g1, m, g3, st = (t.shape[-1] for t in (groups_before, encode, groups_after, stage))
+    g2 = -(-m // gk)
+    ql = (g1 + g2 + g3) * gk
+    keys = torch.cat([dequantize_keys(kq, ks, kz, token_group=gk, dtype=kr.dtype), kr], 2)
+    vals = torch.cat([dequantize_values(vq, vs, vz, dtype=vr.dtype), vr], 2)
+    remap = torch.full((B, H, old_len + 1), -1, dtype=torch.int64)
+    ar = torch.arange(gk)
+    parts = {name: [] for name in ("k_q", "k_scale", "k_zero", "v_q", "v_scale", "v_zero")}
+
+    def copy_groups(gid, at):
+        n = gid.shape[-1]
+        safe = gid.clamp_min(0)
+        tok = (safe.unsqueeze(-1) * gk + ar).reshape(B, H, n * gk)
+        for name, src, idx in (("k_q", kq, safe), ("k_scale", ks, safe), ("k_zero", kz, safe),
+                               ("v_q", vq, tok), ("v_scale", vs, tok), ("v_zero", vz, tok)):
+            parts[name].append(compact_slots(src, idx))
+        new_slot = ((torch.arange(n) + at).view(1, 1, n, 1) * gk + ar).expand(B, H, n, gk)
+        valid = (gid >= 0).unsqueeze(-1).expand(-1, -1, -1, gk)
+        idx = torch.where(valid, tok.view(B, H, n, gk), old_len)
+        remap.scatter_(-1, idx.reshape(B, H, -1), new_slot.reshape(B, H, -1))
+
+    copy_groups(groups_before, 0)
+    safe = encode.clamp_min(0)
+    dead = (encode < 0).unsqueeze(-1)
+    pad = g2 * gk - m
+    src_k = torch.nn.functional.pad(compact_slots(keys, safe).masked_fill(dead, 0), (0, 0, 0, pad))
+    src_v = torch.nn.functional.pad(compact_slots(vals, safe).masked_fill(dead, 0), (0, 0, 0, pad))
+    for name, t in zip(("k_q", "k_scale", "k_zero"), quantize_keys(src_k, token_group=gk)):
+        parts[name].append(t)
+    for name, t in zip(("v_q", "v_scale", "v_zero"), quantize_values(src_v)):
+        parts[name].append(t)
+    remap.scatter_(-1, torch.where(encode >= 0, encode, old_len),
+                   torch.arange(m).view(1, 1, m).expand(B, H, m) + g1 * gk)
+    copy_groups(groups_after, g1 + g2)
+    safe = stage.clamp_min(0)
+    dead = (stage < 0).unsqueeze(-1)
+    out = {name: torch.cat(ts, 2) for name, ts in parts.items()}
+    out["k_residual"] = compact_slots(keys, safe).masked_fill(dead, 0)
+    out["v_residual"] = compact_slots(vals, safe).masked_fill(dead, 0)
+    remap.scatter_(-1, torch.where(stage >= 0, stage, old_len), torch.arange(st).view(1, 1, st).expand(B, H, st) + ql)
+    return out, remap[..., :old_len]

@@ -17,6 +17,8 @@ seeded inputs and records what the reference's own CPU (torch) path returns:
 * quantize_values / quantize_keys payloads                    reference.py:58-90, 182-213
 * PackedKVCache.compact_tokens (token-mode k4v4) and .compact (bf16) after an
   eviction decision                                           cache.py:659-678, 342-365
+* PackedKVCache.rebuild (KIVI channel-mode keys: kept groups copied, sparse groups
+  re-encoded, undecided slots staged in bf16)                 cache.py:236-335
 
 Outputs go to <case>.npz next to this script, with the SHA-256 of the inputs.
 """
@@ -209,6 +211,73 @@ def build_compact(mode: str, seed: int, L: int, B: int, H: int, n: int, C: int) 
     return res
 
 
+def _padded(rows: list, width: int) -> torch.Tensor:
+    out = torch.full((len(rows), width), -1, dtype=torch.int64)
+    for i, r in enumerate(rows):
+        out[i, : len(r)] = torch.as_tensor(r, dtype=torch.int64)
+    return out
+
+
+def build_rebuild(seed: int = 23, L: int = 2, B: int = 1, H: int = 2, n: int = 333) -> dict:
+    """A channel-mode k4v4 reference cache (its own append path: 288 quantized slots in
+    9 key groups, 45 in the bf16 residual), rebuilt by PackedKVCache.rebuild from
+    per-lane index lists of different lengths padded with -1, as the session's _evict_to
+    makes them (session.py:303-361): kept groups ascending, encoded and staged slots
+    ascending by position. Records the arrays before, the index lists, the arrays after
+    (the regions rebuild defines) and the remap."""
+    g = torch.Generator().manual_seed(seed)
+    D, gk = 128, 32
+    quant = QuantizationConfig(key_mode="channel")
+    cache = PackedKVCache(num_layers=L, batch_size=B, num_kv_heads=H, head_dim=D, max_tokens=4096,
+                          quant=quant, device="cpu", backend="torch")
+    cache.begin_append(n)
+    for layer in range(L):
+        k = torch.randn(B, H, n, D, generator=g).to(torch.bfloat16)
+        v = torch.randn(B, H, n, D, generator=g).to(torch.bfloat16)
+        cache.stage_layer(layer, k, v)
+    cache.commit_append()
+    ql, rl, ng = cache.quantized_length, cache.residual_length, cache.quantized_length // gk
+    out = {}
+    for name in ("k_q", "k_scale", "k_zero"):
+        out[f"before_{name}"] = getattr(cache, name)[:, :, :, :ng].clone()
+    for name in ("v_q", "v_scale", "v_zero"):
+        out[f"before_{name}"] = getattr(cache, name)[:, :, :, :ql].clone()
+    for name in ("k_residual", "v_residual"):
+        out[f"before_{name}"] = getattr(cache, name)[:, :, :, :rl].clone()
+    gb, enc, ga, stg = [], [], [], []
+    for _ in range(L * B * H):
+        perm = torch.randperm(ng - 1, generator=g)             # the last group goes "after"
+        kept = sorted(perm[: int(torch.randint(3, 6, (1,), generator=g))].tolist())
+        sparse = sorted(perm[6:8].tolist())
+        slots = sorted(s for grp in sparse for s in range(grp * gk, grp * gk + gk)
+                       if torch.rand(1, generator=g).item() < 0.4)
+        gb.append(kept)
+        enc.append(slots)
+        ga.append([ng - 1])
+        stg.append(sorted(torch.randperm(rl, generator=g)[: int(torch.randint(3, 8, (1,), generator=g))]
+                          .add(ql).tolist()))
+    groups_before = _padded(gb, max(map(len, gb))).view(L, B, H, -1)
+    encode = _padded(enc, max(map(len, enc))).view(L, B, H, -1)
+    groups_after = _padded(ga, 1).view(L, B, H, -1)
+    stage = _padded(stg, max(map(len, stg))).view(L, B, H, -1)
+    remap = cache.rebuild(groups_before, encode, groups_after, stage)    # cache.py:236-335
+    g1, m, g3, st = (t.shape[-1] for t in (groups_before, encode, groups_after, stage))
+    total = g1 + -(-m // gk) + g3
+    for name in ("k_q", "k_scale", "k_zero"):
+        out[f"after_{name}"] = getattr(cache, name)[:, :, :, :total].clone()
+    for name in ("v_q", "v_scale", "v_zero"):
+        out[f"after_{name}"] = getattr(cache, name)[:, :, :, :total * gk].clone()
+    for name in ("k_residual", "v_residual"):
+        out[f"after_{name}"] = getattr(cache, name)[:, :, :, :st].clone()
+    out.update(groups_before=groups_before, encode=encode, groups_after=groups_after, stage=stage,
+               remap=remap)
+    res = {}
+    for key, val in out.items():
+        res[key] = val.view(torch.int16).numpy() if val.dtype in (torch.bfloat16, torch.float16) else val.numpy()
+    res["dtypes"] = np.array([f"{key}:{str(val.dtype)}" for key, val in out.items()])
+    return res
+
+
 def main() -> None:
     for name in CASES:
         np.savez_compressed(HERE / f"{name}.npz", **build_case(name))
@@ -218,6 +287,8 @@ def main() -> None:
     np.savez_compressed(HERE / "compact_token.npz", **build_compact("token", 21, 2, 1, 2, 300, 96))
     np.savez_compressed(HERE / "compact_bf16.npz", **build_compact("bf16", 22, 1, 1, 2, 160, 48))
     print("wrote compact_token, compact_bf16")
+    np.savez_compressed(HERE / "rebuild_channel.npz", **build_rebuild())
+    print("wrote rebuild_channel")
 
 
 if __name__ == "__main__":

@@ -133,3 +133,84 @@ def test_rejected_requests():
         compact_tokens(src, keep, out=src)                       # in place is refused
     empty = compact_tokens(src, keep[:, :, :0])
     assert empty.nf == 0
+
+
+REBUILD_ARRAYS = ("k_q", "k_scale", "k_zero", "v_q", "v_scale", "v_zero", "k_residual", "v_residual")
+
+
+def _rebuilt_regions(out, g_total, st):
+    gk = out.kg
+    return {"k_q": out.kq[:, :, :g_total], "k_scale": out.ks[:, :, :g_total], "k_zero": out.kz[:, :, :g_total],
+            "v_q": out.vq[:, :, :g_total * gk], "v_scale": out.vs[:, :, :g_total * gk],
+            "v_zero": out.vz[:, :, :g_total * gk], "k_residual": out.kf[:, :, :st], "v_residual": out.vf[:, :, :st]}
+
+
+def _channel_prefix(a: dict):
+    from maskahead_b200.layouts import Prefix
+
+    return Prefix(kq=a["k_q"], ks=a["k_scale"], kz=a["k_zero"], vq=a["v_q"], vs=a["v_scale"], vz=a["v_zero"],
+                  kf=a["k_residual"], vf=a["v_residual"], nq=a["v_q"].shape[2], nf=a["k_residual"].shape[2],
+                  kb=4, vb=4, kmode=0)
+
+
+def test_rebuild_matches_reference():
+    """The device rebuild of a channel-mode cache gives the reference's rebuild
+    (cache.py:236-335) bit for bit: kept groups moved, sparse survivors re-encoded,
+    undecided slots staged in bf16, and the remap."""
+    from maskahead_b200.layouts import rebuild
+
+    f = load_compact("rebuild_channel")
+    before = {name: _merge_layers(f[f"before_{name}"]).to(DEV) for name in REBUILD_ARRAYS}
+    idx = [_merge_layers(f[k]).to(DEV) for k in ("groups_before", "encode", "groups_after", "stage")]
+    out, remap = rebuild(_channel_prefix(before), *idx)
+    torch.cuda.synchronize()
+    g_total = f["after_k_q"].shape[3]
+    st = f["after_k_residual"].shape[3]
+    assert out.nq == g_total * 32 and out.nf == st
+    for name, t in _rebuilt_regions(out, g_total, st).items():
+        assert torch.equal(_bytes(t.cpu()), _bytes(_merge_layers(f[f"after_{name}"]))), name
+    assert torch.equal(remap.cpu(), _merge_layers(f["remap"]))
+
+
+def test_rebuild_random_matches_oracle():
+    """A larger channel-mode cache (8 lanes, 64 key groups + a 40-slot bf16 residual) with
+    per-lane index lists of different lengths: device rebuild == oracle, bit for bit."""
+    from maskahead_b200.layouts import pack_prefix, rebuild
+
+    gen = torch.Generator().manual_seed(41)
+    B, H, ng, rl, D, gk = 2, 4, 64, 40, 128, 32
+    k = torch.randn(B, H, ng * gk, D, generator=gen).to(torch.bfloat16).to(DEV)
+    v = torch.randn(B, H, ng * gk, D, generator=gen).to(torch.bfloat16).to(DEV)
+    p = pack_prefix(k, v, key_mode="channel")
+    arrays = {"k_q": p.kq, "k_scale": p.ks, "k_zero": p.kz, "v_q": p.vq, "v_scale": p.vs, "v_zero": p.vz,
+              "k_residual": torch.randn(B, H, rl, D, generator=gen).to(torch.bfloat16).to(DEV),
+              "v_residual": torch.randn(B, H, rl, D, generator=gen).to(torch.bfloat16).to(DEV)}
+    lists = {"gb": [], "enc": [], "ga": [], "st": []}
+    for _ in range(B * H):
+        perm = torch.randperm(ng - 2, generator=gen)
+        kept = perm[: int(torch.randint(10, 30, (1,), generator=gen))].sort().values
+        sparse = perm[30:40]
+        slots = (sparse.view(-1, 1) * gk + torch.arange(gk)).view(-1)
+        slots = slots[torch.rand(slots.numel(), generator=gen) < 0.3].sort().values
+        lists["gb"].append(kept)
+        lists["enc"].append(slots)
+        lists["ga"].append(torch.tensor([ng - 2, ng - 1]))
+        lists["st"].append(torch.randperm(rl, generator=gen)[: int(torch.randint(5, 30, (1,), generator=gen))]
+                           .sort().values + ng * gk)
+
+    def padded(rows):
+        w = max(r.numel() for r in rows)
+        out = torch.full((len(rows), w), -1, dtype=torch.int64)
+        for i, r in enumerate(rows):
+            out[i, : r.numel()] = r
+        return out.view(B, H, w)
+
+    idx = [padded(lists[key]) for key in ("gb", "enc", "ga", "st")]
+    out, remap = rebuild(_channel_prefix(arrays), *[t.to(DEV) for t in idx])
+    torch.cuda.synchronize()
+    want, want_remap = oracle.rebuild_channel({k2: t.cpu() for k2, t in arrays.items()}, *idx)
+    g_total = want["k_q"].shape[2]
+    st = want["k_residual"].shape[2]
+    for name, t in _rebuilt_regions(out, g_total, st).items():
+        assert torch.equal(_bytes(t.cpu()), _bytes(want[name])), name
+    assert torch.equal(remap.cpu(), want_remap)

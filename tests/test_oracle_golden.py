@@ -176,3 +176,25 @@ def test_compaction_out_of_range_rows_are_zero():
     got = oracle.compact_slots(t, keep)
     assert torch.equal(got[:, :, 0], t[:, :, 4]) and torch.equal(got[:, :, 2], t[:, :, 0])
     assert int(got[:, :, 1].abs().sum()) == 0 and int(got[:, :, 3].abs().sum()) == 0
+
+
+REBUILD_ARRAYS = ("k_q", "k_scale", "k_zero", "v_q", "v_scale", "v_zero", "k_residual", "v_residual")
+
+
+def test_rebuild_matches_reference():
+    """rebuild_channel (the oracle's group-preserving rebuild) reproduces the reference
+    cache's rebuild bit-exactly: kept groups, re-encoded groups, the bf16 residual and
+    the remap (every layer at once, the layer axis merged into the batch axis)."""
+    f = load_compact("rebuild_channel")
+
+    def merge(t):
+        return t.reshape(t.shape[0] * t.shape[1], *t.shape[2:])
+
+    before = {name: merge(f[f"before_{name}"]) for name in REBUILD_ARRAYS}
+    idx = [merge(f[k]) for k in ("groups_before", "encode", "groups_after", "stage")]
+    got, remap = oracle.rebuild_channel(before, *idx)
+    for name in REBUILD_ARRAYS:
+        want = merge(f[f"after_{name}"])
+        assert got[name].shape == want.shape, name
+        assert torch.equal(got[name].contiguous().view(torch.uint8), want.contiguous().view(torch.uint8)), name
+    assert torch.equal(remap, merge(f["remap"]))
