@@ -6,7 +6,7 @@
 // caches by a gather (cache.py:342-365 compact, whose bf16 re-staging is exact). It is
 // pure data movement, bound by HBM: per kept slot each array's row is read once from a
 // random slot and written once, contiguously. One launch moves every array: grid.y picks
-// the array, grid.x the (lane, chunk of kCompactChunk slots); each thread copies whole
+// the array, grid.x the (lane, chunk of slots: 256, or more for arrays of short rows); each thread copies whole
 // vectors (16 bytes when the row, the bases and the strides allow it) and issues
 // kUnroll loads before their stores, so every warp keeps several row reads in flight.
 #include "ma_kernels.cuh"
@@ -15,7 +15,7 @@ namespace ma {
 namespace {
 
 constexpr int kCompactThreads = 256;
-constexpr int kCompactChunk = 256;     // kept slots per block
+constexpr int kCompactChunk = 256;     // kept slots per block (at least)
 constexpr int kUnroll = 4;
 
 template <typename V>
@@ -54,13 +54,14 @@ __device__ __forceinline__ void compact_rows(const CompactArray& a, const int64_
   }
 }
 
-__global__ void __launch_bounds__(kCompactThreads) compact_kernel(CompactParams p) {
+__global__ void __launch_bounds__(kCompactThreads, 6) compact_kernel(CompactParams p) {
   const CompactArray& a = p.arrays[blockIdx.y];
   const int lane = blockIdx.x / p.chunks;
   const int chunk = blockIdx.x - lane * p.chunks;
+  if (chunk >= a.chunks) return;   // an array of short rows covers its slots in fewer blocks
   const int64_t b = lane / p.H, h = lane - b * p.H;
-  const int j0 = chunk * kCompactChunk;
-  const int count = min(kCompactChunk, p.C - j0);
+  const int j0 = chunk * a.slots_per_block;
+  const int count = min(a.slots_per_block, p.C - j0);
   const int64_t* keep_lane = p.keep + b * p.sk0 + h * p.sk1;
   switch (a.vec_bytes) {
     case 16: compact_rows<uint4>(a, keep_lane, b, h, j0, count, p.n); break;
@@ -75,7 +76,17 @@ __global__ void __launch_bounds__(kCompactThreads) compact_kernel(CompactParams 
 
 int launch_compact(CompactParams& p, int B, cudaStream_t st) {
   if (p.C == 0 || p.narrays == 0) return MA_OK;
-  p.chunks = (p.C + kCompactChunk - 1) / kCompactChunk;
+  // every thread keeps kUnroll vectors in flight: arrays of short rows take more slots
+  // per block (an 8-byte scale row: 1024 slots), long rows kCompactChunk
+  p.chunks = 0;
+  for (int i = 0; i < p.narrays; ++i) {
+    CompactArray& a = p.arrays[i];
+    const int units = a.row_bytes / a.vec_bytes;
+    const int spb = (kCompactThreads * kUnroll) / units;
+    a.slots_per_block = spb > kCompactChunk ? spb : kCompactChunk;
+    a.chunks = (p.C + a.slots_per_block - 1) / a.slots_per_block;
+    if (a.chunks > p.chunks) p.chunks = a.chunks;
+  }
   const int64_t blocks = (int64_t)B * p.H * p.chunks;
   if (blocks > 0x7fffffffLL) return MA_ERR_UNSUPPORTED;
   dim3 grid((unsigned)blocks, (unsigned)p.narrays);

@@ -126,6 +126,8 @@ struct CompactArray {
   int64_t ds[3];
   int row_bytes;
   int vec_bytes;
+  int slots_per_block;   // set by launch_compact
+  int chunks;            // set by launch_compact
 };
 constexpr int kCompactMaxArrays = 6;
 struct CompactParams {
@@ -135,7 +137,7 @@ struct CompactParams {
   int64_t sk0, sk1;
   int H, C;
   int64_t n;             // source slots: a keep index outside [0, n) writes a zero row
-  int chunks;            // set by launch_compact
+  int chunks;            // set by launch_compact: the most blocks any array needs per lane
 };
 int launch_compact(CompactParams& p, int B, cudaStream_t st);
 
