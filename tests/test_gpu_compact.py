@@ -214,3 +214,30 @@ def test_rebuild_random_matches_oracle():
     for name, t in _rebuilt_regions(out, g_total, st).items():
         assert torch.equal(_bytes(t.cpu()), _bytes(want[name])), name
     assert torch.equal(remap.cpu(), want_remap)
+
+
+@pytest.mark.parametrize("layout", ["bf16", "k4v4_token"])
+def test_attention_after_compaction_equals_masked_attention(layout):
+    """Round trip at the cfg2 layer size (n = 8192, 4 KV heads, 28 query heads, C = 2048):
+    attention over the compacted cache equals attention over the original cache with
+    every slot but the kept ones masked dead (attention does not depend on the order of
+    the keys), within the bf16 output bar of the attention tests (atol = rtol = 2e-2)."""
+    from maskahead_b200.kernels.splitk import splitk_attention
+    from maskahead_b200.layouts import Prefix, as_prefix, compact_tokens, pack_prefix
+
+    gen = torch.Generator().manual_seed(43)
+    B, H, G, T, n, C, D = 1, 4, 7, 32, 8192, 2048, 128
+    k = torch.randn(B, H, n, D, generator=gen).to(torch.bfloat16).to(DEV)
+    v = torch.randn(B, H, n, D, generator=gen).to(torch.bfloat16).to(DEV)
+    q = torch.randn(B, H * G, T, D, generator=gen).to(torch.bfloat16).to(DEV)
+    kc = torch.randn(B, H, T, D, generator=gen).to(torch.bfloat16).to(DEV)
+    vc = torch.randn(B, H, T, D, generator=gen).to(torch.bfloat16).to(DEV)
+    src = Prefix.dense(k, v) if layout == "bf16" else pack_prefix(k, v, key_mode="token")
+    keep = _random_keep(B, H, n, C, gen).to(DEV)
+    compacted = compact_tokens(src, keep)
+    mask = torch.zeros(B, H, n, dtype=torch.uint8, device=DEV)
+    mask.scatter_(-1, keep, 1)
+    got, _ = splitk_attention(q, compacted, kc, vc)
+    want, _ = splitk_attention(q, as_prefix(src, mask=mask), kc, vc)
+    torch.cuda.synchronize()
+    torch.testing.assert_close(got.float(), want.float(), atol=2e-2, rtol=2e-2)
