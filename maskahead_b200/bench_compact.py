@@ -1,6 +1,6 @@
 """Time the cache compaction after an eviction (ma_compact_tokens) on one GPU.
 
-    python -m maskahead_b200.bench_compact [--layout token|bf16] [--lanes N] [--n SLOTS]
+    python -m maskahead_b200.bench_compact [--layout token|bf16|channel] [--lanes N] [--n SLOTS]
                                            [--keep C] [--iters K]
 
 Every layer of a serving batch compacts in one launch: lanes = layers x sequences x KV
@@ -11,6 +11,13 @@ x 2 (each kept slot read once and written once; 160 B per slot for token-mode k4
 no flush is needed between launches. Prints one JSON line: the mean launch time over
 K launches (CUDA events on the launching stream, after 3 warm-up launches) and the
 achieved HBM bandwidth against the measured copy peak.
+
+--layout channel times the whole group-preserving rebuild of a KIVI channel-mode cache
+(`layouts.rebuild`: every launch and device-side index operation of one call) with
+C / 32 kept key groups per lane (the first half of the groups, every other one, and
+groups from the second half), the survivors of 8 further groups re-encoded (a third of
+their slots) and 64 slots staged; its bytes count the kept groups moved (160 B per slot,
+read and written) and the re-encoded and staged slots (read packed, written once).
 """
 
 from __future__ import annotations
@@ -31,9 +38,54 @@ def _peak_gbs() -> tuple[float, str]:
     return 6650.0, "fallback"
 
 
+def _time_rebuild(args, B, H, n, C, D, gen, rnd_u8, dev) -> None:
+    from .layouts import rebuild
+
+    gk, rl = 32, 64
+    ng = n // gk
+
+    def scales(*shape):
+        # finite fp16 scales/zeros in [0.5, 1): random bytes could hold NaN/Inf patterns
+        return (torch.rand(*shape, device=dev, generator=gen) * 0.5 + 0.5).to(torch.float16)
+
+    src = Prefix(kq=rnd_u8(B, H, ng, D, gk // 2), ks=scales(B, H, ng, D), kz=scales(B, H, ng, D),
+                 vq=rnd_u8(B, H, n, D // 32, 16), vs=scales(B, H, n, D // 32), vz=scales(B, H, n, D // 32),
+                 kf=torch.randn(B, H, rl, D, device=dev, generator=gen).to(torch.bfloat16),
+                 vf=torch.randn(B, H, rl, D, device=dev, generator=gen).to(torch.bfloat16),
+                 nq=n, nf=rl, kb=4, vb=4, kmode=0)
+    g1 = C // gk
+    kept = torch.arange(0, 2 * g1, 2, device=dev)[:g1].clamp_max(ng - 10)
+    groups_before = kept.expand(B, H, g1).contiguous()
+    sparse = torch.arange(ng - 9, ng - 1, device=dev)
+    slots = (sparse.view(-1, 1) * gk + torch.arange(0, gk, 3, device=dev)).reshape(-1)
+    encode = slots.expand(B, H, slots.numel()).contiguous()
+    groups_after = torch.full((B, H, 1), ng - 1, device=dev, dtype=torch.int64)
+    stage = (torch.arange(rl, device=dev) + n).expand(B, H, rl).contiguous()
+    for _ in range(3):
+        rebuild(src, groups_before, encode, groups_after, stage)
+    torch.cuda.synchronize()
+    stream = torch.cuda.current_stream()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record(stream)
+    for _ in range(args.iters):
+        rebuild(src, groups_before, encode, groups_after, stage)
+    end.record(stream)
+    torch.cuda.synchronize()
+    us = start.elapsed_time(end) * 1e3 / args.iters
+    lanes = B * H
+    moved = (g1 + 1) * gk * 160 * 2 + encode.shape[-1] * 160 * 2 + rl * 512 * 2
+    alg = lanes * moved
+    peak, kind = _peak_gbs()
+    gbs = alg / (us * 1e-6) / 1e9
+    print(json.dumps({"kernel": "rebuild (channel-mode)", "lanes": lanes, "n": n, "kept_groups": g1 + 1,
+                      "encoded": encode.shape[-1], "staged": rl, "us_per_call": round(us, 2),
+                      "algorithmic_bytes": alg, "achieved_gbs": round(gbs, 1), "peak_gbs": peak,
+                      "peak_kind": kind, "frac": round(gbs / peak, 3)}))
+
+
 def main() -> None:
     ap = argparse.ArgumentParser(description=__doc__.splitlines()[0])
-    ap.add_argument("--layout", choices=("token", "bf16"), default="token")
+    ap.add_argument("--layout", choices=("token", "bf16", "channel"), default="token")
     ap.add_argument("--lanes", type=int, default=28 * 64 * 4, help="layers x sequences x KV heads")
     ap.add_argument("--n", type=int, default=8192, help="slots before the compaction")
     ap.add_argument("--keep", type=int, default=2048, help="slots kept (C)")
@@ -48,6 +100,9 @@ def main() -> None:
     def rnd_u8(*shape):
         return torch.randint(0, 256, shape, dtype=torch.uint8, device=dev, generator=gen)
 
+    if args.layout == "channel":
+        _time_rebuild(args, B, H, n, C, D, gen, rnd_u8, dev)
+        return
     if args.layout == "token":
         def arrays(slots):
             return dict(kq=rnd_u8(B, H, slots, D // 32, 16), ks=rnd_u8(B, H, slots, D // 32, 2).view(torch.float16)[..., 0],
