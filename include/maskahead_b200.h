@@ -36,6 +36,7 @@
  *                        of the append path)
  *   ma_compact_tokens    cache.py:659-678 (compact_tokens) and 342-365 (compact): the
  *                        cache compaction after an eviction (runtime/session.py:270-302)
+ *   ma_rebuild_remap     cache.py:236-335 (the remap of rebuild)
  */
 #ifndef MASKAHEAD_B200_H
 #define MASKAHEAD_B200_H
@@ -272,6 +273,17 @@ MA_API int ma_unpack_prefix(const ma_kv* kv, int B, int H, int D, void* out_k, v
  * reference's gather raises).
  * Several layers at once: pass [L*B] as B when the layer axis merges with the batch
  * axis (contiguous [L,B,H,...] caches).                                               */
+/* The remap of a group-preserving rebuild (cache.py:236-335): remap [B,H,old_len] int64
+ * (contiguous) gets, for every old slot, its slot in the rebuilt cache
+ * [groups_before | encoded | groups_after] + residual, or -1 if dropped. Index lists are
+ * contiguous [B,H,count] int64, -1 = padding: groups_before / groups_after name key
+ * groups of kgroup slots (placed at group 0 and at group g1 + ceil(m/kgroup)), encode
+ * names old slots re-encoded in order from slot g1*kgroup, stage old slots staged in
+ * order from slot (g1 + ceil(m/kgroup) + g3) * kgroup. Entries outside [0, old_len) are
+ * skipped.                                                                            */
+MA_API int ma_rebuild_remap(int B, int H, int old_len, int kgroup, const int64_t* groups_before, int g1,
+                            const int64_t* encode, int m, const int64_t* groups_after, int g3,
+                            const int64_t* stage, int st, int64_t* remap, void* stream);
 MA_API int ma_compact_tokens(const ma_kv* src, const ma_kv* dst, int B, int H, int D, const int64_t* keep,
                              int C, const int64_t skeep[2], void* stream);
 

@@ -100,6 +100,7 @@ _SIGNATURES = {
     "ma_key_divisor": (_i32, [_vp, _i32, _i32, _i32, _i32, _i32, _P(ctypes.c_int64), _vp,
                               _P(ctypes.c_int64), _vp]),
     "ma_compact_tokens": (_i32, [_P(MaKV), _P(MaKV), _i32, _i32, _i32, _vp, _i32, _P(ctypes.c_int64), _vp]),
+    "ma_rebuild_remap": (_i32, [_i32, _i32, _i32, _i32, _vp, _i32, _vp, _i32, _vp, _i32, _vp, _i32, _vp, _vp]),
 }
 
 EXPORTED = tuple(_SIGNATURES)

@@ -555,4 +555,17 @@ int ma_compact_tokens(const ma_kv* src, const ma_kv* dst, int B, int H, int D, c
   return launch_compact(p, B, (cudaStream_t)stream);
 }
 
+int ma_rebuild_remap(int B, int H, int old_len, int kgroup, const int64_t* groups_before, int g1,
+                     const int64_t* encode, int m, const int64_t* groups_after, int g3, const int64_t* stage, int st,
+                     int64_t* remap, void* stream) {
+  if (B <= 0 || H <= 0 || old_len < 0 || kgroup <= 0 || g1 < 0 || m < 0 || g3 < 0 || st < 0) return MA_ERR_ARG;
+  if ((g1 && !groups_before) || (m && !encode) || (g3 && !groups_after) || (st && !stage)) return MA_ERR_ARG;
+  if (old_len > 0 && !remap) return MA_ERR_ARG;
+  const int64_t g2 = ((int64_t)m + kgroup - 1) / kgroup;
+  const int64_t ql = ((int64_t)g1 + g2 + g3) * kgroup;
+  if (ql + st > 0x7fffffffLL) return MA_ERR_ARG;
+  RemapParams p{groups_before, encode, groups_after, stage, remap, g1, (int)g2, g3, m, st, kgroup, old_len, (int)ql};
+  return launch_rebuild_remap(p, B * H, (cudaStream_t)stream);
+}
+
 }  // extern "C"

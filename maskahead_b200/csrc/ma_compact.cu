@@ -72,7 +72,42 @@ __global__ void __launch_bounds__(kCompactThreads, 6) compact_kernel(CompactPara
   }
 }
 
+// The remap of a group-preserving rebuild (cache.py:236-335): one CTA per lane sets every
+// old slot to -1, then writes the new slot of every slot that a kept group, the encoded
+// list or the staged list names (entries < 0 are padding and name nothing).
+__global__ void __launch_bounds__(256) rebuild_remap_kernel(RemapParams p) {
+  const int64_t lane = blockIdx.x;
+  int64_t* remap = p.remap + lane * p.old_len;
+  for (int i = threadIdx.x; i < p.old_len; i += blockDim.x) remap[i] = -1;
+  __syncthreads();
+  const int gk = p.kgroup;
+  for (int pass = 0; pass < 2; ++pass) {
+    const int64_t* gid = pass == 0 ? p.gb + lane * p.g1 : p.ga + lane * p.g3;
+    const int count = (pass == 0 ? p.g1 : p.g3) * gk;
+    const int at = pass == 0 ? 0 : (p.g1 + p.g2) * gk;
+    for (int i = threadIdx.x; i < count; i += blockDim.x) {
+      const int64_t g = gid[i / gk];
+      const int64_t old = g * gk + i % gk;
+      if (g >= 0 && old < p.old_len) remap[old] = at + i;
+    }
+  }
+  for (int i = threadIdx.x; i < p.m; i += blockDim.x) {
+    const int64_t old = p.enc[lane * p.m + i];
+    if (old >= 0 && old < p.old_len) remap[old] = (int64_t)p.g1 * gk + i;
+  }
+  for (int i = threadIdx.x; i < p.st; i += blockDim.x) {
+    const int64_t old = p.stg[lane * p.st + i];
+    if (old >= 0 && old < p.old_len) remap[old] = p.ql + i;
+  }
+}
+
 }  // namespace
+
+int launch_rebuild_remap(const RemapParams& p, int lanes, cudaStream_t st) {
+  if (lanes <= 0 || p.old_len <= 0) return MA_OK;
+  rebuild_remap_kernel<<<lanes, 256, 0, st>>>(p);
+  return cudaGetLastError() == cudaSuccess ? MA_OK : MA_ERR_CUDA;
+}
 
 int launch_compact(CompactParams& p, int B, cudaStream_t st) {
   if (p.C == 0 || p.narrays == 0) return MA_OK;

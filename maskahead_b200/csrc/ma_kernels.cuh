@@ -140,6 +140,16 @@ struct CompactParams {
   int chunks;            // set by launch_compact: the most blocks any array needs per lane
 };
 int launch_compact(CompactParams& p, int B, cudaStream_t st);
+// the remap of a group-preserving rebuild; index lists contiguous [lanes][count]
+struct RemapParams {
+  const int64_t* gb;
+  const int64_t* enc;
+  const int64_t* ga;
+  const int64_t* stg;
+  int64_t* remap;        // [lanes][old_len]
+  int g1, g2, g3, m, st, kgroup, old_len, ql;
+};
+int launch_rebuild_remap(const RemapParams& p, int lanes, cudaStream_t st);
 
 // device properties, cached per device
 int device_sm_count();

@@ -387,7 +387,7 @@ def rebuild(prefix, groups_before: torch.Tensor, encode: torch.Tensor, groups_af
     for t in idx:
         if t.ndim != 3 or tuple(t.shape[:2]) != (B, H):
             raise ValueError("index tensors must be [B, H, *]")
-    gb, enc, ga, stg = idx
+    gb, enc, ga, stg = (t.contiguous() for t in idx)
     g1, m, g3, st = (t.shape[-1] for t in idx)
     g2 = -(-m // gk)
     ql = (g1 + g2 + g3) * gk
@@ -403,8 +403,7 @@ def rebuild(prefix, groups_before: torch.Tensor, encode: torch.Tensor, groups_af
     tail_dtype = src.kf.dtype if src.nf else torch.bfloat16
     kr = torch.empty((B, H, rcap, D), device=dev, dtype=tail_dtype)
     vr = torch.empty_like(kr)
-    remap = torch.full((B, H, old_len + 1), -1, device=dev, dtype=torch.int64)   # last: sink for pads
-    ar = torch.arange(gk, device=dev)
+    remap = torch.empty((B, H, old_len), device=dev, dtype=torch.int64)
     sdesc = kv_descriptor(Prefix(**{s: getattr(src, s) for s in Prefix.__slots__ if s not in ("mask", "lens")}))
     lib = _lib.lib()
 
@@ -420,20 +419,13 @@ def rebuild(prefix, groups_before: torch.Tensor, encode: torch.Tensor, groups_af
         _lib.check("ma_compact_tokens", lib.ma_compact_tokens(
             sdesc.kv, ddesc.kv, B, H, D, safe.data_ptr(), n, i64(safe.stride(0), safe.stride(1)),
             _lib.stream_handle(dev)))
-        tok = (safe.unsqueeze(-1) * gk + ar).reshape(B, H, n * gk)
-        new_slot = ((torch.arange(n, device=dev) + at).view(1, 1, n, 1) * gk + ar).expand(B, H, n, gk)
-        valid = (gid >= 0).unsqueeze(-1).expand(-1, -1, -1, gk).reshape(B, H, n * gk)
-        remap.scatter_(-1, torch.where(valid, tok, old_len), new_slot.reshape(B, H, -1))
 
     copy_groups(gb, 0)
     copy_groups(ga, g1 + g2)
     if m:
         rows_k = torch.zeros((B, H, g2 * gk, D), device=dev, dtype=torch.bfloat16)
         rows_v = torch.zeros_like(rows_k)
-        _gather_rows_into(sdesc, enc.clamp_min(0).contiguous(), rows_k[:, :, :m], rows_v[:, :, :m])
-        dead = (enc < 0).unsqueeze(-1)
-        rows_k[:, :, :m].masked_fill_(dead, 0)
-        rows_v[:, :, :m].masked_fill_(dead, 0)
+        _gather_rows_into(sdesc, enc, rows_k[:, :, :m], rows_v[:, :, :m])     # -1 gathers a zero row
         pk, sk_ = kq[:, :, g1:g1 + g2], ks[:, :, g1:g1 + g2]
         _lib.check("ma_quantize_keys_channel", lib.ma_quantize_keys_channel(
             rows_k.data_ptr(), _lib.MA_BF16, B, H, g2 * gk, D, i64(*_strides3(rows_k)), gk, pk.data_ptr(),
@@ -444,15 +436,12 @@ def rebuild(prefix, groups_before: torch.Tensor, encode: torch.Tensor, groups_af
             rows_v.data_ptr(), _lib.MA_BF16, B, H, g2 * gk, D, i64(*_strides3(rows_v)), None, None, src.vg,
             pv.data_ptr(), i64(*_strides3(pv)), sv_.data_ptr(), vz[:, :, g1 * gk:(g1 + g2) * gk].data_ptr(),
             i64(*_strides3(sv_)), _lib.stream_handle(dev)))
-        slot = torch.arange(m, device=dev).view(1, 1, m).expand(B, H, m) + g1 * gk
-        remap.scatter_(-1, torch.where(enc >= 0, enc, old_len), slot)
     if st:
-        _gather_rows_into(sdesc, stg.clamp_min(0).contiguous(), kr[:, :, :st], vr[:, :, :st])
-        dead = (stg < 0).unsqueeze(-1)
-        kr[:, :, :st].masked_fill_(dead, 0)
-        vr[:, :, :st].masked_fill_(dead, 0)
-        slot = torch.arange(st, device=dev).view(1, 1, st).expand(B, H, st) + ql
-        remap.scatter_(-1, torch.where(stg >= 0, stg, old_len), slot)
+        _gather_rows_into(sdesc, stg, kr[:, :, :st], vr[:, :, :st])
+    _lib.check("ma_rebuild_remap", lib.ma_rebuild_remap(
+        B, H, old_len, gk, gb.data_ptr() if g1 else None, g1, enc.data_ptr() if m else None, m,
+        ga.data_ptr() if g3 else None, g3, stg.data_ptr() if st else None, st, remap.data_ptr(),
+        _lib.stream_handle(dev)))
     out = Prefix(kq=kq, ks=ks, kz=kz, vq=vq, vs=vs, vz=vz, kf=kr, vf=vr, nq=ql, nf=st, kb=4, vb=4, kg=gk,
                  vg=src.vg, kmode=0)
-    return out, remap[..., :old_len]
+    return out, remap
