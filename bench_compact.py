@@ -1,7 +1,7 @@
 """Time the cache compaction after an eviction (ma_compact_tokens) on one GPU.
 
-    python -m maskahead_b200.bench_compact [--layout token|bf16|channel] [--lanes N] [--n SLOTS]
-                                           [--keep C] [--iters K]
+    python bench_compact.py [--layout token|bf16|channel] [--lanes N] [--n SLOTS]
+                            [--keep C] [--iters K]
 
 Every layer of a serving batch compacts in one launch: lanes = layers x sequences x KV
 heads. The source arrays are filled with random bytes (the compaction moves codes and
@@ -24,22 +24,26 @@ from __future__ import annotations
 
 import argparse
 import json
+import sys
 from pathlib import Path
 
-import torch
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
 
-from .layouts import Prefix, compact_tokens
+import torch  # noqa: E402
+
+from maskahead_b200.layouts import Prefix, compact_tokens  # noqa: E402
 
 
 def _peak_gbs() -> tuple[float, str]:
-    p = Path(__file__).resolve().parents[1] / "MEASURED_PEAKS.json"
+    p = ROOT / "MEASURED_PEAKS.json"
     if p.exists():
         return float(json.loads(p.read_text())["hbm_gbs"]), "measured"
     return 6650.0, "fallback"
 
 
 def _time_rebuild(args, B, H, n, C, D, gen, rnd_u8, dev) -> None:
-    from .layouts import rebuild
+    from maskahead_b200.layouts import rebuild
 
     gk, rl = 32, 64
     ng = n // gk

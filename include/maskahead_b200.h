@@ -3,12 +3,19 @@
  *
  * Every entry point takes plain device pointers, element strides and sizes, enqueues
  * its kernels on the given CUDA stream (cudaStream_t passed as void*, NULL = legacy
- * default stream), never synchronizes, never allocates device memory, and returns an
+ * default stream), never synchronizes (the status queries ma_workspace_status and
+ * ma_value_score_noalloc_status excepted), never allocates device memory, and returns an
  * int status: MA_OK (0) or a negative MA_ERR_* code. Arguments are validated on the
  * host before anything is launched; a rejected call launches nothing. Scratch memory
  * is caller-provided ("workspace") and sized by the matching *_workspace() function;
  * a workspace must be zero-filled once when it is allocated (kernels leave it ready
  * for the next call) and must not be shared by calls that can overlap on the GPU.
+ *
+ * Device-side failures: every wait of a kernel is bounded. A wait that gives up records
+ * it in the error word of the call's workspace and the rows it could not finish are
+ * written as NaN; the status of the call itself (MA_OK) only covers the host-side checks
+ * and the launch. ma_workspace_status reads (and clears) that error word and returns
+ * MA_ERR_TIMEOUT when it is set.
  *
  * Conventions
  *   query rows:  Q [B, Hq, T, D], Hq = G * H (GQA); the R = G*T rows of KV head h are
@@ -155,6 +162,21 @@ MA_API const char* ma_status_string(int status);
  * setting. Not part of the reference's interface.                                     */
 MA_API int ma_set_attention_kernel(int which);
 
+/* ---- device-side status --------------------------------------------------------------
+ * ma_workspace_status: waits for the work queued on `stream` (a stream synchronization),
+ * reads the error word of `workspace` (the first 256-byte boundary inside it, for every
+ * workspace layout of this library), clears it and returns MA_ERR_TIMEOUT if a bounded
+ * device wait of a call that used the workspace gave up since the last query, MA_OK if
+ * none did. Not part of the reference's interface (its Triton launches have no device
+ * waits).
+ * ma_set_peer_wait_ns: the bound on a CTA's wait for other CTAs of the same launch (the
+ * split merge of the attention calls and the value-score centre), process-wide; ns <= 0
+ * restores the default (200 ms). Returns the previous bound. A CTA whose wait ends early
+ * writes its rows as NaN and records the timeout; the launch stays consistent for the next
+ * call. The waits on a CTA's own copies and MMAs keep their fixed bounds.            */
+MA_API int ma_workspace_status(void* workspace, size_t workspace_bytes, void* stream);
+MA_API int64_t ma_set_peer_wait_ns(int64_t ns);
+
 /* ---- attention over [prefix | current block] ----------------------------------------
  * out[b, h*G+g, t, :] = softmax over the live prefix slots and the visible current keys.
  * causal_block > 0: query t sees current key j iff (c_pos0+j)/cb <= (q_pos0+t)/cb.
@@ -200,11 +222,15 @@ MA_API int ma_value_score(const ma_kv* kv, int B, int H, int D, const float* a, 
  * n, D)) exceeds it return MA_ERR_UNSUPPORTED. The first call on a device looks up the
  * array's device address; make that first call before any stream capture. Every call
  * shares the array: calls that can overlap on the GPU (two streams, two threads) race.
- * Allocates nothing (no cudaMalloc, cudaFree or allocating library routine).           */
+ * Allocates nothing (no cudaMalloc, cudaFree or allocating library routine).
+ * ma_value_score_noalloc_status: ma_workspace_status on that array (the current device's)
+ * -- MA_ERR_TIMEOUT if a bounded device wait of the last call gave up (its scores then
+ * hold NaN rows). Query it before the next call, which clears the word.               */
 #define MA_NOALLOC_SCRATCH_BYTES ((size_t)8 << 20)
 MA_API int ma_value_score_noalloc(const ma_kv* kv, int B, int H, int D, const float* a,
                                   const int64_t sa[2], float* score, const int64_t sscore[2],
                                   void* stream);
+MA_API int ma_value_score_noalloc_status(void* stream);
 
 /* ---- top-k read set -----------------------------------------------------------------
  * Per (b, h): the k largest scores among live slots (ties: lower slot first), written
@@ -280,7 +306,9 @@ MA_API int ma_unpack_prefix(const ma_kv* kv, int B, int H, int D, void* out_k, v
  * groups of kgroup slots (placed at group 0 and at group g1 + ceil(m/kgroup)), encode
  * names old slots re-encoded in order from slot g1*kgroup, stage old slots staged in
  * order from slot (g1 + ceil(m/kgroup) + g3) * kgroup. Entries outside [0, old_len) are
- * skipped.                                                                            */
+ * skipped. The lists are applied in that order (groups, encode, stage), so a slot named
+ * twice takes the later list's position, as the reference's successive scatters do.
+ * B*H above INT_MAX returns MA_ERR_UNSUPPORTED.                                        */
 MA_API int ma_rebuild_remap(int B, int H, int old_len, int kgroup, const int64_t* groups_before, int g1,
                             const int64_t* encode, int m, const int64_t* groups_after, int g3,
                             const int64_t* stage, int st, int64_t* remap, void* stream);

@@ -10,11 +10,15 @@ on top:
                            value_score, lookahead_survivors
   maskahead_b200.layouts   LayerCacheView, Prefix, the ma_kv descriptor
 
-There is no CPU path: the operators need the built library and a CUDA device.
+Kernel waits are bounded; ``device_status()`` raises ``MaError`` (MA_ERR_TIMEOUT) when one
+gave up since the last check. There is no CPU path: the operators need the built library
+and a CUDA device.
 """
 
-from ._lib import EXPORTED, KernelUnavailableError, LIB_PATH, MaError, load_library
+from ._lib import (EXPORTED, KernelUnavailableError, LIB_PATH, MaError, device_status, load_library,
+                   set_peer_wait_ns)
 
-__version__ = "0.1.0"
+__version__ = "0.2.0"
 
-__all__ = ["EXPORTED", "KernelUnavailableError", "LIB_PATH", "MaError", "load_library", "__version__"]
+__all__ = ["EXPORTED", "KernelUnavailableError", "LIB_PATH", "MaError", "device_status", "load_library",
+           "set_peer_wait_ns", "__version__"]

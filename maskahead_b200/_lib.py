@@ -16,6 +16,7 @@ LIB_PATH = Path(__file__).resolve().parent / "_lib" / "libmaskahead_b200.so"
 
 MA_OK = 0
 MA_ERR_UNSUPPORTED = -2
+MA_ERR_TIMEOUT = -5
 MA_F32, MA_BF16, MA_F16 = 0, 1, 2
 MA_KV_DENSE, MA_KV_PACKED_TOKEN, MA_KV_PACKED_CHANNEL = 0, 1, 2
 
@@ -73,6 +74,9 @@ _SIGNATURES = {
     "ma_version": (_i32, []),
     "ma_status_string": (ctypes.c_char_p, [_i32]),
     "ma_set_attention_kernel": (_i32, [_i32]),
+    "ma_workspace_status": (_i32, [_vp, _sz, _vp]),
+    "ma_set_peer_wait_ns": (ctypes.c_int64, [ctypes.c_int64]),
+    "ma_value_score_noalloc_status": (_i32, [_vp]),
     "ma_prefix_attention_workspace": (_sz, [_i32] * 6),
     "ma_prefix_attention": (_i32, [_P(MaRows), _P(MaKV), _i32, _P(MaBlock), _f32, _i32, _i32, _i32,
                                    _vp, _P(ctypes.c_int64), _vp, _vp, _vp, _vp, _sz, _vp]),
@@ -160,6 +164,35 @@ def stream_handle(device: torch.device) -> int:
 
 # ------------------------------------------------------------------------ workspaces
 _WORKSPACES: dict[tuple, torch.Tensor] = {}
+
+
+def device_status(device: torch.device | int | None = None) -> None:
+    """Raise MaError(MA_ERR_TIMEOUT) if a bounded device-side wait of a kernel that used one
+    of this module's workspaces on `device` gave up since the last check (its rows were
+    written as NaN). Waits for the work queued on the device's current stream and clears
+    the recorded errors."""
+    dev = torch.device("cuda", torch.cuda.current_device() if device is None else
+                       (device if isinstance(device, int) else device.index or 0))
+    lib_ = lib()
+    stream = stream_handle(dev)
+    failed = []
+    for (kind, index, purpose), buf in list(_WORKSPACES.items()):
+        if kind != "cuda" or index != dev.index:
+            continue
+        rc = lib_.ma_workspace_status(buf.data_ptr(), buf.numel(), stream)
+        if rc == MA_ERR_TIMEOUT:
+            failed.append(purpose)
+        elif rc != MA_OK:
+            check("ma_workspace_status", rc)
+    if failed:
+        detail = load_library().ma_status_string(MA_ERR_TIMEOUT).decode()
+        raise MaError("device_status", MA_ERR_TIMEOUT, f"{detail} in the work of: {', '.join(sorted(failed))}")
+
+
+def set_peer_wait_ns(ns: int) -> int:
+    """Bound (ns) on a kernel CTA's wait for the other CTAs of its launch; <= 0 restores the
+    default. Returns the previous bound (ma_set_peer_wait_ns)."""
+    return int(load_library().ma_set_peer_wait_ns(int(ns)))
 
 
 def workspace(device: torch.device, purpose: str, nbytes: int) -> torch.Tensor:

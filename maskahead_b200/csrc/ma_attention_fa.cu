@@ -57,7 +57,6 @@ constexpr int kSmemBytes = 1024 + kQBytes + (kKSlots + kVSlots) * kKVBytes;   //
 constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kColS = 0, kColO = 256;
 constexpr int kOutBox = 32 * 128;
-constexpr uint64_t kMergeWaitNs = 200000000ull;
 constexpr uint64_t kStallNs = 500000000ull;        // MMA issuer: longest time without progress
 constexpr unsigned kIdleNs = 64;                   // MMA issuer back-off when nothing was ready
 constexpr uint64_t kWaitNs = 500000000ull;
@@ -591,7 +590,7 @@ __global__ void __launch_bounds__(kThreads, 1) attn_partial_fa(const __grid_cons
     } else {
       const uint64_t t0 = global_ns();
       while (ld_acquire_u32(&A.fm.sync[group].y) == gen0) {
-        if (global_ns() - t0 > kMergeWaitNs) {
+        if (global_ns() - t0 > A.fm.wait_ns) {
           ok = false;
           atomicExch(A.err, 1);
           break;

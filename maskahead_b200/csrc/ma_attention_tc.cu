@@ -33,7 +33,7 @@
 
 #include "ma_combine.cuh"
 #include "ma_kernels.cuh"
-#include "ma_mma.cuh"
+#include "ma_cp_async.cuh"
 #include "ma_stage.cuh"
 #include "ma_tcgen05.cuh"
 #include "ma_tma.cuh"
@@ -89,7 +89,6 @@ struct __align__(64) Args {
   int fuse;                     // merge the splits in this (cooperative) launch
   FusedMerge fm;
 };
-constexpr uint64_t kMergeWaitNs = 200000000ull;   // bound on the wait for a group's splits
 
 // Per-thread staging of keys [j0, j0+kBN): gathered, masked or packed rows.
 template <bool PACKED>
@@ -667,7 +666,7 @@ __global__ void __launch_bounds__(kThreads, 1) attn_partial_tc(const __grid_cons
     } else {
       const uint64_t t0 = global_ns();
       while (ld_acquire_u32(&A.fm.sync[group].y) == s_gen) {
-        if (global_ns() - t0 > kMergeWaitNs) {
+        if (global_ns() - t0 > A.fm.wait_ns) {
           ok = false;
           atomicExch(A.err, 1);
           break;

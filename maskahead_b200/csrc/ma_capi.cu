@@ -17,6 +17,13 @@ int device_sm_count() {
   return cached[dev];
 }
 
+namespace {
+constexpr uint64_t kDefaultPeerWaitNs = 200000000ull;   // 200 ms
+uint64_t g_peer_wait_ns = kDefaultPeerWaitNs;
+}  // namespace
+
+uint64_t peer_wait_ns() { return g_peer_wait_ns; }
+
 }  // namespace ma
 
 using namespace ma;
@@ -214,6 +221,7 @@ int run_attention(const ma_rows& q, const ma_kv& kv, int H, const ma_block& cur,
       fm.o_p = o_p;
       fm.sync = sync;
       fm.sync_slots = kSyncSlots;
+      fm.wait_ns = peer_wait_ns();
       bool fused = false;
       rc = MA_ERR_UNSUPPORTED;
       if (fa) {
@@ -242,6 +250,27 @@ int run_attention(const ma_rows& q, const ma_kv& kv, int H, const ma_block& cur,
 extern "C" {
 
 int ma_version(void) { return (0 << 16) | 1; }
+
+int64_t ma_set_peer_wait_ns(int64_t ns) {
+  const int64_t prev = (int64_t)g_peer_wait_ns;
+  g_peer_wait_ns = ns > 0 ? (uint64_t)ns : kDefaultPeerWaitNs;
+  return prev;
+}
+
+int ma_workspace_status(void* workspace, size_t workspace_bytes, void* stream) {
+  if (!workspace || workspace_bytes < 256 + sizeof(int)) return MA_ERR_ARG;
+  // the error word sits at the first 256-byte boundary of every workspace layout
+  char* base = reinterpret_cast<char*>((reinterpret_cast<uintptr_t>(workspace) + 255) & ~uintptr_t(255));
+  if (base + sizeof(int) > reinterpret_cast<char*>(workspace) + workspace_bytes) return MA_ERR_ARG;
+  cudaStream_t st = (cudaStream_t)stream;
+  int word = 0;
+  if (cudaMemcpyAsync(&word, base, sizeof(int), cudaMemcpyDeviceToHost, st) != cudaSuccess ||
+      cudaStreamSynchronize(st) != cudaSuccess)
+    return MA_ERR_CUDA;
+  if (word == 0) return MA_OK;
+  if (cudaMemsetAsync(base, 0, sizeof(int), st) != cudaSuccess) return MA_ERR_CUDA;
+  return MA_ERR_TIMEOUT;
+}
 
 int ma_set_attention_kernel(int which) {
   const int prev = g_attention_kernel;
@@ -564,8 +593,10 @@ int ma_rebuild_remap(int B, int H, int old_len, int kgroup, const int64_t* group
   const int64_t g2 = ((int64_t)m + kgroup - 1) / kgroup;
   const int64_t ql = ((int64_t)g1 + g2 + g3) * kgroup;
   if (ql + st > 0x7fffffffLL) return MA_ERR_ARG;
+  const int64_t lanes = (int64_t)B * H;   // one CTA per lane: the grid's x extent
+  if (lanes > 0x7fffffffLL) return MA_ERR_UNSUPPORTED;
   RemapParams p{groups_before, encode, groups_after, stage, remap, g1, (int)g2, g3, m, st, kgroup, old_len, (int)ql};
-  return launch_rebuild_remap(p, B * H, (cudaStream_t)stream);
+  return launch_rebuild_remap(p, (int)lanes, (cudaStream_t)stream);
 }
 
 }  // extern "C"

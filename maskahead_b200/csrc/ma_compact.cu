@@ -74,7 +74,9 @@ __global__ void __launch_bounds__(kCompactThreads, 6) compact_kernel(CompactPara
 
 // The remap of a group-preserving rebuild (cache.py:236-335): one CTA per lane sets every
 // old slot to -1, then writes the new slot of every slot that a kept group, the encoded
-// list or the staged list names (entries < 0 are padding and name nothing).
+// list or the staged list names (entries < 0 are padding and name nothing). The lists are
+// written one after another (groups before, groups after, encoded, staged), as the
+// reference scatters them, so a slot named by two lists takes the later list's slot.
 __global__ void __launch_bounds__(256) rebuild_remap_kernel(RemapParams p) {
   const int64_t lane = blockIdx.x;
   int64_t* remap = p.remap + lane * p.old_len;
@@ -90,11 +92,13 @@ __global__ void __launch_bounds__(256) rebuild_remap_kernel(RemapParams p) {
       const int64_t old = g * gk + i % gk;
       if (g >= 0 && old < p.old_len) remap[old] = at + i;
     }
+    __syncthreads();
   }
   for (int i = threadIdx.x; i < p.m; i += blockDim.x) {
     const int64_t old = p.enc[lane * p.m + i];
     if (old >= 0 && old < p.old_len) remap[old] = (int64_t)p.g1 * gk + i;
   }
+  __syncthreads();
   for (int i = threadIdx.x; i < p.st; i += blockDim.x) {
     const int64_t old = p.stg[lane * p.st + i];
     if (old >= 0 && old < p.old_len) remap[old] = p.ql + i;

@@ -25,7 +25,12 @@ struct FusedMerge {
   float* o_p;
   uint2* sync;      // [B*H*row blocks], zero counters between calls
   int sync_slots;   // capacity of sync
+  uint64_t wait_ns; // bound on a CTA's wait for the other splits of its group
 };
+// The bound on every wait of one CTA for other CTAs of the same launch (the split merge's
+// and the value-score centre's generation words); ma_set_peer_wait_ns. The waits on a
+// CTA's own asynchronous copies and MMAs keep their fixed bounds.
+uint64_t peer_wait_ns();
 // Returns MA_OK with *fused = true when the merge ran inside the launch (the caller
 // then skips launch_attn_combine).
 int launch_attn_partial_tc(const ma_rows& q, const ma_kv& kv, int H, const ma_block& cur, float scale,

@@ -71,6 +71,7 @@ struct __align__(64) Args {
   int H, T2, slots_per_cta, want_centre;
   int nK, nV;               // K ring and V ring slots (phase 2 streams V through nK + nV)
   int given;                // a_j given in `mass` (value score only: no K, no exponentials)
+  uint64_t peer_wait_ns;    // bound on the wait for the head's centre (other CTAs)
 };
 
 __device__ __forceinline__ void sum_sync() { asm volatile("bar.sync 1, %0;\n" ::"r"(kSumThreads) : "memory"); }
@@ -485,7 +486,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefix_mass_fa(const __grid_const
   if (!sLast && threadIdx.x == 0) {
     const uint64_t t0 = global_ns();
     while (ld_acquire_u32(&A.sync[bh].y) == gen0) {
-      if (global_ns() - t0 > kWaitNs) {
+      if (global_ns() - t0 > A.peer_wait_ns) {
         s_wait_ok = 0;
         atomicExch(A.err, 1);
         break;
@@ -602,6 +603,7 @@ int launch_prefix_mass_fa(const ma_rows& q, const ma_kv& kv, int H, const int32_
   A.sync = w.sync;
   A.centre = want_centre ? w.centre : nullptr;
   A.err = w.err;
+  A.peer_wait_ns = peer_wait_ns();
   A.scale = scale;
   A.H = H;
   A.T2 = T2;
@@ -697,6 +699,7 @@ int launch_value_score_fa(const ma_kv& kv, int B, int H, int D, const float* a, 
   A.sync = w.sync;
   A.centre = w.centre;
   A.err = w.err;
+  A.peer_wait_ns = peer_wait_ns();
   A.H = H;
   A.want_centre = 1;
   A.given = 1;

@@ -22,7 +22,7 @@
 // Slot tiles stream through a 2-stage cp.async ring (each CTA holds its whole range,
 // up to 256 slots, in flight from the start). Every wait is bounded.
 #include "ma_kernels.cuh"
-#include "ma_mma.cuh"
+#include "ma_cp_async.cuh"
 #include "ma_stage.cuh"
 #include "ma_tcgen05.cuh"
 
@@ -45,7 +45,6 @@ constexpr int kTileBytes = kTile * kD * 2;  // 32 KB (K or V)
 constexpr int kSmemBytes = 1024 + kQBytes + 2 * kStages * kTileBytes;
 constexpr uint32_t kTmemCols = 256;
 constexpr int kMaxCtas = 1024;              // partial slots per head (the launcher never exceeds)
-constexpr uint64_t kWaitNs = 200000000ull;  // bound on the wait for the head's centre
 
 struct Args {
   ma_rows q;
@@ -63,6 +62,7 @@ struct Args {
   int* err;
   float scale;
   int H, T2, slots_per_cta;
+  uint64_t peer_wait_ns;  // bound on the wait for the head's centre (other CTAs)
 };
 
 template <bool PACKED, bool CENTRE>
@@ -339,7 +339,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefix_mass_tc(const Args A) {
   if (!sLast && threadIdx.x == 0) {
     const uint64_t t0 = global_ns();
     while (ld_acquire_u32(&A.sync[bh].y) == sGen) {
-      if (global_ns() - t0 > kWaitNs) {
+      if (global_ns() - t0 > A.peer_wait_ns) {
         s_wait_ok = 0;
         atomicExch(A.err, 1);
         break;
@@ -433,6 +433,7 @@ int launch_prefix_mass_tc(const ma_rows& q, const ma_kv& kv, int H, const int32_
   A.sync = w.sync;
   A.centre = want_centre ? w.centre : nullptr;
   A.err = w.err;
+  A.peer_wait_ns = peer_wait_ns();
   A.scale = scale;
   A.H = H;
   A.T2 = T2;

@@ -39,6 +39,11 @@ int scratch_address(void** out) {
   return MA_OK;
 }
 
+// Bytes at the front of the array that a call of BH heads needs zeroed: the error word
+// (offset 0) and the (counter, generation) pairs of heads 0..BH-1 (from offset 8), in
+// 256-byte units.
+size_t noalloc_clear_bytes(int BH) { return ((8 + (size_t)BH * sizeof(uint2) + 255) / 256) * 256; }
+
 }  // namespace
 
 extern "C" {
@@ -54,9 +59,18 @@ int ma_value_score_noalloc(const ma_kv* kv, int B, int H, int D, const float* a,
   void* ws = nullptr;
   int rc = scratch_address(&ws);
   if (rc != MA_OK) return rc;
-  // the per-head counters must start at zero; earlier calls leave the rest behind
-  if (cudaMemsetAsync(ws, 0, ma::value_sync_bytes(B * H), (cudaStream_t)stream) != cudaSuccess) return MA_ERR_CUDA;
+  // the error word and this call's per-head (counter, generation) pairs must start at
+  // zero; the rest of the array keeps what earlier calls left and is overwritten before
+  // it is read
+  if (cudaMemsetAsync(ws, 0, noalloc_clear_bytes(B * H), (cudaStream_t)stream) != cudaSuccess) return MA_ERR_CUDA;
   return ma_value_score(kv, B, H, D, a, sa, score, sscore, ws, kScratchBytes, stream);
+}
+
+int ma_value_score_noalloc_status(void* stream) {
+  void* ws = nullptr;
+  const int rc = scratch_address(&ws);
+  if (rc != MA_OK) return rc;
+  return ma_workspace_status(ws, kScratchBytes, stream);
 }
 
 }  // extern "C"

@@ -16,7 +16,7 @@
 #pragma once
 
 #include "ma_common.cuh"
-#include "ma_mma.cuh"
+#include "ma_cp_async.cuh"
 #include "ma_tcgen05.cuh"
 
 namespace ma {

@@ -3,6 +3,10 @@
 These functions are what the reference session's fast path does per layer
 (src/maskahead/runtime/session.py), written against the sm_100a operators:
 
+  dense_required      _dense_required (456-467): whether a layer skips selection and
+                      attends densely (dense-prefix layers, a budget covering the prefix).
+  fast_attend         _fast_attend (1378-1393): the dense layers' sub-steps, attention over
+                      [live prefix | block], optionally with the prefix mass of some rows.
   fast_step0          _fast_step0 (1403-1454): dense attention over [live prefix |
                       block], the block's prefix mass, the value-aware score, the
                       ascending top-k read set and (gather=True) the read set's K/V rows
@@ -31,7 +35,7 @@ from .kernels.ops import gather_packed_kv, select_topk_indices
 from .kernels.splitk import prefix_scores, splitk_attention
 from .layouts import Prefix, as_prefix, kv_descriptor
 
-__all__ = ["Step0Result", "fast_step0", "unpacked_prefix", "gather_read_set", "compact_attention", "probe_attention", "value_score",
+__all__ = ["Step0Result", "dense_required", "fast_attend", "fast_step0", "unpacked_prefix", "gather_read_set", "compact_attention", "probe_attention", "value_score",
            "value_score_prefix", "lookahead_survivors"]
 
 
@@ -42,6 +46,35 @@ class Step0Result:
     mass: torch.Tensor | None            # [B, Hkv, n] prefix mass of the selection rows
     score: torch.Tensor | None           # [B, Hkv, n] value-aware score (value_aware only)
     compact: Prefix | None = None        # the read set's rows, gathered (gather=True only)
+
+
+def dense_required(layer_idx: int, *, dense_prefix_layers: int, old_cache_len: int, topk: int,
+                   query_indices, eviction: bool = False, live_cache_len: int | None = None,
+                   semantic: str = "A") -> bool:
+    """Whether layer `layer_idx` attends densely instead of through a read set
+    (session.py:456-467): the dense semantic, the first `dense_prefix_layers` layers, an
+    empty cache or no selection rows, and -- without eviction -- a budget `topk` (the
+    selector's effective top-k for this cache length) that covers the whole prefix. With
+    eviction the cache is the live set and a covering budget still selects."""
+    if semantic == "dense" or layer_idx < dense_prefix_layers:
+        return True
+    if eviction:
+        return (live_cache_len or 0) == 0 or not query_indices
+    return old_cache_len == 0 or int(topk) >= old_cache_len or not query_indices
+
+
+def fast_attend(query: torch.Tensor, prefix, current_key: torch.Tensor, current_value: torch.Tensor, *,
+                scaling: float | None = None, causal: int = 0, q_pos0: int = 0, mass_rows=None):
+    """Attention over [live prefix | current block] and, with mass_rows, the prefix mass of
+    those rows (session.py:1378-1393): what a dense layer's sub-steps run. Returns
+    (out, mass or None)."""
+    prefix = as_prefix(prefix)
+    out, stats = splitk_attention(query, prefix, current_key, current_value, scaling=scaling, causal_block=causal,
+                                  q_pos0=q_pos0, c_pos0=q_pos0, want_prefix=mass_rows is not None)
+    if mass_rows is None or prefix.n == 0:
+        return out, None
+    mass, _ = prefix_scores(query, prefix, stats, mass_rows, value=False, scaling=scaling)
+    return out, mass
 
 
 def fast_step0(query: torch.Tensor, prefix, current_key: torch.Tensor, current_value: torch.Tensor, *,

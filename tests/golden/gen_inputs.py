@@ -27,7 +27,16 @@ CASES = {
                              packed="token"),
     "small_k4v4_channel": dict(B=1, Hq=8, H=2, D=128, T=32, n=320, dtype="bfloat16", k=64, C=128, seed=10,
                                packed="channel"),
+    # one layer of the benchmarked configurations: cfg2 (bf16 K/V, prefix 8192, read budget
+    # 1024) and cfg3 (the same shape in k4v4 token mode, 1% of the key channels x8)
+    "cfg2_layer": dict(B=1, Hq=28, H=4, D=128, T=32, n=8192, dtype="bfloat16", k=1024, C=2048, seed=1236),
+    "cfg3_layer": dict(B=1, Hq=28, H=4, D=128, T=32, n=8192, dtype="bfloat16", k=1024, C=2048, seed=1237,
+                       packed="token"),
 }
+
+# cases whose packed payloads are too large to store: the fixture's input digest (which
+# covers the payloads) pins them instead
+LARGE = {"cfg2_layer", "cfg3_layer"}
 
 
 def _dt(name: str) -> torch.dtype:

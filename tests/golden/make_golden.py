@@ -1,9 +1,9 @@
 """Generate the golden fixtures in this folder from the REFERENCE implementation.
 
-Run in a container where the reference package is mounted (default location below,
-override with MASKAHEAD_REF_SRC):
+Run where the reference package's source tree is available, naming its ``src``
+directory (the folder that holds the ``maskahead`` package):
 
-    python tests/golden/make_golden.py
+    MASKAHEAD_REF_SRC=<reference checkout>/src python tests/golden/make_golden.py
 
 For each case of gen_inputs.CASES it builds the reference's LayerCacheView on the
 seeded inputs and records what the reference's own CPU (torch) path returns:
@@ -35,10 +35,13 @@ import torch
 
 HERE = Path(__file__).resolve().parent
 sys.path.insert(0, str(HERE))
-sys.path.insert(0, os.environ.get("MASKAHEAD_REF_SRC", "/root/reference/src"))
+_REF_SRC = os.environ.get("MASKAHEAD_REF_SRC")
+if not _REF_SRC or not (Path(_REF_SRC) / "maskahead").is_dir():
+    raise SystemExit("set MASKAHEAD_REF_SRC to the reference's src directory (the folder holding maskahead/)")
+sys.path.insert(0, _REF_SRC)
 os.environ["BITSIEVE_VSCORE_FP32"] = "1"
 
-from gen_inputs import CASES, digest, make_case, make_retain_case  # noqa: E402
+from gen_inputs import CASES, LARGE, digest, make_case, make_retain_case  # noqa: E402
 
 from maskahead.cache import LayerCacheView, PackedKVCache  # noqa: E402
 from maskahead.config import QuantizationConfig  # noqa: E402
@@ -146,7 +149,7 @@ def build_case(name: str) -> dict:
         topk=np.array(topk),
     )
     for key in ("kq", "ks", "kz", "vq", "vs", "vz", "kchan"):
-        if key in extra:
+        if key in extra and name not in LARGE:
             t = extra[key]
             out["packed_" + key] = t.view(torch.int16).numpy() if t.dtype in (torch.float16, torch.bfloat16) else t.numpy()
     return out
@@ -279,9 +282,14 @@ def build_rebuild(seed: int = 23, L: int = 2, B: int = 1, H: int = 2, n: int = 3
 
 
 def main() -> None:
+    only = set(sys.argv[1:])
     for name in CASES:
+        if only and name not in only:
+            continue
         np.savez_compressed(HERE / f"{name}.npz", **build_case(name))
         print("wrote", name)
+    if only:
+        return
     np.savez_compressed(HERE / "retain.npz", **build_retain())
     print("wrote retain")
     np.savez_compressed(HERE / "compact_token.npz", **build_compact("token", 21, 2, 1, 2, 300, 96))

@@ -3,8 +3,9 @@ lookahead probe (block-causal attention of [block | probe blocks] over [prefix |
 plus the probe rows' prefix mass, session.py:2317-2332) and the value score over a cache
 layout (a_j ||v_j - c||, session.py:27-40 with the live values in the compute dtype).
 
-A packed prefix is dequantized once into bf16 (hotpath.unpacked_prefix: the bit-exact
-unpack the gather tests pin) and the oracle runs on those bf16 K/V. Bars: the attention
+A packed prefix is quantized on the CPU by the oracle (token-mode keys with their
+divisor), its payloads are what the device reads, and the oracle runs on its own bf16
+dequantization of the same payloads -- no expected value comes from a device kernel. Bars: the attention
 output at the bf16 bar of the other attention tests (2e-2), the probe mass to 1e-4 (the
 oracle's own prefix statistics against the device's, which sum in another order), the
 value score to 5e-5.
@@ -34,15 +35,16 @@ def _inputs(seed, B=1, Hq=8, H=2, T=96, n=3000, D=128):
 
 
 def _prefix(kind, k, v):
-    from maskahead_b200.hotpath import unpacked_prefix
-    from maskahead_b200.layouts import Prefix, pack_prefix
+    from maskahead_b200.layouts import Prefix
 
-    kd, vd = k.to(DEV), v.to(DEV)
     if kind == "dense":
-        return Prefix.dense(kd, vd), k, v
-    pre = pack_prefix(kd, vd)
-    un = unpacked_prefix(pre, k.shape[0], k.shape[1], k.shape[3])
-    return pre, un.kf.cpu().clone(), un.vf.cpu().clone()
+        return Prefix.dense(k.to(DEV), v.to(DEV)), k, v
+    kchan = oracle.key_channel_divisor(k)
+    kq, ks, kz = oracle.quantize_keys_token(k, kchan)
+    vq, vs, vz = oracle.quantize_values(v)
+    pre = Prefix(kq=kq.to(DEV), ks=ks.to(DEV), kz=kz.to(DEV), vq=vq.to(DEV), vs=vs.to(DEV), vz=vz.to(DEV),
+                 nq=k.shape[2], kb=4, vb=4, kg=32, vg=32, kmode=1, kch=kchan.to(DEV))
+    return pre, oracle.dequantize_keys_token(kq, ks, kz, kchan), oracle.dequantize_values(vq, vs, vz)
 
 
 @pytest.mark.parametrize("kind", ["dense", "packed"])

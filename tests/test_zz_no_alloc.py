@@ -87,3 +87,28 @@ def test_value_score_noalloc_rejects_sizes_beyond_its_scratch():
                                     ctypes.c_void_p(torch.cuda.current_stream().cuda_stream))
     assert rc == -2
     torch.cuda.synchronize()
+
+
+def test_value_score_noalloc_status_reports_a_timeout():
+    """A bounded wait of the no-alloc call that gives up (the centre wait, bounded here at
+    1 ns) shows in ma_value_score_noalloc_status; the next call, with the bound restored,
+    runs clean and matches ma_value_score again."""
+    import maskahead_b200
+    from maskahead_b200._lib import lib as get_lib
+
+    lib = get_lib()
+    stream = torch.cuda.current_stream().cuda_stream
+    a, v = _inputs(8, 1, 4, 8192, 128)
+    kv = _kv(v)
+    want = _with_workspace(lib, kv, a, v, stream)
+    assert lib.ma_value_score_noalloc_status(stream) == 0
+    prev = maskahead_b200.set_peer_wait_ns(1)
+    try:
+        got = _no_alloc(lib, kv, a, v, stream)
+        assert lib.ma_value_score_noalloc_status(stream) == -5
+        assert bool(torch.isnan(got).any())
+    finally:
+        maskahead_b200.set_peer_wait_ns(prev)
+    got = _no_alloc(lib, kv, a, v, stream)
+    assert lib.ma_value_score_noalloc_status(stream) == 0
+    np.testing.assert_allclose(got.cpu().numpy(), want.cpu().numpy(), rtol=2e-5, atol=1e-12)
