@@ -16,6 +16,10 @@ Workloads (--config picks one, the default is the headline cfg
         sequences (strong scaling, no collective). Retention is not part of this step:
         the retention kernel takes one live length for all lanes.
 
+The headline line measures --config (default cfg2); the further configs (--configs,
+default cfg3, cfg4 and cfg5) are measured in the same run, each under "configs" with its
+own timing, e2e leg and per-kernel rooflines.
+
 One step = one block-step over all layers:
   step 0     score (prefix mass of the 32 mask queries x G query heads), value-aware
              score, top-k read set, dense attention over [prefix | block];
@@ -25,7 +29,12 @@ One step = one block-step over all layers:
 Synthetic seeded inputs, N(0,1); every cache exceeds L2 (126 MB), so each step reads it
 from HBM. `value` = tokens/s (32 tokens per block-step per sequence) over all ranks.
 
-  python bench.py [--config cfg2] [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+Per kernel family ("rooflines"): one CUDA graph of one call per layer, L2 flushed before
+every replay, achieved GB/s on algorithmic bytes against the measured HBM copy peak and
+tensor TFLOP/s against the measured bf16 GEMM peaks (burst and sustained).
+
+  python bench.py [--config cfg2] [--configs cfg3,cfg4,cfg5] [--gpus N] [--steps K] [--warmup W]
+                  [--impl ours|reference]
 """
 
 from __future__ import annotations
@@ -80,6 +89,9 @@ def parse_args():
     ap.add_argument("--layers", type=int, default=0,
                     help="override the config's layer count (profiling captures on a small device footprint; "
                          "the JSON line records it and is not the config's headline number)")
+    ap.add_argument("--configs", default="auto",
+                    help="further configs measured in the same run, each reported under 'configs' with its own "
+                         "timing, e2e and rooflines (comma list; 'auto': cfg3,cfg4,cfg5; '' for none)")
     ap.add_argument("--eager", action="store_true",
                     help="time eager block-steps instead of CUDA-graph replays (for launch lists: under ncu "
                          "the replay of a cooperative kernel node fails to launch)")
@@ -87,14 +99,6 @@ def parse_args():
 
 
 # --------------------------------------------------------------------------- helpers
-def peaks():
-    p = ROOT / "MEASURED_PEAKS.json"
-    if p.exists():
-        d = json.loads(p.read_text())
-        return float(d["hbm_gbs"]), float(d["bf16_tflops"]), "measured"
-    return 6650.0, 1590.0, "fallback"
-
-
 class ClockSampler:
     """nvidia-smi clocks and throttle reasons sampled every 200 ms while running."""
 
@@ -151,28 +155,19 @@ def sequence_lengths(cfg: dict) -> list[int]:
 
 
 def rank_share(cfg: dict, rank: int, world: int) -> dict:
-    """What one rank runs: its sequences (lengths) and KV heads."""
+    """What one rank runs: its sequences (lengths) and KV heads (maskahead_b200.shard)."""
+    from maskahead_b200.shard import head_shard, sequence_shard
+
     lens = sequence_lengths(cfg)
     if cfg["shard"] == "heads":
-        if cfg["H"] % world:
-            raise SystemExit(f"{cfg['name']}: {cfg['H']} KV heads do not split over {world} ranks")
-        h = cfg["H"] // world
-        return dict(lens=lens, H=h, Hq=cfg["Hq"] // world, head0=rank * h)
+        try:
+            hs = head_shard(cfg["H"], cfg["Hq"], world, rank)
+        except ValueError as exc:
+            raise SystemExit(f"{cfg['name']}: {exc}")
+        return dict(lens=lens, H=hs.H, Hq=hs.Hq, head0=hs.h0)
     if cfg["scaling"] == "weak":
         return dict(lens=lens, H=cfg["H"], Hq=cfg["Hq"], head0=0)
-    # strong scaling over sequences: contiguous ranges, each cut at the prefix sum nearest
-    # to its ideal share of the total length (every share within one sequence of ideal)
-    total = sum(lens)
-    prefix = [0]
-    for n in lens:
-        prefix.append(prefix[-1] + n)
-    bounds = [0]
-    for r in range(1, world):
-        goal = total * r / world
-        i = min(range(bounds[-1], len(lens) + 1), key=lambda j: abs(prefix[j] - goal))
-        bounds.append(i)
-    bounds.append(len(lens))
-    return dict(lens=lens[bounds[rank]:bounds[rank + 1]], H=cfg["H"], Hq=cfg["Hq"], head0=0)
+    return dict(lens=sequence_shard(lens, world, rank).lens, H=cfg["H"], Hq=cfg["Hq"], head0=0)
 
 
 # ------------------------------------------------------------------------- workload
@@ -266,6 +261,9 @@ class Workload:
                          torch.empty(B, H, c["k"], D, device=device, dtype=bf)) for _ in range(L)]
         torch.cuda.synchronize(device)
         self.outputs = None
+        from maskahead_b200.shard import HeadGather
+
+        self.head_gather = HeadGather(world)
 
     def compact_buffers(self, layer: int):
         return self.compact[layer]
@@ -281,7 +279,7 @@ class Workload:
         """KV-head sharding: the full [B, Hq, T, D] output from every rank's heads (NCCL)."""
         if self.world == 1 or self.cfg["shard"] != "heads":
             return out
-        return gather_heads(out, self.world)
+        return self.head_gather(out)
 
     def block_step(self, retain: bool):
         """One block-step over every layer through the public hot-path API."""
@@ -320,18 +318,6 @@ class Workload:
             keep = lookahead_survivors(self.pos, score, c["C"], recent_window=c["W"], sink_tokens=c["sinks"])
         self.outputs = (outs, idxs, keep)
         return self.outputs
-
-
-def gather_heads(out, world: int):
-    """All-gather of per-rank head outputs [B, Hq/world, T, D] into [B, Hq, T, D]; rank r
-    holds query heads [r*Hq/world, (r+1)*Hq/world) (the heads of its KV heads)."""
-    import torch
-    import torch.distributed as dist
-
-    b = out.shape[0]
-    buf = torch.empty((world * b,) + tuple(out.shape[1:]), device=out.device, dtype=out.dtype)
-    dist.all_gather_into_tensor(buf, out.contiguous())   # rank-major along dim 0
-    return buf.view(world, b, *out.shape[1:]).permute(1, 0, 2, 3, 4).reshape(b, -1, out.shape[2], out.shape[3])
 
 
 def fused_scores(cfg: dict, share: dict) -> bool:
@@ -405,92 +391,134 @@ def algorithmic_bytes(cfg: dict, share: dict) -> dict:
                 block_step=L * (step0 + gather + (cfg["substeps"] - 1) * sub), retention=L * ret)
 
 
-def step0_flops(cfg: dict, share: dict) -> float:
-    """Tensor-core FLOPs of the step-0 attention partial kernel per layer: Q.K^T and P.V."""
-    return 4.0 * share["Hq"] * cfg["T"] * sum(share["lens"]) * cfg["D"]
-
-
 # ---------------------------------------------------------------------- CPU baseline
-def cpu_block_step_time(cfg: dict, sample_layers: int, threads: int | None = None):
-    """The oracle (a restatement of the reference's torch CPU path) timed on the host:
-    step 0 (importance, value-aware rescoring, top-k, dense attention) and the sparse
-    sub-steps (sdpa over the gathered read set) -- with packed caches dequantized first,
-    as the reference's torch path reads them -- plus the retention scoring once per
-    interval, for `sample_layers` layers of one sampled sequence; scaled to one
-    block-step of the whole job (all layers, all sequences by their lengths).
-    Returns (seconds per block-step, threads, sample description)."""
-    import torch
+def cpu_model() -> str:
+    try:
+        for line in Path("/proc/cpuinfo").read_text().splitlines():
+            if line.startswith("model name"):
+                return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    import platform
 
-    import oracle
+    return platform.processor() or "unknown"
+
+
+class CpuBlockStep:
+    """The oracle (a restatement of the reference's torch CPU path) for one sequence of
+    prefix n on the host: per layer step 0 (importance, value-aware rescoring, top-k,
+    dense attention over [prefix | block]) and the sparse sub-steps (sdpa over the gathered
+    read set), with a packed cache dequantized first as the reference's torch path reads
+    it; the retention scoring (probe importance, lookahead value score, survivors) per layer.
+    Inputs of `distinct` layers are generated once (untimed) and used in turn."""
+
+    def __init__(self, cfg: dict, n: int, distinct: int = 4):
+        import torch
+
+        import oracle
+
+        c = self.cfg = cfg
+        self.n = n
+        g = torch.Generator().manual_seed(c["seed"])
+        Hq, H, D, T = c["Hq"], c["H"], c["D"], c["T"]
+        bf = torch.bfloat16
+        self.packed = c["kv"] != "bf16"
+        self.layers = []
+        for _ in range(max(1, min(distinct, c["L"]))):
+            k = torch.randn(1, H, n, D, generator=g).to(bf)
+            v = torch.randn(1, H, n, D, generator=g).to(bf)
+            d = dict(q=[torch.randn(1, Hq, T, D, generator=g).to(bf) for _ in range(c["substeps"])],
+                     kc=torch.randn(1, H, T, D, generator=g).to(bf), vc=torch.randn(1, H, T, D, generator=g).to(bf),
+                     qp=torch.randn(1, Hq, T * (1 + c["probe_blocks"]), D, generator=g).to(bf))
+            if self.packed:
+                kchan = oracle.key_channel_divisor(k)
+                d.update(pk=oracle.quantize_keys_token(k, kchan), pv=oracle.quantize_values(v), kchan=kchan)
+            else:
+                d.update(k=k, v=v)
+            self.layers.append(d)
+        self.pos = torch.arange(n, dtype=torch.int32).expand(1, 1, H, n).contiguous()
+        self.rows = list(range(T))
+        self.probe_rows = list(range(T, T * (1 + c["probe_blocks"])))
+        self.scale = D ** -0.5
+
+    def _kv(self, d):
+        import oracle
+
+        if self.packed:   # the reference's torch path dequantizes the packed view before attending
+            return oracle.dequantize_keys_token(*d["pk"], d["kchan"]), oracle.dequantize_values(*d["pv"])
+        return d["k"], d["v"]
+
+    def layer(self, i: int, retain: bool) -> float:
+        """Seconds of layer i's block-step (and its retention scoring when retain)."""
+        import torch
+
+        import oracle
+
+        c, d = self.cfg, self.layers[i % len(self.layers)]
+        t0 = time.perf_counter()
+        k, v = self._kv(d)
+        q = d["q"][0]
+        imp = oracle.selector_importance(q, k, query_indices=self.rows, scale=self.scale)
+        score = oracle.rescore_by_value(imp, v)
+        idx, _ = oracle.topk_reference_torch(score, c["k"])
+        oracle.dense_attention(q, k, v, d["kc"], d["vc"], scale=self.scale)
+        sk = torch.cat([oracle.gather_per_kv_head(k, idx), d["kc"]], dim=2)
+        sv = torch.cat([oracle.gather_per_kv_head(v, idx), d["vc"]], dim=2)
+        for s in range(1, c["substeps"]):
+            oracle.sdpa_compact(d["q"][s], sk, sv)
+        if retain and c["retention"]:
+            ap = oracle.selector_importance(d["qp"], k, query_indices=self.probe_rows, scale=self.scale)
+            sc = oracle.lookahead_score(imp, ap * c["probe_blocks"], v)
+            oracle.survivors_lookahead(self.pos, sc.unsqueeze(0), c["C"], recent_window=c["W"],
+                                       sink_tokens=c["sinks"])
+        return time.perf_counter() - t0
+
+
+def cpu_baseline(cfg: dict, budget_s: float = 20.0, threads: int | None = None) -> dict:
+    """The oracle timed on the host cores, one sequence (the median length): whole
+    block-steps over all layers when three of them fit in budget_s (each the step 0 and
+    sub-steps of every layer, the retention scoring on every interval-th), else a sample
+    of layers scaled to the block-step; scaled to the job's sequences by length."""
+    import torch
 
     threads = threads or os.cpu_count() or 1
     torch.set_num_threads(threads)
     c = cfg
-    g = torch.Generator().manual_seed(c["seed"])
-    Hq, H, D, T = c["Hq"], c["H"], c["D"], c["T"]
     lens = sequence_lengths(c)
     n = int(statistics.median(lens))
-    bf = torch.bfloat16
-    rows = list(range(T))
-    scale = D ** -0.5
-    packed = c["kv"] != "bf16"
-
-    def one_layer():
-        k = torch.randn(1, H, n, D, generator=g)
-        v = torch.randn(1, H, n, D, generator=g).to(bf)
-        q = torch.randn(1, Hq, T, D, generator=g).to(bf)
-        kc = torch.randn(1, H, T, D, generator=g).to(bf)
-        vc = torch.randn(1, H, T, D, generator=g).to(bf)
-        qp = torch.randn(1, Hq, T * (1 + c["probe_blocks"]), D, generator=g).to(bf)
-        if packed:
-            kb = k.to(bf)
-            kchan = oracle.key_channel_divisor(kb)
-            pk = oracle.quantize_keys_token(kb, kchan)
-            pv = oracle.quantize_values(v)
-        else:
-            k = k.to(bf)
-        t0 = time.perf_counter()
-        if packed:   # the reference's torch path dequantizes the packed view before attending
-            k = oracle.dequantize_keys_token(*pk, kchan)
-            v = oracle.dequantize_values(*pv)
-        imp = oracle.selector_importance(q, k, query_indices=rows, scale=scale)
-        score = oracle.rescore_by_value(imp, v)
-        idx, _ = oracle.topk_reference_torch(score, c["k"])
-        oracle.dense_attention(q, k, v, kc, vc, scale=scale)
-        sk = torch.cat([oracle.gather_per_kv_head(k, idx), kc], dim=2)
-        sv = torch.cat([oracle.gather_per_kv_head(v, idx), vc], dim=2)
-        for _ in range(c["substeps"] - 1):
-            oracle.sdpa_compact(q, sk, sv)
-        t1 = time.perf_counter()
-        if c["retention"]:
-            ap = oracle.selector_importance(qp, k, query_indices=list(range(T, qp.shape[2])), scale=scale)
-            oracle.lookahead_score(imp, ap, v)
-        t2 = time.perf_counter()
-        return t1 - t0, t2 - t1
-
-    one_layer()  # warm-up
-    step, ret = [], []
-    for _ in range(sample_layers):
-        a, b = one_layer()
-        step.append(a)
-        ret.append(b)
-    t_surv = 0.0
-    if c["retention"]:
-        pos = torch.arange(n, dtype=torch.int32).expand(1, 1, H, n).contiguous()
-        sc = torch.rand(1, 1, H, n, generator=g)
-        t0 = time.perf_counter()
-        oracle.survivors_lookahead(pos, sc, c["C"], recent_window=c["W"], sink_tokens=c["sinks"])
-        t_surv = (time.perf_counter() - t0) * c["L"]
-    scale_seqs = sum(lens) / n            # the job's sequences, by length
-    per_block = scale_seqs * (c["L"] * statistics.median(step) +
-                              (c["L"] * statistics.median(ret) + t_surv) / c["interval"])
-    sample = (f"{sample_layers} layer(s) of one sequence (n={n}): step 0 + {c['substeps'] - 1} sparse sub-steps"
-              + (" + retention scoring" if c["retention"] else "")
-              + (" with k4v4 dequantization" if packed else "")
-              + f" (median), scaled to {c['L']} layers x {len(lens)} sequence(s) by length"
-              + (f", retention every {c['interval']} blocks" if c["retention"] else "")
-              + f"; torch fp32 CPU, {threads} threads")
-    return per_block, threads, sample
+    step = CpuBlockStep(c, n)
+    step.layer(0, True)                      # warm-up (untimed)
+    probe = step.layer(1, False)
+    L = c["L"]
+    if 3 * L * probe <= budget_s:
+        reps = max(3, min(c["interval"], int(budget_s // max(L * probe, 1e-6))))
+        times = []
+        for r in range(reps):
+            retain = c["retention"] and (r % c["interval"]) == c["interval"] - 1
+            times.append(sum(step.layer(i, retain) for i in range(L)))
+        plain = [t for r, t in enumerate(times) if not (c["retention"] and (r % c["interval"]) == c["interval"] - 1)]
+        ret = [t for t in times if t not in plain]
+        per_block = statistics.mean(plain) if not ret else \
+            ((c["interval"] - 1) * statistics.mean(plain) + statistics.mean(ret)) / c["interval"]
+        sample = (f"{reps} whole block-steps of one sequence (n={n}, {L} layers: step 0 + {c['substeps'] - 1} "
+                  f"sparse sub-steps each" + (f", the retention scoring in every {c['interval']}th" if ret else "")
+                  + ")" + ("; k4v4 dequantization included" if step.packed else ""))
+        layers_timed, whole_steps = reps * L, reps
+    else:
+        m = max(2, min(L, int(budget_s // max(probe, 1e-6))))
+        plain = [step.layer(i, False) for i in range(m)]
+        ret = [step.layer(i, True) - p for i, p in zip(range(min(2, m)), plain)] if c["retention"] else []
+        per_block = L * statistics.median(plain) + (L * statistics.median(ret) / c["interval"] if ret else 0.0)
+        sample = (f"{m} layer(s) of one sequence (n={n}): step 0 + {c['substeps'] - 1} sparse sub-steps (median), "
+                  f"scaled to {L} layers" + (f", retention scoring every {c['interval']} blocks" if ret else "")
+                  + ("; k4v4 dequantization included" if step.packed else ""))
+        layers_timed, whole_steps = m, 0
+    scale_seqs = sum(lens) / n
+    if len(lens) > 1:
+        sample += f"; scaled to {len(lens)} sequences by length"
+    sample += f"; torch fp32 CPU, {threads} threads"
+    return dict(seconds=per_block * scale_seqs, threads=threads, sample=sample, layers_timed=layers_timed,
+                whole_steps=whole_steps, cpu_model=cpu_model())
 
 
 def tokens_per_step(cfg: dict) -> int:
@@ -499,27 +527,51 @@ def tokens_per_step(cfg: dict) -> int:
 
 def run_reference(args):
     """--impl reference: the reference algorithm's CPU path (the oracle restatement; the
-    reference package itself is not shipped to the GPU box) on the host cores."""
+    reference package is pure Python and does not travel to the GPU box) on every host
+    core, on the same workload as our arm. For a config whose block-step takes a few
+    seconds on the host (cfg2, cfg3) each of the K timed steps is one whole block-step of
+    all layers (the retention scoring in every interval-th), after W untimed ones; for the
+    larger ones each step is a bounded sample (stated) scaled to the block-step."""
+    import torch
+
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
     c = CONFIGS[args.config]
-    t_block, threads, sample = cpu_block_step_time(c, max(1, args.cpu_sample_layers))
-    steps = []
-    for _ in range(max(1, args.steps // 10)):
-        t, _, _ = cpu_block_step_time(c, 1, threads)
-        steps.append(t)
-    t_block = statistics.median(steps + [t_block])
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    lens = sequence_lengths(c)
+    n = int(statistics.median(lens))
+    step = CpuBlockStep(c, n)
+    step.layer(0, True)
+    probe = step.layer(1, False)
     world = args.gpus if c["scaling"] == "weak" else 1
+    if len(lens) == 1 and c["L"] * probe <= 3.0:
+        retain_at = lambda i: c["retention"] and (i % c["interval"]) == c["interval"] - 1  # noqa: E731
+        for i in range(args.warmup):
+            for layer in range(c["L"]):
+                step.layer(layer, retain_at(i))
+        t0 = time.perf_counter()
+        for i in range(args.steps):
+            for layer in range(c["L"]):
+                step.layer(layer, retain_at(i))
+        t_block = (time.perf_counter() - t0) / args.steps
+        steps, warmup = args.steps, args.warmup
+        sample = (f"{args.steps} whole block-steps after {args.warmup} untimed (one sequence, n={n}, {c['L']} layers: "
+                  f"step 0 + {c['substeps'] - 1} sparse sub-steps each, the retention scoring in every "
+                  f"{c['interval']}th)" + ("; k4v4 dequantization included" if step.packed else ""))
+    else:
+        base = cpu_baseline(c, budget_s=30.0, threads=threads)
+        t_block, steps, warmup, sample = base["seconds"], max(1, base["whole_steps"]), 1, base["sample"]
     tok_s = tokens_per_step(c) * world / t_block
     line = {"impl": "reference", "metric": METRIC, "value": tok_s, "unit": "tokens/s", "n_gpus": args.gpus,
-            "steps": args.steps, "warmup": args.warmup, "ms_per_step": t_block * 1e3,
-            "us_per_block_step": t_block * 1e6, "higher_is_better": True, "scaling": c["scaling"],
-            "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "steps": steps, "warmup": warmup, "ms_per_step": t_block * 1e3, "us_per_block_step": t_block * 1e6,
+            "higher_is_better": True, "scaling": c["scaling"], "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic (seeded N(0,1) K/V/Q)",
             "config": {"workload": c["workload"], "global_batch": c["B"] * world, "seq_len": c["n"],
-                       "parallelism": "cpu"},
+                       "parallelism": "cpu (host cores of rank 0)"},
             "cpu_baseline": {"value": tok_s, "unit": "tokens/s", "cores": threads, "kind": "port",
-                             "sample": sample},
+                             "cpu_model": cpu_model(), "sample": sample},
             "e2e": {"value": tok_s, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
 
@@ -549,160 +601,150 @@ def _max_over_ranks(x: float, world: int, dev) -> float:
     return float(t.item())
 
 
-def run_ours(args):
+def _capture(fn, side, stream):
+    """A CUDA graph of fn() captured on the side stream (kernel nodes kept for counting)."""
     import torch
-    import torch.distributed as dist
 
-    import maskahead_b200
-    from maskahead_b200.hotpath import unpacked_prefix
-    from maskahead_b200.kernels import splitk_attention
-
-    world = int(os.environ.get("WORLD_SIZE", "1"))
-    rank = int(os.environ.get("RANK", "0"))
-    local = int(os.environ.get("LOCAL_RANK", "0"))
-    torch.cuda.set_device(local)
-    dev = torch.device("cuda", local)
-    if world > 1:
-        import datetime
-        dist.init_process_group("nccl", device_id=dev, timeout=datetime.timedelta(seconds=120))
-    maskahead_b200.load_library()
-    c = dict(CONFIGS[args.config])
-    if args.layers > 0:
-        c["L"] = args.layers
-    share = rank_share(c, rank, world)
-    seed = c["seed"] + (rank if c["scaling"] == "weak" else 0) * 1000 + share["head0"]
-    wl = Workload(c, dev, seed, share, world)
-    stream = torch.cuda.current_stream(dev)
-    retain_at = lambda i: c["retention"] and (i % c["interval"]) == c["interval"] - 1  # noqa: E731
-
-    # eager warm-up (sizes the workspaces), then one CUDA graph per step kind
-    for i in range(max(1, args.warmup)):
-        wl.block_step(retain=retain_at(i))
-    torch.cuda.synchronize()
-    graphs, graph_outputs, graph_launches = {}, {}, {}
-    side = torch.cuda.Stream(dev)
-    timing = "CUDA-graph replay, CUDA events"
-    try:
-        if args.eager:
-            raise RuntimeError("eager steps requested")
-        side.wait_stream(stream)
-        with torch.cuda.stream(side):
-            for retain in sorted({retain_at(i) for i in range(c["interval"])}):
-                g = torch.cuda.CUDAGraph(keep_graph=True)
-                with torch.cuda.graph(g, stream=side):
-                    graph_outputs[retain] = wl.block_step(retain)
-                graph_launches[retain] = graph_kernel_count(g)
-                g.instantiate()
-                graphs[retain] = g
-        stream.wait_stream(side)
-        torch.cuda.synchronize()
-
-        def step(i):
-            graphs[retain_at(i)].replay()
-    except Exception as exc:  # a collective that cannot be captured: eager steps
-        graphs.clear()
-        torch.cuda.synchronize()
-        timing = ("eager steps (--eager), CUDA events" if args.eager else
-                  f"eager steps (graph capture failed: {type(exc).__name__}), CUDA events")
-
-        def step(i):
-            wl.block_step(retain_at(i))
-
-    for i in range(args.warmup):
-        step(i)
-    torch.cuda.synchronize()
-    if world > 1:
-        dist.barrier()
-    torch.cuda.synchronize()
-    with ClockSampler(local) as clocks:
-        ms = _timed(step, args.steps, stream)
-    torch.cuda.synchronize()
-    ms = _max_over_ranks(ms, world, dev)
-    ms_step = ms / args.steps
-    # diagnostic: each kind of step on its own (a block-step without / with the retention pass)
-    step_kinds = {}
-    if graphs:
-        for retain, g in sorted(graphs.items()):
-            t = _timed(lambda i: g.replay(), 3, stream) / 3
-            step_kinds["retention" if retain else "plain"] = _max_over_ranks(t, world, dev)
-    seqs_job = c["B"] * (world if c["scaling"] == "weak" else 1)
-    tokens = c["T"] * seqs_job
-    value = tokens / (ms_step / 1e3)
-
-    # dominant kernel: the step-0 attention (tensor-core partial pass + combine) per layer
-    hbm_peak, tf_peak, peak_kind = peaks()
-    g0 = torch.cuda.CUDAGraph()
+    g = torch.cuda.CUDAGraph(keep_graph=True)
     side.wait_stream(stream)
-    def step0_attention(layer):
-        # what fast_step0 runs: a packed prefix is unpacked to bf16 first
-        pre = wl.prefix(layer)
-        if pre.nq > 0:
-            pre = unpacked_prefix(pre, wl.B, wl.H, c["D"])
-        splitk_attention(wl.Q[layer, 0], pre, wl.KC[layer, 0], wl.VC[layer, 0], scaling=wl.scale, want_prefix=True)
-
     with torch.cuda.stream(side):
-        for layer in range(c["L"]):   # warm the workspaces outside the capture
-            step0_attention(layer)
-        with torch.cuda.graph(g0, stream=side):
-            for layer in range(c["L"]):
-                step0_attention(layer)
+        with torch.cuda.graph(g, stream=side):
+            out = fn()
     stream.wait_stream(side)
-    for _ in range(3):
-        g0.replay()
-    torch.cuda.synchronize()
-    reps = max(3, args.steps // 2)
-    ms_attn = _timed(lambda i: g0.replay(), reps, stream) / (reps * c["L"])
-    ms_attn = _max_over_ranks(ms_attn, world, dev)
+    count = graph_kernel_count(g)
+    g.instantiate()
+    return g, out, count
+
+
+def kernel_rooflines(c: dict, wl, share: dict, dev, stream, side, reps: int, world: int) -> dict:
+    """Each kernel family of the block-step on its own: a CUDA graph of one call per layer,
+    replayed `reps` times with L2 flushed before every replay (the events bracket the replay
+    only); per launch: time, algorithmic bytes, GB/s and tensor FLOP/s against the measured
+    peaks."""
+    import torch
+
+    from maskahead_b200.hotpath import compact_attention, gather_read_set, unpacked_prefix
+    from maskahead_b200.kernels import prefix_scores, select_topk_indices, splitk_attention
+
+    hbm, tf_burst, tf_sust, kind = peaks_all()
+    L, D, T, k = c["L"], c["D"], c["T"], c["k"]
     ab = algorithmic_bytes(c, share)
-    achieved = ab["step0_layer"] / (ms_attn / 1e3) / 1e9
-    tflops = step0_flops(c, share) / (ms_attn / 1e3) / 1e12
+    B, H, Hq = len(share["lens"]), share["H"], share["Hq"]
+    n_sum = sum(share["lens"])
+    packed = c["kv"] != "bf16"
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
 
-    # end to end through the public API with host buffers
-    e2e = None
-    if not args.no_e2e:
-        hq = wl.Q.cpu().pin_memory()
-        hkc, hvc = wl.KC.cpu().pin_memory(), wl.VC.cpu().pin_memory()
-        hp = [t.cpu().pin_memory() for t in (wl.QP, wl.KCP, wl.VCP)] if c["retention"] else []
-        outs_h = torch.empty((c["L"], wl.B, c["Hq"], c["T"], c["D"]), dtype=wl.Q.dtype).pin_memory()
-        idx_h = torch.empty((c["L"], wl.B, wl.H, c["k"]), dtype=torch.int64).pin_memory()
-        h2d_every = sum(t.numel() * t.element_size() for t in (hq, hkc, hvc))
-        h2d_retain = sum(t.numel() * t.element_size() for t in hp)
-        d2h = outs_h.numel() * outs_h.element_size() + idx_h.numel() * 8
+    def pre(layer):
+        p = wl.prefix(layer)
+        return unpacked_prefix(p, B, H, D) if p.nq > 0 else p
 
-        # Pipelined across steps when the block-step is a captured graph without a data-path
-        # collective: two sets of device inputs (the second captured into its own graphs), the
-        # copy stream moves step i+1's inputs in and step i's results out while step i
-        # computes. Every step still copies its own inputs in and its results out inside
-        # the timed region; the first step's copy-in is not overlapped.
-        pipelined = bool(graphs) and (world == 1 or c.get("shard") != "heads")
-        names = ("Q", "KC", "VC") + (("QP", "KCP", "VCP") if c["retention"] else ())
-        sets, set_graphs, set_outputs = [], [], []
-        if pipelined:
-            sets.append({nm: getattr(wl, nm) for nm in names})
-            set_graphs.append(graphs)
-            set_outputs.append(graph_outputs)
-            second = {nm: getattr(wl, nm).clone() for nm in names}
-            for nm in names:
-                setattr(wl, nm, second[nm])
-            g2, o2 = {}, {}
-            side.wait_stream(stream)
-            with torch.cuda.stream(side):
-                for retain in sorted(graphs):
-                    g = torch.cuda.CUDAGraph()
-                    with torch.cuda.graph(g, stream=side):
-                        o2[retain] = wl.block_step(retain)
-                    g2[retain] = g
-            stream.wait_stream(side)
-            torch.cuda.synchronize()
-            for nm in names:
-                setattr(wl, nm, sets[0][nm])
-            sets.append(second)
-            set_graphs.append(g2)
-            set_outputs.append(o2)
-        host = {"Q": hq, "KC": hkc, "VC": hvc}
-        if c["retention"]:
-            host.update(zip(("QP", "KCP", "VCP"), hp))
-        copy_stream = torch.cuda.Stream(dev)
+    # eager inputs of the later families (outside the graphs)
+    stats, scores, idxs = [], [], []
+    for layer in range(L):
+        _, st = splitk_attention(wl.Q[layer, 0], pre(layer), wl.KC[layer, 0], wl.VC[layer, 0], scaling=wl.scale,
+                                 want_prefix=True)
+        stats.append(st)
+        _, sc = prefix_scores(wl.Q[layer, 0], pre(layer), st, wl.rows, value=True, scaling=wl.scale)
+        scores.append(sc)
+        idx, _ = select_topk_indices(sc, min(k, min(share["lens"])), want_values=False,
+                                     lens=getattr(wl, "lens_t", None))
+        idxs.append(idx)
+    compacts = [gather_read_set(pre(layer), idxs[layer], out=wl.compact_buffers(layer)) for layer in range(L)]
+    torch.cuda.synchronize(dev)
+
+    b_tok = token_bytes(c)
+    q_bytes = B * Hq * T * D * 2
+    families = {
+        "step0_attention": (lambda layer: splitk_attention(wl.Q[layer, 0], pre(layer), wl.KC[layer, 0],
+                                                           wl.VC[layer, 0], scaling=wl.scale, want_prefix=True),
+                            ab["step0_layer"], 4.0 * Hq * T * n_sum * D,
+                            "attn_partial_fa (split-K, merge in the launch)" + (" after the unpack of the packed prefix"
+                                                                               if packed else "")),
+        "mass_value_score": (lambda layer: prefix_scores(wl.Q[layer, 0], pre(layer), stats[layer], wl.rows, value=True,
+                                                         scaling=wl.scale),
+                             n_sum * H * b_tok + q_bytes + 2 * n_sum * H * 4, 2.0 * Hq * T * n_sum * D,
+                             "prefix_mass_fa (mass, centre and value score in one launch)"
+                             + (" over the unpacked prefix" if packed else "")),
+        "select_topk": (lambda layer: select_topk_indices(scores[layer], idxs[layer].shape[2], want_values=False,
+                                                          lens=getattr(wl, "lens_t", None)),
+                        n_sum * H * 4 + B * H * k * 8, 0.0, "select_topk (radix select, ascending emission)"),
+        "gather": (lambda layer: gather_read_set(pre(layer), idxs[layer], out=wl.compact_buffers(layer)),
+                   ab["gather_layer"], 0.0, "gather_kv (read set into the compact cache)"),
+        "substep_attention": (lambda layer: compact_attention(wl.Q[layer, 1], compacts[layer], None, wl.KC[layer, 1],
+                                                              wl.VC[layer, 1], scaling=wl.scale),
+                              ab["substep_layer"], 4.0 * Hq * T * (B * k + B * T) * D,
+                              "attn_partial_fa over the compact cache (merge in the launch)"),
+    }
+    out = {}
+    for name, (fn, nbytes, flops, what) in families.items():
+        for layer in range(L):          # workspaces at their final size before the capture
+            fn(layer)
+        g, _, _ = _capture(lambda: [fn(layer) for layer in range(L)], side, stream)
+        for _ in range(2):
+            g.replay()
+        total = 0.0
+        for _ in range(reps):
+            flush.fill_(1)
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            g.replay()
+            e1.record(stream)
+            e1.synchronize()
+            total += e0.elapsed_time(e1)
+        us = _max_over_ranks(total / (reps * L), world, dev) * 1e3
+        gbs = nbytes / (us * 1e-6) / 1e9
+        row = {"kernel": what, "us_per_launch": us, "bytes_per_launch": int(nbytes), "achieved_gbs": gbs,
+               "hbm_frac": gbs / hbm}
+        if flops:
+            tfl = flops / (us * 1e-6) / 1e12
+            row.update(tflops=tfl, tensor_frac_burst=tfl / tf_burst, tensor_frac_sustained=tfl / tf_sust)
+        out[name] = row
+        del g
+    out["peaks"] = {"hbm_gbs": hbm, "bf16_tflops_burst": tf_burst, "bf16_tflops_sustained": tf_sust, "kind": kind}
+    del flush
+    return out
+
+
+def peaks_all():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return (float(d["hbm_gbs"]), float(d["bf16_tflops"]), float(d.get("bf16_tflops_sustained", d["bf16_tflops"])),
+                "measured")
+    return 6650.0, 1590.0, 1400.0, "fallback"
+
+
+def e2e_leg(c: dict, wl, graphs: dict, graph_outputs: dict, retain_at, args, world: int, dev, stream, side) -> dict:
+    """The block-step end to end through the public API with host buffers: every step
+    copies its queries and block K/V in from pinned host memory and every layer's output
+    and read set out. With captured graphs and no data-path collective the copies of step
+    i+1 (in) and i (out) overlap step i's compute on a copy stream (two device input sets,
+    each with its own graphs); otherwise the steps run serially."""
+    import torch
+
+    L = c["L"]
+    names = ("Q", "KC", "VC") + (("QP", "KCP", "VCP") if c["retention"] else ())
+    host = {nm: getattr(wl, nm).cpu().pin_memory() for nm in names}
+    outs_h = torch.empty((L, wl.B, c["Hq"], c["T"], c["D"]), dtype=wl.Q.dtype).pin_memory()
+    idx_h = torch.empty((L, wl.B, wl.H, c["k"]), dtype=torch.int64).pin_memory()
+    h2d_every = sum(host[nm].numel() * host[nm].element_size() for nm in ("Q", "KC", "VC"))
+    h2d_retain = sum(host[nm].numel() * host[nm].element_size() for nm in names[3:])
+    d2h = outs_h.numel() * outs_h.element_size() + idx_h.numel() * 8
+    pipelined = bool(graphs) and (world == 1 or c.get("shard") != "heads")
+    copy_stream = torch.cuda.Stream(dev)
+    if pipelined:
+        sets = [{nm: getattr(wl, nm) for nm in names}]
+        second = {nm: getattr(wl, nm).clone() for nm in names}
+        for nm in names:
+            setattr(wl, nm, second[nm])
+        g2, o2 = {}, {}
+        for retain in sorted(graphs):
+            g2[retain], o2[retain], _ = _capture(lambda: wl.block_step(retain), side, stream)
+        torch.cuda.synchronize(dev)
+        for nm in names:
+            setattr(wl, nm, sets[0][nm])
+        sets.append(second)
+        set_graphs, set_outputs = [graphs, g2], [graph_outputs, o2]
         ev_in = [torch.cuda.Event(), torch.cuda.Event()]
         ev_done = [torch.cuda.Event(), torch.cuda.Event()]
         ev_out = [torch.cuda.Event(), torch.cuda.Event()]
@@ -726,119 +768,226 @@ def run_ours(args):
             outs, idxs, _ = set_outputs[b][retain]
             with torch.cuda.stream(copy_stream):
                 copy_stream.wait_event(ev_done[b])
-                for layer in range(c["L"]):
+                for layer in range(L):
                     outs_h[layer].copy_(outs[layer], non_blocking=True)
                     idx_h[layer].copy_(idxs[layer], non_blocking=True)
                 ev_out[b].record(copy_stream)
 
-        def run_pipelined(steps):
-            copy_stream.wait_stream(stream)   # after the timing start
+        def run(steps):
+            copy_stream.wait_stream(stream)               # after the timing start
             copy_in(0)
             for i in range(steps):
                 if i + 1 < steps:
                     copy_in(i + 1)
                 compute_and_copy_out(i)
             stream.wait_stream(copy_stream)
+    else:
+        def run(steps):
+            for i in range(steps):
+                retain = retain_at(i)
+                for nm in ("Q", "KC", "VC") + (("QP", "KCP", "VCP") if retain else ()):
+                    getattr(wl, nm).copy_(host[nm], non_blocking=True)
+                if graphs:
+                    graphs[retain].replay()
+                    outs, idxs, _ = graph_outputs[retain]
+                else:
+                    outs, idxs, _ = wl.block_step(retain)
+                for layer in range(L):
+                    outs_h[layer].copy_(outs[layer], non_blocking=True)
+                    idx_h[layer].copy_(idxs[layer], non_blocking=True)
 
-        # the outputs of the captured step live in the graph's static buffers (wl.outputs
-        # holds them after the capture); eager steps produce fresh ones
-        def e2e_step(i):
-            retain = retain_at(i)
-            wl.Q.copy_(hq, non_blocking=True)
-            wl.KC.copy_(hkc, non_blocking=True)
-            wl.VC.copy_(hvc, non_blocking=True)
-            if retain:
-                for dst, src in zip((wl.QP, wl.KCP, wl.VCP), hp):
-                    dst.copy_(src, non_blocking=True)
-            if graphs:
-                graphs[retain].replay()
-                outs, idxs, _ = graph_outputs[retain]
-            else:
-                outs, idxs, _ = wl.block_step(retain)
-            for layer in range(c["L"]):
-                outs_h[layer].copy_(outs[layer], non_blocking=True)
-                idx_h[layer].copy_(idxs[layer], non_blocking=True)
+    run(2)
+    torch.cuda.synchronize(dev)
+    if world > 1:
+        import torch.distributed as dist
 
-        if pipelined:
-            run_pipelined(2)
-        else:
-            for i in range(2):
-                e2e_step(i)
-        torch.cuda.synchronize()
-        if world > 1:
-            dist.barrier()
-        if pipelined:
-            ms_e = _max_over_ranks(_timed(lambda i: run_pipelined(args.steps) if i == 0 else None, 1, stream),
-                                   world, dev)
-        else:
-            ms_e = _max_over_ranks(_timed(e2e_step, args.steps, stream), world, dev)
-        e2e = {"value": tokens / (ms_e / args.steps / 1e3), "unit": "tokens/s",
-               "h2d_bytes_per_step": int(h2d_every + (h2d_retain / c["interval"] if c["retention"] else 0)),
-               "d2h_bytes_per_step": int(d2h), "ms_per_step": ms_e / args.steps,
-               "path": ("pinned host -> device copies of the step's queries and block K/V, the block-step "
-                        "through the public API (maskahead_b200.hotpath) " +
-                        ("as a CUDA-graph replay" if graphs else "eagerly") +
-                        ", device -> pinned host copies of every layer's output and read set" +
-                        ("; copies on a second stream overlap the neighbouring steps' compute (two input "
-                         "sets, the first step's copy-in not overlapped)" if pipelined else ""))}
+        dist.barrier()
+    ms = _max_over_ranks(_timed(lambda i: run(args.steps), 1, stream), world, dev)
+    seqs_job = c["B"] * (world if c["scaling"] == "weak" else 1)
+    return {"value": c["T"] * seqs_job / (ms / args.steps / 1e3), "unit": "tokens/s",
+            "h2d_bytes_per_step": int(h2d_every + (h2d_retain / c["interval"] if c["retention"] else 0)),
+            "d2h_bytes_per_step": int(d2h), "ms_per_step": ms / args.steps,
+            "path": ("pinned host -> device copies of the step's queries and block K/V, the block-step through the "
+                     "public API (maskahead_b200.hotpath) " + ("as a CUDA-graph replay" if graphs else "eagerly") +
+                     ", device -> pinned host copies of every layer's output and read set" +
+                     ("; copies on a second stream overlap the neighbouring steps' compute (two input sets, the first "
+                      "step's copy-in not overlapped)" if pipelined else ""))}
+
+
+def measure(c: dict, args, world: int, rank: int, dev, headline: bool) -> dict:
+    """One config on this rank's share: warm-up, graphs, K timed block-steps (max over
+    ranks), the per-kernel rooflines, the e2e leg and (rank 0, one GPU) the CPU baseline."""
+    import torch
+    import torch.distributed as dist
+
+    share = rank_share(c, rank, world)
+    seed = c["seed"] + (rank if c["scaling"] == "weak" else 0) * 1000 + share["head0"]
+    wl = Workload(c, dev, seed, share, world)
+    stream = torch.cuda.current_stream(dev)
+    side = torch.cuda.Stream(dev)
+    retain_at = lambda i: c["retention"] and (i % c["interval"]) == c["interval"] - 1  # noqa: E731
+    kinds = sorted({retain_at(i) for i in range(c["interval"])})
+    # eager warm-up; every kind of step runs before any capture, so the library's grow-only
+    # workspaces reach their final size first and every graph addresses the same buffers
+    for i in range(max(1, args.warmup)):
+        wl.block_step(retain=retain_at(i))
+    for retain in kinds:
+        wl.block_step(retain=retain)
+    torch.cuda.synchronize(dev)
+    graphs, graph_outputs, graph_launches = {}, {}, {}
+    timing = "CUDA-graph replay, CUDA events"
+    try:
+        if args.eager:
+            raise RuntimeError("eager steps requested")
+        for retain in kinds:
+            graphs[retain], graph_outputs[retain], graph_launches[retain] = _capture(
+                lambda: wl.block_step(retain), side, stream)
+        torch.cuda.synchronize(dev)
+
+        def step(i):
+            graphs[retain_at(i)].replay()
+    except Exception as exc:   # a collective that cannot be captured: eager steps
+        graphs.clear()
+        torch.cuda.synchronize(dev)
+        timing = ("eager steps (--eager), CUDA events" if args.eager else
+                  f"eager steps (graph capture failed: {type(exc).__name__}), CUDA events")
+
+        def step(i):
+            wl.block_step(retain_at(i))
+
+    for i in range(args.warmup):
+        step(i)
+    torch.cuda.synchronize(dev)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize(dev)
+    with ClockSampler(int(os.environ.get("LOCAL_RANK", "0"))) as clocks:
+        ms = _timed(step, args.steps, stream)
+    torch.cuda.synchronize(dev)
+    ms = _max_over_ranks(ms, world, dev)
+    ms_step = ms / args.steps
+    step_kinds = {}
+    if graphs:
+        for retain, g in sorted(graphs.items()):
+            t = _timed(lambda i, g=g: g.replay(), 3, stream) / 3
+            step_kinds["retention" if retain else "plain"] = _max_over_ranks(t, world, dev)
+    seqs_job = c["B"] * (world if c["scaling"] == "weak" else 1)
+    value = c["T"] * seqs_job / (ms_step / 1e3)
+
+    rooflines = kernel_rooflines(c, wl, share, dev, stream, side, max(3, min(10, args.steps // 2)), world)
+    e2e = None if args.no_e2e else e2e_leg(c, wl, graphs, graph_outputs, retain_at, args, world, dev, stream, side)
+    from maskahead_b200 import MaError, device_status
+
+    try:
+        device_status(dev)
+        status = "ok (no bounded device wait gave up)"
+    except MaError as exc:   # the numbers above then include timed-out waits: flagged, not hidden
+        status = f"TIMEOUT: {exc}"
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        t_block, threads, sample = cpu_block_step_time(c, max(1, args.cpu_sample_layers))
-        cpu = {"value": tokens_per_step(c) / t_block, "unit": "tokens/s", "cores": threads, "kind": "port",
-               "sample": sample}
-
-    if world > 1:
-        dist.barrier()
-        for g in list(graphs.values()) + [g0]:
-            del g
-        graphs.clear()
-        del g0
-        torch.cuda.synchronize()
-        dist.destroy_process_group()
-    if rank != 0:
-        return
+        base = cpu_baseline(c, budget_s=20.0 if headline else 8.0)
+        cpu = {"value": tokens_per_step(c) / base["seconds"], "unit": "tokens/s", "cores": base["threads"],
+               "kind": "port", "cpu_model": base["cpu_model"], "sample": base["sample"]}
     n_ret = sum(1 for i in range(args.steps) if retain_at(i))
     if graphs and all(graph_launches.get(r) is not None for r in graphs):
-        # counted: the kernel nodes of the captured step graphs that run this library's kernels
         launches = sum(graph_launches[retain_at(i)] for i in range(args.steps))
         launches_source = "kernel nodes of the captured block-step graphs in namespace ma"
     else:
         launches = n_ret * kernel_launches(c, share, True) + (args.steps - n_ret) * kernel_launches(c, share, False)
         launches_source = "per-step formula (kernel_launches)"
-    if c["scaling"] == "weak":   # every rank runs the same share
+    ab = algorithmic_bytes(c, share)
+    if c["scaling"] == "weak":
         job_ab = {key: world * val for key, val in ab.items()}
-    else:                          # the whole job's sequences and heads
+    else:
         job_ab = algorithmic_bytes(c, dict(lens=sequence_lengths(c), H=c["H"], Hq=c["Hq"]))
     step_bytes = job_ab["block_step"] + job_ab["retention"] / c["interval"]
     parallelism = {"heads": f"kvheads{world} (NCCL all-gather of head outputs)" if world > 1 else "single GPU",
                    "seqs": f"seq{world} (no collective)"}[c["shard"]]
-    line = {
-        "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
-        "warmup": args.warmup, "ms_per_step": ms_step, "us_per_block_step": ms_step * 1e3,
-        "higher_is_better": True, "scaling": c["scaling"], "vs_baseline": None, "dtype": "bf16",
-        "data": "synthetic (seeded N(0,1) K/V/Q, random-init; no model weights)",
+    s0 = rooflines["step0_attention"]
+    roofline = {"kernel": "step-0 attention per layer: " + s0["kernel"], "bound": "hbm",
+                "achieved": s0["achieved_gbs"], "peak": rooflines["peaks"]["hbm_gbs"], "unit": "GB/s",
+                "frac": s0["hbm_frac"], "traffic": ATTN_TRAFFIC_BYTES.get(c["name"]) if world == 1 else None,
+                "peak_kind": f"{rooflines['peaks']['kind']} burst",
+                "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum of the step-0 launch "
+                                  "(profiles/attn_partial_fa_cfg2.md, profiles/attn_partial_fa_cfg4_step0.md)",
+                "us_per_launch": s0["us_per_launch"], "bytes_per_launch": s0["bytes_per_launch"],
+                "tensor_tflops": s0.get("tflops"), "tensor_frac": s0.get("tensor_frac_burst"),
+                "tensor_frac_sustained": s0.get("tensor_frac_sustained")}
+    res = {
+        "value": value, "unit": "tokens/s", "ms_per_step": ms_step, "us_per_block_step": ms_step * 1e3,
+        "scaling": c["scaling"], "steps": args.steps, "warmup": args.warmup,
         "config": {"workload": c["workload"] + (f" [layers overridden: {c['L']}]" if args.layers > 0 else ""),
-                   "global_batch": seqs_job, "seq_len": c["n"],
-                   "parallelism": parallelism, "l2": "inputs larger than L2 (the per-step cache exceeds 126 MB)",
-                   "timing": timing},
-        "roofline": {"kernel": ("step-0 attention per layer: attn_partial_fa (merge fused)" if c["kv"] == "bf16" else
-                                "step-0 attention per layer: unpack of the packed prefix + attn_partial_fa"),
-                     "bound": "hbm",
-                     "achieved": achieved, "peak": hbm_peak, "unit": "GB/s", "frac": achieved / hbm_peak,
-                     "traffic": ATTN_TRAFFIC_BYTES.get(c["name"]), "peak_kind": f"{peak_kind} burst",
-                     "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum of attn_partial_fa, "
-                                       "profiles/attn_partial_fa_cfg2.md (cfg2), profiles/attn_partial_fa_cfg4_step0.md "
-                                       "(cfg4)",
-                     "us_per_launch": ms_attn * 1e3, "tensor_tflops": tflops, "tensor_frac": tflops / tf_peak,
-                     "bytes_per_launch": ab["step0_layer"]},
-        "ms_per_step_kind": step_kinds,
-        "algorithmic_bytes_per_step": step_bytes,
-        "achieved_step_gbs": step_bytes / (ms_step / 1e3) / 1e9,
-        "block_steps_per_s": seqs_job / (ms_step / 1e3),
-        "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": launches, "gpu_launches_source": launches_source,
-        "clocks": clocks.summary(),
+                   "global_batch": seqs_job, "seq_len": c["n"], "parallelism": parallelism,
+                   "l2": "inputs larger than L2 (the per-step cache exceeds 126 MB); the per-kernel timings flush "
+                         "L2 (a 256 MB write) before every replay", "timing": timing},
+        "roofline": roofline, "rooflines": rooflines, "ms_per_step_kind": step_kinds,
+        "algorithmic_bytes_per_step": step_bytes, "achieved_step_gbs": step_bytes / (ms_step / 1e3) / 1e9,
+        "block_steps_per_s": seqs_job / (ms_step / 1e3), "cpu_baseline": cpu, "e2e": e2e,
+        "gpu_launches": launches, "gpu_launches_source": launches_source, "clocks": clocks.summary(),
+        "device_status": status,
     }
+    if world > 1:
+        dist.barrier()
+    graphs.clear()
+    graph_outputs.clear()
+    del wl
+    torch.cuda.synchronize(dev)
+    torch.cuda.empty_cache()
+    return res
+
+
+def run_ours(args):
+    import torch
+    import torch.distributed as dist
+
+    import maskahead_b200
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        import datetime
+
+        dist.init_process_group("nccl", device_id=dev, timeout=datetime.timedelta(seconds=120))
+    maskahead_b200.load_library()
+
+    def cfg_of(name):
+        c = dict(CONFIGS[name])
+        if args.layers > 0:
+            c["L"] = args.layers
+        return c
+
+    if args.configs == "auto":
+        args.configs = "cfg3,cfg4,cfg5"
+    head = measure(cfg_of(args.config), args, world, rank, dev, headline=True)
+    extra = {}
+    names = [x for x in (args.configs.split(",") if args.configs else []) if x and x != args.config]
+    for name in names:
+        if name not in CONFIGS:
+            raise SystemExit(f"unknown config {name}")
+        c = cfg_of(name)
+        if c["shard"] == "heads" and c["H"] % world:
+            extra[name] = {"skipped": f"{c['H']} KV heads do not split over {world} ranks"}
+            continue
+        extra[name] = measure(c, args, world, rank, dev, headline=False)
+    if world > 1:
+        dist.barrier()
+        torch.cuda.synchronize()
+        dist.destroy_process_group()
+    if rank != 0:
+        return
+    line = {"metric": METRIC, "value": head["value"], "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": head["ms_per_step"], "us_per_block_step": head["us_per_block_step"],
+            "higher_is_better": True, "scaling": head["scaling"], "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic (seeded N(0,1) K/V/Q, random-init; no model weights)", "config": head["config"]}
+    for key in ("roofline", "rooflines", "ms_per_step_kind", "algorithmic_bytes_per_step", "achieved_step_gbs",
+                "block_steps_per_s", "cpu_baseline", "e2e", "gpu_launches", "gpu_launches_source", "clocks",
+                "device_status"):
+        line[key] = head[key]
+    line["configs"] = extra
     print(json.dumps(line), flush=True)
 
 

@@ -164,6 +164,9 @@ def stream_handle(device: torch.device) -> int:
 
 # ------------------------------------------------------------------------ workspaces
 _WORKSPACES: dict[tuple, torch.Tensor] = {}
+# purposes whose buffers are C-ABI workspaces (an error word at their first 256-byte
+# boundary); the others are plain data scratch (e.g. the unpacked prefix)
+STATUS_WORKSPACES = frozenset({"attention", "value_score"})
 
 
 def device_status(device: torch.device | int | None = None) -> None:
@@ -177,7 +180,7 @@ def device_status(device: torch.device | int | None = None) -> None:
     stream = stream_handle(dev)
     failed = []
     for (kind, index, purpose), buf in list(_WORKSPACES.items()):
-        if kind != "cuda" or index != dev.index:
+        if kind != "cuda" or index != dev.index or purpose not in STATUS_WORKSPACES:
             continue
         rc = lib_.ma_workspace_status(buf.data_ptr(), buf.numel(), stream)
         if rc == MA_ERR_TIMEOUT:
@@ -195,17 +198,28 @@ def set_peer_wait_ns(ns: int) -> int:
     return int(load_library().ma_set_peer_wait_ns(int(ns)))
 
 
+# Buffers a larger one replaced. They stay allocated for the life of the process: a CUDA
+# graph captured before the growth still addresses them (its kernels keep their counters
+# and error word there), and freed memory would be handed to other tensors while such a
+# graph can still replay.
+_RETIRED: list[torch.Tensor] = []
+
+
 def workspace(device: torch.device, purpose: str, nbytes: int) -> torch.Tensor:
     """Grow-only, zero-initialized scratch per (device, purpose).
 
     Like the reference's module-level scratch pools (ops.py:274-317) it is shared by
     every call on the device, so calls that can overlap (several streams or threads)
-    must bring their own workspace.
+    must bring their own workspace. A buffer that grows is replaced, never freed (graphs
+    captured before keep using it); run the largest calls once before capturing a graph
+    so that its kernels and later eager calls share one buffer.
     """
     key = (device.type, device.index, purpose)
     buf = _WORKSPACES.get(key)
     if buf is None or buf.numel() < nbytes:
         size = max(nbytes, 1 << 20)
+        if buf is not None:
+            _RETIRED.append(buf)
         buf = torch.zeros(size + 256, dtype=torch.uint8, device=device)
         _WORKSPACES[key] = buf
     return buf

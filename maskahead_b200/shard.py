@@ -1,0 +1,104 @@
+"""Multi-GPU partitioning of the select + attend hot path: one process per GPU.
+
+Selection, retention and attention are independent per (sequence, KV head): the eviction
+state, the read set and the retained set are per KV head and shared by its query-head
+group (eviction.py:206-212). Two partitionings follow (the reference itself runs only
+independent replicas, one process per GPU: scripts/gpu_queue.sh:1-49):
+
+* by sequences -- a serving batch of independent sequences. Each rank takes a contiguous
+  range of sequences whose total prefix length is within one sequence of 1/world of the
+  job's; no data-path collective.
+* by KV heads -- one long sequence. Each rank holds H/world KV heads with their G query
+  heads each (query head h*G + g belongs to KV head h) and runs the whole path for them;
+  after every layer step the per-rank head outputs [B, Hq/world, T, D] are all-gathered
+  into [B, Hq, T, D] (NCCL over NVLink), the only exchange.
+
+The functions take plain sizes and work with any torch.distributed backend (NCCL on the
+GPU box, gloo in the CPU tests).
+"""
+
+from __future__ import annotations
+
+from dataclasses import dataclass
+
+import torch
+
+__all__ = ["SequenceShard", "HeadShard", "sequence_shard", "head_shard", "HeadGather"]
+
+
+@dataclass(frozen=True)
+class SequenceShard:
+    lo: int          # first sequence of the rank
+    hi: int          # one past its last
+    lens: list       # their prefix lengths
+
+
+@dataclass(frozen=True)
+class HeadShard:
+    h0: int          # first KV head of the rank
+    H: int           # KV heads of the rank
+    hq0: int         # first query head (h0 * G)
+    Hq: int          # query heads of the rank (H * G)
+
+
+def sequence_shard(lens, world: int, rank: int) -> SequenceShard:
+    """Contiguous range of sequences for `rank`: the cut between ranks r-1 and r is the
+    prefix sum of lengths nearest to r/world of the total, so every rank's share is
+    within one sequence of its ideal."""
+    lens = [int(x) for x in lens]
+    if not 0 <= rank < world:
+        raise ValueError(f"rank {rank} outside [0, {world})")
+    total = sum(lens)
+    prefix = [0]
+    for n in lens:
+        prefix.append(prefix[-1] + n)
+    bounds = [0]
+    for r in range(1, world):
+        goal = total * r / world
+        bounds.append(min(range(bounds[-1], len(lens) + 1), key=lambda j: abs(prefix[j] - goal)))
+    bounds.append(len(lens))
+    lo, hi = bounds[rank], bounds[rank + 1]
+    return SequenceShard(lo, hi, lens[lo:hi])
+
+
+def head_shard(H: int, Hq: int, world: int, rank: int) -> HeadShard:
+    """The KV heads of `rank` (an equal slice; H must divide by world) with their query
+    heads."""
+    if H % world or Hq % H:
+        raise ValueError(f"{H} KV heads ({Hq} query heads) do not split over {world} ranks")
+    h = H // world
+    g = Hq // H
+    return HeadShard(rank * h, h, rank * h * g, h * g)
+
+
+class HeadGather:
+    """All-gather of per-rank head outputs [B, Hq/world, T, D] into [B, Hq, T, D], the
+    heads in global order (rank r holds query heads [r*Hq/world, (r+1)*Hq/world)).
+
+    The receive buffer is allocated once per shape and reused, so a CUDA graph captured
+    around the collective sees fixed addresses. The gathered heads are copied out of it
+    into `out`, or into a new tensor when out is None (never a view of the buffer, which
+    the next call overwrites)."""
+
+    def __init__(self, world: int, group=None):
+        self.world = world
+        self.group = group
+        self._bufs: dict[tuple, torch.Tensor] = {}
+
+    def __call__(self, part: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+        import torch.distributed as dist
+
+        if self.world == 1:
+            return part if out is None else out.copy_(part)
+        b, hq, t, d = part.shape
+        key = (part.device, part.dtype, b, hq, t, d)
+        buf = self._bufs.get(key)
+        if buf is None:
+            buf = torch.empty((self.world, b, hq, t, d), device=part.device, dtype=part.dtype)
+            self._bufs[key] = buf
+        dist.all_gather_into_tensor(buf.view(self.world * b, hq, t, d), part.contiguous(), group=self.group)
+        full = buf.permute(1, 0, 2, 3, 4)
+        if out is None:
+            out = torch.empty((b, self.world * hq, t, d), device=part.device, dtype=part.dtype)
+        out.view(b, self.world, hq, t, d).copy_(full)
+        return out

@@ -1,4 +1,5 @@
-"""Multi-GPU partitioning of the bench workloads, checked on CPU with gloo ranks.
+"""Multi-GPU partitioning (maskahead_b200.shard) of the bench workloads, checked on CPU
+with gloo ranks.
 
 * KV-head sharding (cfg4): every rank gets a disjoint, equal slice of the KV heads with
   their query heads, and the all-gather of the per-rank outputs reassembles the heads in
@@ -18,6 +19,7 @@ import torch.distributed as dist
 import torch.multiprocessing as mp
 
 import bench
+from maskahead_b200.shard import HeadGather, head_shard, sequence_shard
 
 
 def _free_port() -> int:
@@ -37,8 +39,11 @@ def _gather_worker(rank: int, world: int, port: int, result):
         # each query head's block filled with its global head index
         heads = torch.arange(rank * hq, (rank + 1) * hq, dtype=torch.float32)
         out = heads.view(1, hq, 1, 1).expand(1, hq, 4, 8).contiguous()
-        full = bench.gather_heads(out, world)
-        result[rank] = full[0, :, 0, 0].tolist()
+        gather = HeadGather(world)
+        full = gather(out)
+        again = torch.empty_like(full)
+        gather(out * 2, out=again)                   # the receive buffer is reused
+        result[rank] = (full[0, :, 0, 0].tolist(), again[0, :, 0, 0].tolist())
     finally:
         dist.destroy_process_group()
 
@@ -54,7 +59,10 @@ def test_head_shards_gather_in_global_order(world):
     result = mgr.dict()
     mp.spawn(_gather_worker, args=(world, _free_port(), result), nprocs=world, join=True)
     for r in range(world):
-        assert result[r] == [float(h) for h in range(cfg["Hq"])]
+        assert result[r][0] == [float(h) for h in range(cfg["Hq"])]
+        assert result[r][1] == [2.0 * h for h in range(cfg["Hq"])]
+    hs = [head_shard(cfg["H"], cfg["Hq"], world, r) for r in range(world)]
+    assert [h.hq0 for h in hs] == [r * cfg["Hq"] // world for r in range(world)]
 
 
 @pytest.mark.parametrize("world", [1, 2, 4, 8])
@@ -67,3 +75,12 @@ def test_sequence_shards_cover_and_balance(world):
     totals = [sum(p) for p in parts]
     ideal = sum(lens) / world
     assert all(abs(t - ideal) <= max(lens) for t in totals), "every share within one sequence of its ideal"
+    shards = [sequence_shard(lens, world, r) for r in range(world)]
+    assert [s.lo for s in shards[1:]] == [s.hi for s in shards[:-1]] and shards[-1].hi == len(lens)
+
+
+def test_shard_arguments_are_checked():
+    with pytest.raises(ValueError):
+        head_shard(8, 32, 3, 0)
+    with pytest.raises(ValueError):
+        sequence_shard([5, 6], 2, 2)
