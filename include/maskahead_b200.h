@@ -161,6 +161,12 @@ MA_API const char* ma_status_string(int status);
  * general kernels (64-key attention tiles, cp.async-staged mass). Returns the previous
  * setting. Not part of the reference's interface.                                     */
 MA_API int ma_set_attention_kernel(int which);
+/* 1 when the TMA-pipelined attention and scoring kernels read this prefix as it is stored
+ * (dense bf16 without mask or paging; token-mode k4v4 without a dense tail or mask, its
+ * tiles dequantized by producer warps of those kernels), 0 when a caller is better served
+ * by unpacking it to bf16 first (the other kernels still read it in place, slower). Not
+ * part of the reference's interface.                                                  */
+MA_API int ma_kv_read_in_place(const ma_kv* kv, int D);
 
 /* ---- device-side status --------------------------------------------------------------
  * ma_workspace_status: waits for the work queued on `stream` (a stream synchronization),

@@ -22,12 +22,19 @@
 // Per split: (m, l) and o = acc / l as bf16 (ma_common.cuh), stored by TMA, the merge as
 // in ma_attention_tc.cu (fused into a cooperative launch when it is one pass).
 // Every wait is bounded. Semantics follow src/maskahead/kernels/splitk.py:115-190.
+//
+// Packed (token-mode k4v4) prefixes: the PACKED instantiation adds four producer warps
+// that build the K and V tiles from the packed bytes (ma_packed.cuh) instead of TMA loads;
+// the MMA warp hands them a slot by arriving on its kfree / vfree barrier where it would
+// have issued the slot's next TMA load, and they arrive on kfull / vfull (four arrivals)
+// once the slot's rows are stored. The current block stays TMA-fed.
 #include <string.h>
 
 #include <algorithm>
 
 #include "ma_combine.cuh"
 #include "ma_kernels.cuh"
+#include "ma_packed.cuh"
 #include "ma_tcgen05.cuh"
 #include "ma_tma.cuh"
 
@@ -44,6 +51,9 @@ constexpr int kThreads = kWarps * 32;
 constexpr int kRowTile = 128;                      // query rows per CTA (one M tile)
 constexpr int kBN = 128;                           // keys per tile
 constexpr int kD = 128;
+constexpr int kDqWarps = 4;                        // dequantizing producer warps (PACKED)
+constexpr int kThreadsP = kThreads + kDqWarps * 32;
+constexpr int kPrefetchTiles = 4;                  // L2 prefetch distance of the packed rows (tiles)
 constexpr int kKSlots = 3;                         // K tiles in flight (freed once S was read)
 constexpr int kVSlots = 3;                         // V tiles in flight (freed when P.V completes)
 constexpr float kLog2e = 1.4426950408889634f;
@@ -141,7 +151,26 @@ __device__ __forceinline__ void tma_tile(const CUtensorMap* map, int b, int h, i
   tma::load_4d(dst + kKVBlock, map, 64, j0, h, b, bar);
 }
 
-__global__ void __launch_bounds__(kThreads, 1) attn_partial_fa(const __grid_constant__ Args A) {
+// Bounded wait of a producer warp for a slot (lane 0 polls, the warp follows); false when
+// the CTA aborted or the wait gave up.
+__device__ __forceinline__ bool dq_wait(uint64_t* bar, uint32_t parity, volatile int* abort) {
+  bool ok = true;
+  if ((threadIdx.x & 31) == 0) {
+    const uint64_t t0 = global_ns();
+    while (!mbar_test(bar, parity)) {
+      if (*abort || global_ns() - t0 > kWaitNs) {
+        ok = false;
+        *abort = 1;
+        break;
+      }
+      __nanosleep(32);
+    }
+  }
+  return __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
+}
+
+template <bool PACKED>
+__device__ __forceinline__ void attn_fa_body(const Args& A) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sQ = smem;                                   // [2 d blocks][128 rows][128 B]
@@ -149,6 +178,8 @@ __global__ void __launch_bounds__(kThreads, 1) attn_partial_fa(const __grid_cons
   uint8_t* sVs = sKs + kKSlots * kKVBytes;              // V slots
   __shared__ uint32_t s_taddr;
   __shared__ __align__(8) uint64_t kfull[kKSlots], vfull[kVSlots], s_full[2], p_full[2], o_done[2], q_full, mbar_fin;
+  __shared__ __align__(8) uint64_t kfree[PACKED ? kKSlots : 1], vfree[PACKED ? kVSlots : 1];
+  __shared__ __align__(16) float sKch[PACKED ? kD : 1];   // the packed keys' divisor of this (b, h)
   __shared__ int s_abort, s_merge_ok;
 
   // grid (row tiles, splits, heads): the row tiles of one split run side by side, so the
@@ -172,6 +203,8 @@ __global__ void __launch_bounds__(kThreads, 1) attn_partial_fa(const __grid_cons
   const int t_row = row_ok ? r % T : 0;
 
   const bool is_cur = split == A.nsplit;
+  const bool dq = PACKED && !is_cur;   // prefix tiles built by the producer warps
+  const bool merge_warp = warp < kWarps;   // the producer warps take no merge rows
   int begin, end;
   if (is_cur) {
     begin = 0;
@@ -195,10 +228,16 @@ __global__ void __launch_bounds__(kThreads, 1) attn_partial_fa(const __grid_cons
   unsigned gen0 = 0;   // the merge generation, read after pdl_wait, before this CTA arrives (thread 0)
   if (threadIdx.x == kSoftThreads) {
     prefetch_map(&A.qmap);
-    prefetch_map(is_cur ? &A.ckmap : &A.kmap);
-    prefetch_map(is_cur ? &A.cvmap : &A.vmap);
-    for (int i = 0; i < kKSlots; ++i) mbar_init(&kfull[i], 1);
-    for (int i = 0; i < kVSlots; ++i) mbar_init(&vfull[i], 1);
+    if (!dq) {
+      prefetch_map(is_cur ? &A.ckmap : &A.kmap);
+      prefetch_map(is_cur ? &A.cvmap : &A.vmap);
+    }
+    for (int i = 0; i < kKSlots; ++i) mbar_init(&kfull[i], dq ? kDqWarps : 1);
+    for (int i = 0; i < kVSlots; ++i) mbar_init(&vfull[i], dq ? kDqWarps : 1);
+    if (PACKED) {
+      for (int i = 0; i < kKSlots; ++i) mbar_init(&kfree[i], 1);
+      for (int i = 0; i < kVSlots; ++i) mbar_init(&vfree[i], 1);
+    }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&s_full[i], 1);
       mbar_init(&p_full[i], kSoftWarps / 2);
@@ -227,8 +266,10 @@ __global__ void __launch_bounds__(kThreads, 1) attn_partial_fa(const __grid_cons
         tma::load_4d(sQ + kQBlock + i * 32 * 128, &A.qmap, 64, rp % T, h * G + rp / T, b, &q_full);
       }
     }
-    for (int i = 0; i < kKSlots && i < ntiles; ++i) tma_tile(km, b, h, begin + i * kBN, sKs + i * kKVBytes, &kfull[i]);
-    for (int i = 0; i < kVSlots && i < ntiles; ++i) tma_tile(vm, b, h, begin + i * kBN, sVs + i * kKVBytes, &vfull[i]);
+    if (!dq) {
+      for (int i = 0; i < kKSlots && i < ntiles; ++i) tma_tile(km, b, h, begin + i * kBN, sKs + i * kKVBytes, &kfull[i]);
+      for (int i = 0; i < kVSlots && i < ntiles; ++i) tma_tile(vm, b, h, begin + i * kBN, sVs + i * kKVBytes, &vfull[i]);
+    }
   }
   if (warp == 0) tmem_alloc(&s_taddr, kTmemCols);
   fence_before_sync();
@@ -240,7 +281,7 @@ __global__ void __launch_bounds__(kThreads, 1) attn_partial_fa(const __grid_cons
   const uint32_t tO = taddr + lane_base + kColO + 128 * grp;   // this warp's O accumulator
   float m_run = -INFINITY, l_run = 0.f, m_true = -INFINITY;
 
-  if (!softmax_warp) {
+  if (warp == kSoftWarps) {
     // ------------------------------------------------------------ MMA / TMA warp
     if (lane == 0) {
       // Event loop: S(t) needs K(t) loaded and P.V(t-2) seen complete (P(t-2) lives in the
@@ -307,13 +348,15 @@ __global__ void __launch_bounds__(kThreads, 1) attn_partial_fa(const __grid_cons
         }
         // a K slot is free once the S it held was consumed (P.V of that tile issued)
         if (kIss < ntiles && pN > kIss - kKSlots) {
-          tma_tile(km, b, h, begin + kIss * kBN, sKs + (kIss % kKSlots) * kKVBytes, &kfull[kIss % kKSlots]);
+          if (dq) mbar_arrive(&kfree[kIss % kKSlots]);   // the producer warps may refill it
+          else tma_tile(km, b, h, begin + kIss * kBN, sKs + (kIss % kKSlots) * kKVBytes, &kfull[kIss % kKSlots]);
           ++kIss;
           progress = true;
         }
         // a V slot is free once its P.V completed
         if (vIss < ntiles && oD > vIss - kVSlots) {
-          tma_tile(vm, b, h, begin + vIss * kBN, sVs + (vIss % kVSlots) * kKVBytes, &vfull[vIss % kVSlots]);
+          if (dq) mbar_arrive(&vfree[vIss % kVSlots]);
+          else tma_tile(vm, b, h, begin + vIss * kBN, sVs + (vIss % kVSlots) * kKVBytes, &vfull[vIss % kVSlots]);
           ++vIss;
           progress = true;
         }
@@ -338,12 +381,47 @@ __global__ void __launch_bounds__(kThreads, 1) attn_partial_fa(const __grid_cons
       mma_commit(&mbar_fin);
       mbar_wait(&mbar_fin, 0, 20000000ull);
       if (!q_ok) mbar_wait(&q_full, 0, 20000000ull);
-      for (int tt = kObs; tt < kIss; ++tt)
-        mbar_wait(&kfull[tt % kKSlots], (uint32_t)(tt / kKSlots) & 1u, 20000000ull);
-      for (int tt = vObs; tt < vIss; ++tt)
-        mbar_wait(&vfull[tt % kVSlots], (uint32_t)(tt / kVSlots) & 1u, 20000000ull);
+      if (!dq) {   // TMA loads still in flight (the producer warps' stores end with them)
+        for (int tt = kObs; tt < kIss; ++tt)
+          mbar_wait(&kfull[tt % kKSlots], (uint32_t)(tt / kKSlots) & 1u, 20000000ull);
+        for (int tt = vObs; tt < vIss; ++tt)
+          mbar_wait(&vfull[tt % kVSlots], (uint32_t)(tt / kVSlots) & 1u, 20000000ull);
+      }
     }
     __syncwarp();
+  } else if (PACKED && !softmax_warp) {
+    // ------------------------------------------------------------ producer warps (PACKED)
+    // thread dt builds row dt of every K and V tile of the split: tile t's K into slot
+    // t % kKSlots once the MMA warp released it (kfree; the first kKSlots are free), then
+    // its V likewise; the next tile's raw row is loaded before the current one is stored
+    if (dq) {
+      const int dt = threadIdx.x - (kSoftThreads + 32);
+      pdl_wait();   // with a programmatic launch, the cache may come from the kernel before
+      sKch[dt] = A.kv.kchan[(int64_t)b * A.kv.skc[0] + (int64_t)h * A.kv.skc[1] + dt];
+      if (dt == 0)
+        for (int t = 0; t < kPrefetchTiles && t < ntiles; ++t)
+          packed::prefetch_rows(A.kv, b, h, begin + t * kBN, min(end, begin + (t + 1) * kBN));
+      asm volatile("bar.sync 6, %0;\n" ::"r"(kDqWarps * 32) : "memory");
+      packed::RawRow cur, nxt;
+      packed::load_row(A.kv, b, h, begin + dt, end, cur);
+      for (int t = 0; t < ntiles; ++t) {
+        const int tp = t + kPrefetchTiles;
+        if (dt == 0 && tp < ntiles)
+          packed::prefetch_rows(A.kv, b, h, begin + tp * kBN, min(end, begin + (tp + 1) * kBN));
+        if (t + 1 < ntiles) packed::load_row(A.kv, b, h, begin + (t + 1) * kBN + dt, end, nxt);
+        if (t >= kKSlots && !dq_wait(&kfree[t % kKSlots], (uint32_t)((t / kKSlots) - 1) & 1u, &s_abort)) break;
+        packed::store_row<true>(cur.k, cur.ok, sKs + (t % kKSlots) * kKVBytes, dt, sKch);
+        fence_proxy_async();   // generic stores -> the tensor core's reads
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&kfull[t % kKSlots]);
+        if (t >= kVSlots && !dq_wait(&vfree[t % kVSlots], (uint32_t)((t / kVSlots) - 1) & 1u, &s_abort)) break;
+        packed::store_row<false>(cur.v, cur.ok, sVs + (t % kVSlots) * kKVBytes, dt, nullptr);
+        fence_proxy_async();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&vfull[t % kVSlots]);
+        cur = nxt;
+      }
+    }
   } else {
     // ------------------------------------------------------------ softmax warps
     // warp (quarter, grp): rows 32 quarter.. of the tiles t = grp, grp + 2, ..., all 128 keys
@@ -565,7 +643,7 @@ __global__ void __launch_bounds__(kThreads, 1) attn_partial_fa(const __grid_cons
     src.o_base = static_cast<uint32_t>(__cvta_generic_to_shared(sKs));
     src.ml_base = static_cast<uint32_t>(__cvta_generic_to_shared(sVs + 4096));
     src.l16 = lane & 15;
-    for (int rr0 = lo + 2 * warp; rr0 < hi; rr0 += 2 * kWarps) {   // uniform per warp
+    for (int rr0 = lo + 2 * warp; merge_warp && rr0 < hi; rr0 += 2 * kWarps) {   // uniform per warp
       const int rr = rr0 + (lane >> 4);
       src.row = rr < hi ? rr : rr0;
       combine_row16_from<__nv_bfloat16>(A.q, H, A.nsplit, A.cur.Tc > 0, out, A.fm.so[0], A.fm.so[1], A.fm.so[2],
@@ -608,7 +686,7 @@ __global__ void __launch_bounds__(kThreads, 1) attn_partial_fa(const __grid_cons
   const int lo = split * per, hi = min(R_blk, lo + per);
   __nv_bfloat16* out = reinterpret_cast<__nv_bfloat16*>(A.fm.out);
   if (A.nsplit <= 16 && s_merge_ok) {
-    for (int rr0 = lo + 2 * warp; rr0 < hi; rr0 += 2 * kWarps) {   // uniform per warp
+    for (int rr0 = lo + 2 * warp; merge_warp && rr0 < hi; rr0 += 2 * kWarps) {   // uniform per warp
       const int rr = rr0 + (lane >> 4);
       combine_row16<__nv_bfloat16>(A.q, H, A.P, A.nsplit, A.cur.Tc > 0, out, A.fm.so[0], A.fm.so[1], A.fm.so[2],
                                    A.fm.m_p, A.fm.l_p, A.fm.o_p, bh, r0 + rr, rr < hi);
@@ -616,7 +694,7 @@ __global__ void __launch_bounds__(kThreads, 1) attn_partial_fa(const __grid_cons
     return;
   }
   float* sW = reinterpret_cast<float*>(sKs) + warp * kCombineMaxSplits;
-  for (int rr = lo + warp; rr < hi; rr += kWarps) {
+  for (int rr = lo + warp; merge_warp && rr < hi; rr += kWarps) {
     if (s_merge_ok) {
       combine_row<__nv_bfloat16, __nv_bfloat16>(A.q, H, A.P, A.nsplit, A.cur.Tc > 0, out, A.fm.so[0], A.fm.so[1],
                                                 A.fm.so[2], A.fm.m_p, A.fm.l_p, A.fm.o_p, bh, r0 + rr, sW);
@@ -628,6 +706,13 @@ __global__ void __launch_bounds__(kThreads, 1) attn_partial_fa(const __grid_cons
     }
   }
 }
+
+// The bf16 kernel (288 threads) and the PACKED one (416 threads: 13 warps x 32 x 152
+// registers <= 65536; the register cap is set directly because launch bounds would round
+// the block up to 512 threads and allow only 128).
+__global__ void __launch_bounds__(kThreads, 1) attn_partial_fa(const __grid_constant__ Args A) { attn_fa_body<false>(A); }
+__global__ void __maxnreg__(152) attn_partial_fa_packed(const __grid_constant__ Args A) { attn_fa_body<true>(A); }
+
 
 bool tma_map_rows(CUtensorMap* map, const void* base, int B, int H, int n, const int64_t s[3]) {
   // bf16 [B][H][n][128] with element strides s (b, h, row); box: 64 channels x 128 rows
@@ -643,8 +728,10 @@ int fa_key_tile() { return kBN; }
 int fa_row_tile() { return kRowTile; }
 
 bool fa_eligible(const ma_rows& q, const ma_kv& kv, const int64_t* idx, const ma_block& cur, int n_keys) {
-  const bool prefix_ok = n_keys == 0 || (kv.layout == MA_KV_DENSE && kv.dtype == MA_BF16 && !idx && !kv.mask &&
-                                         !kv.pages);
+  const bool dense_ok = kv.layout == MA_KV_DENSE && kv.dtype == MA_BF16 && !kv.mask && !kv.pages;
+  // a token-mode packed prefix: the PACKED instantiation's producer warps read it in place
+  const bool packed_ok = kv.dtype == MA_BF16 && packed::eligible(kv) && n_keys == kv.nq;
+  const bool prefix_ok = n_keys == 0 || (!idx && (dense_ok || packed_ok));
   // a row tile is 128 / T whole query heads, 128 positions of one head, or four 32-row
   // pieces (each within one head)
   const bool rows_ok = q.T > 0 && (kRowTile % q.T == 0 || q.T % 32 == 0);
@@ -657,6 +744,8 @@ int launch_attn_partial_fa(const ma_rows& q, const ma_kv& kv, int H, const ma_bl
   *fused = false;
   if (!fa_eligible(q, kv, nullptr, cur, n_keys) || !(scale > 0.f) || !P.o_bf16 || split_len % kBN != 0)
     return MA_ERR_UNSUPPORTED;
+  const bool packed = n_keys > 0 && kv.layout == MA_KV_PACKED_TOKEN;
+  const int threads = packed ? kThreadsP : kThreads;
   Args A;
   memset(&A, 0, sizeof(A));
   A.q = q;
@@ -672,8 +761,8 @@ int launch_attn_partial_fa(const ma_rows& q, const ma_kv& kv, int H, const ma_bl
   A.nsplit = nsplit;
   A.P = P;
   A.err = err;
-  if (n_keys > 0 && !(tma_map_rows(&A.kmap, kv.kf, q.B, H, kv.nf, kv.skf) &&
-                      tma_map_rows(&A.vmap, kv.vf, q.B, H, kv.nf, kv.svf)))
+  if (n_keys > 0 && !packed && !(tma_map_rows(&A.kmap, kv.kf, q.B, H, kv.nf, kv.skf) &&
+                                  tma_map_rows(&A.vmap, kv.vf, q.B, H, kv.nf, kv.svf)))
     return MA_ERR_UNSUPPORTED;
   if (cur.Tc > 0 && !(tma_map_rows(&A.ckmap, cur.k, q.B, H, cur.Tc, cur.sk) &&
                       tma_map_rows(&A.cvmap, cur.v, q.B, H, cur.Tc, cur.sv)))
@@ -693,7 +782,7 @@ int launch_attn_partial_fa(const ma_rows& q, const ma_kv& kv, int H, const ma_bl
   A.tma_out = (P.Rp % 32 == 0 && prow_total < (1ull << 31) &&
                make_tma_map_2d(&A.omap, true, P.o, kD, prow_total, kD * 2, 64, 32)) ? 1 : 0;
   dim3 grid((R + kRowTile - 1) / kRowTile, P.S, q.B * H);
-  auto kernel = attn_partial_fa;
+  auto kernel = packed ? attn_partial_fa_packed : attn_partial_fa;
   if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes) != cudaSuccess)
     return MA_ERR_CUDA;
   const int rows_per_split = (std::min(kRowTile, R) + (int)grid.y - 1) / (int)grid.y;
@@ -704,11 +793,12 @@ int launch_attn_partial_fa(const ma_rows& q, const ma_kv& kv, int H, const ma_bl
   // that many free SMs in one GPC, so fewer clusters than SMs / size fit (a second wave
   // of clusters cost more than the merge saves)
   if (fm != nullptr && nsplit <= 16 && (int)grid.y <= 16 && rows_per_split <= 2 * kWarps) {
-    static int cluster_nc[17] = {0};   // per cluster size: resident clusters (-1 not schedulable)
+    static int cluster_nc_of[2][17] = {{0}};   // per kernel and cluster size: resident clusters (-1: none)
+    int* cluster_nc = cluster_nc_of[packed ? 1 : 0];
     const int cs = (int)grid.y;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = grid;
-    cfg.blockDim = dim3(kThreads);
+    cfg.blockDim = dim3(threads);
     cfg.dynamicSmemBytes = kSmemBytes;
     cfg.stream = st;
     cudaLaunchAttribute attr[2];
@@ -747,14 +837,14 @@ int launch_attn_partial_fa(const ma_rows& q, const ma_kv& kv, int H, const ma_bl
     int dev = 0, coop = 0, per_sm = 0;
     if (cudaGetDevice(&dev) == cudaSuccess &&
         cudaDeviceGetAttribute(&coop, cudaDevAttrCooperativeLaunch, dev) == cudaSuccess && coop &&
-        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, kThreads, kSmemBytes) == cudaSuccess &&
+        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, threads, kSmemBytes) == cudaSuccess &&
         (long long)grid.x * grid.y * grid.z <= (long long)per_sm * device_sm_count()) {
       Args Af = A;
       Af.fuse = 1;
       Af.fm = *fm;
       cudaLaunchConfig_t cfg = {};
       cfg.gridDim = grid;
-      cfg.blockDim = dim3(kThreads);
+      cfg.blockDim = dim3(threads);
       cfg.dynamicSmemBytes = kSmemBytes;
       cfg.stream = st;
       cudaLaunchAttribute attr[2];
@@ -773,7 +863,7 @@ int launch_attn_partial_fa(const ma_rows& q, const ma_kv& kv, int H, const ma_bl
       }
     }
   }
-  return launch_pdl(kernel, grid, dim3(kThreads), kSmemBytes, st, A) == cudaSuccess ? MA_OK : MA_ERR_CUDA;
+  return launch_pdl(kernel, grid, dim3(threads), kSmemBytes, st, A) == cudaSuccess ? MA_OK : MA_ERR_CUDA;
 }
 
 }  // namespace ma

@@ -1,6 +1,7 @@
 // C ABI of the select + attend hot path: argument validation, split planning and the
 // launch sequence of every entry point declared in include/maskahead_b200.h.
 #include "ma_kernels.cuh"
+#include "ma_packed.cuh"
 
 namespace ma {
 
@@ -270,6 +271,12 @@ int ma_workspace_status(void* workspace, size_t workspace_bytes, void* stream) {
   if (word == 0) return MA_OK;
   if (cudaMemsetAsync(base, 0, sizeof(int), st) != cudaSuccess) return MA_ERR_CUDA;
   return MA_ERR_TIMEOUT;
+}
+
+int ma_kv_read_in_place(const ma_kv* kv, int D) {
+  if (!kv || check_kv(kv, D) != MA_OK || D != 128) return 0;
+  if (kv->layout == MA_KV_DENSE) return kv->dtype == MA_BF16 && !kv->mask && !kv->pages ? 1 : 0;
+  return kv->dtype == MA_BF16 && packed::eligible(*kv) ? 1 : 0;
 }
 
 int ma_set_attention_kernel(int which) {

@@ -20,9 +20,17 @@
 // streams its V tiles again (newest first: V was loaded with an L2 evict_last policy, so
 // most come from L2) through all four slots, and the sum warps write a_j ||v_j - c||.
 // Every wait is bounded.
+//
+// Packed (token-mode k4v4) prefixes: the PACKED instantiation adds four producer warps
+// that build the K tiles (for S^T) and, with the centre, the V tiles of phase 1 from the
+// packed bytes (ma_packed.cuh); the producer/MMA warp releases their slots on kfree / vfree
+// where it would have issued TMA loads. Phase 2 reads V from its phase-1 slots when they
+// still hold every tile, else the sum warps read the packed V rows themselves and dequantize
+// them exactly as the tiles hold them.
 #include <string.h>
 
 #include "ma_kernels.cuh"
+#include "ma_packed.cuh"
 #include "ma_stage.cuh"
 #include "ma_tcgen05.cuh"
 #include "ma_tma.cuh"
@@ -38,6 +46,9 @@ constexpr int kSumThreads = kSumWarps * 32;
 static_assert(kSumThreads == 256, "one selection row per sum thread");
 constexpr int kCentreWarps = 2;              // sum_j a_j v_j: warp c takes slots 64c..64c+63 of each tile
 constexpr int kThreads = kSumThreads + 32 + kCentreWarps * 32;
+constexpr int kDqWarps = 4;                  // dequantizing producer warps (PACKED)
+constexpr int kThreadsP = kThreads + kDqWarps * 32;
+constexpr int kPrefetchTiles = 4;            // L2 prefetch distance of the packed rows (tiles)
 constexpr int kTile = 128;                   // slots per tile (= M = TMEM lanes)
 constexpr int kD = 128;
 constexpr int kMaxRows = 256;                // selection rows (N of the MMA)
@@ -89,7 +100,26 @@ __device__ __forceinline__ uint32_t chunk_off(int j, int c) {
   return (uint32_t)((c >> 3) * kBlock + j * 128 + (((c & 7) ^ (j & 7)) << 4));
 }
 
-__global__ void __launch_bounds__(kThreads, 1) prefix_mass_fa(const __grid_constant__ Args A) {
+// Bounded wait of a producer warp for a slot (lane 0 polls, the warp follows); false when
+// the CTA aborted or the wait gave up.
+__device__ __forceinline__ bool dq_wait(uint64_t* bar, uint32_t parity, volatile int* abort) {
+  bool ok = true;
+  if ((threadIdx.x & 31) == 0) {
+    const uint64_t t0 = global_ns();
+    while (!mbar_test(bar, parity)) {
+      if (*abort || global_ns() - t0 > kWaitNs) {
+        ok = false;
+        *abort = 1;
+        break;
+      }
+      __nanosleep(32);
+    }
+  }
+  return __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
+}
+
+template <bool PACKED>
+__device__ __forceinline__ void mass_fa_body(const Args& A) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sQ = smem;                      // K-major [2 d blocks][Npad rows][128 B]
@@ -101,8 +131,10 @@ __global__ void __launch_bounds__(kThreads, 1) prefix_mass_fa(const __grid_const
   __shared__ __align__(8) uint64_t kfull[kMaxSlots], vfull[kMaxSlots], s_full[2], s_free[2], v_free[kMaxSlots],
       wfull[kMaxSlots], wfree[kMaxSlots], a_full[2], a_free[2], mbar_fin;
   __shared__ int s_abort, s_wait_ok, sLast;
+  __shared__ __align__(8) uint64_t kfree[PACKED ? kMaxSlots : 1], vfree[PACKED ? kMaxSlots : 1];
+  __shared__ __align__(16) float sKch[PACKED ? kD : 1];   // the packed keys' divisor of this (b, h)
 
-  const int n = A.kv.nf;
+  const int n = PACKED ? A.kv.nq : A.kv.nf;   // the packed layout has no dense slots
   const int bh = blockIdx.y;
   const int H = A.H;
   const int b = bh / H, h = bh - (bh / H) * H;
@@ -133,8 +165,10 @@ __global__ void __launch_bounds__(kThreads, 1) prefix_mass_fa(const __grid_const
   // the head's centre generation before this CTA arrives (the last CTA advances it)
   unsigned gen0 = 0;   // read after pdl_wait (below), before this CTA arrives
   if (threadIdx.x == kSumThreads) {
-    asm volatile("prefetch.tensormap [%0];\n" ::"l"(reinterpret_cast<uint64_t>(&A.kmap)) : "memory");
-    asm volatile("prefetch.tensormap [%0];\n" ::"l"(reinterpret_cast<uint64_t>(&A.vmap)) : "memory");
+    if (!PACKED) {   // the packed instantiation has no tensor maps
+      asm volatile("prefetch.tensormap [%0];\n" ::"l"(reinterpret_cast<uint64_t>(&A.kmap)) : "memory");
+      asm volatile("prefetch.tensormap [%0];\n" ::"l"(reinterpret_cast<uint64_t>(&A.vmap)) : "memory");
+    }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&s_full[i], 1);
       mbar_init(&s_free[i], kSumWarps);
@@ -142,8 +176,12 @@ __global__ void __launch_bounds__(kThreads, 1) prefix_mass_fa(const __grid_const
       mbar_init(&a_free[i], kCentreWarps);
     }
     for (int i = 0; i < kMaxSlots; ++i) {
-      mbar_init(&kfull[i], 1);
-      mbar_init(&vfull[i], 1);
+      mbar_init(&kfull[i], PACKED ? kDqWarps : 1);
+      mbar_init(&vfull[i], PACKED ? kDqWarps : 1);
+      if (PACKED) {
+        mbar_init(&kfree[i], 1);
+        mbar_init(&vfree[i], 1);
+      }
       mbar_init(&v_free[i], kCentreWarps);
       mbar_init(&wfull[i], 1);
       mbar_init(&wfree[i], kSumWarps);
@@ -155,11 +193,13 @@ __global__ void __launch_bounds__(kThreads, 1) prefix_mass_fa(const __grid_const
     // the first K and V tiles start loading now, while the sum warps stage Q
     pdl_wait();   // with a programmatic launch, the cache may come from the kernel before
     const uint64_t pol_k = tma::policy_evict_first(), pol_v = tma::policy_evict_last();
-    for (int i = 0; i < nK && i < kTiles; ++i)
-      tile_load(&A.kmap, b, h, begin + i * kTile, sSlot + i * kTileBytes, &kfull[i], pol_k);
-    if (centre)
-      for (int i = 0; i < nV && i < ntiles; ++i)
-        tile_load(&A.vmap, b, h, begin + i * kTile, sSlot + (nK + i) * kTileBytes, &vfull[i], pol_v);
+    if (!PACKED) {
+      for (int i = 0; i < nK && i < kTiles; ++i)
+        tile_load(&A.kmap, b, h, begin + i * kTile, sSlot + i * kTileBytes, &kfull[i], pol_k);
+      if (centre)
+        for (int i = 0; i < nV && i < ntiles; ++i)
+          tile_load(&A.vmap, b, h, begin + i * kTile, sSlot + (nK + i) * kTileBytes, &vfull[i], pol_v);
+    }
   }
   if (sum_warp && given) {
     pdl_wait();   // a (and with a programmatic launch, the outputs) of the kernel before
@@ -207,8 +247,45 @@ __global__ void __launch_bounds__(kThreads, 1) prefix_mass_fa(const __grid_const
   float2 cacc0 = make_float2(0.f, 0.f), cacc1 = cacc0;
   float asum = 0.f;
   const int cw = warp - kSumWarps - 1;   // 0.. for the centre warps
+  const bool dq_warp = PACKED && cw >= kCentreWarps;   // the producer warps (PACKED)
 
-  if (cw >= 0) {
+  if (dq_warp) {
+    // ------------------------------------------------------------ producer warps (PACKED)
+    // thread dt builds row dt of every K tile (slot t % nK, once released on kfree; the
+    // first nK are free) and, with the centre, of every V tile (slot nK + t % nV)
+    const int dt = threadIdx.x - kThreads;
+    const bool want_k = kTiles > 0, want_v = centre;
+    pdl_wait();   // with a programmatic launch, the cache may come from the kernel before
+    if (want_k) sKch[dt] = A.kv.kchan[(int64_t)b * A.kv.skc[0] + (int64_t)h * A.kv.skc[1] + dt];
+    if (dt == 0)
+      for (int t = 0; t < kPrefetchTiles && t < ntiles; ++t)
+        packed::prefetch_rows(A.kv, b, h, begin + t * kTile, min(end, begin + (t + 1) * kTile));
+    asm volatile("bar.sync 6, %0;\n" ::"r"(kDqWarps * 32) : "memory");
+    if (want_k || want_v) {
+      packed::RawRow cur, nxt;
+      packed::load_row(A.kv, b, h, begin + dt, end, cur, want_k, want_v);
+      for (int t = 0; t < ntiles; ++t) {
+        const int tp = t + kPrefetchTiles;
+        if (dt == 0 && tp < ntiles)
+          packed::prefetch_rows(A.kv, b, h, begin + tp * kTile, min(end, begin + (tp + 1) * kTile));
+        if (t + 1 < ntiles) packed::load_row(A.kv, b, h, begin + (t + 1) * kTile + dt, end, nxt, want_k, want_v);
+        if (want_k) {
+          if (t >= nK && !dq_wait(&kfree[t % nK], (uint32_t)((t / nK) - 1) & 1u, &s_abort)) break;
+          packed::store_row<true>(cur.k, cur.ok, sSlot + (t % nK) * kTileBytes, dt, sKch);
+          fence_proxy_async();   // generic stores -> the tensor core's reads
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&kfull[t % nK]);
+        }
+        if (want_v) {
+          if (t >= nV && !dq_wait(&vfree[t % nV], (uint32_t)((t / nV) - 1) & 1u, &s_abort)) break;
+          packed::store_row<false>(cur.v, cur.ok, sSlot + (nK + t % nV) * kTileBytes, dt, nullptr);
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&vfull[t % nV]);
+        }
+        cur = nxt;
+      }
+    }
+  } else if (cw >= 0) {
     // ------------------------------------------------------------ centre warps
     if (centre) {
       const uint32_t lane_off = (uint32_t)((lane & 1) * 8);   // channels 4l..: half of chunk l/2
@@ -291,14 +368,17 @@ __global__ void __launch_bounds__(kThreads, 1) prefix_mass_fa(const __grid_const
         }
         // K slot of tile kIss - nK is free once its S^T completed
         if (kIss < kTiles && sDone > kIss - nK) {
-          tile_load(&A.kmap, b, h, begin + kIss * kTile, sSlot + (kIss % nK) * kTileBytes, &kfull[kIss % nK], pol_k);
+          if (PACKED) mbar_arrive(&kfree[kIss % nK]);   // the producer warps may refill it
+          else tile_load(&A.kmap, b, h, begin + kIss * kTile, sSlot + (kIss % nK) * kTileBytes, &kfull[kIss % nK],
+                         pol_k);
           ++kIss;
           progress = true;
         }
         // V slot of tile vIss - nV is free once the sum warps released it
         if (vIss < vTiles && vfObs > vIss - nV) {
-          tile_load(&A.vmap, b, h, begin + vIss * kTile, sSlot + (nK + vIss % nV) * kTileBytes, &vfull[vIss % nV],
-                    pol_v);
+          if (PACKED) mbar_arrive(&vfree[vIss % nV]);
+          else tile_load(&A.vmap, b, h, begin + vIss * kTile, sSlot + (nK + vIss % nV) * kTileBytes,
+                         &vfull[vIss % nV], pol_v);
           ++vIss;
           progress = true;
         }
@@ -322,8 +402,10 @@ __global__ void __launch_bounds__(kThreads, 1) prefix_mass_fa(const __grid_const
       // drain (bounded): every MMA, every load still in flight
       mma_commit(&mbar_fin);
       mbar_wait(&mbar_fin, 0, 20000000ull);
-      for (int tt = kObs; tt < kIss; ++tt) mbar_wait(&kfull[tt % nK], (uint32_t)(tt / nK) & 1u, 20000000ull);
-      for (int tt = vObs; tt < vIss; ++tt) mbar_wait(&vfull[tt % nV], (uint32_t)(tt / nV) & 1u, 20000000ull);
+      if (!PACKED) {   // TMA loads still in flight (the producer warps' stores end with them)
+        for (int tt = kObs; tt < kIss; ++tt) mbar_wait(&kfull[tt % nK], (uint32_t)(tt / nK) & 1u, 20000000ull);
+        for (int tt = vObs; tt < vIss; ++tt) mbar_wait(&vfull[tt % nV], (uint32_t)(tt / nV) & 1u, 20000000ull);
+      }
     }
     __syncwarp();
   } else {
@@ -426,7 +508,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefix_mass_fa(const __grid_const
   float* sAsum = sRed + kCentreWarps * kD;                 // [kCentreWarps]
   // per-CTA centre partial (the centre warps' halves summed in order); the last CTA of the head
   // reduces the partials in CTA order and publishes c by advancing the generation
-  if (cw >= 0) {
+  if (cw >= 0 && cw < kCentreWarps) {
     *reinterpret_cast<float4*>(sRed + cw * kD + 4 * lane) = make_float4(cacc0.x, cacc0.y, cacc1.x, cacc1.y);
     if (lane == 0) sAsum[cw] = asum;
   }
@@ -499,7 +581,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefix_mass_fa(const __grid_const
   // every V tile of the CTA still in its phase-1 slot (the V ring never wrapped)
   const bool resident = ntiles <= nV;
   if (!sum_warp) {
-    if (warp == kSumWarps && lane == 0 && ok_c && !resident) {
+    if (!PACKED && warp == kSumWarps && lane == 0 && ok_c && !resident) {
       // the CTA's V tiles again, newest first, through every slot
       const uint64_t pol = tma::policy_evict_first();
       int u = 0;
@@ -532,9 +614,34 @@ __global__ void __launch_bounds__(kThreads, 1) prefix_mass_fa(const __grid_const
         const int j = j0 + slot_lane;
         float aj = 0.f;   // issued before the tile's wait
         if (chalf == 0 && j < end) aj = __ldcg(ms + j);
-        bool ok_t = resident || mbar_wait(&wfull[slot], (uint32_t)(u / nS) & 1u, kWaitNs);
+        const bool direct = PACKED && !resident;   // packed rows read here, not from a slot
+        bool ok_t = resident || direct || mbar_wait(&wfull[slot], (uint32_t)(u / nS) & 1u, kWaitNs);
         float2 s0 = make_float2(0.f, 0.f), s1 = s0;
-        if (ok_t) {
+        if (direct) {
+          // this thread's half row, dequantized as the tiles hold it (bf16), then as below
+          packed::RawRow rr;
+          packed::load_row(A.kv, b, h, j, end, rr, false, true);
+          if (rr.ok) {
+            packed::Raw hv;   // this half's payload words and scale/zero pairs (constant indices below)
+            hv.p[0] = chalf ? rr.v.p[2] : rr.v.p[0];
+            hv.p[1] = chalf ? rr.v.p[3] : rr.v.p[1];
+            hv.s = make_uint2(chalf ? rr.v.s.y : rr.v.s.x, 0u);
+            hv.z = make_uint2(chalf ? rr.v.z.y : rr.v.z.x, 0u);
+#pragma unroll
+            for (int c = 0; c < 8; ++c) {
+              float f[8];
+              bf16x8_to_float(packed::chunk<false>(hv, c, nullptr), f);
+              const float4 c0 = *reinterpret_cast<const float4*>(cb + 8 * c);
+              const float4 c1 = *reinterpret_cast<const float4*>(cb + 8 * c + 4);
+              const float2 x0 = make_float2(f[0] - c0.x, f[1] - c0.y), x1 = make_float2(f[2] - c0.z, f[3] - c0.w);
+              const float2 x2 = make_float2(f[4] - c1.x, f[5] - c1.y), x3 = make_float2(f[6] - c1.z, f[7] - c1.w);
+              s0 = ffma2(x0, x0, s0);
+              s1 = ffma2(x1, x1, s1);
+              s0 = ffma2(x2, x2, s0);
+              s1 = ffma2(x3, x3, s1);
+            }
+          }
+        } else if (ok_t) {
           const uint8_t* sV = sSlot + slot * kTileBytes;
 #pragma unroll
           for (int c = 0; c < 8; ++c) {
@@ -558,11 +665,18 @@ __global__ void __launch_bounds__(kThreads, 1) prefix_mass_fa(const __grid_const
           const float tot = s2 + sPart[(u & 1) * kTile + slot_lane];
           sc[j] = !ok_t ? NAN : (kv_live(A.kv, H, b, h, j) ? aj * sqrtf(tot) : 0.f);
         }
-        if (lane == 0 && !resident) mbar_arrive(&wfree[slot]);
+        if (lane == 0 && !resident && !PACKED) mbar_arrive(&wfree[slot]);
       }
     }
   }
 }
+
+// The bf16 kernel (352 threads) and the PACKED one (480 threads: 15 warps x 32 x 136
+// registers <= 65536; the register cap is set directly because launch bounds would round
+// the block up to 512 threads and allow only 128).
+__global__ void __launch_bounds__(kThreads, 1) prefix_mass_fa(const __grid_constant__ Args A) { mass_fa_body<false>(A); }
+__global__ void __maxnreg__(136) prefix_mass_fa_packed(const __grid_constant__ Args A) { mass_fa_body<true>(A); }
+
 
 bool tma_map_rows(CUtensorMap* map, const void* base, int B, int H, int n, const int64_t s[3]) {
   // bf16 [B][H][n][128] with element strides s (b, h, row); box: 64 channels x 128 rows
@@ -578,15 +692,21 @@ int launch_prefix_mass_fa(const ma_rows& q, const ma_kv& kv, int H, const int32_
                           const float* l_p, float scale, float* mass, int64_t sm0, int64_t sm1, float* score,
                           int64_t ss0, int64_t ss1, const ValueWs& w, bool want_centre, bool* fused, cudaStream_t st) {
   *fused = false;
-  const int n = kv.nf;
+  // a dense bf16 cache read by TMA, or a token-mode packed one built by the producer warps
+  const bool packed = kv.layout == MA_KV_PACKED_TOKEN;
+  const int n = packed ? kv.nq : kv.nf;
   const int BH = q.B * H;
   const int G = q.Hq / H;
-  if (!(kv.layout == MA_KV_DENSE && kv.dtype == MA_BF16 && !kv.pages && kv.nq == 0 && q.dtype == MA_BF16 &&
-        q.D == kD && G * T2 <= kMaxRows && n > 0))
+  const bool dense_ok = kv.layout == MA_KV_DENSE && kv.dtype == MA_BF16 && !kv.pages && kv.nq == 0;
+  const bool packed_ok = packed && kv.dtype == MA_BF16 && packed::eligible(kv);
+  if (!((dense_ok || packed_ok) && q.dtype == MA_BF16 && q.D == kD && G * T2 <= kMaxRows && n > 0))
     return MA_ERR_UNSUPPORTED;
+  auto kernel = packed ? prefix_mass_fa_packed : prefix_mass_fa;
+  const int threads = packed ? kThreadsP : kThreads;
   Args A;
   memset(&A, 0, sizeof(A));
-  if (!tma_map_rows(&A.kmap, kv.kf, q.B, H, n, kv.skf) || !tma_map_rows(&A.vmap, kv.vf, q.B, H, n, kv.svf))
+  if (!packed &&
+      (!tma_map_rows(&A.kmap, kv.kf, q.B, H, n, kv.skf) || !tma_map_rows(&A.vmap, kv.vf, q.B, H, n, kv.svf)))
     return MA_ERR_UNSUPPORTED;
   A.q = q;
   A.kv = kv;
@@ -631,27 +751,27 @@ int launch_prefix_mass_fa(const ma_rows& q, const ma_kv& kv, int H, const int32_
   spc = ((spc + kTile - 1) / kTile) * kTile;
   A.slots_per_cta = spc;
   dim3 grid((n + spc - 1) / spc, BH);
-  if (cudaFuncSetAttribute(prefix_mass_fa, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
+  if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
     return MA_ERR_CUDA;
   if (score != nullptr && want_centre && grid.x == 1) {
     // one CTA per head: it reduces its own centre, so the score needs no other CTA
     Args As = A;
     As.score = score;
     *fused = true;
-    return launch_pdl(prefix_mass_fa, grid, dim3(kThreads), smem, st, As) == cudaSuccess ? MA_OK : MA_ERR_CUDA;
+    return launch_pdl(kernel, grid, dim3(threads), smem, st, As) == cudaSuccess ? MA_OK : MA_ERR_CUDA;
   }
   if (score != nullptr && want_centre) {
     // the fused score needs every CTA resident at once: a cooperative launch that fits
     int dev = 0, coop = 0, per_sm = 0;
     if (cudaGetDevice(&dev) == cudaSuccess &&
         cudaDeviceGetAttribute(&coop, cudaDevAttrCooperativeLaunch, dev) == cudaSuccess && coop &&
-        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, prefix_mass_fa, kThreads, smem) == cudaSuccess &&
+        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, threads, smem) == cudaSuccess &&
         (long long)grid.x * grid.y <= (long long)per_sm * sms) {
       Args Ac = A;
       Ac.score = score;
       cudaLaunchConfig_t cfg = {};
       cfg.gridDim = grid;
-      cfg.blockDim = dim3(kThreads);
+      cfg.blockDim = dim3(threads);
       cfg.dynamicSmemBytes = smem;
       cfg.stream = st;
       cudaLaunchAttribute attr[2];
@@ -662,7 +782,7 @@ int launch_prefix_mass_fa(const ma_rows& q, const ma_kv& kv, int H, const int32_
       cfg.attrs = attr;
       for (int na = 2; na >= 1; --na) {
         cfg.numAttrs = na;
-        if (cudaLaunchKernelEx(&cfg, prefix_mass_fa, Ac) == cudaSuccess) {
+        if (cudaLaunchKernelEx(&cfg, kernel, Ac) == cudaSuccess) {
           *fused = true;
           return MA_OK;
         }
@@ -670,18 +790,22 @@ int launch_prefix_mass_fa(const ma_rows& q, const ma_kv& kv, int H, const int32_
       }
     }
   }
-  return launch_pdl(prefix_mass_fa, grid, dim3(kThreads), smem, st, A) == cudaSuccess ? MA_OK : MA_ERR_CUDA;
+  return launch_pdl(kernel, grid, dim3(threads), smem, st, A) == cudaSuccess ? MA_OK : MA_ERR_CUDA;
 }
 
 int launch_value_score_fa(const ma_kv& kv, int B, int H, int D, const float* a, int64_t sa0, int64_t sa1,
                           float* score, int64_t ss0, int64_t ss1, void* ws, cudaStream_t st) {
-  const int n = kv.nf;
+  const bool packed = kv.layout == MA_KV_PACKED_TOKEN;
+  const int n = packed ? kv.nq : kv.nf;
   const int BH = B * H;
-  if (!(kv.layout == MA_KV_DENSE && kv.dtype == MA_BF16 && !kv.pages && kv.nq == 0 && D == kD && n > 0))
-    return MA_ERR_UNSUPPORTED;
+  const bool dense_ok = kv.layout == MA_KV_DENSE && kv.dtype == MA_BF16 && !kv.pages && kv.nq == 0;
+  const bool packed_ok = packed && kv.dtype == MA_BF16 && packed::eligible(kv);
+  if (!((dense_ok || packed_ok) && D == kD && n > 0)) return MA_ERR_UNSUPPORTED;
+  auto kernel = packed ? prefix_mass_fa_packed : prefix_mass_fa;
+  const int threads = packed ? kThreadsP : kThreads;
   Args A;
   memset(&A, 0, sizeof(A));
-  if (!tma_map_rows(&A.vmap, kv.vf, B, H, n, kv.svf)) return MA_ERR_UNSUPPORTED;
+  if (!packed && !tma_map_rows(&A.vmap, kv.vf, B, H, n, kv.svf)) return MA_ERR_UNSUPPORTED;
   const ValueWs w = carve_value_ws(ws, BH, D);
   A.kv = kv;
   A.q.B = B;
@@ -718,18 +842,18 @@ int launch_value_score_fa(const ma_kv& kv, int B, int H, int D, const float* a, 
   spc = ((spc + kTile - 1) / kTile) * kTile;
   A.slots_per_cta = spc;
   dim3 grid((n + spc - 1) / spc, BH);
-  if (cudaFuncSetAttribute(prefix_mass_fa, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
+  if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
     return MA_ERR_CUDA;
   A.score = score;
   if (grid.x == 1)   // one CTA per head: it reduces its own centre
-    return launch_pdl(prefix_mass_fa, grid, dim3(kThreads), smem, st, A) == cudaSuccess ? MA_OK : MA_ERR_CUDA;
+    return launch_pdl(kernel, grid, dim3(threads), smem, st, A) == cudaSuccess ? MA_OK : MA_ERR_CUDA;
   int dev = 0, coop = 0, per_sm = 0;
   if (cudaGetDevice(&dev) == cudaSuccess && cudaDeviceGetAttribute(&coop, cudaDevAttrCooperativeLaunch, dev) == cudaSuccess &&
-      coop && cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, prefix_mass_fa, kThreads, smem) == cudaSuccess &&
+      coop && cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, threads, smem) == cudaSuccess &&
       (long long)grid.x * grid.y <= (long long)per_sm * sms) {
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = grid;
-    cfg.blockDim = dim3(kThreads);
+    cfg.blockDim = dim3(threads);
     cfg.dynamicSmemBytes = smem;
     cfg.stream = st;
     cudaLaunchAttribute attr[2];
@@ -740,7 +864,7 @@ int launch_value_score_fa(const ma_kv& kv, int B, int H, int D, const float* a, 
     cfg.attrs = attr;
     for (int na = 2; na >= 1; --na) {
       cfg.numAttrs = na;
-      if (cudaLaunchKernelEx(&cfg, prefix_mass_fa, A) == cudaSuccess) return MA_OK;
+      if (cudaLaunchKernelEx(&cfg, kernel, A) == cudaSuccess) return MA_OK;
       (void)cudaGetLastError();
     }
   }

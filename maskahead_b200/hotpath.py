@@ -77,10 +77,21 @@ def fast_attend(query: torch.Tensor, prefix, current_key: torch.Tensor, current_
     return out, mass
 
 
+def _needs_unpack(prefix: Prefix, batch: int, heads: int, head_dim: int, unpack) -> bool:
+    """unpack=None (automatic): a packed prefix is unpacked to bf16 first only when the
+    pipelined kernels cannot read it in place (ma_kv_read_in_place)."""
+    if prefix.nq == 0 or unpack is False:
+        return False
+    if unpack is True:
+        return True
+    desc = kv_descriptor(prefix, batch=batch, heads=heads, head_dim=head_dim)
+    return _lib.lib().ma_kv_read_in_place(desc.kv, head_dim) == 0
+
+
 def fast_step0(query: torch.Tensor, prefix, current_key: torch.Tensor, current_value: torch.Tensor, *,
                query_indices, topk: int, value_aware: bool = True, scaling: float | None = None,
                select: bool = True, want_mass: bool = False, gather: bool = False,
-               compact_out: tuple[torch.Tensor, torch.Tensor] | None = None, unpack: bool = True) -> Step0Result:
+               compact_out: tuple[torch.Tensor, torch.Tensor] | None = None, unpack: bool | None = None) -> Step0Result:
     """Step 0 of one layer: attention output, mass, score and the read set (session.py:1403-1454).
 
     The read set is the top min(topk, live) slots by score (value_aware) or mass, dead
@@ -89,13 +100,17 @@ def fast_step0(query: torch.Tensor, prefix, current_key: torch.Tensor, current_v
     sub-steps, optionally into the caller's buffers compact_out = (key, value), each
     [B, Hkv, >= k, D] (the session's state.key / state.value).
 
-    unpack=True: a packed (k4v4) prefix is dequantized once into a contiguous bf16 copy
-    (a per-device scratch) that the attention, scoring and gather passes then read, as the
-    reference's pass 1 unpacks it (splitk.py:465-480; session.py:1438-1441 gathers from
-    that read); the copy keeps the prefix's mask and lengths.
+    A packed (k4v4) prefix is read in place by the pipelined kernels, whose producer warps
+    dequantize its tiles (unpack=None, automatic, when ma_kv_read_in_place allows it).
+    unpack=True, or a prefix they cannot read in place, dequantizes it once into a
+    contiguous bf16 copy (a per-device scratch) that the attention, scoring and gather
+    passes then read, as the reference's pass 1 unpacks it (splitk.py:465-480;
+    session.py:1438-1441 gathers from that read); the copy keeps the prefix's mask and
+    lengths. Either way the values read are the same bf16 numbers.
     """
     prefix = as_prefix(prefix)
-    if unpack and prefix.nq > 0 and query.dtype == torch.bfloat16:
+    if query.dtype == torch.bfloat16 and _needs_unpack(prefix, query.shape[0], current_key.shape[1], query.shape[3],
+                                                         unpack):
         prefix = unpacked_prefix(prefix, query.shape[0], current_key.shape[1], query.shape[3])
     if prefix.n == 0:
         out, _ = splitk_attention(query, prefix, current_key, current_value, scaling=scaling)
@@ -194,17 +209,17 @@ def compact_attention(query: torch.Tensor, prefix, indices: torch.Tensor | None,
 
 def probe_attention(query: torch.Tensor, prefix, current_key: torch.Tensor, current_value: torch.Tensor, *,
                     block_size: int = 32, scaling: float | None = None, probe_rows: torch.Tensor | None = None,
-                    unpack: bool = True):
+                    unpack: bool | None = None):
     """Lookahead probe of one layer (session.py:2317-2332): block-causal attention of the
     probe forward [block k+1 | probe blocks] over [live prefix | itself], and the prefix
     mass of the probe rows (positions block_size..T) times the number of probe blocks.
     probe_rows: those positions as a device int32 tensor (optional; avoids a host copy,
-    e.g. under CUDA-graph capture). unpack=True: a packed (k4v4) prefix is dequantized once
-    into the bf16 scratch of unpacked_prefix, as for step 0 (the probe runs the attention
-    path, whose pass 1 unpacks the prefix: splitk.py:465-480)."""
+    e.g. under CUDA-graph capture). unpack: as for fast_step0 (a packed prefix read in
+    place when the pipelined kernels can, else unpacked once to bf16 first)."""
     t = query.shape[2]
     prefix = as_prefix(prefix)
-    if unpack and prefix.nq > 0 and query.dtype == torch.bfloat16:
+    if query.dtype == torch.bfloat16 and _needs_unpack(prefix, query.shape[0], current_key.shape[1], query.shape[3],
+                                                         unpack):
         prefix = unpacked_prefix(prefix, query.shape[0], current_key.shape[1], query.shape[3])
     out, stats = splitk_attention(query, prefix, current_key, current_value, scaling=scaling,
                                   causal_block=block_size, q_pos0=0, c_pos0=0, want_prefix=True)
@@ -240,19 +255,22 @@ def value_score(a: torch.Tensor, v: torch.Tensor, live_mask: torch.Tensor | None
     return score.reshape(*lead, n)
 
 
-def value_score_prefix(a: torch.Tensor, prefix, *, unpack: bool = True) -> torch.Tensor:
+def value_score_prefix(a: torch.Tensor, prefix, *, unpack: bool | None = None) -> torch.Tensor:
     """value_score over a cache layout (dense, packed k4v4 or paged): a [B, Hkv, n] fp32,
     the values read (dequantized) from the prefix; dead slots score 0 (session.py:27-40,
-    with the live values _live_values dequantizes, runtime/session.py:263-268).
-    unpack=True: a packed prefix is first dequantized into the bf16 scratch of
-    unpacked_prefix -- the reference's _live_values returns the values in the compute dtype
-    (bf16) -- and scored from there; unpack=False reads the packed values in place (fp32
-    dequantization)."""
+    with the live values _live_values dequantizes, runtime/session.py:263-268). The
+    reference's _live_values returns the values in the compute dtype (bf16): unpack=None
+    (automatic) reads a packed prefix in place through the pipelined kernel's producer
+    warps when it can (the same bf16 values), unpack=True dequantizes it into the bf16
+    scratch of unpacked_prefix first; unpack=False reads the packed values in place with
+    whichever kernel serves the layout."""
     lib = _lib.lib()
     prefix = as_prefix(prefix)
     b, h, n = a.shape
     desc = kv_descriptor(prefix, batch=b, heads=h)
-    if unpack and prefix.nq > 0 and (prefix.vf is None or prefix.vf.dtype == torch.bfloat16):
+    in_place = prefix.nq > 0 and unpack is None and lib.ma_kv_read_in_place(desc.kv, desc.head_dim) == 1
+    if unpack is not False and not in_place and prefix.nq > 0 and (prefix.vf is None or
+                                                                  prefix.vf.dtype == torch.bfloat16):
         prefix = unpacked_prefix(prefix, b, h, desc.head_dim)
         desc = kv_descriptor(prefix, batch=b, heads=h)
     a3 = a.to(torch.float32)
