@@ -623,7 +623,7 @@ def kernel_rooflines(c: dict, wl, share: dict, dev, stream, side, reps: int, wor
     peaks."""
     import torch
 
-    from maskahead_b200.hotpath import compact_attention, gather_read_set, unpacked_prefix
+    from maskahead_b200.hotpath import _needs_unpack, compact_attention, gather_read_set, unpacked_prefix
     from maskahead_b200.kernels import prefix_scores, select_topk_indices, splitk_attention
 
     hbm, tf_burst, tf_sust, kind = peaks_all()
@@ -635,21 +635,36 @@ def kernel_rooflines(c: dict, wl, share: dict, dev, stream, side, reps: int, wor
     flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
 
     def pre(layer):
+        # the prefix as fast_step0 reads it: a packed one unpacked to bf16 first (the step-0
+        # family below includes that unpack: it is the path's, once per layer)
         p = wl.prefix(layer)
-        return unpacked_prefix(p, B, H, D) if p.nq > 0 else p
+        return unpacked_prefix(p, B, H, D) if _needs_unpack(p, B, H, D, None) else p
+
+    # the later kernels of step 0 read the same unpacked copy: for them, copies made once
+    # (up to 8 GB of them, cycled over the layers; each larger than L2 or all distinct)
+    copies = []
+    if packed:
+        per = B * H * max(share["lens"]) * D * 2 * 2
+        for layer in range(max(1, min(L, (8 << 30) // max(per, 1)))):
+            u = unpacked_prefix(wl.prefix(layer), B, H, D)
+            copies.append(type(u)(**{**{s: getattr(u, s) for s in type(u).__slots__}, "kf": u.kf.clone(),
+                                     "vf": u.vf.clone()}))
+
+    def pre_k(layer):
+        return copies[layer % len(copies)] if copies else wl.prefix(layer)
 
     # eager inputs of the later families (outside the graphs)
     stats, scores, idxs = [], [], []
     for layer in range(L):
-        _, st = splitk_attention(wl.Q[layer, 0], pre(layer), wl.KC[layer, 0], wl.VC[layer, 0], scaling=wl.scale,
+        _, st = splitk_attention(wl.Q[layer, 0], pre_k(layer), wl.KC[layer, 0], wl.VC[layer, 0], scaling=wl.scale,
                                  want_prefix=True)
         stats.append(st)
-        _, sc = prefix_scores(wl.Q[layer, 0], pre(layer), st, wl.rows, value=True, scaling=wl.scale)
+        _, sc = prefix_scores(wl.Q[layer, 0], pre_k(layer), st, wl.rows, value=True, scaling=wl.scale)
         scores.append(sc)
         idx, _ = select_topk_indices(sc, min(k, min(share["lens"])), want_values=False,
                                      lens=getattr(wl, "lens_t", None))
         idxs.append(idx)
-    compacts = [gather_read_set(pre(layer), idxs[layer], out=wl.compact_buffers(layer)) for layer in range(L)]
+    compacts = [gather_read_set(pre_k(layer), idxs[layer], out=wl.compact_buffers(layer)) for layer in range(L)]
     torch.cuda.synchronize(dev)
 
     b_tok = token_bytes(c)
@@ -658,18 +673,19 @@ def kernel_rooflines(c: dict, wl, share: dict, dev, stream, side, reps: int, wor
         "step0_attention": (lambda layer: splitk_attention(wl.Q[layer, 0], pre(layer), wl.KC[layer, 0],
                                                            wl.VC[layer, 0], scaling=wl.scale, want_prefix=True),
                             ab["step0_layer"], 4.0 * Hq * T * n_sum * D,
-                            "attn_partial_fa (split-K, merge in the launch)" + (" after the unpack of the packed prefix"
-                                                                               if packed else "")),
-        "mass_value_score": (lambda layer: prefix_scores(wl.Q[layer, 0], pre(layer), stats[layer], wl.rows, value=True,
-                                                         scaling=wl.scale),
-                             n_sum * H * b_tok + q_bytes + 2 * n_sum * H * 4, 2.0 * Hq * T * n_sum * D,
+                            ("unpack of the packed prefix to bf16 + " if packed else "")
+                            + "attn_partial_fa (split-K, merge in the launch)"),
+        "mass_value_score": (lambda layer: prefix_scores(wl.Q[layer, 0], pre_k(layer), stats[layer], wl.rows,
+                                                         value=True, scaling=wl.scale),
+                             n_sum * H * (512 if packed else b_tok) + q_bytes + 2 * n_sum * H * 4, 2.0 * Hq * T * n_sum * D,
                              "prefix_mass_fa (mass, centre and value score in one launch)"
-                             + (" over the unpacked prefix" if packed else "")),
+                             + (" over the step's unpacked bf16 copy" if packed else "")),
         "select_topk": (lambda layer: select_topk_indices(scores[layer], idxs[layer].shape[2], want_values=False,
                                                           lens=getattr(wl, "lens_t", None)),
                         n_sum * H * 4 + B * H * k * 8, 0.0, "select_topk (radix select, ascending emission)"),
-        "gather": (lambda layer: gather_read_set(pre(layer), idxs[layer], out=wl.compact_buffers(layer)),
-                   ab["gather_layer"], 0.0, "gather_kv (read set into the compact cache)"),
+        "gather": (lambda layer: gather_read_set(pre_k(layer), idxs[layer], out=wl.compact_buffers(layer)),
+                   ab["gather_layer"] + (B * H * c["k"] * (512 - b_tok) if packed else 0), 0.0,
+                   "gather_kv (read set into the compact cache" + (", from the unpacked bf16 copy)" if packed else ")")),
         "substep_attention": (lambda layer: compact_attention(wl.Q[layer, 1], compacts[layer], None, wl.KC[layer, 1],
                                                               wl.VC[layer, 1], scaling=wl.scale),
                               ab["substep_layer"], 4.0 * Hq * T * (B * k + B * T) * D,

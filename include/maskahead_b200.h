@@ -167,6 +167,10 @@ MA_API int ma_set_attention_kernel(int which);
  * by unpacking it to bf16 first (the other kernels still read it in place, slower). Not
  * part of the reference's interface.                                                  */
 MA_API int ma_kv_read_in_place(const ma_kv* kv, int D);
+/* The CUDA runtime's message for the error behind the last MA_ERR_CUDA of this thread
+ * (the library links its own runtime, so a caller's cudaGetLastError cannot see it);
+ * reading it clears it.                                                              */
+MA_API const char* ma_last_cuda_error(void);
 
 /* ---- device-side status --------------------------------------------------------------
  * ma_workspace_status: waits for the work queued on `stream` (a stream synchronization),

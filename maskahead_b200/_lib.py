@@ -16,6 +16,7 @@ LIB_PATH = Path(__file__).resolve().parent / "_lib" / "libmaskahead_b200.so"
 
 MA_OK = 0
 MA_ERR_UNSUPPORTED = -2
+MA_ERR_CUDA = -4
 MA_ERR_TIMEOUT = -5
 MA_F32, MA_BF16, MA_F16 = 0, 1, 2
 MA_KV_DENSE, MA_KV_PACKED_TOKEN, MA_KV_PACKED_CHANNEL = 0, 1, 2
@@ -75,6 +76,7 @@ _SIGNATURES = {
     "ma_status_string": (ctypes.c_char_p, [_i32]),
     "ma_set_attention_kernel": (_i32, [_i32]),
     "ma_kv_read_in_place": (_i32, [_P(MaKV), _i32]),
+    "ma_last_cuda_error": (ctypes.c_char_p, []),
     "ma_workspace_status": (_i32, [_vp, _sz, _vp]),
     "ma_set_peer_wait_ns": (ctypes.c_int64, [ctypes.c_int64]),
     "ma_value_score_noalloc_status": (_i32, [_vp]),
@@ -139,7 +141,10 @@ def lib() -> ctypes.CDLL:
 
 def check(fn: str, status: int) -> None:
     if status != MA_OK:
-        detail = load_library().ma_status_string(status).decode()
+        lib_ = load_library()
+        detail = lib_.ma_status_string(status).decode()
+        if status == MA_ERR_CUDA:
+            detail += ": " + lib_.ma_last_cuda_error().decode()
         raise MaError(fn, status, detail)
 
 

@@ -23,10 +23,10 @@
 // in ma_attention_tc.cu (fused into a cooperative launch when it is one pass).
 // Every wait is bounded. Semantics follow src/maskahead/kernels/splitk.py:115-190.
 //
-// Packed (token-mode k4v4) prefixes: the PACKED instantiation adds four producer warps
+// Packed (token-mode k4v4) prefixes: the PACKED instantiation adds three producer warps
 // that build the K and V tiles from the packed bytes (ma_packed.cuh) instead of TMA loads;
 // the MMA warp hands them a slot by arriving on its kfree / vfree barrier where it would
-// have issued the slot's next TMA load, and they arrive on kfull / vfull (four arrivals)
+// have issued the slot's next TMA load, and they arrive on kfull / vfull (three arrivals)
 // once the slot's rows are stored. The current block stays TMA-fed.
 #include <string.h>
 
@@ -51,9 +51,13 @@ constexpr int kThreads = kWarps * 32;
 constexpr int kRowTile = 128;                      // query rows per CTA (one M tile)
 constexpr int kBN = 128;                           // keys per tile
 constexpr int kD = 128;
-constexpr int kDqWarps = 4;                        // dequantizing producer warps (PACKED)
+constexpr int kDqWarps = 3;                        // dequantizing producer warps (PACKED): 12 warps,
+                                                   // three per SM sub-partition (168 registers each)
+constexpr int kDqThreads = kDqWarps * 32;
+constexpr int kDqItems = (2 * 128 + kDqThreads - 1) / kDqThreads;   // half rows per thread and array
 constexpr int kThreadsP = kThreads + kDqWarps * 32;
-constexpr int kPrefetchTiles = 4;                  // L2 prefetch distance of the packed rows (tiles)
+constexpr int kStages = 3;                         // PACKED: staged raw tiles in flight (bulk copies)
+constexpr int kPackedSlots = 2;                    // PACKED: K and V slots each (the staging takes the rest)
 constexpr int kKSlots = 3;                         // K tiles in flight (freed once S was read)
 constexpr int kVSlots = 3;                         // V tiles in flight (freed when P.V completes)
 constexpr float kLog2e = 1.4426950408889634f;
@@ -64,6 +68,7 @@ constexpr int kQBytes = 2 * kQBlock;
 constexpr int kKVBlock = kBN * 128;                // 16 KB: [128 rows][128 B]
 constexpr int kKVBytes = 2 * kKVBlock;             // a K or V tile: 32 KB
 constexpr int kSmemBytes = 1024 + kQBytes + (kKSlots + kVSlots) * kKVBytes;   // 225 KB
+constexpr int kSmemBytesP = 1024 + kQBytes + 2 * kPackedSlots * kKVBytes + kStages * packed::kStageBytes;   // 221 KB
 constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kColS = 0, kColO = 256;
 constexpr int kOutBox = 32 * 128;
@@ -155,15 +160,14 @@ __device__ __forceinline__ void tma_tile(const CUtensorMap* map, int b, int h, i
 // the CTA aborted or the wait gave up.
 __device__ __forceinline__ bool dq_wait(uint64_t* bar, uint32_t parity, volatile int* abort) {
   bool ok = true;
-  if ((threadIdx.x & 31) == 0) {
+  if ((threadIdx.x & 31) == 0 && !mbar_try_wait(bar, parity)) {   // try_wait blocks a while itself
     const uint64_t t0 = global_ns();
-    while (!mbar_test(bar, parity)) {
+    while (!mbar_try_wait(bar, parity)) {
       if (*abort || global_ns() - t0 > kWaitNs) {
         ok = false;
         *abort = 1;
         break;
       }
-      __nanosleep(32);
     }
   }
   return __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
@@ -174,11 +178,15 @@ __device__ __forceinline__ void attn_fa_body(const Args& A) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sQ = smem;                                   // [2 d blocks][128 rows][128 B]
+  constexpr int KS = PACKED ? kPackedSlots : kKSlots;   // K tiles in flight
+  constexpr int VS = PACKED ? kPackedSlots : kVSlots;   // V tiles in flight
   uint8_t* sKs = sQ + kQBytes;                          // K slots
-  uint8_t* sVs = sKs + kKSlots * kKVBytes;              // V slots
+  uint8_t* sVs = sKs + KS * kKVBytes;                   // V slots
+  uint8_t* sStg = sVs + VS * kKVBytes;                  // PACKED: the staging ring of raw tiles
   __shared__ uint32_t s_taddr;
-  __shared__ __align__(8) uint64_t kfull[kKSlots], vfull[kVSlots], s_full[2], p_full[2], o_done[2], q_full, mbar_fin;
-  __shared__ __align__(8) uint64_t kfree[PACKED ? kKSlots : 1], vfree[PACKED ? kVSlots : 1];
+  __shared__ __align__(8) uint64_t kfull[KS], vfull[VS], s_full[2], p_full[2], o_done[2], q_full, mbar_fin;
+  __shared__ __align__(8) uint64_t kfree[PACKED ? kPackedSlots : 1], vfree[PACKED ? kPackedSlots : 1];
+  __shared__ __align__(8) uint64_t rfull[PACKED ? kStages : 1], rfree[PACKED ? kStages : 1];
   __shared__ __align__(16) float sKch[PACKED ? kD : 1];   // the packed keys' divisor of this (b, h)
   __shared__ int s_abort, s_merge_ok;
 
@@ -232,11 +240,15 @@ __device__ __forceinline__ void attn_fa_body(const Args& A) {
       prefetch_map(is_cur ? &A.ckmap : &A.kmap);
       prefetch_map(is_cur ? &A.cvmap : &A.vmap);
     }
-    for (int i = 0; i < kKSlots; ++i) mbar_init(&kfull[i], dq ? kDqWarps : 1);
-    for (int i = 0; i < kVSlots; ++i) mbar_init(&vfull[i], dq ? kDqWarps : 1);
+    for (int i = 0; i < KS; ++i) mbar_init(&kfull[i], dq ? kDqWarps : 1);
+    for (int i = 0; i < VS; ++i) mbar_init(&vfull[i], dq ? kDqWarps : 1);
     if (PACKED) {
-      for (int i = 0; i < kKSlots; ++i) mbar_init(&kfree[i], 1);
-      for (int i = 0; i < kVSlots; ++i) mbar_init(&vfree[i], 1);
+      for (int i = 0; i < KS; ++i) mbar_init(&kfree[i], 1);
+      for (int i = 0; i < VS; ++i) mbar_init(&vfree[i], 1);
+      for (int i = 0; i < kStages; ++i) {
+        mbar_init(&rfull[i], 1);
+        mbar_init(&rfree[i], kDqWarps);
+      }
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&s_full[i], 1);
@@ -267,8 +279,12 @@ __device__ __forceinline__ void attn_fa_body(const Args& A) {
       }
     }
     if (!dq) {
-      for (int i = 0; i < kKSlots && i < ntiles; ++i) tma_tile(km, b, h, begin + i * kBN, sKs + i * kKVBytes, &kfull[i]);
-      for (int i = 0; i < kVSlots && i < ntiles; ++i) tma_tile(vm, b, h, begin + i * kBN, sVs + i * kKVBytes, &vfull[i]);
+      for (int i = 0; i < KS && i < ntiles; ++i) tma_tile(km, b, h, begin + i * kBN, sKs + i * kKVBytes, &kfull[i]);
+      for (int i = 0; i < VS && i < ntiles; ++i) tma_tile(vm, b, h, begin + i * kBN, sVs + i * kKVBytes, &vfull[i]);
+    } else {   // the first raw tiles into the staging ring
+      for (int i = 0; i < kStages && i < ntiles; ++i)
+        packed::stage_tile(A.kv, b, h, begin + i * kBN, min(end, begin + (i + 1) * kBN), sStg + i * packed::kStageBytes,
+                           &rfull[i]);
     }
   }
   if (warp == 0) tmem_alloc(&s_taddr, kTmemCols);
@@ -292,8 +308,10 @@ __device__ __forceinline__ void attn_fa_body(const Args& A) {
       // one completed but unobserved phase, so the parity tests are unambiguous.
       bool ok = true;
       // the queries and the first min(3, ntiles) K and V tiles were issued at setup
-      int kIss = min(kKSlots, ntiles), kObs = 0, vIss = min(kVSlots, ntiles), vObs = 0;
+      int kIss = min(KS, ntiles), kObs = 0, vIss = min(VS, ntiles), vObs = 0;
       int sN = 0, pN = 0, oD = 0;                   // S issued, P.V issued, P.V seen complete
+      // PACKED: raw tiles staged, staged tiles seen consumed by the producer warps
+      int rIss = dq ? min(kStages, ntiles) : ntiles, rfObs = 0;
       const CUtensorMap* km = is_cur ? &A.ckmap : &A.kmap;
       const CUtensorMap* vm = is_cur ? &A.cvmap : &A.vmap;
       const bool q_ok = mbar_wait(&q_full, 0);
@@ -310,11 +328,11 @@ __device__ __forceinline__ void attn_fa_body(const Args& A) {
       int spins = 0;
       while (ok && pN < ntiles) {
         bool progress = false;
-        if (kObs < kIss && mbar_test(&kfull[kObs % kKSlots], (uint32_t)(kObs / kKSlots) & 1u)) {
+        if (kObs < kIss && mbar_test(&kfull[kObs % KS], (uint32_t)(kObs / KS) & 1u)) {
           ++kObs;
           progress = true;
         }
-        if (vObs < vIss && mbar_test(&vfull[vObs % kVSlots], (uint32_t)(vObs / kVSlots) & 1u)) {
+        if (vObs < vIss && mbar_test(&vfull[vObs % VS], (uint32_t)(vObs / VS) & 1u)) {
           ++vObs;
           progress = true;
         }
@@ -324,7 +342,7 @@ __device__ __forceinline__ void attn_fa_body(const Args& A) {
         }
         if (sN < ntiles && kObs > sN && oD >= sN - 1) {
           fence_after_sync();
-          const uint64_t bd0 = kdesc + (uint64_t)((sN % kKSlots) * (kKVBytes / 16));
+          const uint64_t bd0 = kdesc + (uint64_t)((sN % KS) * (kKVBytes / 16));
           const uint32_t dS = taddr + kColS + (sN & 1) * 128;
 #pragma unroll
           for (int kk = 0; kk < kD / 16; ++kk)
@@ -336,7 +354,7 @@ __device__ __forceinline__ void attn_fa_body(const Args& A) {
         }
         if (pN < sN && vObs > pN && mbar_test(&p_full[pN & 1], (uint32_t)(pN >> 1) & 1u)) {
           fence_after_sync();
-          const uint64_t bd0 = vdesc + (uint64_t)((pN % kVSlots) * (kKVBytes / 16));
+          const uint64_t bd0 = vdesc + (uint64_t)((pN % VS) * (kKVBytes / 16));
           const uint32_t aP = taddr + kColS + (pN & 1) * 128;
 #pragma unroll
           for (int kk = 0; kk < kBN / 16; ++kk)   // keys 16kk..: P columns 64 (kk / 4) + 8 (kk % 4)
@@ -346,17 +364,30 @@ __device__ __forceinline__ void attn_fa_body(const Args& A) {
           ++pN;
           progress = true;
         }
+        // PACKED: a stage takes the next raw tile once the producer warps consumed its last
+        if (dq) {
+          if (rfObs < rIss && mbar_test(&rfree[rfObs % kStages], (uint32_t)(rfObs / kStages) & 1u)) {
+            ++rfObs;
+            progress = true;
+          }
+          if (rIss < ntiles && rfObs > rIss - kStages) {
+            packed::stage_tile(A.kv, b, h, begin + rIss * kBN, min(end, begin + (rIss + 1) * kBN),
+                               sStg + (rIss % kStages) * packed::kStageBytes, &rfull[rIss % kStages]);
+            ++rIss;
+            progress = true;
+          }
+        }
         // a K slot is free once the S it held was consumed (P.V of that tile issued)
-        if (kIss < ntiles && pN > kIss - kKSlots) {
-          if (dq) mbar_arrive(&kfree[kIss % kKSlots]);   // the producer warps may refill it
-          else tma_tile(km, b, h, begin + kIss * kBN, sKs + (kIss % kKSlots) * kKVBytes, &kfull[kIss % kKSlots]);
+        if (kIss < ntiles && pN > kIss - KS) {
+          if (dq) mbar_arrive(&kfree[kIss % KS]);   // the producer warps may refill it
+          else tma_tile(km, b, h, begin + kIss * kBN, sKs + (kIss % KS) * kKVBytes, &kfull[kIss % KS]);
           ++kIss;
           progress = true;
         }
         // a V slot is free once its P.V completed
-        if (vIss < ntiles && oD > vIss - kVSlots) {
-          if (dq) mbar_arrive(&vfree[vIss % kVSlots]);
-          else tma_tile(vm, b, h, begin + vIss * kBN, sVs + (vIss % kVSlots) * kKVBytes, &vfull[vIss % kVSlots]);
+        if (vIss < ntiles && oD > vIss - VS) {
+          if (dq) mbar_arrive(&vfree[vIss % VS]);
+          else tma_tile(vm, b, h, begin + vIss * kBN, sVs + (vIss % VS) * kKVBytes, &vfull[vIss % VS]);
           ++vIss;
           progress = true;
         }
@@ -383,43 +414,58 @@ __device__ __forceinline__ void attn_fa_body(const Args& A) {
       if (!q_ok) mbar_wait(&q_full, 0, 20000000ull);
       if (!dq) {   // TMA loads still in flight (the producer warps' stores end with them)
         for (int tt = kObs; tt < kIss; ++tt)
-          mbar_wait(&kfull[tt % kKSlots], (uint32_t)(tt / kKSlots) & 1u, 20000000ull);
+          mbar_wait(&kfull[tt % KS], (uint32_t)(tt / KS) & 1u, 20000000ull);
         for (int tt = vObs; tt < vIss; ++tt)
-          mbar_wait(&vfull[tt % kVSlots], (uint32_t)(tt / kVSlots) & 1u, 20000000ull);
+          mbar_wait(&vfull[tt % VS], (uint32_t)(tt / VS) & 1u, 20000000ull);
+      } else {     // bulk copies into the staging ring still in flight
+        for (int tt = rfObs; tt < rIss; ++tt)
+          mbar_wait(&rfull[tt % kStages], (uint32_t)(tt / kStages) & 1u, 20000000ull);
       }
     }
     __syncwarp();
   } else if (PACKED && !softmax_warp) {
     // ------------------------------------------------------------ producer warps (PACKED)
-    // thread dt builds row dt of every K and V tile of the split: tile t's K into slot
-    // t % kKSlots once the MMA warp released it (kfree; the first kKSlots are free), then
-    // its V likewise; the next tile's raw row is loaded before the current one is stored
+    // Tile t's raw rows arrive in stage t % kStages (rfull); its K items go into slot
+    // t % KS once the MMA warp released it (kfree; the first KS are free), its V items into
+    // slot t % VS likewise, then the stage is handed back (rfree). An item is (row, 32-channel
+    // group), item it = dt + kDqThreads * i being group it & 3 of row it >> 2, so a warp
+    // reads 512 consecutive staged bytes.
     if (dq) {
       const int dt = threadIdx.x - (kSoftThreads + 32);
       pdl_wait();   // with a programmatic launch, the cache may come from the kernel before
-      sKch[dt] = A.kv.kchan[(int64_t)b * A.kv.skc[0] + (int64_t)h * A.kv.skc[1] + dt];
-      if (dt == 0)
-        for (int t = 0; t < kPrefetchTiles && t < ntiles; ++t)
-          packed::prefetch_rows(A.kv, b, h, begin + t * kBN, min(end, begin + (t + 1) * kBN));
-      asm volatile("bar.sync 6, %0;\n" ::"r"(kDqWarps * 32) : "memory");
-      packed::RawRow cur, nxt;
-      packed::load_row(A.kv, b, h, begin + dt, end, cur);
+      for (int c = dt; c < kD; c += kDqThreads)
+        sKch[c] = A.kv.kchan[(int64_t)b * A.kv.skc[0] + (int64_t)h * A.kv.skc[1] + c];
+      asm volatile("bar.sync 6, %0;\n" ::"r"(kDqThreads) : "memory");
+      constexpr int kItems = (kBN * 4 + kDqThreads - 1) / kDqThreads;
       for (int t = 0; t < ntiles; ++t) {
-        const int tp = t + kPrefetchTiles;
-        if (dt == 0 && tp < ntiles)
-          packed::prefetch_rows(A.kv, b, h, begin + tp * kBN, min(end, begin + (tp + 1) * kBN));
-        if (t + 1 < ntiles) packed::load_row(A.kv, b, h, begin + (t + 1) * kBN + dt, end, nxt);
-        if (t >= kKSlots && !dq_wait(&kfree[t % kKSlots], (uint32_t)((t / kKSlots) - 1) & 1u, &s_abort)) break;
-        packed::store_row<true>(cur.k, cur.ok, sKs + (t % kKSlots) * kKVBytes, dt, sKch);
+        const int j0 = begin + t * kBN;
+        const uint8_t* stg = sStg + (t % kStages) * packed::kStageBytes;
+        if (!dq_wait(&rfull[t % kStages], (uint32_t)(t / kStages) & 1u, &s_abort)) break;
+        if (t >= KS && !dq_wait(&kfree[t % KS], (uint32_t)((t / KS) - 1) & 1u, &s_abort)) break;
+#pragma unroll
+        for (int i = 0; i < kItems; ++i) {
+          const int it = dt + kDqThreads * i;
+          if (it < kBN * 4)
+            packed::dequant_item<true>(stg, it >> 2, it & 3, packed::row_ok(A.kv, b, j0 + (it >> 2), end),
+                                       sKs + (t % KS) * kKVBytes, sKch);
+        }
         fence_proxy_async();   // generic stores -> the tensor core's reads
         __syncwarp();
-        if (lane == 0) mbar_arrive(&kfull[t % kKSlots]);
-        if (t >= kVSlots && !dq_wait(&vfree[t % kVSlots], (uint32_t)((t / kVSlots) - 1) & 1u, &s_abort)) break;
-        packed::store_row<false>(cur.v, cur.ok, sVs + (t % kVSlots) * kKVBytes, dt, nullptr);
+        if (lane == 0) mbar_arrive(&kfull[t % KS]);
+        if (t >= VS && !dq_wait(&vfree[t % VS], (uint32_t)((t / VS) - 1) & 1u, &s_abort)) break;
+#pragma unroll
+        for (int i = 0; i < kItems; ++i) {
+          const int it = dt + kDqThreads * i;
+          if (it < kBN * 4)
+            packed::dequant_item<false>(stg, it >> 2, it & 3, packed::row_ok(A.kv, b, j0 + (it >> 2), end),
+                                        sVs + (t % VS) * kKVBytes, nullptr);
+        }
         fence_proxy_async();
         __syncwarp();
-        if (lane == 0) mbar_arrive(&vfull[t % kVSlots]);
-        cur = nxt;
+        if (lane == 0) {
+          mbar_arrive(&vfull[t % VS]);
+          mbar_arrive(&rfree[t % kStages]);   // the stage's raw rows are read
+        }
       }
     }
   } else {
@@ -707,11 +753,12 @@ __device__ __forceinline__ void attn_fa_body(const Args& A) {
   }
 }
 
-// The bf16 kernel (288 threads) and the PACKED one (416 threads: 13 warps x 32 x 152
-// registers <= 65536; the register cap is set directly because launch bounds would round
-// the block up to 512 threads and allow only 128).
+// The bf16 kernel (288 threads) and the PACKED one (384 threads: 12 warps, three on each SM
+// sub-partition, whose quarter of the register file leaves 168 registers a thread).
 __global__ void __launch_bounds__(kThreads, 1) attn_partial_fa(const __grid_constant__ Args A) { attn_fa_body<false>(A); }
-__global__ void __maxnreg__(152) attn_partial_fa_packed(const __grid_constant__ Args A) { attn_fa_body<true>(A); }
+__global__ void __launch_bounds__(kThreadsP, 1) attn_partial_fa_packed(const __grid_constant__ Args A) {
+  attn_fa_body<true>(A);
+}
 
 
 bool tma_map_rows(CUtensorMap* map, const void* base, int B, int H, int n, const int64_t s[3]) {
@@ -783,7 +830,8 @@ int launch_attn_partial_fa(const ma_rows& q, const ma_kv& kv, int H, const ma_bl
                make_tma_map_2d(&A.omap, true, P.o, kD, prow_total, kD * 2, 64, 32)) ? 1 : 0;
   dim3 grid((R + kRowTile - 1) / kRowTile, P.S, q.B * H);
   auto kernel = packed ? attn_partial_fa_packed : attn_partial_fa;
-  if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes) != cudaSuccess)
+  const int smem = packed ? kSmemBytesP : kSmemBytes;
+  if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
     return MA_ERR_CUDA;
   const int rows_per_split = (std::min(kRowTile, R) + (int)grid.y - 1) / (int)grid.y;
   // cluster merge: with at most 16 splits (prefix ones + the block) a group's CTAs form one
@@ -799,7 +847,7 @@ int launch_attn_partial_fa(const ma_rows& q, const ma_kv& kv, int H, const ma_bl
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = grid;
     cfg.blockDim = dim3(threads);
-    cfg.dynamicSmemBytes = kSmemBytes;
+    cfg.dynamicSmemBytes = smem;
     cfg.stream = st;
     cudaLaunchAttribute attr[2];
     attr[0].id = cudaLaunchAttributeClusterDimension;
@@ -837,7 +885,7 @@ int launch_attn_partial_fa(const ma_rows& q, const ma_kv& kv, int H, const ma_bl
     int dev = 0, coop = 0, per_sm = 0;
     if (cudaGetDevice(&dev) == cudaSuccess &&
         cudaDeviceGetAttribute(&coop, cudaDevAttrCooperativeLaunch, dev) == cudaSuccess && coop &&
-        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, threads, kSmemBytes) == cudaSuccess &&
+        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, threads, smem) == cudaSuccess &&
         (long long)grid.x * grid.y * grid.z <= (long long)per_sm * device_sm_count()) {
       Args Af = A;
       Af.fuse = 1;
@@ -845,7 +893,7 @@ int launch_attn_partial_fa(const ma_rows& q, const ma_kv& kv, int H, const ma_bl
       cudaLaunchConfig_t cfg = {};
       cfg.gridDim = grid;
       cfg.blockDim = dim3(threads);
-      cfg.dynamicSmemBytes = kSmemBytes;
+      cfg.dynamicSmemBytes = smem;
       cfg.stream = st;
       cudaLaunchAttribute attr[2];
       attr[0].id = cudaLaunchAttributeCooperative;
@@ -863,7 +911,7 @@ int launch_attn_partial_fa(const ma_rows& q, const ma_kv& kv, int H, const ma_bl
       }
     }
   }
-  return launch_pdl(kernel, grid, dim3(threads), kSmemBytes, st, A) == cudaSuccess ? MA_OK : MA_ERR_CUDA;
+  return launch_pdl(kernel, grid, dim3(threads), smem, st, A) == cudaSuccess ? MA_OK : MA_ERR_CUDA;
 }
 
 }  // namespace ma

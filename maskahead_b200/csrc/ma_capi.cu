@@ -273,6 +273,11 @@ int ma_workspace_status(void* workspace, size_t workspace_bytes, void* stream) {
   return MA_ERR_TIMEOUT;
 }
 
+const char* ma_last_cuda_error(void) {
+  const cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? "no CUDA error pending" : cudaGetErrorString(e);
+}
+
 int ma_kv_read_in_place(const ma_kv* kv, int D) {
   if (!kv || check_kv(kv, D) != MA_OK || D != 128) return 0;
   if (kv->layout == MA_KV_DENSE) return kv->dtype == MA_BF16 && !kv->mask && !kv->pages ? 1 : 0;

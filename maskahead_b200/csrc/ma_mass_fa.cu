@@ -104,15 +104,14 @@ __device__ __forceinline__ uint32_t chunk_off(int j, int c) {
 // the CTA aborted or the wait gave up.
 __device__ __forceinline__ bool dq_wait(uint64_t* bar, uint32_t parity, volatile int* abort) {
   bool ok = true;
-  if ((threadIdx.x & 31) == 0) {
+  if ((threadIdx.x & 31) == 0 && !mbar_try_wait(bar, parity)) {   // try_wait blocks a while itself
     const uint64_t t0 = global_ns();
-    while (!mbar_test(bar, parity)) {
+    while (!mbar_try_wait(bar, parity)) {
       if (*abort || global_ns() - t0 > kWaitNs) {
         ok = false;
         *abort = 1;
         break;
       }
-      __nanosleep(32);
     }
   }
   return __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
@@ -671,11 +670,11 @@ __device__ __forceinline__ void mass_fa_body(const Args& A) {
   }
 }
 
-// The bf16 kernel (352 threads) and the PACKED one (480 threads: 15 warps x 32 x 136
-// registers <= 65536; the register cap is set directly because launch bounds would round
-// the block up to 512 threads and allow only 128).
+// The bf16 kernel (352 threads) and the PACKED one (480 threads: 15 warps, four of them on
+// three of the SM sub-partitions, whose quarter of the register file leaves 128 registers
+// a thread).
 __global__ void __launch_bounds__(kThreads, 1) prefix_mass_fa(const __grid_constant__ Args A) { mass_fa_body<false>(A); }
-__global__ void __maxnreg__(136) prefix_mass_fa_packed(const __grid_constant__ Args A) { mass_fa_body<true>(A); }
+__global__ void __launch_bounds__(kThreadsP, 1) prefix_mass_fa_packed(const __grid_constant__ Args A) { mass_fa_body<true>(A); }
 
 
 bool tma_map_rows(CUtensorMap* map, const void* base, int B, int H, int n, const int64_t s[3]) {

@@ -21,9 +21,10 @@
 //     through the packed fp32 pipe (fma.rn.f32x2, mul.rn.f32x2), one cvt per bf16 pair;
 //   * rows past the sequence's end (or on a page outside the pool) are written as zeros.
 //
-// Raw rows come from L2: one lane prefetches the byte ranges of a few tiles ahead with
-// cp.async.bulk.prefetch.L2 (no shared memory), and each thread loads the next tile's row
-// before it stores the current one.
+// Raw rows reach shared memory by bulk copies (cp.async.bulk, completion on an mbarrier)
+// that one thread issues a few tiles ahead into a staging ring (stage_tile); the producer
+// warps then turn a staged tile into bf16 tiles (dequant_item). Kernels that keep raw rows
+// in registers instead (the value pass of the mass kernel) read them with load_row.
 #pragma once
 
 #include "ma_common.cuh"
@@ -125,6 +126,73 @@ __device__ __forceinline__ void load_row(const ma_kv& kv, int b, int h, int j, i
              (int64_t)sb * kv.svs[0] + (int64_t)h * kv.svs[1] + (int64_t)sj * 4, r.v);
 }
 
+// ------------------------------------------------------------------- staging ring
+// One staged tile: the 128 rows' payloads (row r at r*64) of K and V, then their
+// scale/zero words (row r at r*8) -- 160 bytes per row.
+constexpr int kStageBytes = kTileRows * (2 * kRowBytes + 4 * 8);   // 20 KB
+constexpr int kStgKq = 0, kStgVq = kTileRows * kRowBytes, kStgKs = 2 * kTileRows * kRowBytes;
+constexpr int kStgKz = kStgKs + kTileRows * 8, kStgVs = kStgKz + kTileRows * 8, kStgVz = kStgVs + kTileRows * 8;
+
+__device__ __forceinline__ void bulk_copy(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];\n" ::"r"(
+                   tc::smem_addr(dst)),
+               "l"(src), "r"(bytes), "r"(tc::smem_addr(bar))
+               : "memory");
+}
+
+// The copies of rows [j0, j1) of head h of sequence b into a staging stage: one set of six
+// (K and V payloads, scales, zeros) per storage segment (one per page crossed), each
+// segment's row count rounded up to even so every scale/zero copy is a multiple of 16 bytes
+// (the extra row exists: nq and page sizes are even, segments start at even slots); a
+// segment on a page outside the pool is not copied. Returns the bytes they move; with ISSUE
+// the copies are issued, completing on `bar` (whose transaction count the caller set).
+template <bool ISSUE>
+__device__ __forceinline__ uint32_t stage_copies(const ma_kv& kv, int b, int h, int j0, int j1, uint8_t* stg,
+                                                 uint64_t* bar) {
+  uint32_t total = 0;
+  for (int j = j0; j < j1;) {
+    const int seg_end = kv.pages ? min(j1, (j / kv.page_size + 1) * kv.page_size) : j1;
+    int sb, sj;
+    if (locate(kv, b, j, sb, sj)) {
+      int cnt = seg_end - j;
+      const int avail = kv.pages ? kv.page_size - sj : kv.nq - j;
+      cnt = min(cnt + (cnt & 1), avail);
+      if (ISSUE) {
+        const int r0 = j - j0;
+        const int64_t q = (int64_t)sb * kv.skq[0] + (int64_t)h * kv.skq[1] + (int64_t)sj * kRowBytes;
+        const int64_t qv = (int64_t)sb * kv.svq[0] + (int64_t)h * kv.svq[1] + (int64_t)sj * kRowBytes;
+        const int64_t s = (int64_t)sb * kv.sks[0] + (int64_t)h * kv.sks[1] + (int64_t)sj * 4;
+        const int64_t sv = (int64_t)sb * kv.svs[0] + (int64_t)h * kv.svs[1] + (int64_t)sj * 4;
+        bulk_copy(stg + kStgKq + r0 * kRowBytes, kv.kq + q, (uint32_t)cnt * kRowBytes, bar);
+        bulk_copy(stg + kStgVq + r0 * kRowBytes, kv.vq + qv, (uint32_t)cnt * kRowBytes, bar);
+        bulk_copy(stg + kStgKs + r0 * 8, kv.ks + s, (uint32_t)cnt * 8, bar);
+        bulk_copy(stg + kStgKz + r0 * 8, kv.kz + s, (uint32_t)cnt * 8, bar);
+        bulk_copy(stg + kStgVs + r0 * 8, kv.vs + sv, (uint32_t)cnt * 8, bar);
+        bulk_copy(stg + kStgVz + r0 * 8, kv.vz + sv, (uint32_t)cnt * 8, bar);
+      }
+      total += (uint32_t)cnt * (2 * kRowBytes + 32);
+    }
+    j = seg_end;
+  }
+  return total;
+}
+
+// Stage rows [j0, j1): the transaction count, then the copies (one issuing thread).
+__device__ __forceinline__ void stage_tile(const ma_kv& kv, int b, int h, int j0, int j1, uint8_t* stg,
+                                           uint64_t* bar) {
+  const uint32_t bytes = stage_copies<false>(kv, b, h, j0, j1, stg, bar);
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%1], %0;\n" ::"r"(bytes), "r"(tc::smem_addr(bar))
+               : "memory");
+  stage_copies<true>(kv, b, h, j0, j1, stg, bar);
+}
+
+// Whether slot j of sequence b holds a row the tiles must carry (below end, on a page of
+// the pool); the others are written as zeros.
+__device__ __forceinline__ bool row_ok(const ma_kv& kv, int b, int j, int end) {
+  int sb, sj;
+  return j < end && locate(kv, b, j, sb, sj);
+}
+
 __device__ __forceinline__ float2 fmul2(float2 a, float2 b) {
   uint64_t d;
   asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(tc::f2_bits(a)), "l"(tc::f2_bits(b)));
@@ -140,13 +208,10 @@ __device__ __forceinline__ uint32_t half_word(uint2 w, int g) {
   return ((g & 2) ? w.y : w.x) >> (16 * (g & 1));
 }
 
-// Chunk c (channels 8c..8c+7) of a row: 8 codes of payload word c -> bf16 x 8.
+// 8 codes of payload word w (element 2i in the low nibble of byte i) -> bf16 x 8:
+// fma(code, s, z) in fp32, times the divisor kch8[0..7] for keys, one rounding.
 template <bool KEY>
-__device__ __forceinline__ uint4 chunk(const Raw& r, int c, const float* kchan_s) {
-  const uint32_t w = (&r.p[c >> 2].x)[c & 3];
-  const int g = c >> 2;   // 32-channel group
-  const float s = __half2float(__ushort_as_half((uint16_t)half_word(r.s, g)));
-  const float z = __half2float(__ushort_as_half((uint16_t)half_word(r.z, g)));
+__device__ __forceinline__ uint4 chunk_core(uint32_t w, float s, float z, const float* kch8) {
   const uint32_t lo = w & 0x0F0F0F0Fu, hi = (w >> 4) & 0x0F0F0F0Fu;
   const float2 bias = make_float2(-8388608.f, -8388608.f), s2 = make_float2(s, s), z2 = make_float2(z, z);
   uint4 out;
@@ -156,11 +221,45 @@ __device__ __forceinline__ uint4 chunk(const Raw& r, int c, const float* kchan_s
     const uint32_t sel = (uint32_t)i | 0x7540u;
     float2 x = tc::fadd2(make_float2(magic(lo, sel), magic(hi, sel)), bias);
     x = tc::ffma2(x, s2, z2);
-    if (KEY) x = fmul2(x, *reinterpret_cast<const float2*>(kchan_s + 8 * c + 2 * i));
+    if (KEY) x = fmul2(x, *reinterpret_cast<const float2*>(kch8 + 2 * i));
     __nv_bfloat162 v = __floats2bfloat162_rn(x.x, x.y);
     o[i] = *reinterpret_cast<uint32_t*>(&v);
   }
   return out;
+}
+
+// Chunk c (channels 8c..8c+7) of a raw row.
+template <bool KEY>
+__device__ __forceinline__ uint4 chunk(const Raw& r, int c, const float* kchan_s) {
+  const uint32_t w = (&r.p[c >> 2].x)[c & 3];
+  const int g = c >> 2;   // 32-channel group
+  const float s = __half2float(__ushort_as_half((uint16_t)half_word(r.s, g)));
+  const float z = __half2float(__ushort_as_half((uint16_t)half_word(r.z, g)));
+  return chunk_core<KEY>(w, s, z, KEY ? kchan_s + 8 * c : nullptr);
+}
+
+// Item (row, group g) of a staged tile: the group's 32 values of K (KEY, times kchan) or V
+// dequantized into chunks 4g..4g+3 of the tile's row (zeros if !ok).
+template <bool KEY>
+__device__ __forceinline__ void dequant_item(const uint8_t* stg, int row, int g, bool ok, uint8_t* tile,
+                                             const float* kchan_s) {
+  uint8_t* line = tile + (g >> 1) * kBlockBytes + row * 128;
+  if (!ok) {
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+      *reinterpret_cast<uint4*>(line + ((((4 * g + i) & 7) ^ (row & 7)) << 4)) = make_uint4(0, 0, 0, 0);
+    return;
+  }
+  const uint4 p = *reinterpret_cast<const uint4*>(stg + (KEY ? kStgKq : kStgVq) + row * kRowBytes + g * 16);
+  const float s = __half2float(*reinterpret_cast<const __half*>(stg + (KEY ? kStgKs : kStgVs) + row * 8 + g * 2));
+  const float z = __half2float(*reinterpret_cast<const __half*>(stg + (KEY ? kStgKz : kStgVz) + row * 8 + g * 2));
+  const uint32_t w[4] = {p.x, p.y, p.z, p.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int c = 4 * g + i;
+    *reinterpret_cast<uint4*>(line + (((c & 7) ^ (row & 7)) << 4)) =
+        chunk_core<KEY>(w[i], s, z, KEY ? kchan_s + 8 * c : nullptr);
+  }
 }
 
 // Row `row` of a bf16 SW128 tile (two 64-channel blocks) from a raw row (zeros if !ok).

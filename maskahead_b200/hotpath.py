@@ -78,14 +78,19 @@ def fast_attend(query: torch.Tensor, prefix, current_key: torch.Tensor, current_
 
 
 def _needs_unpack(prefix: Prefix, batch: int, heads: int, head_dim: int, unpack) -> bool:
-    """unpack=None (automatic): a packed prefix is unpacked to bf16 first only when the
-    pipelined kernels cannot read it in place (ma_kv_read_in_place)."""
-    if prefix.nq == 0 or unpack is False:
-        return False
-    if unpack is True:
-        return True
-    desc = kv_descriptor(prefix, batch=batch, heads=heads, head_dim=head_dim)
-    return _lib.lib().ma_kv_read_in_place(desc.kv, head_dim) == 0
+    """Whether an attention pass (step 0, the probe) unpacks a packed prefix to bf16 first.
+
+    unpack=None (automatic) and True: yes. On B200 the unpack kernel followed by the
+    TMA-fed bf16 kernels is the faster route for attention: the unpack does the
+    dequantization once on every SM, and its output of a layer stays in L2 for the
+    attention, scoring and gather passes, while dequantizing producer warps inside the
+    attention kernel compete with its softmax warps for issue slots and are repeated by
+    every row tile of a head (measured: a cfg3 layer's step-0 attention 29 us unpacked
+    against 36 us in place, 16 paged cfg5 sequences 0.16 + unpack against 0.76 ms).
+    unpack=False reads the prefix in place: the pipelined kernels' producer warps for a
+    token-mode layout they accept (ma_kv_read_in_place), the general kernels otherwise;
+    that route moves only the packed bytes (160 per slot and head)."""
+    return prefix.nq > 0 and unpack is not False
 
 
 def fast_step0(query: torch.Tensor, prefix, current_key: torch.Tensor, current_value: torch.Tensor, *,
@@ -100,13 +105,12 @@ def fast_step0(query: torch.Tensor, prefix, current_key: torch.Tensor, current_v
     sub-steps, optionally into the caller's buffers compact_out = (key, value), each
     [B, Hkv, >= k, D] (the session's state.key / state.value).
 
-    A packed (k4v4) prefix is read in place by the pipelined kernels, whose producer warps
-    dequantize its tiles (unpack=None, automatic, when ma_kv_read_in_place allows it).
-    unpack=True, or a prefix they cannot read in place, dequantizes it once into a
-    contiguous bf16 copy (a per-device scratch) that the attention, scoring and gather
-    passes then read, as the reference's pass 1 unpacks it (splitk.py:465-480;
-    session.py:1438-1441 gathers from that read); the copy keeps the prefix's mask and
-    lengths. Either way the values read are the same bf16 numbers.
+    A packed (k4v4) prefix is dequantized once into a contiguous bf16 copy (a per-device
+    scratch) that the attention, scoring and gather passes then read, as the reference's
+    pass 1 unpacks it (splitk.py:465-480; session.py:1438-1441 gathers from that read); the
+    copy keeps the prefix's mask and lengths. unpack=False reads the packed prefix in place
+    instead (_needs_unpack has the trade-off); either way the values read are the same
+    bf16 numbers.
     """
     prefix = as_prefix(prefix)
     if query.dtype == torch.bfloat16 and _needs_unpack(prefix, query.shape[0], current_key.shape[1], query.shape[3],
@@ -214,8 +218,8 @@ def probe_attention(query: torch.Tensor, prefix, current_key: torch.Tensor, curr
     probe forward [block k+1 | probe blocks] over [live prefix | itself], and the prefix
     mass of the probe rows (positions block_size..T) times the number of probe blocks.
     probe_rows: those positions as a device int32 tensor (optional; avoids a host copy,
-    e.g. under CUDA-graph capture). unpack: as for fast_step0 (a packed prefix read in
-    place when the pipelined kernels can, else unpacked once to bf16 first)."""
+    e.g. under CUDA-graph capture). unpack: as for fast_step0 (a packed prefix is unpacked
+    once to bf16 first unless unpack=False)."""
     t = query.shape[2]
     prefix = as_prefix(prefix)
     if query.dtype == torch.bfloat16 and _needs_unpack(prefix, query.shape[0], current_key.shape[1], query.shape[3],
@@ -268,6 +272,8 @@ def value_score_prefix(a: torch.Tensor, prefix, *, unpack: bool | None = None) -
     prefix = as_prefix(prefix)
     b, h, n = a.shape
     desc = kv_descriptor(prefix, batch=b, heads=h)
+    # only V is read here: in place the producer warps' dequantization replaces the unpack's
+    # (cfg3 layer: 78 against 118 us)
     in_place = prefix.nq > 0 and unpack is None and lib.ma_kv_read_in_place(desc.kv, desc.head_dim) == 1
     if unpack is not False and not in_place and prefix.nq > 0 and (prefix.vf is None or
                                                                   prefix.vf.dtype == torch.bfloat16):

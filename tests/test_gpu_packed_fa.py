@@ -1,4 +1,5 @@
-"""The pipelined kernels reading token-mode k4v4 prefixes in place.
+"""The pipelined kernels reading token-mode k4v4 prefixes in place (unpack=False; the
+default attention route unpacks first, which measured faster on B200).
 
 The producer warps of attn_partial_fa and prefix_mass_fa dequantize the packed rows into
 the same bf16 tiles an unpack followed by TMA loads would give them (fma(code, scale,
@@ -125,13 +126,17 @@ def test_packed_attention_and_scores_equal_the_unpacked_path(case):
     _same(score_p, score_u)
 
 
-def test_packed_step0_matches_the_oracle():
+@pytest.mark.parametrize("unpack", [None, False], ids=["unpacked_first", "in_place"])
+def test_packed_step0_matches_the_oracle(unpack):
+    """fast_step0 over a packed prefix, unpacked first (the default) or read in place by
+    the producer warps (unpack=False)."""
     from maskahead_b200.hotpath import fast_step0
 
     B, Hq, H, n, T, topk = 1, 28, 4, 4096, 32, 512
     pre, k, v = _packed(B, H, n, seed=99)
     q, kc, vc = _inputs(B, Hq, H, T, seed=100)
-    res = fast_step0(q, pre, kc, vc, query_indices=list(range(T)), topk=topk, scaling=128 ** -0.5, gather=True)
+    res = fast_step0(q, pre, kc, vc, query_indices=list(range(T)), topk=topk, scaling=128 ** -0.5, gather=True,
+                     unpack=unpack)
     torch.cuda.synchronize()
     qc, kcc, vcc = q.cpu(), kc.cpu(), vc.cpu()
     imp = oracle.selector_importance(qc, k, query_indices=list(range(T)), scale=128 ** -0.5)

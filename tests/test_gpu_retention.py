@@ -65,9 +65,9 @@ def test_probe_attention_matches_oracle(kind, T, probe_blocks):
 
 @pytest.mark.parametrize("n", [3000, 9000])
 def test_value_score_prefix_packed_matches_oracle(n):
-    """unpack=True scores the bf16-dequantized values (the reference's compute dtype);
-    unpack=False reads the packed values in place (fp32 dequantization), within bf16
-    rounding of the first."""
+    """The default (the packed values read in place by the producer warps of the value
+    pass) and unpack=True score the bf16-dequantized values (the reference's compute
+    dtype); unpack=False reads the packed values in place as well."""
     from maskahead_b200.hotpath import value_score_prefix
 
     _, k, v, _, _ = _inputs(n, H=4, n=n)
