@@ -24,8 +24,9 @@ One step = one block-step over all layers:
   step 0     score (prefix mass of the 32 mask queries x G query heads), value-aware
              score, top-k read set, dense attention over [prefix | block];
   3 sparse sub-steps: attention over [read set | block];
-  retention (every 4th block, interval_blocks = 4): probe attention of the lookahead
-             block(s), probe mass, lookahead value score, survivors.
+  retention (every 4th block, interval_blocks = 4): the lookahead probe merged into step 0
+             (one launch over [block | probe blocks], block-causal), the probe mass, the
+             lookahead value score, survivors.
 Synthetic seeded inputs, N(0,1); every cache exceeds L2 (126 MB), so each step reads it
 from HBM. `value` = tokens/s (32 tokens per block-step per sequence) over all ranks.
 
@@ -284,19 +285,30 @@ class Workload:
     def block_step(self, retain: bool):
         """One block-step over every layer through the public hot-path API."""
         import torch
-        from maskahead_b200.hotpath import (compact_attention, fast_step0, lookahead_survivors,
-                                            probe_attention, value_score, value_score_prefix)
+        from maskahead_b200.hotpath import (compact_attention, fast_step0, lookahead_survivors, value_score,
+                                            value_score_prefix)
 
         c = self.cfg
-        outs, idxs, masses = [], [], []
+        # a retention block runs its lookahead probe merged into step 0 (lookahead_merge):
+        # one launch over [block | probe blocks] per layer instead of a second pass
+        merge = retain and c["retention"]
+        outs, idxs, masses, probe = [], [], [], []
         for layer in range(c["L"]):
             pre = self.prefix(layer)
             # the read set's rows are gathered once into the layer's compact cache (the
             # session's state.key / state.value), which every sub-step attends
-            res = fast_step0(self.Q[layer, 0], pre, self.KC[layer, 0], self.VC[layer, 0], query_indices=self.rows,
-                             topk=c["k"], value_aware=True, scaling=self.scale, gather=True,
-                             compact_out=self.compact_buffers(layer))
-            out = self.gather_heads(res.out)
+            if merge:
+                res = fast_step0(self.QP[layer], pre, self.KCP[layer], self.VCP[layer], query_indices=self.rows,
+                                 topk=c["k"], value_aware=True, scaling=self.scale, gather=True,
+                                 compact_out=self.compact_buffers(layer), probe_blocks=c["probe_blocks"],
+                                 block_size=c["T"], probe_rows=self.probe_rows)
+                out = self.gather_heads(res.out[:, :, :c["T"]])   # the block's rows
+                probe.append(res.probe_mass)
+            else:
+                res = fast_step0(self.Q[layer, 0], pre, self.KC[layer, 0], self.VC[layer, 0], query_indices=self.rows,
+                                 topk=c["k"], value_aware=True, scaling=self.scale, gather=True,
+                                 compact_out=self.compact_buffers(layer))
+                out = self.gather_heads(res.out)
             for s in range(1, c["substeps"]):
                 out = self.gather_heads(compact_attention(self.Q[layer, s], res.compact, None, self.KC[layer, s],
                                                           self.VC[layer, s], scaling=self.scale))
@@ -305,11 +317,6 @@ class Workload:
             masses.append(res.mass)
         keep = None
         if retain and c["retention"]:
-            probe = []
-            for layer in range(c["L"]):
-                _, ap = probe_attention(self.QP[layer], self.prefix(layer), self.KCP[layer], self.VCP[layer],
-                                        block_size=c["T"], scaling=self.scale, probe_rows=self.probe_rows)
-                probe.append(ap)
             a = torch.stack(masses) + torch.stack(probe)
             if self.V is not None:
                 score = value_score(a, self.V)
@@ -329,12 +336,12 @@ def fused_scores(cfg: dict, share: dict) -> bool:
 def kernel_launches(cfg: dict, share: dict, retain: bool) -> int:
     """Our kernels in one block-step: step 0 = attention partial + combine + mass (with the
     fused value score, or + value apply) + top-k; each sub-step = partial + combine;
-    retention = per layer probe partial + combine + mass, then value centre + apply (once
+    retention = per layer the merged probe's mass launch, then value centre + apply (once
     for dense values, per layer for packed ones) and the survivors."""
     step0 = 4 if fused_scores(cfg, share) else 5
     n = (step0 + 2 * (cfg["substeps"] - 1)) * cfg["L"]
     if retain and cfg["retention"]:
-        n += 3 * cfg["L"] + (2 if cfg["kv"] == "bf16" else 2 * cfg["L"]) + 1
+        n += cfg["L"] + (2 if cfg["kv"] == "bf16" else 2 * cfg["L"]) + 1
     return n
 
 

@@ -44,6 +44,7 @@
  *   ma_compact_tokens    cache.py:659-678 (compact_tokens) and 342-365 (compact): the
  *                        cache compaction after an eviction (runtime/session.py:270-302)
  *   ma_rebuild_remap     cache.py:236-335 (the remap of rebuild)
+ *   ma_evict_plan        runtime/session.py:303-356 (_evict_to: the rebuild's index lists)
  */
 #ifndef MASKAHEAD_B200_H
 #define MASKAHEAD_B200_H
@@ -319,6 +320,24 @@ MA_API int ma_unpack_prefix(const ma_kv* kv, int B, int H, int D, void* out_k, v
  * skipped. The lists are applied in that order (groups, encode, stage), so a slot named
  * twice takes the later list's position, as the reference's successive scatters do.
  * B*H above INT_MAX returns MA_ERR_UNSUPPORTED.                                        */
+/* The planning of that rebuild after an eviction (runtime/session.py:303-356, the lazy
+ * group-preserving compaction of _evict_to): per lane (the flattened [L,B,H] axis) the live
+ * entries' physical slots phys [lanes, live] int32 and positions pos [lanes, live] int64
+ * (lane strides sphys_spos = {phys, pos}; positions increase along the live axis, as the
+ * eviction state keeps them). A key group of kgroup slots below quantized_length with at
+ * least `need` live entries is kept whole (need 0: no group is), except the last
+ * tail_groups; an entry at or past quantized_length (staged) among the recent_window
+ * newest positions stays staged; every other entry is re-encoded. Writes groups_before
+ * [lanes, ng] (ng = max(1, quantized_length / kgroup)), encode and stage [lanes, live]
+ * (contiguous int64, each list ascending / in position order, padded with -1),
+ * counts [lanes, 3] int32 (the three lengths) and maxes [4] int32: the three maxima over
+ * lanes -- the widths the reference pads its lists to -- and the number of lanes whose
+ * positions do not increase (their lists are not meaningful). ng above 8192 returns
+ * MA_ERR_UNSUPPORTED.                                                                  */
+MA_API int ma_evict_plan(const int32_t* phys, const int64_t* pos, int lanes, int live, const int64_t sphys_spos[2],
+                         int quantized_length, int kgroup, int need, int tail_groups, int recent_window,
+                         int64_t* groups_before, int64_t* encode, int64_t* stage, int32_t* counts, int32_t* maxes,
+                         void* stream);
 MA_API int ma_rebuild_remap(int B, int H, int old_len, int kgroup, const int64_t* groups_before, int g1,
                             const int64_t* encode, int m, const int64_t* groups_after, int g3,
                             const int64_t* stage, int st, int64_t* remap, void* stream);

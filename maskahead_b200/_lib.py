@@ -108,6 +108,8 @@ _SIGNATURES = {
                               _P(ctypes.c_int64), _vp]),
     "ma_compact_tokens": (_i32, [_P(MaKV), _P(MaKV), _i32, _i32, _i32, _vp, _i32, _P(ctypes.c_int64), _vp]),
     "ma_rebuild_remap": (_i32, [_i32, _i32, _i32, _i32, _vp, _i32, _vp, _i32, _vp, _i32, _vp, _i32, _vp, _vp]),
+    "ma_evict_plan": (_i32, [_vp, _vp, _i32, _i32, _P(ctypes.c_int64), _i32, _i32, _i32, _i32, _i32, _vp, _vp, _vp,
+                             _vp, _vp, _vp]),
 }
 
 EXPORTED = tuple(_SIGNATURES)

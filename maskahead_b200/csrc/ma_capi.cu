@@ -596,6 +596,23 @@ int ma_compact_tokens(const ma_kv* src, const ma_kv* dst, int B, int H, int D, c
   return launch_compact(p, B, (cudaStream_t)stream);
 }
 
+int ma_evict_plan(const int32_t* phys, const int64_t* pos, int lanes, int live, const int64_t sphys_spos[2],
+                  int quantized_length, int kgroup, int need, int tail_groups, int recent_window,
+                  int64_t* groups_before, int64_t* encode, int64_t* stage, int32_t* counts, int32_t* maxes,
+                  void* stream) {
+  if (lanes < 0 || live < 0 || quantized_length < 0 || kgroup <= 0 || need < 0 || tail_groups < 0 ||
+      recent_window < 0 || !sphys_spos || !maxes)
+    return MA_ERR_ARG;
+  const int ng = quantized_length / kgroup > 1 ? quantized_length / kgroup : 1;
+  if (ng > kEvictMaxGroups || tail_groups > ng) return MA_ERR_UNSUPPORTED;
+  if (lanes > 0 && live > 0 && (!phys || !pos || !groups_before || !encode || !stage || !counts)) return MA_ERR_ARG;
+  if (lanes > 0 && (!groups_before || !counts)) return MA_ERR_ARG;
+  if (sphys_spos[0] < live || sphys_spos[1] < live) return MA_ERR_ARG;
+  EvictPlanParams p{phys, pos, sphys_spos[0], sphys_spos[1], live, quantized_length, kgroup, need, tail_groups,
+                    recent_window, groups_before, encode, stage, counts, maxes};
+  return launch_evict_plan(p, lanes, (cudaStream_t)stream);
+}
+
 int ma_rebuild_remap(int B, int H, int old_len, int kgroup, const int64_t* groups_before, int g1,
                      const int64_t* encode, int m, const int64_t* groups_after, int g3, const int64_t* stage, int st,
                      int64_t* remap, void* stream) {

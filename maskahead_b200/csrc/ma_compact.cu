@@ -107,6 +107,117 @@ __global__ void __launch_bounds__(256) rebuild_remap_kernel(RemapParams p) {
 
 }  // namespace
 
+// The planning of a group-preserving rebuild after an eviction (session.py:303-356), one
+// CTA per lane. Live entry i (slot phys[i], position pos[i]) lies in key group
+// phys / kgroup when phys < ql; a group is kept whole when at least `need` live entries
+// lie in it (need 0: none is) and it is not one of the last tail_groups; an entry is
+// staged when it is not packed (phys >= ql) and among the recent_window newest positions
+// (pos >= the window's smallest); every other entry not in a kept group is re-encoded. The
+// kept groups ascend; the encoded and staged slots follow the live axis, which is position
+// order (the eviction state keeps it sorted: checked here, a lane out of order is counted
+// in maxes[3] and its lists are not meaningful). Lists are padded with -1 to their full
+// width; counts[lane] gets the three lengths and maxes[0..2] their maxima over lanes.
+constexpr int kPlanThreads = 1024;
+
+// exclusive prefix of `flag` over the block (every thread calls it), plus the block total
+__device__ __forceinline__ int block_scan(bool flag, int* warp_tot, int* total) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const unsigned m = __ballot_sync(0xffffffffu, flag);
+  const int in_warp = __popc(m & ((1u << lane) - 1u));
+  __syncthreads();                      // warp_tot free (a previous call's reads are done)
+  if (lane == 0) warp_tot[warp] = __popc(m);
+  __syncthreads();
+  if (warp == 0) {
+    const int v = lane < (int)(blockDim.x >> 5) ? warp_tot[lane] : 0;
+    int incl = v;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int u = __shfl_up_sync(0xffffffffu, incl, o);
+      if (lane >= o) incl += u;
+    }
+    warp_tot[lane] = incl - v;          // exclusive prefix of the warp totals
+    if (lane == 31) warp_tot[32] = incl;
+  }
+  __syncthreads();
+  *total = warp_tot[32];
+  return warp_tot[warp] + in_warp;
+}
+
+__global__ void __launch_bounds__(kPlanThreads) evict_plan_kernel(EvictPlanParams p) {
+  __shared__ int cnt[kEvictMaxGroups + 1];
+  __shared__ unsigned char keepg[kEvictMaxGroups];
+  __shared__ int warp_tot[33];
+  __shared__ int s_bad;
+  const int64_t lane = blockIdx.x;
+  const int32_t* phys = p.phys + lane * p.sphys;
+  const int64_t* pos = p.pos + lane * p.spos;
+  const int gk = p.kgroup, ql = p.ql, live = p.live;
+  const int ng = max(1, ql / gk);
+  for (int g = threadIdx.x; g <= ng; g += blockDim.x) cnt[g] = 0;
+  if (threadIdx.x == 0) s_bad = 0;
+  __syncthreads();
+  for (int i = threadIdx.x; i < live; i += blockDim.x) {
+    const int s = phys[i];
+    atomicAdd(&cnt[(s >= 0 && s < ql) ? s / gk : ng], 1);
+    if (i + 1 < live && pos[i + 1] <= pos[i]) s_bad = 1;
+  }
+  __syncthreads();
+  const int keep_to = ng - p.tail_groups;
+  for (int g = threadIdx.x; g < ng; g += blockDim.x) keepg[g] = (p.need > 0 && cnt[g] >= p.need && g < keep_to) ? 1 : 0;
+  __syncthreads();
+  // kept groups, ascending
+  int total, n_groups = 0;
+  for (int g0 = 0; g0 < ng; g0 += blockDim.x) {
+    const int g = g0 + threadIdx.x;
+    const bool f = g < ng && keepg[g];
+    const int at = block_scan(f, warp_tot, &total);
+    if (f) p.groups_before[lane * ng + n_groups + at] = g;
+    n_groups += total;
+  }
+  for (int k = n_groups + threadIdx.x; k < ng; k += blockDim.x) p.groups_before[lane * ng + k] = -1;
+  // the recent window's smallest position
+  const int w = min(p.recent_window, live);
+  const int64_t thr = w > 0 ? pos[live - w] : INT64_MAX;
+  int n_enc = 0, n_stg = 0;
+  for (int i0 = 0; i0 < live; i0 += blockDim.x) {
+    const int i = i0 + threadIdx.x;
+    bool enc = false, stg = false;
+    int s = -1;
+    if (i < live) {
+      s = phys[i];
+      const bool in_q = s >= 0 && s < ql;
+      const bool kept = in_q && keepg[s / gk];
+      stg = !in_q && pos[i] >= thr;
+      enc = !kept && !stg;
+    }
+    int tot_e, tot_s;
+    const int at_e = block_scan(enc, warp_tot, &tot_e);
+    if (enc) p.encode[lane * live + n_enc + at_e] = s;
+    const int at_s = block_scan(stg, warp_tot, &tot_s);
+    if (stg) p.stage[lane * live + n_stg + at_s] = s;
+    n_enc += tot_e;
+    n_stg += tot_s;
+  }
+  for (int k = n_enc + threadIdx.x; k < live; k += blockDim.x) p.encode[lane * live + k] = -1;
+  for (int k = n_stg + threadIdx.x; k < live; k += blockDim.x) p.stage[lane * live + k] = -1;
+  if (threadIdx.x == 0) {
+    p.counts[lane * 3 + 0] = n_groups;
+    p.counts[lane * 3 + 1] = n_enc;
+    p.counts[lane * 3 + 2] = n_stg;
+    atomicMax(&p.maxes[0], n_groups);
+    atomicMax(&p.maxes[1], n_enc);
+    atomicMax(&p.maxes[2], n_stg);
+    if (s_bad) atomicAdd(&p.maxes[3], 1);
+  }
+}
+
+int launch_evict_plan(const EvictPlanParams& p, int lanes, cudaStream_t st) {
+  if (cudaMemsetAsync(p.maxes, 0, 4 * sizeof(int32_t), st) != cudaSuccess) return MA_ERR_CUDA;
+  if (lanes == 0) return MA_OK;
+  evict_plan_kernel<<<lanes, kPlanThreads, 0, st>>>(p);
+  return cudaGetLastError() == cudaSuccess ? MA_OK : MA_ERR_CUDA;
+}
+
 int launch_rebuild_remap(const RemapParams& p, int lanes, cudaStream_t st) {
   if (lanes <= 0 || p.old_len <= 0) return MA_OK;
   rebuild_remap_kernel<<<lanes, 256, 0, st>>>(p);

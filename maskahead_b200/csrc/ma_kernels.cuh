@@ -155,6 +155,20 @@ struct RemapParams {
   int g1, g2, g3, m, st, kgroup, old_len, ql;
 };
 int launch_rebuild_remap(const RemapParams& p, int lanes, cudaStream_t st);
+// The index lists of a group-preserving rebuild after an eviction (ma_evict_plan).
+struct EvictPlanParams {
+  const int32_t* phys;   // [lanes][live] physical slot of each live entry
+  const int64_t* pos;    // [lanes][live] its position (increasing along the live axis)
+  int64_t sphys, spos;   // lane strides
+  int live, ql, kgroup, need, tail_groups, recent_window;
+  int64_t* groups_before;   // [lanes][ng]
+  int64_t* encode;          // [lanes][live]
+  int64_t* stage;           // [lanes][live]
+  int32_t* counts;          // [lanes][3]
+  int32_t* maxes;           // [4]: the three maxima over lanes, lanes out of position order
+};
+constexpr int kEvictMaxGroups = 8192;
+int launch_evict_plan(const EvictPlanParams& p, int lanes, cudaStream_t st);
 
 // device properties, cached per device
 int device_sm_count();

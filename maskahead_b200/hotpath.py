@@ -46,6 +46,7 @@ class Step0Result:
     mass: torch.Tensor | None            # [B, Hkv, n] prefix mass of the selection rows
     score: torch.Tensor | None           # [B, Hkv, n] value-aware score (value_aware only)
     compact: Prefix | None = None        # the read set's rows, gathered (gather=True only)
+    probe_mass: torch.Tensor | None = None   # [B, Hkv, n] merged probe's prefix mass (probe_blocks > 0)
 
 
 def dense_required(layer_idx: int, *, dense_prefix_layers: int, old_cache_len: int, topk: int,
@@ -96,7 +97,8 @@ def _needs_unpack(prefix: Prefix, batch: int, heads: int, head_dim: int, unpack)
 def fast_step0(query: torch.Tensor, prefix, current_key: torch.Tensor, current_value: torch.Tensor, *,
                query_indices, topk: int, value_aware: bool = True, scaling: float | None = None,
                select: bool = True, want_mass: bool = False, gather: bool = False,
-               compact_out: tuple[torch.Tensor, torch.Tensor] | None = None, unpack: bool | None = None) -> Step0Result:
+               compact_out: tuple[torch.Tensor, torch.Tensor] | None = None, unpack: bool | None = None,
+               probe_blocks: int = 0, block_size: int = 32, probe_rows: torch.Tensor | None = None) -> Step0Result:
     """Step 0 of one layer: attention output, mass, score and the read set (session.py:1403-1454).
 
     The read set is the top min(topk, live) slots by score (value_aware) or mass, dead
@@ -111,6 +113,16 @@ def fast_step0(query: torch.Tensor, prefix, current_key: torch.Tensor, current_v
     copy keeps the prefix's mask and lengths. unpack=False reads the packed prefix in place
     instead (_needs_unpack has the trade-off); either way the values read are the same
     bf16 numbers.
+
+    probe_blocks > 0 merges the lookahead probe into this pass (lookahead_merge,
+    eviction.py:125-128; session.py:1949-1960): query and the current keys/values hold
+    [block | probe_blocks blocks of block_size], one attention launch covers every row,
+    block-causal by block_size as the probe forward attends (session.py:2326: the block's
+    rows see only its own keys, probe block i the blocks <= i), the block's selection rows
+    (query_indices, positions < block_size) score and select as usual, and probe_mass is the
+    prefix mass of the probe rows (positions block_size.., or the device int32 probe_rows)
+    times probe_blocks (session.py:2331). That replaces the separate probe_attention pass
+    over the prefix.
     """
     prefix = as_prefix(prefix)
     if query.dtype == torch.bfloat16 and _needs_unpack(prefix, query.shape[0], current_key.shape[1], query.shape[3],
@@ -119,11 +131,18 @@ def fast_step0(query: torch.Tensor, prefix, current_key: torch.Tensor, current_v
     if prefix.n == 0:
         out, _ = splitk_attention(query, prefix, current_key, current_value, scaling=scaling)
         return Step0Result(out, None, None, None)
-    need_stats = select or want_mass
+    need_stats = select or want_mass or probe_blocks > 0
     out, stats = splitk_attention(query, prefix, current_key, current_value, scaling=scaling,
-                                  want_prefix=need_stats)
+                                  causal_block=block_size if probe_blocks > 0 else 0, want_prefix=need_stats)
     if not need_stats:
         return Step0Result(out, None, None, None)
+    probe_mass = None
+    if probe_blocks > 0:
+        rows = probe_rows if probe_rows is not None else list(range(block_size, query.shape[2]))
+        probe_mass, _ = prefix_scores(query, prefix, stats, rows, value=False, scaling=scaling)
+        probe_mass = probe_mass * probe_blocks
+        if not (select or want_mass):
+            return Step0Result(out, None, None, None, probe_mass=probe_mass)
     value = select and value_aware
     mass, score = prefix_scores(query, prefix, stats, query_indices, value=value, scaling=scaling)
     idx = None
@@ -135,7 +154,7 @@ def fast_step0(query: torch.Tensor, prefix, current_key: torch.Tensor, current_v
     compact = None
     if select and gather:
         compact = gather_read_set(prefix, idx, dtype=query.dtype, out=compact_out)
-    return Step0Result(out, idx, mass, score, compact)
+    return Step0Result(out, idx, mass, score, compact, probe_mass)
 
 
 def unpacked_prefix(prefix, batch: int, heads: int, head_dim: int) -> Prefix:

@@ -20,6 +20,7 @@ sequence's live length (ragged batches).
 
 from __future__ import annotations
 
+import math
 from dataclasses import dataclass
 
 import torch
@@ -445,3 +446,56 @@ def rebuild(prefix, groups_before: torch.Tensor, encode: torch.Tensor, groups_af
     out = Prefix(kq=kq, ks=ks, kz=kz, vq=vq, vs=vs, vz=vz, kf=kr, vf=vr, nq=ql, nf=st, kb=4, vb=4, kg=gk,
                  vg=src.vg, kmode=0)
     return out, remap
+
+
+def evict_plan(phys: torch.Tensor, pos: torch.Tensor, *, quantized_length: int, key_group: int = 32,
+               repack_below: float = 1.0, compaction: str = "lazy", recent_window: int = 64, tail: int = 0,
+               tail_stage: bool = False, cache_length: int | None = None):
+    """The index lists of the rebuild after an eviction (_evict_to, session.py:303-356), on
+    the device: phys [L,B,H,live] int32 (the live entries' slots) and pos [L,B,H,live]
+    (their positions, increasing along the live axis as the eviction state keeps them).
+
+    A key group with at least max(1, ceil(repack_below * key_group)) live entries is kept
+    whole (compaction "lazy"; none with "full"), the unadmitted tail's groups excepted;
+    staged entries among the recent_window newest positions stay staged; the others are
+    re-encoded. Returns (groups_before, encode, groups_after, stage) as [L,B,H,*] int64
+    padded with -1 to the largest count over lanes: the arguments of rebuild (and of the
+    reference's PackedKVCache.rebuild). The lists are built by one kernel; their widths
+    take one host read of three counts, as the reference's padding does
+    (session.py:323-325)."""
+    lib = _lib.lib()
+    if phys.ndim != 4 or pos.shape != phys.shape:
+        raise ValueError("phys and pos must be [L, B, H, live]")
+    if compaction not in ("lazy", "full"):
+        raise ValueError(f"compaction must be 'lazy' or 'full', got {compaction!r}")
+    L, B, H, live = phys.shape
+    lanes = L * B * H
+    dev = phys.device
+    gk, ql = int(key_group), int(quantized_length)
+    ng = max(1, ql // gk)
+    need = max(1, math.ceil(repack_below * gk)) if compaction == "lazy" else 0
+    tail_groups = tail // gk if tail and not tail_stage else 0
+    ph = phys.reshape(lanes, live).to(torch.int32).contiguous()
+    ps = pos.reshape(lanes, live).to(torch.int64).contiguous()
+    gb = torch.empty((lanes, ng), device=dev, dtype=torch.int64)
+    enc = torch.empty((lanes, live), device=dev, dtype=torch.int64)
+    stg = torch.empty((lanes, live), device=dev, dtype=torch.int64)
+    counts = torch.empty((lanes, 3), device=dev, dtype=torch.int32)
+    maxes = torch.empty(4, device=dev, dtype=torch.int32)
+    _lib.check("ma_evict_plan", lib.ma_evict_plan(
+        ph.data_ptr(), ps.data_ptr(), lanes, live, _lib.i64(live, live), ql, gk, need, tail_groups,
+        int(recent_window), gb.data_ptr(), enc.data_ptr(), stg.data_ptr(), counts.data_ptr(), maxes.data_ptr(),
+        _lib.stream_handle(dev)))
+    g1, m, st, bad = maxes.tolist()
+    if bad:
+        raise ValueError(f"{bad} lane(s) hold live entries out of position order")
+    groups_before = gb[:, :g1].reshape(L, B, H, g1)
+    encode = enc[:, :m].reshape(L, B, H, m)
+    stage = stg[:, :st].reshape(L, B, H, st)
+    groups_after = torch.empty((L, B, H, 0), device=dev, dtype=torch.int64)
+    if tail and tail_stage:
+        tail_slots = torch.arange(cache_length - tail, cache_length, device=dev).view(1, 1, 1, -1)
+        stage = torch.cat([stage, tail_slots.expand(L, B, H, tail)], -1)
+    elif tail:
+        groups_after = torch.arange(ng - tail_groups, ng, device=dev).expand(L, B, H, -1).contiguous()
+    return groups_before, encode, groups_after, stage

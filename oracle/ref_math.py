@@ -22,7 +22,7 @@ __all__ = [
     "value_score", "rescore_by_value", "order_keys", "topk_sorted", "topk_reference_torch",
     "dense_attention", "prefix_attention", "prefix_mass", "sdpa_compact", "gather_per_kv_head",
     "survivors_lookahead", "lookahead_score", "effective_topk",
-    "pages_to_contiguous", "compact_slots", "rebuild_channel",
+    "pages_to_contiguous", "compact_slots", "rebuild_channel", "evict_plan",
 ]
 
 
@@ -483,3 +483,71 @@ def rebuild_channel(arrays: dict, groups_before: torch.Tensor, encode: torch.Ten
     out["v_residual"] = compact_slots(vals, safe).masked_fill(dead, 0)
     remap.scatter_(-1, torch.where(stage >= 0, stage, old_len), torch.arange(st).view(1, 1, st).expand(B, H, st) + ql)
     return out, remap[..., :old_len]
+
+
+# ----------------------------------------------------------------- eviction planning
+def evict_plan(phys: torch.Tensor, pos: torch.Tensor, *, quantized_length: int, token_group: int = 32,
+               repack_below: float = 1.0, compaction: str = "lazy", recent_window: int = 64,
+               tail: int = 0, tail_stage: bool = False, cache_length: int | None = None):
+    """The index lists of a group-preserving rebuild after an eviction decision.
+
+    Restates the planning part of BitSieveSession._evict_to for a channel-mode packed cache
+    (session.py:303-356): phys / pos [L,B,H,live] are the live entries' physical slots and
+    positions (after EvictionState.compact). A key group with at least
+    max(1, ceil(repack_below * gk)) live entries is kept whole ("lazy"; none with
+    "full"), except the unadmitted tail's groups; staged entries (slot >= ql) among the
+    recent_window newest positions stay staged; every other live entry is re-encoded.
+    Returns (groups_before, encode, groups_after, stage) as [L,B,H,*] int64 padded with -1
+    to the largest count over lanes -- the arguments of PackedKVCache.rebuild. Encoded and
+    staged slots are ordered by position (then slot); the tail's slots are staged after
+    the others (cache.stage) or its groups placed after everything (tail_groups).
+    """
+    gk, ql = token_group, quantized_length
+    phys = phys.to(torch.int64)
+    posl = pos.to(torch.int64)
+    L, B, H, live = phys.shape
+    in_q = phys < ql
+    ng = max(1, ql // gk)
+    grp = torch.where(in_q, phys // gk, torch.full_like(phys, ng))
+    counts = torch.zeros((L, B, H, ng + 1), dtype=torch.int64)
+    counts.scatter_add_(-1, grp, torch.ones_like(grp))
+    counts = counts[..., :ng]
+    if compaction == "lazy":
+        need = max(1, int(math.ceil(repack_below * gk)))
+        keep_g = counts >= need
+    else:
+        keep_g = torch.zeros_like(counts, dtype=torch.bool)
+    tail_groups = 0
+    if tail and not tail_stage:
+        tail_groups = tail // gk
+        keep_g[..., ng - tail_groups:] = False
+    in_kept = in_q & keep_g.gather(-1, grp.clamp_max(ng - 1)) & (grp < ng)
+    w = min(recent_window, live)
+    if w:
+        thr = posl.topk(w, dim=-1).values.amin(-1, keepdim=True)
+    else:
+        thr = torch.full((L, B, H, 1), 1 << 60, dtype=torch.int64)
+    undecided = ~in_q & (posl >= thr)
+    encode = ~in_kept & ~undecided
+    big = 1 << 62
+
+    def packed(sel, key):
+        n = int(sel.sum(-1).max().item()) if sel.numel() else 0
+        k2 = torch.where(sel, key, big).sort(dim=-1).values[..., :n]
+        return torch.where(k2 >= big, -1, k2)
+
+    def slots_by_pos(sel):
+        k2 = packed(sel, posl * (1 << 24) + phys)
+        return torch.where(k2 < 0, -1, k2 % (1 << 24))
+
+    groups_before = packed(keep_g, torch.arange(ng).expand(L, B, H, ng))
+    enc = slots_by_pos(encode)
+    stage = slots_by_pos(undecided)
+    empty = torch.empty((L, B, H, 0), dtype=torch.int64)
+    groups_after = empty
+    if tail and tail_stage:
+        tail_slots = torch.arange(cache_length - tail, cache_length).view(1, 1, 1, -1).expand(L, B, H, tail)
+        stage = torch.cat([stage, tail_slots], -1)
+    elif tail:
+        groups_after = torch.arange(ng - tail_groups, ng).expand(L, B, H, -1)
+    return groups_before, enc, groups_after, stage

@@ -19,6 +19,8 @@ seeded inputs and records what the reference's own CPU (torch) path returns:
   eviction decision                                           cache.py:659-678, 342-365
 * PackedKVCache.rebuild (KIVI channel-mode keys: kept groups copied, sparse groups
   re-encoded, undecided slots staged in bf16)                 cache.py:236-335
+* BitSieveSession._evict_to planning a rebuild after an eviction (the group decision and
+  the index lists it hands to rebuild)                         runtime/session.py:270-361
 
 Outputs go to <case>.npz next to this script, with the SHA-256 of the inputs.
 """
@@ -281,8 +283,71 @@ def build_rebuild(seed: int = 23, L: int = 2, B: int = 1, H: int = 2, n: int = 3
     return res
 
 
+def build_evict(seed: int = 31, L: int = 2, B: int = 1, H: int = 2, n: int = 333, C: int = 190,
+                W: int = 40) -> dict:
+    """A channel-mode reference cache (288 quantized slots in 9 key groups, 45 staged), an
+    EvictionState whose live entries have increasing positions and physical slots that are
+    a near-identity permutation, then BitSieveSession._evict_to with per-lane survivor sets
+    (three whole key groups plus random entries, ascending) on a stub session. Records the
+    live entries' slots and positions after the eviction's compaction, the index lists
+    _evict_to hands to cache.rebuild, its remap and the live entries' new slots."""
+    g = torch.Generator().manual_seed(seed)
+    D, gk = 128, 32
+    quant = QuantizationConfig(key_mode="channel")
+    cache = PackedKVCache(num_layers=L, batch_size=B, num_kv_heads=H, head_dim=D, max_tokens=4096,
+                          quant=quant, device="cpu", backend="torch")
+    cache.begin_append(n)
+    for layer in range(L):
+        cache.stage_layer(layer, torch.randn(B, H, n, D, generator=g).to(torch.bfloat16),
+                          torch.randn(B, H, n, D, generator=g).to(torch.bfloat16))
+    cache.commit_append()
+    phys0 = torch.arange(n)
+    for _ in range(12):                                     # a few slots moved by earlier rebuilds
+        i, j = torch.randint(0, n, (2,), generator=g).tolist()
+        phys0[i], phys0[j] = phys0[j].clone(), phys0[i].clone()
+    positions = torch.arange(n) * 3 + 7
+    st = EvictionState(num_layers=L, batch_size=B, num_kv_heads=H, capacity=n, device="cpu")
+    st.append(positions, phys=phys0)
+    keep = torch.empty(L, B, H, C, dtype=torch.int64)
+    for lane in range(L * B * H):
+        whole = torch.randperm(8, generator=g)[:3]
+        forced = torch.cat([(phys0 // gk == int(x)).nonzero().flatten() for x in whole])
+        rest = torch.tensor([i for i in torch.randperm(n, generator=g).tolist() if i not in set(forced.tolist())])
+        keep.view(-1, C)[lane] = torch.cat([forced, rest[: C - forced.numel()]]).sort().values
+    captured = {}
+    orig = cache.rebuild
+
+    def rebuild(gb, enc, ga, stg):
+        captured.update(groups_before=gb.clone(), encode=enc.clone(), groups_after=ga.clone(), stage=stg.clone())
+        remap = orig(gb, enc, ga, stg)
+        captured["remap"] = remap.clone()
+        return remap
+
+    cache.rebuild = rebuild
+    compact = st.compact
+
+    def compact_and_record(k):
+        compact(k)
+        captured.update(phys=st.phys[..., : st.live].clone(), pos=st.pos[..., : st.live].clone())
+
+    st.compact = compact_and_record
+    cfg = EvictionConfig(policy="lookahead", recent_window=W, capacity_floor=C)
+    stub = types.SimpleNamespace(_eviction=st, config=types.SimpleNamespace(eviction=cfg), _attn_log=None,
+                                 _phys_compact=True, cache=cache, _next_position=cache.get_seq_length(),
+                                 trace=types.SimpleNamespace(add_counter=lambda *a, **k: None))
+    BitSieveSession._evict_to(stub, keep)
+    out = {key: val.numpy() for key, val in captured.items()}
+    out.update(keep=keep.numpy(), new_phys=st.phys[..., : st.live].numpy(), quantized_length=np.array(288),
+               recent_window=np.array(W), repack_below=np.array(cfg.repack_below), compaction=np.array(cfg.compaction))
+    return out
+
+
 def main() -> None:
     only = set(sys.argv[1:])
+    if "evict_channel" in only:
+        np.savez_compressed(HERE / "evict_channel.npz", **build_evict())
+        print("wrote evict_channel")
+        return
     for name in CASES:
         if only and name not in only:
             continue
@@ -297,6 +362,8 @@ def main() -> None:
     print("wrote compact_token, compact_bf16")
     np.savez_compressed(HERE / "rebuild_channel.npz", **build_rebuild())
     print("wrote rebuild_channel")
+    np.savez_compressed(HERE / "evict_channel.npz", **build_evict())
+    print("wrote evict_channel")
 
 
 if __name__ == "__main__":

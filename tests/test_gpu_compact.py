@@ -11,6 +11,9 @@
 
 from __future__ import annotations
 
+from pathlib import Path
+
+import numpy as np
 import pytest
 import torch
 
@@ -20,6 +23,7 @@ from test_oracle_golden import load_compact
 pytestmark = pytest.mark.gpu
 
 DEV = "cuda"
+GOLDEN = Path(__file__).resolve().parent / "golden"
 
 
 def _merge_layers(t: torch.Tensor) -> torch.Tensor:
@@ -241,3 +245,70 @@ def test_attention_after_compaction_equals_masked_attention(layout):
     want, _ = splitk_attention(q, as_prefix(src, mask=mask), kc, vc)
     torch.cuda.synchronize()
     torch.testing.assert_close(got.float(), want.float(), atol=2e-2, rtol=2e-2)
+
+
+def test_evict_plan_matches_reference():
+    """ma_evict_plan on the reference's own _evict_to case (evict_channel.npz): the same
+    kept groups, encoded and staged slots, bit for bit, and the remap ma_rebuild_remap
+    builds from them equals the reference rebuild's."""
+    from maskahead_b200._lib import i64, lib as get_lib
+    from maskahead_b200.layouts import evict_plan
+
+    g = dict(np.load(GOLDEN / "evict_channel.npz"))
+    gb, enc, ga, stg = evict_plan(torch.from_numpy(g["phys"]).to(DEV), torch.from_numpy(g["pos"]).to(DEV),
+                                  quantized_length=int(g["quantized_length"]), recent_window=int(g["recent_window"]),
+                                  repack_below=float(g["repack_below"]), compaction=str(g["compaction"]))
+    for got, key in ((gb, "groups_before"), (enc, "encode"), (ga, "groups_after"), (stg, "stage")):
+        np.testing.assert_array_equal(got.cpu().numpy(), g[key], err_msg=key)
+    L, B, H, old_len = g["remap"].shape
+    remap = torch.empty((L * B, H, old_len), dtype=torch.int64, device=DEV)
+    parts = [t.reshape(L * B, H, -1).contiguous() for t in (gb, enc, ga, stg)]
+    rc = get_lib().ma_rebuild_remap(L * B, H, old_len, 32, parts[0].data_ptr(), parts[0].shape[-1], parts[1].data_ptr(),
+                                    parts[1].shape[-1], parts[2].data_ptr(), parts[2].shape[-1], parts[3].data_ptr(),
+                                    parts[3].shape[-1], remap.data_ptr(), torch.cuda.current_stream().cuda_stream)
+    assert rc == 0
+    torch.cuda.synchronize()
+    np.testing.assert_array_equal(remap.cpu().numpy().reshape(g["remap"].shape), g["remap"])
+
+
+@pytest.mark.parametrize("mode", ["lazy", "full", "tail_groups", "tail_stage", "no_window"])
+def test_evict_plan_matches_oracle(mode):
+    """Larger lanes (2 x 2 x 4, 3000 live of 9000 slots, 280 key groups) against the
+    oracle's restatement: lazy and full compaction, a tail of unadmitted groups placed
+    after or staged, no recent window."""
+    from maskahead_b200.layouts import evict_plan
+
+    gen = torch.Generator().manual_seed(77)
+    L, B, H, n, live, ql = 2, 2, 4, 9000, 3000, 8960
+    lanes = L * B * H
+    phys = torch.empty(lanes, live, dtype=torch.int32)
+    for i in range(lanes):
+        base = torch.arange(n)
+        for _ in range(200):
+            a, b = torch.randint(0, n, (2,), generator=gen).tolist()
+            base[a], base[b] = base[b].clone(), base[a].clone()
+        whole = torch.randperm(ql // 32, generator=gen)[:12]
+        forced = torch.cat([(base // 32 == int(x)).nonzero().flatten() for x in whole])
+        fset = set(forced.tolist())
+        rest = torch.tensor([j for j in torch.randperm(n, generator=gen).tolist() if j not in fset][: live - forced.numel()])
+        sel = torch.cat([forced, rest]).sort().values
+        phys[i] = base[sel].to(torch.int32)
+    pos = (torch.arange(live) * 5 + 11).expand(lanes, live).contiguous().to(torch.int64)
+    phys, pos = phys.view(L, B, H, live), pos.view(L, B, H, live)
+    kw = dict(quantized_length=ql, recent_window=0 if mode == "no_window" else 64,
+              compaction="full" if mode == "full" else "lazy")
+    if mode.startswith("tail"):
+        kw.update(tail=64, tail_stage=mode == "tail_stage", cache_length=n)
+    got = evict_plan(phys.to(DEV), pos.to(DEV), **kw)
+    want = oracle.evict_plan(phys, pos, **kw)
+    for a, b, name in zip(got, want, ("groups_before", "encode", "groups_after", "stage")):
+        np.testing.assert_array_equal(a.cpu().numpy(), b.numpy(), err_msg=name)
+
+
+def test_evict_plan_rejects_positions_out_of_order():
+    from maskahead_b200.layouts import evict_plan
+
+    phys = torch.arange(200, dtype=torch.int32).view(1, 1, 1, 200)
+    pos = torch.arange(200, dtype=torch.int64).flip(-1).view(1, 1, 1, 200)
+    with pytest.raises(ValueError):
+        evict_plan(phys.to(DEV), pos.to(DEV), quantized_length=192)

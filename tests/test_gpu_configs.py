@@ -190,6 +190,44 @@ def test_cfg4_layer_block_step_and_retention():
                    pos.reshape(-1, n).numpy(), C, W, sinks)
 
 
+@pytest.mark.parametrize("probe_blocks,Hq,H", [(1, 28, 4), (2, 32, 8)], ids=["cfg2_probe1", "cfg4_probe2"])
+def test_merged_probe_step0(probe_blocks, Hq, H):
+    """lookahead_merge: step 0 over [block | probe blocks] in one launch, block-causal. The
+    block's rows select as usual (their keys: the block only), the probe rows' prefix mass
+    times the probe blocks, and the outputs of every row against the oracle's
+    prefix_attention(causal_block=32) + prefix_mass; the probe mass equals the separate
+    probe pass's (the same attention launch)."""
+    from maskahead_b200.hotpath import fast_step0, probe_attention
+    from maskahead_b200.layouts import Prefix
+
+    B, D, T, n, topk = 1, 128, 32, 8192, 1024
+    tp = T * (1 + probe_blocks)
+    scale = D ** -0.5
+    gen = torch.Generator().manual_seed(808 + probe_blocks)
+    k = torch.randn(B, H, n, D, generator=gen).to(torch.bfloat16)
+    v = torch.randn(B, H, n, D, generator=gen).to(torch.bfloat16)
+    q = torch.randn(B, Hq, tp, D, generator=gen).to(torch.bfloat16)
+    kc = torch.randn(B, H, tp, D, generator=gen).to(torch.bfloat16)
+    vc = torch.randn(B, H, tp, D, generator=gen).to(torch.bfloat16)
+    prefix = Prefix.dense(k.to(DEV), v.to(DEV))
+    rows = list(range(T))
+    res = fast_step0(q.to(DEV), prefix, kc.to(DEV), vc.to(DEV), query_indices=rows, topk=topk, scaling=scale,
+                     probe_blocks=probe_blocks, block_size=T)
+    _, sep = probe_attention(q.to(DEV), prefix, kc.to(DEV), vc.to(DEV), block_size=T, scaling=scale)
+    torch.cuda.synchronize()
+    want, (mp, lp, _) = oracle.prefix_attention(q, k, v, kc, vc, scale=scale, causal_block=T, q_pos0=0, c_pos0=0)
+    np.testing.assert_allclose(res.out.float().cpu().numpy(), want.float().numpy(), rtol=RTOL, atol=ATOL)
+    imp = oracle.prefix_mass(q, k, mp, lp, rows, scale=scale)
+    np.testing.assert_allclose(res.mass.cpu().numpy(), imp.numpy(), rtol=2e-5, atol=1e-9)
+    vs = oracle.rescore_by_value(imp, v)
+    np.testing.assert_allclose(res.score.cpu().numpy(), vs.numpy(), rtol=5e-5, atol=1e-9)
+    want_idx, _ = oracle.topk_sorted(vs, topk)
+    band_equal(res.indices.cpu().numpy(), want_idx.numpy(), vs.numpy(), topk)
+    pm = oracle.prefix_mass(q, k, mp, lp, list(range(T, tp)), scale=scale) * probe_blocks
+    np.testing.assert_allclose(res.probe_mass.cpu().numpy(), pm.numpy(), rtol=1e-4, atol=1e-9)
+    assert torch.equal(res.probe_mass, sep), "the merged probe mass is the separate pass's"
+
+
 def _paged_k4v4_batch(lens, H, D, page, seed):
     """Sequences quantized on the CPU by the oracle (token-mode keys with their own divisor,
     1% of the key channels x8 as outliers), their payloads scattered into a shuffled pool of

@@ -198,3 +198,18 @@ def test_rebuild_matches_reference():
         assert got[name].shape == want.shape, name
         assert torch.equal(got[name].contiguous().view(torch.uint8), want.contiguous().view(torch.uint8)), name
     assert torch.equal(remap, merge(f["remap"]))
+
+
+def test_oracle_evict_plan_matches_reference():
+    """The eviction planning of BitSieveSession._evict_to (session.py:303-356), recorded
+    from the reference on a channel-mode cache: the kept groups, the re-encoded and staged
+    slots in position order, and the live entries' slots after the reference's rebuild."""
+    g = _load("evict_channel")
+    gb, enc, ga, stg = oracle.evict_plan(torch.from_numpy(g["phys"]), torch.from_numpy(g["pos"]),
+                                         quantized_length=int(g["quantized_length"]),
+                                         recent_window=int(g["recent_window"]),
+                                         repack_below=float(g["repack_below"]), compaction=str(g["compaction"]))
+    for got, key in ((gb, "groups_before"), (enc, "encode"), (ga, "groups_after"), (stg, "stage")):
+        np.testing.assert_array_equal(got.numpy(), g[key], err_msg=key)
+    new_phys = torch.from_numpy(g["remap"]).gather(-1, torch.from_numpy(g["phys"]).long())
+    np.testing.assert_array_equal(new_phys.numpy(), g["new_phys"])
