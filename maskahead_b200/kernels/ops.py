@@ -2,7 +2,10 @@
 
 Drop-in counterparts of src/maskahead/kernels/ops.py in the reference, with the same
 signatures: ``selector_topk`` (333-521, 790-832), ``gather_packed_kv`` (570-662,
-835-855) and ``dense_packed_attention`` (130-264, 766-787). ``backend``,
+835-855), ``dense_packed_attention`` (130-264, 766-787) and the cache's quantizers
+``quantize_key_groups_into`` (665-712) and ``quantize_values_into`` (715-763); plus
+``sdpa_compact`` (src/maskahead/reference.py:403-426), the attention over a session's
+compact buffer. ``backend``,
 ``kernel_variant``, ``scratch`` and ``logits_dtype`` are accepted for compatibility and
 ignored: there is a single backend, logits never leave registers, and its scratch lives
 in per-device workspaces. There is no CPU path: without the built library or a CUDA
@@ -22,7 +25,8 @@ from ..layouts import LayerCacheView, Prefix, as_prefix, kv_descriptor
 from .splitk import prefix_scores, splitk_attention
 
 __all__ = ["KernelUnavailableError", "SelectorResult", "SelectorScratch", "selector_topk",
-           "gather_packed_kv", "dense_packed_attention", "select_topk_indices", "LayerCacheView"]
+           "gather_packed_kv", "dense_packed_attention", "select_topk_indices", "LayerCacheView",
+           "quantize_key_groups_into", "quantize_values_into", "sdpa_compact"]
 
 
 @dataclass(slots=True)
@@ -151,3 +155,78 @@ def dense_packed_attention(query: torch.Tensor, view, current_key: torch.Tensor,
     prefix = as_prefix(view) if length is None or length > 0 else Prefix()
     out, _ = splitk_attention(query, prefix, current_key, current_value, scaling=scaling)
     return out
+
+
+def sdpa_compact(query: torch.Tensor, key: torch.Tensor, value: torch.Tensor) -> torch.Tensor:
+    """softmax(q k^T / sqrt(D)) v over every key, no mask, GQA by head groups (reference.py:
+    403-426): the sub-step attention over a session's compact buffer [selected | block]."""
+    if query.ndim != 4 or key.ndim != 4 or key.shape != value.shape:
+        raise ValueError("Q/K/V must be rank-4 [B,H,T,D] with matching K and V")
+    if query.shape[1] % key.shape[1]:
+        raise ValueError("Hq must be divisible by Hkv")
+    out, _ = splitk_attention(query, Prefix.dense(key, value), None, None)
+    return out
+
+
+def _quant_outputs(payload: torch.Tensor, scale: torch.Tensor, zero: torch.Tensor, inner: tuple[int, ...]):
+    if scale.dtype != torch.float16 or zero.dtype != torch.float16 or payload.dtype != torch.uint8:
+        raise KernelUnavailableError("the sm_100a quantizers write uint8 payloads with float16 scale/zero "
+                                     "(quant.param_dtype = float16)")
+    if scale.stride() != zero.stride():
+        raise ValueError("scale and zero must share one layout")
+    if scale.stride(-1) != 1 or payload.stride(-1) != 1 or payload.stride(-2) != payload.shape[-1]:
+        raise ValueError("the innermost output dimensions must be contiguous")
+    if tuple(payload.shape[3:]) != inner:
+        raise ValueError(f"payload inner shape {tuple(payload.shape[3:])}, expected {inner}")
+
+
+def _quant_source(source: torch.Tensor, bits: int, group: int, what: str) -> torch.Tensor:
+    if bits != 4 or group != 32:
+        raise KernelUnavailableError(f"the sm_100a quantizers implement 4-bit {what} over groups of 32 "
+                                     f"(got bits={bits}, group={group})")
+    if source.ndim != 4 or not source.is_cuda or source.dtype not in (torch.bfloat16, torch.float32):
+        raise ValueError("source must be a bfloat16 or float32 CUDA tensor [B, H, t, D]")
+    return source if source.stride(-1) == 1 else source.contiguous()
+
+
+def quantize_key_groups_into(source: torch.Tensor, out_payload: torch.Tensor, out_scale: torch.Tensor,
+                             out_zero: torch.Tensor, *, bits: int, token_group: int, backend: str = "auto") -> None:
+    """KIVI keys: per channel over groups of token_group tokens, computed in the source's
+    dtype (reference.py:58-90), into payload [B,H,t/g,D,g*bits/8] u8 and scale/zero
+    [B,H,t/g,D] fp16 -- views into the cache (cache.py:499-517)."""
+    lib = _lib.lib()
+    x = _quant_source(source, bits, token_group, "keys")
+    b, h, t, d = x.shape
+    if t % token_group or tuple(out_payload.shape[:3]) != (b, h, t // token_group):
+        raise ValueError("invalid key quantization output geometry")
+    _quant_outputs(out_payload, out_scale, out_zero, (d, token_group * bits // 8))
+    if tuple(out_scale.shape) != (b, h, t // token_group, d):
+        raise ValueError("invalid key scale geometry")
+    if t == 0:
+        return
+    _lib.check("ma_quantize_keys_channel", lib.ma_quantize_keys_channel(
+        x.data_ptr(), _lib.dtype_code(x.dtype), b, h, t, d, _lib.i64(*x.stride()[:3]), token_group,
+        out_payload.data_ptr(), _lib.i64(*out_payload.stride()[:3]), out_scale.data_ptr(), out_zero.data_ptr(),
+        _lib.i64(*out_scale.stride()[:3]), _lib.stream_handle(x.device)))
+
+
+def quantize_values_into(source: torch.Tensor, out_payload: torch.Tensor, out_scale: torch.Tensor,
+                         out_zero: torch.Tensor, *, bits: int, channel_group: int, backend: str = "auto") -> None:
+    """Per token over groups of channel_group channels, computed in the source's dtype
+    (reference.py:182-213), into payload [B,H,t,D/g,g*bits/8] u8 and scale/zero
+    [B,H,t,D/g] fp16 -- values, and token-mode keys already divided by the channel
+    divisor (cache.py:482-540)."""
+    lib = _lib.lib()
+    x = _quant_source(source, bits, channel_group, "tokens")
+    b, h, t, d = x.shape
+    if d % channel_group or tuple(out_payload.shape[:3]) != (b, h, t):
+        raise ValueError("invalid value quantization output geometry")
+    _quant_outputs(out_payload, out_scale, out_zero, (d // channel_group, channel_group * bits // 8))
+    if tuple(out_scale.shape) != (b, h, t, d // channel_group):
+        raise ValueError("invalid value scale geometry")
+    if t == 0:
+        return
+    _lib.check("ma_quantize_tokens", lib.ma_quantize_tokens(
+        x.data_ptr(), _lib.dtype_code(x.dtype), b, h, t, d, _lib.i64(*x.stride()[:3]), None, None, channel_group,
+        out_payload.data_ptr(), _lib.i64(*out_payload.stride()[:3]), out_scale.data_ptr(), out_zero.data_ptr(),
+        _lib.i64(*out_scale.stride()[:3]), _lib.stream_handle(x.device)))

@@ -105,10 +105,11 @@ def prefix_scores(query, prefix, stats, q_rows, *, value: bool, scaling=None, **
     return mass, score
 
 
-def dequantize_prefix(prefix, b: int, hkv: int, d: int, dtype=torch.bfloat16, *, out=None, **_tuning):
+def dequantize_prefix(prefix, b: int, hkv: int, d: int, dtype=torch.bfloat16, block_n: int = 64, *, out=None):
     """The whole prefix as contiguous [B, Hkv, n, D] tensors (splitk.py:465-480): every slot
     dequantized (packed part) or copied (dense tail) in one launch; slots past lens[b] or on
-    a bad page are zeros. out = (key, value) buffers of that shape (optional)."""
+    a bad page are zeros. out = (key, value) buffers of that shape (optional). block_n (the
+    reference's Triton tile) is accepted and ignored."""
     lib = _lib.lib()
     prefix = as_prefix(prefix)
     n = prefix.n

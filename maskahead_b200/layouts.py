@@ -98,7 +98,8 @@ def as_prefix(view_or_prefix, mask=None) -> Prefix:
     elif hasattr(view_or_prefix, "k_bits"):
         p = Prefix.from_view(view_or_prefix)
     elif hasattr(view_or_prefix, "nq") and hasattr(view_or_prefix, "kf"):
-        p = Prefix(**{s: getattr(view_or_prefix, s) for s in Prefix.__slots__})
+        # another Prefix class with these fields (the reference's has no pages / lens)
+        p = Prefix(**{s: getattr(view_or_prefix, s) for s in Prefix.__slots__ if hasattr(view_or_prefix, s)})
     else:
         raise TypeError(f"expected a LayerCacheView or Prefix, got {type(view_or_prefix).__name__}")
     if mask is not None:
