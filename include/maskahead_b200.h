@@ -159,8 +159,11 @@ MA_API int ma_version(void);                       /* (major << 16) | minor     
 MA_API const char* ma_status_string(int status);
 /* Kernel choice for TMA-eligible dense bf16 calls (process-wide; for tests and A/B
  * timing): 0 = automatic (the TMA-pipelined attention and mass kernels), 1 = always the
- * general kernels (64-key attention tiles, cp.async-staged mass). Returns the previous
- * setting. Not part of the reference's interface.                                     */
+ * general kernels (64-key attention tiles, cp.async-staged mass), 2 = the pipelined
+ * attention with one 128-row M tile per CTA, 3 = with a pair of M tiles per CTA whenever
+ * a KV head has more than 128 query rows. Returns the previous setting. A workspace size
+ * queried under one setting may be too small under another. Not part of the reference's
+ * interface.                                                                          */
 MA_API int ma_set_attention_kernel(int which);
 /* 1 when the TMA-pipelined attention and scoring kernels read this prefix as it is stored
  * (dense bf16 without mask or paging; token-mode k4v4 without a dense tail or mask, its

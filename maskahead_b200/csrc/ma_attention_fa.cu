@@ -1,15 +1,18 @@
 // Split-K attention over [prefix | current block] for contiguous bf16 keys/values read by
-// TMA: one 128-row M tile per CTA, S double-buffered and P kept in tensor memory.
+// TMA: one 128-row M tile per CTA (or two, below), S double-buffered and P kept in tensor
+// memory.
 //
-// CTA = 8 softmax warps + 1 MMA/TMA warp over 128 query rows (r0..r0+127 of one KV head's
-// R = G*T rows, ordered g*T + t) and one key range (a split of the prefix, or the current
-// block). Keys come in tiles of 128: K and V each through 3 slots of 32 KB (a K slot is
-// refilled once its S was read, a V slot once its P.V completed). Tensor memory (512
+// CTA = 8 softmax warps, 1 MMA warp and 1 TMA warp over 128 query rows (r0..r0+127 of one
+// KV head's R = G*T rows, ordered g*T + t) and one key range (a split of the prefix, or the
+// current block). Keys come in tiles of 128: K and V each through 3 slots of 32 KB (a K
+// slot is refilled once its S was read, a V slot once its P.V completed: the MMA warp
+// releases the slot on kfree / vfree, the TMA warp issues the load -- a TMA issue can hold
+// its thread for hundreds of cycles, time the MMA issuer cannot give). Tensor memory (512
 // columns): S(t) = Q K(t)^T in buffer t&1 (columns [128(t&1), +128)), and two output
 // accumulators, O0 for the even tiles in [256, 384) and O1 for the odd ones in [384, 512).
 // Per tile t:
 //   MMA warp   S(t) = Q K(t)^T (8 MMAs 128x128x16, A = Q, B = K, K-major in shared memory),
-//              issued once K(t) is loaded and P.V(t-2) (whose P lives in the buffer) is done
+//              issued once K(t) is loaded and P.V(t-2) (whose P lives in the buffer) issued
 //   softmax    the four warps of group t&1 (warps 4(t&1)..+3), warp w holding rows 32(w&3)..
 //              and all 128 keys: the row max, lazy rescale of its O(t&1), P = 2^(u - m)
 //              rounded to bf16 written as bf16 pairs over S's columns 0..31 and 64..95
@@ -23,11 +26,20 @@
 // in ma_attention_tc.cu (fused into a cooperative launch when it is one pass).
 // Every wait is bounded. Semantics follow src/maskahead/kernels/splitk.py:115-190.
 //
+// Row-tile pairs (PAIR): with more than 128 rows per KV head (R = 224 for 28 query heads
+// over 4 KV heads and 32-row blocks) one CTA takes rows r0..r0+255 as two M tiles that
+// share every K and V tile: warp group g owns M tile g (S(u) for u = 2t + g in buffer g,
+// its own O accumulator in O_g, its own running max and sum), the MMA warp issues
+// S0(t) = Q0 K(t)^T, S1(t) = Q1 K(t)^T, P0 V(t), P1 V(t), and a K slot is refilled once
+// both S of its tile were consumed, a V slot once both P.V completed. Each K/V byte then
+// crosses into shared memory (and, for a packed prefix, is dequantized) once per head
+// instead of once per row tile; the slots shrink to three K and two V (Q takes 64 KB).
+//
 // Packed (token-mode k4v4) prefixes: the PACKED instantiation adds three producer warps
-// that build the K and V tiles from the packed bytes (ma_packed.cuh) instead of TMA loads;
-// the MMA warp hands them a slot by arriving on its kfree / vfree barrier where it would
-// have issued the slot's next TMA load, and they arrive on kfull / vfull (three arrivals)
-// once the slot's rows are stored. The current block stays TMA-fed.
+// that build the K and V tiles from the packed bytes (ma_packed.cuh) instead of TMA loads:
+// in place of the TMA warp they take the slots the MMA warp releases on kfree / vfree and
+// arrive on kfull / vfull (three arrivals) once the slot's rows are stored. The current
+// block stays TMA-fed (its loads issued by the MMA warp).
 #include <string.h>
 
 #include <algorithm>
@@ -47,14 +59,14 @@ using namespace tc;
 constexpr int kSoftWarps = 8;
 constexpr int kSoftThreads = kSoftWarps * 32;
 constexpr int kWarps = kSoftWarps + 1;
-constexpr int kThreads = kWarps * 32;
+constexpr int kThreads = kWarps * 32;              // the softmax and MMA warps (they take the merge rows)
+constexpr int kThreadsB = kThreads + 32;           // bf16 kernels: + the TMA warp
 constexpr int kRowTile = 128;                      // query rows per CTA (one M tile)
 constexpr int kBN = 128;                           // keys per tile
 constexpr int kD = 128;
 constexpr int kDqWarps = 3;                        // dequantizing producer warps (PACKED): 12 warps,
                                                    // three per SM sub-partition (168 registers each)
 constexpr int kDqThreads = kDqWarps * 32;
-constexpr int kDqItems = (2 * 128 + kDqThreads - 1) / kDqThreads;   // half rows per thread and array
 constexpr int kThreadsP = kThreads + kDqWarps * 32;
 constexpr int kStages = 3;                         // PACKED: staged raw tiles in flight (bulk copies)
 constexpr int kPackedSlots = 2;                    // PACKED: K and V slots each (the staging takes the rest)
@@ -69,6 +81,15 @@ constexpr int kKVBlock = kBN * 128;                // 16 KB: [128 rows][128 B]
 constexpr int kKVBytes = 2 * kKVBlock;             // a K or V tile: 32 KB
 constexpr int kSmemBytes = 1024 + kQBytes + (kKSlots + kVSlots) * kKVBytes;   // 225 KB
 constexpr int kSmemBytesP = 1024 + kQBytes + 2 * kPackedSlots * kKVBytes + kStages * packed::kStageBytes;   // 221 KB
+constexpr int kPairKSlots = 3;                     // PAIR: K tiles in flight (bf16)
+constexpr int kPairVSlots = 2;                     // PAIR: V tiles in flight (bf16)
+constexpr int kPairKSlotsP = 2;                    // PAIR + PACKED: K tiles in flight
+constexpr int kPairVSlotsP = 1;                    // PAIR + PACKED: V tiles in flight
+constexpr int kPairStages = 3;                     // PAIR + PACKED: staged raw tiles
+constexpr int kPgCache = 256;                      // PACKED: page-table entries kept in shared memory
+constexpr int kSmemBytes2 = 1024 + 2 * kQBytes + (kPairKSlots + kPairVSlots) * kKVBytes;   // 225 KB
+constexpr int kSmemBytesP2 =                                                               // 221 KB
+    1024 + 2 * kQBytes + (kPairKSlotsP + kPairVSlotsP) * kKVBytes + kPairStages * packed::kStageBytes;
 constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kColS = 0, kColO = 256;
 constexpr int kOutBox = 32 * 128;
@@ -173,21 +194,28 @@ __device__ __forceinline__ bool dq_wait(uint64_t* bar, uint32_t parity, volatile
   return __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
 }
 
-template <bool PACKED>
+template <bool PACKED, bool PAIR>
 __device__ __forceinline__ void attn_fa_body(const Args& A) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t* sQ = smem;                                   // [2 d blocks][128 rows][128 B]
-  constexpr int KS = PACKED ? kPackedSlots : kKSlots;   // K tiles in flight
-  constexpr int VS = PACKED ? kPackedSlots : kVSlots;   // V tiles in flight
-  uint8_t* sKs = sQ + kQBytes;                          // K slots
+  uint8_t* sQ = smem;                                   // per M tile: [2 d blocks][128 rows][128 B]
+  // K and V tiles in flight: the loads run two tiles ahead of the tensor core (PAIR: three
+  // K and two V slots beside 64 KB of Q; PAIR + PACKED: two and one, so that three raw
+  // tiles fit the staging ring, a V slot's next dequantization overlapping the next S)
+  constexpr int KS = PAIR ? (PACKED ? kPairKSlotsP : kPairKSlots) : PACKED ? kPackedSlots : kKSlots;
+  constexpr int VS = PAIR ? (PACKED ? kPairVSlotsP : kPairVSlots) : PACKED ? kPackedSlots : kVSlots;
+  constexpr int NST = PAIR ? kPairStages : kStages;     // PACKED: staged raw tiles
+  constexpr int kQT = PAIR ? 2 : 1;                     // M tiles per CTA
+  constexpr int kRows = kQT * kRowTile;                 // query rows per CTA
+  uint8_t* sKs = sQ + kQT * kQBytes;                    // K slots
   uint8_t* sVs = sKs + KS * kKVBytes;                   // V slots
   uint8_t* sStg = sVs + VS * kKVBytes;                  // PACKED: the staging ring of raw tiles
   __shared__ uint32_t s_taddr;
   __shared__ __align__(8) uint64_t kfull[KS], vfull[VS], s_full[2], p_full[2], o_done[2], q_full, mbar_fin;
-  __shared__ __align__(8) uint64_t kfree[PACKED ? kPackedSlots : 1], vfree[PACKED ? kPackedSlots : 1];
-  __shared__ __align__(8) uint64_t rfull[PACKED ? kStages : 1], rfree[PACKED ? kStages : 1];
+  __shared__ __align__(8) uint64_t kfree[KS], vfree[VS];
+  __shared__ __align__(8) uint64_t rfull[PACKED ? NST : 1], rfree[PACKED ? NST : 1];
   __shared__ __align__(16) float sKch[PACKED ? kD : 1];   // the packed keys' divisor of this (b, h)
+  __shared__ int sPg[PACKED ? kPgCache : 1];              // the page-table entries of [begin, end)
   __shared__ int s_abort, s_merge_ok;
 
   // grid (row tiles, splits, heads): the row tiles of one split run side by side, so the
@@ -199,13 +227,15 @@ __device__ __forceinline__ void attn_fa_body(const Args& A) {
   const int T = A.q.T;
   const int G = A.q.Hq / H;
   const int R = G * T;
-  const int r0 = blockIdx.x * kRowTile;
+  const int r0 = blockIdx.x * kRows;                     // the CTA's first row
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const bool softmax_warp = warp < kSoftWarps;
-  const int quarter = warp & 3, grp = (warp >> 2) & 1;   // rows 32*quarter.., the tiles t = grp mod 2
+  // rows 32*quarter.. of the M tile; single: the tiles t = grp mod 2, PAIR: M tile grp
+  const int quarter = warp & 3, grp = (warp >> 2) & 1;
+  const int rg0 = r0 + (PAIR ? kRowTile * grp : 0);      // this warp group's M tile
   const int rl = quarter * 32 + lane;
-  const int r = r0 + rl;
-  const int wrow0 = r0 + quarter * 32;
+  const int r = rg0 + rl;
+  const int wrow0 = rg0 + quarter * 32;
   const bool warp_rows = softmax_warp && wrow0 < R;      // the same for both warps of a pair
   const bool row_ok = softmax_warp && r < R;
   const int t_row = row_ok ? r % T : 0;
@@ -230,8 +260,20 @@ __device__ __forceinline__ void attn_fa_body(const Args& A) {
     vis_end = min(end, ((A.q_pos0 + t_row) / A.causal_block + 1) * A.causal_block - A.c_pos0);
   if (!row_ok) vis_end = begin;
   const int ntiles = end > begin ? (end - begin + kBN - 1) / kBN : 0;
+  const int nU = kQT * ntiles;   // S tiles: u = kQT t + M tile
   const float c2 = A.scale * kLog2e;
   const int group = bh * gridDim.x + blockIdx.x;
+
+  // PACKED paged prefix: the entries of the pages [begin, end) crosses, read once (the MMA
+  // warp's lanes) for the staging copies and the producers' row checks
+  const int pps = A.kv.pages ? A.kv.page_size : 1;
+  const int npg = (dq && A.kv.pages && end > begin) ? (end - 1) / pps - begin / pps + 1 : 0;
+  const packed::PageCache pc{sPg, begin / pps, npg <= kPgCache ? npg : 0};
+  if (dq && pc.n > 0 && warp == kSoftWarps) {
+    pdl_wait();
+    for (int i = lane; i < pc.n; i += 32) sPg[i] = A.kv.pages[(int64_t)b * A.kv.spg + pc.p0 + i];
+    __syncwarp();
+  }
 
   unsigned gen0 = 0;   // the merge generation, read after pdl_wait, before this CTA arrives (thread 0)
   if (threadIdx.x == kSoftThreads) {
@@ -242,10 +284,10 @@ __device__ __forceinline__ void attn_fa_body(const Args& A) {
     }
     for (int i = 0; i < KS; ++i) mbar_init(&kfull[i], dq ? kDqWarps : 1);
     for (int i = 0; i < VS; ++i) mbar_init(&vfull[i], dq ? kDqWarps : 1);
+    for (int i = 0; i < KS; ++i) mbar_init(&kfree[i], 1);
+    for (int i = 0; i < VS; ++i) mbar_init(&vfree[i], 1);
     if (PACKED) {
-      for (int i = 0; i < KS; ++i) mbar_init(&kfree[i], 1);
-      for (int i = 0; i < VS; ++i) mbar_init(&vfree[i], 1);
-      for (int i = 0; i < kStages; ++i) {
+      for (int i = 0; i < NST; ++i) {
         mbar_init(&rfull[i], 1);
         mbar_init(&rfree[i], kDqWarps);
       }
@@ -264,27 +306,31 @@ __device__ __forceinline__ void attn_fa_body(const Args& A) {
     pdl_wait();   // with a programmatic launch, the inputs may come from the kernel before
     const CUtensorMap* km = is_cur ? &A.ckmap : &A.kmap;
     const CUtensorMap* vm = is_cur ? &A.cvmap : &A.vmap;
-    tma::expect_tx(&q_full, (uint32_t)kQBytes);
-    if (A.q_mode == 1) {          // 128 consecutive positions of one query head
-      tma::load_4d(sQ, &A.qmap, 0, r0 % T, h * G + r0 / T, b, &q_full);
-      tma::load_4d(sQ + kQBlock, &A.qmap, 64, r0 % T, h * G + r0 / T, b, &q_full);
-    } else if (A.q_mode == 0) {   // 128 / T whole query heads
-      tma::load_4d(sQ, &A.qmap, 0, 0, h * G + r0 / T, b, &q_full);
-      tma::load_4d(sQ + kQBlock, &A.qmap, 64, 0, h * G + r0 / T, b, &q_full);
-    } else {                      // four 32-row pieces, each inside one query head
-      for (int i = 0; i < kRowTile / 32; ++i) {
-        const int rp = r0 + 32 * i;   // rows past R load neighbouring or zero rows: never used
-        tma::load_4d(sQ + i * 32 * 128, &A.qmap, 0, rp % T, h * G + rp / T, b, &q_full);
-        tma::load_4d(sQ + kQBlock + i * 32 * 128, &A.qmap, 64, rp % T, h * G + rp / T, b, &q_full);
+    tma::expect_tx(&q_full, (uint32_t)(kQT * kQBytes));
+    for (int qt = 0; qt < kQT; ++qt) {
+      const int rq = r0 + qt * kRowTile;   // rows past R load neighbouring or zero rows: never used
+      uint8_t* dQ = sQ + qt * kQBytes;
+      if (A.q_mode == 1) {          // 128 consecutive positions of one query head
+        tma::load_4d(dQ, &A.qmap, 0, rq % T, h * G + rq / T, b, &q_full);
+        tma::load_4d(dQ + kQBlock, &A.qmap, 64, rq % T, h * G + rq / T, b, &q_full);
+      } else if (A.q_mode == 0) {   // 128 / T whole query heads
+        tma::load_4d(dQ, &A.qmap, 0, 0, h * G + rq / T, b, &q_full);
+        tma::load_4d(dQ + kQBlock, &A.qmap, 64, 0, h * G + rq / T, b, &q_full);
+      } else {                      // four 32-row pieces, each inside one query head
+        for (int i = 0; i < kRowTile / 32; ++i) {
+          const int rp = rq + 32 * i;
+          tma::load_4d(dQ + i * 32 * 128, &A.qmap, 0, rp % T, h * G + rp / T, b, &q_full);
+          tma::load_4d(dQ + kQBlock + i * 32 * 128, &A.qmap, 64, rp % T, h * G + rp / T, b, &q_full);
+        }
       }
     }
     if (!dq) {
       for (int i = 0; i < KS && i < ntiles; ++i) tma_tile(km, b, h, begin + i * kBN, sKs + i * kKVBytes, &kfull[i]);
       for (int i = 0; i < VS && i < ntiles; ++i) tma_tile(vm, b, h, begin + i * kBN, sVs + i * kKVBytes, &vfull[i]);
     } else {   // the first raw tiles into the staging ring
-      for (int i = 0; i < kStages && i < ntiles; ++i)
+      for (int i = 0; i < NST && i < ntiles; ++i)
         packed::stage_tile(A.kv, b, h, begin + i * kBN, min(end, begin + (i + 1) * kBN), sStg + i * packed::kStageBytes,
-                           &rfull[i]);
+                           &rfull[i], pc);
     }
   }
   if (warp == 0) tmem_alloc(&s_taddr, kTmemCols);
@@ -298,20 +344,23 @@ __device__ __forceinline__ void attn_fa_body(const Args& A) {
   float m_run = -INFINITY, l_run = 0.f, m_true = -INFINITY;
 
   if (warp == kSoftWarps) {
-    // ------------------------------------------------------------ MMA / TMA warp
+    // ------------------------------------------------------------ MMA warp
     if (lane == 0) {
-      // Event loop: S(t) needs K(t) loaded and P.V(t-2) seen complete (P(t-2) lives in the
-      // buffer, and O(t&1) may be rescaled only after it); P.V(t) needs V(t) and the
-      // softmax's P(t). P.V completes in issue order, so oD counts completions over both
-      // o_done barriers alternately. A K slot takes its next tile once the S it held was
-      // consumed (its P.V issued), a V slot once its P.V completed. Each barrier has at most
-      // one completed but unobserved phase, so the parity tests are unambiguous.
+      // Event loop over the S tiles u (single: u = t; PAIR: u = 2t + M tile): S(u) needs
+      // K(t) loaded and P.V(u-2) issued -- P(u-2) lives in S(u)'s buffer, and tcgen05.mma
+      // operations of one thread execute in issue order, so S(u) overwrites P(u-2) only
+      // after P.V(u-2) read it (a softmax that rescales O(u&1) waits for P.V(u-2) itself);
+      // P.V(u) needs V(t) and the softmax's P(u). P.V completes in issue order, so oD
+      // counts completions over both o_done barriers alternately. A K slot takes its next
+      // tile once every S it fed was consumed (the tile's last P.V issued), a V slot once the
+      // tile's last P.V completed. Each barrier has at most one completed but unobserved
+      // phase, so the parity tests are unambiguous.
       bool ok = true;
       // the queries and the first min(3, ntiles) K and V tiles were issued at setup
       int kIss = min(KS, ntiles), kObs = 0, vIss = min(VS, ntiles), vObs = 0;
       int sN = 0, pN = 0, oD = 0;                   // S issued, P.V issued, P.V seen complete
       // PACKED: raw tiles staged, staged tiles seen consumed by the producer warps
-      int rIss = dq ? min(kStages, ntiles) : ntiles, rfObs = 0;
+      int rIss = dq ? min(NST, ntiles) : ntiles, rfObs = 0;
       const CUtensorMap* km = is_cur ? &A.ckmap : &A.kmap;
       const CUtensorMap* vm = is_cur ? &A.cvmap : &A.vmap;
       const bool q_ok = mbar_wait(&q_full, 0);
@@ -326,7 +375,7 @@ __device__ __forceinline__ void attn_fa_body(const Args& A) {
       uint64_t t_idle = 0;
       bool armed = false;
       int spins = 0;
-      while (ok && pN < ntiles) {
+      while (ok && pN < nU) {
         bool progress = false;
         if (kObs < kIss && mbar_test(&kfull[kObs % KS], (uint32_t)(kObs / KS) & 1u)) {
           ++kObs;
@@ -340,21 +389,22 @@ __device__ __forceinline__ void attn_fa_body(const Args& A) {
           ++oD;
           progress = true;
         }
-        if (sN < ntiles && kObs > sN && oD >= sN - 1) {
+        if (sN < nU && kObs > sN / kQT && pN >= sN - 1) {
           fence_after_sync();
-          const uint64_t bd0 = kdesc + (uint64_t)((sN % KS) * (kKVBytes / 16));
+          const uint64_t bd0 = kdesc + (uint64_t)(((sN / kQT) % KS) * (kKVBytes / 16));
+          const uint64_t qd0 = qdesc + (uint64_t)((sN % kQT) * (kQBytes / 16));
           const uint32_t dS = taddr + kColS + (sN & 1) * 128;
 #pragma unroll
           for (int kk = 0; kk < kD / 16; ++kk)
-            mma_bf16(dS, qdesc + (uint64_t)(((kk >> 2) * kQBlock + (kk & 3) * 32) >> 4),
+            mma_bf16(dS, qd0 + (uint64_t)(((kk >> 2) * kQBlock + (kk & 3) * 32) >> 4),
                      bd0 + (uint64_t)(((kk >> 2) * kKVBlock + (kk & 3) * 32) >> 4), idS, kk > 0);
           mma_commit(&s_full[sN & 1]);
           ++sN;
           progress = true;
         }
-        if (pN < sN && vObs > pN && mbar_test(&p_full[pN & 1], (uint32_t)(pN >> 1) & 1u)) {
+        if (pN < sN && vObs > pN / kQT && mbar_test(&p_full[pN & 1], (uint32_t)(pN >> 1) & 1u)) {
           fence_after_sync();
-          const uint64_t bd0 = vdesc + (uint64_t)((pN % VS) * (kKVBytes / 16));
+          const uint64_t bd0 = vdesc + (uint64_t)(((pN / kQT) % VS) * (kKVBytes / 16));
           const uint32_t aP = taddr + kColS + (pN & 1) * 128;
 #pragma unroll
           for (int kk = 0; kk < kBN / 16; ++kk)   // keys 16kk..: P columns 64 (kk / 4) + 8 (kk % 4)
@@ -366,27 +416,29 @@ __device__ __forceinline__ void attn_fa_body(const Args& A) {
         }
         // PACKED: a stage takes the next raw tile once the producer warps consumed its last
         if (dq) {
-          if (rfObs < rIss && mbar_test(&rfree[rfObs % kStages], (uint32_t)(rfObs / kStages) & 1u)) {
+          if (rfObs < rIss && mbar_test(&rfree[rfObs % NST], (uint32_t)(rfObs / NST) & 1u)) {
             ++rfObs;
             progress = true;
           }
-          if (rIss < ntiles && rfObs > rIss - kStages) {
+          if (rIss < ntiles && rfObs > rIss - NST) {
             packed::stage_tile(A.kv, b, h, begin + rIss * kBN, min(end, begin + (rIss + 1) * kBN),
-                               sStg + (rIss % kStages) * packed::kStageBytes, &rfull[rIss % kStages]);
+                               sStg + (rIss % NST) * packed::kStageBytes, &rfull[rIss % NST], pc);
             ++rIss;
             progress = true;
           }
         }
-        // a K slot is free once the S it held was consumed (P.V of that tile issued)
-        if (kIss < ntiles && pN > kIss - KS) {
-          if (dq) mbar_arrive(&kfree[kIss % KS]);   // the producer warps may refill it
+        // a K slot is free once the S it fed were consumed (the tile's last P.V issued); the
+        // TMA warp (bf16) or the producer warps (packed) refill it -- a TMA issue can stall
+        // its thread for hundreds of cycles, which this loop must not spend
+        if (kIss < ntiles && pN >= kQT * (kIss - KS + 1)) {
+          if (dq || !PACKED) mbar_arrive(&kfree[kIss % KS]);
           else tma_tile(km, b, h, begin + kIss * kBN, sKs + (kIss % KS) * kKVBytes, &kfull[kIss % KS]);
           ++kIss;
           progress = true;
         }
-        // a V slot is free once its P.V completed
-        if (vIss < ntiles && oD > vIss - VS) {
-          if (dq) mbar_arrive(&vfree[vIss % VS]);
+        // a V slot is free once the tile's last P.V completed
+        if (vIss < ntiles && oD >= kQT * (vIss - VS + 1)) {
+          if (dq || !PACKED) mbar_arrive(&vfree[vIss % VS]);
           else tma_tile(vm, b, h, begin + vIss * kBN, sVs + (vIss % VS) * kKVBytes, &vfull[vIss % VS]);
           ++vIss;
           progress = true;
@@ -412,22 +464,67 @@ __device__ __forceinline__ void attn_fa_body(const Args& A) {
       mma_commit(&mbar_fin);
       mbar_wait(&mbar_fin, 0, 20000000ull);
       if (!q_ok) mbar_wait(&q_full, 0, 20000000ull);
-      if (!dq) {   // TMA loads still in flight (the producer warps' stores end with them)
+      if (PACKED && !dq) {   // TMA loads still in flight (bf16: the TMA warp drains its own)
         for (int tt = kObs; tt < kIss; ++tt)
           mbar_wait(&kfull[tt % KS], (uint32_t)(tt / KS) & 1u, 20000000ull);
         for (int tt = vObs; tt < vIss; ++tt)
           mbar_wait(&vfull[tt % VS], (uint32_t)(tt / VS) & 1u, 20000000ull);
-      } else {     // bulk copies into the staging ring still in flight
+      } else if (dq) {   // bulk copies into the staging ring still in flight
         for (int tt = rfObs; tt < rIss; ++tt)
-          mbar_wait(&rfull[tt % kStages], (uint32_t)(tt / kStages) & 1u, 20000000ull);
+          mbar_wait(&rfull[tt % NST], (uint32_t)(tt / NST) & 1u, 20000000ull);
       }
+    }
+    __syncwarp();
+  } else if (!PACKED && warp == kSoftWarps + 1) {
+    // ------------------------------------------------------------ TMA warp (bf16)
+    // K tile t >= KS goes into slot t % KS once the MMA warp released it (kfree), V tile t
+    // into slot t % VS likewise (vfree); the first KS and VS were issued at setup. At most
+    // KS K and VS V loads are in flight at a time (a slot is released only after its tile
+    // was consumed), so at the end the last ones issued are waited for.
+    if (lane == 0) {
+      pdl_wait();   // with a programmatic launch, the cache may come from the kernel before
+      const CUtensorMap* km = is_cur ? &A.ckmap : &A.kmap;
+      const CUtensorMap* vm = is_cur ? &A.cvmap : &A.vmap;
+      int kN = min(KS, ntiles), vN = min(VS, ntiles);
+      uint64_t t_idle = 0;
+      bool armed = false;
+      int spins = 0;
+      while (kN < ntiles || vN < ntiles) {
+        bool progress = false;
+        if (kN < ntiles && mbar_test(&kfree[kN % KS], (uint32_t)((kN / KS) - 1) & 1u)) {
+          tma_tile(km, b, h, begin + kN * kBN, sKs + (kN % KS) * kKVBytes, &kfull[kN % KS]);
+          ++kN;
+          progress = true;
+        }
+        if (vN < ntiles && mbar_test(&vfree[vN % VS], (uint32_t)((vN / VS) - 1) & 1u)) {
+          tma_tile(vm, b, h, begin + vN * kBN, sVs + (vN % VS) * kKVBytes, &vfull[vN % VS]);
+          ++vN;
+          progress = true;
+        }
+        if (progress) {
+          spins = 0;
+          armed = false;
+        } else if (__nanosleep(kIdleNs), ++spins == 256) {   // idle: bounded like the MMA warp
+          spins = 0;
+          const uint64_t now = global_ns();
+          if (!armed) {
+            t_idle = now;
+            armed = true;
+          } else if (now - t_idle > kStallNs) {
+            s_abort = 1;
+          }
+          if (s_abort) break;
+        }
+      }
+      for (int x = max(0, kN - KS); x < kN; ++x) mbar_wait(&kfull[x % KS], (uint32_t)(x / KS) & 1u, 20000000ull);
+      for (int x = max(0, vN - VS); x < vN; ++x) mbar_wait(&vfull[x % VS], (uint32_t)(x / VS) & 1u, 20000000ull);
     }
     __syncwarp();
   } else if (PACKED && !softmax_warp) {
     // ------------------------------------------------------------ producer warps (PACKED)
-    // Tile t's raw rows arrive in stage t % kStages (rfull); its K items go into slot
-    // t % KS once the MMA warp released it (kfree; the first KS are free), its V items into
-    // slot t % VS likewise, then the stage is handed back (rfree). An item is (row, 32-channel
+    // Tile t's raw rows arrive in stage t % NST (rfull); its K items go into slot t % KS
+    // once the MMA warp released it (kfree; the first KS are free), its V items into slot
+    // t % VS likewise, then the stage is handed back (rfree). An item is (row, 32-channel
     // group), item it = dt + kDqThreads * i being group it & 3 of row it >> 2, so a warp
     // reads 512 consecutive staged bytes.
     if (dq) {
@@ -439,15 +536,23 @@ __device__ __forceinline__ void attn_fa_body(const Args& A) {
       constexpr int kItems = (kBN * 4 + kDqThreads - 1) / kDqThreads;
       for (int t = 0; t < ntiles; ++t) {
         const int j0 = begin + t * kBN;
-        const uint8_t* stg = sStg + (t % kStages) * packed::kStageBytes;
-        if (!dq_wait(&rfull[t % kStages], (uint32_t)(t / kStages) & 1u, &s_abort)) break;
+        const uint8_t* stg = sStg + (t % NST) * packed::kStageBytes;
+        // the tile's rows that exist (below end, on a page of the pool), one bit per row:
+        // four page-table lookups a lane, in parallel, instead of one per item
+        uint32_t okm[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) okm[i] = __ballot_sync(0xffffffffu, packed::row_ok(A.kv, b, j0 + 32 * i + lane, end, pc));
+        auto ok_row = [&](int row) {
+          const uint32_t m = row < 64 ? (row < 32 ? okm[0] : okm[1]) : (row < 96 ? okm[2] : okm[3]);
+          return ((m >> (row & 31)) & 1u) != 0;
+        };
+        if (!dq_wait(&rfull[t % NST], (uint32_t)(t / NST) & 1u, &s_abort)) break;
         if (t >= KS && !dq_wait(&kfree[t % KS], (uint32_t)((t / KS) - 1) & 1u, &s_abort)) break;
 #pragma unroll
         for (int i = 0; i < kItems; ++i) {
           const int it = dt + kDqThreads * i;
           if (it < kBN * 4)
-            packed::dequant_item<true>(stg, it >> 2, it & 3, packed::row_ok(A.kv, b, j0 + (it >> 2), end),
-                                       sKs + (t % KS) * kKVBytes, sKch);
+            packed::dequant_item<true>(stg, it >> 2, it & 3, ok_row(it >> 2), sKs + (t % KS) * kKVBytes, sKch);
         }
         fence_proxy_async();   // generic stores -> the tensor core's reads
         __syncwarp();
@@ -457,28 +562,29 @@ __device__ __forceinline__ void attn_fa_body(const Args& A) {
         for (int i = 0; i < kItems; ++i) {
           const int it = dt + kDqThreads * i;
           if (it < kBN * 4)
-            packed::dequant_item<false>(stg, it >> 2, it & 3, packed::row_ok(A.kv, b, j0 + (it >> 2), end),
-                                        sVs + (t % VS) * kKVBytes, nullptr);
+            packed::dequant_item<false>(stg, it >> 2, it & 3, ok_row(it >> 2), sVs + (t % VS) * kKVBytes, nullptr);
         }
         fence_proxy_async();
         __syncwarp();
         if (lane == 0) {
           mbar_arrive(&vfull[t % VS]);
-          mbar_arrive(&rfree[t % kStages]);   // the stage's raw rows are read
+          mbar_arrive(&rfree[t % NST]);   // the stage's raw rows are read
         }
       }
     }
   } else {
     // ------------------------------------------------------------ softmax warps
-    // warp (quarter, grp): rows 32 quarter.. of the tiles t = grp, grp + 2, ..., all 128 keys
-    // of each, with its own running max, row sum and O accumulator; the two warps that share
-    // a sub-partition work on different tiles, so one's exponentials overlap the other's
-    // tensor-memory reads, maxima and stores
+    // warp (quarter, grp): rows 32 quarter.. of the tiles t = grp, grp + 2, ... (PAIR: of
+    // M tile grp, every tile t), all 128 keys of each, with its own running max, row sum
+    // and O accumulator; the two warps that share a sub-partition work on different S
+    // tiles, so one's exponentials overlap the other's tensor-memory reads, maxima and
+    // stores
     pdl_wait();   // the partials and outputs may still be in use by the kernel before
     if (A.fuse && threadIdx.x == 0) gen0 = *reinterpret_cast<volatile const unsigned*>(&A.fm.sync[group].y);
     const float2 c2x2 = make_float2(c2, c2);
-    int k = 0;   // this warp's tiles done
-    for (int t = grp; t < ntiles; t += 2, ++k) {
+    const int nk = PAIR ? ntiles : (ntiles > grp ? (ntiles - grp + 1) / 2 : 0);   // this warp's S tiles
+    for (int k = 0; k < nk; ++k) {
+      const int t = PAIR ? k : grp + 2 * k;   // its k-th S tile reads K/V tile t
       const bool ok = mbar_wait(&s_full[grp], (uint32_t)k & 1u);
       fence_after_sync();
       if (!ok) s_abort = 1;
@@ -565,8 +671,8 @@ __device__ __forceinline__ void attn_fa_body(const Args& A) {
       __syncwarp();
       if (lane == 0) mbar_arrive(&p_full[grp]);
     }
-    if (ntiles > grp && !s_abort) {   // this warp's last P.V
-      if (!mbar_wait(&o_done[grp], (uint32_t)(((ntiles - 1 - grp) >> 1) & 1), kWaitNs)) s_abort = 1;
+    if (nk > 0 && !s_abort) {   // this warp's last P.V
+      if (!mbar_wait(&o_done[grp], (uint32_t)((nk - 1) & 1), kWaitNs)) s_abort = 1;
       fence_after_sync();
     }
   }
@@ -576,7 +682,80 @@ __device__ __forceinline__ void attn_fa_body(const Args& A) {
   fence_after_sync();
   if (threadIdx.x == 0) pdl_launch_dependents();   // the next kernel's prologue may start
 
-  if (softmax_warp) {
+  if (PAIR && softmax_warp) {
+    // each M tile's rows are final in their own group: o = O_g / l under the group's running
+    // max; warp (quarter, grp) writes all 128 channels of its 32 rows (the slots are
+    // drained: two output boxes per warp in the K and V slots, or the cluster's rows)
+    const int rc = r - r0;   // the row within the CTA
+    const int64_t prow = ((int64_t)bh * A.P.S + split) * A.P.Rp + r;
+    const int prow0 = (int)(((int64_t)bh * A.P.S + split) * A.P.Rp + wrow0);
+    float2* sML = reinterpret_cast<float2*>(sVs + 4096);   // cluster merge: this split's (m, l)
+    uint8_t* sO = sKs;                                     // cluster merge: its rows (64 KB)
+    if (s_abort != 0) {
+      if (threadIdx.x == 0) atomicExch(A.err, 1);
+      if (row_ok) {
+        if (A.cmerge) sML[rc] = make_float2(NAN, NAN);
+        else A.P.ml[prow] = make_float2(NAN, NAN);
+      }
+    } else {
+      if (row_ok) {
+        const float fix = (m_true == -INFINITY) ? 1.f : ex2(m_run - m_true * c2);
+        if (A.cmerge) sML[rc] = make_float2(m_true * A.scale, l_run * fix);
+        else A.P.ml[prow] = make_float2(m_true * A.scale, l_run * fix);
+      }
+      const float inv = l_run > 0.f ? 1.f / l_run : 0.f;
+      if (warp_rows) {
+        const bool via_tma = ntiles > 0 && A.tma_out && !A.cmerge;
+        uint8_t* box = sKs + warp * 2 * kOutBox;   // two 32-row boxes: channels 0..63, 64..127
+        uint4* dst = reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(A.P.o) + prow * kD);
+        const uint32_t tOg = taddr + lane_base + kColO + 128 * grp;
+#pragma unroll 1
+        for (int c = 0; c < 4; ++c) {
+          float o[32];
+          if (ntiles > 0) {
+            tmem_ld32(tOg + 32 * c, o);
+            tmem_ld_wait();
+#pragma unroll
+            for (int i = 0; i < 32; ++i) o[i] *= inv;
+          } else {
+#pragma unroll
+            for (int i = 0; i < 32; ++i) o[i] = 0.f;
+          }
+          if (A.cmerge) {   // the row into shared memory, chunk cc of row rc at cc ^ (rc & 15)
+#pragma unroll
+            for (int qq = 0; qq < 4; ++qq) {
+              const int cc = 4 * c + qq;
+              *reinterpret_cast<uint4*>(sO + rc * 256 + ((cc ^ (rc & 15)) << 4)) = float8_to_bf16x8(o + 8 * qq);
+            }
+          } else if (via_tma) {
+            uint8_t* line = box + (c >> 1) * kOutBox + lane * 128;
+#pragma unroll
+            for (int qq = 0; qq < 4; ++qq)
+              *reinterpret_cast<uint4*>(line + (((4 * (c & 1) + qq) ^ (lane & 7)) << 4)) = float8_to_bf16x8(o + 8 * qq);
+          } else if (row_ok) {
+#pragma unroll
+            for (int qq = 0; qq < 4; ++qq) dst[4 * c + qq] = float8_to_bf16x8(o + 8 * qq);
+          }
+        }
+        if (via_tma) {
+          fence_proxy_async();
+          __syncwarp();
+          if (lane == 0) {
+            tma::store_2d(&A.omap, 0, prow0, box);
+            tma::store_2d(&A.omap, 64, prow0, box + kOutBox);
+            tma::store_commit();
+            if (A.fuse) {   // other CTAs read these rows: complete, then order for generic loads
+              tma::store_wait_all();
+              asm volatile("fence.proxy.async.global;\n" ::: "memory");
+            } else {
+              tma::store_wait_read();
+            }
+          }
+          __syncwarp();
+        }
+      }
+    }
+  } else if (softmax_warp) {
     // the two tile groups' row states meet (the slots are drained: scratch in the V slots):
     // both are rescaled to the larger running max M, l = l0 f0 + l1 f1, o = (O0 f0 + O1 f1) / l;
     // warp (quarter, grp) writes channels 64 grp.. of its rows
@@ -681,7 +860,7 @@ __device__ __forceinline__ void attn_fa_body(const Args& A) {
     // ---- cluster merge: the group's splits are the cluster's CTAs (rank = split); each
     // merges its share of the rows from every rank's shared memory, by half warps
     cluster_sync();   // every split's rows and (m, l) are in its shared memory
-    const int R_blk = min(kRowTile, R - r0);
+    const int R_blk = min(kRows, R - r0);
     const int per = (R_blk + (int)gridDim.y - 1) / (int)gridDim.y;
     const int lo = split * per, hi = min(R_blk, lo + per);
     __nv_bfloat16* out = reinterpret_cast<__nv_bfloat16*>(A.fm.out);
@@ -727,7 +906,7 @@ __device__ __forceinline__ void attn_fa_body(const Args& A) {
   __syncthreads();
   // this split's share of the group's rows: a half warp per row with at most 16 prefix
   // splits, else a warp per row (weights scratch in the slots)
-  const int R_blk = min(kRowTile, R - r0);
+  const int R_blk = min(kRows, R - r0);
   const int per = (R_blk + (int)gridDim.y - 1) / (int)gridDim.y;
   const int lo = split * per, hi = min(R_blk, lo + per);
   __nv_bfloat16* out = reinterpret_cast<__nv_bfloat16*>(A.fm.out);
@@ -753,12 +932,23 @@ __device__ __forceinline__ void attn_fa_body(const Args& A) {
   }
 }
 
-// The bf16 kernel (288 threads) and the PACKED one (384 threads: 12 warps, three on each SM
-// sub-partition, whose quarter of the register file leaves 168 registers a thread).
-__global__ void __launch_bounds__(kThreads, 1) attn_partial_fa(const __grid_constant__ Args A) { attn_fa_body<false>(A); }
-__global__ void __launch_bounds__(kThreadsP, 1) attn_partial_fa_packed(const __grid_constant__ Args A) {
-  attn_fa_body<true>(A);
+// The bf16 kernels (320 threads: softmax, MMA and TMA warps) and the PACKED ones (384
+// threads: 12 warps, three on each SM sub-partition, whose quarter of the register file
+// leaves 168 registers a thread), for one M tile per CTA or a pair.
+__global__ void __launch_bounds__(kThreadsB, 1) attn_partial_fa(const __grid_constant__ Args A) {
+  attn_fa_body<false, false>(A);
 }
+__global__ void __launch_bounds__(kThreadsP, 1) attn_partial_fa_packed(const __grid_constant__ Args A) {
+  attn_fa_body<true, false>(A);
+}
+__global__ void __launch_bounds__(kThreadsB, 1) attn_partial_fa_pair(const __grid_constant__ Args A) {
+  attn_fa_body<false, true>(A);
+}
+__global__ void __launch_bounds__(kThreadsP, 1) attn_partial_fa_pair_packed(const __grid_constant__ Args A) {
+  attn_fa_body<true, true>(A);
+}
+
+int g_pairs = 0;   // fa_set_pairs
 
 
 bool tma_map_rows(CUtensorMap* map, const void* base, int B, int H, int n, const int64_t s[3]) {
@@ -772,7 +962,15 @@ bool tma_map_rows(CUtensorMap* map, const void* base, int B, int H, int n, const
 }  // namespace
 
 int fa_key_tile() { return kBN; }
-int fa_row_tile() { return kRowTile; }
+void fa_set_pairs(int mode) { g_pairs = mode; }
+int fa_row_tile(int R, int BH) {
+  // automatic: pairs when the (KV head, M tile) units alone fill the GPU (a serving batch),
+  // so that sharing each K/V tile between two M tiles does not cost parallelism; below
+  // that, one M tile per CTA and more splits (a single long sequence)
+  const bool many = (long long)BH * ((R + kRowTile - 1) / kRowTile) > device_sm_count();
+  const bool pair = g_pairs == 2 || (g_pairs == 0 && many);
+  return pair && R > kRowTile ? 2 * kRowTile : kRowTile;
+}
 
 bool fa_eligible(const ma_rows& q, const ma_kv& kv, const int64_t* idx, const ma_block& cur, int n_keys) {
   const bool dense_ok = kv.layout == MA_KV_DENSE && kv.dtype == MA_BF16 && !kv.mask && !kv.pages;
@@ -792,7 +990,11 @@ int launch_attn_partial_fa(const ma_rows& q, const ma_kv& kv, int H, const ma_bl
   if (!fa_eligible(q, kv, nullptr, cur, n_keys) || !(scale > 0.f) || !P.o_bf16 || split_len % kBN != 0)
     return MA_ERR_UNSUPPORTED;
   const bool packed = n_keys > 0 && kv.layout == MA_KV_PACKED_TOKEN;
-  const int threads = packed ? kThreadsP : kThreads;
+  const int threads = packed ? kThreadsP : kThreadsB;
+  const int G = q.Hq / H;
+  const int R = G * q.T;
+  const int rows = fa_row_tile(R, q.B * H);   // the plan's row blocks: one M tile per CTA or a pair
+  const bool pair = rows > kRowTile;
   Args A;
   memset(&A, 0, sizeof(A));
   A.q = q;
@@ -822,18 +1024,18 @@ int launch_attn_partial_fa(const ma_rows& q, const ma_kv& kv, int H, const ma_bl
                              (uint32_t)(A.q_mode == 0 ? kRowTile / q.T : 1), 1};
     if (!make_tma_map_bf16_4d(&A.qmap, q.q, dims, strides, box)) return MA_ERR_UNSUPPORTED;
   }
-  const int G = q.Hq / H;
-  const int R = G * q.T;
   // partial rows [BH * S * Rp][D] bf16, stored by 32-row x 64-channel boxes
   const uint64_t prow_total = (uint64_t)q.B * H * P.S * P.Rp;
   A.tma_out = (P.Rp % 32 == 0 && prow_total < (1ull << 31) &&
                make_tma_map_2d(&A.omap, true, P.o, kD, prow_total, kD * 2, 64, 32)) ? 1 : 0;
-  dim3 grid((R + kRowTile - 1) / kRowTile, P.S, q.B * H);
-  auto kernel = packed ? attn_partial_fa_packed : attn_partial_fa;
-  const int smem = packed ? kSmemBytesP : kSmemBytes;
+  dim3 grid((R + rows - 1) / rows, P.S, q.B * H);
+  const int kid = (packed ? 1 : 0) + (pair ? 2 : 0);
+  auto kernel = pair ? (packed ? attn_partial_fa_pair_packed : attn_partial_fa_pair)
+                     : (packed ? attn_partial_fa_packed : attn_partial_fa);
+  const int smem = pair ? (packed ? kSmemBytesP2 : kSmemBytes2) : (packed ? kSmemBytesP : kSmemBytes);
   if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
     return MA_ERR_CUDA;
-  const int rows_per_split = (std::min(kRowTile, R) + (int)grid.y - 1) / (int)grid.y;
+  const int rows_per_split = (std::min(rows, R) + (int)grid.y - 1) / (int)grid.y;
   // cluster merge: with at most 16 splits (prefix ones + the block) a group's CTAs form one
   // thread-block cluster and merge through distributed shared memory (no global round
   // trips); the hardware co-schedules a cluster's CTAs, so no cooperative launch is needed.
@@ -841,8 +1043,8 @@ int launch_attn_partial_fa(const ma_rows& q, const ma_kv& kv, int H, const ma_bl
   // that many free SMs in one GPC, so fewer clusters than SMs / size fit (a second wave
   // of clusters cost more than the merge saves)
   if (fm != nullptr && nsplit <= 16 && (int)grid.y <= 16 && rows_per_split <= 2 * kWarps) {
-    static int cluster_nc_of[2][17] = {{0}};   // per kernel and cluster size: resident clusters (-1: none)
-    int* cluster_nc = cluster_nc_of[packed ? 1 : 0];
+    static int cluster_nc_of[4][17] = {{0}};   // per kernel and cluster size: resident clusters (-1: none)
+    int* cluster_nc = cluster_nc_of[kid];
     const int cs = (int)grid.y;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = grid;
@@ -915,3 +1117,4 @@ int launch_attn_partial_fa(const ma_rows& q, const ma_kv& kv, int H, const ma_bl
 }
 
 }  // namespace ma
+

@@ -125,7 +125,7 @@ int key_tile(bool mma) { return mma ? tc_key_tile() : simt_key_tile(); }
 // than a few key tiles -- each split pays for staging its rows and writing R x D partials.
 Plan plan_splits(int BH, int R, int n, int Tc, bool mma, bool fa = false) {
   Plan p;
-  const int rt = fa ? fa_row_tile() : row_tile(mma), kt = fa ? fa_key_tile() : key_tile(mma);
+  const int rt = fa ? fa_row_tile(R, BH) : row_tile(mma), kt = fa ? fa_key_tile() : key_tile(mma);
   const int row_blocks = (R + rt - 1) / rt;
   // tensor-core partial rows are stored per 32-row warp box
   p.Rp = mma ? ((R + 31) / 32) * 32 : row_blocks * rt;
@@ -286,7 +286,8 @@ int ma_kv_read_in_place(const ma_kv* kv, int D) {
 
 int ma_set_attention_kernel(int which) {
   const int prev = g_attention_kernel;
-  g_attention_kernel = (which == 1) ? 1 : 0;
+  g_attention_kernel = (which >= 1 && which <= 3) ? which : 0;
+  fa_set_pairs(g_attention_kernel == 2 ? 1 : g_attention_kernel == 3 ? 2 : 0);
   return prev;
 }
 

@@ -43,11 +43,14 @@ int tc_key_tile();
 // ma_attention_fa.cu (TMA-fed bf16: the dense prefix without a read set, mask or paging,
 // and the current block; 128-row x 128-key tiles, S double-buffered and P in tensor
 // memory). split_len must be a multiple of fa_key_tile() and the plan's row blocks are
-// fa_row_tile() rows; MA_ERR_UNSUPPORTED when the call is not TMA-eligible (the caller
-// then uses launch_attn_partial_tc).
+// fa_row_tile(R, B*H) rows (128, or 256 when a CTA takes a pair of M tiles);
+// MA_ERR_UNSUPPORTED when the call is not TMA-eligible (the caller then uses
+// launch_attn_partial_tc). fa_set_pairs: 0 = automatic, 1 = one M tile per CTA, 2 = pairs
+// whenever R > 128.
 bool fa_eligible(const ma_rows& q, const ma_kv& kv, const int64_t* idx, const ma_block& cur, int n_keys);
 int fa_key_tile();
-int fa_row_tile();
+int fa_row_tile(int R, int BH);
+void fa_set_pairs(int mode);
 int launch_attn_partial_fa(const ma_rows& q, const ma_kv& kv, int H, const ma_block& cur, float scale,
                            int causal_block, int q_pos0, int c_pos0, int n_keys, int split_len, int nsplit,
                            const Partials& P, int* err, const FusedMerge* fm, bool* fused, cudaStream_t st);

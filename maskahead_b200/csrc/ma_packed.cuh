@@ -22,8 +22,9 @@
 //   * rows past the sequence's end (or on a page outside the pool) are written as zeros.
 //
 // Raw rows reach shared memory by bulk copies (cp.async.bulk, completion on an mbarrier)
-// that one thread issues a few tiles ahead into a staging ring (stage_tile); the producer
-// warps then turn a staged tile into bf16 tiles (dequant_item). Kernels that keep raw rows
+// that one thread issues a few tiles ahead into a staging ring (stage_tile, the page-table
+// entries of the CTA's range read once into shared memory: PageCache); the producer warps
+// then turn a staged tile into bf16 tiles (dequant_item). Kernels that keep raw rows
 // in registers instead (the value pass of the mass kernel) read them with load_row.
 #pragma once
 
@@ -140,6 +141,27 @@ __device__ __forceinline__ void bulk_copy(void* dst, const void* src, uint32_t b
                : "memory");
 }
 
+// The page-table entries of a CTA's key range, copied to shared memory once: pages
+// p0 .. p0 + n - 1 of the CTA's sequence (n = 0: none cached). A lookup outside them reads
+// the global table.
+struct PageCache {
+  const int* s;
+  int p0, n;
+};
+__device__ __forceinline__ bool locate(const ma_kv& kv, int b, int j, int& sb, int& sj, const PageCache& pc) {
+  if (kv.pages != nullptr) {
+    const int pi = j / kv.page_size;
+    const int k = pi - pc.p0;
+    if (k >= 0 && k < pc.n) {
+      const int p = pc.s[k];
+      sb = (p >= 0 && p < kv.num_pages) ? p : -1;
+      sj = j - pi * kv.page_size;
+      return sb >= 0;
+    }
+  }
+  return locate(kv, b, j, sb, sj);
+}
+
 // The copies of rows [j0, j1) of head h of sequence b into a staging stage: one set of six
 // (K and V payloads, scales, zeros) per storage segment (one per page crossed), each
 // segment's row count rounded up to even so every scale/zero copy is a multiple of 16 bytes
@@ -148,12 +170,12 @@ __device__ __forceinline__ void bulk_copy(void* dst, const void* src, uint32_t b
 // the copies are issued, completing on `bar` (whose transaction count the caller set).
 template <bool ISSUE>
 __device__ __forceinline__ uint32_t stage_copies(const ma_kv& kv, int b, int h, int j0, int j1, uint8_t* stg,
-                                                 uint64_t* bar) {
+                                                 uint64_t* bar, const PageCache& pc) {
   uint32_t total = 0;
   for (int j = j0; j < j1;) {
     const int seg_end = kv.pages ? min(j1, (j / kv.page_size + 1) * kv.page_size) : j1;
     int sb, sj;
-    if (locate(kv, b, j, sb, sj)) {
+    if (locate(kv, b, j, sb, sj, pc)) {
       int cnt = seg_end - j;
       const int avail = kv.pages ? kv.page_size - sj : kv.nq - j;
       cnt = min(cnt + (cnt & 1), avail);
@@ -179,18 +201,18 @@ __device__ __forceinline__ uint32_t stage_copies(const ma_kv& kv, int b, int h, 
 
 // Stage rows [j0, j1): the transaction count, then the copies (one issuing thread).
 __device__ __forceinline__ void stage_tile(const ma_kv& kv, int b, int h, int j0, int j1, uint8_t* stg,
-                                           uint64_t* bar) {
-  const uint32_t bytes = stage_copies<false>(kv, b, h, j0, j1, stg, bar);
+                                           uint64_t* bar, const PageCache& pc) {
+  const uint32_t bytes = stage_copies<false>(kv, b, h, j0, j1, stg, bar, pc);
   asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%1], %0;\n" ::"r"(bytes), "r"(tc::smem_addr(bar))
                : "memory");
-  stage_copies<true>(kv, b, h, j0, j1, stg, bar);
+  stage_copies<true>(kv, b, h, j0, j1, stg, bar, pc);
 }
 
 // Whether slot j of sequence b holds a row the tiles must carry (below end, on a page of
 // the pool); the others are written as zeros.
-__device__ __forceinline__ bool row_ok(const ma_kv& kv, int b, int j, int end) {
+__device__ __forceinline__ bool row_ok(const ma_kv& kv, int b, int j, int end, const PageCache& pc) {
   int sb, sj;
-  return j < end && locate(kv, b, j, sb, sj);
+  return j < end && locate(kv, b, j, sb, sj, pc);
 }
 
 __device__ __forceinline__ float2 fmul2(float2 a, float2 b) {

@@ -1,7 +1,9 @@
 """GPU parity of the 128-key-tile attention kernel (TMA-fed dense bf16 prefix and current
 block) and of the 64-key-tile kernel it replaces there, against the CPU oracle.
 
-Both kernels are run on the same inputs (``ma_set_attention_kernel``) and compared with
+The pipelined kernel runs with one 128-row M tile per CTA and with a pair of M tiles per
+CTA sharing the K/V tiles (R > 128), and the 64-key kernel on the same inputs
+(``ma_set_attention_kernel`` 2, 3 and 1); each is compared with
 ``oracle.prefix_attention`` at the bf16 bar of the other attention tests (atol = rtol =
 2e-2: bf16 output rounding plus the bf16 P operand of P.V); the prefix-only statistics
 (max, sum, normalized output) are compared the same way. The sizes cover: an empty prefix,
@@ -71,7 +73,7 @@ def test_fa_kernel_matches_oracle_and_tc(B, Hq, H, T, n, Tc, causal):
     want, (mp, lp, op) = oracle.prefix_attention(q, k, v, kc, vc, causal_block=causal, q_pos0=q_pos0, c_pos0=0)
     dev = [x.to(DEV) for x in (q, k, v, kc, vc)]
     outs = {}
-    for which in (0, 1):
+    for which in (2, 3, 1):
         out, st = _run(which, *dev, causal, q_pos0, 0, n > 0)
         np.testing.assert_allclose(out.float().cpu().numpy(), want.float().numpy(), rtol=TOL, atol=TOL,
                                    err_msg=f"kernel {which}")
@@ -80,14 +82,19 @@ def test_fa_kernel_matches_oracle_and_tc(B, Hq, H, T, n, Tc, causal):
             np.testing.assert_allclose(st[1].cpu().numpy(), lp.numpy(), rtol=TOL, atol=TOL)
             np.testing.assert_allclose(st[2].cpu().numpy(), op.numpy(), rtol=TOL, atol=TOL)
         outs[which] = out.float().cpu()
-    # the two kernels differ only in summation order and the lazy-rescale reference
-    np.testing.assert_allclose(outs[0].numpy(), outs[1].numpy(), rtol=TOL, atol=TOL)
+    # the kernels differ only in summation order and the lazy-rescale reference (a pair's
+    # warp group takes every key tile of its rows, one M tile's two groups alternate tiles
+    # and merge, and the pair's plan has twice the splits)
+    np.testing.assert_allclose(outs[2].numpy(), outs[1].numpy(), rtol=TOL, atol=TOL)
+    np.testing.assert_allclose(outs[3].numpy(), outs[2].numpy(), rtol=TOL, atol=TOL)
 
 
-def test_fa_kernel_large_logits_rescale():
-    """Logits growing along the keys force the lazy rescale of O on nearly every tile."""
+@pytest.mark.parametrize("which,Hq", [(2, 8), (3, 16)])
+def test_fa_kernel_large_logits_rescale(which, Hq):
+    """Logits growing along the keys force the lazy rescale of O on nearly every tile (one
+    M tile per CTA, and a pair: R = 256)."""
     gen = torch.Generator().manual_seed(7)
-    B, Hq, H, T, n, D = 1, 8, 2, 32, 3000, 128
+    B, H, T, n, D = 1, 2, 32, 3000, 128
     q = torch.randn(B, Hq, T, D, generator=gen).to(torch.bfloat16)
     ramp = torch.linspace(0.0, 6.0, n)[None, None, :, None]
     k = (torch.randn(B, H, n, D, generator=gen) * 0.5 + ramp * q.float().mean(dim=(1, 2))[:, None, None, :].sign())
@@ -96,7 +103,7 @@ def test_fa_kernel_large_logits_rescale():
     kc = torch.randn(B, H, T, D, generator=gen).to(torch.bfloat16)
     vc = torch.randn(B, H, T, D, generator=gen).to(torch.bfloat16)
     want, _ = oracle.prefix_attention(q, k, v, kc, vc, causal_block=32)
-    out, _ = _run(0, *[x.to(DEV) for x in (q, k, v, kc, vc)], 32, 0, 0, False)
+    out, _ = _run(which, *[x.to(DEV) for x in (q, k, v, kc, vc)], 32, 0, 0, False)
     np.testing.assert_allclose(out.float().cpu().numpy(), want.float().numpy(), rtol=TOL, atol=TOL)
 
 

@@ -99,8 +99,20 @@ CASES = [
 ]
 
 
+@pytest.mark.parametrize("which", [2, 3], ids=["one_m_tile", "m_tile_pairs"])
 @pytest.mark.parametrize("case", CASES, ids=[f"n{c['n']}_T{c['T']}{'_paged' if 'page' in c else ''}" for c in CASES])
-def test_packed_attention_and_scores_equal_the_unpacked_path(case):
+def test_packed_attention_and_scores_equal_the_unpacked_path(case, which):
+    """With one M tile per CTA and with pairs of M tiles (ma_set_attention_kernel 2, 3)."""
+    from maskahead_b200._lib import lib
+
+    prev = lib().ma_set_attention_kernel(which)
+    try:
+        _packed_equals_unpacked(case)
+    finally:
+        lib().ma_set_attention_kernel(prev)
+
+
+def _packed_equals_unpacked(case):
     from maskahead_b200.hotpath import unpacked_prefix
     from maskahead_b200.kernels import prefix_scores, splitk_attention
 
