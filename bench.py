@@ -262,9 +262,15 @@ class Workload:
                          torch.empty(B, H, c["k"], D, device=device, dtype=bf)) for _ in range(L)]
         torch.cuda.synchronize(device)
         self.outputs = None
-        from maskahead_b200.shard import HeadGather
+        from maskahead_b200.shard import HeadGather, PeerHeadGather
 
-        self.head_gather = HeadGather(world)
+        if world > 1 and c["shard"] == "heads":
+            import torch.distributed as dist
+
+            # the head outputs of every layer step, by this library's peer-store kernel
+            self.head_gather = PeerHeadGather(world, dist.get_rank())
+        else:
+            self.head_gather = HeadGather(world)
 
     def compact_buffers(self, layer: int):
         return self.compact[layer]

@@ -372,6 +372,35 @@ MA_API int ma_quantize_keys_channel(const void* k, int32_t dtype, int B, int H, 
 MA_API int ma_key_divisor(const void* k, int32_t dtype, int B, int H, int n, int D, const int64_t sk[3],
                           float* kchan, const int64_t skc[2], void* stream);
 
+/* ---- KV-head sharding: the head outputs exchanged over NVLink ------------------------
+ * Every rank of a KV-head-sharded layer step (shard.py: rank r holds query heads
+ * [r Hl, (r+1) Hl), Hl = Hq / world) needs all ranks' outputs; the reference runs
+ * independent replicas only (scripts/gpu_queue.sh:1-49), so this has no reference
+ * counterpart. Each rank allocates a receive region (ma_peer_alloc, its own device
+ * allocation, zeroed, ma_head_gather_region_bytes(B, Hq, T) bytes) and shares it through a
+ * CUDA IPC handle (ma_ipc_get_handle / ma_ipc_open_handle, handle of
+ * ma_ipc_handle_bytes() bytes; ma_ipc_close_handle, ma_peer_free to release).
+ * ma_head_gather: this rank's rows part [B, Hl, T, D] (bf16, strides sp over (b, head, t),
+ *   D = 128) go into every rank's region by peer stores from this library's kernel (no
+ *   multicast), then the call waits -- bounded by ma_set_peer_wait_ns -- for every rank's
+ *   rows in its own region and copies them to out [B, Hq, T, D] (strides so). regions[p]
+ *   = rank p's region as mapped in this process (regions[rank] this rank's own). Every
+ *   rank makes the same sequence of calls (one process per GPU, all running); the call
+ *   counter lives in the workspace (ma_head_gather_workspace() bytes, zeroed once), so a
+ *   CUDA graph of the calls replays correctly. A wait that gave up is reported by
+ *   ma_workspace_status (MA_ERR_TIMEOUT); out then holds stale rows of the other ranks. */
+MA_API size_t ma_head_gather_region_bytes(int B, int Hq, int T);
+MA_API size_t ma_head_gather_workspace(void);
+MA_API int ma_peer_alloc(size_t bytes, void** ptr);
+MA_API int ma_peer_free(void* ptr);
+MA_API size_t ma_ipc_handle_bytes(void);
+MA_API int ma_ipc_get_handle(void* ptr, void* handle);
+MA_API int ma_ipc_open_handle(const void* handle, void** ptr);
+MA_API int ma_ipc_close_handle(void* ptr);
+MA_API int ma_head_gather(const void* part, const int64_t sp[3], int B, int Hl, int T, int D, int world, int rank,
+                          void* const* regions, void* out, const int64_t so[3], void* workspace,
+                          size_t workspace_bytes, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -110,6 +110,16 @@ _SIGNATURES = {
     "ma_rebuild_remap": (_i32, [_i32, _i32, _i32, _i32, _vp, _i32, _vp, _i32, _vp, _i32, _vp, _i32, _vp, _vp]),
     "ma_evict_plan": (_i32, [_vp, _vp, _i32, _i32, _P(ctypes.c_int64), _i32, _i32, _i32, _i32, _i32, _vp, _vp, _vp,
                              _vp, _vp, _vp]),
+    "ma_head_gather_region_bytes": (_sz, [_i32, _i32, _i32]),
+    "ma_head_gather_workspace": (_sz, []),
+    "ma_peer_alloc": (_i32, [_sz, _P(_vp)]),
+    "ma_peer_free": (_i32, [_vp]),
+    "ma_ipc_handle_bytes": (_sz, []),
+    "ma_ipc_get_handle": (_i32, [_vp, _vp]),
+    "ma_ipc_open_handle": (_i32, [_vp, _P(_vp)]),
+    "ma_ipc_close_handle": (_i32, [_vp]),
+    "ma_head_gather": (_i32, [_vp, _P(ctypes.c_int64), _i32, _i32, _i32, _i32, _i32, _i32, _P(_vp), _vp,
+                              _P(ctypes.c_int64), _vp, _sz, _vp]),
 }
 
 EXPORTED = tuple(_SIGNATURES)
@@ -175,6 +185,8 @@ _WORKSPACES: dict[tuple, torch.Tensor] = {}
 # purposes whose buffers are C-ABI workspaces (an error word at their first 256-byte
 # boundary); the others are plain data scratch (e.g. the unpacked prefix)
 STATUS_WORKSPACES = frozenset({"attention", "value_score"})
+# further C-ABI workspaces with an error word, owned by objects (device index, buffer)
+STATUS_EXTRA: list[tuple[int, torch.Tensor]] = []
 
 
 def device_status(device: torch.device | int | None = None) -> None:
@@ -193,6 +205,14 @@ def device_status(device: torch.device | int | None = None) -> None:
         rc = lib_.ma_workspace_status(buf.data_ptr(), buf.numel(), stream)
         if rc == MA_ERR_TIMEOUT:
             failed.append(purpose)
+        elif rc != MA_OK:
+            check("ma_workspace_status", rc)
+    for index, buf in list(STATUS_EXTRA):
+        if index != dev.index:
+            continue
+        rc = lib_.ma_workspace_status(buf.data_ptr(), buf.numel(), stream)
+        if rc == MA_ERR_TIMEOUT:
+            failed.append("head_gather")
         elif rc != MA_OK:
             check("ma_workspace_status", rc)
     if failed:

@@ -1,5 +1,7 @@
 // C ABI of the select + attend hot path: argument validation, split planning and the
 // launch sequence of every entry point declared in include/maskahead_b200.h.
+#include <string.h>
+
 #include "ma_kernels.cuh"
 #include "ma_packed.cuh"
 
@@ -627,6 +629,60 @@ int ma_rebuild_remap(int B, int H, int old_len, int kgroup, const int64_t* group
   if (lanes > 0x7fffffffLL) return MA_ERR_UNSUPPORTED;
   RemapParams p{groups_before, encode, groups_after, stage, remap, g1, (int)g2, g3, m, st, kgroup, old_len, (int)ql};
   return launch_rebuild_remap(p, (int)lanes, (cudaStream_t)stream);
+}
+
+// ------------------------------------------------------------------ KV-head sharding
+size_t ma_head_gather_region_bytes(int B, int Hq, int T) {
+  if (B <= 0 || Hq <= 0 || T <= 0) return 0;
+  return ma::head_gather_region_bytes(B, Hq, T);
+}
+
+size_t ma_head_gather_workspace(void) { return 512; }
+
+int ma_peer_alloc(size_t bytes, void** ptr) {
+  if (!ptr || bytes == 0) return MA_ERR_ARG;
+  *ptr = nullptr;
+  void* p = nullptr;
+  if (cudaMalloc(&p, bytes) != cudaSuccess) return MA_ERR_CUDA;
+  if (cudaMemset(p, 0, bytes) != cudaSuccess) {
+    cudaFree(p);
+    return MA_ERR_CUDA;
+  }
+  *ptr = p;
+  return MA_OK;
+}
+
+int ma_peer_free(void* ptr) { return cudaFree(ptr) == cudaSuccess ? MA_OK : MA_ERR_CUDA; }
+
+size_t ma_ipc_handle_bytes(void) { return sizeof(cudaIpcMemHandle_t); }
+
+int ma_ipc_get_handle(void* ptr, void* handle) {
+  if (!ptr || !handle) return MA_ERR_ARG;
+  cudaIpcMemHandle_t h;
+  if (cudaIpcGetMemHandle(&h, ptr) != cudaSuccess) return MA_ERR_CUDA;
+  memcpy(handle, &h, sizeof(h));
+  return MA_OK;
+}
+
+int ma_ipc_open_handle(const void* handle, void** ptr) {
+  if (!handle || !ptr) return MA_ERR_ARG;
+  cudaIpcMemHandle_t h;
+  memcpy(&h, handle, sizeof(h));
+  *ptr = nullptr;
+  return cudaIpcOpenMemHandle(ptr, h, cudaIpcMemLazyEnablePeerAccess) == cudaSuccess ? MA_OK : MA_ERR_CUDA;
+}
+
+int ma_ipc_close_handle(void* ptr) { return cudaIpcCloseMemHandle(ptr) == cudaSuccess ? MA_OK : MA_ERR_CUDA; }
+
+int ma_head_gather(const void* part, const int64_t sp[3], int B, int Hl, int T, int D, int world, int rank,
+                   void* const* regions, void* out, const int64_t so[3], void* workspace, size_t workspace_bytes,
+                   void* stream) {
+  if (!part || !sp || !regions || !out || !so) return MA_ERR_ARG;
+  if (D != 128) return MA_ERR_UNSUPPORTED;
+  if (!workspace || workspace_bytes < ma_head_gather_workspace()) return MA_ERR_WORKSPACE;
+  if (!aligned16(part) || !aligned16(out) || !strides16(sp, 3, 2) || !strides16(so, 3, 2)) return MA_ERR_ARG;
+  return ma::launch_head_gather(part, sp, B, Hl, T, world, rank, regions, out, so, workspace, peer_wait_ns(),
+                                (cudaStream_t)stream);
 }
 
 }  // extern "C"

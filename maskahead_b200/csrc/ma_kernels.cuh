@@ -173,6 +173,12 @@ struct EvictPlanParams {
 constexpr int kEvictMaxGroups = 8192;
 int launch_evict_plan(const EvictPlanParams& p, int lanes, cudaStream_t st);
 
+// ma_peer.cu: KV-head sharding's exchange of head outputs by peer stores
+size_t head_gather_region_bytes(int B, int Hq, int T);
+int launch_head_gather(const void* part, const int64_t sp[3], int B, int Hl, int T, int world, int rank,
+                       void* const* regions, void* out, const int64_t so[3], void* ws, uint64_t wait_ns,
+                       cudaStream_t st);
+
 // device properties, cached per device
 int device_sm_count();
 

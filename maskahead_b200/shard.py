@@ -10,8 +10,10 @@ independent replicas, one process per GPU: scripts/gpu_queue.sh:1-49):
   job's; no data-path collective.
 * by KV heads -- one long sequence. Each rank holds H/world KV heads with their G query
   heads each (query head h*G + g belongs to KV head h) and runs the whole path for them;
-  after every layer step the per-rank head outputs [B, Hq/world, T, D] are all-gathered
-  into [B, Hq, T, D] (NCCL over NVLink), the only exchange.
+  after every layer step the per-rank head outputs [B, Hq/world, T, D] are gathered into
+  [B, Hq, T, D] on every rank, the only exchange: PeerHeadGather does it with this
+  library's own kernel (peer stores over NVLink into IPC-mapped receive regions,
+  ma_head_gather), HeadGather with an NCCL all-gather.
 
 The functions take plain sizes and work with any torch.distributed backend (NCCL on the
 GPU box, gloo in the CPU tests).
@@ -19,11 +21,12 @@ GPU box, gloo in the CPU tests).
 
 from __future__ import annotations
 
+import ctypes
 from dataclasses import dataclass
 
 import torch
 
-__all__ = ["SequenceShard", "HeadShard", "sequence_shard", "head_shard", "HeadGather"]
+__all__ = ["SequenceShard", "HeadShard", "sequence_shard", "head_shard", "HeadGather", "PeerHeadGather"]
 
 
 @dataclass(frozen=True)
@@ -102,3 +105,93 @@ class HeadGather:
             out = torch.empty((b, self.world * hq, t, d), device=part.device, dtype=part.dtype)
         out.view(b, self.world, hq, t, d).copy_(full)
         return out
+
+
+class PeerHeadGather:
+    """The exchange of HeadGather by this library's own kernel (ma_head_gather): every rank
+    stores its head outputs straight into every rank's receive region over NVLink -- its
+    own device allocation, mapped into the peers through a CUDA IPC handle -- and waits
+    (bounded) for every rank's flag of the call before copying the region out.
+
+    One instance per process group, one rank per GPU; every rank makes the same calls in
+    the same order, as with a collective. The first call of a shape allocates the region
+    and exchanges the handles (torch.distributed, so it must run outside CUDA-graph
+    capture); later calls, captured or not, launch two kernels. A wait that gave up is
+    reported by maskahead_b200.device_status()."""
+
+    def __init__(self, world: int, rank: int, group=None):
+        self.world, self.rank, self.group = world, rank, group
+        self._regions: dict[tuple, tuple] = {}
+
+    def _region(self, dev: torch.device, b: int, hq: int, t: int):
+        import torch.distributed as dist
+
+        from . import _lib
+
+        key = (dev.index, b, hq, t)
+        reg = self._regions.get(key)
+        if reg is not None:
+            return reg
+        lib = _lib.lib()
+        ptr = ctypes.c_void_p()
+        _lib.check("ma_peer_alloc", lib.ma_peer_alloc(lib.ma_head_gather_region_bytes(b, hq, t), ctypes.byref(ptr)))
+        torch.cuda.synchronize(dev)   # the zeroed region before any peer can write it
+        hb = lib.ma_ipc_handle_bytes()
+        handle = (ctypes.c_char * hb)()
+        _lib.check("ma_ipc_get_handle", lib.ma_ipc_get_handle(ptr, handle))
+        handles = [None] * self.world
+        dist.all_gather_object(handles, bytes(handle), group=self.group)
+        bases, opened = [], []
+        for p, h in enumerate(handles):
+            if p == self.rank:
+                bases.append(ptr.value)
+                continue
+            q = ctypes.c_void_p()
+            _lib.check("ma_ipc_open_handle", lib.ma_ipc_open_handle((ctypes.c_char * hb).from_buffer_copy(h),
+                                                                    ctypes.byref(q)))
+            bases.append(q.value)
+            opened.append(q.value)
+        # the call counter and error word of this region (zeroed; ma_workspace_status reads it)
+        ws = torch.zeros(lib.ma_head_gather_workspace() + 256, dtype=torch.uint8, device=dev)
+        _lib.STATUS_EXTRA.append((dev.index, ws))
+        dist.barrier(group=self.group)   # every rank mapped every region
+        reg = (ptr, (ctypes.c_void_p * self.world)(*bases), opened, ws)
+        self._regions[key] = reg
+        return reg
+
+    def __call__(self, part: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+        from . import _lib
+
+        if self.world == 1:
+            return part if out is None else out.copy_(part)
+        b, hl, t, d = part.shape
+        if part.dtype != torch.bfloat16 or part.stride(-1) != 1:
+            raise ValueError("part must be a bfloat16 [B, Hl, T, D] tensor with a contiguous last dimension")
+        dev = part.device
+        _ptr, bases, _opened, ws = self._region(dev, b, hl * self.world, t)
+        if out is None:
+            out = torch.empty((b, hl * self.world, t, d), device=dev, dtype=part.dtype)
+        lib = _lib.lib()
+        _lib.check("ma_head_gather", lib.ma_head_gather(
+            part.data_ptr(), _lib.i64(*part.stride()[:3]), b, hl, t, d, self.world, self.rank, bases, out.data_ptr(),
+            _lib.i64(*out.stride()[:3]), ws.data_ptr(), ws.numel(), _lib.stream_handle(dev)))
+        return out
+
+    def close(self) -> None:
+        """Unmap the peers' regions and free this rank's (after a barrier: no rank may still
+        write into them)."""
+        import torch.distributed as dist
+
+        from . import _lib
+
+        if not self._regions:
+            return
+        torch.cuda.synchronize()
+        dist.barrier(group=self.group)
+        lib = _lib.lib()
+        for ptr, _bases, opened, ws in self._regions.values():
+            for q in opened:
+                lib.ma_ipc_close_handle(q)
+            lib.ma_peer_free(ptr)
+            _lib.STATUS_EXTRA[:] = [(i, w) for i, w in _lib.STATUS_EXTRA if w is not ws]
+        self._regions.clear()
