@@ -10,7 +10,8 @@ Workloads (--config picks one, the default is the headline cfg
         per 32-channel group, 1% of the key channels x8 as outliers before quantization).
   cfg4  32 layers, 32 query / 8 KV heads, bf16, prefix 65536, read budget 4096, retain
         8192, two lookahead blocks; --gpus N shards the KV heads (strong scaling) and
-        all-gathers the head outputs of every layer step over NVLink (NCCL).
+        gathers the head outputs of every layer step over NVLink (peer stores of this
+        library's own kernel into IPC-mapped receive regions, ma_head_gather).
   cfg5  serving batch: 256 sequences of the cfg3 shape, prefix lengths U[4096, 16384],
         k4v4 token mode in a shuffled pool of 64-slot pages; --gpus N shards the
         sequences (strong scaling, no collective). Retention is not part of this step:
@@ -65,7 +66,7 @@ CONFIGS = {
     "cfg4": dict(_BASE, name="cfg4", L=32, Hq=32, H=8, n=65536, k=4096, C=8192, probe_blocks=2, shard="heads",
                  scaling="strong",
                  workload="cfg4: 32 layers, 32q/8kv heads, d128, bf16 K/V, prefix 65536, k_r 4096, C 8192, "
-                          "2 lookahead blocks; KV heads sharded across ranks, NCCL all-gather of head outputs"),
+                          "2 lookahead blocks; KV heads sharded across ranks, head outputs gathered by peer stores over NVLink"),
     "cfg5": dict(_BASE, name="cfg5", B=256, n=16384, n_min=4096, kv="k4v4_token_paged", page=64,
                  scaling="strong", retention=False,
                  workload="cfg5: 256 sequences of the cfg3 shape, prefix U[4096,16384], k4v4 token mode in "
@@ -90,6 +91,9 @@ def parse_args():
     ap.add_argument("--layers", type=int, default=0,
                     help="override the config's layer count (profiling captures on a small device footprint; "
                          "the JSON line records it and is not the config's headline number)")
+    ap.add_argument("--batch", type=int, default=0,
+                    help="override the config's number of sequences (profiling captures on a small device "
+                         "footprint; the JSON line records it and is not the config's headline number)")
     ap.add_argument("--configs", default="auto",
                     help="further configs measured in the same run, each reported under 'configs' with its own "
                          "timing, e2e and rooflines (comma list; 'auto': cfg3,cfg4,cfg5; '' for none)")
@@ -931,7 +935,8 @@ def measure(c: dict, args, world: int, rank: int, dev, headline: bool) -> dict:
     else:
         job_ab = algorithmic_bytes(c, dict(lens=sequence_lengths(c), H=c["H"], Hq=c["Hq"]))
     step_bytes = job_ab["block_step"] + job_ab["retention"] / c["interval"]
-    parallelism = {"heads": f"kvheads{world} (NCCL all-gather of head outputs)" if world > 1 else "single GPU",
+    parallelism = {"heads": f"kvheads{world} (head outputs gathered by peer stores over NVLink)" if world > 1
+                   else "single GPU",
                    "seqs": f"seq{world} (no collective)"}[c["shard"]]
     s0 = rooflines["step0_attention"]
     roofline = {"kernel": "step-0 attention per layer: " + s0["kernel"], "bound": "hbm",
@@ -946,7 +951,8 @@ def measure(c: dict, args, world: int, rank: int, dev, headline: bool) -> dict:
     res = {
         "value": value, "unit": "tokens/s", "ms_per_step": ms_step, "us_per_block_step": ms_step * 1e3,
         "scaling": c["scaling"], "steps": args.steps, "warmup": args.warmup,
-        "config": {"workload": c["workload"] + (f" [layers overridden: {c['L']}]" if args.layers > 0 else ""),
+        "config": {"workload": c["workload"] + (f" [layers overridden: {c['L']}]" if args.layers > 0 else "")
+                   + (f" [sequences overridden: {c['B']}]" if args.batch > 0 else ""),
                    "global_batch": seqs_job, "seq_len": c["n"], "parallelism": parallelism,
                    "l2": "inputs larger than L2 (the per-step cache exceeds 126 MB); the per-kernel timings flush "
                          "L2 (a 256 MB write) before every replay", "timing": timing},
@@ -987,6 +993,8 @@ def run_ours(args):
         c = dict(CONFIGS[name])
         if args.layers > 0:
             c["L"] = args.layers
+        if args.batch > 0:
+            c["B"] = args.batch
         return c
 
     if args.configs == "auto":
