@@ -8,6 +8,7 @@
 // torch.topk: src/maskahead/kernels/ops.py:377-380, 509-516). Ties at the k-th score
 // go to the lower slot index.
 #include "ma_kernels.cuh"
+#include "ma_packed.cuh"
 
 namespace ma {
 
@@ -751,6 +752,201 @@ __global__ void __launch_bounds__(256) unpack_token_kernel(ma_kv kv, int H, int 
   }
 }
 
+// The same unpack with thread = (slot, 16-channel half of a 32-channel group): 8 threads a
+// slot, 32 slots a pass, 8-byte code loads and the thread's 16 key divisors in registers.
+// Twice the CTAs of unpack_token_kernel for the same slots: faster on a short prefix (cfg3:
+// 7.6 against 10.2 µs a layer), slower on a long batch, whose wider loads keep more bytes
+// in flight (cfg5: 2.07 against 1.83 ms).
+constexpr int kUnpack16Tok = 32;
+__global__ void __launch_bounds__(256) unpack_token16_kernel(ma_kv kv, int H, int n, __nv_bfloat16* __restrict__ ok_,
+                                                           __nv_bfloat16* __restrict__ ov_, int64_t sok0, int64_t sok1,
+                                                           int64_t sok2, int64_t sov0, int64_t sov1, int64_t sov2,
+                                                           int live_only) {
+  const int bh = blockIdx.y;
+  const int b = bh / H, h = bh - (bh / H) * H;
+  const int jj = threadIdx.x >> 3, c = threadIdx.x & 7, g = c >> 1;   // channels 16c..16c+15
+  float kc[16];
+  {
+    const float4* kp = reinterpret_cast<const float4*>(kv.kchan + (int64_t)b * kv.skc[0] + (int64_t)h * kv.skc[1] + 16 * c);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float4 x = __ldg(kp + i);
+      kc[4 * i] = x.x;
+      kc[4 * i + 1] = x.y;
+      kc[4 * i + 2] = x.z;
+      kc[4 * i + 3] = x.w;
+    }
+  }
+  if (live_only && kv.lens) n = max(0, min(n, kv.lens[b]));
+  for (int j = blockIdx.x * kUnpack16Tok + jj; j < n; j += gridDim.x * kUnpack16Tok) {
+    uint4* dk = reinterpret_cast<uint4*>(ok_ + (int64_t)b * sok0 + (int64_t)h * sok1 + (int64_t)j * sok2 + 16 * c);
+    uint4* dv = reinterpret_cast<uint4*>(ov_ + (int64_t)b * sov0 + (int64_t)h * sov1 + (int64_t)j * sov2 + 16 * c);
+    const bool live = kv_exists(kv, b, j);
+    float f[16];
+    if (j < kv.nq && live) {
+      int sb = b, sj = j;
+      if (kv_paged(kv, j)) kv_page(kv, b, j, sb, sj);
+      // half c & 1 of group c >> 1: payload bytes 8c..8c+7, element k in nibble k
+      const uint2 pk = __ldg(reinterpret_cast<const uint2*>(
+          kv.kq + (int64_t)sb * kv.skq[0] + (int64_t)h * kv.skq[1] + (int64_t)sj * kv.skq[2] + 8 * c));
+      const uint2 pv = __ldg(reinterpret_cast<const uint2*>(
+          kv.vq + (int64_t)sb * kv.svq[0] + (int64_t)h * kv.svq[1] + (int64_t)sj * kv.svq[2] + 8 * c));
+      const int64_t kso = (int64_t)sb * kv.sks[0] + (int64_t)h * kv.sks[1] + (int64_t)sj * kv.sks[2] + g;
+      const int64_t vso = (int64_t)sb * kv.svs[0] + (int64_t)h * kv.svs[1] + (int64_t)sj * kv.svs[2] + g;
+      const float ks = half_bits_to_float(kv.ks[kso]), kz = half_bits_to_float(kv.kz[kso]);
+      const float vs = half_bits_to_float(kv.vs[vso]), vz = half_bits_to_float(kv.vz[vso]);
+#pragma unroll
+      for (int i = 0; i < 16; ++i) {
+        const uint32_t w = i < 8 ? pk.x : pk.y;
+        const float code = __uint_as_float(0x4B000000u | ((w >> (4 * (i & 7))) & 0xFu)) - 8388608.f;
+        f[i] = fmaf(code, ks, kz) * kc[i];
+      }
+      dk[0] = float8_to_bf16x8(f);
+      dk[1] = float8_to_bf16x8(f + 8);
+#pragma unroll
+      for (int i = 0; i < 16; ++i) {
+        const uint32_t w = i < 8 ? pv.x : pv.y;
+        const float code = __uint_as_float(0x4B000000u | ((w >> (4 * (i & 7))) & 0xFu)) - 8388608.f;
+        f[i] = fmaf(code, vs, vz);
+      }
+      dv[0] = float8_to_bf16x8(f);
+      dv[1] = float8_to_bf16x8(f + 8);
+    } else if (j >= kv.nq && live) {   // the dense tail
+      kv_read8<true>(kv, b, h, j, 2 * c, f);
+      kv_read8<true>(kv, b, h, j, 2 * c + 1, f + 8);
+      dk[0] = float8_to_bf16x8(f);
+      dk[1] = float8_to_bf16x8(f + 8);
+      kv_read8<false>(kv, b, h, j, 2 * c, f);
+      kv_read8<false>(kv, b, h, j, 2 * c + 1, f + 8);
+      dv[0] = float8_to_bf16x8(f);
+      dv[1] = float8_to_bf16x8(f + 8);
+    } else {
+      const uint4 z = make_uint4(0, 0, 0, 0);
+      dk[0] = z;
+      dk[1] = z;
+      dv[0] = z;
+      dv[1] = z;
+    }
+  }
+}
+
+
+// The unpack of a long batch with its input staged by bulk copies: a CTA takes consecutive
+// 128-slot units of one (b, h); one thread copies each unit's raw rows (K and V payloads,
+// scales, zeros: 20 KB, per page crossed) into a ring of kUnpackStages stages a few units
+// ahead (cp.async.bulk, completion on an mbarrier), so each SM keeps far more bytes in
+// flight than register loads can; all 8 warps convert a staged unit, thread = (slot,
+// 8-channel chunk), 16-byte stores two slots a warp. The arithmetic is kv_read8's.
+constexpr int kUnpackStages = 3;
+constexpr int kUnpackUnits = 8;   // units a CTA takes
+__global__ void __launch_bounds__(256) unpack_staged_kernel(ma_kv kv, int H, int n, __nv_bfloat16* __restrict__ ok_,
+                                                            __nv_bfloat16* __restrict__ ov_, int64_t sok0, int64_t sok1,
+                                                            int64_t sok2, int64_t sov0, int64_t sov1, int64_t sov2,
+                                                            int live_only) {
+  extern __shared__ __align__(128) uint8_t stg_raw[];
+  __shared__ __align__(8) uint64_t sfull[kUnpackStages];
+  const int bh = blockIdx.y;
+  const int b = bh / H, h = bh - (bh / H) * H;
+  const int c = threadIdx.x & 15, g = c >> 2;
+  pdl_wait();   // with a programmatic launch, the cache may come from the kernel before
+  const int nq = min(n, kv.nq);
+  int end = nq;
+  if (kv.lens) end = max(0, min(end, kv.lens[b]));
+  const int u0 = blockIdx.x * kUnpackUnits;
+  const int last = live_only ? end : nq;   // slots written: below lens[b], or every one (zeros past it)
+  const int units = max(0, min(kUnpackUnits, (last - u0 * 128 + 127) / 128));
+  const packed::PageCache pc{nullptr, 0, 0};
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < kUnpackStages; ++i) tc::mbar_init(&sfull[i], 1);
+    asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
+    for (int i = 0; i < kUnpackStages && i < units; ++i) {
+      const int j0 = (u0 + i) * 128;
+      packed::stage_tile(kv, b, h, j0, min(end, j0 + 128), stg_raw + i * packed::kStageBytes, &sfull[i], pc);
+    }
+  }
+  float kc[8];
+  {
+    const float4* kp = reinterpret_cast<const float4*>(kv.kchan + (int64_t)b * kv.skc[0] + (int64_t)h * kv.skc[1] + 8 * c);
+    const float4 a = __ldg(kp), d = __ldg(kp + 1);
+    kc[0] = a.x; kc[1] = a.y; kc[2] = a.z; kc[3] = a.w;
+    kc[4] = d.x; kc[5] = d.y; kc[6] = d.z; kc[7] = d.w;
+  }
+  __syncthreads();
+  for (int u = 0; u < units; ++u) {
+    const int j0 = (u0 + u) * 128;
+    const uint8_t* stg = stg_raw + (u % kUnpackStages) * packed::kStageBytes;
+    const bool ok = tc::mbar_wait(&sfull[u % kUnpackStages], (uint32_t)(u / kUnpackStages) & 1u, 200000000ull);
+#pragma unroll 2
+    for (int i = 0; i < 8; ++i) {
+      const int r = (threadIdx.x >> 4) + 16 * i;
+      const int j = j0 + r;
+      if (j >= last) continue;
+      uint4* dk = reinterpret_cast<uint4*>(ok_ + (int64_t)b * sok0 + (int64_t)h * sok1 + (int64_t)j * sok2 + 8 * c);
+      uint4* dv = reinterpret_cast<uint4*>(ov_ + (int64_t)b * sov0 + (int64_t)h * sov1 + (int64_t)j * sov2 + 8 * c);
+      int sb, sj;
+      if (!ok || j >= end || !packed::locate(kv, b, j, sb, sj)) {
+        *dk = make_uint4(0, 0, 0, 0);
+        *dv = make_uint4(0, 0, 0, 0);
+        continue;
+      }
+      float f[8];
+      const uint32_t wk = *reinterpret_cast<const uint32_t*>(stg + packed::kStgKq + r * 64 + 4 * c);
+      const uint32_t wv = *reinterpret_cast<const uint32_t*>(stg + packed::kStgVq + r * 64 + 4 * c);
+      const float ks = half_bits_to_float(*reinterpret_cast<const uint16_t*>(stg + packed::kStgKs + r * 8 + 2 * g));
+      const float kz = half_bits_to_float(*reinterpret_cast<const uint16_t*>(stg + packed::kStgKz + r * 8 + 2 * g));
+      const float vs = half_bits_to_float(*reinterpret_cast<const uint16_t*>(stg + packed::kStgVs + r * 8 + 2 * g));
+      const float vz = half_bits_to_float(*reinterpret_cast<const uint16_t*>(stg + packed::kStgVz + r * 8 + 2 * g));
+#pragma unroll
+      for (int k = 0; k < 8; ++k) {
+        const float code = __uint_as_float(0x4B000000u | ((wk >> (4 * k)) & 0xFu)) - 8388608.f;
+        f[k] = fmaf(code, ks, kz) * kc[k];
+      }
+      *dk = float8_to_bf16x8(f);
+#pragma unroll
+      for (int k = 0; k < 8; ++k) {
+        const float code = __uint_as_float(0x4B000000u | ((wv >> (4 * k)) & 0xFu)) - 8388608.f;
+        f[k] = fmaf(code, vs, vz);
+      }
+      *dv = float8_to_bf16x8(f);
+    }
+    __syncthreads();   // every thread is done with the stage
+    if (threadIdx.x == 0 && u + kUnpackStages < units) {
+      const int jn = (u0 + u + kUnpackStages) * 128;
+      packed::stage_tile(kv, b, h, jn, min(end, jn + 128), stg_raw + (u % kUnpackStages) * packed::kStageBytes,
+                         &sfull[u % kUnpackStages], pc);
+    }
+  }
+}
+
+// the unpack of n slots of BH (b, h) pairs: the 16-channel form up to 2^20 slot-heads (a
+// single sequence), the 32-channel one above; each CTA takes about four passes
+void launch_unpack(const ma_kv& kv, int BH, int H, int n, void* out_k, void* out_v, const int64_t sok[3],
+                   const int64_t sov[3], int live_only, cudaStream_t st) {
+  // a long batch of a purely packed prefix (no dense tail): the staged form
+  if ((long long)BH * n > (1ll << 20) && kv.nf == 0 && packed::eligible(kv)) {
+    static bool attr = false;
+    const int smem = kUnpackStages * packed::kStageBytes;
+    if (!attr && cudaFuncSetAttribute(unpack_staged_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) ==
+                     cudaSuccess)
+      attr = true;
+    const dim3 grid((n + 128 * kUnpackUnits - 1) / (128 * kUnpackUnits), BH);
+    unpack_staged_kernel<<<grid, 256, smem, st>>>(kv, H, n, (__nv_bfloat16*)out_k, (__nv_bfloat16*)out_v, sok[0],
+                                                  sok[1], sok[2], sov[0], sov[1], sov[2], live_only);
+    return;
+  }
+  const bool narrow = (long long)BH * n <= (1ll << 20);
+  const int tok = narrow ? kUnpack16Tok : kUnpackTok;
+  int gx = (n + tok - 1) / tok;
+  if (gx > 8) gx = (gx + 3) / 4;
+  const dim3 ugrid(gx, BH);
+  if (narrow)
+    unpack_token16_kernel<<<ugrid, 256, 0, st>>>(kv, H, n, (__nv_bfloat16*)out_k, (__nv_bfloat16*)out_v, sok[0],
+                                                 sok[1], sok[2], sov[0], sov[1], sov[2], live_only);
+  else
+    unpack_token_kernel<<<ugrid, 256, 0, st>>>(kv, H, n, (__nv_bfloat16*)out_k, (__nv_bfloat16*)out_v, sok[0],
+                                               sok[1], sok[2], sov[0], sov[1], sov[2], live_only);
+}
+
 }  // namespace
 
 int launch_select_topk(const float* score, int B, int H, int n, int64_t ss0, int64_t ss1,
@@ -851,11 +1047,7 @@ int launch_unpack_live(const ma_kv& kv, int B, int H, int D, void* out_k, void* 
         kv.kgroup == 32 && (kv.nf == 0 || kv.kf)))
     return MA_ERR_UNSUPPORTED;
   if (k == 0) return MA_OK;
-  int gx = (k + kUnpackTok - 1) / kUnpackTok;
-  if (gx > 8) gx = (gx + 3) / 4;   // each CTA takes about four 64-slot rows
-  dim3 ugrid(gx, B * H);
-  unpack_token_kernel<<<ugrid, 256, 0, st>>>(kv, H, k, (__nv_bfloat16*)out_k, (__nv_bfloat16*)out_v, sok[0], sok[1],
-                                             sok[2], sov[0], sov[1], sov[2], 1);
+  launch_unpack(kv, B * H, H, k, out_k, out_v, sok, sov, 1, st);
   return cudaGetLastError() == cudaSuccess ? MA_OK : MA_ERR_CUDA;
 }
 
@@ -866,11 +1058,7 @@ int launch_gather_kv(const ma_kv& kv, int B, int H, int D, const int64_t* idx, i
   if (!idx && kv.layout == MA_KV_PACKED_TOKEN && kv.dtype == MA_BF16 && out_dtype == MA_BF16 && D == 128 &&
       kv.kchan && kv.vgroup == 32 && kv.kgroup == 32 && (kv.nf == 0 || kv.kf)) {
     // the whole token-mode prefix: the contiguous unpack
-    int gx = (k + kUnpackTok - 1) / kUnpackTok;
-    if (gx > 8) gx = (gx + 3) / 4;   // each CTA takes about four 64-slot rows
-    dim3 ugrid(gx, B * H);
-    unpack_token_kernel<<<ugrid, 256, 0, st>>>(kv, H, k, (__nv_bfloat16*)out_k, (__nv_bfloat16*)out_v, sok[0], sok[1],
-                                               sok[2], sov[0], sov[1], sov[2], 0);
+    launch_unpack(kv, B * H, H, k, out_k, out_v, sok, sov, 0, st);
     return cudaGetLastError() == cudaSuccess ? MA_OK : MA_ERR_CUDA;
   }
   dim3 grid((k + kGatherTok - 1) / kGatherTok, B * H);

@@ -211,3 +211,61 @@ def test_unpack_prefix_writes_the_live_slots_only():
     for b, L in enumerate(lens):
         assert torch.equal(un.kf[b, :, :L].cpu(), want_k[b, :, :L].cpu())
         assert torch.equal(un.vf[b, :, :L].cpu(), want_v[b, :, :L].cpu())
+
+
+@pytest.mark.parametrize("live_only", [True, False], ids=["unpack_prefix", "dequantize_prefix"])
+def test_long_batch_unpack_equals_the_per_sequence_unpack(live_only):
+    """Above 2^20 slot-heads a token-mode batch is unpacked by the staged kernel (bulk-copied
+    raw rows, all warps converting); each sequence unpacked alone takes the per-slot kernel.
+    Both are the same dequantization: equal bit for bit below lens[b] (and zeros past it
+    when every slot is written), on a ragged batch in a shuffled pool of 64-slot pages."""
+    from maskahead_b200._lib import i64, lib as get_lib
+    from maskahead_b200.kernels.splitk import dequantize_prefix
+    from maskahead_b200.layouts import Prefix, key_divisor, kv_descriptor, quantize_tokens
+
+    g = torch.Generator(device=DEV).manual_seed(5)
+    B, H, D, page, n = 24, 4, 128, 64, 16384
+    lens = torch.randint(4096, n + 1, (B,), generator=torch.Generator().manual_seed(6)).tolist()
+    need = [(x + page - 1) // page for x in lens]
+    P = sum(need) + 3
+    order = torch.randperm(P, generator=torch.Generator().manual_seed(7))
+    table = torch.full((B, n // page), -1, dtype=torch.int32)
+    owner = torch.zeros(P, dtype=torch.int64)
+    at = 0
+    for b, m in enumerate(need):
+        table[b, :m] = order[at:at + m].to(torch.int32)
+        owner[order[at:at + m]] = b
+        at += m
+    kpool = torch.randn(P, H, page, D, generator=g, device=DEV).to(torch.bfloat16)
+    vpool = torch.randn(P, H, page, D, generator=g, device=DEV).to(torch.bfloat16)
+    kchan = torch.rand(B, H, D, generator=g, device=DEV) + 0.5
+    kq, ks, kz = quantize_tokens(kpool, kchan[owner.to(DEV)])
+    vq, vs, vz = quantize_tokens(vpool)
+    arrays = dict(kq=kq, ks=ks, kz=kz, vq=vq, vs=vs, vz=vz, nq=n, kb=4, vb=4, kg=32, vg=32, kmode=1, page_size=page)
+    lens_t = torch.tensor(lens, dtype=torch.int32, device=DEV)
+    pre = Prefix(**arrays, kch=kchan, pages=table.to(DEV), lens=lens_t)
+    lib = get_lib()
+
+    def unpack(p, batch):
+        if not live_only:
+            return dequantize_prefix(p, batch, H, D)
+        ko = torch.full((batch, H, n, D), 7.0, dtype=torch.bfloat16, device=DEV)
+        vo = torch.full_like(ko, -3.0)
+        desc = kv_descriptor(p, batch=batch, heads=H, head_dim=D)
+        assert lib.ma_unpack_prefix(desc.kv, batch, H, D, ko.data_ptr(), vo.data_ptr(), i64(*ko.stride()[:3]),
+                                    i64(*vo.stride()[:3]), torch.cuda.current_stream().cuda_stream) == 0
+        return ko, vo
+
+    got_k, got_v = unpack(pre, B)
+    torch.cuda.synchronize()
+    for b in range(0, B, 5):
+        one = Prefix(**arrays, kch=kchan[b:b + 1], pages=table[b:b + 1].to(DEV), lens=lens_t[b:b + 1])
+        want_k, want_v = unpack(one, 1)
+        torch.cuda.synchronize()
+        L = lens[b]
+        assert torch.equal(got_k[b, :, :L], want_k[0, :, :L])
+        assert torch.equal(got_v[b, :, :L], want_v[0, :, :L])
+        if live_only:
+            assert bool((got_k[b, :, L:] == 7.0).all()) and bool((got_v[b, :, L:] == -3.0).all())
+        else:
+            assert not bool(got_k[b, :, L:].any()) and not bool(got_v[b, :, L:].any())
