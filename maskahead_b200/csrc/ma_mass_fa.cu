@@ -412,40 +412,32 @@ __device__ __forceinline__ void mass_fa_body(const Args& A) {
     __shared__ int sDecide;
     const uint32_t tRow = taddr + ((uint32_t)(quarter * 32) << 16);
     const float2 c2x2 = make_float2(c2, c2);
-    // the row chunks are 64 columns, taken alternately by the two warps of a slot quarter;
-    // rows past R2 read -inf from sNB, and the columns past Npad of a last partial chunk
-    // are zeroed once here (the MMAs never write them), so no chunk needs a bound check
-    if (!given && (Npad & 63) != 0 && ((Npad >> 6) & 1) == chalf) {
-      const uint32_t z[16] = {0u, 0u, 0u, 0u, 0u, 0u, 0u, 0u, 0u, 0u, 0u, 0u, 0u, 0u, 0u, 0u};
-      for (int col = Npad; col < (Npad | 63) + 1; col += 16) {
-        tmem_st16(tRow + col, z);
-        tmem_st16(tRow + 256 + col, z);
-      }
-      tmem_st_wait();
-    }
+    // the two warps of a slot quarter split the Npad row columns evenly: half 0 takes
+    // [0, h0), half 1 [h0, Npad) (h0 = Npad / 2 rounded up to 16), in 32-column chunks and
+    // a 16-column tail; rows past R2 read -inf from sNB
+    const int h0 = ((Npad / 2 + 15) / 16) * 16;
+    const int col_lo = chalf ? h0 : 0, col_hi = chalf ? Npad : h0;
     for (int t = 0; t < ntiles; ++t) {
       const int j0 = begin + t * kTile;
       if (!given) {
       if (!mbar_wait(&s_full[t & 1], (uint32_t)(t >> 1) & 1u, kWaitNs)) s_abort = 1;
       fence_after_sync();
-      // this thread: slot slot_lane, row chunks chalf, chalf + 2, ...
+      // this thread: slot slot_lane, row columns [col_lo, col_hi)
       float2 a0 = make_float2(0.f, 0.f), a1 = a0, a2 = a0, a3 = a0;
       const uint32_t tS = tRow + (t & 1) * 256;
-#pragma unroll 1
-      for (int c = chalf; c * 64 < Npad; c += 2) {
-        float sv[64];
-        tmem_ld32(tS + c * 64, sv);
-        tmem_ld32(tS + c * 64 + 32, sv + 32);
-        tmem_ld_wait();
-        const float* nb = sNB + c * 64;
+      // 32-column chunks, the next one's tensor-memory load in flight during this one's
+      // exponentials (a wait covers every load issued before it), then a 16-column tail
+      auto chunk = [&](const float* v, int col, int width) {
+        const float* nb = sNB + col;
 #pragma unroll
-        for (int i = 0; i < 64; i += 8) {
+        for (int i = 0; i < 32; i += 8) {
+          if (i >= width) break;
           const float4 b0 = *reinterpret_cast<const float4*>(nb + i);
           const float4 b1 = *reinterpret_cast<const float4*>(nb + i + 4);
-          float2 x0 = ffma2(make_float2(sv[i], sv[i + 1]), c2x2, make_float2(b0.x, b0.y));
-          float2 x1 = ffma2(make_float2(sv[i + 2], sv[i + 3]), c2x2, make_float2(b0.z, b0.w));
-          float2 x2 = ffma2(make_float2(sv[i + 4], sv[i + 5]), c2x2, make_float2(b1.x, b1.y));
-          float2 x3 = ffma2(make_float2(sv[i + 6], sv[i + 7]), c2x2, make_float2(b1.z, b1.w));
+          float2 x0 = ffma2(make_float2(v[i], v[i + 1]), c2x2, make_float2(b0.x, b0.y));
+          float2 x1 = ffma2(make_float2(v[i + 2], v[i + 3]), c2x2, make_float2(b0.z, b0.w));
+          float2 x2 = ffma2(make_float2(v[i + 4], v[i + 5]), c2x2, make_float2(b1.x, b1.y));
+          float2 x3 = ffma2(make_float2(v[i + 6], v[i + 7]), c2x2, make_float2(b1.z, b1.w));
           x0 = make_float2(ex2(x0.x), ex2(x0.y));
           x1 = make_float2(ex2(x1.x), ex2(x1.y));
           x2 = make_float2(ex2(x2.x), ex2(x2.y));
@@ -455,6 +447,27 @@ __device__ __forceinline__ void mass_fa_body(const Args& A) {
           a2 = fadd2(a2, x2);
           a3 = fadd2(a3, x3);
         }
+      };
+      float sa[32], sb[32];
+      const int n32 = (col_hi - col_lo) / 32;   // full chunks
+      if (n32 > 0) tmem_ld32(tS + col_lo, sa);
+      tmem_ld_wait();
+#pragma unroll 1
+      for (int i = 0; i < n32; i += 2) {
+        const int col = col_lo + 32 * i;
+        if (i + 1 < n32) tmem_ld32(tS + col + 32, sb);
+        chunk(sa, col, 32);
+        tmem_ld_wait();
+        if (i + 1 < n32) {
+          if (i + 2 < n32) tmem_ld32(tS + col + 64, sa);
+          chunk(sb, col + 32, 32);
+          tmem_ld_wait();
+        }
+      }
+      if (col_lo + 32 * n32 < col_hi) {   // the 16-column tail
+        tmem_ld16(tS + col_lo + 32 * n32, sa);
+        tmem_ld_wait();
+        chunk(sa, col_lo + 32 * n32, 16);
       }
       sHalf[chalf][slot_lane] = ((a0.x + a0.y) + (a1.x + a1.y)) + ((a2.x + a2.y) + (a3.x + a3.y));
       fence_before_sync();
