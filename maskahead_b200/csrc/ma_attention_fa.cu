@@ -23,7 +23,12 @@
 // the group's previous P.V: lazy, only when the max grows by more than e^8); the epilogue
 // merges the two states.
 // Per split: (m, l) and o = acc / l as bf16 (ma_common.cuh), stored by TMA, the merge as
-// in ma_attention_tc.cu (fused into a cooperative launch when it is one pass).
+// in ma_attention_tc.cu (fused into a cooperative launch when it is one pass). With at
+// most 16 splits a row block's splits form one thread-block cluster and merge on chip:
+// every split keeps its partial in shared memory and the others pull their share of the
+// rows from it, or -- every split one key tile, as in the sub-steps over the compact
+// cache -- every split copies each CTA's share into that CTA with the bulk-copy engine
+// (one copy per destination, counted on the receiver's mbarrier).
 // Every wait is bounded. Semantics follow src/maskahead/kernels/splitk.py:115-190.
 //
 // Row-tile pairs (PAIR): with more than 128 rows per KV head (R = 224 for 28 query heads
@@ -136,6 +141,7 @@ __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
 // rank s; its rows at sO (256 bytes per row, 16-byte chunk c of row i at c ^ (i & 15)) and
 // its (m, l) pairs at sML.
 struct ClusterPartials {
+  static constexpr bool kLaneMl = true;   // one distributed-shared-memory load per pair
   uint32_t o_base, ml_base;   // this CTA's sO / sML as shared::cta addresses
   int row, l16;
   __device__ __forceinline__ uint4 o(int s) const {
@@ -155,6 +161,28 @@ struct ClusterPartials {
     return make_float2(__uint_as_float(x), __uint_as_float(y));
   }
 };
+
+// The partial rows every split of the cluster copied to this CTA (the pushed merge): the
+// CTA that merges rows [lo, lo + per) holds split s's row lo + i at slot s per + i (256
+// bytes, 16-byte chunk c at c ^ ((lo + i) & 15), the sender's layout) and its (m, l) in
+// the 16-byte entry ml_base[s per + i].
+struct PushedPartials {
+  static constexpr bool kLaneMl = false;
+  const uint8_t* o_base;
+  const float4* ml_base;
+  int per, lo, i, l16;
+  __device__ __forceinline__ uint4 o(int s) const {
+    return *reinterpret_cast<const uint4*>(o_base + (s * per + i) * 256 + ((l16 ^ ((lo + i) & 15)) << 4));
+  }
+  __device__ __forceinline__ float2 ml(int s) const {
+    const float4 e = ml_base[s * per + i];
+    return make_float2(e.x, e.y);
+  }
+};
+constexpr int kRxMlOffset = 40960;   // the pushed (m, l) entries after at most 143 x 256 bytes of rows
+constexpr int kPushMlOffset = 4096;  // a split's own (m, l) entries in its V slot 0 (after the scratch)
+static_assert(kKSlots >= 3 && 143 * 256 <= kRxMlOffset && kRxMlOffset + 143 * 16 <= 2 * kKVBytes,
+              "the pushed rows fit K slots 1 and 2");
 
 // the max of 64 values (four independent max3 chains)
 __device__ __forceinline__ float max64(const float (&v)[64]) {
@@ -211,7 +239,7 @@ __device__ __forceinline__ void attn_fa_body(const Args& A) {
   uint8_t* sVs = sKs + KS * kKVBytes;                   // V slots
   uint8_t* sStg = sVs + VS * kKVBytes;                  // PACKED: the staging ring of raw tiles
   __shared__ uint32_t s_taddr;
-  __shared__ __align__(8) uint64_t kfull[KS], vfull[VS], s_full[2], p_full[2], o_done[2], q_full, mbar_fin;
+  __shared__ __align__(8) uint64_t kfull[KS], vfull[VS], s_full[2], p_full[2], o_done[2], q_full, mbar_fin, rx_full;
   __shared__ __align__(8) uint64_t kfree[KS], vfree[VS];
   __shared__ __align__(8) uint64_t rfull[PACKED ? NST : 1], rfree[PACKED ? NST : 1];
   __shared__ __align__(16) float sKch[PACKED ? kD : 1];   // the packed keys' divisor of this (b, h)
@@ -243,6 +271,15 @@ __device__ __forceinline__ void attn_fa_body(const Args& A) {
   const bool is_cur = split == A.nsplit;
   const bool dq = PACKED && !is_cur;   // prefix tiles built by the producer warps
   const bool merge_warp = warp < kWarps;   // the producer warps take no merge rows
+  // pushed cluster merge (every CTA of the cluster has at most one key tile, so K slots 1
+  // and 2 stay free): split j of the cluster merges rows [j mper, +mper) of the row block;
+  // every split lays its partial out in its own K slot 0 and copies those rows into CTA
+  // j's K slots 1 and 2 with the bulk-copy engine
+  const bool push = !PAIR && !PACKED && A.cmerge == 2;
+  const int R_blk = min(kRows, R - r0);
+  const int mper = (R_blk + (int)gridDim.y - 1) / (int)gridDim.y;
+  uint8_t* sRx = sKs + kKVBytes;
+  float4* sRxML = reinterpret_cast<float4*>(sRx + kRxMlOffset);
   int begin, end;
   if (is_cur) {
     begin = 0;
@@ -299,8 +336,13 @@ __device__ __forceinline__ void attn_fa_body(const Args& A) {
     }
     mbar_init(&q_full, 1);
     mbar_init(&mbar_fin, 1);
+    if (push) mbar_init(&rx_full, 1);
     s_abort = 0;
     asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
+    if (push) {   // every split's rows of this CTA's share: 256 bytes + a 16-byte (m, l) each
+      const int own = max(0, min(R_blk, (split + 1) * mper) - split * mper);
+      tma::expect_tx(&rx_full, (uint32_t)((int)gridDim.y * own * (kD * 2 + 16)));
+    }
     // the queries and the first K and V tiles start loading now, before the TMEM
     // allocation and the setup barrier
     pdl_wait();   // with a programmatic launch, the inputs may come from the kernel before
@@ -337,6 +379,7 @@ __device__ __forceinline__ void attn_fa_body(const Args& A) {
   fence_before_sync();
   __syncthreads();
   fence_after_sync();
+  if (push) cluster_arrive_relaxed();   // rx_full is initialized (waited on before the first send)
   const uint32_t taddr = s_taddr;
   const uint32_t lane_base = (uint32_t)(quarter * 32) << 16;
   const uint32_t tS = taddr + lane_base + kColS + 128 * grp;   // this warp's S buffer (its rows)
@@ -681,6 +724,7 @@ __device__ __forceinline__ void attn_fa_body(const Args& A) {
   __syncthreads();
   fence_after_sync();
   if (threadIdx.x == 0) pdl_launch_dependents();   // the next kernel's prologue may start
+  if (push) cluster_wait();   // every CTA's rx_full is initialized: the sends may start
 
   if (PAIR && softmax_warp) {
     // each M tile's rows are final in their own group: o = O_g / l under the group's running
@@ -776,10 +820,12 @@ __device__ __forceinline__ void attn_fa_body(const Args& A) {
     const int prow0 = (int)(((int64_t)bh * A.P.S + split) * A.P.Rp + wrow0);
     float2* sML = reinterpret_cast<float2*>(sVs + 4096);   // cluster merge: this split's (m, l)
     uint8_t* sO = sKs;                                     // cluster merge: its rows (32 KB)
+    float4* sMLq = reinterpret_cast<float4*>(sVs + kPushMlOffset);   // pushed merge: 16-byte (m, l)
     if (s_abort != 0) {
       if (threadIdx.x == 0) atomicExch(A.err, 1);
       if (row_ok && grp == 0) {
-        if (A.cmerge) sML[rl] = make_float2(NAN, NAN);
+        if (push) sMLq[rl] = make_float4(NAN, NAN, 0.f, 0.f);
+        else if (A.cmerge) sML[rl] = make_float2(NAN, NAN);
         else A.P.ml[prow] = make_float2(NAN, NAN);
       }
     } else {
@@ -787,7 +833,8 @@ __device__ __forceinline__ void attn_fa_body(const Args& A) {
       // either reference
       if (row_ok && grp == 0) {
         const float fix = (mt == -INFINITY) ? 1.f : ex2(M - mt * c2);
-        if (A.cmerge) sML[rl] = make_float2(mt * A.scale, l * fix);
+        if (push) sMLq[rl] = make_float4(mt * A.scale, l * fix, 0.f, 0.f);
+        else if (A.cmerge) sML[rl] = make_float2(mt * A.scale, l * fix);
         else A.P.ml[prow] = make_float2(mt * A.scale, l * fix);
       }
       const float inv = l > 0.f ? 1.f / l : 0.f;
@@ -852,15 +899,51 @@ __device__ __forceinline__ void attn_fa_body(const Args& A) {
       }
     }
   }
+  if (push) fence_proxy_async();   // the partial's rows -> the copy engine's reads
   fence_before_sync();
   __syncthreads();
   fence_after_sync();
   if (warp == 0) tmem_dealloc(taddr, kTmemCols);
+  if (push) {
+    // ---- pushed merge: lane j of the MMA warp copies rows [j mper, +mper) of this split's
+    // partial (K slot 0) and their (m, l) into CTA j; this CTA merges its rows [lo, hi) of
+    // every split from its own shared memory once rx_full has counted every byte
+    const int lo = split * mper, hi = min(R_blk, lo + mper);
+    if (warp == kSoftWarps && lane < (int)gridDim.y) {
+      const int jlo = lane * mper, own = max(0, min(R_blk, jlo + mper) - jlo);
+      if (own > 0) {
+        const uint32_t bar = peer_addr(&rx_full, (uint32_t)lane);
+        bulk_copy_to_peer(peer_addr(sRx + split * mper * 256, (uint32_t)lane), smem_addr(sKs + jlo * 256),
+                          (uint32_t)(own * 256), bar);
+        bulk_copy_to_peer(peer_addr(sRxML + split * mper, (uint32_t)lane),
+                          smem_addr(reinterpret_cast<float4*>(sVs + kPushMlOffset) + jlo), (uint32_t)(own * 16), bar);
+      }
+    }
+    const bool rx_ok = mbar_wait(&rx_full, 0u, kWaitNs);
+    if (!rx_ok && threadIdx.x == 0) atomicExch(A.err, 1);
+    cluster_arrive_relaxed();   // every copy into this CTA is done (its own copies' sources
+                                // are free once every CTA has arrived; no data rides on it)
+    __nv_bfloat16* out = reinterpret_cast<__nv_bfloat16*>(A.fm.out);
+    PushedPartials src;
+    src.o_base = sRx;
+    src.ml_base = sRxML;
+    src.per = mper;
+    src.lo = lo;
+    src.l16 = lane & 15;
+    for (int rr0 = lo + 2 * warp; merge_warp && rr0 < hi; rr0 += 2 * kWarps) {   // uniform per warp
+      const int rr = rr0 + (lane >> 4);
+      src.i = (rr < hi ? rr : rr0) - lo;
+      combine_row16_from<__nv_bfloat16>(A.q, H, A.nsplit, A.cur.Tc > 0, out, A.fm.so[0], A.fm.so[1], A.fm.so[2],
+                                        A.fm.m_p, A.fm.l_p, A.fm.o_p, bh, r0 + rr, rr < hi, src);
+    }
+    cluster_wait();   // no CTA leaves while a copy out of its shared memory may be running
+    if (!rx_ok) mbar_wait(&rx_full, 0u, kWaitNs);   // late copies land before this CTA exits
+    return;
+  }
   if (A.cmerge) {
     // ---- cluster merge: the group's splits are the cluster's CTAs (rank = split); each
     // merges its share of the rows from every rank's shared memory, by half warps
     cluster_sync();   // every split's rows and (m, l) are in its shared memory
-    const int R_blk = min(kRows, R - r0);
     const int per = (R_blk + (int)gridDim.y - 1) / (int)gridDim.y;
     const int lo = split * per, hi = min(R_blk, lo + per);
     __nv_bfloat16* out = reinterpret_cast<__nv_bfloat16*>(A.fm.out);
@@ -906,7 +989,6 @@ __device__ __forceinline__ void attn_fa_body(const Args& A) {
   __syncthreads();
   // this split's share of the group's rows: a half warp per row with at most 16 prefix
   // splits, else a warp per row (weights scratch in the slots)
-  const int R_blk = min(kRows, R - r0);
   const int per = (R_blk + (int)gridDim.y - 1) / (int)gridDim.y;
   const int lo = split * per, hi = min(R_blk, lo + per);
   __nv_bfloat16* out = reinterpret_cast<__nv_bfloat16*>(A.fm.out);
@@ -1069,7 +1151,9 @@ int launch_attn_partial_fa(const ma_rows& q, const ma_kv& kv, int H, const ma_bl
     }
     if (cluster_nc[cs] > 0 && (long long)grid.x * grid.z <= cluster_nc[cs]) {
       Args Ac = A;
-      Ac.cmerge = 1;
+      // one key tile per CTA: the splits push their rows to the merging CTA (K slots 1
+      // and 2 of every CTA stay free), else every CTA pulls them from the others
+      Ac.cmerge = (!pair && !packed && split_len <= kBN && cur.Tc <= kBN) ? 2 : 1;
       Ac.fm = *fm;
       cfg.numAttrs = 2;
       if (cudaLaunchKernelEx(&cfg, kernel, Ac) == cudaSuccess) {

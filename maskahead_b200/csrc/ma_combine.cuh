@@ -133,12 +133,14 @@ __device__ __forceinline__ void combine_row(const ma_rows& q, int H, const Parti
 }
 
 // A half warp (16 lanes) merges row r when there are at most 16 prefix splits, for bf16
-// partials of D = 128: lane l of the half holds channels 8l..8l+7 and split l's (m, l)
-// pair, so a warp merges two rows at once (row r of the upper half ignored when !valid;
-// every lane of the warp must call, shuffles span the whole warp). The arithmetic is
-// combine_row's: w_s = l_s exp(m_s - M), prefix statistics, then the current block.
-// src.o(s) gives this lane's 8 channels of split s's row (bf16), src.ml(s) its (m, l);
-// split nsplit is the current block.
+// partials of D = 128: lane l of the half holds channels 8l..8l+7, so a warp merges two
+// rows at once (row r of the upper half ignored when !valid). The arithmetic is
+// combine_row's: w_s = l_s exp(m_s - M), prefix statistics, then the current block. Every
+// lane loads all splits' rows and (m, l) pairs at once (or, for a source with kLaneMl,
+// lane i the pair of split i, shared by shuffles; every lane of the warp must then call)
+// and derives the weights itself: the merge is one round trip to wherever the partials are,
+// with no reduction chain after it. src.o(s) gives this lane's 8 channels of split s's row
+// (bf16), src.ml(s) its (m, l); split nsplit is the current block.
 template <typename QT, typename Src>
 __device__ __forceinline__ void combine_row16_from(const ma_rows& q, int H, int nsplit, bool has_cur,
                                                    QT* __restrict__ out, int64_t so0, int64_t so1, int64_t so2,
@@ -148,32 +150,38 @@ __device__ __forceinline__ void combine_row16_from(const ma_rows& q, int H, int 
   const int G = q.Hq / H;
   const int R = G * q.T;
   const int l16 = threadIdx.x & 15;
-  const int half = threadIdx.x & 16;
   const int d0 = 8 * l16;
-  // every split's 8 channels and the current block's, in flight first
   uint4 buf[16];
+  float2 ml[16];
 #pragma unroll
   for (int i = 0; i < 16; ++i) buf[i] = (valid && i < nsplit) ? src.o(i) : make_uint4(0u, 0u, 0u, 0u);
+  if constexpr (Src::kLaneMl) {   // lane i loads split i's pair, the half warp shares them
+    const float2 mine = (valid && l16 < nsplit) ? src.ml(l16) : make_float2(-INFINITY, 0.f);
+    const int half = threadIdx.x & 16;
+#pragma unroll
+    for (int i = 0; i < 16; ++i)
+      ml[i] = make_float2(__shfl_sync(0xffffffffu, mine.x, half | i), __shfl_sync(0xffffffffu, mine.y, half | i));
+  } else {
+#pragma unroll
+    for (int i = 0; i < 16; ++i) ml[i] = (valid && i < nsplit) ? src.ml(i) : make_float2(-INFINITY, 0.f);
+  }
   float2 mlc = make_float2(-INFINITY, 0.f);
   uint4 oc = make_uint4(0u, 0u, 0u, 0u);
   if (valid && has_cur) {
     mlc = src.ml(nsplit);
     oc = src.o(nsplit);
   }
-  const float2 mls = (valid && l16 < nsplit) ? src.ml(l16) : make_float2(-INFINITY, 0.f);
-  float M = mls.x;
+  float M = -INFINITY;
 #pragma unroll
-  for (int off = 8; off > 0; off >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, off));
+  for (int i = 0; i < 16; ++i) M = fmaxf(M, ml[i].x);
   const float Ms = (M == -INFINITY) ? 0.f : M;
-  const float w = l16 < nsplit ? mls.y * expf(mls.x - Ms) : 0.f;
-  float L = w;
-#pragma unroll
-  for (int off = 8; off > 0; off >>= 1) L += __shfl_xor_sync(0xffffffffu, L, off);
+  float L = 0.f;
   float A[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
 #pragma unroll
   for (int i = 0; i < 16; ++i) {
     if (i < nsplit) {
-      const float wi = __shfl_sync(0xffffffffu, w, half | i);
+      const float wi = ml[i].y * expf(ml[i].x - Ms);
+      L += wi;
       float f[8];
       bf16x8_to_float(buf[i], f);
 #pragma unroll
@@ -212,6 +220,7 @@ __device__ __forceinline__ void combine_row16_from(const ma_rows& q, int H, int 
 
 // The partial rows of the global split buffers (bf16, split s of row r at row0 + s*Rp).
 struct GlobalPartials {
+  static constexpr bool kLaneMl = false;
   const __nv_bfloat16* po;
   const float2* pml;
   int64_t row0, step;

@@ -225,6 +225,23 @@ __device__ __forceinline__ uint32_t cluster_rank() {
 __device__ __forceinline__ void cluster_sync() {
   asm volatile("barrier.cluster.arrive.release.aligned;\nbarrier.cluster.wait.acquire.aligned;\n" ::: "memory");
 }
+// the two halves of the cluster barrier, for work between the arrival and the wait (every
+// thread of every CTA in the cluster arrives once per phase, warp-converged)
+__device__ __forceinline__ void cluster_arrive_relaxed() {
+  asm volatile("barrier.cluster.arrive.relaxed.aligned;\n" ::: "memory");
+}
+__device__ __forceinline__ void cluster_wait() {
+  asm volatile("barrier.cluster.wait.acquire.aligned;\n" ::: "memory");
+}
+// A bulk copy (the copy engine; `bytes` a multiple of 16, both addresses 16-byte aligned)
+// from this CTA's shared memory into another CTA's, counted on that CTA's mbarrier
+// (complete_tx): the receiver learns that the data is there by waiting on its own barrier.
+// dst and mbar are shared::cluster addresses of the same CTA (peer_addr), src a
+// shared::cta address of this one, whose bytes must stay unchanged until the copy is done.
+__device__ __forceinline__ void bulk_copy_to_peer(uint32_t dst, uint32_t src, uint32_t bytes, uint32_t mbar) {
+  asm volatile("cp.async.bulk.shared::cluster.shared::cta.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];\n"
+               ::"r"(dst), "r"(src), "r"(bytes), "r"(mbar) : "memory");
+}
 // address of this shared variable in CTA `rank` of the cluster
 __device__ __forceinline__ uint32_t peer_addr(const void* p, uint32_t rank) {
   uint32_t a;

@@ -10,7 +10,11 @@ CTA sharing the K/V tiles (R > 128), and the 64-key kernel on the same inputs
 prefixes shorter than one tile, one key past a tile boundary, several splits, a
 current block longer than one tile, one and two 128-row M tiles, several row tiles
 (R = G*T > 256), and query blocks whose length neither divides nor is a multiple of 128
-(T = 96, 160: the row tile is loaded as four 32-row pieces).
+(T = 96, 160: the row tile is loaded as four 32-row pieces). The splits of a row block
+merge in one launch: in a thread-block cluster (each CTA pulling its share of the rows
+from the others' shared memory, or -- when every split is at most one key tile, as in the
+sub-steps -- each CTA pushing its rows into the shared memory of the CTA that merges
+them), else through global memory in a cooperative launch, else in a separate pass.
 """
 
 from __future__ import annotations
@@ -54,6 +58,9 @@ def _run(which, q, k, v, kc, vc, causal, q_pos0, c_pos0, want_prefix):
     (2, 6, 2, 64, 127, 64, 32),      # one partial tile
     (1, 7, 1, 32, 129, 32, 32),      # a tile boundary + 1, R = 224 (two M tiles)
     (1, 28, 4, 32, 1100, 32, 32),    # cfg2-like heads, several splits
+    (1, 28, 4, 32, 1024, 32, 32),    # cfg2's sub-step: nine one-tile splits push their rows
+    (3, 8, 2, 32, 300, 32, 32),      # one-tile splits, six clusters, R = 128
+    (2, 8, 2, 32, 256, 32, 0),       # one-tile splits, R = 128 over three CTAs per cluster
     (1, 8, 2, 128, 5000, 160, 64),   # current block longer than a tile, R = 512 (two row tiles)
     (1, 4, 4, 256, 2048, 256, 128),  # T = 256: one query head per row tile
     (1, 16, 4, 96, 3000, 96, 32),    # T = 96 (a block + two probe blocks): 32-row query pieces
@@ -107,10 +114,12 @@ def test_fa_kernel_large_logits_rescale(which, Hq):
     np.testing.assert_allclose(out.float().cpu().numpy(), want.float().numpy(), rtol=TOL, atol=TOL)
 
 
-def test_fa_kernel_repeated_calls_are_identical():
-    """The fused merge's counters reset between calls: the same inputs give the same bits."""
+@pytest.mark.parametrize("n", [8192, 1024])
+def test_fa_kernel_repeated_calls_are_identical(n):
+    """The fused merge's counters reset between calls, and the pushed merge's barriers
+    start afresh: the same inputs give the same bits."""
     gen = torch.Generator().manual_seed(3)
-    B, Hq, H, T, n, D = 1, 28, 4, 32, 8192, 128
+    B, Hq, H, T, D = 1, 28, 4, 32, 128
     dev = [torch.randn(*s, generator=gen).to(torch.bfloat16).to(DEV)
            for s in ((B, Hq, T, D), (B, H, n, D), (B, H, n, D), (B, H, T, D), (B, H, T, D))]
     first, _ = _run(0, *dev, 32, 0, 0, False)
