@@ -223,12 +223,23 @@ class Workload:
         if c["kv"] == "bf16":
             self.K = randn(L, B, H, n, D)
             self.V = randn(L, B, H, n, D)
+            self.prefix_all = Prefix.dense(self.K.flatten(0, 1), self.V.flatten(0, 1))
         elif c["kv"] == "k4v4_token":
+            packs = []
             for _ in range(L):
                 k = torch.randn(B, H, n, D, generator=g, device=device)
                 _outliers(k, g)
-                self.prefixes.append(pack_prefix(k.to(bf), randn(B, H, n, D), key_mode="token"))
+                packs.append(pack_prefix(k.to(bf), randn(B, H, n, D), key_mode="token"))
                 del k
+            # one layer-stacked allocation [L*B, H, n, ...] per field (a cache's layers side
+            # by side), each layer's Prefix a view of its slice
+            fields = ("kq", "ks", "kz", "vq", "vs", "vz", "kch")
+            stacked = {f: torch.cat([getattr(pk, f) for pk in packs]) for f in fields}
+            meta = {sl: getattr(packs[0], sl) for sl in Prefix.__slots__
+                    if sl not in fields and sl not in ("kf", "vf", "mask", "pages", "lens")}
+            del packs
+            self.prefixes = [Prefix(**{f: stacked[f][l * B:(l + 1) * B] for f in fields}, **meta) for l in range(L)]
+            self.prefix_all = Prefix(**stacked, **meta)
         elif c["kv"] == "k4v4_token_paged":
             page = c["page"]
             need = [(x + page - 1) // page for x in lens]
@@ -261,9 +272,21 @@ class Workload:
         else:
             raise ValueError(c["kv"])
         # each layer's compact cache: the read set's K/V rows, gathered at step 0 and attended
-        # by the sub-steps (the session's state.key / state.value)
-        self.compact = [(torch.empty(B, H, c["k"], D, device=device, dtype=bf),
-                         torch.empty(B, H, c["k"], D, device=device, dtype=bf)) for _ in range(L)]
+        # by the sub-steps (the session's state.key / state.value); layer-stacked
+        self.CK = torch.empty(L, B, H, c["k"], D, device=device, dtype=bf)
+        self.CV = torch.empty_like(self.CK)
+        self.compact = [(self.CK[layer], self.CV[layer]) for layer in range(L)]
+        # one sequence per rank (cfg2, cfg3, cfg4): a layer's selection is a few CTAs per
+        # launch, so step 0 selects for every layer at once after the step-0 attention of
+        # all layers (the session's finish_step0), over the layer-stacked cache and the
+        # prefix statistics each layer's attention writes into its slice of MP / LP
+        self.batched = B == 1 and c["kv"] in ("bf16", "k4v4_token")
+        G = Hq // H
+        self.MP = torch.empty(L, B, H, G * T, device=device, dtype=torch.float32)
+        self.LP = torch.empty_like(self.MP)
+        if c["retention"]:
+            self.MPR = torch.empty(L, B, H, G * T * (1 + P), device=device, dtype=torch.float32)
+            self.LPR = torch.empty_like(self.MPR)
         torch.cuda.synchronize(device)
         self.outputs = None
         from maskahead_b200.shard import HeadGather, PeerHeadGather
@@ -299,6 +322,8 @@ class Workload:
                                             value_score_prefix)
 
         c = self.cfg
+        if self.batched:
+            return self.block_step_batched(retain)
         # a retention block runs its lookahead probe merged into step 0 (lookahead_merge):
         # one launch over [block | probe blocks] per layer instead of a second pass
         merge = retain and c["retention"]
@@ -334,6 +359,59 @@ class Workload:
                 score = torch.stack([value_score_prefix(a[layer], self.prefix(layer)) for layer in range(c["L"])])
             keep = lookahead_survivors(self.pos, score, c["C"], recent_window=c["W"], sink_tokens=c["sinks"])
         self.outputs = (outs, idxs, keep)
+        return self.outputs
+
+
+    def block_step_batched(self, retain: bool):
+        """The block-step with step 0's selection run once for every layer: the step-0
+        attention of each layer (its prefix statistics into the layer's slice of MP / LP),
+        then select_step0 over the layer-stacked queries, cache and statistics (mass, score,
+        top-k and the gather into the layer-stacked compact caches -- and, on a retention
+        block, the merged probe's mass -- one launch each for all layers), then the
+        sub-steps of every layer."""
+        import torch
+        from maskahead_b200.hotpath import (compact_attention, lookahead_survivors, select_step0,
+                                            step0_attention, value_score, value_score_prefix)
+        from maskahead_b200.layouts import Prefix
+
+        c = self.cfg
+        L, T = c["L"], c["T"]
+        merge = retain and c["retention"]
+        outs = []
+        for layer in range(L):
+            if merge:
+                out, _ = step0_attention(self.QP[layer], self.prefix(layer), self.KCP[layer], self.VCP[layer],
+                                         scaling=self.scale, stats_out=(self.MPR[layer], self.LPR[layer]),
+                                         probe_blocks=c["probe_blocks"], block_size=T)
+                outs.append(self.gather_heads(out[:, :, :T]))
+            else:
+                out, _ = step0_attention(self.Q[layer, 0], self.prefix(layer), self.KC[layer, 0], self.VC[layer, 0],
+                                         scaling=self.scale, stats_out=(self.MP[layer], self.LP[layer]))
+                outs.append(self.gather_heads(out))
+        # B == 1: merging the layer and batch axes of the queries is a view
+        if merge:
+            q0, st = self.QP.flatten(0, 1), (self.MPR.flatten(0, 1), self.LPR.flatten(0, 1))
+        else:
+            q0, st = self.Q[:, 0].flatten(0, 1), (self.MP.flatten(0, 1), self.LP.flatten(0, 1))
+        res = select_step0(q0, self.prefix_all, st, query_indices=self.rows, topk=c["k"], value_aware=True,
+                           scaling=self.scale, gather=True, compact_out=(self.CK.flatten(0, 1), self.CV.flatten(0, 1)),
+                           probe_blocks=c["probe_blocks"] if merge else 0, block_size=T, probe_rows=self.probe_rows)
+        for layer in range(L):
+            compact = Prefix.dense(self.CK[layer], self.CV[layer])
+            for s in range(1, c["substeps"]):
+                outs[layer] = self.gather_heads(compact_attention(self.Q[layer, s], compact, None, self.KC[layer, s],
+                                                                  self.VC[layer, s], scaling=self.scale))
+        n = self.prefix_all.n
+        idx = res.indices.view(L, self.B, self.H, -1)
+        keep = None
+        if merge:
+            a = res.mass.view(L, self.B, self.H, n) + res.probe_mass.view(L, self.B, self.H, n)
+            if self.V is not None:
+                score = value_score(a, self.V)
+            else:   # packed values in place, every layer in one call
+                score = value_score_prefix(a.flatten(0, 1), self.prefix_all).view(L, self.B, self.H, n)
+            keep = lookahead_survivors(self.pos, score, c["C"], recent_window=c["W"], sink_tokens=c["sinks"])
+        self.outputs = (outs, [idx[layer] for layer in range(L)], keep)
         return self.outputs
 
 

@@ -12,6 +12,13 @@ These functions are what the reference session's fast path does per layer
                       ascending top-k read set and (gather=True) the read set's K/V rows
                       gathered once into a compact dense cache (1438-1447, gather_dequant
                       1174-1190).
+  step0_attention     fast_step0's attention half (the prefix statistics optionally into
+                      the caller's layer-stacked buffers).
+  select_step0        fast_step0's selection half on the step-0 statistics, for one layer
+                      or for every layer of the step at once, stacked along the batch
+                      axis (the session's finish_step0, 1264-1285: nothing reads a layer's
+                      read set before its first sub-step, so the selection of all layers
+                      can follow the step-0 forward as one pass).
   gather_read_set     that gather on its own.
   compact_attention   _compact_attention / sdpa_compact (1286-1336; reference.py:403-426):
                       attention over [read set | block], from the compact cache (as the
@@ -35,13 +42,14 @@ from .kernels.ops import gather_packed_kv, select_topk_indices
 from .kernels.splitk import prefix_scores, splitk_attention
 from .layouts import Prefix, as_prefix, kv_descriptor
 
-__all__ = ["Step0Result", "dense_required", "fast_attend", "fast_step0", "unpacked_prefix", "gather_read_set", "compact_attention", "probe_attention", "value_score",
+__all__ = ["Step0Result", "dense_required", "fast_attend", "fast_step0", "step0_attention", "select_step0",
+           "unpacked_prefix", "gather_read_set", "compact_attention", "probe_attention", "value_score",
            "value_score_prefix", "lookahead_survivors"]
 
 
 @dataclass(slots=True)
 class Step0Result:
-    out: torch.Tensor                    # [B, Hq, T, D] attention output
+    out: torch.Tensor | None             # [B, Hq, T, D] attention output (None from select_step0)
     indices: torch.Tensor | None         # [B, Hkv, k] ascending read set (None: dense layer)
     mass: torch.Tensor | None            # [B, Hkv, n] prefix mass of the selection rows
     score: torch.Tensor | None           # [B, Hkv, n] value-aware score (value_aware only)
@@ -123,26 +131,78 @@ def fast_step0(query: torch.Tensor, prefix, current_key: torch.Tensor, current_v
     prefix mass of the probe rows (positions block_size.., or the device int32 probe_rows)
     times probe_blocks (session.py:2331). That replaces the separate probe_attention pass
     over the prefix.
+
+    fast_step0 = step0_attention, then select_step0 on its statistics.
+    """
+    need_stats = select or want_mass or probe_blocks > 0
+    out, stats = step0_attention(query, prefix, current_key, current_value, scaling=scaling, want_stats=need_stats,
+                                 unpack=unpack, probe_blocks=probe_blocks, block_size=block_size)
+    if stats is None:
+        return Step0Result(out, None, None, None)
+    res = select_step0(query, prefix, stats, query_indices=query_indices, topk=topk, value_aware=value_aware,
+                       scaling=scaling, select=select, want_mass=want_mass, gather=gather,
+                       compact_out=compact_out, probe_blocks=probe_blocks, block_size=block_size,
+                       probe_rows=probe_rows)
+    res.out = out
+    return res
+
+
+def step0_attention(query: torch.Tensor, prefix, current_key: torch.Tensor, current_value: torch.Tensor, *,
+                    scaling: float | None = None, want_stats: bool = True,
+                    stats_out: tuple[torch.Tensor, torch.Tensor] | None = None, unpack: bool | None = None,
+                    probe_blocks: int = 0, block_size: int = 32):
+    """fast_step0's attention half: the output over [live prefix | block] (block-causal by
+    block_size when probe_blocks > 0 merges the probe) and, with want_stats, the prefix
+    statistics stats = (M_p, L_p, O_p, prefix read) that select_step0 takes (None for an
+    empty prefix or without want_stats). A packed prefix is unpacked first as fast_step0
+    says (the stats then name the unpacked copy, which the next call's unpack overwrites).
+
+    stats_out = (M_p, L_p): contiguous fp32 [B, Hkv, G*T] buffers -- one layer's slice of
+    layer-stacked buffers -- that receive the statistics instead (O_p is not computed):
+    the session's step-0 forward, whose selection select_step0 runs for every layer at once
+    over the stacked statistics and the layer-stacked cache.
     """
     prefix = as_prefix(prefix)
     if query.dtype == torch.bfloat16 and _needs_unpack(prefix, query.shape[0], current_key.shape[1], query.shape[3],
                                                          unpack):
         prefix = unpacked_prefix(prefix, query.shape[0], current_key.shape[1], query.shape[3])
+    causal = block_size if probe_blocks > 0 else 0
     if prefix.n == 0:
-        out, _ = splitk_attention(query, prefix, current_key, current_value, scaling=scaling)
-        return Step0Result(out, None, None, None)
-    need_stats = select or want_mass or probe_blocks > 0
-    out, stats = splitk_attention(query, prefix, current_key, current_value, scaling=scaling,
-                                  causal_block=block_size if probe_blocks > 0 else 0, want_prefix=need_stats)
-    if not need_stats:
-        return Step0Result(out, None, None, None)
+        out, _ = splitk_attention(query, prefix, current_key, current_value, scaling=scaling, causal_block=causal)
+        return out, None
+    out, stats = splitk_attention(query, prefix, current_key, current_value, scaling=scaling, causal_block=causal,
+                                  want_prefix=want_stats, stats_out=stats_out)
+    return out, stats
+
+
+def select_step0(query: torch.Tensor, prefix, stats, *, query_indices, topk: int, value_aware: bool = True,
+                 scaling: float | None = None, select: bool = True, want_mass: bool = False,
+                 gather: bool = False, compact_out: tuple[torch.Tensor, torch.Tensor] | None = None,
+                 probe_blocks: int = 0, block_size: int = 32,
+                 probe_rows: torch.Tensor | None = None) -> Step0Result:
+    """The selection half of fast_step0 (session.py:1424-1454): from the step-0 prefix
+    statistics stats = (M_p, L_p, ...) of splitk_attention, the mass, score, read set,
+    compact cache and merged probe's mass, as fast_step0 returns them (out None).
+
+    Several layers at once: stack them along the batch axis -- query [L*B, Hq, T, D] (the
+    step-0 queries), prefix over [L*B, Hkv, n, D] (a layer-stacked cache), stats of
+    [L*B, Hkv, G*T] (each layer's attention writing its slice through stats_out) and
+    compact_out [L*B, Hkv, >= k, D] -- and one launch per kernel serves every layer: the
+    mass of 4 KV heads at a time is a few CTAs per launch, of 28 layers' at once a wave.
+    Every slot's mass is the same number either way (its sum over the rows does not depend
+    on the launch), and so are the read sets up to ties of the value-aware score, whose
+    head centre is summed in a launch-dependent order.
+    """
+    prefix = as_prefix(prefix)
+    if len(stats) < 4 or stats[3] is None:
+        stats = (stats[0], stats[1], None, prefix)
     probe_mass = None
     if probe_blocks > 0:
         rows = probe_rows if probe_rows is not None else list(range(block_size, query.shape[2]))
         probe_mass, _ = prefix_scores(query, prefix, stats, rows, value=False, scaling=scaling)
         probe_mass = probe_mass * probe_blocks
         if not (select or want_mass):
-            return Step0Result(out, None, None, None, probe_mass=probe_mass)
+            return Step0Result(None, None, None, None, probe_mass=probe_mass)
     value = select and value_aware
     mass, score = prefix_scores(query, prefix, stats, query_indices, value=value, scaling=scaling)
     idx = None
@@ -153,8 +213,8 @@ def fast_step0(query: torch.Tensor, prefix, current_key: torch.Tensor, current_v
         idx, _ = select_topk_indices(rank, k, prefix.mask, want_values=False, lens=prefix.lens)
     compact = None
     if select and gather:
-        compact = gather_read_set(prefix, idx, dtype=query.dtype, out=compact_out)
-    return Step0Result(out, idx, mass, score, compact, probe_mass)
+        compact = gather_read_set(stats[3], idx, dtype=query.dtype, out=compact_out)
+    return Step0Result(None, idx, mass, score, compact, probe_mass)
 
 
 def unpacked_prefix(prefix, batch: int, heads: int, head_dim: int) -> Prefix:

@@ -25,13 +25,16 @@ __all__ = ["Prefix", "splitk_attention", "prefix_scores", "dequantize_prefix"]
 
 def splitk_attention(query, prefix, current_key, current_value, *, scaling=None,
                      causal_block: int = 0, q_pos0: int = 0, c_pos0: int = 0, want_prefix: bool = False,
-                     **_tuning):
+                     stats_out=None, **_tuning):
     """softmax over [prefix | current] for every query row (splitk.py:493-579).
 
     Returns (out [B,Hq,T,D] in the query dtype, stats) with stats = (M_p, L_p, O_p,
     prefix) when want_prefix: prefix-only max and sum [B,Hkv,R] and normalized output
     [B,Hkv,R,D] fp32 per row r = g*T + t. causal_block > 0: query q_pos0+t sees current
     key c_pos0+j only if (c_pos0+j)//causal_block <= (q_pos0+t)//causal_block.
+    stats_out = (M_p, L_p) or (M_p, L_p, O_p): contiguous fp32 buffers of those shapes to
+    write the statistics into (e.g. one layer's slice of layer-stacked buffers); O_p is
+    then computed only if given. Implies want_prefix.
     """
     lib = _lib.lib()
     prefix = as_prefix(prefix)
@@ -52,7 +55,15 @@ def splitk_attention(query, prefix, current_key, current_value, *, scaling=None,
         desc, kv = None, _lib.MaKV()
         kv.layout, kv.dtype = _lib.MA_KV_DENSE, rows.dtype
     out = torch.empty_like(query)
-    if want_prefix:
+    if stats_out is not None:
+        mp, lp = stats_out[0], stats_out[1]
+        op = stats_out[2] if len(stats_out) > 2 else None
+        for x, shape in ((mp, (b, hkv, r)), (lp, (b, hkv, r)), (op, (b, hkv, r, d))):
+            if x is not None and (tuple(x.shape) != shape or x.dtype != torch.float32 or not x.is_contiguous()
+                                  or x.device != dev):
+                raise ValueError(f"stats_out: need contiguous float32 {shape} tensors on {dev}")
+        want_prefix = True
+    elif want_prefix:
         mp = torch.empty((b, hkv, r), device=dev, dtype=torch.float32)
         lp = torch.empty_like(mp)
         op = torch.empty((b, hkv, r, d), device=dev, dtype=torch.float32)
