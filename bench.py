@@ -218,7 +218,7 @@ class Workload:
         self.rows = torch.arange(T, device=device, dtype=torch.int32)
         self.probe_rows = torch.arange(T, T * (1 + P), device=device, dtype=torch.int32)
         self.scale = D ** -0.5
-        self.K = self.V = None
+        self.K = self.V = self.UK = self.UV = None
         self.prefixes = []
         if c["kv"] == "bf16":
             self.K = randn(L, B, H, n, D)
@@ -240,6 +240,10 @@ class Workload:
             del packs
             self.prefixes = [Prefix(**{f: stacked[f][l * B:(l + 1) * B] for f in fields}, **meta) for l in range(L)]
             self.prefix_all = Prefix(**stacked, **meta)
+            # each layer's step-0 unpack (the path's bf16 copy of the packed prefix) into its
+            # slice of layer-stacked buffers, which the batched selection then reads
+            self.UK = torch.empty(L, B, H, n, D, device=device, dtype=bf)
+            self.UV = torch.empty_like(self.UK)
         elif c["kv"] == "k4v4_token_paged":
             page = c["page"]
             need = [(x + page - 1) // page for x in lens]
@@ -301,6 +305,20 @@ class Workload:
 
     def compact_buffers(self, layer: int):
         return self.compact[layer]
+
+    def unpack_out(self, layer: int):
+        """Where a packed prefix's step-0 unpack goes in the batched block-step: this
+        layer's slice of the stacked copy (None: the library's scratch)."""
+        return None if self.UK is None else (self.UK[layer], self.UV[layer])
+
+    def prefix_sel(self):
+        """The layer-stacked cache the batched selection reads: the bf16 cache, or the
+        step's unpacked copies of a packed one (the same bf16 numbers)."""
+        from maskahead_b200.layouts import Prefix
+
+        if self.UK is not None:
+            return Prefix.dense(self.UK.flatten(0, 1), self.UV.flatten(0, 1))
+        return self.prefix_all
 
     def prefix(self, layer: int):
         from maskahead_b200.layouts import Prefix
@@ -382,18 +400,20 @@ class Workload:
             if merge:
                 out, _ = step0_attention(self.QP[layer], self.prefix(layer), self.KCP[layer], self.VCP[layer],
                                          scaling=self.scale, stats_out=(self.MPR[layer], self.LPR[layer]),
-                                         probe_blocks=c["probe_blocks"], block_size=T)
+                                         unpack_out=self.unpack_out(layer), probe_blocks=c["probe_blocks"],
+                                         block_size=T)
                 outs.append(self.gather_heads(out[:, :, :T]))
             else:
                 out, _ = step0_attention(self.Q[layer, 0], self.prefix(layer), self.KC[layer, 0], self.VC[layer, 0],
-                                         scaling=self.scale, stats_out=(self.MP[layer], self.LP[layer]))
+                                         scaling=self.scale, stats_out=(self.MP[layer], self.LP[layer]),
+                                         unpack_out=self.unpack_out(layer))
                 outs.append(self.gather_heads(out))
         # B == 1: merging the layer and batch axes of the queries is a view
         if merge:
             q0, st = self.QP.flatten(0, 1), (self.MPR.flatten(0, 1), self.LPR.flatten(0, 1))
         else:
             q0, st = self.Q[:, 0].flatten(0, 1), (self.MP.flatten(0, 1), self.LP.flatten(0, 1))
-        res = select_step0(q0, self.prefix_all, st, query_indices=self.rows, topk=c["k"], value_aware=True,
+        res = select_step0(q0, self.prefix_sel(), st, query_indices=self.rows, topk=c["k"], value_aware=True,
                            scaling=self.scale, gather=True, compact_out=(self.CK.flatten(0, 1), self.CV.flatten(0, 1)),
                            probe_blocks=c["probe_blocks"] if merge else 0, block_size=T, probe_rows=self.probe_rows)
         for layer in range(L):
@@ -406,10 +426,7 @@ class Workload:
         keep = None
         if merge:
             a = res.mass.view(L, self.B, self.H, n) + res.probe_mass.view(L, self.B, self.H, n)
-            if self.V is not None:
-                score = value_score(a, self.V)
-            else:   # packed values in place, every layer in one call
-                score = value_score_prefix(a.flatten(0, 1), self.prefix_all).view(L, self.B, self.H, n)
+            score = value_score(a, self.V if self.V is not None else self.UV)   # every layer in one call
             keep = lookahead_survivors(self.pos, score, c["C"], recent_window=c["W"], sink_tokens=c["sinks"])
         self.outputs = (outs, [idx[layer] for layer in range(L)], keep)
         return self.outputs
@@ -422,14 +439,20 @@ def fused_scores(cfg: dict, share: dict) -> bool:
 
 
 def kernel_launches(cfg: dict, share: dict, retain: bool) -> int:
-    """Our kernels in one block-step: step 0 = attention partial + combine + mass (with the
-    fused value score, or + value apply) + top-k; each sub-step = partial + combine;
-    retention = per layer the merged probe's mass launch, then value centre + apply (once
-    for dense values, per layer for packed ones) and the survivors."""
-    step0 = 4 if fused_scores(cfg, share) else 5
-    n = (step0 + 2 * (cfg["substeps"] - 1)) * cfg["L"]
+    """Our kernels in one block-step (an upper bound; the bench counts the captured graph's
+    kernel nodes when it can): step 0 = attention partial + combine + mass (with the fused
+    value score, or + value apply) + top-k + gather per layer -- with the selection batched
+    over the layers (one sequence), the attention per layer and the rest once; each
+    sub-step = partial + combine; retention = the merged probe's mass launch (per layer, or
+    once batched), then value centre + apply (once for dense values, per layer for packed
+    ones unless batched) and the survivors."""
+    L = cfg["L"]
+    batched = len(share["lens"]) == 1 and cfg["kv"] in ("bf16", "k4v4_token")
+    fused = (L * share["H"] <= 148) if batched else fused_scores(cfg, share)
+    select = 3 if fused else 4
+    n = L * (2 + 2 * (cfg["substeps"] - 1)) + select * (1 if batched else L)
     if retain and cfg["retention"]:
-        n += cfg["L"] + (2 if cfg["kv"] == "bf16" else 2 * cfg["L"]) + 1
+        n += (1 if batched else L) + (2 if cfg["kv"] == "bf16" or batched else 2 * L) + 1
     return n
 
 
@@ -760,6 +783,13 @@ def kernel_rooflines(c: dict, wl, share: dict, dev, stream, side, reps: int, wor
                                      lens=getattr(wl, "lens_t", None))
         idxs.append(idx)
     compacts = [gather_read_set(pre_k(layer), idxs[layer], out=wl.compact_buffers(layer)) for layer in range(L)]
+    if wl.batched:   # the selection's inputs of every layer, stacked as the block-step passes them
+        q_all = wl.Q[:, 0].flatten(0, 1)
+        sel_prefix = wl.prefix_sel()
+        st_all = (torch.cat([st[0] for st in stats]), torch.cat([st[1] for st in stats]), None, sel_prefix)
+        sc_all = torch.cat(scores)
+        idx_all = torch.cat(idxs)
+        ck_all, cv_all = wl.CK.flatten(0, 1), wl.CV.flatten(0, 1)
     torch.cuda.synchronize(dev)
 
     b_tok = token_bytes(c)
@@ -786,11 +816,33 @@ def kernel_rooflines(c: dict, wl, share: dict, dev, stream, side, reps: int, wor
                               ab["substep_layer"], 4.0 * Hq * T * (B * k + B * T) * D,
                               "attn_partial_fa over the compact cache (merge in the launch)"),
     }
+    per_launch = {name: 1 for name in families}
+    if wl.batched:
+        # the block-step's selection: one launch over every layer (the layer-stacked inputs);
+        # the per-launch figures below are then for all L layers
+        sel = {
+            "mass_value_score": (lambda layer: prefix_scores(q_all, sel_prefix, st_all, wl.rows, value=True,
+                                                             scaling=wl.scale),
+                                 L * (n_sum * H * (512 if packed else b_tok) + q_bytes + 2 * n_sum * H * 4),
+                                 L * 2.0 * Hq * T * n_sum * D,
+                                 "prefix_mass_fa over the layer-stacked cache (every layer in one launch)"
+                                 + (", the step's unpacked bf16 copies" if packed else "")),
+            "select_topk": (lambda layer: select_topk_indices(sc_all, idx_all.shape[2], want_values=False),
+                            L * (n_sum * H * 4 + B * H * k * 8), 0.0,
+                            "select_topk over every layer's scores in one launch"),
+            "gather": (lambda layer: gather_read_set(sel_prefix, idx_all, out=(ck_all, cv_all)),
+                       L * (ab["gather_layer"] + (B * H * c["k"] * (512 - b_tok) if packed else 0)), 0.0,
+                       "gather_kv of every layer's read set into the layer-stacked compact caches"
+                       + (" (from the unpacked bf16 copies)" if packed else "")),
+        }
+        families.update(sel)
+        per_launch.update({name: L for name in sel})
     out = {}
     for name, (fn, nbytes, flops, what) in families.items():
-        for layer in range(L):          # workspaces at their final size before the capture
+        calls = 1 if per_launch[name] > 1 else L   # one launch covers every layer, or one per layer
+        for layer in range(calls):      # workspaces at their final size before the capture
             fn(layer)
-        g, _, _ = _capture(lambda: [fn(layer) for layer in range(L)], side, stream)
+        g, _, _ = _capture(lambda: [fn(layer) for layer in range(calls)], side, stream)
         for _ in range(2):
             g.replay()
         total = 0.0
@@ -802,10 +854,10 @@ def kernel_rooflines(c: dict, wl, share: dict, dev, stream, side, reps: int, wor
             e1.record(stream)
             e1.synchronize()
             total += e0.elapsed_time(e1)
-        us = _max_over_ranks(total / (reps * L), world, dev) * 1e3
+        us = _max_over_ranks(total / (reps * calls), world, dev) * 1e3
         gbs = nbytes / (us * 1e-6) / 1e9
         row = {"kernel": what, "us_per_launch": us, "bytes_per_launch": int(nbytes), "achieved_gbs": gbs,
-               "hbm_frac": gbs / hbm}
+               "hbm_frac": gbs / hbm, "layers_per_launch": per_launch[name]}
         if flops:
             tfl = flops / (us * 1e-6) / 1e12
             row.update(tflops=tfl, tensor_frac_burst=tfl / tf_burst, tensor_frac_sustained=tfl / tf_sust)

@@ -150,6 +150,7 @@ def fast_step0(query: torch.Tensor, prefix, current_key: torch.Tensor, current_v
 def step0_attention(query: torch.Tensor, prefix, current_key: torch.Tensor, current_value: torch.Tensor, *,
                     scaling: float | None = None, want_stats: bool = True,
                     stats_out: tuple[torch.Tensor, torch.Tensor] | None = None, unpack: bool | None = None,
+                    unpack_out: tuple[torch.Tensor, torch.Tensor] | None = None,
                     probe_blocks: int = 0, block_size: int = 32):
     """fast_step0's attention half: the output over [live prefix | block] (block-causal by
     block_size when probe_blocks > 0 merges the probe) and, with want_stats, the prefix
@@ -160,12 +161,14 @@ def step0_attention(query: torch.Tensor, prefix, current_key: torch.Tensor, curr
     stats_out = (M_p, L_p): contiguous fp32 [B, Hkv, G*T] buffers -- one layer's slice of
     layer-stacked buffers -- that receive the statistics instead (O_p is not computed):
     the session's step-0 forward, whose selection select_step0 runs for every layer at once
-    over the stacked statistics and the layer-stacked cache.
+    over the stacked statistics and the layer-stacked cache. unpack_out = (key, value): the
+    buffers a packed prefix is unpacked into (unpacked_prefix's out), so that the
+    selection can read every layer's unpacked copy.
     """
     prefix = as_prefix(prefix)
     if query.dtype == torch.bfloat16 and _needs_unpack(prefix, query.shape[0], current_key.shape[1], query.shape[3],
                                                          unpack):
-        prefix = unpacked_prefix(prefix, query.shape[0], current_key.shape[1], query.shape[3])
+        prefix = unpacked_prefix(prefix, query.shape[0], current_key.shape[1], query.shape[3], out=unpack_out)
     causal = block_size if probe_blocks > 0 else 0
     if prefix.n == 0:
         out, _ = splitk_attention(query, prefix, current_key, current_value, scaling=scaling, causal_block=causal)
@@ -217,17 +220,27 @@ def select_step0(query: torch.Tensor, prefix, stats, *, query_indices, topk: int
     return Step0Result(None, idx, mass, score, compact, probe_mass)
 
 
-def unpacked_prefix(prefix, batch: int, heads: int, head_dim: int) -> Prefix:
+def unpacked_prefix(prefix, batch: int, heads: int, head_dim: int, *,
+                    out: tuple[torch.Tensor, torch.Tensor] | None = None) -> Prefix:
     """The prefix dequantized into contiguous bf16 [B, Hkv, n, D] K/V held in a per-device
-    scratch (reused by the next call), with the prefix's mask and lengths."""
+    scratch (reused by the next call), or in out = (key, value) -- e.g. one layer's slice
+    of layer-stacked buffers that a later select_step0 reads -- with the prefix's mask and
+    lengths."""
     from .kernels.splitk import dequantize_prefix
 
     prefix = as_prefix(prefix)
     n = prefix.n
     dev = (prefix.kq if prefix.nq else prefix.kf).device
     nbytes = batch * heads * n * head_dim * 2
-    kb = _lib.workspace(dev, "unpack_k", nbytes)[:nbytes].view(torch.bfloat16).view(batch, heads, n, head_dim)
-    vb = _lib.workspace(dev, "unpack_v", nbytes)[:nbytes].view(torch.bfloat16).view(batch, heads, n, head_dim)
+    if out is not None:
+        kb, vb = out
+        for x in (kb, vb):
+            if (tuple(x.shape) != (batch, heads, n, head_dim) or x.dtype != torch.bfloat16 or not x.is_contiguous()
+                    or x.device != dev):
+                raise ValueError(f"out: need contiguous bfloat16 {(batch, heads, n, head_dim)} tensors on {dev}")
+    else:
+        kb = _lib.workspace(dev, "unpack_k", nbytes)[:nbytes].view(torch.bfloat16).view(batch, heads, n, head_dim)
+        vb = _lib.workspace(dev, "unpack_v", nbytes)[:nbytes].view(torch.bfloat16).view(batch, heads, n, head_dim)
     rc = _lib.MA_ERR_UNSUPPORTED
     if n > 0 and prefix.lens is not None:
         # a ragged batch: only the slots below each sequence's length are written (every

@@ -11,7 +11,9 @@ the head centre's sum (rtol 1e-5), the read sets equal up to that score's ties (
 1e-5 of the k-th score, the bar of the other selection tests) and the compact cache
 bit-exact where the read sets agree; on a retention block the merged probe's mass bit
 for bit as well. Cases: bf16 and k4v4 token-mode caches (the packed one stacked as one
-allocation of all layers, read in place by the selection), four layers of cfg2's heads.
+allocation of all layers, read by the selection in place, or through the step's unpacked
+copies that each layer's attention leaves in its slice of stacked buffers), four layers
+of cfg2's heads.
 """
 
 from __future__ import annotations
@@ -46,13 +48,13 @@ def _caches(kind, g):
     return per, Prefix(**stacked, **meta)
 
 
-@pytest.mark.parametrize("kind", ["bf16", "k4v4_token"])
+@pytest.mark.parametrize("kind", ["bf16", "k4v4_token", "k4v4_token_unpacked"])
 @pytest.mark.parametrize("probe_blocks", [0, 2])
 def test_all_layers_selected_at_once_equal_the_per_layer_step0(kind, probe_blocks):
     from maskahead_b200.hotpath import fast_step0, select_step0, step0_attention
 
     g = torch.Generator(device=DEV).manual_seed(11 + probe_blocks)
-    per, stacked = _caches(kind, g)
+    per, stacked = _caches("bf16" if kind == "bf16" else "k4v4_token", g)
     Tq = T * (1 + probe_blocks)
     q = torch.randn(L, B, HQ, Tq, D, generator=g, device=DEV).to(torch.bfloat16)
     kc = torch.randn(L, B, H, Tq, D, generator=g, device=DEV).to(torch.bfloat16)
@@ -75,9 +77,18 @@ def test_all_layers_selected_at_once_equal_the_per_layer_step0(kind, probe_block
     mp = torch.empty(L, B, H, G * Tq, device=DEV, dtype=torch.float32)
     lp = torch.empty_like(mp)
     outs = []
+    uk = uv = None
+    if kind == "k4v4_token_unpacked":
+        from maskahead_b200.layouts import Prefix
+
+        uk = torch.empty(L, B, H, N, D, device=DEV, dtype=torch.bfloat16)
+        uv = torch.empty_like(uk)
     for i in range(L):
-        out, _ = step0_attention(q[i], per[i], kc[i], vc[i], scaling=scale, stats_out=(mp[i], lp[i]), **kw)
+        out, _ = step0_attention(q[i], per[i], kc[i], vc[i], scaling=scale, stats_out=(mp[i], lp[i]),
+                                 unpack_out=None if uk is None else (uk[i], uv[i]), **kw)
         outs.append(out)
+    if uk is not None:
+        stacked = Prefix.dense(uk.flatten(0, 1), uv.flatten(0, 1))
     CK = torch.empty(L, B, H, K, D, device=DEV, dtype=torch.bfloat16)
     CV = torch.empty_like(CK)
     got = select_step0(q.flatten(0, 1), stacked, (mp.flatten(0, 1), lp.flatten(0, 1)), query_indices=rows, topk=K,
