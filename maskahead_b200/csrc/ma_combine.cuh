@@ -140,8 +140,9 @@ __device__ __forceinline__ void combine_row(const ma_rows& q, int H, const Parti
 // lane i the pair of split i, shared by shuffles; every lane of the warp must then call)
 // and derives the weights itself: the merge is one round trip to wherever the partials are,
 // with no reduction chain after it. src.o(s) gives this lane's 8 channels of split s's row
-// (bf16), src.ml(s) its (m, l); split nsplit is the current block.
-template <typename QT, typename Src>
+// (bf16), src.ml(s) its (m, l); split nsplit is the current block. NS (nsplit <= NS <= 16)
+// bounds the unrolled loops: a launch that merges few splits keeps few registers.
+template <typename QT, typename Src, int NS = 16>
 __device__ __forceinline__ void combine_row16_from(const ma_rows& q, int H, int nsplit, bool has_cur,
                                                    QT* __restrict__ out, int64_t so0, int64_t so1, int64_t so2,
                                                    float* __restrict__ m_p, float* __restrict__ l_p,
@@ -151,19 +152,20 @@ __device__ __forceinline__ void combine_row16_from(const ma_rows& q, int H, int 
   const int R = G * q.T;
   const int l16 = threadIdx.x & 15;
   const int d0 = 8 * l16;
-  uint4 buf[16];
-  float2 ml[16];
+  static_assert(NS >= 1 && NS <= 16, "at most 16 prefix splits");
+  uint4 buf[NS];
+  float2 ml[NS];
 #pragma unroll
-  for (int i = 0; i < 16; ++i) buf[i] = (valid && i < nsplit) ? src.o(i) : make_uint4(0u, 0u, 0u, 0u);
+  for (int i = 0; i < NS; ++i) buf[i] = (valid && i < nsplit) ? src.o(i) : make_uint4(0u, 0u, 0u, 0u);
   if constexpr (Src::kLaneMl) {   // lane i loads split i's pair, the half warp shares them
     const float2 mine = (valid && l16 < nsplit) ? src.ml(l16) : make_float2(-INFINITY, 0.f);
     const int half = threadIdx.x & 16;
 #pragma unroll
-    for (int i = 0; i < 16; ++i)
+    for (int i = 0; i < NS; ++i)
       ml[i] = make_float2(__shfl_sync(0xffffffffu, mine.x, half | i), __shfl_sync(0xffffffffu, mine.y, half | i));
   } else {
 #pragma unroll
-    for (int i = 0; i < 16; ++i) ml[i] = (valid && i < nsplit) ? src.ml(i) : make_float2(-INFINITY, 0.f);
+    for (int i = 0; i < NS; ++i) ml[i] = (valid && i < nsplit) ? src.ml(i) : make_float2(-INFINITY, 0.f);
   }
   float2 mlc = make_float2(-INFINITY, 0.f);
   uint4 oc = make_uint4(0u, 0u, 0u, 0u);
@@ -173,12 +175,12 @@ __device__ __forceinline__ void combine_row16_from(const ma_rows& q, int H, int 
   }
   float M = -INFINITY;
 #pragma unroll
-  for (int i = 0; i < 16; ++i) M = fmaxf(M, ml[i].x);
+  for (int i = 0; i < NS; ++i) M = fmaxf(M, ml[i].x);
   const float Ms = (M == -INFINITY) ? 0.f : M;
   float L = 0.f;
   float A[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-  for (int i = 0; i < 16; ++i) {
+  for (int i = 0; i < NS; ++i) {
     if (i < nsplit) {
       const float wi = ml[i].y * expf(ml[i].x - Ms);
       L += wi;
@@ -231,7 +233,7 @@ struct GlobalPartials {
   __device__ __forceinline__ float2 ml(int s) const { return __ldcg(&pml[row0 + (int64_t)s * step]); }
 };
 
-template <typename QT>
+template <typename QT, int NS = 16>
 __device__ __forceinline__ void combine_row16(const ma_rows& q, int H, const Partials& P, int nsplit, bool has_cur,
                                               QT* __restrict__ out, int64_t so0, int64_t so1, int64_t so2,
                                               float* __restrict__ m_p, float* __restrict__ l_p,
@@ -242,7 +244,8 @@ __device__ __forceinline__ void combine_row16(const ma_rows& q, int H, const Par
   src.row0 = (int64_t)bh * P.S * P.Rp + r;
   src.step = P.Rp;
   src.d0 = 8 * (threadIdx.x & 15);
-  combine_row16_from<QT>(q, H, nsplit, has_cur, out, so0, so1, so2, m_p, l_p, o_p, bh, r, valid, src);
+  combine_row16_from<QT, GlobalPartials, NS>(q, H, nsplit, has_cur, out, so0, so1, so2, m_p, l_p, o_p, bh, r, valid,
+                                              src);
 }
 
 }  // namespace ma
