@@ -165,6 +165,13 @@ MA_API const char* ma_status_string(int status);
  * queried under one setting may be too small under another. Not part of the reference's
  * interface.                                                                          */
 MA_API int ma_set_attention_kernel(int which);
+/* Work per CTA of the mass / value-score kernel over a ragged batch (ma_kv.lens set; process-
+ * wide; for tests and A/B timing): at most `tiles` 128-slot tiles per CTA, so that heads of
+ * long sequences spread over several CTAs (the score then follows in a second launch);
+ * 0 = automatic (16 tiles when the batch has fewer heads than twice the SM count, else
+ * no cap), < 0 = no cap (one CTA per head when the heads fill the GPU, the score in the
+ * same launch). Returns the previous setting. Not part of the reference's interface.  */
+MA_API int ma_set_mass_tiles(int tiles);
 /* 1 when the TMA-pipelined attention and scoring kernels read this prefix as it is stored
  * (dense bf16 without mask or paging; token-mode k4v4 without a dense tail or mask, its
  * tiles dequantized by producer warps of those kernels), 0 when a caller is better served

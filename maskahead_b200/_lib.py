@@ -75,6 +75,7 @@ _SIGNATURES = {
     "ma_version": (_i32, []),
     "ma_status_string": (ctypes.c_char_p, [_i32]),
     "ma_set_attention_kernel": (_i32, [_i32]),
+    "ma_set_mass_tiles": (_i32, [_i32]),
     "ma_kv_read_in_place": (_i32, [_P(MaKV), _i32]),
     "ma_last_cuda_error": (ctypes.c_char_p, []),
     "ma_workspace_status": (_i32, [_vp, _sz, _vp]),

@@ -119,6 +119,9 @@ struct __align__(64) Args {
   int* err;
   int fuse;
   int cmerge;                   // the group's splits form one cluster: partials in shared memory
+  int fold;                     // the current block is the last prefix split's final key tile
+                                // (no split of its own; no prefix-only statistics)
+  int direct;                   // one split per row block: the epilogue writes the output rows
   FusedMerge fm;
 };
 
@@ -296,7 +299,19 @@ __device__ __forceinline__ void attn_fa_body(const Args& A) {
   if (is_cur && A.causal_block > 0)
     vis_end = min(end, ((A.q_pos0 + t_row) / A.causal_block + 1) * A.causal_block - A.c_pos0);
   if (!row_ok) vis_end = begin;
-  const int ntiles = end > begin ? (end - begin + kBN - 1) / kBN : 0;
+  const int ntp = end > begin ? (end - begin + kBN - 1) / kBN : 0;   // key tiles of [begin, end)
+  // folded: the last prefix split also takes the current block, as one more key tile (keys
+  // [0, Tc) of the block's maps), so the block needs no split of its own
+  const bool fold_here = !PACKED && A.fold && !is_cur && split == A.nsplit - 1 && A.cur.Tc > 0;
+  const int ntiles = ntp + (fold_here ? 1 : 0);
+  const bool has_cur = A.cur.Tc > 0 && !A.fold;   // the merges: a block split after the prefix ones
+  // key tile t's tensor map (K or V) and first key: the prefix's, or the block's for the
+  // block split and for a folded split's last tile
+  auto tile_map = [&](int t, bool v, int& x) -> const CUtensorMap* {
+    const bool blk = is_cur || (fold_here && t >= ntp);
+    x = blk ? (t - (is_cur ? 0 : ntp)) * kBN : begin + t * kBN;
+    return blk ? (v ? &A.cvmap : &A.ckmap) : (v ? &A.vmap : &A.kmap);
+  };
   const int nU = kQT * ntiles;   // S tiles: u = kQT t + M tile
   const float c2 = A.scale * kLog2e;
   const int group = bh * gridDim.x + blockIdx.x;
@@ -318,6 +333,10 @@ __device__ __forceinline__ void attn_fa_body(const Args& A) {
     if (!dq) {
       prefetch_map(is_cur ? &A.ckmap : &A.kmap);
       prefetch_map(is_cur ? &A.cvmap : &A.vmap);
+      if (fold_here) {
+        prefetch_map(&A.ckmap);
+        prefetch_map(&A.cvmap);
+      }
     }
     for (int i = 0; i < KS; ++i) mbar_init(&kfull[i], dq ? kDqWarps : 1);
     for (int i = 0; i < VS; ++i) mbar_init(&vfull[i], dq ? kDqWarps : 1);
@@ -346,8 +365,6 @@ __device__ __forceinline__ void attn_fa_body(const Args& A) {
     // the queries and the first K and V tiles start loading now, before the TMEM
     // allocation and the setup barrier
     pdl_wait();   // with a programmatic launch, the inputs may come from the kernel before
-    const CUtensorMap* km = is_cur ? &A.ckmap : &A.kmap;
-    const CUtensorMap* vm = is_cur ? &A.cvmap : &A.vmap;
     tma::expect_tx(&q_full, (uint32_t)(kQT * kQBytes));
     for (int qt = 0; qt < kQT; ++qt) {
       const int rq = r0 + qt * kRowTile;   // rows past R load neighbouring or zero rows: never used
@@ -367,8 +384,16 @@ __device__ __forceinline__ void attn_fa_body(const Args& A) {
       }
     }
     if (!dq) {
-      for (int i = 0; i < KS && i < ntiles; ++i) tma_tile(km, b, h, begin + i * kBN, sKs + i * kKVBytes, &kfull[i]);
-      for (int i = 0; i < VS && i < ntiles; ++i) tma_tile(vm, b, h, begin + i * kBN, sVs + i * kKVBytes, &vfull[i]);
+      for (int i = 0; i < KS && i < ntiles; ++i) {
+        int x;
+        const CUtensorMap* m = tile_map(i, false, x);
+        tma_tile(m, b, h, x, sKs + i * kKVBytes, &kfull[i]);
+      }
+      for (int i = 0; i < VS && i < ntiles; ++i) {
+        int x;
+        const CUtensorMap* m = tile_map(i, true, x);
+        tma_tile(m, b, h, x, sVs + i * kKVBytes, &vfull[i]);
+      }
     } else {   // the first raw tiles into the staging ring
       for (int i = 0; i < NST && i < ntiles; ++i)
         packed::stage_tile(A.kv, b, h, begin + i * kBN, min(end, begin + (i + 1) * kBN), sStg + i * packed::kStageBytes,
@@ -404,8 +429,6 @@ __device__ __forceinline__ void attn_fa_body(const Args& A) {
       int sN = 0, pN = 0, oD = 0;                   // S issued, P.V issued, P.V seen complete
       // PACKED: raw tiles staged, staged tiles seen consumed by the producer warps
       int rIss = dq ? min(NST, ntiles) : ntiles, rfObs = 0;
-      const CUtensorMap* km = is_cur ? &A.ckmap : &A.kmap;
-      const CUtensorMap* vm = is_cur ? &A.cvmap : &A.vmap;
       const bool q_ok = mbar_wait(&q_full, 0);
       ok = q_ok;
       const uint32_t idS = idesc_bf16(kRowTile, kBN, false, false);
@@ -474,15 +497,25 @@ __device__ __forceinline__ void attn_fa_body(const Args& A) {
         // TMA warp (bf16) or the producer warps (packed) refill it -- a TMA issue can stall
         // its thread for hundreds of cycles, which this loop must not spend
         if (kIss < ntiles && pN >= kQT * (kIss - KS + 1)) {
-          if (dq || !PACKED) mbar_arrive(&kfree[kIss % KS]);
-          else tma_tile(km, b, h, begin + kIss * kBN, sKs + (kIss % KS) * kKVBytes, &kfull[kIss % KS]);
+          if (dq || !PACKED) {
+            mbar_arrive(&kfree[kIss % KS]);
+          } else {
+            int x;
+            const CUtensorMap* m = tile_map(kIss, false, x);
+            tma_tile(m, b, h, x, sKs + (kIss % KS) * kKVBytes, &kfull[kIss % KS]);
+          }
           ++kIss;
           progress = true;
         }
         // a V slot is free once the tile's last P.V completed
         if (vIss < ntiles && oD >= kQT * (vIss - VS + 1)) {
-          if (dq || !PACKED) mbar_arrive(&vfree[vIss % VS]);
-          else tma_tile(vm, b, h, begin + vIss * kBN, sVs + (vIss % VS) * kKVBytes, &vfull[vIss % VS]);
+          if (dq || !PACKED) {
+            mbar_arrive(&vfree[vIss % VS]);
+          } else {
+            int x;
+            const CUtensorMap* m = tile_map(vIss, true, x);
+            tma_tile(m, b, h, x, sVs + (vIss % VS) * kKVBytes, &vfull[vIss % VS]);
+          }
           ++vIss;
           progress = true;
         }
@@ -526,8 +559,6 @@ __device__ __forceinline__ void attn_fa_body(const Args& A) {
     // was consumed), so at the end the last ones issued are waited for.
     if (lane == 0) {
       pdl_wait();   // with a programmatic launch, the cache may come from the kernel before
-      const CUtensorMap* km = is_cur ? &A.ckmap : &A.kmap;
-      const CUtensorMap* vm = is_cur ? &A.cvmap : &A.vmap;
       int kN = min(KS, ntiles), vN = min(VS, ntiles);
       uint64_t t_idle = 0;
       bool armed = false;
@@ -535,12 +566,16 @@ __device__ __forceinline__ void attn_fa_body(const Args& A) {
       while (kN < ntiles || vN < ntiles) {
         bool progress = false;
         if (kN < ntiles && mbar_test(&kfree[kN % KS], (uint32_t)((kN / KS) - 1) & 1u)) {
-          tma_tile(km, b, h, begin + kN * kBN, sKs + (kN % KS) * kKVBytes, &kfull[kN % KS]);
+          int x;
+          const CUtensorMap* m = tile_map(kN, false, x);
+          tma_tile(m, b, h, x, sKs + (kN % KS) * kKVBytes, &kfull[kN % KS]);
           ++kN;
           progress = true;
         }
         if (vN < ntiles && mbar_test(&vfree[vN % VS], (uint32_t)((vN / VS) - 1) & 1u)) {
-          tma_tile(vm, b, h, begin + vN * kBN, sVs + (vN % VS) * kKVBytes, &vfull[vN % VS]);
+          int x;
+          const CUtensorMap* m = tile_map(vN, true, x);
+          tma_tile(m, b, h, x, sVs + (vN % VS) * kKVBytes, &vfull[vN % VS]);
           ++vN;
           progress = true;
         }
@@ -633,7 +668,8 @@ __device__ __forceinline__ void attn_fa_body(const Args& A) {
       if (!ok) s_abort = 1;
       if (s_abort) break;
       if (warp_rows) {
-        const int lim = vis_end - (begin + t * kBN);   // keys i >= lim of the tile are hidden
+        // keys i >= lim of the tile are hidden (a folded block tile: its first Tc keys exist)
+        const int lim = (fold_here && t == ntp) ? (row_ok ? A.cur.Tc : 0) : vis_end - (begin + t * kBN);
         const bool full = __all_sync(0xffffffffu, lim >= kBN);
         float sv[64];
         // the row max: keys 64..127 (read, not kept), then keys 0..63 (kept)
@@ -726,6 +762,14 @@ __device__ __forceinline__ void attn_fa_body(const Args& A) {
   if (threadIdx.x == 0) pdl_launch_dependents();   // the next kernel's prologue may start
   if (push) cluster_wait();   // every CTA's rx_full is initialized: the sends may start
 
+  // direct (one split per row block): the row of the output this thread's row goes to
+  uint4* out_row = nullptr;
+  if (A.direct && row_ok) {
+    const int g = r / T, tt = r - (r / T) * T;
+    out_row = reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(A.fm.out) + (int64_t)b * A.fm.so[0] +
+                                       (int64_t)(h * G + g) * A.fm.so[1] + (int64_t)tt * A.fm.so[2]);
+  }
+  const uint4 nan8 = make_uint4(0x7fc07fc0u, 0x7fc07fc0u, 0x7fc07fc0u, 0x7fc07fc0u);   // bf16 NaN x 8
   if (PAIR && softmax_warp) {
     // each M tile's rows are final in their own group: o = O_g / l under the group's running
     // max; warp (quarter, grp) writes all 128 channels of its 32 rows (the slots are
@@ -738,8 +782,13 @@ __device__ __forceinline__ void attn_fa_body(const Args& A) {
     if (s_abort != 0) {
       if (threadIdx.x == 0) atomicExch(A.err, 1);
       if (row_ok) {
-        if (A.cmerge) sML[rc] = make_float2(NAN, NAN);
-        else A.P.ml[prow] = make_float2(NAN, NAN);
+        if (A.direct) {
+          for (int i = 0; i < kD / 8; ++i) out_row[i] = nan8;
+        } else if (A.cmerge) {
+          sML[rc] = make_float2(NAN, NAN);
+        } else {
+          A.P.ml[prow] = make_float2(NAN, NAN);
+        }
       }
     } else {
       if (row_ok) {
@@ -749,9 +798,9 @@ __device__ __forceinline__ void attn_fa_body(const Args& A) {
       }
       const float inv = l_run > 0.f ? 1.f / l_run : 0.f;
       if (warp_rows) {
-        const bool via_tma = ntiles > 0 && A.tma_out && !A.cmerge;
+        const bool via_tma = ntiles > 0 && A.tma_out && !A.cmerge && !A.direct;
         uint8_t* box = sKs + warp * 2 * kOutBox;   // two 32-row boxes: channels 0..63, 64..127
-        uint4* dst = reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(A.P.o) + prow * kD);
+        uint4* dst = A.direct ? out_row : reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(A.P.o) + prow * kD);
         const uint32_t tOg = taddr + lane_base + kColO + 128 * grp;
 #pragma unroll 1
         for (int c = 0; c < 4; ++c) {
@@ -824,9 +873,15 @@ __device__ __forceinline__ void attn_fa_body(const Args& A) {
     if (s_abort != 0) {
       if (threadIdx.x == 0) atomicExch(A.err, 1);
       if (row_ok && grp == 0) {
-        if (push) sMLq[rl] = make_float4(NAN, NAN, 0.f, 0.f);
-        else if (A.cmerge) sML[rl] = make_float2(NAN, NAN);
-        else A.P.ml[prow] = make_float2(NAN, NAN);
+        if (A.direct) {
+          for (int i = 0; i < kD / 8; ++i) out_row[i] = nan8;
+        } else if (push) {
+          sMLq[rl] = make_float4(NAN, NAN, 0.f, 0.f);
+        } else if (A.cmerge) {
+          sML[rl] = make_float2(NAN, NAN);
+        } else {
+          A.P.ml[prow] = make_float2(NAN, NAN);
+        }
       }
     } else {
       // the exact max: l under M times 2^(M - m_true) <= 1; o = acc / l is the same under
@@ -839,12 +894,13 @@ __device__ __forceinline__ void attn_fa_body(const Args& A) {
       }
       const float inv = l > 0.f ? 1.f / l : 0.f;
       if (warp_rows) {
-        const bool via_tma = ntiles > 0 && A.tma_out && !A.cmerge;
+        const bool via_tma = ntiles > 0 && A.tma_out && !A.cmerge && !A.direct;
         // the warp's 32 rows x 64 channels -> one box in the K slots, 128-byte swizzled
         // (chunk q of line i at q ^ (i & 7)), stored by lane 0; else straight to global
         uint8_t* box = sKs + warp * kOutBox;
         uint8_t* line = box + lane * 128;
-        uint4* dst = reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(A.P.o) + prow * kD + 64 * grp);
+        uint4* dst = A.direct ? out_row + 8 * grp
+                              : reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(A.P.o) + prow * kD + 64 * grp);
         const uint32_t tO0 = taddr + lane_base + kColO + 64 * grp, tO1 = tO0 + 128;
 #pragma unroll 1
         for (int c = 0; c < 2; ++c) {
@@ -933,7 +989,7 @@ __device__ __forceinline__ void attn_fa_body(const Args& A) {
     for (int rr0 = lo + 2 * warp; merge_warp && rr0 < hi; rr0 += 2 * kWarps) {   // uniform per warp
       const int rr = rr0 + (lane >> 4);
       src.i = (rr < hi ? rr : rr0) - lo;
-      combine_row16_from<__nv_bfloat16>(A.q, H, A.nsplit, A.cur.Tc > 0, out, A.fm.so[0], A.fm.so[1], A.fm.so[2],
+      combine_row16_from<__nv_bfloat16>(A.q, H, A.nsplit, has_cur, out, A.fm.so[0], A.fm.so[1], A.fm.so[2],
                                         A.fm.m_p, A.fm.l_p, A.fm.o_p, bh, r0 + rr, rr < hi, src);
     }
     cluster_wait();   // no CTA leaves while a copy out of its shared memory may be running
@@ -954,7 +1010,7 @@ __device__ __forceinline__ void attn_fa_body(const Args& A) {
     for (int rr0 = lo + 2 * warp; merge_warp && rr0 < hi; rr0 += 2 * kWarps) {   // uniform per warp
       const int rr = rr0 + (lane >> 4);
       src.row = rr < hi ? rr : rr0;
-      combine_row16_from<__nv_bfloat16>(A.q, H, A.nsplit, A.cur.Tc > 0, out, A.fm.so[0], A.fm.so[1], A.fm.so[2],
+      combine_row16_from<__nv_bfloat16>(A.q, H, A.nsplit, has_cur, out, A.fm.so[0], A.fm.so[1], A.fm.so[2],
                                         A.fm.m_p, A.fm.l_p, A.fm.o_p, bh, r0 + rr, rr < hi, src);
     }
     cluster_sync();   // no CTA leaves while another may still read its shared memory
@@ -995,7 +1051,7 @@ __device__ __forceinline__ void attn_fa_body(const Args& A) {
   if (A.nsplit <= 16 && s_merge_ok) {
     for (int rr0 = lo + 2 * warp; merge_warp && rr0 < hi; rr0 += 2 * kWarps) {   // uniform per warp
       const int rr = rr0 + (lane >> 4);
-      combine_row16<__nv_bfloat16>(A.q, H, A.P, A.nsplit, A.cur.Tc > 0, out, A.fm.so[0], A.fm.so[1], A.fm.so[2],
+      combine_row16<__nv_bfloat16>(A.q, H, A.P, A.nsplit, has_cur, out, A.fm.so[0], A.fm.so[1], A.fm.so[2],
                                    A.fm.m_p, A.fm.l_p, A.fm.o_p, bh, r0 + rr, rr < hi);
     }
     return;
@@ -1003,7 +1059,7 @@ __device__ __forceinline__ void attn_fa_body(const Args& A) {
   float* sW = reinterpret_cast<float*>(sKs) + warp * kCombineMaxSplits;
   for (int rr = lo + warp; merge_warp && rr < hi; rr += kWarps) {
     if (s_merge_ok) {
-      combine_row<__nv_bfloat16, __nv_bfloat16>(A.q, H, A.P, A.nsplit, A.cur.Tc > 0, out, A.fm.so[0], A.fm.so[1],
+      combine_row<__nv_bfloat16, __nv_bfloat16>(A.q, H, A.P, A.nsplit, has_cur, out, A.fm.so[0], A.fm.so[1],
                                                 A.fm.so[2], A.fm.m_p, A.fm.l_p, A.fm.o_p, bh, r0 + rr, sW);
     } else if (lane == 0) {   // a split never arrived: the row is reported as NaN
       const int rw = r0 + rr;
@@ -1067,11 +1123,16 @@ bool fa_eligible(const ma_rows& q, const ma_kv& kv, const int64_t* idx, const ma
 
 int launch_attn_partial_fa(const ma_rows& q, const ma_kv& kv, int H, const ma_block& cur, float scale,
                            int causal_block, int q_pos0, int c_pos0, int n_keys, int split_len, int nsplit,
-                           const Partials& P, int* err, const FusedMerge* fm, bool* fused, cudaStream_t st) {
+                           const Partials& P, int* err, const FusedMerge* fm, bool fold, bool* fused,
+                           cudaStream_t st) {
   *fused = false;
   if (!fa_eligible(q, kv, nullptr, cur, n_keys) || !(scale > 0.f) || !P.o_bf16 || split_len % kBN != 0)
     return MA_ERR_UNSUPPORTED;
   const bool packed = n_keys > 0 && kv.layout == MA_KV_PACKED_TOKEN;
+  // a folded block: only into bf16 prefix splits, one key tile of the block, no causal mask
+  if (fold && (packed || causal_block > 0 || cur.Tc <= 0 || cur.Tc > kBN || n_keys <= 0 || nsplit < 1 ||
+               P.S != nsplit || fm == nullptr || fm->m_p || fm->l_p || fm->o_p))
+    return MA_ERR_ARG;
   const int threads = packed ? kThreadsP : kThreadsB;
   const int G = q.Hq / H;
   const int R = G * q.T;
@@ -1092,6 +1153,7 @@ int launch_attn_partial_fa(const ma_rows& q, const ma_kv& kv, int H, const ma_bl
   A.nsplit = nsplit;
   A.P = P;
   A.err = err;
+  A.fold = fold ? 1 : 0;
   if (n_keys > 0 && !packed && !(tma_map_rows(&A.kmap, kv.kf, q.B, H, kv.nf, kv.skf) &&
                                   tma_map_rows(&A.vmap, kv.vf, q.B, H, kv.nf, kv.svf)))
     return MA_ERR_UNSUPPORTED;
@@ -1118,6 +1180,15 @@ int launch_attn_partial_fa(const ma_rows& q, const ma_kv& kv, int H, const ma_bl
   if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
     return MA_ERR_CUDA;
   const int rows_per_split = (std::min(rows, R) + (int)grid.y - 1) / (int)grid.y;
+  if (fold && grid.y == 1) {
+    // one split holds every key of its rows: they are final in the epilogue, no merge
+    Args Ad = A;
+    Ad.direct = 1;
+    Ad.fm = *fm;
+    if (launch_pdl(kernel, grid, dim3(threads), smem, st, Ad) != cudaSuccess) return MA_ERR_CUDA;
+    *fused = true;
+    return MA_OK;
+  }
   // cluster merge: with at most 16 splits (prefix ones + the block) a group's CTAs form one
   // thread-block cluster and merge through distributed shared memory (no global round
   // trips); the hardware co-schedules a cluster's CTAs, so no cooperative launch is needed.
@@ -1153,7 +1224,7 @@ int launch_attn_partial_fa(const ma_rows& q, const ma_kv& kv, int H, const ma_bl
       Args Ac = A;
       // one key tile per CTA: the splits push their rows to the merging CTA (K slots 1
       // and 2 of every CTA stay free), else every CTA pulls them from the others
-      Ac.cmerge = (!pair && !packed && split_len <= kBN && cur.Tc <= kBN) ? 2 : 1;
+      Ac.cmerge = (!pair && !packed && !fold && split_len <= kBN && cur.Tc <= kBN) ? 2 : 1;
       Ac.fm = *fm;
       cfg.numAttrs = 2;
       if (cudaLaunchKernelEx(&cfg, kernel, Ac) == cudaSuccess) {

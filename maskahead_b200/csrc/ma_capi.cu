@@ -206,6 +206,15 @@ int run_attention(const ma_rows& q, const ma_kv& kv, int H, const ma_block& cur,
   // workspace too)
   const bool fa = mma && !fa_disabled() && fa_eligible(q, kv, idx, cur, n_keys);
   Plan p = plan_splits(q.B * H, R, n_keys, cur.Tc, mma, fa);
+  // the current block as the last prefix split's final key tile, when no prefix-only
+  // statistics are asked for and that split is long (or the only one): a block split of its
+  // own would be a CTA of one short tile per row block, plus a merge of one more split
+  const int kt = fa ? fa_key_tile() : 0;
+  const bool fold = fa && !idx && n_keys > 0 && kv.layout != MA_KV_PACKED_TOKEN && !m_p && !l_p && !o_p &&
+                    causal_block == 0 && cur.Tc > 0 && cur.Tc <= kt && p.nsplit >= 1 &&
+                    (p.nsplit == 1 || p.split_len >= 4 * kt);
+  if (fold) p.S = p.nsplit;
+  bool folded = false;
   if (!ws || ws_bytes < partials_bytes(q.B * H, p.S, p.Rp, q.D, p.o_bf16) + 512 + kSyncBytes)
     return MA_ERR_WORKSPACE;
   int* err = nullptr;
@@ -229,10 +238,12 @@ int run_attention(const ma_rows& q, const ma_kv& kv, int H, const ma_block& cur,
       rc = MA_ERR_UNSUPPORTED;
       if (fa) {
         rc = launch_attn_partial_fa(q, kv, H, cur, scale, causal_block, q_pos0, c_pos0, n_keys, p.split_len,
-                                    p.nsplit, P, err, &fm, &fused, st);
+                                    p.nsplit, P, err, &fm, fold, &fused, st);
         if (rc == MA_ERR_UNSUPPORTED) {   // a tensor map the TMA cannot describe: 64-key kernel
           p = plan_splits(q.B * H, R, n_keys, cur.Tc, mma);
           P = carve_partials(ws, q.B * H, p, q.D, &err, &sync);
+        } else {
+          folded = fold;
         }
       }
       if (rc == MA_ERR_UNSUPPORTED)
@@ -245,7 +256,7 @@ int run_attention(const ma_rows& q, const ma_kv& kv, int H, const ma_block& cur,
       if (rc != MA_OK) return rc;
     }
   }
-  return launch_attn_combine(q, H, P, p.nsplit, cur.Tc > 0, out, so, m_p, l_p, o_p, st);
+  return launch_attn_combine(q, H, P, p.nsplit, cur.Tc > 0 && !folded, out, so, m_p, l_p, o_p, st);
 }
 
 }  // namespace
@@ -290,6 +301,12 @@ int ma_set_attention_kernel(int which) {
   const int prev = g_attention_kernel;
   g_attention_kernel = (which >= 1 && which <= 3) ? which : 0;
   fa_set_pairs(g_attention_kernel == 2 ? 1 : g_attention_kernel == 3 ? 2 : 0);
+  return prev;
+}
+
+int ma_set_mass_tiles(int tiles) {
+  const int prev = fa_mass_tiles();
+  fa_set_mass_tiles(tiles);
   return prev;
 }
 

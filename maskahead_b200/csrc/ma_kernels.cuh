@@ -51,9 +51,14 @@ bool fa_eligible(const ma_rows& q, const ma_kv& kv, const int64_t* idx, const ma
 int fa_key_tile();
 int fa_row_tile(int R, int BH);
 void fa_set_pairs(int mode);
+// the mass kernel's CTAs over a ragged batch: at most `tiles` 128-slot tiles each (0: the
+// automatic policy, < 0: no cap)
+void fa_set_mass_tiles(int tiles);
+int fa_mass_tiles();
 int launch_attn_partial_fa(const ma_rows& q, const ma_kv& kv, int H, const ma_block& cur, float scale,
                            int causal_block, int q_pos0, int c_pos0, int n_keys, int split_len, int nsplit,
-                           const Partials& P, int* err, const FusedMerge* fm, bool* fused, cudaStream_t st);
+                           const Partials& P, int* err, const FusedMerge* fm, bool fold, bool* fused,
+                           cudaStream_t st);
 
 // ma_combine.cu
 int launch_attn_combine(const ma_rows& q, int H, const Partials& P, int nsplit, bool has_cur,

@@ -58,6 +58,7 @@ constexpr int kMaxSlots = 6;                 // tile slots (phase 1: K ring, the
 constexpr int kSmemLimit = 227 * 1024;       // dynamic + static shared memory of one CTA
 constexpr int kStaticSmem = 8 * 1024;        // bound on this kernel's static shared memory
 constexpr uint32_t kTmemCols = 512;          // two S^T buffers of up to 256 columns
+constexpr int kRaggedTiles = 16;             // tiles per CTA at most, for a ragged batch of few heads
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr uint64_t kWaitNs = 200000000ull;
 constexpr uint64_t kStallNs = 500000000ull;
@@ -82,6 +83,7 @@ struct __align__(64) Args {
   int H, T2, slots_per_cta, want_centre;
   int nK, nV;               // K ring and V ring slots (phase 2 streams V through nK + nV)
   int given;                // a_j given in `mass` (value score only: no K, no exponentials)
+  int score_only;           // phase 2 alone: a_j in `mass` and the centre in `centre` are final
   uint64_t peer_wait_ns;    // bound on the wait for the head's centre (other CTAs)
 };
 
@@ -154,7 +156,9 @@ __device__ __forceinline__ void mass_fa_body(const Args& A) {
     pdl_wait();      // before, with a programmatic launch); those slots get 0 below
     end = max(begin, min(end_all, A.kv.lens[b]));
   }
-  const int ntiles = end > begin ? (end - begin + kTile - 1) / kTile : 0;
+  const bool score_only = A.score_only != 0;
+  const int ntiles2 = end > begin ? (end - begin + kTile - 1) / kTile : 0;   // phase 2's tiles
+  const int ntiles = score_only ? 0 : ntiles2;                               // phase 1's
   const float inv_rows = 1.f / (float)R2;
   const float c2 = A.scale * kLog2e;
   const bool centre = A.want_centre != 0;
@@ -512,7 +516,8 @@ __device__ __forceinline__ void mass_fa_body(const Args& A) {
   if (warp == 0) tmem_dealloc(taddr, kTmemCols);
   const bool aborted = s_abort != 0;
   if (aborted && threadIdx.x == 0) atomicExch(A.err, 1);
-  if (!centre) return;
+  if (!centre && !score_only) return;
+  if (!score_only) {
 
   // centre partials per centre warp, in K slot 0 (drained; V tiles may stay in their slots;
   // nK >= 1 in every mode)
@@ -573,11 +578,12 @@ __device__ __forceinline__ void mass_fa_body(const Args& A) {
       atomicAdd(&A.sync[bh].y, 1u);
     }
   }
+  }   // !score_only
   if (A.score == nullptr) return;
 
   // ---- phase 2: a_j ||v_j - c|| for this CTA's slots (cooperative launch: every CTA of
   // the head is resident, so the generation advances)
-  if (!sLast && threadIdx.x == 0) {
+  if (!score_only && !sLast && threadIdx.x == 0) {
     const uint64_t t0 = global_ns();
     while (ld_acquire_u32(&A.sync[bh].y) == gen0) {
       if (global_ns() - t0 > A.peer_wait_ns) {
@@ -591,16 +597,16 @@ __device__ __forceinline__ void mass_fa_body(const Args& A) {
   __syncthreads();
   const bool ok_c = s_wait_ok != 0 && !aborted;
   // every V tile of the CTA still in its phase-1 slot (the V ring never wrapped)
-  const bool resident = ntiles <= nV;
+  const bool resident = !score_only && ntiles <= nV;
   if (!sum_warp) {
     if (!PACKED && warp == kSumWarps && lane == 0 && ok_c && !resident) {
       // the CTA's V tiles again, newest first, through every slot
       const uint64_t pol = tma::policy_evict_first();
       int u = 0;
-      for (; u < ntiles; ++u) {
+      for (; u < ntiles2; ++u) {
         const int slot = u % nS;
         if (u >= nS && !mbar_wait(&wfree[slot], (uint32_t)((u / nS) - 1) & 1u, kWaitNs)) break;
-        tile_load(&A.vmap, b, h, begin + (ntiles - 1 - u) * kTile, sSlot + slot * kTileBytes, &wfull[slot], pol);
+        tile_load(&A.vmap, b, h, begin + (ntiles2 - 1 - u) * kTile, sSlot + slot * kTileBytes, &wfull[slot], pol);
       }
       // drain (bounded): the last load of every slot
       for (int uu = max(0, u - nS); uu < u; ++uu)
@@ -620,9 +626,9 @@ __device__ __forceinline__ void mass_fa_body(const Args& A) {
       sum_sync();
       const float* ms = A.mass + (int64_t)b * A.sm0 + (int64_t)h * A.sm1;
       const float* cb = sC + 64 * chalf;
-      for (int u = 0; u < ntiles; ++u) {
-        const int slot = resident ? nK + (ntiles - 1 - u) : u % nS;
-        const int j0 = begin + (ntiles - 1 - u) * kTile;
+      for (int u = 0; u < ntiles2; ++u) {
+        const int slot = resident ? nK + (ntiles2 - 1 - u) : u % nS;
+        const int j0 = begin + (ntiles2 - 1 - u) * kTile;
         const int j = j0 + slot_lane;
         float aj = 0.f;   // issued before the tile's wait
         if (chalf == 0 && j < end) aj = __ldcg(ms + j);
@@ -700,6 +706,11 @@ bool tma_map_rows(CUtensorMap* map, const void* base, int B, int H, int n, const
 
 }  // namespace
 
+int g_mass_tiles = 0;   // fa_set_mass_tiles: 0 automatic, > 0 a fixed cap, -1 none
+
+void fa_set_mass_tiles(int tiles) { g_mass_tiles = tiles < 0 ? -1 : tiles; }
+int fa_mass_tiles() { return g_mass_tiles; }
+
 int launch_prefix_mass_fa(const ma_rows& q, const ma_kv& kv, int H, const int32_t* q_rows, int T2, const float* m_p,
                           const float* l_p, float scale, float* mass, int64_t sm0, int64_t sm1, float* score,
                           int64_t ss0, int64_t ss1, const ValueWs& w, bool want_centre, bool* fused, cudaStream_t st) {
@@ -761,6 +772,14 @@ int launch_prefix_mass_fa(const ma_rows& q, const ma_kv& kv, int H, const int32_
   if (per_head < 1) per_head = 1;
   int spc = (n + per_head - 1) / per_head;
   spc = ((spc + kTile - 1) / kTile) * kTile;
+  // a ragged batch (a serving batch of sequences of different lengths) with fewer heads
+  // than two waves of CTAs: a CTA per head, or a fixed share of each head, would leave the
+  // longest sequences' heads on the critical path; CTAs of at most kRaggedTiles tiles
+  // balance it over several waves (the centre is reduced by each head's last CTA, the score
+  // follows in a second launch). With more heads one CTA per head balances well enough and
+  // keeps the score in the same launch (V partly from L2).
+  const int cap = g_mass_tiles > 0 ? g_mass_tiles : (g_mass_tiles == 0 && BH < 2 * sms) ? kRaggedTiles : 0;
+  if (kv.lens && cap > 0 && spc > cap * kTile) spc = cap * kTile;
   A.slots_per_cta = spc;
   dim3 grid((n + spc - 1) / spc, BH);
   if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
@@ -802,7 +821,20 @@ int launch_prefix_mass_fa(const ma_rows& q, const ma_kv& kv, int H, const int32_
       }
     }
   }
-  return launch_pdl(kernel, grid, dim3(threads), smem, st, A) == cudaSuccess ? MA_OK : MA_ERR_CUDA;
+  if (launch_pdl(kernel, grid, dim3(threads), smem, st, A) != cudaSuccess) return MA_ERR_CUDA;
+  if (score != nullptr && want_centre && !packed) {
+    // the score in a second launch of the same grid: phase 2 alone, once every head's mass
+    // and centre are final (no CTA waits for another)
+    Args As = A;
+    As.given = 1;
+    As.score_only = 1;
+    As.want_centre = 0;
+    As.score = score;
+    As.centre = w.centre;
+    if (launch_pdl(kernel, grid, dim3(threads), smem, st, As) != cudaSuccess) return MA_ERR_CUDA;
+    *fused = true;
+  }
+  return MA_OK;
 }
 
 int launch_value_score_fa(const ma_kv& kv, int B, int H, int D, const float* a, int64_t sa0, int64_t sa1,

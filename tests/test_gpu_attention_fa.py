@@ -126,3 +126,48 @@ def test_fa_kernel_repeated_calls_are_identical(n):
     for _ in range(3):
         again, _ = _run(0, *dev, 32, 0, 0, False)
         assert torch.equal(first, again)
+
+
+@pytest.mark.parametrize("which,B,Hq,H,n,ragged", [
+    (0, 16, 28, 4, 1024, False),   # cfg5's sub-step shape: one split per row block, rows written directly
+    (3, 16, 28, 4, 1024, False),   # the same with pairs of M tiles
+    (2, 8, 28, 4, 8192, False),    # two 32-tile splits, the block folded into the second, merged in one launch
+    (3, 8, 28, 4, 8192, True),     # pairs, ragged lengths (some sequences end in the first split)
+    (0, 24, 28, 4, 6000, True),    # ragged, more CTAs than one wave: the separate merge
+])
+def test_fa_folded_block_matches_oracle(which, B, Hq, H, n, ragged):
+    """Without prefix-only statistics (the sub-steps) the current block is the last prefix
+    split's final key tile instead of a split of its own; a single split per row block then
+    writes its rows as the output. Compared with the oracle per sequence, and with the same
+    call asking for the statistics (block as its own split)."""
+    from maskahead_b200.kernels import splitk_attention
+    from maskahead_b200.layouts import Prefix
+
+    gen = torch.Generator().manual_seed(11 * n + B + which)
+    T = Tc = 32
+    D = 128
+    q = torch.randn(B, Hq, T, D, generator=gen).to(torch.bfloat16)
+    k = torch.randn(B, H, n, D, generator=gen).to(torch.bfloat16)
+    v = torch.randn(B, H, n, D, generator=gen).to(torch.bfloat16)
+    kc = torch.randn(B, H, Tc, D, generator=gen).to(torch.bfloat16)
+    vc = torch.randn(B, H, Tc, D, generator=gen).to(torch.bfloat16)
+    lens = (torch.randint(1, n + 1, (B,), generator=gen) if ragged else torch.full((B,), n)).to(torch.int32)
+    if ragged:
+        lens[0] = 1            # one key
+        lens[-1] = n           # every key
+    dq, dk, dv, dkc, dvc = (x.to(DEV) for x in (q, k, v, kc, vc))
+    pre = Prefix(kf=dk, vf=dv, nf=n, lens=lens.to(DEV) if ragged else None)
+    prev = _lib().ma_set_attention_kernel(which)
+    try:
+        out, _ = splitk_attention(dq, pre, dkc, dvc)
+        out_split, _ = splitk_attention(dq, pre, dkc, dvc, want_prefix=True)
+        torch.cuda.synchronize()
+    finally:
+        _lib().ma_set_attention_kernel(prev)
+    for bi in range(B):
+        L = int(lens[bi])
+        want, _ = oracle.prefix_attention(q[bi:bi + 1], k[bi:bi + 1, :, :L], v[bi:bi + 1, :, :L], kc[bi:bi + 1],
+                                          vc[bi:bi + 1])
+        np.testing.assert_allclose(out[bi:bi + 1].float().cpu().numpy(), want.float().numpy(), rtol=TOL, atol=TOL,
+                                   err_msg=f"sequence {bi} (length {L})")
+    np.testing.assert_allclose(out.float().cpu().numpy(), out_split.float().cpu().numpy(), rtol=TOL, atol=TOL)

@@ -112,3 +112,51 @@ def test_value_score_after_mass_calls_of_other_head_counts(lanes, n):
         torch.cuda.synchronize()
         want = oracle.value_score(a, v)
         np.testing.assert_allclose(got.numpy(), want.numpy(), rtol=5e-5, atol=1e-9)
+
+
+@pytest.mark.parametrize("B,n,cap", [
+    (16, 16384, 0),   # a ragged serving batch (64 heads): CTAs of at most 16 tiles, score in a second launch
+    (40, 9000, 8),    # more heads than SMs, 8-tile CTAs
+])
+def test_mass_fa_ragged_batch_split_matches_oracle(B, n, cap):
+    """A ragged batch (ma_kv.lens) spreads each head over CTAs of a few tiles -- the longest
+    sequences' heads no longer set the launch's time -- with the centre reduced by each
+    head's last CTA and the score in a second launch of phase 2 alone. Same bars as above,
+    per sequence against the oracle, and against one CTA per head (ma_set_mass_tiles(-1))."""
+    from maskahead_b200.kernels import prefix_scores, splitk_attention
+    from maskahead_b200.layouts import Prefix
+
+    gen = torch.Generator().manual_seed(n + B)
+    Hq, H, T, D = 28, 4, 32, 128
+    q = torch.randn(B, Hq, T, D, generator=gen).to(torch.bfloat16)
+    k = torch.randn(B, H, n, D, generator=gen).to(torch.bfloat16)
+    v = torch.randn(B, H, n, D, generator=gen).to(torch.bfloat16)
+    lens = torch.randint(1, n + 1, (B,), generator=gen).to(torch.int32)
+    lens[0], lens[1] = 1, n
+    qd = q.to(DEV)
+    pre = Prefix(kf=k.to(DEV), vf=v.to(DEV), nf=n, lens=lens.to(DEV))
+    _, st = splitk_attention(qd, pre, None, None, want_prefix=True)
+    rows = list(range(T))
+    rows_t = torch.tensor(rows, dtype=torch.int32, device=DEV)
+    out = {}
+    for setting in (cap, -1):
+        prev = _lib().ma_set_mass_tiles(setting)
+        try:
+            mass, score = prefix_scores(qd, pre, st, rows_t, value=True)
+            torch.cuda.synchronize()
+        finally:
+            _lib().ma_set_mass_tiles(prev)
+        out[setting] = (mass.cpu(), score.cpu())
+    mass, score = out[cap]
+    for bi in range(B):
+        L = int(lens[bi])
+        mp, lp = st[0][bi:bi + 1].cpu(), st[1][bi:bi + 1].cpu()
+        want_mass = oracle.prefix_mass(q[bi:bi + 1], k[bi:bi + 1, :, :L], mp, lp, rows)
+        np.testing.assert_allclose(mass[bi:bi + 1, :, :L].numpy(), want_mass.numpy(), rtol=2e-5, atol=1e-9,
+                                   err_msg=f"sequence {bi} (length {L})")
+        want_score = oracle.value_score(want_mass, v[bi:bi + 1, :, :L])
+        np.testing.assert_allclose(score[bi:bi + 1, :, :L].numpy(), want_score.numpy(), rtol=5e-5, atol=1e-9,
+                                   err_msg=f"sequence {bi} (length {L})")
+        assert not mass[bi, :, L:].any() and not score[bi, :, L:].any(), "slots past the length must be 0"
+    np.testing.assert_allclose(mass.numpy(), out[-1][0].numpy(), rtol=2e-5, atol=1e-9)
+    np.testing.assert_allclose(score.numpy(), out[-1][1].numpy(), rtol=5e-5, atol=1e-9)
