@@ -333,6 +333,18 @@ class Workload:
             return out
         return self.head_gather(out)
 
+    def head_gather_arg(self, rows: int):
+        """KV-head sharding: the attention call's head_gather argument -- the exchange of
+        its output rows t < rows inside the attention launch, into a new [B, Hq, rows, D]
+        tensor -- or None (one rank, or sequences sharded)."""
+        import torch
+
+        if self.world == 1 or self.cfg["shard"] != "heads":
+            return None
+        c = self.cfg
+        gout = torch.empty(len(self.lens), c["Hq"], rows, c["D"], device=self.device, dtype=torch.bfloat16)
+        return (self.head_gather, gout)
+
     def block_step(self, retain: bool):
         """One block-step over every layer through the public hot-path API."""
         import torch
@@ -397,17 +409,18 @@ class Workload:
         merge = retain and c["retention"]
         outs = []
         for layer in range(L):
+            hg = self.head_gather_arg(T)   # KV-head sharding: the exchange inside the launch
             if merge:
                 out, _ = step0_attention(self.QP[layer], self.prefix(layer), self.KCP[layer], self.VCP[layer],
                                          scaling=self.scale, stats_out=(self.MPR[layer], self.LPR[layer]),
                                          unpack_out=self.unpack_out(layer), probe_blocks=c["probe_blocks"],
-                                         block_size=T)
-                outs.append(self.gather_heads(out[:, :, :T]))
+                                         block_size=T, head_gather=hg)
+                outs.append(out[:, :, :T] if hg is None else hg[1])
             else:
                 out, _ = step0_attention(self.Q[layer, 0], self.prefix(layer), self.KC[layer, 0], self.VC[layer, 0],
                                          scaling=self.scale, stats_out=(self.MP[layer], self.LP[layer]),
-                                         unpack_out=self.unpack_out(layer))
-                outs.append(self.gather_heads(out))
+                                         unpack_out=self.unpack_out(layer), head_gather=hg)
+                outs.append(out if hg is None else hg[1])
         # B == 1: merging the layer and batch axes of the queries is a view
         if merge:
             q0, st = self.QP.flatten(0, 1), (self.MPR.flatten(0, 1), self.LPR.flatten(0, 1))
@@ -419,8 +432,10 @@ class Workload:
         for layer in range(L):
             compact = Prefix.dense(self.CK[layer], self.CV[layer])
             for s in range(1, c["substeps"]):
-                outs[layer] = self.gather_heads(compact_attention(self.Q[layer, s], compact, None, self.KC[layer, s],
-                                                                  self.VC[layer, s], scaling=self.scale))
+                hg = self.head_gather_arg(T)
+                out = compact_attention(self.Q[layer, s], compact, None, self.KC[layer, s], self.VC[layer, s],
+                                        scaling=self.scale, head_gather=hg)
+                outs[layer] = out if hg is None else hg[1]
         n = self.prefix_all.n
         idx = res.indices.view(L, self.B, self.H, -1)
         keep = None

@@ -407,6 +407,22 @@ MA_API int ma_ipc_close_handle(void* ptr);
 MA_API int ma_head_gather(const void* part, const int64_t sp[3], int B, int Hl, int T, int D, int world, int rank,
                           void* const* regions, void* out, const int64_t so[3], void* workspace,
                           size_t workspace_bytes, void* stream);
+/* ma_prefix_attention_gather: ma_prefix_attention of this rank's query heads (out [B, Hl, T,
+ *   D], q->Hq = Hl) and the head gather of its rows t < Tg in the same launch: the split
+ *   merge stores every finished row into every rank's region (regions and gather_ws as for
+ *   ma_head_gather; the region sized ma_head_gather_region_bytes(B, Hq, Tg)), the launch's
+ *   CTAs wait -- bounded -- for every rank's rows and copy them to gout [B, Hq, Tg, D]
+ *   (strides sgo), Hq = world * Hl. When the attention cannot merge in one resident wave
+ *   (its plan needs more CTAs than the GPU holds at once, or the prefix is not read by
+ *   TMA) the gather runs as ma_head_gather's kernels after it, with the same result. Calls
+ *   share gather_ws's counters with ma_head_gather, so the two may alternate. No reference
+ *   counterpart (the reference does not shard heads): it fuses the per-layer attention
+ *   with the all-gather of head outputs that KV-head sharding adds after it.           */
+MA_API int ma_prefix_attention_gather(const ma_rows* q, const ma_kv* kv, int H, const ma_block* cur, float scale,
+                                      int causal_block, int q_pos0, int c_pos0, void* out, const int64_t so[3],
+                                      float* m_p, float* l_p, float* o_p, void* workspace, size_t workspace_bytes,
+                                      int world, int rank, void* const* regions, int Tg, void* gout,
+                                      const int64_t sgo[3], void* gather_ws, size_t gather_ws_bytes, void* stream);
 
 #ifdef __cplusplus
 }

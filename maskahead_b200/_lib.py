@@ -121,6 +121,9 @@ _SIGNATURES = {
     "ma_ipc_close_handle": (_i32, [_vp]),
     "ma_head_gather": (_i32, [_vp, _P(ctypes.c_int64), _i32, _i32, _i32, _i32, _i32, _i32, _P(_vp), _vp,
                               _P(ctypes.c_int64), _vp, _sz, _vp]),
+    "ma_prefix_attention_gather": (_i32, [_P(MaRows), _P(MaKV), _i32, _P(MaBlock), _f32, _i32, _i32, _i32,
+                                          _vp, _P(ctypes.c_int64), _vp, _vp, _vp, _vp, _sz, _i32, _i32, _P(_vp),
+                                          _i32, _vp, _P(ctypes.c_int64), _vp, _sz, _vp]),
 }
 
 EXPORTED = tuple(_SIGNATURES)

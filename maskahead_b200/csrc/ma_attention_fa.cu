@@ -247,7 +247,8 @@ __device__ __forceinline__ void attn_fa_body(const Args& A) {
   __shared__ __align__(8) uint64_t rfull[PACKED ? NST : 1], rfree[PACKED ? NST : 1];
   __shared__ __align__(16) float sKch[PACKED ? kD : 1];   // the packed keys' divisor of this (b, h)
   __shared__ int sPg[PACKED ? kPgCache : 1];              // the page-table entries of [begin, end)
-  __shared__ int s_abort, s_merge_ok;
+  __shared__ int s_abort, s_merge_ok, s_gather_ok;
+  __shared__ uint32_t s_epoch, s_cum;   // the fused head gather: call number, CTAs of the calls before
 
   // grid (row tiles, splits, heads): the row tiles of one split run side by side, so the
   // second and later ones read that split's K/V from L2
@@ -1041,8 +1042,17 @@ __device__ __forceinline__ void attn_fa_body(const Args& A) {
       }
     }
     s_merge_ok = ok ? 1 : 0;
+    // the fused head gather: this call's number and the CTAs of the calls before it (the
+    // last CTA of the previous call wrote them; this launch reads them only after that
+    // launch completed: pdl_wait above)
+    if (A.fm.gather) {
+      s_epoch = *reinterpret_cast<volatile const uint32_t*>(A.fm.po.ws + 2) + 1u;
+      s_cum = *reinterpret_cast<volatile const uint32_t*>(A.fm.po.ws + 4);
+    }
   }
   __syncthreads();
+  const PeerOut* po = A.fm.gather ? &A.fm.po : nullptr;
+  const uint32_t pslot = s_epoch & 1u;
   // this split's share of the group's rows: a half warp per row with at most 16 prefix
   // splits, else a warp per row (weights scratch in the slots)
   const int per = (R_blk + (int)gridDim.y - 1) / (int)gridDim.y;
@@ -1052,20 +1062,86 @@ __device__ __forceinline__ void attn_fa_body(const Args& A) {
     for (int rr0 = lo + 2 * warp; merge_warp && rr0 < hi; rr0 += 2 * kWarps) {   // uniform per warp
       const int rr = rr0 + (lane >> 4);
       combine_row16<__nv_bfloat16>(A.q, H, A.P, A.nsplit, has_cur, out, A.fm.so[0], A.fm.so[1], A.fm.so[2],
-                                   A.fm.m_p, A.fm.l_p, A.fm.o_p, bh, r0 + rr, rr < hi);
+                                   A.fm.m_p, A.fm.l_p, A.fm.o_p, bh, r0 + rr, rr < hi, po, pslot);
     }
-    return;
+  } else {
+    float* sW = reinterpret_cast<float*>(sKs) + warp * kCombineMaxSplits;
+    for (int rr = lo + warp; merge_warp && rr < hi; rr += kWarps) {
+      if (s_merge_ok) {
+        combine_row<__nv_bfloat16, __nv_bfloat16>(A.q, H, A.P, A.nsplit, has_cur, out, A.fm.so[0], A.fm.so[1],
+                                                  A.fm.so[2], A.fm.m_p, A.fm.l_p, A.fm.o_p, bh, r0 + rr, sW, po,
+                                                  pslot);
+      } else if (lane == 0) {   // a split never arrived: the row is reported as NaN
+        const int rw = r0 + rr;
+        const int g = rw / T, tt = rw - (rw / T) * T;
+        __nv_bfloat16* dst = out + (int64_t)b * A.fm.so[0] + (int64_t)(h * G + g) * A.fm.so[1] + (int64_t)tt * A.fm.so[2];
+        for (int d = 0; d < kD; ++d) dst[d] = __float2bfloat16_rn(NAN);
+      }
+    }
   }
-  float* sW = reinterpret_cast<float*>(sKs) + warp * kCombineMaxSplits;
-  for (int rr = lo + warp; merge_warp && rr < hi; rr += kWarps) {
-    if (s_merge_ok) {
-      combine_row<__nv_bfloat16, __nv_bfloat16>(A.q, H, A.P, A.nsplit, has_cur, out, A.fm.so[0], A.fm.so[1],
-                                                A.fm.so[2], A.fm.m_p, A.fm.l_p, A.fm.o_p, bh, r0 + rr, sW);
-    } else if (lane == 0) {   // a split never arrived: the row is reported as NaN
-      const int rw = r0 + rr;
-      const int g = rw / T, tt = rw - (rw / T) * T;
-      __nv_bfloat16* dst = out + (int64_t)b * A.fm.so[0] + (int64_t)(h * G + g) * A.fm.so[1] + (int64_t)tt * A.fm.so[2];
-      for (int d = 0; d < kD; ++d) dst[d] = __float2bfloat16_rn(NAN);
+  if (po == nullptr) return;
+
+  // ---- fused head gather (every CTA of the launch is resident: cooperative launch). Each
+  // CTA, once its rows are stored, adds 1 to its rank's arrival counter in every rank's
+  // region -- a release reduction at system scope: the CTA barrier makes every thread's
+  // peer stores observed by thread 0 and the release is cumulative, so one per CTA orders
+  // them all (a fence in every thread measured ~1.5 us slower per call) -- then waits
+  // (bounded) until every rank's counter in this rank's region holds the CTAs of every
+  // call so far (every rank runs the same calls with the same grids, so the running
+  // totals agree), and copies its share of the slot -- every rank's rows -- into the
+  // gathered output; the last CTA to finish records the call. A rank is at most one call
+  // ahead of another (it cannot finish call e + 1 before every CTA of every rank arrived
+  // for e + 1), so the two slots never mix calls.
+  __syncthreads();
+  const uint32_t nctas = gridDim.x * gridDim.y * gridDim.z;
+  const uint32_t ep = s_epoch, want = s_cum + nctas;
+  if (threadIdx.x == 0) {
+    for (int p = 0; p < po->world; ++p) {
+      uint32_t* cnt = reinterpret_cast<uint32_t*>(po->base[p] + 2 * po->slot_bytes) + po->rank;
+      asm volatile("red.release.sys.global.add.u32 [%0], 1;\n" ::"l"(cnt) : "memory");
+    }
+    const uint32_t* mine = reinterpret_cast<const uint32_t*>(po->base[po->rank] + 2 * po->slot_bytes);
+    const uint64_t t0 = global_ns();
+    bool ok = true;
+    for (int p = 0; p < po->world && ok; ++p) {
+      for (;;) {
+        uint32_t f;
+        asm volatile("ld.acquire.sys.global.u32 %0, [%1];\n" : "=r"(f) : "l"(mine + p) : "memory");
+        if ((int32_t)(f - want) >= 0) break;
+        if (global_ns() - t0 > A.fm.wait_ns) {
+          ok = false;
+          break;
+        }
+      }
+    }
+    if (!ok) atomicExch(A.err, 1);
+    s_gather_ok = ok ? 1 : 0;
+  }
+  __syncthreads();
+  if (s_gather_ok) {
+    asm volatile("fence.acq_rel.sys;\n" ::: "memory");
+    const int Hq = po->Hl * po->world, Tg = po->Tg;
+    const char* src = po->base[po->rank] + (int64_t)pslot * po->slot_bytes;
+    __nv_bfloat16* gout = reinterpret_cast<__nv_bfloat16*>(po->out);
+    const int64_t chunks = (int64_t)A.q.B * Hq * Tg * (kD / 8);
+    const int64_t cta = ((int64_t)blockIdx.z * gridDim.y + blockIdx.y) * gridDim.x + blockIdx.x;
+    for (int64_t i = cta * blockDim.x + threadIdx.x; i < chunks; i += (int64_t)nctas * blockDim.x) {
+      const int c = (int)(i & 15);
+      const int64_t row = i >> 4;
+      const int t = (int)(row % Tg);
+      const int64_t bq = row / Tg;
+      const int hq = (int)(bq % Hq), bb = (int)(bq / Hq);
+      const uint4 v = __ldcg(reinterpret_cast<const uint4*>(src + row * (kD * 2)) + c);
+      reinterpret_cast<uint4*>(gout + (int64_t)bb * po->so[0] + (int64_t)hq * po->so[1] + (int64_t)t * po->so[2])[c] = v;
+    }
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    uint32_t* gw = po->ws;
+    if (atomicAdd(gw + 3, 1u) == nctas - 1) {
+      gw[3] = 0u;
+      gw[4] = want;
+      gw[2] = ep;
     }
   }
 }
@@ -1124,8 +1200,9 @@ bool fa_eligible(const ma_rows& q, const ma_kv& kv, const int64_t* idx, const ma
 int launch_attn_partial_fa(const ma_rows& q, const ma_kv& kv, int H, const ma_block& cur, float scale,
                            int causal_block, int q_pos0, int c_pos0, int n_keys, int split_len, int nsplit,
                            const Partials& P, int* err, const FusedMerge* fm, bool fold, bool* fused,
-                           cudaStream_t st) {
+                           bool* gathered, cudaStream_t st) {
   *fused = false;
+  if (gathered) *gathered = false;
   if (!fa_eligible(q, kv, nullptr, cur, n_keys) || !(scale > 0.f) || !P.o_bf16 || split_len % kBN != 0)
     return MA_ERR_UNSUPPORTED;
   const bool packed = n_keys > 0 && kv.layout == MA_KV_PACKED_TOKEN;
@@ -1180,7 +1257,10 @@ int launch_attn_partial_fa(const ma_rows& q, const ma_kv& kv, int H, const ma_bl
   if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
     return MA_ERR_CUDA;
   const int rows_per_split = (std::min(rows, R) + (int)grid.y - 1) / (int)grid.y;
-  if (fold && grid.y == 1) {
+  // a head gather runs only inside the cooperative merge (its CTAs wait for one another);
+  // without one the caller gathers in separate launches
+  const bool gather = fm != nullptr && fm->gather;
+  if (fold && grid.y == 1 && !gather) {
     // one split holds every key of its rows: they are final in the epilogue, no merge
     Args Ad = A;
     Ad.direct = 1;
@@ -1195,7 +1275,7 @@ int launch_attn_partial_fa(const ma_rows& q, const ma_kv& kv, int H, const ma_bl
   // Only when every cluster is resident at once: a cluster of one-CTA-per-SM blocks needs
   // that many free SMs in one GPC, so fewer clusters than SMs / size fit (a second wave
   // of clusters cost more than the merge saves)
-  if (fm != nullptr && nsplit <= 16 && (int)grid.y <= 16 && rows_per_split <= 2 * kWarps) {
+  if (fm != nullptr && !gather && nsplit <= 16 && (int)grid.y <= 16 && rows_per_split <= 2 * kWarps) {
     static int cluster_nc_of[4][17] = {{0}};   // per kernel and cluster size: resident clusters (-1: none)
     int* cluster_nc = cluster_nc_of[kid];
     const int cs = (int)grid.y;
@@ -1262,6 +1342,7 @@ int launch_attn_partial_fa(const ma_rows& q, const ma_kv& kv, int H, const ma_bl
         cfg.numAttrs = na;
         if (cudaLaunchKernelEx(&cfg, kernel, Af) == cudaSuccess) {
           *fused = true;
+          if (gathered) *gathered = gather;
           return MA_OK;
         }
         (void)cudaGetLastError();

@@ -194,11 +194,21 @@ Partials carve_partials(void* ws, int BH, const Plan& p, int D, int** err, uint2
   return P;
 }
 
+// The head gather in its own launches (ma_head_gather's kernels), when the attention's merge
+// could not run it: the call's rows t < Tg of `out` go to every rank, the gathered rows
+// into po->out.
+int separate_gather(const ma_rows& q, const PeerOut* po, void* const* regions, const void* out, const int64_t so[3],
+                    cudaStream_t st) {
+  return launch_head_gather(out, so, q.B, q.Hq, po->Tg, po->world, po->rank, regions, po->out, po->so, po->ws,
+                            peer_wait_ns(), st);
+}
+
 // shared by the prefix and the read-set attention: partial pass + combine
 int run_attention(const ma_rows& q, const ma_kv& kv, int H, const ma_block& cur, float scale,
                   int causal_block, int q_pos0, int c_pos0, const int64_t* idx, int64_t si0,
                   int64_t si1, int n_keys, void* out, const int64_t so[3], float* m_p, float* l_p,
-                  float* o_p, void* ws, size_t ws_bytes, cudaStream_t st) {
+                  float* o_p, void* ws, size_t ws_bytes, cudaStream_t st, const PeerOut* po = nullptr,
+                  void* const* regions = nullptr) {
   const int G = q.Hq / H;
   const int R = G * q.T;
   const bool mma = use_mma_attention(q, kv, scale);
@@ -215,6 +225,7 @@ int run_attention(const ma_rows& q, const ma_kv& kv, int H, const ma_block& cur,
                     (p.nsplit == 1 || p.split_len >= 4 * kt);
   if (fold) p.S = p.nsplit;
   bool folded = false;
+  bool gathered = false;   // the head gather ran inside the attention launch
   if (!ws || ws_bytes < partials_bytes(q.B * H, p.S, p.Rp, q.D, p.o_bf16) + 512 + kSyncBytes)
     return MA_ERR_WORKSPACE;
   int* err = nullptr;
@@ -234,11 +245,13 @@ int run_attention(const ma_rows& q, const ma_kv& kv, int H, const ma_block& cur,
       fm.sync = sync;
       fm.sync_slots = kSyncSlots;
       fm.wait_ns = peer_wait_ns();
+      fm.gather = po != nullptr ? 1 : 0;
+      if (po != nullptr) fm.po = *po;
       bool fused = false;
       rc = MA_ERR_UNSUPPORTED;
       if (fa) {
         rc = launch_attn_partial_fa(q, kv, H, cur, scale, causal_block, q_pos0, c_pos0, n_keys, p.split_len,
-                                    p.nsplit, P, err, &fm, fold, &fused, st);
+                                    p.nsplit, P, err, &fm, fold, &fused, &gathered, st);
         if (rc == MA_ERR_UNSUPPORTED) {   // a tensor map the TMA cannot describe: 64-key kernel
           p = plan_splits(q.B * H, R, n_keys, cur.Tc, mma);
           P = carve_partials(ws, q.B * H, p, q.D, &err, &sync);
@@ -246,17 +259,22 @@ int run_attention(const ma_rows& q, const ma_kv& kv, int H, const ma_block& cur,
           folded = fold;
         }
       }
-      if (rc == MA_ERR_UNSUPPORTED)
+      if (rc == MA_ERR_UNSUPPORTED) {
+        fm.gather = 0;   // only the pipelined kernel's cooperative merge gathers
         rc = launch_attn_partial_tc(q, kv, H, cur, scale, causal_block, q_pos0, c_pos0, idx, si0, si1, n_keys,
                                     p.split_len, p.nsplit, P, err, &fm, &fused, st);
-      if (rc != MA_OK || fused) return rc;
+      }
+      if (rc != MA_OK) return rc;
+      if (fused) return (po != nullptr && !gathered) ? separate_gather(q, po, regions, out, so, st) : MA_OK;
     } else {
       rc = launch_attn_partial_simt(q, kv, H, cur, scale, causal_block, q_pos0, c_pos0, idx, si0, si1, n_keys,
                                     p.split_len, p.nsplit, P, st);
       if (rc != MA_OK) return rc;
     }
   }
-  return launch_attn_combine(q, H, P, p.nsplit, cur.Tc > 0 && !folded, out, so, m_p, l_p, o_p, st);
+  rc = launch_attn_combine(q, H, P, p.nsplit, cur.Tc > 0 && !folded, out, so, m_p, l_p, o_p, st);
+  if (rc != MA_OK || po == nullptr) return rc;
+  return separate_gather(q, po, regions, out, so, st);
 }
 
 }  // namespace
@@ -344,6 +362,43 @@ int ma_prefix_attention(const ma_rows* q, const ma_kv* kv, int H, const ma_block
   return run_attention(*q, *kv, H, *cur, scale, causal_block, q_pos0, c_pos0, nullptr, 0, 0,
                        kv->nq + kv->nf, out, so, m_p, l_p, o_p, workspace, workspace_bytes,
                        (cudaStream_t)stream);
+}
+
+int ma_prefix_attention_gather(const ma_rows* q, const ma_kv* kv, int H, const ma_block* cur, float scale,
+                               int causal_block, int q_pos0, int c_pos0, void* out, const int64_t so[3],
+                               float* m_p, float* l_p, float* o_p, void* workspace, size_t workspace_bytes,
+                               int world, int rank, void* const* regions, int Tg, void* gout,
+                               const int64_t sgo[3], void* gather_ws, size_t gather_ws_bytes, void* stream) {
+  int rc = check_rows(q);
+  if (rc) return rc;
+  if (H <= 0 || q->Hq % H) return MA_ERR_ARG;
+  if ((rc = check_kv(kv, q->D))) return rc;
+  if ((rc = check_block(cur, q, H))) return rc;
+  if (!out || !so || !aligned16(out) || !strides16(so, 3, esize(q->dtype))) return MA_ERR_ARG;
+  if ((m_p == nullptr) != (l_p == nullptr)) return MA_ERR_ARG;
+  if (o_p && !aligned16(o_p)) return MA_ERR_ARG;
+  if (causal_block < 0) return MA_ERR_ARG;
+  if (kv->nq + kv->nf == 0 && cur->Tc == 0) return MA_ERR_ARG;
+  if (q->dtype != MA_BF16 || q->D != 128) return MA_ERR_UNSUPPORTED;
+  if (world < 1 || world > kPeerMaxWorld || rank < 0 || rank >= world || !regions) return MA_ERR_ARG;
+  if (Tg < 1 || Tg > q->T || !gout || !sgo || !aligned16(gout) || !strides16(sgo, 3, 2)) return MA_ERR_ARG;
+  if (!gather_ws || gather_ws_bytes < ma_head_gather_workspace()) return MA_ERR_WORKSPACE;
+  PeerOut po;
+  memset(&po, 0, sizeof(po));
+  for (int p = 0; p < world; ++p) {
+    if (!regions[p] || (reinterpret_cast<uintptr_t>(regions[p]) & 255)) return MA_ERR_ARG;
+    po.base[p] = reinterpret_cast<char*>(regions[p]);
+  }
+  po.ws = reinterpret_cast<uint32_t*>((reinterpret_cast<uintptr_t>(gather_ws) + 255) & ~uintptr_t(255));
+  po.slot_bytes = (int64_t)((head_gather_region_bytes(q->B, q->Hq * world, Tg) - 256) / 2);
+  po.out = gout;
+  for (int i = 0; i < 3; ++i) po.so[i] = sgo[i];
+  po.world = world;
+  po.rank = rank;
+  po.Hl = q->Hq;
+  po.Tg = Tg;
+  return run_attention(*q, *kv, H, *cur, scale, causal_block, q_pos0, c_pos0, nullptr, 0, 0, kv->nq + kv->nf, out,
+                       so, m_p, l_p, o_p, workspace, workspace_bytes, (cudaStream_t)stream, &po, regions);
 }
 
 int ma_prefix_scores(const ma_rows* q, const ma_kv* kv, int H, const int32_t* q_rows, int T2,

@@ -12,6 +12,28 @@ namespace ma {
 constexpr int kCombineMaxSplits = 256;   // partial slots per row (the planner never exceeds this)
 constexpr int kCombineChunk = 16;
 
+// The fused head gather's peer stores of one finished row's channels [d0, d0 + N) (bf16):
+// row (b, query head hq of this rank, t) goes to slot `slot` of every rank's region, as
+// global query head rank * Hl + hq (plain 8- or 16-byte stores over NVLink).
+template <int N>
+__device__ __forceinline__ void peer_store_row(const PeerOut* po, uint32_t slot, int b, int hq, int t, int d0,
+                                               const float* v) {
+  if (po == nullptr || t >= po->Tg) return;
+  const int Hq = po->Hl * po->world;
+  const int64_t off = (int64_t)slot * po->slot_bytes +
+                      ((((int64_t)b * Hq + (int64_t)po->rank * po->Hl + hq) * po->Tg + t) * 128 + d0) * 2;
+  uint32_t w[N / 2];
+#pragma unroll
+  for (int i = 0; i < N / 2; ++i) {
+    __nv_bfloat162 x = __floats2bfloat162_rn(v[2 * i], v[2 * i + 1]);
+    w[i] = *reinterpret_cast<uint32_t*>(&x);
+  }
+  for (int p = 0; p < po->world; ++p) {
+    if constexpr (N == 8) *reinterpret_cast<uint4*>(po->base[p] + off) = make_uint4(w[0], w[1], w[2], w[3]);
+    else *reinterpret_cast<uint2*>(po->base[p] + off) = make_uint2(w[0], w[1]);
+  }
+}
+
 // Four channels of a partial row, fp32 or bf16.
 __device__ __forceinline__ float4 load_o4(const float* p) { return __ldcg(reinterpret_cast<const float4*>(p)); }
 __device__ __forceinline__ float4 load_o4(const __nv_bfloat16* p) {
@@ -30,7 +52,8 @@ template <typename QT, typename OT>
 __device__ __forceinline__ void combine_row(const ma_rows& q, int H, const Partials& P, int nsplit, bool has_cur,
                                             QT* __restrict__ out, int64_t so0, int64_t so1, int64_t so2,
                                             float* __restrict__ m_p, float* __restrict__ l_p, float* __restrict__ o_p,
-                                            int bh, int r, float* __restrict__ sWw) {
+                                            int bh, int r, float* __restrict__ sWw, const PeerOut* po = nullptr,
+                                            uint32_t slot = 0) {
   const int D = q.D;
   const int G = q.Hq / H;
   const int R = G * q.T;
@@ -129,6 +152,8 @@ __device__ __forceinline__ void combine_row(const ma_rows& q, int H, const Parti
     const int g = r / q.T, t = r - (r / q.T) * q.T;
     QT* dst = out + (int64_t)b * so0 + (int64_t)(h * G + g) * so1 + (int64_t)t * so2 + d0;
     store4(dst, A.x * inv, A.y * inv, A.z * inv, A.w * inv);
+    const float v[4] = {A.x * inv, A.y * inv, A.z * inv, A.w * inv};
+    peer_store_row<4>(po, slot, b, h * G + g, t, d0, v);
   }
 }
 
@@ -146,7 +171,8 @@ template <typename QT, typename Src, int NS = 16>
 __device__ __forceinline__ void combine_row16_from(const ma_rows& q, int H, int nsplit, bool has_cur,
                                                    QT* __restrict__ out, int64_t so0, int64_t so1, int64_t so2,
                                                    float* __restrict__ m_p, float* __restrict__ l_p,
-                                                   float* __restrict__ o_p, int bh, int r, bool valid, const Src& src) {
+                                                   float* __restrict__ o_p, int bh, int r, bool valid, const Src& src,
+                                                   const PeerOut* po = nullptr, uint32_t slot = 0) {
   constexpr int D = 128;
   const int G = q.Hq / H;
   const int R = G * q.T;
@@ -218,6 +244,8 @@ __device__ __forceinline__ void combine_row16_from(const ma_rows& q, int H, int 
   QT* dst = out + (int64_t)b * so0 + (int64_t)(h * G + g) * so1 + (int64_t)t * so2 + d0;
   store4(dst, A[0] * inv, A[1] * inv, A[2] * inv, A[3] * inv);
   store4(dst + 4, A[4] * inv, A[5] * inv, A[6] * inv, A[7] * inv);
+  const float v[8] = {A[0] * inv, A[1] * inv, A[2] * inv, A[3] * inv, A[4] * inv, A[5] * inv, A[6] * inv, A[7] * inv};
+  peer_store_row<8>(po, slot, b, h * G + g, t, d0, v);
 }
 
 // The partial rows of the global split buffers (bf16, split s of row r at row0 + s*Rp).
@@ -237,7 +265,8 @@ template <typename QT, int NS = 16>
 __device__ __forceinline__ void combine_row16(const ma_rows& q, int H, const Partials& P, int nsplit, bool has_cur,
                                               QT* __restrict__ out, int64_t so0, int64_t so1, int64_t so2,
                                               float* __restrict__ m_p, float* __restrict__ l_p,
-                                              float* __restrict__ o_p, int bh, int r, bool valid) {
+                                              float* __restrict__ o_p, int bh, int r, bool valid,
+                                              const PeerOut* po = nullptr, uint32_t slot = 0) {
   GlobalPartials src;
   src.po = reinterpret_cast<const __nv_bfloat16*>(P.o);
   src.pml = P.ml;
@@ -245,7 +274,7 @@ __device__ __forceinline__ void combine_row16(const ma_rows& q, int H, const Par
   src.step = P.Rp;
   src.d0 = 8 * (threadIdx.x & 15);
   combine_row16_from<QT, GlobalPartials, NS>(q, H, nsplit, has_cur, out, so0, so1, so2, m_p, l_p, o_p, bh, r, valid,
-                                              src);
+                                              src, po, slot);
 }
 
 }  // namespace ma

@@ -198,6 +198,22 @@ __device__ __forceinline__ void kv_read8(const ma_kv& kv, int b, int h, int j, i
 // writes o in fp32, the tensor-core kernel in bf16 (the combine weights each split by
 // l * exp(m - M), so normalized outputs lose nothing to the split's scale).
 // ----------------------------------------------------------------------------------
+// The fused head gather of a KV-head-sharded attention call: the merge stores every final
+// row (t < Tg) of this rank's query heads into slot `calls & 1` of every rank's receive
+// region ([slot 0: B Hq Tg D bf16][slot 1][counters: world u32], Hq = world * Hl; mapped
+// here through CUDA IPC), then the launch's CTAs arrive on every rank's counter of this
+// rank and wait for every rank's CTAs before copying the slot into `out` [B, Hq, Tg, D].
+struct PeerOut {
+  char* base[8];        // every rank's region as mapped here (this rank's own is local)
+  uint32_t* ws;         // [0] error, [1] CTA arrivals, [2] calls done, [3] copy arrivals,
+                        // [4] CTAs of every rank's calls so far (per rank)
+  int64_t slot_bytes;
+  void* out;            // the gathered rows [B, Hq, Tg, D] bf16, strides so
+  int64_t so[3];
+  int world, rank, Hl, Tg;
+};
+constexpr int kPeerMaxWorld = 8;
+
 struct Partials {
   float2* ml;   // [BH][S][Rp]
   void* o;      // [BH][S][Rp][D], fp32 or bf16 (o_bf16)

@@ -26,6 +26,8 @@ struct FusedMerge {
   uint2* sync;      // [B*H*row blocks], zero counters between calls
   int sync_slots;   // capacity of sync
   uint64_t wait_ns; // bound on a CTA's wait for the other splits of its group
+  int gather;       // the merge also runs the head gather `po` (cooperative launch only)
+  PeerOut po;
 };
 // The bound on every wait of one CTA for other CTAs of the same launch (the split merge's
 // and the value-score centre's generation words); ma_set_peer_wait_ns. The waits on a
@@ -58,7 +60,7 @@ int fa_mass_tiles();
 int launch_attn_partial_fa(const ma_rows& q, const ma_kv& kv, int H, const ma_block& cur, float scale,
                            int causal_block, int q_pos0, int c_pos0, int n_keys, int split_len, int nsplit,
                            const Partials& P, int* err, const FusedMerge* fm, bool fold, bool* fused,
-                           cudaStream_t st);
+                           bool* gathered, cudaStream_t st);
 
 // ma_combine.cu
 int launch_attn_combine(const ma_rows& q, int H, const Partials& P, int nsplit, bool has_cur,

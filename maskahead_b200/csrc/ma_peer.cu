@@ -6,18 +6,22 @@
 // owns a receive region in its own HBM, mapped into every peer's address space through a
 // CUDA IPC handle:
 //
-//   [slot 0: B Hq T D bf16][slot 1: same][flags: world u32]
+//   [slot 0: B Hq T D bf16][slot 1: same][counters: world u32]
 //
 // and call e (e = 1, 2, ...; kept in the caller's workspace, so a CUDA graph replays it)
 // runs head_gather_kernel: its CTAs store the rank's rows straight into slot e & 1 of every
 // rank's region (plain peer stores over NVLink, 16 bytes a thread; no TMA and no multicast
-// on peer memory), fence at system scope and count themselves; the last CTA writes flag
-// e into slot `rank` of every region (release, system scope) and waits -- bounded -- until
-// its own region's flags from all ranks reach e. head_gather_copy_kernel then copies the
-// slot to the caller's [B, Hq, T, D] output. Two slots suffice: a rank writes slot s of
-// call e + 2 only after it saw every rank's flag of call e + 1, which a rank sets only
-// after its copy of call e (stream order). A wait that gives up sets the workspace's error
-// word (ma_workspace_status reads it) and the call returns without the peers' rows.
+// on peer memory), and each CTA then adds 1 to counter `rank` of every region (a release
+// reduction at system scope); the last CTA of the rank waits -- bounded -- until every
+// rank's counter in its own region holds the CTAs of every call so far (all ranks run the
+// same calls with the same grids, so the running totals agree). head_gather_copy_kernel
+// then copies the slot to the caller's [B, Hq, T, D] output. The attention launch can run
+// the same exchange itself (ma_prefix_attention_gather: its merge stores the rows, its CTAs
+// arrive on the same counters); the two forms share the counters and may alternate. Two
+// slots suffice: a rank writes slot s of call e + 2 only after every CTA of every rank
+// arrived for call e + 1, which a rank's CTAs do only after its copy of call e (stream
+// order). A wait that gives up sets the workspace's error word (ma_workspace_status reads
+// it) and the call returns without the peers' rows.
 #include <string.h>
 
 #include <algorithm>
@@ -39,8 +43,8 @@ struct PeerBases {
   char* base[kMaxWorld];   // every rank's region as mapped here (this rank's own is local)
 };
 
-__device__ __forceinline__ void st_release_sys_u32(uint32_t* p, uint32_t v) {
-  asm volatile("st.release.sys.global.u32 [%0], %1;\n" ::"l"(p), "r"(v) : "memory");
+__device__ __forceinline__ void red_release_sys_add(uint32_t* p) {
+  asm volatile("red.release.sys.global.add.u32 [%0], 1;\n" ::"l"(p) : "memory");
 }
 __device__ __forceinline__ uint32_t ld_acquire_sys_u32(const uint32_t* p) {
   uint32_t v;
@@ -48,7 +52,8 @@ __device__ __forceinline__ uint32_t ld_acquire_sys_u32(const uint32_t* p) {
   return v;
 }
 
-// ws (this rank's, 256-byte aligned): [0] error word, [1] CTA arrival counter, [2] calls done
+// ws (this rank's, 256-byte aligned): [0] error word, [1] CTA arrival counter, [2] calls done,
+// [3] (the fused form's copy arrivals), [4] every rank's CTAs of the calls so far, per rank
 __global__ void __launch_bounds__(kGatherThreads) head_gather_kernel(
     const __nv_bfloat16* __restrict__ part, int64_t sp0, int64_t sp1, int64_t sp2, int B, int Hl, int T, int world,
     int rank, int64_t slot_bytes, PeerBases peers, uint32_t* ws, uint64_t wait_ns) {
@@ -70,29 +75,29 @@ __global__ void __launch_bounds__(kGatherThreads) head_gather_kernel(
   }
   __syncthreads();
   if (threadIdx.x != 0) return;
-  __threadfence_system();   // this CTA's peer stores before its arrival
-  if (atomicAdd(ws + 1, 1u) != gridDim.x - 1) return;
-  // the last CTA: every CTA's rows are out; publish this rank's flag in every region
-  ws[1] = 0u;
-  __threadfence_system();
+  // this CTA arrives on its rank's counter in every rank's region: a release reduction at
+  // system scope (the CTA barrier makes every thread's peer stores observed by thread 0,
+  // the release is cumulative)
   const int64_t flags_off = 2 * slot_bytes;
-  for (int p = 0; p < world; ++p)
-    st_release_sys_u32(reinterpret_cast<uint32_t*>(peers.base[p] + flags_off) + rank, epoch);
-  // every rank's rows in this rank's region: its flag here has reached this call (a rank
-  // can be one call ahead, never two)
+  for (int p = 0; p < world; ++p) red_release_sys_add(reinterpret_cast<uint32_t*>(peers.base[p] + flags_off) + rank);
+  if (atomicAdd(ws + 1, 1u) != gridDim.x - 1) return;
+  // the last CTA of this rank: every rank's rows in this rank's region once every rank's
+  // counter here holds the CTAs of every call so far (the same grids on every rank)
+  ws[1] = 0u;
+  const uint32_t want = *reinterpret_cast<volatile uint32_t*>(ws + 4) + gridDim.x;
   const uint32_t* mine = reinterpret_cast<const uint32_t*>(peers.base[rank] + flags_off);
   const uint64_t t0 = global_ns();
   bool ok = true;
   for (int q = 0; q < world && ok; ++q) {
-    while ((int32_t)(ld_acquire_sys_u32(mine + q) - epoch) < 0) {
+    while ((int32_t)(ld_acquire_sys_u32(mine + q) - want) < 0) {
       if (global_ns() - t0 > wait_ns) {
         ok = false;
         break;
       }
-      __nanosleep(128);
     }
   }
   if (!ok) atomicExch(reinterpret_cast<int*>(ws), 1);
+  ws[4] = want;
   ws[2] = epoch;   // the copy kernel reads the slot from it
 }
 

@@ -151,7 +151,7 @@ def step0_attention(query: torch.Tensor, prefix, current_key: torch.Tensor, curr
                     scaling: float | None = None, want_stats: bool = True,
                     stats_out: tuple[torch.Tensor, torch.Tensor] | None = None, unpack: bool | None = None,
                     unpack_out: tuple[torch.Tensor, torch.Tensor] | None = None,
-                    probe_blocks: int = 0, block_size: int = 32):
+                    probe_blocks: int = 0, block_size: int = 32, head_gather=None):
     """fast_step0's attention half: the output over [live prefix | block] (block-causal by
     block_size when probe_blocks > 0 merges the probe) and, with want_stats, the prefix
     statistics stats = (M_p, L_p, O_p, prefix read) that select_step0 takes (None for an
@@ -163,7 +163,9 @@ def step0_attention(query: torch.Tensor, prefix, current_key: torch.Tensor, curr
     the session's step-0 forward, whose selection select_step0 runs for every layer at once
     over the stacked statistics and the layer-stacked cache. unpack_out = (key, value): the
     buffers a packed prefix is unpacked into (unpacked_prefix's out), so that the
-    selection can read every layer's unpacked copy.
+    selection can read every layer's unpacked copy. head_gather = (gather, gathered): the
+    KV-head-sharded exchange of the output rows t < gathered.shape[2] in the same launch
+    (splitk_attention).
     """
     prefix = as_prefix(prefix)
     if query.dtype == torch.bfloat16 and _needs_unpack(prefix, query.shape[0], current_key.shape[1], query.shape[3],
@@ -171,10 +173,11 @@ def step0_attention(query: torch.Tensor, prefix, current_key: torch.Tensor, curr
         prefix = unpacked_prefix(prefix, query.shape[0], current_key.shape[1], query.shape[3], out=unpack_out)
     causal = block_size if probe_blocks > 0 else 0
     if prefix.n == 0:
-        out, _ = splitk_attention(query, prefix, current_key, current_value, scaling=scaling, causal_block=causal)
+        out, _ = splitk_attention(query, prefix, current_key, current_value, scaling=scaling, causal_block=causal,
+                                  head_gather=head_gather)
         return out, None
     out, stats = splitk_attention(query, prefix, current_key, current_value, scaling=scaling, causal_block=causal,
-                                  want_prefix=want_stats, stats_out=stats_out)
+                                  want_prefix=want_stats, stats_out=stats_out, head_gather=head_gather)
     return out, stats
 
 
@@ -272,15 +275,18 @@ def gather_read_set(prefix, indices: torch.Tensor, *, dtype: torch.dtype = torch
 
 
 def compact_attention(query: torch.Tensor, prefix, indices: torch.Tensor | None, current_key: torch.Tensor,
-                      current_value: torch.Tensor, *, scaling: float | None = None) -> torch.Tensor:
+                      current_value: torch.Tensor, *, scaling: float | None = None, head_gather=None) -> torch.Tensor:
     """Attention of every query row over [prefix[indices] | current block] (sdpa_compact
     over the gathered read set, session.py:1286-1336). indices=None: prefix is the
     compact cache itself (gather_read_set / fast_step0(gather=True)), attended as a
     contiguous dense cache; else the selected slots are read straight from the (packed or
-    dense) cache by index."""
+    dense) cache by index. head_gather = (gather, gathered): with indices=None, the
+    KV-head-sharded exchange of the output in the same launch (splitk_attention)."""
     if indices is None:
-        out, _ = splitk_attention(query, prefix, current_key, current_value, scaling=scaling)
+        out, _ = splitk_attention(query, prefix, current_key, current_value, scaling=scaling, head_gather=head_gather)
         return out
+    if head_gather is not None:
+        raise ValueError("head_gather: only for the compact cache (indices=None)")
     lib = _lib.lib()
     prefix = as_prefix(prefix)
     b, hq, t, d = query.shape

@@ -25,7 +25,7 @@ __all__ = ["Prefix", "splitk_attention", "prefix_scores", "dequantize_prefix"]
 
 def splitk_attention(query, prefix, current_key, current_value, *, scaling=None,
                      causal_block: int = 0, q_pos0: int = 0, c_pos0: int = 0, want_prefix: bool = False,
-                     stats_out=None, **_tuning):
+                     stats_out=None, head_gather=None, **_tuning):
     """softmax over [prefix | current] for every query row (splitk.py:493-579).
 
     Returns (out [B,Hq,T,D] in the query dtype, stats) with stats = (M_p, L_p, O_p,
@@ -35,6 +35,11 @@ def splitk_attention(query, prefix, current_key, current_value, *, scaling=None,
     stats_out = (M_p, L_p) or (M_p, L_p, O_p): contiguous fp32 buffers of those shapes to
     write the statistics into (e.g. one layer's slice of layer-stacked buffers); O_p is
     then computed only if given. Implies want_prefix.
+    head_gather = (gather, gathered): KV-head sharding (maskahead_b200.shard.PeerHeadGather
+    of the process group, every rank making the same calls): this rank's output rows
+    t < gathered.shape[2] are exchanged with every rank's in the same launch (the split
+    merge stores them into every rank's receive region) and gathered holds all of them,
+    [B, world * Hq, Tg, D] bf16, when the call returns on the stream.
     """
     lib = _lib.lib()
     prefix = as_prefix(prefix)
@@ -72,10 +77,23 @@ def splitk_attention(query, prefix, current_key, current_value, *, scaling=None,
     nbytes = lib.ma_prefix_attention_workspace(b, hkv, r, prefix.n, d, cur.Tc)
     ws = _lib.workspace(dev, "attention", nbytes)
     scale = float(scaling if scaling is not None else d ** -0.5)
-    _lib.check("ma_prefix_attention", lib.ma_prefix_attention(
-        rows, kv, hkv, cur, scale, int(causal_block), int(q_pos0), int(c_pos0),
-        out.data_ptr(), _lib.i64(*out.stride()[:3]), _lib.ptr(mp), _lib.ptr(lp), _lib.ptr(op),
-        ws.data_ptr(), ws.numel(), _lib.stream_handle(dev)))
+    if head_gather is not None:
+        gather, gout = head_gather
+        tg = gout.shape[2]
+        if (gout.dtype != torch.bfloat16 or gout.device != dev or tuple(gout.shape) != (b, hq * gather.world, tg, d)
+                or gout.stride(-1) != 1 or not 0 < tg <= t):
+            raise ValueError(f"head_gather: need a bfloat16 [{b}, {hq * gather.world}, Tg <= {t}, {d}] tensor on {dev}")
+        bases, gws = gather.region(dev, b, hq * gather.world, tg)
+        _lib.check("ma_prefix_attention_gather", lib.ma_prefix_attention_gather(
+            rows, kv, hkv, cur, scale, int(causal_block), int(q_pos0), int(c_pos0),
+            out.data_ptr(), _lib.i64(*out.stride()[:3]), _lib.ptr(mp), _lib.ptr(lp), _lib.ptr(op),
+            ws.data_ptr(), ws.numel(), gather.world, gather.rank, bases, tg, gout.data_ptr(),
+            _lib.i64(*gout.stride()[:3]), gws.data_ptr(), gws.numel(), _lib.stream_handle(dev)))
+    else:
+        _lib.check("ma_prefix_attention", lib.ma_prefix_attention(
+            rows, kv, hkv, cur, scale, int(causal_block), int(q_pos0), int(c_pos0),
+            out.data_ptr(), _lib.i64(*out.stride()[:3]), _lib.ptr(mp), _lib.ptr(lp), _lib.ptr(op),
+            ws.data_ptr(), ws.numel(), _lib.stream_handle(dev)))
     del qkeep, ckeep, desc
     return out, ((mp, lp, op, prefix) if want_prefix else None)
 

@@ -116,7 +116,9 @@ class PeerHeadGather:
     One instance per process group, one rank per GPU; every rank makes the same calls in
     the same order, as with a collective. The first call of a shape allocates the region
     and exchanges the handles (torch.distributed, so it must run outside CUDA-graph
-    capture); later calls, captured or not, launch two kernels. A wait that gave up is
+    capture); later calls, captured or not, launch two kernels. The attention can run the
+    same exchange inside its own launch (splitk_attention(..., head_gather=(this,
+    gathered)): its merge stores the rows, no further launch). A wait that gave up is
     reported by maskahead_b200.device_status()."""
 
     def __init__(self, world: int, rank: int, group=None):
@@ -158,6 +160,14 @@ class PeerHeadGather:
         reg = (ptr, (ctypes.c_void_p * self.world)(*bases), opened, ws)
         self._regions[key] = reg
         return reg
+
+    def region(self, dev: torch.device, b: int, hq: int, t: int):
+        """(regions, workspace) of the exchange of [b, hq, t, 128] rows, for an attention
+        launch that runs the exchange itself (splitk_attention's head_gather): the peers'
+        regions as mapped here (a ctypes array) and this rank's counters. The first call
+        of a shape allocates and maps (outside CUDA-graph capture, like __call__'s)."""
+        _ptr, bases, _opened, ws = self._region(dev, b, hq, t)
+        return bases, ws
 
     def __call__(self, part: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
         from . import _lib
