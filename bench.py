@@ -73,9 +73,11 @@ CONFIGS = {
                           "64-slot pages (shuffled pool), sequences sharded across ranks; step 0 + 3 sub-steps"),
 }
 METRIC = "µs per block-step select+attend; achieved HBM GB/s vs peak; tokens/s at 1/2/4/8 GPU"
-# DRAM bytes (read + write) per launch of the step-0 attention kernel, from the ncu captures
-# summarized in profiles/attn_partial_fa_cfg2.md and profiles/attn_partial_fa_cfg4_step0.md
-ATTN_TRAFFIC_BYTES = {"cfg2": 17_142_528, "cfg4": 273_547_264}
+# DRAM bytes (read + write) per launch of a kernel family, from the ncu captures summarized in
+# profiles/attn_partial_fa_cfg2.md (cfg2 step 0 and sub-step) and
+# profiles/attn_partial_fa_cfg4_step0.md (cfg4 step 0)
+TRAFFIC_BYTES = {("cfg2", "step0_attention"): 17_142_528, ("cfg4", "step0_attention"): 273_547_264,
+                 ("cfg2", "substep_attention"): 2_461_952}
 
 
 def parse_args():
@@ -1083,14 +1085,35 @@ def measure(c: dict, args, world: int, rank: int, dev, headline: bool) -> dict:
     parallelism = {"heads": f"kvheads{world} (head outputs gathered by peer stores over NVLink)" if world > 1
                    else "single GPU",
                    "seqs": f"seq{world} (no collective)"}[c["shard"]]
-    s0 = rooflines["step0_attention"]
-    roofline = {"kernel": "step-0 attention per layer: " + s0["kernel"], "bound": "hbm",
-                "achieved": s0["achieved_gbs"], "peak": rooflines["peaks"]["hbm_gbs"], "unit": "GB/s",
-                "frac": s0["hbm_frac"], "traffic": ATTN_TRAFFIC_BYTES.get(c["name"]) if world == 1 else None,
-                "peak_kind": f"{rooflines['peaks']['kind']} burst",
-                "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum of the step-0 launch "
-                                  "(profiles/attn_partial_fa_cfg2.md, profiles/attn_partial_fa_cfg4_step0.md)",
+    # the dominant kernel: the family with the largest share of a plain block-step (its time
+    # per launch x its launches per step); bound by the tensor pipe when its arithmetic
+    # intensity is above the measured ridge, else by HBM
+    peaks = rooflines["peaks"]
+    fams = {k: v for k, v in rooflines.items() if isinstance(v, dict) and "us_per_launch" in v}
+    for name, v in fams.items():
+        mult = c["substeps"] - 1 if name == "substep_attention" else 1
+        v["launches_per_step"] = c["L"] // v["layers_per_launch"] * mult
+        v["us_per_step"] = v["us_per_launch"] * v["launches_per_step"]
+    total_us = sum(v["us_per_step"] for v in fams.values())
+    for v in fams.values():
+        v["share"] = v["us_per_step"] / total_us
+    top = max(fams, key=lambda k: fams[k]["us_per_step"])
+    s0 = fams[top]
+    ai = s0["tflops"] * 1e12 / (s0["achieved_gbs"] * 1e9) if s0.get("tflops") else 0.0
+    tensor = ai * peaks["hbm_gbs"] > peaks["bf16_tflops_burst"] * 1e3
+    traffic = TRAFFIC_BYTES.get((c["name"], top)) if world == 1 and not args.layers and not args.batch else None
+    roofline = {"kernel": f"{top}: {s0['kernel']} ({s0['share']:.0%} of the kernel time of a plain block-step)",
+                "bound": "tensor" if tensor else "hbm",
+                "achieved": s0["tflops"] if tensor else s0["achieved_gbs"],
+                "peak": peaks["bf16_tflops_burst"] if tensor else peaks["hbm_gbs"],
+                "unit": "TFLOP/s" if tensor else "GB/s",
+                "frac": s0["tensor_frac_burst"] if tensor else s0["hbm_frac"],
+                "traffic": traffic, "peak_kind": f"{peaks['kind']} burst",
+                "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum of one launch "
+                                  "(profiles/attn_partial_fa_cfg2.md, profiles/attn_partial_fa_cfg4_step0.md); "
+                                  "null where no capture of this family at this config is committed",
                 "us_per_launch": s0["us_per_launch"], "bytes_per_launch": s0["bytes_per_launch"],
+                "arithmetic_intensity_flop_per_byte": ai, "hbm_frac": s0["hbm_frac"],
                 "tensor_tflops": s0.get("tflops"), "tensor_frac": s0.get("tensor_frac_burst"),
                 "tensor_frac_sustained": s0.get("tensor_frac_sustained")}
     res = {
