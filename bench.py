@@ -329,6 +329,16 @@ class Workload:
             return self.prefixes[layer]
         return Prefix.dense(self.K[layer], self.V[layer])
 
+    def step0_prefix(self, layer: int):
+        """The prefix step 0 of the batched block-step attends: the layer's slice of the
+        step's unpacked copy for a packed cache (unpacked at the start of the step), else
+        the cache."""
+        from maskahead_b200.layouts import Prefix
+
+        if self.UK is not None:
+            return Prefix.dense(self.UK[layer], self.UV[layer])
+        return self.prefix(layer)
+
     def gather_heads(self, out):
         """KV-head sharding: the full [B, Hq, T, D] output from every rank's heads (NCCL)."""
         if self.world == 1 or self.cfg["shard"] != "heads":
@@ -403,25 +413,31 @@ class Workload:
         sub-steps of every layer."""
         import torch
         from maskahead_b200.hotpath import (compact_attention, lookahead_survivors, select_step0,
-                                            step0_attention, value_score, value_score_prefix)
+                                            step0_attention, unpacked_prefix, value_score, value_score_prefix)
         from maskahead_b200.layouts import Prefix
 
         c = self.cfg
         L, T = c["L"], c["T"]
         merge = retain and c["retention"]
         outs = []
+        if self.UK is not None:
+            # a packed cache: every layer's prefix unpacked in one launch at the start of the
+            # block-step (the cache does not change during it) into the layer-stacked copy
+            # that step 0's attention of each layer and the batched selection read
+            unpacked_prefix(self.prefix_all, L * self.B, self.H, c["D"],
+                            out=(self.UK.flatten(0, 1), self.UV.flatten(0, 1)))
         for layer in range(L):
             hg = self.head_gather_arg(T)   # KV-head sharding: the exchange inside the launch
             if merge:
-                out, _ = step0_attention(self.QP[layer], self.prefix(layer), self.KCP[layer], self.VCP[layer],
+                out, _ = step0_attention(self.QP[layer], self.step0_prefix(layer), self.KCP[layer], self.VCP[layer],
                                          scaling=self.scale, stats_out=(self.MPR[layer], self.LPR[layer]),
-                                         unpack_out=self.unpack_out(layer), probe_blocks=c["probe_blocks"],
+                                         probe_blocks=c["probe_blocks"],
                                          block_size=T, head_gather=hg)
                 outs.append(out[:, :, :T] if hg is None else hg[1])
             else:
-                out, _ = step0_attention(self.Q[layer, 0], self.prefix(layer), self.KC[layer, 0], self.VC[layer, 0],
+                out, _ = step0_attention(self.Q[layer, 0], self.step0_prefix(layer), self.KC[layer, 0], self.VC[layer, 0],
                                          scaling=self.scale, stats_out=(self.MP[layer], self.LP[layer]),
-                                         unpack_out=self.unpack_out(layer), head_gather=hg)
+                                         head_gather=hg)
                 outs.append(out if hg is None else hg[1])
         # B == 1: merging the layer and batch axes of the queries is a view
         if merge:
